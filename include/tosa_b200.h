@@ -1,0 +1,210 @@
+/*
+ * tosa_b200 -- B200 (sm_100a) execution backend for the dense-contraction path
+ * of the tosa-interp TOSA interpreter: CONV2D, DEPTHWISE_CONV2D and MATMUL
+ * with their zero points, bias and acc_type, fused with the RESCALE (and
+ * CLAMP) that follows them, plus AVG_POOL2D / MAX_POOL2D and the glue ops the
+ * quantized graphs need (standalone RESCALE, CLAMP, ADD).
+ *
+ * C ABI: plain pointers and sizes, no C++ types, no exceptions across the
+ * boundary. Every entry point returns a tb_status; on failure the thread's
+ * last error message (tb_last_error) says why.
+ *
+ * Memory: tensor data passed to the operator entry points are DEVICE pointers
+ * on the context's device (allocate with tb_malloc or any CUDA allocator on
+ * the same device). Small attribute arrays (RESCALE multiplier/shift) are HOST
+ * pointers, as they are CONST tensors of the graph. `stream` is a
+ * cudaStream_t (NULL = the legacy default stream); launches are asynchronous
+ * and data-dependent errors (the reference's RESCALE/apply_scale range
+ * errors) are reported by the next tb_synchronize on that context.
+ *
+ * Reference interfaces replaced (tosa-interp, path:line):
+ *   operator dispatch          src/ops/mod.rs:22-150 (dispatch)
+ *   CONV2D                     src/ops/conv.rs:502-508 (eval_conv2d), :398-500
+ *   DEPTHWISE_CONV2D           src/ops/conv.rs:518-524
+ *   MATMUL                     src/ops/matmul.rs:176-178 (eval_matmul), :98-174
+ *   RESCALE                    src/ops/type_conv.rs:111-191 (eval_rescale)
+ *   CLAMP                      src/ops/elementwise.rs:319-343 (eval_clamp)
+ *   ADD                        src/ops/elementwise.rs:395-397 (eval_add)
+ *   AVG_POOL2D / MAX_POOL2D    src/ops/pool.rs:146-151, :233-238
+ *   run_graph*                 src/lib.rs:20-43; Interpreter::run src/interpreter.rs:122-147
+ *   InterpreterHook / HookSet  src/stats.rs:11-75
+ *   Error                      src/error.rs:4-31
+ */
+#ifndef TOSA_B200_H
+#define TOSA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define TB_API __attribute__((visibility("default")))
+#else
+#define TB_API
+#endif
+
+/* Status codes. 1..9 map one-to-one onto the reference's Error variants
+ * (src/error.rs:4-31); 64.. are backend conditions. */
+typedef enum tb_status {
+    TB_OK = 0,
+    TB_ERR_DESERIALIZE = 1,      /* Error::Deserialize */
+    TB_ERR_UNSUPPORTED_OP = 2,   /* Error::UnsupportedOp */
+    TB_ERR_TENSOR_NOT_FOUND = 3, /* Error::TensorNotFound */
+    TB_ERR_DTYPE_MISMATCH = 4,   /* Error::DTypeMismatch */
+    TB_ERR_SHAPE_MISMATCH = 5,   /* Error::ShapeMismatch */
+    TB_ERR_BROADCAST = 6,        /* Error::Broadcast */
+    TB_ERR_GRAPH = 7,            /* Error::GraphError (ERROR_IF, apply_scale range) */
+    TB_ERR_CONTROL_FLOW = 8,     /* Error::ControlFlow */
+    TB_ERR_IO = 9,               /* Error::Io */
+    TB_ERR_CUDA = 64,            /* a CUDA call failed */
+    TB_ERR_TIMEOUT = 65,         /* a bounded device wait gave up */
+    TB_ERR_INVALID_ARGUMENT = 66,/* null pointer, bad handle */
+    TB_ERR_NOT_ACCELERATED = 67  /* valid TOSA this backend does not run (caller keeps its own path) */
+} tb_status;
+
+/* DType codes: the serialized TOSA DType enum (schema/tosa.fbs:26-46). */
+enum {
+    TB_DT_BOOL = 1, TB_DT_INT4 = 2, TB_DT_INT8 = 3, TB_DT_INT16 = 4, TB_DT_INT32 = 5,
+    TB_DT_INT48 = 6, TB_DT_FP32 = 7, TB_DT_FP16 = 8, TB_DT_BF16 = 9, TB_DT_SHAPE = 10,
+    TB_DT_FP8E4M3 = 11, TB_DT_FP8E5M2 = 12, TB_DT_INT64 = 17
+};
+/* RescaleAttribute.rounding_mode (schema/tosa.fbs:60-65). */
+enum { TB_ROUND_SINGLE = 1, TB_ROUND_INEXACT = 2, TB_ROUND_DOUBLE = 3 };
+/* NanPropagationMode (schema/tosa.fbs:54-58). */
+enum { TB_NAN_PROPAGATE = 1, TB_NAN_IGNORE = 2 };
+
+typedef struct tb_context tb_context;
+
+/* ---- context, memory, errors ------------------------------------------- */
+
+/* One context per CUDA device; not shared between threads. */
+TB_API tb_status tb_context_create(int device, tb_context **out);
+TB_API void tb_context_destroy(tb_context *ctx);
+/* Message of the last failure on the calling thread ("" if none). */
+TB_API const char *tb_last_error(void);
+/* Wait for `stream`, then read and clear the context's device error word;
+ * returns TB_ERR_GRAPH if a kernel hit a RESCALE/apply_scale range error
+ * (src/ops/quant.rs:18-25, src/ops/type_conv.rs:183-186), TB_ERR_TIMEOUT if a
+ * bounded wait gave up. */
+TB_API tb_status tb_synchronize(tb_context *ctx, void *stream);
+TB_API tb_status tb_malloc(tb_context *ctx, size_t bytes, void **dptr);
+TB_API tb_status tb_free(tb_context *ctx, void *dptr);
+TB_API tb_status tb_memcpy_h2d(tb_context *ctx, void *dst, const void *src, size_t bytes, void *stream);
+TB_API tb_status tb_memcpy_d2h(tb_context *ctx, void *dst, const void *src, size_t bytes, void *stream);
+/* Number of kernels this context launched so far (for launch accounting). */
+TB_API uint64_t tb_launch_count(tb_context *ctx);
+/* Diagnostics: with TB_TRACE=1 in the environment at context creation, the
+ * tensor-core kernels record clock64 stamps of CTA 0 (producer stage issues,
+ * MMA stage starts, row-sum stage ends, epilogue tile start/end); copies the
+ * 512-entry buffer to host512. */
+TB_API tb_status tb_debug_trace(tb_context *ctx, long long *host512);
+
+/* ---- fused RESCALE epilogue ---------------------------------------------- */
+
+/* The RESCALE that follows a contraction (src/ops/type_conv.rs:111-191), and
+ * optionally the CLAMP after it (src/ops/elementwise.rs:319-343). The RESCALE
+ * input is the contraction's int32 result, so input_zp must be 0 and
+ * input_unsigned false, as the reference requires for INT32 input. */
+typedef struct tb_rescale_attr {
+    int32_t scale32;          /* RescaleAttribute.scale32 */
+    int32_t rounding_mode;    /* TB_ROUND_* */
+    int32_t per_channel;      /* multiplier/shift have `channels` entries */
+    int32_t input_unsigned;
+    int32_t output_unsigned;
+    int32_t input_zp;         /* raw value of the input_zp operand */
+    int32_t output_zp;        /* raw value of the output_zp operand */
+    int32_t out_dtype;        /* TB_DT_INT8 / INT16 / INT32 */
+    int32_t channels;         /* 1, or the last dimension when per_channel */
+    const int32_t *multiplier;/* HOST, `channels` values (int16 values widened when !scale32) */
+    const int8_t *shift;      /* HOST, `channels` values */
+    int32_t clamp_enabled;    /* fuse a following CLAMP of the RESCALE output */
+    int32_t clamp_min, clamp_max;
+} tb_rescale_attr;
+
+/* ---- MATMUL (src/ops/matmul.rs:98-174) -------------------------------------
+ * a [n,h,c], b [n,c,w] -> out [n,h,w]. Integer: INT8 x INT8 -> INT32 with
+ * zero points; float: BF16 x BF16 -> FP32 and FP16 x FP16 -> FP32 (fp32
+ * accumulation, results within the stated tolerance of the reference). With a
+ * rescale attribute the INT32 result is rescaled in the same kernel and `out`
+ * has rescale->out_dtype. */
+typedef struct tb_matmul_desc {
+    int32_t n, h, c, w;
+    int32_t a_dtype, b_dtype, out_dtype;
+    int32_t a_zp, b_zp;
+} tb_matmul_desc;
+
+typedef struct tb_matmul_plan tb_matmul_plan;
+TB_API tb_status tb_matmul_plan_create(tb_context *ctx, const tb_matmul_desc *desc, const tb_rescale_attr *rescale,
+                                       tb_matmul_plan **out);
+TB_API tb_status tb_matmul_plan_run(tb_matmul_plan *plan, const void *a, const void *b, void *out, void *stream);
+TB_API void tb_matmul_plan_destroy(tb_matmul_plan *plan);
+TB_API tb_status tb_matmul(tb_context *ctx, const tb_matmul_desc *desc, const tb_rescale_attr *rescale,
+                           const void *a, const void *b, void *out, void *stream);
+
+/* ---- CONV2D / DEPTHWISE_CONV2D (src/ops/conv.rs:398-524) -------------------
+ * input NHWC [n,ih,iw,ic]; CONV2D weight OHWI [oc,kh,kw,ic]; DEPTHWISE weight
+ * [kh,kw,ic,m] with oc = ic*m; bias [bias_len] (1 or oc) of out_dtype;
+ * pad = [top, bottom, left, right]. Integer: INT8 x INT8|INT4 (INT4 held one
+ * value per byte) -> INT32 with zero points; float: BF16 x BF16 and
+ * FP16 x FP16 with acc_type FP32 -> out_dtype (BF16/FP16/FP32 per the
+ * reference's type tables). The weight and bias pointers are read when the
+ * plan is created (per-channel sums) and again at every run. */
+typedef struct tb_conv2d_desc {
+    int32_t n, ih, iw, ic;
+    int32_t oc, kh, kw;       /* CONV2D; for DEPTHWISE oc = ic * m */
+    int32_t m;                /* DEPTHWISE channel multiplier (ignored by CONV2D) */
+    int32_t pad[4], stride[2], dilation[2];
+    int32_t in_dtype, w_dtype, acc_dtype, out_dtype;
+    int32_t input_zp, weight_zp;
+    int32_t bias_len;
+} tb_conv2d_desc;
+
+typedef struct tb_conv2d_plan tb_conv2d_plan;
+TB_API tb_status tb_conv2d_plan_create(tb_context *ctx, const tb_conv2d_desc *desc, const void *weight,
+                                       const void *bias, const tb_rescale_attr *rescale, tb_conv2d_plan **out);
+TB_API tb_status tb_depthwise_conv2d_plan_create(tb_context *ctx, const tb_conv2d_desc *desc, const void *weight,
+                                                 const void *bias, const tb_rescale_attr *rescale,
+                                                 tb_conv2d_plan **out);
+TB_API tb_status tb_conv2d_plan_run(tb_conv2d_plan *plan, const void *input, void *out, void *stream);
+TB_API void tb_conv2d_plan_destroy(tb_conv2d_plan *plan);
+TB_API tb_status tb_conv2d(tb_context *ctx, const tb_conv2d_desc *desc, const tb_rescale_attr *rescale,
+                           const void *input, const void *weight, const void *bias, void *out, void *stream);
+TB_API tb_status tb_depthwise_conv2d(tb_context *ctx, const tb_conv2d_desc *desc, const tb_rescale_attr *rescale,
+                                     const void *input, const void *weight, const void *bias, void *out,
+                                     void *stream);
+
+/* ---- standalone elementwise ops ----------------------------------------- */
+
+/* RESCALE of `count` elements of in_dtype (INT8/INT16/INT32), channel of
+ * element i = i % channels when per_channel (src/ops/type_conv.rs:111-191). */
+TB_API tb_status tb_rescale(tb_context *ctx, const tb_rescale_attr *attr, int32_t in_dtype, const void *input,
+                            int64_t count, void *out, void *stream);
+/* CLAMP (src/ops/elementwise.rs:319-343): INT8/INT16 with integer bounds, or
+ * FP16/BF16/FP32 with float bounds and a NaN mode. */
+TB_API tb_status tb_clamp(tb_context *ctx, int32_t dtype, const void *input, int64_t count, int64_t min_i,
+                          int64_t max_i, float min_f, float max_f, int32_t nan_mode, void *out, void *stream);
+/* ADD of two equal-shape tensors (INT32 wraps; FP32 rounds), src/ops/elementwise.rs:395-397. */
+TB_API tb_status tb_add(tb_context *ctx, int32_t dtype, const void *a, const void *b, int64_t count, void *out,
+                        void *stream);
+
+/* ---- pooling (src/ops/pool.rs:146-286) ----------------------------------- */
+typedef struct tb_pool2d_desc {
+    int32_t n, ih, iw, c;
+    int32_t kernel[2], stride[2], pad[4];
+    int32_t dtype;            /* INT8 / INT16 / FP16 / BF16 / FP32 */
+    int32_t acc_dtype;        /* AVG_POOL2D: INT32 for integers, FP32 for floats */
+    int32_t input_zp, output_zp; /* AVG_POOL2D, INT8 only */
+    int32_t nan_mode;         /* MAX_POOL2D */
+} tb_pool2d_desc;
+TB_API tb_status tb_avg_pool2d(tb_context *ctx, const tb_pool2d_desc *desc, const void *input, void *out,
+                               void *stream);
+TB_API tb_status tb_max_pool2d(tb_context *ctx, const tb_pool2d_desc *desc, const void *input, void *out,
+                               void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TOSA_B200_H */

@@ -1,0 +1,317 @@
+"""GPU parity of the tensor-core contractions against the CPU oracle.
+
+Integer results must be bit-exact (the reference's AccI32 wraps mod 2^32, so
+any summation order gives the same bits). Float MATMUL / CONV2D results
+accumulate in fp32 on the tensor core in a different order than the
+reference's sequential AccF32 loop; they must lie within
+
+    |gpu - ref| <= 2 * ulp_bf16(ref) + 2^-16 * sum_k |a_k * b_k|
+
+(2 bf16 ULP of the reference value, plus an absolute floor scaled by the
+dot product's magnitude for results near zero, where cancellation makes a
+relative bound meaningless).
+"""
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from tests import helpers as H
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+from tosa_b200 import _lib as L  # noqa: E402
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    c = L.Context(0)
+    yield c
+    c.close()
+
+
+def dev(a, dtype):
+    return torch.from_numpy(np.ascontiguousarray(a).astype(dtype)).cuda()
+
+
+def run_matmul(ctx, a, b, za, zb, rescale=None, a_dtype=L.DT_INT8, out_dtype=L.DT_INT32):
+    n, h, c = a.shape
+    w = b.shape[2]
+    d = L.MatmulDesc(n=n, h=h, c=c, w=w, a_dtype=a_dtype, b_dtype=a_dtype, out_dtype=out_dtype, a_zp=za, b_zp=zb)
+    if a_dtype == L.DT_INT8:
+        ta, tb = dev(a, np.int8), dev(b, np.int8)
+        odt = {L.DT_INT8: torch.int8, L.DT_INT16: torch.int16, L.DT_INT32: torch.int32}[
+            rescale.out_dtype if rescale is not None else L.DT_INT32]
+    else:
+        tdt = torch.bfloat16 if a_dtype == L.DT_BF16 else torch.float16
+        ta = torch.from_numpy(a.astype(np.float32)).to(tdt).cuda()
+        tb = torch.from_numpy(b.astype(np.float32)).to(tdt).cuda()
+        odt = torch.float32
+    out = torch.empty((n, h, w), dtype=odt, device="cuda")
+    L.check(L.load().tb_matmul(ctx.h, d, rescale, L.ptr(ta), L.ptr(tb), L.ptr(out), L.stream_ptr()))
+    ctx.synchronize()
+    return out.cpu().numpy()
+
+
+MATMUL_SHAPES = [
+    (1, 128, 128, 128, 0, 0),
+    (2, 200, 96, 160, -5, 7),      # M tail, K < BK, N tail with BN=256
+    (3, 130, 256, 64, 3, 0),       # a_zp only
+    (1, 64, 1024, 384, 0, -8),     # b_zp only, N spans 2 tiles
+    (2, 257, 528, 272, -128, 127), # extreme zero points
+]
+
+
+@pytest.mark.parametrize("n,h,c,w,za,zb", MATMUL_SHAPES)
+def test_matmul_int8_tensor_core(ctx, n, h, c, w, za, zb):
+    rng = np.random.default_rng(n * 1000 + h + c + w)
+    a = rng.integers(-128, 128, (n, h, c), dtype=np.int64)
+    b = rng.integers(-128, 128, (n, c, w), dtype=np.int64)
+    got = run_matmul(ctx, a, b, za, zb)
+    exp = H.oracle_matmul_int(a, b, za, zb)
+    assert np.array_equal(got.astype(np.int64), exp)
+
+
+@pytest.mark.parametrize("rounding", [L.ROUND_SINGLE, L.ROUND_DOUBLE])
+@pytest.mark.parametrize("per_channel", [False, True])
+def test_matmul_int8_fused_rescale(ctx, rounding, per_channel):
+    rng = np.random.default_rng(7 + rounding + per_channel)
+    n, h, c, w = 2, 160, 256, 192
+    a = rng.integers(-128, 128, (n, h, c), dtype=np.int64)
+    b = rng.integers(-128, 128, (n, c, w), dtype=np.int64)
+    za, zb = int(rng.integers(-8, 9)), int(rng.integers(-8, 9))
+    ch = w if per_channel else 1
+    mult = rng.integers(1 << 30, (1 << 31) - 1, ch)
+    shift = rng.integers(32, 40, ch)
+    attr = L.rescale_attr(mult, shift, rounding=rounding, output_zp=5, out_dtype=L.DT_INT8)
+    got = run_matmul(ctx, a, b, za, zb, rescale=attr)
+    acc = H.oracle_matmul_int(a, b, za, zb)
+    rc, exp = H.oracle_rescale(acc, L.DT_INT32, L.DT_INT8, mult, shift, 0, 5, 1, rounding, int(per_channel))
+    assert rc == 0
+    assert np.array_equal(got.reshape(-1).astype(np.int64), exp)
+
+
+def test_matmul_int8_rescale_small_shift_checks(ctx):
+    """Shifts below 32 take the checked epilogue: in-range values are exact,
+    out-of-range values are reported as GraphError (quant.rs:21-25)."""
+    rng = np.random.default_rng(11)
+    n, h, c, w = 1, 128, 64, 128
+    a = rng.integers(-4, 5, (n, h, c), dtype=np.int64)
+    b = rng.integers(-4, 5, (n, c, w), dtype=np.int64)
+    mult = [1 << 20] * w
+    shift = [24] * w
+    attr = L.rescale_attr(mult, shift, rounding=L.ROUND_SINGLE, out_dtype=L.DT_INT16)
+    got = run_matmul(ctx, a, b, 0, 0, rescale=attr)
+    acc = H.oracle_matmul_int(a, b, 0, 0)
+    rc, exp = H.oracle_rescale(acc, L.DT_INT32, L.DT_INT16, mult, shift, 0, 0, 1, L.ROUND_SINGLE, 1)
+    assert rc == 0 and np.array_equal(got.reshape(-1).astype(np.int64), exp)
+    # value out of range for shift 4: |v| >= 2^3
+    attr2 = L.rescale_attr([1 << 20] * w, [4] * w, rounding=L.ROUND_SINGLE, out_dtype=L.DT_INT16)
+    with pytest.raises(L.TbError) as ei:
+        run_matmul(ctx, a * 0 + 100, b * 0 + 100, 0, 0, rescale=attr2)
+    assert ei.value.kind == "GraphError"
+
+
+@pytest.mark.parametrize("n,h,c,w", [(33, 7, 9, 32), (3, 5, 17, 13)])
+def test_matmul_int8_direct_path(ctx, n, h, c, w):
+    """Rows not a multiple of 16 bytes take the CUDA-core kernel."""
+    rng = np.random.default_rng(n + h)
+    a = rng.integers(-128, 128, (n, h, c), dtype=np.int64)
+    b = rng.integers(-128, 128, (n, c, w), dtype=np.int64)
+    got = run_matmul(ctx, a, b, -80, -9)
+    assert np.array_equal(got.astype(np.int64), H.oracle_matmul_int(a, b, -80, -9))
+
+
+def float_tolerance_ok(got, exp, a, b):
+    absab = np.einsum("nhc,ncw->nhw", np.abs(a.astype(np.float64)), np.abs(b.astype(np.float64)))
+    tol = 2 * H.ulp_bf16(exp) + 2.0 ** -16 * absab
+    err = np.abs(got.astype(np.float64) - exp.astype(np.float64))
+    return bool(np.all(err <= tol)), float(np.max(err / np.maximum(tol, 1e-30)))
+
+
+@pytest.mark.parametrize("dt", [L.DT_BF16, L.DT_FP16])
+@pytest.mark.parametrize("n,h,c,w", [(1, 128, 128, 128), (2, 192, 320, 200), (4, 64, 512, 256)])
+def test_matmul_float_tensor_core(ctx, dt, n, h, c, w):
+    rng = np.random.default_rng(c + w)
+    a = rng.normal(0, 1, (n, h, c)).astype(np.float32)
+    b = rng.normal(0, 1, (n, c, w)).astype(np.float32)
+    if dt == L.DT_BF16:
+        a, b = H.bf16_round(a), H.bf16_round(b)
+    else:
+        a, b = a.astype(np.float16).astype(np.float32), b.astype(np.float16).astype(np.float32)
+    got = run_matmul(ctx, a, b, 0, 0, a_dtype=dt, out_dtype=L.DT_FP32)
+    exp = H.oracle_matmul_float(a, b, O.D["FP32"])
+    ok, worst = float_tolerance_ok(got, exp, a, b)
+    assert ok, f"worst error / tolerance = {worst}"
+
+
+# ---------------------------------------------------------------------------
+# CONV2D
+# ---------------------------------------------------------------------------
+
+
+def run_conv(ctx, x, w, bias, zx, zw, pad, stride, dil, rescale=None, depthwise=False,
+             in_dtype=L.DT_INT8, acc=L.DT_INT32, out_dtype=L.DT_INT32):
+    n, ih, iw, ic = x.shape
+    if depthwise:
+        kh, kw, _, m = w.shape
+        oc = ic * m
+    else:
+        oc, kh, kw, _ = w.shape
+        m = 1
+    d = L.conv_desc(n, ih, iw, ic, oc, kh, kw, pad, stride, dil, in_dtype, in_dtype, acc, out_dtype, zx, zw,
+                    len(bias), m)
+    oh, ow = L.conv_out_hw(ih, iw, kh, kw, pad, stride, dil)
+    if in_dtype == L.DT_INT8:
+        tx, tw, tbias = dev(x, np.int8), dev(w, np.int8), dev(bias, np.int32)
+        odt = {L.DT_INT8: torch.int8, L.DT_INT16: torch.int16, L.DT_INT32: torch.int32}[
+            rescale.out_dtype if rescale is not None else L.DT_INT32]
+    else:
+        tdt = torch.bfloat16 if in_dtype == L.DT_BF16 else torch.float16
+        tx = torch.from_numpy(x.astype(np.float32)).to(tdt).cuda()
+        tw = torch.from_numpy(w.astype(np.float32)).to(tdt).cuda()
+        odt = {L.DT_BF16: torch.bfloat16, L.DT_FP16: torch.float16, L.DT_FP32: torch.float32}[out_dtype]
+        tbias = torch.from_numpy(bias.astype(np.float32)).to(odt).cuda()
+    out = torch.empty((n, oh, ow, oc), dtype=odt, device="cuda")
+    fn = L.load().tb_depthwise_conv2d if depthwise else L.load().tb_conv2d
+    L.check(fn(ctx.h, d, rescale, L.ptr(tx), L.ptr(tw), L.ptr(tbias), L.ptr(out), L.stream_ptr()))
+    ctx.synchronize()
+    return out.float().cpu().numpy() if in_dtype != L.DT_INT8 else out.cpu().numpy()
+
+
+CONV_CASES = [
+    # (n, ih, iw, ic, oc, kh, kw, pad, stride, dil, zx, zw)
+    (1, 8, 8, 64, 64, 3, 3, (1, 1, 1, 1), (1, 1), (1, 1), -3, 0),
+    (2, 14, 14, 128, 96, 3, 3, (1, 1, 1, 1), (1, 1), (1, 1), 5, -2),
+    (2, 10, 11, 32, 40, 3, 3, (1, 0, 2, 1), (2, 1), (2, 1), -49, 1),
+    (1, 16, 16, 64, 256, 1, 1, (0, 0, 0, 0), (1, 1), (1, 1), 7, 3),
+    (2, 15, 15, 64, 128, 1, 1, (0, 0, 0, 0), (2, 2), (1, 1), -8, 8),
+    (1, 13, 13, 16, 64, 5, 5, (2, 2, 2, 2), (2, 2), (1, 1), 4, -4),
+    (1, 7, 7, 256, 320, 3, 3, (1, 1, 1, 1), (1, 1), (1, 1), 0, 0),
+]
+
+
+@pytest.mark.parametrize("case", CONV_CASES)
+def test_conv2d_int8_tensor_core(ctx, case):
+    n, ih, iw, ic, oc, kh, kw, pad, stride, dil, zx, zw = case
+    rng = np.random.default_rng(ih * 31 + ic + oc)
+    x = rng.integers(-128, 128, (n, ih, iw, ic), dtype=np.int64)
+    w = rng.integers(-127, 128, (oc, kh, kw, ic), dtype=np.int64)
+    bias = rng.integers(-32768, 32768, oc, dtype=np.int64)
+    got = run_conv(ctx, x, w, bias, zx, zw, pad, stride, dil)
+    exp = H.oracle_conv_int(x, w, bias, zx, zw, pad, stride, dil)
+    assert got.shape == exp.shape
+    assert np.array_equal(got.astype(np.int64), exp)
+
+
+def test_conv2d_config1_fused_rescale(ctx):
+    """[1,56,56,64] x [64,3,3,64], pad 1, zx=-3, zw=0,
+    per-channel double-round RESCALE to int8 with output_zp 5."""
+    rng = np.random.default_rng(20261201)
+    x = rng.integers(-128, 128, (1, 56, 56, 64), dtype=np.int64)
+    w = rng.integers(-127, 128, (64, 3, 3, 64), dtype=np.int64)
+    bias = rng.integers(-32768, 32768, 64, dtype=np.int64)
+    mult = rng.integers(1 << 30, (1 << 31) - 1, 64, endpoint=True)
+    shift = rng.integers(30, 39, 64)
+    attr = L.rescale_attr(mult, shift, rounding=L.ROUND_DOUBLE, output_zp=5, out_dtype=L.DT_INT8)
+    got = run_conv(ctx, x, w, bias, -3, 0, (1, 1, 1, 1), (1, 1), (1, 1), rescale=attr)
+    acc = H.oracle_conv_int(x, w, bias, -3, 0, (1, 1, 1, 1), (1, 1), (1, 1))
+    rc, exp = H.oracle_rescale(acc, L.DT_INT32, L.DT_INT8, mult, shift, 0, 5, 1, L.ROUND_DOUBLE, 1)
+    if rc != 0:
+        with pytest.raises(L.TbError):
+            run_conv(ctx, x, w, bias, -3, 0, (1, 1, 1, 1), (1, 1), (1, 1), rescale=attr)
+        return
+    assert np.array_equal(got.reshape(-1).astype(np.int64), exp)
+
+
+def test_conv2d_int8_rescale_clamp(ctx):
+    rng = np.random.default_rng(99)
+    x = rng.integers(-128, 128, (2, 11, 11, 64), dtype=np.int64)
+    w = rng.integers(-127, 128, (128, 3, 3, 64), dtype=np.int64)
+    bias = rng.integers(-1000, 1000, 128, dtype=np.int64)
+    mult = rng.integers(1 << 30, (1 << 31) - 1, 128)
+    shift = rng.integers(36, 42, 128)
+    attr = L.rescale_attr(mult, shift, rounding=L.ROUND_DOUBLE, output_zp=-4, out_dtype=L.DT_INT8, clamp=(0, 127))
+    got = run_conv(ctx, x, w, bias, 2, -3, (1, 1, 1, 1), (2, 2), (1, 1), rescale=attr)
+    acc = H.oracle_conv_int(x, w, bias, 2, -3, (1, 1, 1, 1), (2, 2), (1, 1))
+    rc, r = H.oracle_rescale(acc, L.DT_INT32, L.DT_INT8, mult, shift, 0, -4, 1, L.ROUND_DOUBLE, 1)
+    assert rc == 0
+    assert np.array_equal(got.reshape(-1).astype(np.int64), np.clip(r, 0, 127))
+
+
+@pytest.mark.parametrize("case", [
+    (2, 10, 5, 3, 7, 3, 3, (1, 0, 2, 1), (2, 1), (2, 1), -49, 1),  # ic=3: direct kernel
+    (2, 8, 8, 24, 16, 3, 3, (1, 1, 1, 1), (1, 1), (1, 1), 3, 2),
+])
+def test_conv2d_int8_direct_path(ctx, case):
+    n, ih, iw, ic, oc, kh, kw, pad, stride, dil, zx, zw = case
+    rng = np.random.default_rng(ic)
+    x = rng.integers(-128, 128, (n, ih, iw, ic), dtype=np.int64)
+    w = rng.integers(-127, 128, (oc, kh, kw, ic), dtype=np.int64)
+    bias = rng.integers(-2 ** 31, 2 ** 31, 1, dtype=np.int64)
+    got = run_conv(ctx, x, w, bias, zx, zw, pad, stride, dil)
+    assert np.array_equal(got.astype(np.int64), H.oracle_conv_int(x, w, bias, zx, zw, pad, stride, dil))
+
+
+@pytest.mark.parametrize("dt,out_dt", [(L.DT_BF16, L.DT_BF16), (L.DT_BF16, L.DT_FP32), (L.DT_FP16, L.DT_FP16)])
+def test_conv2d_float_tensor_core(ctx, dt, out_dt):
+    rng = np.random.default_rng(dt * 10 + out_dt)
+    x = rng.normal(0, 1, (2, 12, 12, 64)).astype(np.float32)
+    w = rng.normal(0, 0.1, (96, 3, 3, 64)).astype(np.float32)
+    bias = rng.normal(0, 1, 96).astype(np.float32)
+    rnd = H.bf16_round if dt == L.DT_BF16 else (lambda v: v.astype(np.float16).astype(np.float32))
+    x, w = rnd(x), rnd(w)
+    bias = H.bf16_round(bias) if out_dt == L.DT_BF16 else (
+        bias.astype(np.float16).astype(np.float32) if out_dt == L.DT_FP16 else bias)
+    pad, stride, dil = (1, 1, 1, 1), (1, 1), (1, 1)
+    got = run_conv(ctx, x, w, bias, 0, 0, pad, stride, dil, in_dtype=dt, acc=L.DT_FP32, out_dtype=out_dt)
+    exp = H.oracle_conv_float(x, w, bias, O.D["FP32"], out_dt, pad, stride, dil)
+    # |x*w| summed over the window, for the absolute floor
+    absx = np.abs(x.astype(np.float64))
+    xp = np.pad(absx, ((0, 0), (1, 1), (1, 1), (0, 0)))
+    absw = np.abs(w.astype(np.float64))
+    mag = np.zeros(exp.shape)
+    for ky in range(3):
+        for kx in range(3):
+            mag += np.einsum("nhwc,oc->nhwo", xp[:, ky:ky + 12, kx:kx + 12, :], absw[:, ky, kx, :])
+    out_ulp = H.ulp_bf16(exp) if out_dt != L.DT_FP16 else 2.0 ** (np.floor(np.log2(np.maximum(np.abs(exp), 2.0 ** -14))) - 10)
+    tol = 2 * np.maximum(out_ulp, H.ulp_bf16(exp)) + 2.0 ** -16 * mag
+    err = np.abs(got.astype(np.float64) - exp)
+    assert np.all(err <= tol), float(np.max(err / tol))
+
+
+# ---------------------------------------------------------------------------
+# DEPTHWISE_CONV2D
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("case", [
+    (2, 28, 28, 96, 1, 3, 3, (1, 1, 1, 1), (1, 1), (1, 1), -5, 3),
+    (1, 16, 16, 64, 1, 3, 3, (0, 1, 0, 1), (2, 2), (1, 1), 7, 0),
+    (2, 5, 6, 2, 3, 3, 3, (1, 1, 0, 1), (2, 2), (1, 2), 53, 39),
+])
+def test_depthwise_int8(ctx, case):
+    n, ih, iw, c, m, kh, kw, pad, stride, dil, zx, zw = case
+    rng = np.random.default_rng(c * 7 + m)
+    x = rng.integers(-128, 128, (n, ih, iw, c), dtype=np.int64)
+    w = rng.integers(-127, 128, (kh, kw, c, m), dtype=np.int64)
+    bias = rng.integers(-5000, 5000, c * m, dtype=np.int64)
+    got = run_conv(ctx, x, w, bias, zx, zw, pad, stride, dil, depthwise=True)
+    exp = H.oracle_conv_int(x, w, bias, zx, zw, pad, stride, dil, depthwise=True)
+    assert np.array_equal(got.astype(np.int64), exp)
+
+
+def test_depthwise_int8_fused_rescale_clamp(ctx):
+    rng = np.random.default_rng(5)
+    n, ih, iw, c = 2, 15, 15, 144
+    x = rng.integers(-128, 128, (n, ih, iw, c), dtype=np.int64)
+    w = rng.integers(-127, 128, (3, 3, c, 1), dtype=np.int64)
+    bias = rng.integers(-5000, 5000, c, dtype=np.int64)
+    mult = rng.integers(1 << 30, (1 << 31) - 1, c)
+    shift = rng.integers(34, 40, c)
+    attr = L.rescale_attr(mult, shift, rounding=L.ROUND_DOUBLE, output_zp=3, out_dtype=L.DT_INT8, clamp=(0, 127))
+    got = run_conv(ctx, x, w, bias, -2, 1, (1, 1, 1, 1), (2, 2), (1, 1), rescale=attr, depthwise=True)
+    acc = H.oracle_conv_int(x, w, bias, -2, 1, (1, 1, 1, 1), (2, 2), (1, 1), depthwise=True)
+    rc, r = H.oracle_rescale(acc, L.DT_INT32, L.DT_INT8, mult, shift, 0, 3, 1, L.ROUND_DOUBLE, 1)
+    assert rc == 0
+    assert np.array_equal(got.reshape(-1).astype(np.int64), np.clip(r, 0, 127))

@@ -1,0 +1,1057 @@
+// Host side of libtosa_b200: contexts, tensor maps, the static ERROR_IF
+// checks of each operator (as the reference performs them before computing),
+// plans that precompute zero-point terms, and kernel launches.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "internal.hpp"
+#include "simt_kernels.cuh"
+#include "simt_ops.cuh"
+#include "gemm_launch.cuh"
+
+namespace tb {
+
+static thread_local std::string g_last_error;
+
+tb_status fail(tb_status st, const char* fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return st;
+}
+
+// ---------------------------------------------------------------------------
+// Tensor maps (driver entry points resolved through the runtime)
+// ---------------------------------------------------------------------------
+
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+typedef CUresult (*PFN_encodeIm2col)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                     const cuuint64_t*, const int*, const int*, cuuint32_t, cuuint32_t,
+                                     const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                     CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static PFN_encodeTiled g_encode_tiled = nullptr;
+static PFN_encodeIm2col g_encode_im2col = nullptr;
+static std::once_flag g_encode_once;
+
+static tb_status load_encoders() {
+    std::call_once(g_encode_once, [] {
+        cudaDriverEntryPointQueryResult q;
+        void* fn = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode_tiled = reinterpret_cast<PFN_encodeTiled>(fn);
+        fn = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeIm2col", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode_im2col = reinterpret_cast<PFN_encodeIm2col>(fn);
+    });
+    if (!g_encode_tiled || !g_encode_im2col) return fail(TB_ERR_CUDA, "cuTensorMapEncode* entry points unavailable");
+    return TB_OK;
+}
+
+tb_status encode_tiled(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* base, const uint64_t* dims,
+                       const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swz) {
+    TB_TRY(load_encoders());
+    cuuint32_t es[5] = {1, 1, 1, 1, 1};
+    CUresult r = g_encode_tiled(map, dt, rank, const_cast<void*>(base), dims, strides_bytes, box, es,
+                                CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(TB_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+    return TB_OK;
+}
+
+tb_status encode_im2col(CUtensorMap* map, CUtensorMapDataType dt, const void* base, const uint64_t* dims,
+                        const uint64_t* strides_bytes, const int* lower, const int* upper, uint32_t channels,
+                        uint32_t pixels, const uint32_t* elem_strides, CUtensorMapSwizzle swz) {
+    TB_TRY(load_encoders());
+    CUresult r = g_encode_im2col(map, dt, 4, const_cast<void*>(base), dims, strides_bytes, lower, upper, channels,
+                                 pixels, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(TB_ERR_CUDA, "cuTensorMapEncodeIm2col failed (%d)", static_cast<int>(r));
+    return TB_OK;
+}
+
+static CUtensorMapDataType tmap_dtype(int dt) {
+    if (dt == TB_DT_BF16) return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    if (dt == TB_DT_FP16) return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    return CU_TENSOR_MAP_DATA_TYPE_UINT8;
+}
+
+static int grid_for(const tb_context* ctx, long long work, int block = 256) {
+    long long g = (work + block - 1) / block;
+    long long cap = static_cast<long long>(ctx->num_sms) * 8;
+    if (g > cap) g = cap;
+    if (g < 1) g = 1;
+    return static_cast<int>(g);
+}
+
+#define TB_LAUNCHED(ctx)                                                                               \
+    do {                                                                                               \
+        cudaError_t e_ = cudaGetLastError();                                                           \
+        if (e_ != cudaSuccess) return ::tb::fail(TB_ERR_CUDA, "kernel launch failed: %s", cudaGetErrorString(e_)); \
+        (ctx)->launches++;                                                                             \
+    } while (0)
+
+// ---------------------------------------------------------------------------
+// RESCALE validation (src/ops/type_conv.rs:128-171) and device plan
+// ---------------------------------------------------------------------------
+
+static int bit_width(int dt) { return dt == TB_DT_INT8 ? 8 : dt == TB_DT_INT16 ? 16 : dt == TB_DT_INT32 ? 32 : 48; }
+static void int_range(int dt, int64_t* lo, int64_t* hi) {
+    switch (dt) {
+    case TB_DT_INT8: *lo = -128; *hi = 127; break;
+    case TB_DT_INT16: *lo = -32768; *hi = 32767; break;
+    case TB_DT_INT32: *lo = INT32_MIN; *hi = INT32_MAX; break;
+    default: *lo = -(1ll << 47); *hi = (1ll << 47) - 1;
+    }
+}
+
+tb_status check_rescale(const tb_rescale_attr* a, int in_t, int64_t shape_last, int64_t* in_zp_ext, int64_t* out_zp_ext,
+                        int32_t* lo, int32_t* hi) {
+    const int out_t = a->out_dtype;
+    if (!(in_t == TB_DT_INT8 || in_t == TB_DT_INT16 || in_t == TB_DT_INT32 || in_t == TB_DT_INT48) ||
+        !(out_t == TB_DT_INT8 || out_t == TB_DT_INT16 || out_t == TB_DT_INT32))
+        return fail(TB_ERR_DTYPE_MISMATCH, "RESCALE: unsupported types %d -> %d", in_t, out_t);
+    if (a->rounding_mode < 1 || a->rounding_mode > 3) return fail(TB_ERR_GRAPH, "RESCALE: unsupported rounding mode");
+    if (a->scale32 && in_t == TB_DT_INT48) return fail(TB_ERR_GRAPH, "RESCALE: scale32 is not allowed for INT48 input");
+    if (!a->scale32 && a->rounding_mode == TB_ROUND_DOUBLE)
+        return fail(TB_ERR_GRAPH, "RESCALE: double rounding requires scale32");
+    const bool has32 = in_t == TB_DT_INT32 || in_t == TB_DT_INT48 || out_t == TB_DT_INT32;
+    if ((a->input_unsigned && a->output_unsigned) || ((a->input_unsigned || a->output_unsigned) && has32))
+        return fail(TB_ERR_GRAPH, "RESCALE: invalid combination of input_unsigned/output_unsigned and types");
+    const int64_t channels = a->per_channel ? shape_last : 1;
+    if (a->channels != channels)
+        return fail(TB_ERR_GRAPH, "RESCALE: multiplier and shift must have %lld elements", (long long)channels);
+    if (!a->multiplier || !a->shift) return fail(TB_ERR_INVALID_ARGUMENT, "RESCALE: null multiplier/shift");
+    auto extend = [](int dt, int64_t v, bool uns) { return uns ? (v & ((1ll << bit_width(dt)) - 1)) : v; };
+    const int64_t izp = extend(in_t, a->input_zp, a->input_unsigned);
+    const int64_t ozp = extend(out_t, a->output_zp, a->output_unsigned);
+    auto zp_ok = [](int dt, int64_t zp, bool uns) {
+        return dt == TB_DT_INT8 || zp == 0 || (dt == TB_DT_INT16 && uns && zp == 32768);
+    };
+    if (!zp_ok(in_t, izp, a->input_unsigned) || !zp_ok(out_t, ozp, a->output_unsigned))
+        return fail(TB_ERR_GRAPH, "RESCALE: zero point not allowed for this type");
+    int64_t l, h;
+    if (a->output_unsigned) { l = 0; h = (1ll << bit_width(out_t)) - 1; }
+    else int_range(out_t, &l, &h);
+    if (a->clamp_enabled) {
+        if (a->clamp_max < a->clamp_min) return fail(TB_ERR_GRAPH, "CLAMP: max_val must not be smaller than min_val");
+        if (a->output_unsigned) return fail(TB_ERR_NOT_ACCELERATED, "CLAMP fusion after an unsigned RESCALE");
+        // clamp(clamp(v, l, h), cmin, cmax) as one clamp (constant when disjoint).
+        int64_t nl = std::max<int64_t>(l, a->clamp_min), nh = std::min<int64_t>(h, a->clamp_max);
+        if (nl > nh) {
+            const int64_t c = a->clamp_min > h ? a->clamp_min : a->clamp_max;
+            nl = nh = c;
+        }
+        l = nl;
+        h = nh;
+    }
+    *in_zp_ext = izp;
+    *out_zp_ext = ozp;
+    *lo = static_cast<int32_t>(l);
+    *hi = static_cast<int32_t>(h);
+    return TB_OK;
+}
+
+tb_status make_rescale_plan(tb_context* ctx, const tb_rescale_attr* a, int in_t, int64_t shape_last, RescalePlan* r) {
+    (void)ctx;
+    int64_t izp, ozp;
+    int32_t lo, hi;
+    TB_TRY(check_rescale(a, in_t, shape_last, &izp, &ozp, &lo, &hi));
+    r->enabled = true;
+    r->scale32 = a->scale32;
+    r->rounding = a->rounding_mode;
+    r->per_channel = a->per_channel;
+    r->channels = a->channels;
+    r->out_zp = static_cast<int32_t>(ozp);
+    r->lo = lo;
+    r->hi = hi;
+    r->out_dtype = a->out_dtype;
+    std::vector<int32_t> m(a->channels), s(a->channels);
+    bool fast = a->scale32 && a->rounding_mode != TB_ROUND_INEXACT && izp == 0;
+    for (int i = 0; i < a->channels; ++i) {
+        m[i] = a->multiplier[i];
+        s[i] = a->shift[i];
+        if (m[i] < 0 || s[i] < 32 || s[i] > 62) fast = false;
+    }
+    r->fast = fast;
+    if (fast) {
+        // R = 2^(s-1) (+2^30 for v >= 0, -2^30 for v < 0 under double rounding) as 64-bit lo/hi words;
+        // when every shift is <= 55 the output zero point rides along as zp * 2^s (the 64-bit sum then
+        // stays below 2^63 and the shifted result gains exactly zp). Padded to whole 256-column tiles
+        // with channel 0 so the kernel needs no index clamp.
+        bool fold = true;
+        for (int i = 0; i < a->channels; ++i)
+            if (s[i] > 55) fold = false;
+        r->zp_folded = fold;
+        const size_t padded = (static_cast<size_t>(a->channels) + 255) / 256 * 256;
+        std::vector<int32_t> rq(8 * padded, 0);
+        for (size_t pi = 0; pi < padded; ++pi) {
+            const int i = pi < static_cast<size_t>(a->channels) ? static_cast<int>(pi) : 0;
+            const int64_t base = (1ll << (s[i] - 1)) + (fold ? static_cast<int64_t>(ozp) * (1ll << s[i]) : 0);
+            const int64_t dr = a->rounding_mode == TB_ROUND_DOUBLE ? (1ll << 30) : 0;
+            const uint64_t rp = static_cast<uint64_t>(base + dr), rn = static_cast<uint64_t>(base - dr);
+            int32_t* q = &rq[8 * pi];
+            q[0] = m[i];
+            q[1] = s[i] - 32;
+            q[2] = static_cast<int32_t>(rp & 0xffffffffu);
+            q[3] = static_cast<int32_t>(rp >> 32);
+            q[4] = static_cast<int32_t>(rn & 0xffffffffu);
+            q[5] = static_cast<int32_t>(rn >> 32);
+        }
+        TB_CUDA(cudaMalloc(&r->d_rq, sizeof(int32_t) * rq.size()));
+        TB_CUDA(cudaMemcpy(r->d_rq, rq.data(), sizeof(int32_t) * rq.size(), cudaMemcpyHostToDevice));
+    }
+    TB_CUDA(cudaMalloc(&r->d_mult, sizeof(int32_t) * a->channels));
+    TB_CUDA(cudaMalloc(&r->d_shift, sizeof(int32_t) * a->channels));
+    TB_CUDA(cudaMemcpy(r->d_mult, m.data(), sizeof(int32_t) * a->channels, cudaMemcpyHostToDevice));
+    TB_CUDA(cudaMemcpy(r->d_shift, s.data(), sizeof(int32_t) * a->channels, cudaMemcpyHostToDevice));
+    return TB_OK;
+}
+
+void free_rescale_plan(RescalePlan* r) {
+    if (r->d_mult) cudaFree(r->d_mult);
+    if (r->d_shift) cudaFree(r->d_shift);
+    if (r->d_rq) cudaFree(r->d_rq);
+    r->d_mult = r->d_shift = r->d_rq = nullptr;
+}
+
+static RescaleArgs rescale_args(const RescalePlan& r) {
+    RescaleArgs a;
+    a.multiplier = r.d_mult;
+    a.shift = r.d_shift;
+    a.per_channel = r.per_channel;
+    a.scale32 = r.scale32;
+    a.rounding = r.rounding;
+    a.out_zp = r.out_zp;
+    a.lo = r.lo;
+    a.hi = r.hi;
+    return a;
+}
+
+static IntEpiDev int_epi(const RescalePlan& r) {
+    IntEpiDev e;
+    e.rescale = r.enabled ? 1 : 0;
+    e.rs = rescale_args(r);
+    e.out_dtype = r.enabled ? r.out_dtype : TB_DT_INT32;
+    return e;
+}
+
+// ---------------------------------------------------------------------------
+// Tensor-core GEMM launch (one instantiation per tile configuration)
+// ---------------------------------------------------------------------------
+
+// Tensor-core GEMM launches live in gemm_i8_mm.cu, gemm_i8_conv.cu and gemm_f16.cu
+// (one translation unit per family so they compile in parallel).
+
+}  // namespace tb
+
+using namespace tb;
+
+// ===========================================================================
+// C ABI: context
+// ===========================================================================
+
+extern "C" {
+
+TB_API const char* tb_last_error(void) { return g_last_error.c_str(); }
+
+TB_API tb_status tb_context_create(int device, tb_context** out) {
+    if (!out) return fail(TB_ERR_INVALID_ARGUMENT, "null output pointer");
+    *out = nullptr;
+    int count = 0;
+    TB_CUDA(cudaGetDeviceCount(&count));
+    if (device < 0 || device >= count) return fail(TB_ERR_INVALID_ARGUMENT, "no CUDA device %d", device);
+    TB_CUDA(cudaSetDevice(device));
+    cudaDeviceProp prop;
+    TB_CUDA(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10)
+        return fail(TB_ERR_NOT_ACCELERATED, "device %d is sm_%d%d; this library is built for sm_100a", device,
+                    prop.major, prop.minor);
+    tb_context* ctx = new tb_context;
+    ctx->device = device;
+    ctx->num_sms = prop.multiProcessorCount;
+    double ms = 2000.0;
+    if (const char* env = getenv("TB_WAIT_TIMEOUT_MS")) ms = atof(env);
+    ctx->timeout_cycles = static_cast<long long>(ms * 1e-3 * prop.clockRate * 1e3);
+    cudaError_t e = cudaMalloc(&ctx->dev_err, sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMemset(ctx->dev_err, 0, sizeof(uint32_t));
+    if (e != cudaSuccess) {
+        delete ctx;
+        return fail(TB_ERR_CUDA, "error-word allocation failed: %s", cudaGetErrorString(e));
+    }
+    if (const char* env = getenv("TB_TRACE")) {
+        if (atoi(env) && cudaMalloc(&ctx->trace, 512 * sizeof(long long)) == cudaSuccess)
+            cudaMemset(ctx->trace, 0, 512 * sizeof(long long));
+    }
+    *out = ctx;
+    return TB_OK;
+}
+
+TB_API tb_status tb_debug_trace(tb_context* ctx, long long* host512) {
+    if (!ctx || !host512) return fail(TB_ERR_INVALID_ARGUMENT, "null argument");
+    if (!ctx->trace) return fail(TB_ERR_INVALID_ARGUMENT, "context created without TB_TRACE=1");
+    TB_CUDA(cudaMemcpy(host512, ctx->trace, 512 * sizeof(long long), cudaMemcpyDeviceToHost));
+    return TB_OK;
+}
+
+TB_API void tb_context_destroy(tb_context* ctx) {
+    if (!ctx) return;
+    cudaSetDevice(ctx->device);
+    if (ctx->dev_err) cudaFree(ctx->dev_err);
+    if (ctx->trace) cudaFree(ctx->trace);
+    delete ctx;
+}
+
+TB_API tb_status tb_synchronize(tb_context* ctx, void* stream) {
+    if (!ctx) return fail(TB_ERR_INVALID_ARGUMENT, "null context");
+    TB_CUDA(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+    uint32_t word = 0;
+    TB_CUDA(cudaMemcpy(&word, ctx->dev_err, sizeof word, cudaMemcpyDeviceToHost));
+    if (word) {
+        TB_CUDA(cudaMemset(ctx->dev_err, 0, sizeof(uint32_t)));
+        if (word & DEV_ERR_TIMEOUT) return fail(TB_ERR_TIMEOUT, "a device wait timed out (error word 0x%x)", word);
+        if (word & DEV_ERR_SCALE)
+            return fail(TB_ERR_GRAPH, "apply_scale: value out of range for the shift, or result exceeds int32");
+        return fail(TB_ERR_GRAPH, "device error word 0x%x", word);
+    }
+    return TB_OK;
+}
+
+TB_API tb_status tb_malloc(tb_context* ctx, size_t bytes, void** dptr) {
+    if (!ctx || !dptr) return fail(TB_ERR_INVALID_ARGUMENT, "null argument");
+    TB_CUDA(cudaMalloc(dptr, bytes ? bytes : 1));
+    return TB_OK;
+}
+
+TB_API tb_status tb_free(tb_context* ctx, void* dptr) {
+    if (!ctx) return fail(TB_ERR_INVALID_ARGUMENT, "null context");
+    if (dptr) TB_CUDA(cudaFree(dptr));
+    return TB_OK;
+}
+
+TB_API tb_status tb_memcpy_h2d(tb_context* ctx, void* dst, const void* src, size_t bytes, void* stream) {
+    if (!ctx) return fail(TB_ERR_INVALID_ARGUMENT, "null context");
+    TB_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, static_cast<cudaStream_t>(stream)));
+    return TB_OK;
+}
+
+TB_API tb_status tb_memcpy_d2h(tb_context* ctx, void* dst, const void* src, size_t bytes, void* stream) {
+    if (!ctx) return fail(TB_ERR_INVALID_ARGUMENT, "null context");
+    TB_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, static_cast<cudaStream_t>(stream)));
+    return TB_OK;
+}
+
+TB_API uint64_t tb_launch_count(tb_context* ctx) { return ctx ? ctx->launches : 0; }
+
+}  // extern "C"
+
+// ===========================================================================
+// MATMUL
+// ===========================================================================
+
+struct tb_matmul_plan {
+    tb_context* ctx = nullptr;
+    tb_matmul_desc d{};
+    int path = 0;  // 0 TC int8, 1 TC f16/bf16, 2 direct int, 3 direct float
+    RescalePlan rs;
+    int bn = 256;
+    int32_t* d_colterm = nullptr;  // [n][w] (+ one tile of padding) when a_zp != 0
+    unsigned int* d_counter = nullptr;  // column-sum units finished, grows by `units` per run
+    unsigned int epoch = 0;
+    const void* a_cached = nullptr;
+    const void* b_cached = nullptr;
+    CUtensorMap tmA, tmB;
+};
+
+extern "C" TB_API tb_status tb_matmul_plan_create(tb_context* ctx, const tb_matmul_desc* d,
+                                                  const tb_rescale_attr* rescale, tb_matmul_plan** out) {
+    if (!ctx || !d || !out) return fail(TB_ERR_INVALID_ARGUMENT, "null argument");
+    *out = nullptr;
+    TB_CUDA(cudaSetDevice(ctx->device));
+    if (d->n < 0 || d->h < 0 || d->c < 0 || d->w < 0) return fail(TB_ERR_SHAPE_MISMATCH, "MATMUL: negative dimension");
+    // matmul_types (src/ops/matmul.rs:30-38), restricted to what runs here.
+    const int at = d->a_dtype, bt = d->b_dtype, ot = d->out_dtype;
+    const bool int8 = at == TB_DT_INT8 && bt == TB_DT_INT8 && ot == TB_DT_INT32;
+    const bool fl = (at == bt) && (at == TB_DT_BF16 || at == TB_DT_FP16) && ot == TB_DT_FP32;
+    const bool valid_other = (at == TB_DT_INT16 && bt == TB_DT_INT16 && ot == TB_DT_INT48) ||
+                             (at == TB_DT_FP16 && bt == TB_DT_FP16 && ot == TB_DT_FP16) ||
+                             (at == TB_DT_FP32 && bt == TB_DT_FP32 && ot == TB_DT_FP32);
+    if (!int8 && !fl) {
+        if (valid_other) return fail(TB_ERR_NOT_ACCELERATED, "MATMUL types %d x %d -> %d are not accelerated", at, bt, ot);
+        return fail(TB_ERR_DTYPE_MISMATCH, "MATMUL: unsupported types a=%d b=%d output=%d", at, bt, ot);
+    }
+    if (int8) {
+        if ((d->a_zp != 0 && at != TB_DT_INT8) || (d->b_zp != 0 && bt != TB_DT_INT8))
+            return fail(TB_ERR_GRAPH, "MATMUL: zero points must be zero for non-int8 inputs");
+    } else if (d->a_zp != 0 || d->b_zp != 0) {
+        return fail(TB_ERR_GRAPH, "MATMUL: zero points must be zero for floating-point inputs");
+    }
+    if (rescale && !int8) return fail(TB_ERR_DTYPE_MISMATCH, "MATMUL: RESCALE needs an integer result");
+    tb_matmul_plan* p = new tb_matmul_plan;
+    p->ctx = ctx;
+    p->d = *d;
+    if (rescale) {
+        tb_status s = make_rescale_plan(ctx, rescale, TB_DT_INT32, d->w, &p->rs);
+        if (s != TB_OK) { delete p; return s; }
+    }
+    const int e = int8 ? 1 : 2;
+    const bool tma_ok = (static_cast<long long>(d->c) * e) % 16 == 0 && (static_cast<long long>(d->w) * e) % 16 == 0 &&
+                        d->c > 0 && d->w > 0 && d->h > 0 && d->n > 0;
+    p->path = tma_ok ? (int8 ? 0 : 1) : (int8 ? 2 : 3);
+    p->bn = d->w <= 128 ? 128 : 256;
+    if (p->path == 0 && d->a_zp != 0) {
+        // padded by one tile: the epilogue reads whole 32-column chunks without clamping
+        cudaError_t ce = cudaMalloc(&p->d_colterm, sizeof(int32_t) * (static_cast<size_t>(d->n) * d->w + 256));
+        if (ce == cudaSuccess) ce = cudaMalloc(&p->d_counter, sizeof(unsigned int));
+        if (ce == cudaSuccess) ce = cudaMemset(p->d_counter, 0, sizeof(unsigned int));
+        if (ce != cudaSuccess) { free_rescale_plan(&p->rs); delete p; return fail(TB_ERR_CUDA, "colterm alloc failed"); }
+    }
+    *out = p;
+    return TB_OK;
+}
+
+extern "C" TB_API tb_status tb_matmul_plan_run(tb_matmul_plan* p, const void* a, const void* b, void* out,
+                                               void* stream_) {
+    if (!p || !a || !b || !out) return fail(TB_ERR_INVALID_ARGUMENT, "null argument");
+    tb_context* ctx = p->ctx;
+    cudaStream_t st = static_cast<cudaStream_t>(stream_);
+    const tb_matmul_desc& d = p->d;
+    const long long total = static_cast<long long>(d.n) * d.h * d.w;
+    if (total == 0) return TB_OK;
+    if (p->path >= 2 || !aligned16(a) || !aligned16(b)) {
+        if (d.a_dtype == TB_DT_INT8) {
+            matmul_direct_int<<<grid_for(ctx, total), 256, 0, st>>>(d.n, d.h, d.c, d.w, static_cast<const int8_t*>(a),
+                                                                    static_cast<const int8_t*>(b), d.a_zp, d.b_zp,
+                                                                    int_epi(p->rs), out, ctx->dev_err);
+        } else {
+            matmul_direct_float<<<grid_for(ctx, total), 256, 0, st>>>(d.n, d.h, d.c, d.w, a, b, d.a_dtype,
+                                                                      TB_DT_FP32, out);
+        }
+        TB_LAUNCHED(ctx);
+        return TB_OK;
+    }
+    const int e = p->path == 0 ? 1 : 2;
+    if (a != p->a_cached) {
+        const uint64_t dims[3] = {static_cast<uint64_t>(d.c), static_cast<uint64_t>(d.h), static_cast<uint64_t>(d.n)};
+        const uint64_t str[2] = {static_cast<uint64_t>(d.c) * e, static_cast<uint64_t>(d.c) * d.h * e};
+        const uint32_t box[3] = {static_cast<uint32_t>(128 / e), 128, 1};
+        TB_TRY(encode_tiled(&p->tmA, tmap_dtype(d.a_dtype), 3, a, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B));
+        p->a_cached = a;
+    }
+    if (b != p->b_cached) {
+        const uint64_t dims[3] = {static_cast<uint64_t>(d.w), static_cast<uint64_t>(d.c), static_cast<uint64_t>(d.n)};
+        const uint64_t str[2] = {static_cast<uint64_t>(d.w) * e, static_cast<uint64_t>(d.w) * d.c * e};
+        const uint32_t box[3] = {static_cast<uint32_t>(128 / e), static_cast<uint32_t>(128 / e), 1};
+        TB_TRY(encode_tiled(&p->tmB, tmap_dtype(d.b_dtype), 3, b, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B));
+        p->b_cached = b;
+    }
+    GemmParams gp{};
+    gp.M = d.h;
+    gp.N = d.w;
+    gp.K = d.c;
+    gp.batch = d.n;
+    gp.in_bf16 = d.a_dtype == TB_DT_BF16;
+    gp.k_blocks = (d.c + (128 / e) - 1) / (128 / e);
+    gp.out = out;
+    gp.out_batch_stride = static_cast<long long>(d.h) * d.w;
+    gp.ldo = d.w;
+    GemmEpilogue& ep = gp.epi;
+    if (p->path == 0) {
+        if (d.a_zp != 0) {
+            // colterm = -a_zp * colsum(B) + c * a_zp * b_zp, reduced inside the GEMM by the epilogue warps
+            // during the first main loop (cooperative launch; see ColsumJob).
+            const int32_t cst = static_cast<int32_t>(static_cast<uint32_t>(d.c) * static_cast<uint32_t>(d.a_zp) *
+                                                     static_cast<uint32_t>(d.b_zp));
+            ColsumJob& cs = gp.cs;
+            cs.b = static_cast<const int8_t*>(b);
+            cs.c = d.c;
+            cs.w = d.w;
+            cs.units = d.n * ((d.w + 63) / 64);
+            cs.scale = -d.a_zp;
+            cs.add = cst;
+            cs.out = p->d_colterm;
+            cs.counter = p->d_counter;
+            if (static_cast<unsigned long long>(p->epoch + 1) * cs.units >= (1ull << 31)) {
+                TB_CUDA(cudaMemsetAsync(p->d_counter, 0, sizeof(unsigned int), st));
+                p->epoch = 0;
+            }
+            p->epoch += 1;
+            cs.target = p->epoch * static_cast<unsigned int>(cs.units);
+            ep.colterm = p->d_colterm;
+            ep.colterm_bstride = d.w;
+        }
+        ep.row_zp_neg = -d.b_zp;
+        if (p->rs.enabled) {
+            ep.mode = EPI_RESCALE;
+            ep.rs = rescale_args(p->rs);
+            ep.rs_fast = p->rs.fast;
+            ep.rs_zp_folded = p->rs.zp_folded;
+            ep.rq = reinterpret_cast<const int4*>(p->rs.d_rq);
+            ep.out_dtype = p->rs.out_dtype;
+        } else {
+            ep.mode = EPI_I32;
+            ep.out_dtype = TB_DT_INT32;
+        }
+        return launch_i8_matmul(ctx, p->bn, epilogue_kind(ep), p->tmA, p->tmB, gp, st);
+    }
+    ep.mode = EPI_F32;
+    ep.out_dtype = TB_DT_FP32;
+    return launch_f16_matmul(ctx, p->bn, p->tmA, p->tmB, gp, st);
+}
+
+extern "C" TB_API void tb_matmul_plan_destroy(tb_matmul_plan* p) {
+    if (!p) return;
+    free_rescale_plan(&p->rs);
+    if (p->d_colterm) cudaFree(p->d_colterm);
+    if (p->d_counter) cudaFree(p->d_counter);
+    delete p;
+}
+
+extern "C" TB_API tb_status tb_matmul(tb_context* ctx, const tb_matmul_desc* d, const tb_rescale_attr* rescale,
+                                      const void* a, const void* b, void* out, void* stream) {
+    tb_matmul_plan* p = nullptr;
+    TB_TRY(tb_matmul_plan_create(ctx, d, rescale, &p));
+    tb_status s = tb_matmul_plan_run(p, a, b, out, stream);
+    // The plan's device buffers may still be read by queued kernels.
+    cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+    tb_matmul_plan_destroy(p);
+    return s;
+}
+
+// ===========================================================================
+// CONV2D / DEPTHWISE_CONV2D
+// ===========================================================================
+
+struct tb_conv2d_plan {
+    tb_context* ctx = nullptr;
+    tb_conv2d_desc d{};
+    bool depthwise = false;
+    int oh = 0, ow = 0;
+    int path = 0;  // 0 TC int8, 1 TC f16/bf16, 2 direct int, 3 direct float, 4 dw int vec4, 5 dw int, 6 dw float
+    const void* weight = nullptr;
+    const void* bias = nullptr;
+    RescalePlan rs;
+    int bn = 64, bk = 128;
+    int32_t* d_colterm = nullptr;   // [n_classes][ct_ld] column terms of each border class
+    int32_t* d_ctdelta = nullptr;   // [n_classes][ct_ld] class terms minus the base class's
+    long long ct_ld = 0;            // output channels padded to whole 256-column tiles
+    int base_class = 0;             // the interior class (all taps valid) when there is one
+    uint8_t* d_rowclass = nullptr;
+    uint8_t* d_colclass = nullptr;
+    int n_cx = 1;
+    const void* in_cached = nullptr;
+    CUtensorMap tmA, tmB;
+    float* d_fbias = nullptr;  // float bias widened to f32
+};
+
+static tb_status conv_extent(const char* op, int in, int pb, int pa, int k, int dil, int stride, int* out) {
+    // src/ops/conv.rs:54-75
+    const long long full = static_cast<long long>(in) - 1 + pb + pa - static_cast<long long>(k - 1) * dil;
+    if (full % stride != 0) return fail(TB_ERR_GRAPH, "%s: parameters must yield exact integer output dimensions", op);
+    const long long o = full / stride + 1;
+    if (o < 1) return fail(TB_ERR_GRAPH, "%s: output dimension %lld must be positive", op, o);
+    *out = static_cast<int>(o);
+    return TB_OK;
+}
+
+// Valid tap range [lo, hi] of output position o (possibly empty: lo > hi).
+static void tap_range(int o, int stride, int pad, int dil, int k, int in, int* lo, int* hi) {
+    int l = 0, h = k - 1;
+    while (l <= h && o * stride + l * dil - pad < 0) ++l;
+    while (h >= l && o * stride + h * dil - pad >= in) --h;
+    *lo = l;
+    *hi = h;
+}
+
+static tb_status conv_plan_create(tb_context* ctx, const tb_conv2d_desc* d, const void* weight, const void* bias,
+                                  const tb_rescale_attr* rescale, bool depthwise, tb_conv2d_plan** out) {
+    if (!ctx || !d || !out || !weight || !bias) return fail(TB_ERR_INVALID_ARGUMENT, "null argument");
+    *out = nullptr;
+    TB_CUDA(cudaSetDevice(ctx->device));
+    const char* op = depthwise ? "DEPTHWISE_CONV2D" : "CONV2D";
+    // conv.rs:77-92 attribute checks
+    for (int i = 0; i < 4; ++i)
+        if (d->pad[i] < 0) return fail(TB_ERR_GRAPH, "%s: pad must be non-negative", op);
+    for (int i = 0; i < 2; ++i) {
+        if (d->stride[i] < 1) return fail(TB_ERR_GRAPH, "%s: stride must be at least 1", op);
+        if (d->dilation[i] < 1) return fail(TB_ERR_GRAPH, "%s: dilation must be at least 1", op);
+    }
+    const int oc = depthwise ? d->ic * d->m : d->oc;
+    if (depthwise && d->m < 1) return fail(TB_ERR_SHAPE_MISMATCH, "%s: channel multiplier must be positive", op);
+    int oh = 0, ow = 0;
+    TB_TRY(conv_extent(op, d->ih, d->pad[0], d->pad[1], d->kh, d->dilation[0], d->stride[0], &oh));
+    TB_TRY(conv_extent(op, d->iw, d->pad[2], d->pad[3], d->kw, d->dilation[1], d->stride[1], &ow));
+    if (d->bias_len != oc && d->bias_len != 1)
+        return fail(TB_ERR_SHAPE_MISMATCH, "%s: bias channels %d must be 1 or match output channels %d", op,
+                    d->bias_len, oc);
+    const int it = d->in_dtype, wt = d->w_dtype, at = d->acc_dtype, ot = d->out_dtype;
+    const bool int8 = it == TB_DT_INT8 && (wt == TB_DT_INT8 || wt == TB_DT_INT4) && at == TB_DT_INT32 &&
+                      ot == TB_DT_INT32;
+    // float: the tables admit (F16,F16,F32,F16|F32) and (BF16,BF16,F32,BF16|F32) for CONV2D and
+    // (F16,F16,F32,F16), (BF16,BF16,F32,BF16) for DEPTHWISE; only fp32 accumulation runs here.
+    bool fl = it == wt && (it == TB_DT_BF16 || it == TB_DT_FP16) && at == TB_DT_FP32 &&
+              (ot == it || (!depthwise && ot == TB_DT_FP32));
+    if (!int8 && !fl) return fail(TB_ERR_NOT_ACCELERATED, "%s types in=%d w=%d acc=%d out=%d are not accelerated", op,
+                                  it, wt, at, ot);
+    if (int8) {
+        if (d->weight_zp != 0 && wt != TB_DT_INT8)
+            return fail(TB_ERR_GRAPH, "%s: weight zero point must be zero for non-int8 weight", op);
+    } else if (d->input_zp != 0 || d->weight_zp != 0) {
+        return fail(TB_ERR_GRAPH, "%s: zero points must be zero for floating-point operands", op);
+    }
+    if (rescale && !int8) return fail(TB_ERR_DTYPE_MISMATCH, "%s: RESCALE needs an integer result", op);
+
+    tb_conv2d_plan* p = new tb_conv2d_plan;
+    p->ctx = ctx;
+    p->d = *d;
+    p->d.oc = oc;
+    p->depthwise = depthwise;
+    p->oh = oh;
+    p->ow = ow;
+    p->weight = weight;
+    p->bias = bias;
+    auto bail = [&](tb_status s) {
+        tb_conv2d_plan_destroy(p);
+        return s;
+    };
+    if (rescale) {
+        tb_status s = make_rescale_plan(ctx, rescale, TB_DT_INT32, oc, &p->rs);
+        if (s != TB_OK) return bail(s);
+    }
+    if (depthwise) {
+        p->path = int8 ? ((d->m == 1 && d->ic % 4 == 0) ? 4 : 5) : 6;
+        *out = p;
+        return TB_OK;
+    }
+    const int e = int8 ? 1 : 2;
+    const long long taps = static_cast<long long>(d->kh) * d->kw;
+    const bool tma_ok = (static_cast<long long>(d->ic) * e) % 16 == 0 && d->n > 0 && oh > 0 && ow > 0 &&
+                        d->pad[0] <= 127 && d->pad[2] <= 127 && d->kw * d->dilation[1] < 256 &&
+                        d->kh * d->dilation[0] < 256 && (taps * d->ic * e) % 16 == 0 && oh <= 255 && ow <= 255 &&
+                        aligned16(weight);
+    p->path = tma_ok ? (int8 ? 0 : 1) : (int8 ? 2 : 3);
+    if (p->path == 1) {
+        // float bias widened once (the epilogue adds it in f32)
+        cudaError_t ce = cudaMalloc(&p->d_fbias, sizeof(float) * d->bias_len);
+        if (ce != cudaSuccess) return bail(fail(TB_ERR_CUDA, "bias alloc failed"));
+    }
+    if (p->path >= 2) { *out = p; return TB_OK; }
+
+    p->bn = oc <= 64 ? 64 : oc <= 128 ? 128 : 256;
+    p->bk = (int8 && d->ic <= 64) ? 64 : 128;
+    const int bke = p->bk / e;
+    // Weight tensor map: [OC][KH*KW*IC], K-major.
+    {
+        const uint64_t K = static_cast<uint64_t>(taps) * d->ic;
+        const uint64_t dims[3] = {K, static_cast<uint64_t>(oc), 1};
+        const uint64_t str[2] = {K * e, K * e * oc};
+        const uint32_t box[3] = {static_cast<uint32_t>(bke), static_cast<uint32_t>(p->bn), 1};
+        tb_status s = encode_tiled(&p->tmB, tmap_dtype(wt), 3, weight, dims, str, box,
+                                   p->bk == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+        if (s != TB_OK) return bail(s);
+    }
+    if (p->path == 1) {
+        // bias of the output type -> f32 table (exact)
+        std::vector<float> fb(d->bias_len);
+        std::vector<uint16_t> raw(d->bias_len);
+        std::vector<float> raw32(d->bias_len);
+        cudaError_t ce;
+        if (ot == TB_DT_FP32) ce = cudaMemcpy(fb.data(), bias, sizeof(float) * d->bias_len, cudaMemcpyDeviceToHost);
+        else {
+            ce = cudaMemcpy(raw.data(), bias, sizeof(uint16_t) * d->bias_len, cudaMemcpyDeviceToHost);
+            for (int i = 0; i < d->bias_len; ++i) {
+                if (ot == TB_DT_BF16) {
+                    uint32_t u = static_cast<uint32_t>(raw[i]) << 16;
+                    memcpy(&fb[i], &u, 4);
+                } else {
+                    __half h;
+                    memcpy(&h, &raw[i], 2);
+                    fb[i] = __half2float(h);
+                }
+            }
+        }
+        if (ce == cudaSuccess) ce = cudaMemcpy(p->d_fbias, fb.data(), sizeof(float) * d->bias_len, cudaMemcpyHostToDevice);
+        if (ce != cudaSuccess) return bail(fail(TB_ERR_CUDA, "bias upload failed"));
+        *out = p;
+        return TB_OK;
+    }
+    // Integer: border classes and the per-class column terms.
+    std::vector<int> ky_r, kx_r;
+    std::vector<uint8_t> rowc(oh), colc(ow);
+    auto classify = [](int n_out, int stride, int pad, int dil, int k, int in, std::vector<int>& ranges,
+                       std::vector<uint8_t>& cls) {
+        for (int o = 0; o < n_out; ++o) {
+            int lo, hi;
+            tap_range(o, stride, pad, dil, k, in, &lo, &hi);
+            int found = -1;
+            for (size_t c = 0; c < ranges.size() / 2; ++c)
+                if (ranges[2 * c] == lo && ranges[2 * c + 1] == hi) { found = static_cast<int>(c); break; }
+            if (found < 0) {
+                found = static_cast<int>(ranges.size() / 2);
+                ranges.push_back(lo);
+                ranges.push_back(hi);
+            }
+            cls[o] = static_cast<uint8_t>(found);
+        }
+    };
+    classify(oh, d->stride[0], d->pad[0], d->dilation[0], d->kh, d->ih, ky_r, rowc);
+    classify(ow, d->stride[1], d->pad[2], d->dilation[1], d->kw, d->iw, kx_r, colc);
+    const int n_ry = static_cast<int>(ky_r.size() / 2), n_rx = static_cast<int>(kx_r.size() / 2);
+    if (n_ry > 255 || n_rx > 255) return bail(fail(TB_ERR_NOT_ACCELERATED, "%s: too many border classes", op));
+    p->n_cx = n_rx;
+    int ry_full = 0, rx_full = 0;
+    for (int c = 0; c < n_ry; ++c)
+        if (ky_r[2 * c] == 0 && ky_r[2 * c + 1] == d->kh - 1) ry_full = c;
+    for (int c = 0; c < n_rx; ++c)
+        if (kx_r[2 * c] == 0 && kx_r[2 * c + 1] == d->kw - 1) rx_full = c;
+    p->base_class = ry_full * n_rx + rx_full;
+    p->ct_ld = (static_cast<long long>(oc) + 255) / 256 * 256;
+    int32_t* d_wsum = nullptr;
+    int* d_ranges = nullptr;
+    const size_t tab = sizeof(int32_t) * static_cast<size_t>(n_ry) * n_rx * p->ct_ld;
+    cudaError_t ce = cudaMalloc(&p->d_colterm, tab);
+    if (ce == cudaSuccess) ce = cudaMalloc(&p->d_ctdelta, tab);
+    if (ce == cudaSuccess) ce = cudaMalloc(&p->d_rowclass, oh);
+    if (ce == cudaSuccess) ce = cudaMalloc(&p->d_colclass, ow);
+    if (ce == cudaSuccess) ce = cudaMalloc(&d_wsum, sizeof(int32_t) * oc * taps);
+    if (ce == cudaSuccess) ce = cudaMalloc(&d_ranges, sizeof(int) * (ky_r.size() + kx_r.size()));
+    if (ce == cudaSuccess) ce = cudaMemcpy(p->d_rowclass, rowc.data(), oh, cudaMemcpyHostToDevice);
+    if (ce == cudaSuccess) ce = cudaMemcpy(p->d_colclass, colc.data(), ow, cudaMemcpyHostToDevice);
+    if (ce == cudaSuccess) ce = cudaMemcpy(d_ranges, ky_r.data(), sizeof(int) * ky_r.size(), cudaMemcpyHostToDevice);
+    if (ce == cudaSuccess)
+        ce = cudaMemcpy(d_ranges + ky_r.size(), kx_r.data(), sizeof(int) * kx_r.size(), cudaMemcpyHostToDevice);
+    if (ce != cudaSuccess) {
+        if (d_wsum) cudaFree(d_wsum);
+        if (d_ranges) cudaFree(d_ranges);
+        return bail(fail(TB_ERR_CUDA, "conv plan allocation failed: %s", cudaGetErrorString(ce)));
+    }
+    conv_weight_tap_sums<<<grid_for(ctx, oc * taps), 256>>>(oc, static_cast<int>(taps), d->ic,
+                                                            static_cast<const int8_t*>(weight), d_wsum);
+    conv_colterm<<<grid_for(ctx, static_cast<long long>(n_ry) * n_rx * p->ct_ld), 256>>>(
+        oc, p->ct_ld, d->kh, d->kw, d->ic, n_ry, n_rx, p->base_class, d_ranges, d_ranges + ky_r.size(), d_wsum,
+        static_cast<const int32_t*>(bias), d->bias_len, d->input_zp, d->weight_zp, p->d_colterm, p->d_ctdelta);
+    ce = cudaDeviceSynchronize();
+    cudaFree(d_wsum);
+    cudaFree(d_ranges);
+    ctx->launches += 2;
+    if (ce != cudaSuccess) return bail(fail(TB_ERR_CUDA, "conv plan kernels failed: %s", cudaGetErrorString(ce)));
+    *out = p;
+    return TB_OK;
+}
+
+extern "C" TB_API tb_status tb_conv2d_plan_create(tb_context* ctx, const tb_conv2d_desc* d, const void* weight,
+                                                  const void* bias, const tb_rescale_attr* rescale,
+                                                  tb_conv2d_plan** out) {
+    return conv_plan_create(ctx, d, weight, bias, rescale, false, out);
+}
+
+extern "C" TB_API tb_status tb_depthwise_conv2d_plan_create(tb_context* ctx, const tb_conv2d_desc* d,
+                                                            const void* weight, const void* bias,
+                                                            const tb_rescale_attr* rescale, tb_conv2d_plan** out) {
+    return conv_plan_create(ctx, d, weight, bias, rescale, true, out);
+}
+
+extern "C" TB_API tb_status tb_conv2d_plan_run(tb_conv2d_plan* p, const void* input, void* out, void* stream_) {
+    if (!p || !input || !out) return fail(TB_ERR_INVALID_ARGUMENT, "null argument");
+    tb_context* ctx = p->ctx;
+    cudaStream_t st = static_cast<cudaStream_t>(stream_);
+    const tb_conv2d_desc& d = p->d;
+    ConvGeomDev g;
+    g.n = d.n; g.ih = d.ih; g.iw = d.iw; g.ic = d.ic; g.oc = d.oc; g.kh = d.kh; g.kw = d.kw;
+    g.oh = p->oh; g.ow = p->ow; g.m = d.m;
+    g.pad_t = d.pad[0]; g.pad_l = d.pad[2]; g.sh = d.stride[0]; g.sw = d.stride[1];
+    g.dh = d.dilation[0]; g.dw = d.dilation[1];
+    const long long total = static_cast<long long>(d.n) * p->oh * p->ow * d.oc;
+    if (total == 0) return TB_OK;
+    int path = p->path;
+    if (path <= 1 && !aligned16(input)) path = path == 0 ? 2 : 3;
+    switch (path) {
+    case 2:
+        conv2d_direct_int<<<grid_for(ctx, total), 256, 0, st>>>(g, static_cast<const int8_t*>(input),
+                                                                static_cast<const int8_t*>(p->weight),
+                                                                static_cast<const int32_t*>(p->bias), d.bias_len,
+                                                                d.input_zp, d.weight_zp, int_epi(p->rs), out,
+                                                                ctx->dev_err);
+        TB_LAUNCHED(ctx);
+        return TB_OK;
+    case 3:
+        conv2d_direct_float<<<grid_for(ctx, total), 256, 0, st>>>(g, input, p->weight, p->bias, d.bias_len, d.in_dtype,
+                                                                  d.w_dtype, d.out_dtype, out);
+        TB_LAUNCHED(ctx);
+        return TB_OK;
+    case 4:
+        depthwise_int_vec4<<<grid_for(ctx, total / 4), 256, 0, st>>>(g, static_cast<const int8_t*>(input),
+                                                                    static_cast<const int8_t*>(p->weight),
+                                                                    static_cast<const int32_t*>(p->bias), d.bias_len,
+                                                                    d.input_zp, d.weight_zp, int_epi(p->rs), out,
+                                                                    ctx->dev_err);
+        TB_LAUNCHED(ctx);
+        return TB_OK;
+    case 5:
+        depthwise_int_generic<<<grid_for(ctx, total), 256, 0, st>>>(g, static_cast<const int8_t*>(input),
+                                                                   static_cast<const int8_t*>(p->weight),
+                                                                   static_cast<const int32_t*>(p->bias), d.bias_len,
+                                                                   d.input_zp, d.weight_zp, int_epi(p->rs), out,
+                                                                   ctx->dev_err);
+        TB_LAUNCHED(ctx);
+        return TB_OK;
+    case 6:
+        depthwise_float<<<grid_for(ctx, total), 256, 0, st>>>(g, input, p->weight, p->bias, d.bias_len, d.in_dtype,
+                                                              d.out_dtype, out);
+        TB_LAUNCHED(ctx);
+        return TB_OK;
+    default: break;
+    }
+    const int e = path == 0 ? 1 : 2;
+    const int bke = p->bk / e;
+    if (input != p->in_cached) {
+        const uint64_t dims[4] = {static_cast<uint64_t>(d.ic), static_cast<uint64_t>(d.iw), static_cast<uint64_t>(d.ih),
+                                  static_cast<uint64_t>(d.n)};
+        const uint64_t str[3] = {static_cast<uint64_t>(d.ic) * e, static_cast<uint64_t>(d.ic) * d.iw * e,
+                                 static_cast<uint64_t>(d.ic) * d.iw * d.ih * e};
+        const int lower[2] = {-d.pad[2], -d.pad[0]};
+        const int upper[2] = {d.pad[3] - (d.kw - 1) * d.dilation[1], d.pad[1] - (d.kh - 1) * d.dilation[0]};
+        const uint32_t es[4] = {1, static_cast<uint32_t>(d.stride[1]), static_cast<uint32_t>(d.stride[0]), 1};
+        TB_TRY(encode_im2col(&p->tmA, tmap_dtype(d.in_dtype), input, dims, str, lower, upper,
+                             static_cast<uint32_t>(bke), 128, es,
+                             p->bk == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B));
+        p->in_cached = input;
+    }
+    GemmParams gp{};
+    gp.M = d.n * p->oh * p->ow;
+    gp.N = d.oc;
+    gp.K = d.kh * d.kw * d.ic;
+    gp.batch = 1;
+    gp.in_bf16 = d.in_dtype == TB_DT_BF16;
+    gp.c_blocks = (d.ic + bke - 1) / bke;
+    gp.k_blocks = d.kh * d.kw * gp.c_blocks;
+    gp.conv_OW = p->ow;
+    gp.conv_OHOW = p->oh * p->ow;
+    gp.stride_h = d.stride[0];
+    gp.stride_w = d.stride[1];
+    gp.pad_t = d.pad[0];
+    gp.pad_l = d.pad[2];
+    gp.KW = d.kw;
+    gp.dil_h = d.dilation[0];
+    gp.dil_w = d.dilation[1];
+    gp.IC = d.ic;
+    gp.out = out;
+    gp.out_batch_stride = 0;
+    gp.ldo = d.oc;
+    GemmEpilogue& ep = gp.epi;
+    if (path == 1) {
+        ep.mode = EPI_FCONV;
+        ep.out_dtype = d.out_dtype;
+        ep.fbias = p->d_fbias;
+        ep.fbias_len = d.bias_len;
+        return launch_f16_conv(ctx, p->bn, p->tmA, p->tmB, gp, st);
+    }
+    ep.colterm = p->d_colterm + static_cast<long long>(p->base_class) * p->ct_ld;
+    ep.colterm_bstride = 0;
+    ep.ct_delta = p->d_ctdelta;
+    ep.ct_ld = p->ct_ld;
+    ep.base_class = p->base_class;
+    ep.rowclass = p->d_rowclass;
+    ep.colclass = p->d_colclass;
+    ep.n_col_classes = p->n_cx;
+    ep.row_zp_neg = -d.weight_zp;
+    if (p->rs.enabled) {
+        ep.mode = EPI_RESCALE;
+        ep.rs = rescale_args(p->rs);
+        ep.rs_fast = p->rs.fast;
+        ep.rs_zp_folded = p->rs.zp_folded;
+        ep.rq = reinterpret_cast<const int4*>(p->rs.d_rq);
+        ep.out_dtype = p->rs.out_dtype;
+    } else {
+        ep.mode = EPI_I32;
+        ep.out_dtype = TB_DT_INT32;
+    }
+    return launch_i8_conv(ctx, p->bn, p->bk, epilogue_kind(ep), p->tmA, p->tmB, gp, st);
+}
+
+extern "C" TB_API void tb_conv2d_plan_destroy(tb_conv2d_plan* p) {
+    if (!p) return;
+    free_rescale_plan(&p->rs);
+    if (p->d_colterm) cudaFree(p->d_colterm);
+    if (p->d_ctdelta) cudaFree(p->d_ctdelta);
+    if (p->d_rowclass) cudaFree(p->d_rowclass);
+    if (p->d_colclass) cudaFree(p->d_colclass);
+    if (p->d_fbias) cudaFree(p->d_fbias);
+    delete p;
+}
+
+extern "C" TB_API tb_status tb_conv2d(tb_context* ctx, const tb_conv2d_desc* d, const tb_rescale_attr* rescale,
+                                      const void* input, const void* weight, const void* bias, void* out,
+                                      void* stream) {
+    tb_conv2d_plan* p = nullptr;
+    TB_TRY(tb_conv2d_plan_create(ctx, d, weight, bias, rescale, &p));
+    tb_status s = tb_conv2d_plan_run(p, input, out, stream);
+    cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+    tb_conv2d_plan_destroy(p);
+    return s;
+}
+
+extern "C" TB_API tb_status tb_depthwise_conv2d(tb_context* ctx, const tb_conv2d_desc* d,
+                                                const tb_rescale_attr* rescale, const void* input,
+                                                const void* weight, const void* bias, void* out, void* stream) {
+    tb_conv2d_plan* p = nullptr;
+    TB_TRY(tb_depthwise_conv2d_plan_create(ctx, d, weight, bias, rescale, &p));
+    tb_status s = tb_conv2d_plan_run(p, input, out, stream);
+    cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+    tb_conv2d_plan_destroy(p);
+    return s;
+}
+
+// ===========================================================================
+// Elementwise and pooling
+// ===========================================================================
+
+extern "C" TB_API tb_status tb_rescale(tb_context* ctx, const tb_rescale_attr* attr, int32_t in_dtype,
+                                       const void* input, int64_t count, void* out, void* stream_) {
+    if (!ctx || !attr || (count > 0 && (!input || !out))) return fail(TB_ERR_INVALID_ARGUMENT, "null argument");
+    if (in_dtype == TB_DT_INT48) return fail(TB_ERR_NOT_ACCELERATED, "RESCALE of INT48 input is not accelerated");
+    TB_CUDA(cudaSetDevice(ctx->device));
+    RescalePlan r;
+    int64_t izp = 0, ozp = 0;
+    int32_t lo, hi;
+    TB_TRY(check_rescale(attr, in_dtype, attr->channels, &izp, &ozp, &lo, &hi));
+    TB_TRY(make_rescale_plan(ctx, attr, in_dtype, attr->channels, &r));
+    cudaStream_t st = static_cast<cudaStream_t>(stream_);
+    if (count > 0) {
+        rescale_elementwise<<<grid_for(ctx, count), 256, 0, st>>>(input, in_dtype, attr->input_unsigned,
+                                                                  static_cast<int32_t>(izp), count, attr->channels,
+                                                                  rescale_args(r), attr->out_dtype, out, ctx->dev_err);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) { free_rescale_plan(&r); return fail(TB_ERR_CUDA, "rescale launch: %s", cudaGetErrorString(e)); }
+        ctx->launches++;
+    }
+    cudaStreamSynchronize(st);
+    free_rescale_plan(&r);
+    return TB_OK;
+}
+
+extern "C" TB_API tb_status tb_clamp(tb_context* ctx, int32_t dtype, const void* input, int64_t count, int64_t min_i,
+                                     int64_t max_i, float min_f, float max_f, int32_t nan_mode, void* out,
+                                     void* stream_) {
+    if (!ctx || (count > 0 && (!input || !out))) return fail(TB_ERR_INVALID_ARGUMENT, "null argument");
+    cudaStream_t st = static_cast<cudaStream_t>(stream_);
+    if (nan_mode != TB_NAN_PROPAGATE && nan_mode != TB_NAN_IGNORE)
+        return fail(TB_ERR_GRAPH, "CLAMP: nan_mode must be PROPAGATE or IGNORE");
+    if (dtype == TB_DT_INT8 || dtype == TB_DT_INT16) {
+        if (max_i < min_i) return fail(TB_ERR_GRAPH, "CLAMP: max_val must not be smaller than min_val");
+        if (count == 0) return TB_OK;
+        clamp_int<<<grid_for(ctx, count), 256, 0, st>>>(input, dtype, count, static_cast<int32_t>(min_i),
+                                                       static_cast<int32_t>(max_i), out);
+    } else if (dtype == TB_DT_FP16 || dtype == TB_DT_BF16 || dtype == TB_DT_FP32) {
+        if (min_f != min_f || max_f != max_f || max_f < min_f)
+            return fail(TB_ERR_GRAPH, "CLAMP: min_val/max_val must be ordered and not NaN");
+        if (count == 0) return TB_OK;
+        clamp_float<<<grid_for(ctx, count), 256, 0, st>>>(input, dtype, count, min_f, max_f, nan_mode, out);
+    } else {
+        return fail(TB_ERR_DTYPE_MISMATCH, "CLAMP: unsupported dtype %d", dtype);
+    }
+    TB_LAUNCHED(ctx);
+    return TB_OK;
+}
+
+extern "C" TB_API tb_status tb_add(tb_context* ctx, int32_t dtype, const void* a, const void* b, int64_t count,
+                                   void* out, void* stream_) {
+    if (!ctx || (count > 0 && (!a || !b || !out))) return fail(TB_ERR_INVALID_ARGUMENT, "null argument");
+    if (!(dtype == TB_DT_INT32 || dtype == TB_DT_FP32 || dtype == TB_DT_FP16 || dtype == TB_DT_BF16))
+        return fail(TB_ERR_NOT_ACCELERATED, "ADD dtype %d is not accelerated", dtype);
+    if (count == 0) return TB_OK;
+    add_elementwise<<<grid_for(ctx, count), 256, 0, static_cast<cudaStream_t>(stream_)>>>(a, b, dtype, count, out);
+    TB_LAUNCHED(ctx);
+    return TB_OK;
+}
+
+static tb_status pool_geom(const char* op, const tb_pool2d_desc* d, PoolGeomDev* g) {
+    // src/ops/pool.rs:31-70
+    for (int i = 0; i < 4; ++i)
+        if (d->pad[i] < 0) return fail(TB_ERR_GRAPH, "%s: pad must be non-negative", op);
+    for (int i = 0; i < 2; ++i)
+        if (d->kernel[i] < 1 || d->stride[i] < 1) return fail(TB_ERR_GRAPH, "%s: kernel and stride must be at least 1", op);
+    if (d->pad[0] >= d->kernel[0] || d->pad[1] >= d->kernel[0] || d->pad[2] >= d->kernel[1] || d->pad[3] >= d->kernel[1])
+        return fail(TB_ERR_GRAPH, "%s: pad must be smaller than kernel", op);
+    if (d->ih == 0 || d->iw == 0) return fail(TB_ERR_GRAPH, "%s: input height and width must be positive", op);
+    auto extent = [&](int size, int a, int b, int k, int s, int* o) -> tb_status {
+        const long long full = static_cast<long long>(size) + a + b - k;
+        if (full < 0 || full % s != 0) return fail(TB_ERR_GRAPH, "%s: parameters must yield exact integer output dimensions", op);
+        *o = static_cast<int>(full / s + 1);
+        return TB_OK;
+    };
+    g->n = d->n; g->ih = d->ih; g->iw = d->iw; g->c = d->c;
+    TB_TRY(extent(d->ih, d->pad[0], d->pad[1], d->kernel[0], d->stride[0], &g->oh));
+    TB_TRY(extent(d->iw, d->pad[2], d->pad[3], d->kernel[1], d->stride[1], &g->ow));
+    g->ky = d->kernel[0]; g->kx = d->kernel[1]; g->sy = d->stride[0]; g->sx = d->stride[1];
+    g->pad_t = d->pad[0]; g->pad_l = d->pad[2];
+    return TB_OK;
+}
+
+extern "C" TB_API tb_status tb_avg_pool2d(tb_context* ctx, const tb_pool2d_desc* d, const void* input, void* out,
+                                          void* stream_) {
+    if (!ctx || !d) return fail(TB_ERR_INVALID_ARGUMENT, "null argument");
+    PoolGeomDev g;
+    TB_TRY(pool_geom("AVG_POOL2D", d, &g));
+    const int dt = d->dtype, at = d->acc_dtype;
+    const bool ok = ((dt == TB_DT_INT8 || dt == TB_DT_INT16) && at == TB_DT_INT32) ||
+                    (dt == TB_DT_FP16 && (at == TB_DT_FP16 || at == TB_DT_FP32)) ||
+                    ((dt == TB_DT_BF16 || dt == TB_DT_FP32) && at == TB_DT_FP32);
+    if (!ok) return fail(TB_ERR_NOT_ACCELERATED, "AVG_POOL2D types %d/%d are not accelerated", dt, at);
+    if (dt != TB_DT_INT8 && (d->input_zp != 0 || d->output_zp != 0))
+        return fail(TB_ERR_GRAPH, "AVG_POOL2D: zero points must be zero for non-int8 data");
+    const long long total = static_cast<long long>(g.n) * g.oh * g.ow * g.c;
+    if (total == 0) return TB_OK;
+    if (!input || !out) return fail(TB_ERR_INVALID_ARGUMENT, "null argument");
+    cudaStream_t st = static_cast<cudaStream_t>(stream_);
+    if (dt == TB_DT_INT8 && g.c % 4 == 0 && aligned16(input))
+        avg_pool_i8_vec4<<<grid_for(ctx, total / 4), 256, 0, st>>>(g, static_cast<const int8_t*>(input), d->input_zp,
+                                                                  d->output_zp, static_cast<int8_t*>(out), ctx->dev_err);
+    else if (dt == TB_DT_INT8 || dt == TB_DT_INT16)
+        avg_pool_int<<<grid_for(ctx, total), 256, 0, st>>>(g, input, dt, d->input_zp, d->output_zp, out, ctx->dev_err);
+    else
+        avg_pool_float<<<grid_for(ctx, total), 256, 0, st>>>(g, input, dt, at, out);
+    TB_LAUNCHED(ctx);
+    return TB_OK;
+}
+
+extern "C" TB_API tb_status tb_max_pool2d(tb_context* ctx, const tb_pool2d_desc* d, const void* input, void* out,
+                                          void* stream_) {
+    if (!ctx || !d) return fail(TB_ERR_INVALID_ARGUMENT, "null argument");
+    if (d->nan_mode != TB_NAN_PROPAGATE && d->nan_mode != TB_NAN_IGNORE)
+        return fail(TB_ERR_GRAPH, "MAX_POOL2D: nan_mode must be PROPAGATE or IGNORE");
+    PoolGeomDev g;
+    TB_TRY(pool_geom("MAX_POOL2D", d, &g));
+    const int dt = d->dtype;
+    const long long total = static_cast<long long>(g.n) * g.oh * g.ow * g.c;
+    cudaStream_t st = static_cast<cudaStream_t>(stream_);
+    if (!(dt == TB_DT_INT8 || dt == TB_DT_INT16 || dt == TB_DT_FP16 || dt == TB_DT_BF16 || dt == TB_DT_FP32))
+        return fail(TB_ERR_NOT_ACCELERATED, "MAX_POOL2D dtype %d is not accelerated", dt);
+    if (total == 0) return TB_OK;
+    if (!input || !out) return fail(TB_ERR_INVALID_ARGUMENT, "null argument");
+    if (dt == TB_DT_INT8 && g.c % 4 == 0 && aligned16(input))
+        max_pool_i8_vec4<<<grid_for(ctx, total / 4), 256, 0, st>>>(g, static_cast<const int8_t*>(input),
+                                                                  static_cast<int8_t*>(out));
+    else if (dt == TB_DT_INT8 || dt == TB_DT_INT16)
+        max_pool_int<<<grid_for(ctx, total), 256, 0, st>>>(g, input, dt, out);
+    else
+        max_pool_float<<<grid_for(ctx, total), 256, 0, st>>>(g, input, dt, d->nan_mode, out);
+    TB_LAUNCHED(ctx);
+    return TB_OK;
+}

@@ -1,0 +1,103 @@
+// Launch helpers of the tensor-core GEMM: one template instantiation per tile
+// configuration and epilogue kind. The instantiations are spread over
+// gemm_i8_mm.cu, gemm_i8_conv.cu and gemm_f16.cu, which expose the plain
+// functions declared at the bottom.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "internal.hpp"
+#include "tc_gemm.cuh"
+
+namespace tb {
+
+#define TB_GEMM_LAUNCHED(ctx)                                                                          \
+    do {                                                                                               \
+        cudaError_t e_ = cudaGetLastError();                                                           \
+        if (e_ != cudaSuccess) return ::tb::fail(TB_ERR_CUDA, "kernel launch failed: %s", cudaGetErrorString(e_)); \
+        (ctx)->launches++;                                                                             \
+    } while (0)
+
+template <class Cfg, int EK>
+tb_status launch_gemm(tb_context* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB, GemmParams p,
+                      cudaStream_t stream) {
+    static bool attr_set = false;  // the attribute is per function and process-wide
+    if (!attr_set) {
+        TB_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<Cfg, EK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     Cfg::SMEM_BYTES));
+        attr_set = true;
+    }
+    p.m_tiles = (p.M + Cfg::BM - 1) / Cfg::BM;
+    p.n_tiles = (p.N + Cfg::kBN - 1) / Cfg::kBN;
+    p.total_tiles = p.batch * p.m_tiles * p.n_tiles;
+    p.err = ctx->dev_err;
+    p.timeout_cycles = ctx->timeout_cycles;
+    p.trace = ctx->trace;
+    const int grid = std::min(p.total_tiles, ctx->num_sms);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if (p.epi.pdl_wait) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
+    if (p.cs.b != nullptr) {
+        // CTAs wait on one another's column sums: all must be resident at once.
+        attr[na].id = cudaLaunchAttributeCooperative;
+        attr[na].val.cooperative = 1;
+        ++na;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = na;
+    TB_CUDA(cudaLaunchKernelEx(&cfg, tc_gemm_kernel<Cfg, EK>, tmA, tmB, p));
+    TB_GEMM_LAUNCHED(ctx);
+    return TB_OK;
+}
+
+constexpr int gemm_stages(int bn, int bk) { return (196608 / ((128 + bn) * bk)) < 8 ? (196608 / ((128 + bn) * bk)) : 8; }
+
+// Epilogue kind for a prepared epilogue.
+inline int epilogue_kind(const GemmEpilogue& e) {
+    if (e.mode == EPI_I32) return EK_I32;
+    if (e.mode == EPI_F32) return EK_F32;
+    if (e.mode == EPI_FCONV) return EK_FCONV;
+    if (!e.rs_fast || e.out_dtype != DT_INT8) return EK_SLOW;
+    const bool dbl = e.rs.rounding == ROUND_DOUBLE;
+    if (e.rs.per_channel) return dbl ? EK_FAST_PC_D : EK_FAST_PC_S;
+    return dbl ? EK_FAST_T_D : EK_FAST_T_S;
+}
+
+// Switch over the integer epilogue kinds for one tile configuration.
+template <class Cfg>
+tb_status launch_int_ek(tb_context* ctx, int ek, const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p,
+                        cudaStream_t st) {
+    switch (ek) {
+    case EK_I32: return launch_gemm<Cfg, EK_I32>(ctx, a, b, p, st);
+    case EK_SLOW: return launch_gemm<Cfg, EK_SLOW>(ctx, a, b, p, st);
+    case EK_FAST_T_S: return launch_gemm<Cfg, EK_FAST_T_S>(ctx, a, b, p, st);
+    case EK_FAST_T_D: return launch_gemm<Cfg, EK_FAST_T_D>(ctx, a, b, p, st);
+    case EK_FAST_PC_S: return launch_gemm<Cfg, EK_FAST_PC_S>(ctx, a, b, p, st);
+    case EK_FAST_PC_D: return launch_gemm<Cfg, EK_FAST_PC_D>(ctx, a, b, p, st);
+    default: return fail(TB_ERR_NOT_ACCELERATED, "no integer epilogue kind %d", ek);
+    }
+}
+
+// Implemented in gemm_i8_mm.cu / gemm_i8_conv.cu / gemm_f16.cu.
+tb_status launch_i8_matmul(tb_context* ctx, int bn, int ek, const CUtensorMap& a, const CUtensorMap& b,
+                           const GemmParams& p, cudaStream_t st);
+tb_status launch_i8_conv(tb_context* ctx, int bn, int bk, int ek, const CUtensorMap& a, const CUtensorMap& b,
+                         const GemmParams& p, cudaStream_t st);
+tb_status launch_f16_matmul(tb_context* ctx, int bn, const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p,
+                            cudaStream_t st);
+tb_status launch_f16_conv(tb_context* ctx, int bn, const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p,
+                          cudaStream_t st);
+
+}  // namespace tb

@@ -1,0 +1,81 @@
+// Internal host-side definitions shared by the backend's translation units.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <string>
+#include <vector>
+
+#include "../../include/tosa_b200.h"
+
+struct tb_context {
+    int device = 0;
+    int num_sms = 148;
+    uint32_t* dev_err = nullptr;     // device error word (DEV_ERR_* bits)
+    long long timeout_cycles = 0;    // bound on every in-kernel wait
+    uint64_t launches = 0;
+    long long* trace = nullptr;      // optional GEMM timeline buffer (TB_TRACE=1)
+};
+
+namespace tb {
+
+// Records the calling thread's last error message and returns `st`.
+tb_status fail(tb_status st, const char* fmt, ...);
+
+#define TB_CUDA(call)                                                                          \
+    do {                                                                                       \
+        cudaError_t e_ = (call);                                                               \
+        if (e_ != cudaSuccess)                                                                 \
+            return ::tb::fail(TB_ERR_CUDA, "%s failed: %s", #call, cudaGetErrorString(e_));    \
+    } while (0)
+
+#define TB_TRY(expr)                         \
+    do {                                     \
+        tb_status s_ = (expr);               \
+        if (s_ != TB_OK) return s_;          \
+    } while (0)
+
+// Driver entry points fetched through the runtime (no libcuda link).
+tb_status encode_tiled(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* base, const uint64_t* dims,
+                       const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swz);
+tb_status encode_im2col(CUtensorMap* map, CUtensorMapDataType dt, const void* base, const uint64_t* dims /*C,W,H,N*/,
+                        const uint64_t* strides_bytes /*3*/, const int* lower /*w,h*/, const int* upper /*w,h*/,
+                        uint32_t channels, uint32_t pixels, const uint32_t* elem_strides /*4*/,
+                        CUtensorMapSwizzle swz);
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline int elem_bytes(int dt) {
+    switch (dt) {
+    case TB_DT_BOOL: case TB_DT_INT4: case TB_DT_INT8: case TB_DT_FP8E4M3: case TB_DT_FP8E5M2: return 1;
+    case TB_DT_INT16: case TB_DT_FP16: case TB_DT_BF16: return 2;
+    case TB_DT_INT32: case TB_DT_FP32: return 4;
+    default: return 8;
+    }
+}
+
+// Resolved RESCALE epilogue (device copies of multiplier/shift).
+struct RescalePlan {
+    bool enabled = false;
+    int scale32 = 1, rounding = 1, per_channel = 0, channels = 1;
+    int32_t out_zp = 0, lo = 0, hi = 0;
+    int out_dtype = TB_DT_INT32;
+    bool fast = false;             // every shift >= 32 and multiplier >= 0 (scale32 single/double)
+    bool zp_folded = false;        // output zero point folded into the packed rounding constants
+    int32_t* d_mult = nullptr;     // [channels]
+    int32_t* d_shift = nullptr;    // [channels]
+    int32_t* d_rq = nullptr;       // fast path: [channels][8] {m, s-32, rp_lo, rp_hi, rn_lo, rn_hi, 0, 0}
+};
+
+// Validate a fused/standalone RESCALE (src/ops/type_conv.rs:128-171) for
+// input type in_dtype with `shape_last` as the last dimension.
+tb_status check_rescale(const tb_rescale_attr* a, int in_dtype, int64_t shape_last, int64_t* in_zp_ext,
+                        int64_t* out_zp_ext, int32_t* lo, int32_t* hi);
+tb_status make_rescale_plan(tb_context* ctx, const tb_rescale_attr* a, int in_dtype, int64_t shape_last,
+                            RescalePlan* out);
+void free_rescale_plan(RescalePlan* r);
+
+}  // namespace tb

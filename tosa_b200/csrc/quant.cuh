@@ -1,0 +1,97 @@
+// Device-side TOSA fixed-point arithmetic: RESCALE (scale32 single/double
+// rounding, scale16, inexact) and the float rounding used by the float
+// convolution epilogue. Semantics follow the reference interpreter:
+//   apply_scale_32   src/ops/quant.rs:17-32
+//   apply_scale_16   src/ops/type_conv.rs:86-92
+//   RESCALE element  src/ops/type_conv.rs:174-188
+//   round_to         src/ops/common.rs:100-108 (round to nearest even)
+#pragma once
+
+#include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+namespace tb {
+
+// Error bits of the per-context device error word.
+enum : uint32_t {
+    DEV_ERR_SCALE = 1u,    // apply_scale range / int32 overflow (Error::GraphError)
+    DEV_ERR_TIMEOUT = 2u,  // a bounded wait gave up
+    DEV_ERR_INTERNAL = 4u,
+};
+
+// Rounding modes (schema RoundingMode enum).
+enum : int { ROUND_SINGLE = 1, ROUND_INEXACT = 2, ROUND_DOUBLE = 3 };
+
+// DType codes (schema DType enum).
+enum : int {
+    DT_BOOL = 1, DT_INT4 = 2, DT_INT8 = 3, DT_INT16 = 4, DT_INT32 = 5, DT_INT48 = 6,
+    DT_FP32 = 7, DT_FP16 = 8, DT_BF16 = 9, DT_SHAPE = 10, DT_INT64 = 17,
+};
+
+struct RescaleArgs {
+    const int32_t* multiplier;  // [channels] (scale32: int32 values; scale16: int16 values widened)
+    const int32_t* shift;       // [channels], widened from int8
+    int per_channel;
+    int scale32;
+    int rounding;               // ROUND_*
+    int32_t out_zp;             // already extended for an unsigned output
+    int32_t lo, hi;             // output clamp range, intersected with a fused CLAMP
+};
+
+// General RESCALE of one value x = extend(v) - in_zp. Returns the clamped
+// result; sets *err on the conditions where the reference returns Err.
+__device__ __forceinline__ int64_t rescale_value(int64_t x, int32_t m, int32_t s, int rounding, int scale32,
+                                                 int32_t out_zp, int32_t lo, int32_t hi, uint32_t* err) {
+    int64_t scaled;
+    if (rounding == ROUND_INEXACT) {
+        // (f32(x) * f32(m)) * 2^-s, each product rounded to nearest, then
+        // round-half-even to int32 with saturation (NaN -> 0).
+        float t = __fmul_rn(__ll2float_rn(x), __int2float_rn(m));
+        float p2 = __int_as_float((127 - s) << 23);  // exact 2^-s for s in [2, 62]
+        t = __fmul_rn(t, p2);
+        scaled = static_cast<int64_t>(__float2int_rn(t));
+    } else if (scale32) {
+        if (m < 0 || s < 2 || s > 62) { *err |= DEV_ERR_SCALE; return 0; }
+        const int64_t half = static_cast<int64_t>(1) << (s - 1);
+        const int32_t xv = static_cast<int32_t>(x);
+        if (static_cast<int64_t>(xv) < -half || static_cast<int64_t>(xv) >= half) { *err |= DEV_ERR_SCALE; return 0; }
+        int64_t round = half;
+        if (rounding == ROUND_DOUBLE && s > 31) round += xv >= 0 ? (1ll << 30) : -(1ll << 30);
+        scaled = (static_cast<int64_t>(xv) * m + round) >> s;
+        if (scaled < INT32_MIN || scaled > INT32_MAX) { *err |= DEV_ERR_SCALE; return 0; }
+    } else {
+        const int16_t m16 = static_cast<int16_t>(m);
+        if (m16 < 0 || s < 2 || s > 62) { *err |= DEV_ERR_SCALE; return 0; }
+        scaled = (x * m16 + (static_cast<int64_t>(1) << (s - 1))) >> s;
+        if (scaled < INT32_MIN || scaled > INT32_MAX) { *err |= DEV_ERR_SCALE; return 0; }
+    }
+    int64_t r = scaled + out_zp;
+    if (r < INT32_MIN || r > INT32_MAX) { *err |= DEV_ERR_SCALE; return 0; }
+    r = r < lo ? lo : r;
+    r = r > hi ? hi : r;
+    return r;
+}
+
+// Fast path for scale32 single/double rounding when the host has verified
+// that every shift is >= 32 and every multiplier is non-negative: then every
+// int32 input is in range and no intermediate can overflow, so the result is
+// ((v * m + round) >> s) + out_zp, clamped.
+__device__ __forceinline__ int32_t rescale_fast(int32_t v, int32_t m, int32_t s, int64_t round_pos, int double_round,
+                                                int32_t out_zp, int32_t lo, int32_t hi) {
+    int64_t round = round_pos;
+    if (double_round && v < 0) round -= (1ll << 31);  // +2^30 for v >= 0, -2^30 otherwise
+    int32_t r = static_cast<int32_t>((static_cast<int64_t>(v) * m + round) >> s) + out_zp;
+    r = max(r, lo);
+    r = min(r, hi);
+    return r;
+}
+
+// f32 -> dtype -> f32 rounding (round to nearest even).
+__device__ __forceinline__ float round_to_dtype(float x, int dtype) {
+    if (dtype == DT_BF16) return __bfloat162float(__float2bfloat16_rn(x));
+    if (dtype == DT_FP16) return __half2float(__float2half_rn(x));
+    return x;
+}
+
+}  // namespace tb

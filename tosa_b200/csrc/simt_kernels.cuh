@@ -1,0 +1,407 @@
+// CUDA-core kernels of the backend:
+//   * HBM-bound operators: DEPTHWISE_CONV2D, AVG_POOL2D, MAX_POOL2D, RESCALE,
+//     CLAMP, ADD (vectorised over 4 channels where the layout allows);
+//   * helpers of the tensor-core path: zero-point sums of weights / B columns
+//     and the per-border-class column-term tables of a convolution plan;
+//   * direct CONV2D / MATMUL for shapes the TMA tiles cannot address (channel
+//     counts that are not multiples of 16 bytes, e.g. the conformance shapes
+//     and RGB stems). These follow the reference's loop order, so the float
+//     variants reproduce AccF32 bit for bit.
+#pragma once
+
+#include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "ptx.cuh"
+#include "quant.cuh"
+
+namespace tb {
+
+struct ConvGeomDev {
+    int n, ih, iw, ic, oc, kh, kw, oh, ow, m;
+    int pad_t, pad_l, sh, sw, dh, dw;
+};
+
+// Integer result of a contraction -> optional RESCALE -> store.
+struct IntEpiDev {
+    int rescale;          // 0: store int32, 1: RESCALE
+    RescaleArgs rs;
+    int out_dtype;
+};
+
+__device__ __forceinline__ void store_int(void* out, long long idx, int dtype, int32_t v) {
+    if (dtype == DT_INT8) static_cast<int8_t*>(out)[idx] = static_cast<int8_t>(v);
+    else if (dtype == DT_INT16) static_cast<int16_t*>(out)[idx] = static_cast<int16_t>(v);
+    else static_cast<int32_t*>(out)[idx] = v;
+}
+
+__device__ __forceinline__ void finish_int(const IntEpiDev& e, int32_t v, int ch, void* out, long long idx,
+                                           uint32_t* err) {
+    if (!e.rescale) {
+        static_cast<int32_t*>(out)[idx] = v;
+        return;
+    }
+    const int c = e.rs.per_channel ? ch : 0;
+    const int64_t r = rescale_value(v, e.rs.multiplier[c], e.rs.shift[c], e.rs.rounding, e.rs.scale32, e.rs.out_zp,
+                                    e.rs.lo, e.rs.hi, err);
+    store_int(out, idx, e.out_dtype, static_cast<int32_t>(r));
+}
+
+__device__ __forceinline__ float load_f(const void* p, long long i, int dt) {
+    if (dt == DT_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+    if (dt == DT_FP16) return __half2float(static_cast<const __half*>(p)[i]);
+    return static_cast<const float*>(p)[i];
+}
+__device__ __forceinline__ void store_f(void* p, long long i, int dt, float v) {
+    if (dt == DT_BF16) static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+    else if (dt == DT_FP16) static_cast<__half*>(p)[i] = __float2half_rn(v);
+    else static_cast<float*>(p)[i] = v;
+}
+
+// ---------------------------------------------------------------------------
+// Direct CONV2D (one thread per output element), reference loop order
+// (src/ops/conv.rs:147-181): taps row-major, ic innermost.
+// ---------------------------------------------------------------------------
+__global__ void conv2d_direct_int(ConvGeomDev g, const int8_t* __restrict__ x, const int8_t* __restrict__ w,
+                                  const int32_t* __restrict__ bias, int bias_len, int32_t zx, int32_t zw,
+                                  IntEpiDev e, void* out, uint32_t* err) {
+    const long long total = static_cast<long long>(g.n) * g.oh * g.ow * g.oc;
+    uint32_t lerr = 0;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int oc = static_cast<int>(i % g.oc);
+        long long r = i / g.oc;
+        const int ox = static_cast<int>(r % g.ow);
+        r /= g.ow;
+        const int oy = static_cast<int>(r % g.oh);
+        const int b = static_cast<int>(r / g.oh);
+        uint32_t acc = 0;
+        for (int ky = 0; ky < g.kh; ++ky) {
+            const int y = oy * g.sh + ky * g.dh - g.pad_t;
+            if (y < 0 || y >= g.ih) continue;
+            for (int kx = 0; kx < g.kw; ++kx) {
+                const int xx = ox * g.sw + kx * g.dw - g.pad_l;
+                if (xx < 0 || xx >= g.iw) continue;
+                const int8_t* xp = x + ((static_cast<long long>(b) * g.ih + y) * g.iw + xx) * g.ic;
+                const int8_t* wp = w + ((static_cast<long long>(oc) * g.kh + ky) * g.kw + kx) * g.ic;
+                for (int c = 0; c < g.ic; ++c)
+                    acc += static_cast<uint32_t>(static_cast<int32_t>(xp[c]) - zx) *
+                           static_cast<uint32_t>(static_cast<int32_t>(wp[c]) - zw);
+            }
+        }
+        acc += static_cast<uint32_t>(bias[bias_len == 1 ? 0 : oc]);
+        finish_int(e, static_cast<int32_t>(acc), oc, out, i, &lerr);
+    }
+    if (lerr) atomicOr(err, lerr);
+}
+
+__global__ void conv2d_direct_float(ConvGeomDev g, const void* __restrict__ x, const void* __restrict__ w,
+                                    const void* __restrict__ bias, int bias_len, int in_dt, int w_dt, int out_dt,
+                                    void* out) {
+    const long long total = static_cast<long long>(g.n) * g.oh * g.ow * g.oc;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int oc = static_cast<int>(i % g.oc);
+        long long r = i / g.oc;
+        const int ox = static_cast<int>(r % g.ow);
+        r /= g.ow;
+        const int oy = static_cast<int>(r % g.oh);
+        const int b = static_cast<int>(r / g.oh);
+        float acc = 0.f;
+        for (int ky = 0; ky < g.kh; ++ky) {
+            const int y = oy * g.sh + ky * g.dh - g.pad_t;
+            if (y < 0 || y >= g.ih) continue;
+            for (int kx = 0; kx < g.kw; ++kx) {
+                const int xx = ox * g.sw + kx * g.dw - g.pad_l;
+                if (xx < 0 || xx >= g.iw) continue;
+                const long long xb = ((static_cast<long long>(b) * g.ih + y) * g.iw + xx) * g.ic;
+                const long long wb = ((static_cast<long long>(oc) * g.kh + ky) * g.kw + kx) * g.ic;
+                for (int c = 0; c < g.ic; ++c)
+                    acc = __fadd_rn(acc, __fmul_rn(load_f(x, xb + c, in_dt), load_f(w, wb + c, w_dt)));
+            }
+        }
+        const float bv = load_f(bias, bias_len == 1 ? 0 : oc, out_dt);
+        store_f(out, i, out_dt, round_to_dtype(__fadd_rn(round_to_dtype(acc, out_dt), bv), out_dt));
+    }
+}
+
+// ---------------------------------------------------------------------------
+// DEPTHWISE_CONV2D (src/ops/conv.rs:234-266). HBM-bound: one thread computes
+// 4 consecutive output channels of one output pixel when m == 1 and c % 4 == 0
+// (char4 loads of activations and weights), else one channel.
+// ---------------------------------------------------------------------------
+__global__ void depthwise_int_vec4(ConvGeomDev g, const int8_t* __restrict__ x, const int8_t* __restrict__ w,
+                                   const int32_t* __restrict__ bias, int bias_len, int32_t zx, int32_t zw,
+                                   IntEpiDev e, void* out, uint32_t* err) {
+    const int cg = g.ic >> 2;
+    const long long total = static_cast<long long>(g.n) * g.oh * g.ow * cg;
+    uint32_t lerr = 0;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int c4 = static_cast<int>(i % cg) * 4;
+        long long r = i / cg;
+        const int ox = static_cast<int>(r % g.ow);
+        r /= g.ow;
+        const int oy = static_cast<int>(r % g.oh);
+        const int b = static_cast<int>(r / g.oh);
+        uint32_t acc[4] = {0, 0, 0, 0};
+        const int iy0 = oy * g.sh - g.pad_t, ix0 = ox * g.sw - g.pad_l;
+        for (int ky = 0; ky < g.kh; ++ky) {
+            const int y = iy0 + ky * g.dh;
+            if (y < 0 || y >= g.ih) continue;
+            for (int kx = 0; kx < g.kw; ++kx) {
+                const int xx = ix0 + kx * g.dw;
+                if (xx < 0 || xx >= g.iw) continue;
+                const char4 xv = __ldg(reinterpret_cast<const char4*>(
+                    x + ((static_cast<long long>(b) * g.ih + y) * g.iw + xx) * g.ic + c4));
+                const char4 wv = __ldg(reinterpret_cast<const char4*>(w + (ky * g.kw + kx) * g.ic + c4));
+                acc[0] += static_cast<uint32_t>(xv.x - zx) * static_cast<uint32_t>(wv.x - zw);
+                acc[1] += static_cast<uint32_t>(xv.y - zx) * static_cast<uint32_t>(wv.y - zw);
+                acc[2] += static_cast<uint32_t>(xv.z - zx) * static_cast<uint32_t>(wv.z - zw);
+                acc[3] += static_cast<uint32_t>(xv.w - zx) * static_cast<uint32_t>(wv.w - zw);
+            }
+        }
+        const long long o = ((static_cast<long long>(b) * g.oh + oy) * g.ow + ox) * g.ic + c4;
+        if (e.rescale && e.out_dtype == DT_INT8) {
+            char4 ov;
+            int32_t rv[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int ch = c4 + k;
+                const int32_t v = static_cast<int32_t>(acc[k] + static_cast<uint32_t>(bias[bias_len == 1 ? 0 : ch]));
+                const int pc = e.rs.per_channel ? ch : 0;
+                rv[k] = static_cast<int32_t>(rescale_value(v, e.rs.multiplier[pc], e.rs.shift[pc], e.rs.rounding,
+                                                           e.rs.scale32, e.rs.out_zp, e.rs.lo, e.rs.hi, &lerr));
+            }
+            ov.x = static_cast<signed char>(rv[0]);
+            ov.y = static_cast<signed char>(rv[1]);
+            ov.z = static_cast<signed char>(rv[2]);
+            ov.w = static_cast<signed char>(rv[3]);
+            *reinterpret_cast<char4*>(static_cast<int8_t*>(out) + o) = ov;
+        } else {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int ch = c4 + k;
+                const int32_t v = static_cast<int32_t>(acc[k] + static_cast<uint32_t>(bias[bias_len == 1 ? 0 : ch]));
+                finish_int(e, v, ch, out, o + k, &lerr);
+            }
+        }
+    }
+    if (lerr) atomicOr(err, lerr);
+}
+
+__global__ void depthwise_int_generic(ConvGeomDev g, const int8_t* __restrict__ x, const int8_t* __restrict__ w,
+                                      const int32_t* __restrict__ bias, int bias_len, int32_t zx, int32_t zw,
+                                      IntEpiDev e, void* out, uint32_t* err) {
+    const int cm = g.ic * g.m;
+    const long long total = static_cast<long long>(g.n) * g.oh * g.ow * cm;
+    uint32_t lerr = 0;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int oc = static_cast<int>(i % cm);
+        const int c = oc / g.m, mm = oc % g.m;
+        long long r = i / cm;
+        const int ox = static_cast<int>(r % g.ow);
+        r /= g.ow;
+        const int oy = static_cast<int>(r % g.oh);
+        const int b = static_cast<int>(r / g.oh);
+        uint32_t acc = 0;
+        for (int ky = 0; ky < g.kh; ++ky) {
+            const int y = oy * g.sh - g.pad_t + ky * g.dh;
+            if (y < 0 || y >= g.ih) continue;
+            for (int kx = 0; kx < g.kw; ++kx) {
+                const int xx = ox * g.sw - g.pad_l + kx * g.dw;
+                if (xx < 0 || xx >= g.iw) continue;
+                const int32_t xv = x[((static_cast<long long>(b) * g.ih + y) * g.iw + xx) * g.ic + c];
+                const int32_t wv = w[((ky * g.kw + kx) * g.ic + c) * g.m + mm];
+                acc += static_cast<uint32_t>(xv - zx) * static_cast<uint32_t>(wv - zw);
+            }
+        }
+        acc += static_cast<uint32_t>(bias[bias_len == 1 ? 0 : oc]);
+        finish_int(e, static_cast<int32_t>(acc), oc, out, i, &lerr);
+    }
+    if (lerr) atomicOr(err, lerr);
+}
+
+__global__ void depthwise_float(ConvGeomDev g, const void* __restrict__ x, const void* __restrict__ w,
+                                const void* __restrict__ bias, int bias_len, int in_dt, int out_dt, void* out) {
+    const int cm = g.ic * g.m;
+    const long long total = static_cast<long long>(g.n) * g.oh * g.ow * cm;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int oc = static_cast<int>(i % cm);
+        const int c = oc / g.m, mm = oc % g.m;
+        long long r = i / cm;
+        const int ox = static_cast<int>(r % g.ow);
+        r /= g.ow;
+        const int oy = static_cast<int>(r % g.oh);
+        const int b = static_cast<int>(r / g.oh);
+        float acc = 0.f;
+        for (int ky = 0; ky < g.kh; ++ky) {
+            const int y = oy * g.sh - g.pad_t + ky * g.dh;
+            if (y < 0 || y >= g.ih) continue;
+            for (int kx = 0; kx < g.kw; ++kx) {
+                const int xx = ox * g.sw - g.pad_l + kx * g.dw;
+                if (xx < 0 || xx >= g.iw) continue;
+                const float xv = load_f(x, ((static_cast<long long>(b) * g.ih + y) * g.iw + xx) * g.ic + c, in_dt);
+                const float wv = load_f(w, ((ky * g.kw + kx) * g.ic + c) * g.m + mm, in_dt);
+                acc = __fadd_rn(acc, __fmul_rn(xv, wv));
+            }
+        }
+        const float bv = load_f(bias, bias_len == 1 ? 0 : oc, out_dt);
+        store_f(out, i, out_dt, round_to_dtype(__fadd_rn(round_to_dtype(acc, out_dt), bv), out_dt));
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Direct MATMUL (src/ops/matmul.rs:80-95), one thread per output element.
+// ---------------------------------------------------------------------------
+__global__ void matmul_direct_int(int n, int h, int c, int w, const int8_t* __restrict__ a,
+                                  const int8_t* __restrict__ bm, int32_t za, int32_t zb, IntEpiDev e, void* out,
+                                  uint32_t* err) {
+    const long long total = static_cast<long long>(n) * h * w;
+    uint32_t lerr = 0;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int col = static_cast<int>(i % w);
+        const long long rowi = i / w;  // bn*h + row
+        const int bn = static_cast<int>(rowi / h);
+        const int8_t* ar = a + rowi * c;
+        const int8_t* bc = bm + static_cast<long long>(bn) * c * w + col;
+        uint32_t acc = 0;
+        for (int k = 0; k < c; ++k)
+            acc += static_cast<uint32_t>(ar[k] - za) * static_cast<uint32_t>(bc[static_cast<long long>(k) * w] - zb);
+        finish_int(e, static_cast<int32_t>(acc), col, out, i, &lerr);
+    }
+    if (lerr) atomicOr(err, lerr);
+}
+
+__global__ void matmul_direct_float(int n, int h, int c, int w, const void* __restrict__ a, const void* __restrict__ bm,
+                                    int in_dt, int out_dt, void* out) {
+    const long long total = static_cast<long long>(n) * h * w;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int col = static_cast<int>(i % w);
+        const long long rowi = i / w;
+        const int bn = static_cast<int>(rowi / h);
+        float acc = 0.f;
+        for (int k = 0; k < c; ++k)
+            acc = __fadd_rn(acc, __fmul_rn(load_f(a, rowi * c + k, in_dt),
+                                           load_f(bm, (static_cast<long long>(bn) * c + k) * w + col, in_dt)));
+        store_f(out, i, out_dt, acc);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Zero-point helpers of the tensor-core path
+// ---------------------------------------------------------------------------
+
+// colsum[b][col] += scale * sum_{k in chunk} B[b][k][col] (+ add once per
+// column)  (MATMUL, B is [n,c,w], w % 16 == 0; colsum zeroed first). With
+// scale = -a_zp and add = c*a_zp*b_zp this yields the epilogue's column term. Block = 64 column groups of 16 bytes x
+// 4 row slices; grid (ceil(w/1024), ceil(c/kchunk), n). Each thread sums 16
+// columns over kchunk/4 rows with 16-byte loads, the 4 slices are combined in
+// shared memory and each block adds its 1024 partial sums atomically. The
+// kernel releases its dependent launch immediately: the GEMM that consumes the
+// sums waits for them only in its epilogue (griddepcontrol.wait).
+__global__ void __launch_bounds__(256) matmul_colsum(int c, int w, int kchunk, const int8_t* __restrict__ bm,
+                                                     int32_t scale, int32_t add, int32_t* __restrict__ colsum) {
+    grid_launch_dependents();
+    __shared__ int32_t part[3][1024];
+    const int cg = threadIdx.x & 63, slice = threadIdx.x >> 6;
+    const int col = blockIdx.x * 1024 + cg * 16;
+    const int k0 = blockIdx.y * kchunk;
+    const int bn = blockIdx.z;
+    const int rows = max(0, min(kchunk, c - k0));
+    int s[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) s[i] = 0;
+    if (col < w) {
+        const int8_t* p = bm + (static_cast<long long>(bn) * c + k0) * w + col;
+#pragma unroll 16
+        for (int k = slice; k < rows; k += 4) {
+            const int4 v = __ldg(reinterpret_cast<const int4*>(p + static_cast<long long>(k) * w));
+            const int words[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                s[4 * q + 0] += static_cast<int8_t>(words[q] & 0xff);
+                s[4 * q + 1] += static_cast<int8_t>((words[q] >> 8) & 0xff);
+                s[4 * q + 2] += static_cast<int8_t>((words[q] >> 16) & 0xff);
+                s[4 * q + 3] += words[q] >> 24;
+            }
+        }
+    }
+    if (slice > 0) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) part[slice - 1][cg * 16 + i] = s[i];
+    }
+    __syncthreads();
+    if (slice == 0 && col < w) {
+        int32_t* o = colsum + static_cast<long long>(bn) * w + col;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int t = s[i] + part[0][cg * 16 + i] + part[1][cg * 16 + i] + part[2][cg * 16 + i];
+            const uint32_t contrib = static_cast<uint32_t>(scale) * static_cast<uint32_t>(t) +
+                                     (blockIdx.y == 0 ? static_cast<uint32_t>(add) : 0u);
+            if (col + i < w) atomicAdd(reinterpret_cast<unsigned int*>(o + i), contrib);
+        }
+    }
+}
+
+// wsum[oc][tap] = sum_ic w[oc][tap][ic]  (CONV2D weights OHWI, taps = kh*kw).
+__global__ void conv_weight_tap_sums(int oc, int taps, int ic, const int8_t* __restrict__ w, int32_t* __restrict__ wsum) {
+    const long long total = static_cast<long long>(oc) * taps;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int8_t* p = w + i * ic;
+        int32_t s = 0;
+        for (int c = 0; c < ic; ++c) s += p[c];
+        wsum[i] = s;
+    }
+}
+
+// colterm[cls][o] = bias[o] - zx * sum_{valid taps of cls} wsum[o][tap]
+//                  + n_valid(cls) * ic * zx * zw     (all mod 2^32)
+// Class cls = ry * n_rx + rx; row class ry admits taps ky in [ky_lo, ky_hi],
+// column class rx admits kx in [kx_lo, kx_hi]. Rows are `ld` long (padded with
+// zeros past oc); delta[cls][o] = colterm[cls][o] - colterm[base][o].
+__device__ __forceinline__ uint32_t conv_class_term(int o, int cls, int n_rx, int kh, int kw, int ic,
+                                                    const int* ky_range, const int* kx_range, const int32_t* wsum,
+                                                    const int32_t* bias, int bias_len, int32_t zx, int32_t zw) {
+    const int ry = cls / n_rx, rx = cls % n_rx;
+    const int ky0 = ky_range[2 * ry], ky1 = ky_range[2 * ry + 1];
+    const int kx0 = kx_range[2 * rx], kx1 = kx_range[2 * rx + 1];
+    uint32_t ws = 0, nvalid = 0;
+    for (int ky = ky0; ky <= ky1; ++ky)
+        for (int kx = kx0; kx <= kx1; ++kx) {
+            ws += static_cast<uint32_t>(wsum[static_cast<long long>(o) * kh * kw + ky * kw + kx]);
+            ++nvalid;
+        }
+    const uint32_t b = static_cast<uint32_t>(bias[bias_len == 1 ? 0 : o]);
+    return b - static_cast<uint32_t>(zx) * ws +
+           nvalid * static_cast<uint32_t>(ic) * static_cast<uint32_t>(zx) * static_cast<uint32_t>(zw);
+}
+
+__global__ void conv_colterm(int oc, long long ld, int kh, int kw, int ic, int n_ry, int n_rx, int base,
+                             const int* __restrict__ ky_range, const int* __restrict__ kx_range,
+                             const int32_t* __restrict__ wsum, const int32_t* __restrict__ bias, int bias_len,
+                             int32_t zx, int32_t zw, int32_t* __restrict__ colterm, int32_t* __restrict__ delta) {
+    const long long total = static_cast<long long>(n_ry) * n_rx * ld;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int o = static_cast<int>(i % ld);
+        const int cls = static_cast<int>(i / ld);
+        if (o >= oc) {
+            colterm[i] = 0;
+            delta[i] = 0;
+            continue;
+        }
+        const uint32_t t = conv_class_term(o, cls, n_rx, kh, kw, ic, ky_range, kx_range, wsum, bias, bias_len, zx, zw);
+        const uint32_t tb = conv_class_term(o, base, n_rx, kh, kw, ic, ky_range, kx_range, wsum, bias, bias_len, zx, zw);
+        colterm[i] = static_cast<int32_t>(t);
+        delta[i] = static_cast<int32_t>(t - tb);
+    }
+}
+
+}  // namespace tb

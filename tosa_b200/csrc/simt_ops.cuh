@@ -1,0 +1,304 @@
+// HBM-bound pooling and elementwise kernels (CUDA cores).
+//   AVG_POOL2D   src/ops/pool.rs:164-231 (int: wrapping i32 sum of x - zp over
+//                in-bounds taps, then apply_scale_32 by reciprocal_scale(count))
+//   MAX_POOL2D   src/ops/pool.rs:251-286
+//   RESCALE      src/ops/type_conv.rs:168-190
+//   CLAMP        src/ops/elementwise.rs:319-343
+//   ADD          src/ops/elementwise.rs:395-397
+// Every thread walks a grid-stride loop; int8 NHWC pooling handles 4
+// channels per thread with char4 loads when C % 4 == 0.
+#pragma once
+
+#include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "quant.cuh"
+#include "simt_kernels.cuh"
+
+namespace tb {
+
+struct PoolGeomDev {
+    int n, ih, iw, c, oh, ow, ky, kx, sy, sx, pad_t, pad_l;
+};
+
+// quant.rs:6-11
+__device__ __forceinline__ void reciprocal_scale_dev(int32_t value, int32_t* m, int32_t* s) {
+    const int k = 32 - __clz(static_cast<uint32_t>(value) - 1u);
+    const int64_t numerator = ((1ll << 30) + 1) << k;
+    *m = static_cast<int32_t>(numerator / value);
+    *s = 30 + k;
+}
+
+__device__ __forceinline__ int32_t int_lo(int dt) { return dt == DT_INT8 ? -128 : dt == DT_INT16 ? -32768 : INT32_MIN; }
+__device__ __forceinline__ int32_t int_hi(int dt) { return dt == DT_INT8 ? 127 : dt == DT_INT16 ? 32767 : INT32_MAX; }
+
+__device__ __forceinline__ int32_t load_int(const void* p, long long i, int dt) {
+    if (dt == DT_INT8) return static_cast<const int8_t*>(p)[i];
+    if (dt == DT_INT16) return static_cast<const int16_t*>(p)[i];
+    return static_cast<const int32_t*>(p)[i];
+}
+
+// One AVG_POOL2D output (integer), channel c of pixel (b, oy, ox).
+__device__ __forceinline__ int32_t avg_pool_int_one(const PoolGeomDev& g, const void* x, int dt, int b, int oy, int ox,
+                                                    int c, int32_t zi, int32_t zo, uint32_t* err) {
+    const int iy0 = oy * g.sy - g.pad_t, ix0 = ox * g.sx - g.pad_l;
+    uint32_t acc = 0;
+    int count = 0;
+    for (int ky = 0; ky < g.ky; ++ky) {
+        const int y = iy0 + ky;
+        if (y < 0 || y >= g.ih) continue;
+        for (int kx = 0; kx < g.kx; ++kx) {
+            const int xx = ix0 + kx;
+            if (xx < 0 || xx >= g.iw) continue;
+            acc += static_cast<uint32_t>(load_int(x, ((static_cast<long long>(b) * g.ih + y) * g.iw + xx) * g.c + c, dt) - zi);
+            ++count;
+        }
+    }
+    int32_t m, s;
+    reciprocal_scale_dev(count, &m, &s);
+    const int64_t r = rescale_value(static_cast<int32_t>(acc), m, s, ROUND_SINGLE, 1, zo, int_lo(dt), int_hi(dt), err);
+    return static_cast<int32_t>(r);
+}
+
+__global__ void avg_pool_int(PoolGeomDev g, const void* __restrict__ x, int dt, int32_t zi, int32_t zo, void* out,
+                             uint32_t* err) {
+    const long long total = static_cast<long long>(g.n) * g.oh * g.ow * g.c;
+    uint32_t lerr = 0;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int c = static_cast<int>(i % g.c);
+        long long r = i / g.c;
+        const int ox = static_cast<int>(r % g.ow);
+        r /= g.ow;
+        const int oy = static_cast<int>(r % g.oh);
+        const int b = static_cast<int>(r / g.oh);
+        store_int(out, i, dt, avg_pool_int_one(g, x, dt, b, oy, ox, c, zi, zo, &lerr));
+    }
+    if (lerr) atomicOr(err, lerr);
+}
+
+// int8, C % 4 == 0: four channels per thread.
+__global__ void avg_pool_i8_vec4(PoolGeomDev g, const int8_t* __restrict__ x, int32_t zi, int32_t zo, int8_t* out,
+                                 uint32_t* err) {
+    const int cg = g.c >> 2;
+    const long long total = static_cast<long long>(g.n) * g.oh * g.ow * cg;
+    uint32_t lerr = 0;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int c4 = static_cast<int>(i % cg) * 4;
+        long long r = i / cg;
+        const int ox = static_cast<int>(r % g.ow);
+        r /= g.ow;
+        const int oy = static_cast<int>(r % g.oh);
+        const int b = static_cast<int>(r / g.oh);
+        const int iy0 = oy * g.sy - g.pad_t, ix0 = ox * g.sx - g.pad_l;
+        uint32_t acc[4] = {0, 0, 0, 0};
+        int count = 0;
+        for (int ky = 0; ky < g.ky; ++ky) {
+            const int y = iy0 + ky;
+            if (y < 0 || y >= g.ih) continue;
+            for (int kx = 0; kx < g.kx; ++kx) {
+                const int xx = ix0 + kx;
+                if (xx < 0 || xx >= g.iw) continue;
+                const char4 v = __ldg(reinterpret_cast<const char4*>(
+                    x + ((static_cast<long long>(b) * g.ih + y) * g.iw + xx) * g.c + c4));
+                acc[0] += static_cast<uint32_t>(v.x - zi);
+                acc[1] += static_cast<uint32_t>(v.y - zi);
+                acc[2] += static_cast<uint32_t>(v.z - zi);
+                acc[3] += static_cast<uint32_t>(v.w - zi);
+                ++count;
+            }
+        }
+        int32_t m, s;
+        reciprocal_scale_dev(count, &m, &s);
+        char4 o;
+        o.x = static_cast<signed char>(rescale_value(static_cast<int32_t>(acc[0]), m, s, ROUND_SINGLE, 1, zo, -128, 127, &lerr));
+        o.y = static_cast<signed char>(rescale_value(static_cast<int32_t>(acc[1]), m, s, ROUND_SINGLE, 1, zo, -128, 127, &lerr));
+        o.z = static_cast<signed char>(rescale_value(static_cast<int32_t>(acc[2]), m, s, ROUND_SINGLE, 1, zo, -128, 127, &lerr));
+        o.w = static_cast<signed char>(rescale_value(static_cast<int32_t>(acc[3]), m, s, ROUND_SINGLE, 1, zo, -128, 127, &lerr));
+        reinterpret_cast<char4*>(out)[i] = o;
+    }
+    if (lerr) atomicOr(err, lerr);
+}
+
+// Float AVG_POOL2D: every add and the division rounded to acc_dt, the result
+// rounded to the data type (pool.rs:215-227).
+__global__ void avg_pool_float(PoolGeomDev g, const void* __restrict__ x, int dt, int acc_dt, void* out) {
+    const long long total = static_cast<long long>(g.n) * g.oh * g.ow * g.c;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int c = static_cast<int>(i % g.c);
+        long long r = i / g.c;
+        const int ox = static_cast<int>(r % g.ow);
+        r /= g.ow;
+        const int oy = static_cast<int>(r % g.oh);
+        const int b = static_cast<int>(r / g.oh);
+        const int iy0 = oy * g.sy - g.pad_t, ix0 = ox * g.sx - g.pad_l;
+        float acc = 0.f;
+        int count = 0;
+        for (int ky = 0; ky < g.ky; ++ky) {
+            const int y = iy0 + ky;
+            if (y < 0 || y >= g.ih) continue;
+            for (int kx = 0; kx < g.kx; ++kx) {
+                const int xx = ix0 + kx;
+                if (xx < 0 || xx >= g.iw) continue;
+                acc = round_to_dtype(__fadd_rn(acc, load_f(x, ((static_cast<long long>(b) * g.ih + y) * g.iw + xx) * g.c + c, dt)),
+                                     acc_dt);
+                ++count;
+            }
+        }
+        const float v = round_to_dtype(__fdiv_rn(acc, static_cast<float>(count)), acc_dt);
+        store_f(out, i, dt, round_to_dtype(v, dt));
+    }
+}
+
+__global__ void max_pool_int(PoolGeomDev g, const void* __restrict__ x, int dt, void* out) {
+    const long long total = static_cast<long long>(g.n) * g.oh * g.ow * g.c;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int c = static_cast<int>(i % g.c);
+        long long r = i / g.c;
+        const int ox = static_cast<int>(r % g.ow);
+        r /= g.ow;
+        const int oy = static_cast<int>(r % g.oh);
+        const int b = static_cast<int>(r / g.oh);
+        const int iy0 = oy * g.sy - g.pad_t, ix0 = ox * g.sx - g.pad_l;
+        int32_t m = int_lo(dt);
+        for (int ky = 0; ky < g.ky; ++ky) {
+            const int y = iy0 + ky;
+            if (y < 0 || y >= g.ih) continue;
+            for (int kx = 0; kx < g.kx; ++kx) {
+                const int xx = ix0 + kx;
+                if (xx < 0 || xx >= g.iw) continue;
+                m = max(m, load_int(x, ((static_cast<long long>(b) * g.ih + y) * g.iw + xx) * g.c + c, dt));
+            }
+        }
+        store_int(out, i, dt, m);
+    }
+}
+
+// int8, C % 4 == 0: byte-wise signed max over char4 words (__vmaxs4).
+__global__ void max_pool_i8_vec4(PoolGeomDev g, const int8_t* __restrict__ x, int8_t* out) {
+    const int cg = g.c >> 2;
+    const long long total = static_cast<long long>(g.n) * g.oh * g.ow * cg;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int c4 = static_cast<int>(i % cg) * 4;
+        long long r = i / cg;
+        const int ox = static_cast<int>(r % g.ow);
+        r /= g.ow;
+        const int oy = static_cast<int>(r % g.oh);
+        const int b = static_cast<int>(r / g.oh);
+        const int iy0 = oy * g.sy - g.pad_t, ix0 = ox * g.sx - g.pad_l;
+        unsigned m = 0x80808080u;
+        for (int ky = 0; ky < g.ky; ++ky) {
+            const int y = iy0 + ky;
+            if (y < 0 || y >= g.ih) continue;
+            for (int kx = 0; kx < g.kx; ++kx) {
+                const int xx = ix0 + kx;
+                if (xx < 0 || xx >= g.iw) continue;
+                const unsigned v = __ldg(reinterpret_cast<const unsigned*>(
+                    x + ((static_cast<long long>(b) * g.ih + y) * g.iw + xx) * g.c + c4));
+                m = __vmaxs4(m, v);
+            }
+        }
+        reinterpret_cast<unsigned*>(out)[i] = m;
+    }
+}
+
+// NaN-aware max / min of the reference (common.rs:153-177): ties keep a (max)
+// or b (min); with IGNORE a NaN operand yields the other one.
+__device__ __forceinline__ float nan_pick(float a, float b, int mode) {
+    if (mode == 2) return isnan(a) ? b : a;
+    return __int_as_float(0x7fc00000);
+}
+__device__ __forceinline__ float nan_max(float a, float b, int mode) {
+    if (isnan(a) || isnan(b)) return nan_pick(a, b, mode);
+    return a >= b ? a : b;
+}
+__device__ __forceinline__ float nan_min(float a, float b, int mode) {
+    if (isnan(a) || isnan(b)) return nan_pick(a, b, mode);
+    return a < b ? a : b;
+}
+
+__global__ void max_pool_float(PoolGeomDev g, const void* __restrict__ x, int dt, int nan_mode, void* out) {
+    const long long total = static_cast<long long>(g.n) * g.oh * g.ow * g.c;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int c = static_cast<int>(i % g.c);
+        long long r = i / g.c;
+        const int ox = static_cast<int>(r % g.ow);
+        r /= g.ow;
+        const int oy = static_cast<int>(r % g.oh);
+        const int b = static_cast<int>(r / g.oh);
+        const int iy0 = oy * g.sy - g.pad_t, ix0 = ox * g.sx - g.pad_l;
+        float m = nan_mode == 2 ? __int_as_float(0x7fc00000) : -INFINITY;
+        for (int ky = 0; ky < g.ky; ++ky) {
+            const int y = iy0 + ky;
+            if (y < 0 || y >= g.ih) continue;
+            for (int kx = 0; kx < g.kx; ++kx) {
+                const int xx = ix0 + kx;
+                if (xx < 0 || xx >= g.iw) continue;
+                m = nan_max(m, load_f(x, ((static_cast<long long>(b) * g.ih + y) * g.iw + xx) * g.c + c, dt), nan_mode);
+            }
+        }
+        store_f(out, i, dt, m);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Elementwise
+// ---------------------------------------------------------------------------
+
+// RESCALE: x = extend(v) - in_zp (extend masks to the width when unsigned).
+__global__ void rescale_elementwise(const void* __restrict__ in, int in_dt, int in_unsigned, int32_t in_zp_ext,
+                                    long long count, int channels, RescaleArgs rs, int out_dt, void* out,
+                                    uint32_t* err) {
+    uint32_t lerr = 0;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < count;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        int64_t v = load_int(in, i, in_dt);
+        if (in_unsigned) v &= in_dt == DT_INT8 ? 0xff : 0xffff;
+        const int64_t x = v - in_zp_ext;
+        const int ch = rs.per_channel ? static_cast<int>(i % channels) : 0;
+        const int64_t r = rescale_value(x, rs.multiplier[ch], rs.shift[ch], rs.rounding, rs.scale32, rs.out_zp, rs.lo,
+                                        rs.hi, &lerr);
+        store_int(out, i, out_dt, static_cast<int32_t>(r));
+    }
+    if (lerr) atomicOr(err, lerr);
+}
+
+__global__ void clamp_int(const void* __restrict__ in, int dt, long long count, int32_t lo, int32_t hi, void* out) {
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < count;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        int32_t v = load_int(in, i, dt);
+        v = max(v, lo);
+        v = min(v, hi);
+        store_int(out, i, dt, v);
+    }
+}
+
+__global__ void clamp_float(const void* __restrict__ in, int dt, long long count, float lo, float hi, int nan_mode,
+                            void* out) {
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < count;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const float v = nan_min(nan_max(load_f(in, i, dt), lo, nan_mode), hi, nan_mode);
+        store_f(out, i, dt, v);
+    }
+}
+
+__global__ void add_elementwise(const void* __restrict__ a, const void* __restrict__ b, int dt, long long count,
+                                void* out) {
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < count;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        if (dt == DT_INT32) {
+            static_cast<int32_t*>(out)[i] = static_cast<int32_t>(static_cast<uint32_t>(static_cast<const int32_t*>(a)[i]) +
+                                                                 static_cast<uint32_t>(static_cast<const int32_t*>(b)[i]));
+        } else {
+            store_f(out, i, dt, round_to_dtype(__fadd_rn(load_f(a, i, dt), load_f(b, i, dt)), dt));
+        }
+    }
+}
+
+}  // namespace tb

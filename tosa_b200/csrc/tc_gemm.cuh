@@ -1,0 +1,703 @@
+// Persistent warp-specialised tcgen05 GEMM / implicit-GEMM convolution for
+// sm_100a with a fused TOSA epilogue.
+//
+// One CTA per SM (384 threads, 12 warps):
+//   warp 0      TMA producer: A tiles (plain 3-D tiles, or im2col windows of
+//               an NHWC activation for CONV2D) and B tiles into a STAGES-deep
+//               shared-memory ring; no multicast.
+//   warp 1      TMEM owner and MMA issuer: tcgen05.mma (kind::i8 -> s32, or
+//               kind::f16 -> f32) into one of two 128 x BN accumulators.
+//   warps 2-3   zero-point row sums: when the B-side zero point is non-zero,
+//               sum every A row of each stage from shared memory (dp4a, bank-
+//               conflict-free chunk order) so the epilogue can apply
+//               -zp_b * rowsum(A). 64 rows per warp.
+//   warps 4-11  epilogue, two warps per SM sub-partition: warp w reads TMEM
+//               lanes 32*(w%4)..+31 (one output row per thread) and the half
+//               (w-4)/4 of the tile's columns; the next 16 columns are loaded
+//               from TMEM while the current ones are processed.
+//
+// The accumulator is double-buffered in TMEM, so the epilogue of tile t
+// overlaps the main loop of tile t+1. All waits are bounded: a wait that
+// gives up sets DEV_ERR_TIMEOUT in the device error word and the CTA unwinds.
+//
+// Arithmetic contract (integer): the tensor core forms sum(a*b) over raw
+// int8 operands exactly; with the zero points the reference's
+//   sum_valid (x - zx)(w - zw)
+//     = sum x*w - zw*sum_valid x - zx*sum_valid w + n_valid*zx*zw  (mod 2^32)
+// is rebuilt in the epilogue. Padded convolution taps are zero-filled by TMA
+// and so drop out of sum x*w and of the row sums; the per-output-channel
+// terms depend only on which taps are valid, so they are precomputed per
+// border class by the convolution plan (a base table plus per-class deltas).
+// All sums wrap mod 2^32 like AccI32 (src/ops/accum.rs:28-41), so the result
+// is bit-exact in any order.
+//
+// RESCALE fast path (every shift in [32, 62], multiplier >= 0; checked on the
+// host): the reference's apply_scale_32 (src/ops/quant.rs:17-32) computes
+// (v*m + round) >> s with round = 2^(s-1) [+2^30 for v >= 0, -2^30 for v < 0
+// under double rounding], then adds the output zero point. In this range every
+// int32 v is admissible and nothing overflows, so the kernel evaluates the
+// high word of the 64-bit sum v*m + R with two instructions (mad.lo.cc +
+// madc.hi) and shifts it right by s-32. The host packs per channel
+// {m, s-32, R_lo, R_hi} for v >= 0 and {R_lo, R_hi} for v < 0, where R already
+// contains the output zero point as zp * 2^s when s <= 55 (exact: the sum stays
+// below 2^63 and zp * 2^s only adds zp to the shifted result).
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+
+#include "ptx.cuh"
+#include "quant.cuh"
+
+namespace tb {
+
+enum : int { EPI_I32 = 0, EPI_RESCALE = 1, EPI_F32 = 2, EPI_FCONV = 3 };
+
+// Compile-time epilogue kind: each kernel instantiation carries only the code
+// of one epilogue, which keeps its hot loop small and well scheduled.
+enum : int {
+    EK_I32 = 0,        // int32 store of acc + zero-point terms
+    EK_SLOW = 1,       // general RESCALE (range checks, inexact, scale16), any integer output type
+    EK_FAST_T_S = 2,   // fast RESCALE, per-tensor, single rounding, int8 out
+    EK_FAST_T_D = 3,   // fast RESCALE, per-tensor, double rounding, int8 out
+    EK_FAST_PC_S = 4,  // fast RESCALE, per-channel, single rounding, int8 out
+    EK_FAST_PC_D = 5,  // fast RESCALE, per-channel, double rounding, int8 out
+    EK_F32 = 6,        // float accumulator stored as fp32
+    EK_FCONV = 7,      // float convolution: round(round(acc) + bias) to the output type
+};
+
+constexpr int kGemmThreads = 384;
+constexpr int kEpiWarps = 8;
+
+struct GemmEpilogue {
+    int mode;                  // EPI_*
+    // Integer terms: v = acc + colterm[b][n] (+ ct_delta[class][n] on border rows) + row_zp_neg * rowsum(A row)
+    const int32_t* colterm;    // [batch or 1][>= N padded to the tile] or nullptr (then 0)
+    long long colterm_bstride; // per batch index (MATMUL: per-batch column sums), 0 otherwise
+    const int32_t* ct_delta;   // [n_classes][ct_ld] or nullptr (CONV2D border classes)
+    long long ct_ld;
+    int base_class;            // class whose terms are in colterm
+    int32_t row_zp_neg;        // -zp of the B side (0 disables the row sums)
+    int pdl_wait;              // colterm is produced by the preceding kernel (programmatic dependent launch)
+    // Convolution border classes: class = rowclass[oy] * n_col_classes + colclass[ox]
+    const uint8_t* rowclass;   // [OH] or nullptr (single class)
+    const uint8_t* colclass;   // [OW]
+    int n_col_classes;
+    // RESCALE
+    RescaleArgs rs;
+    int rs_fast;               // every shift in [32, 62], multipliers >= 0 (host-verified)
+    int rs_zp_folded;          // out_zp is inside the packed R constants
+    const int4* rq;            // fast path: [channels padded][2]: {m, s-32, rp_lo, rp_hi}, {rn_lo, rn_hi, -, -}
+    int out_dtype;             // DT_INT8 / DT_INT16 / DT_INT32 / DT_FP32 / DT_BF16 / DT_FP16
+    // Float convolution: out = round(round(acc) + fbias[n])
+    const float* fbias;        // [N] or [1]
+    int fbias_len;
+};
+
+// Column sums of MATMUL's B operand computed inside the GEMM (a_zp != 0):
+// the epilogue warps of every CTA reduce a share of 64-column units of
+// B[n][c][w] while the first main loop runs, write the final column term
+// scale * colsum + add, and count finished units on a global counter; every
+// epilogue waits (bounded) until counter >= target before its first tile.
+// target grows by `units` per launch, so the counter never needs a reset.
+// Requires all CTAs co-resident (cooperative launch).
+struct ColsumJob {
+    const int8_t* b;           // nullptr: no job
+    int c, w, units;           // units = n * ceil(w / 64)
+    int32_t scale, add;
+    int32_t* out;              // [n][w] (+ padding)
+    unsigned int* counter;
+    unsigned int target;
+};
+
+struct GemmParams {
+    int M, N, K;               // per batch
+    int batch;
+    int in_bf16;               // kind::f16 operands: 1 = bf16, 0 = f16
+    int m_tiles, n_tiles, k_blocks;
+    int total_tiles;
+    // im2col geometry (CONV2D)
+    int conv_OW, conv_OHOW;
+    int stride_h, stride_w, pad_t, pad_l;
+    int KW, dil_h, dil_w;
+    int c_blocks;              // k blocks per filter tap
+    int IC;                    // channels per tap (B column offset per tap)
+    // output
+    void* out;
+    long long out_batch_stride;  // elements
+    long long ldo;               // elements per output row
+    GemmEpilogue epi;
+    uint32_t* err;
+    long long timeout_cycles;
+    // Optional timeline of CTA 0 (clock64 stamps), nullptr in normal runs:
+    // [0,128) producer per stage issue, [128,256) MMA per stage start,
+    // [256,384) row-sum per stage done, [384,400) epilogue tile start/end.
+    long long* trace;
+    ColsumJob cs;
+};
+
+template <int KIND, int BN, int BK_BYTES, bool B_MN_MAJOR, bool IM2COL, int STAGES>
+struct GemmCfg {
+    static constexpr int kKind = KIND;            // 0: int8, 1: f16/bf16
+    static constexpr int BM = 128;
+    static constexpr int kBN = BN;
+    static constexpr int kBKBytes = BK_BYTES;     // 64 (SW64) or 128 (SW128)
+    static constexpr int kElem = KIND == 0 ? 1 : 2;
+    static constexpr int BK = BK_BYTES / kElem;   // elements of K per stage
+    static constexpr int kMmaK = 32 / kElem;      // K per tcgen05.mma (32 bytes)
+    static constexpr int kStages = STAGES;
+    static constexpr bool kBMN = B_MN_MAJOR;
+    static constexpr bool kIm2col = IM2COL;
+    static constexpr int A_BYTES = BM * BK_BYTES;
+    static constexpr int B_BYTES = BN * BK_BYTES;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int SW_CODE = BK_BYTES == 128 ? 2 : 4;        // UMMA layout type
+    static constexpr int ATOM_SBO = 8 * BK_BYTES;                   // 8 rows of one swizzle atom
+    // MN-major B: 128-byte rows of N, one box per 128 bytes of N.
+    static constexpr int B_MN_CHUNK = 128 / kElem;                  // N elements per box
+    static constexpr int B_MN_BOX_BYTES = BK * 128;                 // BK k-rows x 128 bytes
+    static constexpr int TMEM_COLS = 2 * BN <= 32 ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
+    static constexpr int SCRATCH_BYTES = 8192;  // epilogue: column-sum reduction and staged column terms
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 2048 /*barriers, row sums*/ + SCRATCH_BYTES;
+    static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "UMMA N for M=128; each epilogue half walks pairs of 16-column chunks");
+    static_assert(!B_MN_MAJOR || BK_BYTES == 128, "MN-major B uses 128-byte K blocks");
+};
+
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ void tile_coords(const GemmParams& p, int tile, int& b, int& mt, int& nt) {
+    // m fastest so CTAs running concurrently share the B tile in L2.
+    mt = tile % p.m_tiles;
+    int rest = tile / p.m_tiles;
+    nt = rest % p.n_tiles;
+    b = rest / p.n_tiles;
+}
+
+// Makes the 16 registers of a finished tcgen05.ld visible only after the
+// wait: the asm redefines them, so no use can be scheduled above it.
+__device__ __forceinline__ void tmem_wait_regs(uint32_t (&r)[16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15]));
+}
+
+constexpr int kChunk = 16;  // output columns per thread per TMEM load
+
+__device__ __forceinline__ uint32_t pack4_i8(int32_t a, int32_t b, int32_t c, int32_t d) {
+    const uint32_t lo = __byte_perm(static_cast<uint32_t>(a), static_cast<uint32_t>(b), 0x0040);
+    const uint32_t hi = __byte_perm(static_cast<uint32_t>(c), static_cast<uint32_t>(d), 0x0040);
+    return __byte_perm(lo, hi, 0x5410);
+}
+
+// High word of the 64-bit sum v*m + (rhi:rlo), v and m signed 32-bit.
+__device__ __forceinline__ int32_t mad_wide_hi(int32_t v, int32_t m, uint32_t rlo, uint32_t rhi) {
+    const int64_t r = static_cast<int64_t>((static_cast<uint64_t>(rhi) << 32) | rlo);
+    const int64_t t = static_cast<int64_t>(v) * m + r;  // one wide multiply-add with a 64-bit addend
+    return static_cast<int32_t>(static_cast<uint64_t>(t) >> 32);
+}
+
+template <bool PC, bool DBL>
+__device__ __forceinline__ void rescale_fast(const int32_t (&v)[kChunk], int32_t (&res)[kChunk],
+                                             const int4* __restrict__ rq, int4 P, int4 Q, int n0, int32_t lo,
+                                             int32_t hi, int32_t add_zp) {
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j) {
+        if (PC) {
+            P = __ldg(rq + 2 * (n0 + j));
+            if (DBL) Q = __ldg(rq + 2 * (n0 + j) + 1);
+        }
+        uint32_t rlo = static_cast<uint32_t>(P.z), rhi = static_cast<uint32_t>(P.w);
+        if (DBL) {
+            const bool neg = v[j] < 0;
+            rlo = neg ? static_cast<uint32_t>(Q.x) : rlo;
+            rhi = neg ? static_cast<uint32_t>(Q.y) : rhi;
+        }
+        const int32_t y = (mad_wide_hi(v[j], P.x, rlo, rhi) >> P.y) + add_zp;
+        res[j] = min(max(y, lo), hi);
+    }
+}
+
+// Epilogue for kChunk consecutive output columns n0.. of one row (one thread).
+template <int EK>
+__device__ __forceinline__ void epilogue_chunk(const GemmParams& p, const uint32_t (&acc)[kChunk], int n0,
+                                               long long orow, int32_t rowterm, const int32_t* colterm,
+                                               const int32_t* delta, int4 P0, int4 Q0, uint32_t& err) {
+    const GemmEpilogue& e = p.epi;
+    uint8_t* outp = reinterpret_cast<uint8_t*>(p.out);
+    const int ncols = min(kChunk, p.N - n0);
+    if constexpr (EK == EK_F32 || EK == EK_FCONV) {
+        float v[kChunk];
+#pragma unroll
+        for (int j = 0; j < kChunk; ++j) {
+            float a = __uint_as_float(acc[j]);
+            if constexpr (EK == EK_FCONV) {
+                const int n = min(n0 + j, p.N - 1);
+                const float bias = __ldg(e.fbias + (e.fbias_len == 1 ? 0 : n));
+                a = round_to_dtype(__fadd_rn(round_to_dtype(a, e.out_dtype), bias), e.out_dtype);
+            }
+            v[j] = a;
+        }
+        if (e.out_dtype == DT_FP32) {
+            float* o = reinterpret_cast<float*>(outp) + orow + n0;
+            if (ncols == kChunk && ((reinterpret_cast<uintptr_t>(o) & 15) == 0)) {
+#pragma unroll
+                for (int j = 0; j < kChunk; j += 4) *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < kChunk; ++j) if (j < ncols) o[j] = v[j];
+            }
+        } else if (e.out_dtype == DT_BF16) {
+            __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(outp) + orow + n0;
+#pragma unroll
+            for (int j = 0; j < kChunk; ++j) if (j < ncols) o[j] = __float2bfloat16_rn(v[j]);
+        } else {
+            __half* o = reinterpret_cast<__half*>(outp) + orow + n0;
+#pragma unroll
+            for (int j = 0; j < kChunk; ++j) if (j < ncols) o[j] = __float2half_rn(v[j]);
+        }
+        return;
+    } else {
+    // colterm / delta are padded by the host to whole tiles, so n0 + j needs no clamp.
+    int32_t v[kChunk];
+    if (colterm != nullptr) {
+        // 16-byte loads of the column terms (tables are 16-byte aligned and padded to whole tiles)
+        // column terms staged in shared memory for the tile (16-byte loads)
+        const int4* ct4 = reinterpret_cast<const int4*>(colterm + n0);
+#pragma unroll
+        for (int j = 0; j < kChunk; j += 4) {
+            const int4 c = ct4[j / 4];
+            v[j + 0] = static_cast<int32_t>(acc[j + 0] + static_cast<uint32_t>(c.x) + static_cast<uint32_t>(rowterm));
+            v[j + 1] = static_cast<int32_t>(acc[j + 1] + static_cast<uint32_t>(c.y) + static_cast<uint32_t>(rowterm));
+            v[j + 2] = static_cast<int32_t>(acc[j + 2] + static_cast<uint32_t>(c.z) + static_cast<uint32_t>(rowterm));
+            v[j + 3] = static_cast<int32_t>(acc[j + 3] + static_cast<uint32_t>(c.w) + static_cast<uint32_t>(rowterm));
+        }
+        if (delta != nullptr) {
+            const int4* d4 = reinterpret_cast<const int4*>(delta + n0);
+#pragma unroll
+            for (int j = 0; j < kChunk; j += 4) {
+                const int4 c = __ldg(d4 + j / 4);
+                v[j + 0] = static_cast<int32_t>(static_cast<uint32_t>(v[j + 0]) + static_cast<uint32_t>(c.x));
+                v[j + 1] = static_cast<int32_t>(static_cast<uint32_t>(v[j + 1]) + static_cast<uint32_t>(c.y));
+                v[j + 2] = static_cast<int32_t>(static_cast<uint32_t>(v[j + 2]) + static_cast<uint32_t>(c.z));
+                v[j + 3] = static_cast<int32_t>(static_cast<uint32_t>(v[j + 3]) + static_cast<uint32_t>(c.w));
+            }
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < kChunk; ++j) v[j] = static_cast<int32_t>(acc[j] + static_cast<uint32_t>(rowterm));
+    }
+    if constexpr (EK == EK_I32) {
+        int32_t* o = reinterpret_cast<int32_t*>(outp) + orow + n0;
+        if (ncols == kChunk && ((reinterpret_cast<uintptr_t>(o) & 15) == 0)) {
+#pragma unroll
+            for (int j = 0; j < kChunk; j += 4) *reinterpret_cast<int4*>(o + j) = make_int4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < kChunk; ++j) if (j < ncols) o[j] = v[j];
+        }
+        return;
+    }
+    // RESCALE (+ fused CLAMP through r.lo / r.hi)
+    const RescaleArgs& r = e.rs;
+    int32_t res[kChunk];
+    if constexpr (EK >= EK_FAST_T_S && EK <= EK_FAST_PC_D) {
+        constexpr bool PC = EK == EK_FAST_PC_S || EK == EK_FAST_PC_D;
+        constexpr bool DBL = EK == EK_FAST_T_D || EK == EK_FAST_PC_D;
+        rescale_fast<PC, DBL>(v, res, e.rq, P0, Q0, n0, r.lo, r.hi, e.rs_zp_folded ? 0 : r.out_zp);
+        int8_t* o = reinterpret_cast<int8_t*>(outp) + orow + n0;
+        if (ncols == kChunk && ((reinterpret_cast<uintptr_t>(o) & 15) == 0)) {
+            *reinterpret_cast<uint4*>(o) = make_uint4(pack4_i8(res[0], res[1], res[2], res[3]),
+                                                      pack4_i8(res[4], res[5], res[6], res[7]),
+                                                      pack4_i8(res[8], res[9], res[10], res[11]),
+                                                      pack4_i8(res[12], res[13], res[14], res[15]));
+        } else {
+#pragma unroll
+            for (int j = 0; j < kChunk; ++j) if (j < ncols) o[j] = static_cast<int8_t>(res[j]);
+        }
+        return;
+    } else {
+        // General apply_scale semantics with range checks (shifts below 32, inexact rounding, scale16).
+        uint32_t dummy = 0;
+#pragma unroll
+        for (int j = 0; j < kChunk; ++j) {
+            const int ch = r.per_channel ? min(n0 + j, p.N - 1) : 0;
+            res[j] = static_cast<int32_t>(rescale_value(v[j], __ldg(r.multiplier + ch), __ldg(r.shift + ch),
+                                                        r.rounding, r.scale32, r.out_zp, r.lo, r.hi,
+                                                        j < ncols ? &err : &dummy));
+        }
+    }
+    if (e.out_dtype == DT_INT8) {
+        int8_t* o = reinterpret_cast<int8_t*>(outp) + orow + n0;
+        if (ncols == kChunk && ((reinterpret_cast<uintptr_t>(o) & 15) == 0)) {
+            *reinterpret_cast<uint4*>(o) = make_uint4(pack4_i8(res[0], res[1], res[2], res[3]),
+                                                      pack4_i8(res[4], res[5], res[6], res[7]),
+                                                      pack4_i8(res[8], res[9], res[10], res[11]),
+                                                      pack4_i8(res[12], res[13], res[14], res[15]));
+        } else {
+#pragma unroll
+            for (int j = 0; j < kChunk; ++j) if (j < ncols) o[j] = static_cast<int8_t>(res[j]);
+        }
+    } else if (e.out_dtype == DT_INT16) {
+        int16_t* o = reinterpret_cast<int16_t*>(outp) + orow + n0;
+#pragma unroll
+        for (int j = 0; j < kChunk; ++j) if (j < ncols) o[j] = static_cast<int16_t>(res[j]);
+    } else {
+        int32_t* o = reinterpret_cast<int32_t*>(outp) + orow + n0;
+#pragma unroll
+        for (int j = 0; j < kChunk; ++j) if (j < ncols) o[j] = res[j];
+    }
+    }
+}
+
+template <class Cfg, int EK>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
+    constexpr int BM = Cfg::BM, BN = Cfg::kBN, S = Cfg::kStages;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* stage_base = smem;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::STAGE_BYTES);
+    uint64_t* full = bars;               // [S]
+    uint64_t* empty = bars + S;          // [S]
+    uint64_t* tfull = bars + 2 * S;      // [2]
+    uint64_t* tempty = bars + 2 * S + 2; // [2]
+    uint64_t* rsfull = bars + 2 * S + 4; // [2]
+    uint64_t* rsempty = bars + 2 * S + 6;// [2]
+    uint64_t* mdrain = bars + 2 * S + 8; // [1]
+    uint64_t* ebar = bars + 2 * S + 9;   // [1] epilogue-group barrier (8 warps)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 10);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    int32_t* rowsum_buf = reinterpret_cast<int32_t*>(tmem_slot + 4);  // [2][128]
+    int32_t* scratch = reinterpret_cast<int32_t*>(smem + S * Cfg::STAGE_BYTES + 2048);  // SCRATCH_BYTES
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const bool need_rowsum = Cfg::kKind == 0 && p.epi.row_zp_neg != 0;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], need_rowsum ? 3 : 1);  // MMA commit + two row-sum warps
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], kEpiWarps);
+            mbar_init(&rsfull[b], 2);
+            mbar_init(&rsempty[b], kEpiWarps);
+        }
+        mbar_init(&mdrain[0], 1);
+        mbar_init(&ebar[0], kEpiWarps);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const long long limit = p.timeout_cycles;
+    if (p.trace && blockIdx.x == 0 && threadIdx.x == 0) p.trace[400] = clock64();
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            uint32_t it = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
+                int b, mt, nt;
+                tile_coords(p, tile, b, mt, nt);
+                const int m0 = mt * BM, n0 = nt * BN;
+                int img = 0, wb = 0, hb = 0;
+                if constexpr (Cfg::kIm2col) {
+                    img = m0 / p.conv_OHOW;
+                    const int rem = m0 - img * p.conv_OHOW;
+                    const int oy = rem / p.conv_OW, ox = rem - oy * p.conv_OW;
+                    wb = ox * p.stride_w - p.pad_l;
+                    hb = oy * p.stride_h - p.pad_t;
+                }
+                for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+                    const int s = it % S;
+                    const uint32_t ph = (it / S) & 1;
+                    if (!mbar_wait_bounded(&empty[s], ph ^ 1, abort_flag, limit)) { ok = false; break; }
+                    uint8_t* sa = stage_base + s * Cfg::STAGE_BYTES;
+                    uint8_t* sb = sa + Cfg::A_BYTES;
+                    if (p.trace && blockIdx.x == 0 && it < 128) p.trace[it] = clock64();
+                    mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
+                    if constexpr (Cfg::kIm2col) {
+                        const int tap = kb / p.c_blocks, cb = kb - tap * p.c_blocks;
+                        const int ky = tap / p.KW, kx = tap - ky * p.KW;
+                        tma_load_im2col_4d(sa, &tmA, &full[s], cb * Cfg::BK, wb, hb, img,
+                                           static_cast<uint16_t>(kx * p.dil_w), static_cast<uint16_t>(ky * p.dil_h));
+                        tma_load_3d(sb, &tmB, &full[s], tap * p.IC + cb * Cfg::BK, n0, 0);
+                    } else {
+                        tma_load_3d(sa, &tmA, &full[s], kb * Cfg::BK, m0, b);
+                        if constexpr (Cfg::kBMN) {
+#pragma unroll
+                            for (int j = 0; j < BN / Cfg::B_MN_CHUNK; ++j)
+                                tma_load_3d(sb + j * Cfg::B_MN_BOX_BYTES, &tmB, &full[s], n0 + j * Cfg::B_MN_CHUNK,
+                                            kb * Cfg::BK, b);
+                        } else {
+                            tma_load_3d(sb, &tmB, &full[s], kb * Cfg::BK, n0, 0);
+                        }
+                    }
+                }
+            }
+            if (!ok) { atomicOr(p.err, DEV_ERR_TIMEOUT); *abort_flag = 1; }
+            // Drain: every issued load must land before the CTA may exit.
+            const uint32_t first = it > static_cast<uint32_t>(S) ? it - S : 0;
+            for (uint32_t i = first; i < it; ++i) mbar_wait_bounded(&full[i % S], (i / S) & 1, nullptr, limit);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            const uint32_t idesc = Cfg::kKind == 0 ? idesc_i8(BM, BN, Cfg::kBMN)
+                                                   : idesc_f16(BM, BN, p.in_bf16 != 0, Cfg::kBMN);
+            uint32_t it = 0, tcount = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++tcount) {
+                const int buf = tcount & 1;
+                const uint32_t tph = (tcount >> 1) & 1;
+                if (!mbar_wait_bounded(&tempty[buf], tph ^ 1, abort_flag, limit)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * BN);
+                for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+                    const int s = it % S;
+                    const uint32_t ph = (it / S) & 1;
+                    if (!mbar_wait_bounded(&full[s], ph, abort_flag, limit)) { ok = false; break; }
+                    tc_fence_after();
+                    if (p.trace && blockIdx.x == 0 && it < 128) p.trace[128 + it] = clock64();
+                    const uint32_t sa = smem_u32(stage_base + s * Cfg::STAGE_BYTES);
+                    const uint32_t sb = sa + Cfg::A_BYTES;
+#pragma unroll
+                    for (int k = 0; k < Cfg::kBKBytes / 32; ++k) {
+                        const uint64_t ad = smem_desc(sa + k * 32, 16, Cfg::ATOM_SBO, Cfg::SW_CODE);
+                        uint64_t bd;
+                        if constexpr (Cfg::kBMN) {
+                            // k-rows of 128 bytes; 8-row groups 1024 B apart; 128-byte N chunks one box apart.
+                            bd = smem_desc(sb + k * Cfg::kMmaK * 128, Cfg::B_MN_BOX_BYTES, 1024, 2);
+                        } else {
+                            bd = smem_desc(sb + k * 32, 16, Cfg::ATOM_SBO, Cfg::SW_CODE);
+                        }
+                        tc_mma<Cfg::kKind>(d_tmem, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                    }
+                    tc_commit(&empty[s]);  // frees the stage once these MMAs have read it
+                }
+                if (!ok) break;
+                tc_commit(&tfull[buf]);    // accumulator ready for the epilogue
+            }
+            if (!ok) {
+                atomicOr(p.err, DEV_ERR_TIMEOUT);
+                *abort_flag = 1;
+                // Let every issued MMA finish before TMEM is released.
+                tc_commit(&mdrain[0]);
+                mbar_wait_bounded(&mdrain[0], 0, nullptr, limit);
+            }
+        }
+    } else if (warp == 2 || warp == 3) {
+        // ------------------------------------------------------------ A row sums (int8, zp_b != 0)
+        if (need_rowsum) {
+            const int row0 = (warp - 2) * 64;
+            uint32_t it = 0, tcount = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++tcount) {
+                int sum0 = 0, sum1 = 0;
+                for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+                    const int s = it % S;
+                    const uint32_t ph = (it / S) & 1;
+                    if (!mbar_wait_bounded(&full[s], ph, abort_flag, limit)) { ok = false; break; }
+                    const uint8_t* sa = stage_base + s * Cfg::STAGE_BYTES;
+                    const int4* r0 = reinterpret_cast<const int4*>(sa + (row0 + lane) * Cfg::kBKBytes);
+                    const int4* r1 = reinterpret_cast<const int4*>(sa + (row0 + 32 + lane) * Cfg::kBKBytes);
+                    // Chunk order rotated per lane: the 8 lanes of a shared-memory phase hit 8 different
+                    // 16-byte bank groups (rows are 128 or 64 bytes long).
+                    const int rot = Cfg::kBKBytes == 128 ? (lane & 7) : ((lane >> 1) & 3);
+#pragma unroll
+                    for (int c = 0; c < Cfg::kBKBytes / 16; ++c) {
+                        const int cc = c ^ rot;
+                        const int4 v0 = r0[cc];
+                        const int4 v1 = r1[cc];
+                        sum0 = __dp4a(v0.x, 0x01010101, sum0);
+                        sum0 = __dp4a(v0.y, 0x01010101, sum0);
+                        sum0 = __dp4a(v0.z, 0x01010101, sum0);
+                        sum0 = __dp4a(v0.w, 0x01010101, sum0);
+                        sum1 = __dp4a(v1.x, 0x01010101, sum1);
+                        sum1 = __dp4a(v1.y, 0x01010101, sum1);
+                        sum1 = __dp4a(v1.z, 0x01010101, sum1);
+                        sum1 = __dp4a(v1.w, 0x01010101, sum1);
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&empty[s]);
+                    if (p.trace && blockIdx.x == 0 && it < 128 && warp == 2 && lane == 0) p.trace[256 + it] = clock64();
+                }
+                if (!ok) break;
+                const int buf = tcount & 1;
+                const uint32_t tph = (tcount >> 1) & 1;
+                if (!mbar_wait_bounded(&rsempty[buf], tph ^ 1, abort_flag, limit)) { ok = false; break; }
+                rowsum_buf[buf * 128 + row0 + lane] = sum0;
+                rowsum_buf[buf * 128 + row0 + 32 + lane] = sum1;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&rsfull[buf]);
+            }
+            if (!ok && lane == 0) { atomicOr(p.err, DEV_ERR_TIMEOUT); *abort_flag = 1; }
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue (warps 4..11)
+        const int q = warp & 3;                 // TMEM lane quadrant
+        const int half = (warp - 4) >> 2;       // which half of the tile's columns
+        const int row = q * 32 + lane;          // row within the tile
+        const GemmEpilogue& e = p.epi;
+        if (e.pdl_wait) grid_dependency_wait();
+        const int et = threadIdx.x - 128;       // 0..255 within the epilogue warps
+        // Bounded barrier of the 8 epilogue warps (an mbarrier phase per use).
+        uint32_t ephase = 0;
+        auto epi_sync = [&]() -> bool {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ebar[0]);
+            const bool done = mbar_wait_bounded(&ebar[0], ephase, abort_flag, limit);
+            ephase ^= 1;
+            return done;
+        };
+        int32_t* ct_stage = scratch + 1024;     // [2][256] column terms of the current tile
+        bool ok = true;
+        if (p.cs.b != nullptr) {
+            // ---- column sums of B (MATMUL a_zp): 16 column groups of 4 bytes x 16 row slices
+            const ColsumJob& cs = p.cs;
+            const int g = et & 15, slice = et >> 4;
+            const int units_w = (cs.w + 63) / 64;
+            for (int u = blockIdx.x; u < cs.units; u += gridDim.x) {
+                const int bn = u / units_w, col = (u % units_w) * 64 + g * 4;
+                int s0 = 0, s1 = 0, s2 = 0, s3 = 0;
+                if (col < cs.w) {
+                    const int8_t* src = cs.b + (static_cast<long long>(bn) * cs.c + slice) * cs.w + col;
+#pragma unroll 8
+                    for (int k = slice; k < cs.c; k += 16, src += 16ll * cs.w) {
+                        const int x = __ldg(reinterpret_cast<const int*>(src));
+                        s0 += static_cast<int8_t>(x & 0xff);
+                        s1 += static_cast<int8_t>((x >> 8) & 0xff);
+                        s2 += static_cast<int8_t>((x >> 16) & 0xff);
+                        s3 += x >> 24;
+                    }
+                }
+                int32_t* red = scratch;  // [16 slices][64 columns]
+                red[slice * 64 + g * 4 + 0] = s0;
+                red[slice * 64 + g * 4 + 1] = s1;
+                red[slice * 64 + g * 4 + 2] = s2;
+                red[slice * 64 + g * 4 + 3] = s3;
+                if (!epi_sync()) { ok = false; break; }
+                if (et < 64) {
+                    int t = 0;
+#pragma unroll
+                    for (int sl = 0; sl < 16; ++sl) t += red[sl * 64 + et];
+                    const int cc = (u % units_w) * 64 + et;
+                    if (cc < cs.w)
+                        cs.out[static_cast<long long>(bn) * cs.w + cc] =
+                            static_cast<int32_t>(static_cast<uint32_t>(cs.scale) * static_cast<uint32_t>(t) +
+                                                 static_cast<uint32_t>(cs.add));
+                    __threadfence();
+                }
+                if (!epi_sync()) { ok = false; break; }
+                if (et == 0) atomicAdd(cs.counter, 1u);
+            }
+        }
+        uint32_t tcount = 0;
+        uint32_t err = 0;
+        constexpr int HALF = BN / 2;
+        for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++tcount) {
+            int b, mt, nt;
+            tile_coords(p, tile, b, mt, nt);
+            const int buf = tcount & 1;
+            const uint32_t tph = (tcount >> 1) & 1;
+            if (!mbar_wait_bounded(&tfull[buf], tph, abort_flag, limit)) { ok = false; break; }
+            tc_fence_after();
+            if (p.trace && blockIdx.x == 0 && tcount < 8 && threadIdx.x == 128) p.trace[384 + 2 * tcount] = clock64();
+            int32_t rowterm = 0;
+            if (need_rowsum) {
+                if (!mbar_wait_bounded(&rsfull[buf], tph, abort_flag, limit)) { ok = false; break; }
+                rowterm = static_cast<int32_t>(static_cast<uint32_t>(e.row_zp_neg) *
+                                               static_cast<uint32_t>(rowsum_buf[buf * 128 + row]));
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&rsempty[buf]);
+            }
+            const int m = mt * BM + row;
+            const bool row_ok = m < p.M;
+            const int32_t* colterm = nullptr;
+            if (e.colterm != nullptr) {
+                if (p.cs.b != nullptr && tcount == 0) {
+                    // all column sums published (bounded wait on the cross-CTA counter)
+                    const long long t0 = clock64();
+                    while (*reinterpret_cast<volatile unsigned int*>(p.cs.counter) < p.cs.target) {
+                        if (*abort_flag || clock64() - t0 > limit) { ok = false; break; }
+                    }
+                    __threadfence();
+                    if (!ok) break;
+                }
+                // stage this tile's column terms in shared memory
+                int32_t* cst = ct_stage + (tcount & 1) * 256;
+                if (et < BN) cst[et] = e.colterm[b * e.colterm_bstride + nt * BN + et];
+                if (!epi_sync()) { ok = false; break; }
+                colterm = cst - nt * BN;
+            }
+            const int32_t* delta = nullptr;
+            if (e.rowclass != nullptr && row_ok) {
+                const int rem = m % p.conv_OHOW;
+                const int oy = rem / p.conv_OW, ox = rem % p.conv_OW;
+                const int cls = e.rowclass[oy] * e.n_col_classes + e.colclass[ox];
+                if (cls != e.base_class) delta = e.ct_delta + static_cast<long long>(cls) * e.ct_ld;
+            }
+            const int cbase = half * HALF;
+            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                                   static_cast<uint32_t>(buf * BN + cbase);
+            const long long orow = static_cast<long long>(b) * p.out_batch_stride + static_cast<long long>(m) * p.ldo;
+            const int nb = nt * BN + cbase;
+            // Per-tensor rescale constants (channel 0), loaded once per tile.
+            int4 P0 = make_int4(0, 0, 0, 0), Q0 = make_int4(0, 0, 0, 0);
+            if constexpr (EK >= EK_FAST_T_S && EK <= EK_FAST_PC_D) {
+                P0 = __ldg(e.rq);
+                Q0 = __ldg(e.rq + 1);
+            }
+            // Two register sets: the next chunk's TMEM load overlaps this chunk's epilogue.
+            uint32_t accA[kChunk], accB[kChunk];
+            __syncwarp();
+            tmem_ld_32x32b_x16(taddr, accA);
+            tmem_wait_regs(accA);
+#pragma unroll 1
+            for (int c0 = 0; c0 < HALF; c0 += 2 * kChunk) {
+                const bool tr = p.trace && blockIdx.x == 0 && tcount == 0 && threadIdx.x == 128;
+                if (tr) p.trace[408 + (c0 / kChunk) * 2] = clock64();
+                __syncwarp();
+                tmem_ld_32x32b_x16(taddr + c0 + kChunk, accB);
+                if (row_ok && nb + c0 < p.N) epilogue_chunk<EK>(p, accA, nb + c0, orow, rowterm, colterm, delta, P0, Q0, err);
+                if (tr) p.trace[409 + (c0 / kChunk) * 2] = clock64();
+                __syncwarp();
+                tmem_wait_regs(accB);
+                if (c0 + 2 * kChunk < HALF) tmem_ld_32x32b_x16(taddr + c0 + 2 * kChunk, accA);
+                if (row_ok && nb + c0 + kChunk < p.N)
+                    epilogue_chunk<EK>(p, accB, nb + c0 + kChunk, orow, rowterm, colterm, delta, P0, Q0, err);
+                __syncwarp();
+                if (c0 + 2 * kChunk < HALF) tmem_wait_regs(accA);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[buf]);
+            if (p.trace && blockIdx.x == 0 && tcount < 8 && threadIdx.x == 128) p.trace[385 + 2 * tcount] = clock64();
+        }
+        if (!ok && lane == 0) { atomicOr(p.err, DEV_ERR_TIMEOUT); *abort_flag = 1; }
+        if (err) atomicOr(p.err, err);
+    }
+
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+    }
+}
+
+}  // namespace tb
