@@ -92,7 +92,7 @@ static CUtensorMapDataType tmap_dtype(int dt) {
     return CU_TENSOR_MAP_DATA_TYPE_UINT8;
 }
 
-static int grid_for(const tb_context* ctx, long long work, int block = 256) {
+int grid_for(const tb_context* ctx, long long work, int block) {
     long long g = (work + block - 1) / block;
     long long cap = static_cast<long long>(ctx->num_sms) * 8;
     if (g > cap) g = cap;
@@ -168,8 +168,8 @@ tb_status check_rescale(const tb_rescale_attr* a, int in_t, int64_t shape_last, 
     return TB_OK;
 }
 
-tb_status make_rescale_plan(tb_context* ctx, const tb_rescale_attr* a, int in_t, int64_t shape_last, RescalePlan* r) {
-    (void)ctx;
+tb_status prepare_rescale(const tb_rescale_attr* a, int in_t, int64_t shape_last, RescalePlan* r,
+                          std::vector<int32_t>* blob) {
     int64_t izp, ozp;
     int32_t lo, hi;
     TB_TRY(check_rescale(a, in_t, shape_last, &izp, &ozp, &lo, &hi));
@@ -190,6 +190,10 @@ tb_status make_rescale_plan(tb_context* ctx, const tb_rescale_attr* a, int in_t,
         if (m[i] < 0 || s[i] < 32 || s[i] > 62) fast = false;
     }
     r->fast = fast;
+    // Blob layout (int32 words): [rq: 8 per padded channel (fast path only)] [multiplier] [shift].
+    const size_t padded = (static_cast<size_t>(a->channels) + 255) / 256 * 256;
+    const size_t rq_words = fast ? 8 * padded : 0;
+    blob->assign(rq_words + 2 * static_cast<size_t>(a->channels), 0);
     if (fast) {
         // R = 2^(s-1) (+2^30 for v >= 0, -2^30 for v < 0 under double rounding) as 64-bit lo/hi words;
         // when every shift is <= 55 the output zero point rides along as zp * 2^s (the 64-bit sum then
@@ -199,14 +203,12 @@ tb_status make_rescale_plan(tb_context* ctx, const tb_rescale_attr* a, int in_t,
         for (int i = 0; i < a->channels; ++i)
             if (s[i] > 55) fold = false;
         r->zp_folded = fold;
-        const size_t padded = (static_cast<size_t>(a->channels) + 255) / 256 * 256;
-        std::vector<int32_t> rq(8 * padded, 0);
         for (size_t pi = 0; pi < padded; ++pi) {
             const int i = pi < static_cast<size_t>(a->channels) ? static_cast<int>(pi) : 0;
             const int64_t base = (1ll << (s[i] - 1)) + (fold ? static_cast<int64_t>(ozp) * (1ll << s[i]) : 0);
             const int64_t dr = a->rounding_mode == TB_ROUND_DOUBLE ? (1ll << 30) : 0;
             const uint64_t rp = static_cast<uint64_t>(base + dr), rn = static_cast<uint64_t>(base - dr);
-            int32_t* q = &rq[8 * pi];
+            int32_t* q = &(*blob)[8 * pi];
             q[0] = m[i];
             q[1] = s[i] - 32;
             q[2] = static_cast<int32_t>(rp & 0xffffffffu);
@@ -214,24 +216,37 @@ tb_status make_rescale_plan(tb_context* ctx, const tb_rescale_attr* a, int in_t,
             q[4] = static_cast<int32_t>(rn & 0xffffffffu);
             q[5] = static_cast<int32_t>(rn >> 32);
         }
-        TB_CUDA(cudaMalloc(&r->d_rq, sizeof(int32_t) * rq.size()));
-        TB_CUDA(cudaMemcpy(r->d_rq, rq.data(), sizeof(int32_t) * rq.size(), cudaMemcpyHostToDevice));
     }
-    TB_CUDA(cudaMalloc(&r->d_mult, sizeof(int32_t) * a->channels));
-    TB_CUDA(cudaMalloc(&r->d_shift, sizeof(int32_t) * a->channels));
-    TB_CUDA(cudaMemcpy(r->d_mult, m.data(), sizeof(int32_t) * a->channels, cudaMemcpyHostToDevice));
-    TB_CUDA(cudaMemcpy(r->d_shift, s.data(), sizeof(int32_t) * a->channels, cudaMemcpyHostToDevice));
+    std::copy(m.begin(), m.end(), blob->begin() + rq_words);
+    std::copy(s.begin(), s.end(), blob->begin() + rq_words + a->channels);
+    return TB_OK;
+}
+
+void place_rescale(RescalePlan* r, int32_t* dev_blob) {
+    const size_t padded = (static_cast<size_t>(r->channels) + 255) / 256 * 256;
+    const size_t rq_words = r->fast ? 8 * padded : 0;
+    r->d_rq = r->fast ? dev_blob : nullptr;
+    r->d_mult = dev_blob + rq_words;
+    r->d_shift = dev_blob + rq_words + r->channels;
+}
+
+tb_status make_rescale_plan(tb_context* ctx, const tb_rescale_attr* a, int in_t, int64_t shape_last, RescalePlan* r) {
+    (void)ctx;
+    std::vector<int32_t> blob;
+    TB_TRY(prepare_rescale(a, in_t, shape_last, r, &blob));
+    TB_CUDA(cudaMalloc(&r->d_blob, sizeof(int32_t) * blob.size()));
+    TB_CUDA(cudaMemcpy(r->d_blob, blob.data(), sizeof(int32_t) * blob.size(), cudaMemcpyHostToDevice));
+    place_rescale(r, r->d_blob);
     return TB_OK;
 }
 
 void free_rescale_plan(RescalePlan* r) {
-    if (r->d_mult) cudaFree(r->d_mult);
-    if (r->d_shift) cudaFree(r->d_shift);
-    if (r->d_rq) cudaFree(r->d_rq);
+    if (r->d_blob) cudaFree(r->d_blob);
+    r->d_blob = nullptr;
     r->d_mult = r->d_shift = r->d_rq = nullptr;
 }
 
-static RescaleArgs rescale_args(const RescalePlan& r) {
+RescaleArgs rescale_args(const RescalePlan& r) {
     RescaleArgs a;
     a.multiplier = r.d_mult;
     a.shift = r.d_shift;
@@ -244,7 +259,7 @@ static RescaleArgs rescale_args(const RescalePlan& r) {
     return a;
 }
 
-static IntEpiDev int_epi(const RescalePlan& r) {
+IntEpiDev int_epi(const RescalePlan& r) {
     IntEpiDev e;
     e.rescale = r.enabled ? 1 : 0;
     e.rs = rescale_args(r);
@@ -365,25 +380,10 @@ TB_API uint64_t tb_launch_count(tb_context* ctx) { return ctx ? ctx->launches : 
 // MATMUL
 // ===========================================================================
 
-struct tb_matmul_plan {
-    tb_context* ctx = nullptr;
-    tb_matmul_desc d{};
-    int path = 0;  // 0 TC int8, 1 TC f16/bf16, 2 direct int, 3 direct float
-    RescalePlan rs;
-    int bn = 256;
-    int32_t* d_colterm = nullptr;  // [n][w] (+ one tile of padding) when a_zp != 0
-    unsigned int* d_counter = nullptr;  // column-sum units finished, grows by `units` per run
-    unsigned int epoch = 0;
-    const void* a_cached = nullptr;
-    const void* b_cached = nullptr;
-    CUtensorMap tmA, tmB;
-};
 
-extern "C" TB_API tb_status tb_matmul_plan_create(tb_context* ctx, const tb_matmul_desc* d,
-                                                  const tb_rescale_attr* rescale, tb_matmul_plan** out) {
-    if (!ctx || !d || !out) return fail(TB_ERR_INVALID_ARGUMENT, "null argument");
-    *out = nullptr;
-    TB_CUDA(cudaSetDevice(ctx->device));
+namespace tb {
+
+tb_status matmul_validate(const tb_matmul_desc* d, bool has_rescale, int* path, int* bn) {
     if (d->n < 0 || d->h < 0 || d->c < 0 || d->w < 0) return fail(TB_ERR_SHAPE_MISMATCH, "MATMUL: negative dimension");
     // matmul_types (src/ops/matmul.rs:30-38), restricted to what runs here.
     const int at = d->a_dtype, bt = d->b_dtype, ot = d->out_dtype;
@@ -402,21 +402,35 @@ extern "C" TB_API tb_status tb_matmul_plan_create(tb_context* ctx, const tb_matm
     } else if (d->a_zp != 0 || d->b_zp != 0) {
         return fail(TB_ERR_GRAPH, "MATMUL: zero points must be zero for floating-point inputs");
     }
-    if (rescale && !int8) return fail(TB_ERR_DTYPE_MISMATCH, "MATMUL: RESCALE needs an integer result");
+    if (has_rescale && !int8) return fail(TB_ERR_DTYPE_MISMATCH, "MATMUL: RESCALE needs an integer result");
+    const int e = int8 ? 1 : 2;
+    const bool tma_ok = (static_cast<long long>(d->c) * e) % 16 == 0 && (static_cast<long long>(d->w) * e) % 16 == 0 &&
+                        d->c > 0 && d->w > 0 && d->h > 0 && d->n > 0;
+    *path = tma_ok ? (int8 ? 0 : 1) : (int8 ? 2 : 3);
+    *bn = d->w <= 128 ? 128 : 256;
+    return TB_OK;
+}
+
+}  // namespace tb
+
+extern "C" TB_API tb_status tb_matmul_plan_create(tb_context* ctx, const tb_matmul_desc* d,
+                                                  const tb_rescale_attr* rescale, tb_matmul_plan** out) {
+    if (!ctx || !d || !out) return fail(TB_ERR_INVALID_ARGUMENT, "null argument");
+    *out = nullptr;
+    TB_CUDA(cudaSetDevice(ctx->device));
+    int path = 0, bn = 256;
+    TB_TRY(matmul_validate(d, rescale != nullptr, &path, &bn));
     tb_matmul_plan* p = new tb_matmul_plan;
     p->ctx = ctx;
     p->d = *d;
+    p->path = path;
+    p->bn = bn;
     if (rescale) {
         tb_status s = make_rescale_plan(ctx, rescale, TB_DT_INT32, d->w, &p->rs);
         if (s != TB_OK) { delete p; return s; }
     }
-    const int e = int8 ? 1 : 2;
-    const bool tma_ok = (static_cast<long long>(d->c) * e) % 16 == 0 && (static_cast<long long>(d->w) * e) % 16 == 0 &&
-                        d->c > 0 && d->w > 0 && d->h > 0 && d->n > 0;
-    p->path = tma_ok ? (int8 ? 0 : 1) : (int8 ? 2 : 3);
-    p->bn = d->w <= 128 ? 128 : 256;
     if (p->path == 0 && d->a_zp != 0) {
-        // padded by one tile: the epilogue reads whole 32-column chunks without clamping
+        // padded by one tile: the epilogue reads whole 16-column chunks without clamping
         cudaError_t ce = cudaMalloc(&p->d_colterm, sizeof(int32_t) * (static_cast<size_t>(d->n) * d->w + 256));
         if (ce == cudaSuccess) ce = cudaMalloc(&p->d_counter, sizeof(unsigned int));
         if (ce == cudaSuccess) ce = cudaMemset(p->d_counter, 0, sizeof(unsigned int));

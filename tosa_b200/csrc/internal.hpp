@@ -68,6 +68,7 @@ struct RescalePlan {
     int32_t* d_mult = nullptr;     // [channels]
     int32_t* d_shift = nullptr;    // [channels]
     int32_t* d_rq = nullptr;       // fast path: [channels][8] {m, s-32, rp_lo, rp_hi, rn_lo, rn_hi, 0, 0}
+    int32_t* d_blob = nullptr;     // owned allocation holding rq, multiplier and shift
 };
 
 // Validate a fused/standalone RESCALE (src/ops/type_conv.rs:128-171) for
@@ -77,5 +78,32 @@ tb_status check_rescale(const tb_rescale_attr* a, int in_dtype, int64_t shape_la
 tb_status make_rescale_plan(tb_context* ctx, const tb_rescale_attr* a, int in_dtype, int64_t shape_last,
                             RescalePlan* out);
 void free_rescale_plan(RescalePlan* r);
+// Host half of make_rescale_plan: validates and builds the device blob
+// (packed fast-path constants, multipliers, shifts) without allocating.
+tb_status prepare_rescale(const tb_rescale_attr* a, int in_t, int64_t shape_last, RescalePlan* r,
+                          std::vector<int32_t>* blob);
+// Points the plan's device arrays into a blob already copied to the device.
+void place_rescale(RescalePlan* r, int32_t* dev_blob);
+
+int grid_for(const tb_context* ctx, long long work, int block = 256);
+
+// MATMUL static checks (src/ops/matmul.rs:112-153) and path choice:
+// path 0 tensor-core int8, 1 tensor-core f16/bf16, 2 direct int8, 3 direct float.
+tb_status matmul_validate(const tb_matmul_desc* d, bool has_rescale, int* path, int* bn);
 
 }  // namespace tb
+
+// A prepared MATMUL (see tb_matmul_plan_create).
+struct tb_matmul_plan {
+    tb_context* ctx = nullptr;
+    tb_matmul_desc d{};
+    int path = 0;  // 0 TC int8, 1 TC f16/bf16, 2 direct int, 3 direct float
+    tb::RescalePlan rs;
+    int bn = 256;
+    int32_t* d_colterm = nullptr;  // [n][w] (+ one tile of padding) when a_zp != 0
+    unsigned int* d_counter = nullptr;  // column-sum units finished, grows by `units` per run
+    unsigned int epoch = 0;
+    const void* a_cached = nullptr;
+    const void* b_cached = nullptr;
+    CUtensorMap tmA, tmB;
+};
