@@ -144,6 +144,22 @@ TB_API void tb_matmul_plan_destroy(tb_matmul_plan *plan);
 TB_API tb_status tb_matmul(tb_context *ctx, const tb_matmul_desc *desc, const tb_rescale_attr *rescale,
                            const void *a, const void *b, void *out, void *stream);
 
+/* INT8 x INT8 -> INT32 MATMUL (+ optional fused RESCALE) that allocates no
+ * device memory. This entry point has no counterpart in the reference; it is
+ * for callers that cannot call cudaMalloc (their device memory belongs to
+ * another allocator, or allocation is not allowed where they run). The
+ * caller passes device inputs and outputs; the kernel's scratch lives in a
+ * fixed 2 MiB file-scope device array that every GPU using the library holds
+ * until exit, which limits n*w to 131072 when a_zp != 0 and the rescale to
+ * 16384 channels (larger shapes are rejected with TB_ERR_INVALID_ARGUMENT).
+ * Runs on the calling thread's current device; its first call on a device
+ * resolves the array's device address (cudaGetSymbolAddress), so make that
+ * first call before any stream capture. Every call clears the scratch it
+ * needs, then waits for `stream` and returns data-dependent errors itself.
+ * Calls that overlap on the GPU share the array and race: serialise them. */
+TB_API tb_status tb_matmul_i8_noalloc(const tb_matmul_desc *desc, const tb_rescale_attr *rescale, const void *a,
+                                      const void *b, void *out, void *stream);
+
 /* ---- CONV2D / DEPTHWISE_CONV2D (src/ops/conv.rs:398-524) -------------------
  * input NHWC [n,ih,iw,ic]; CONV2D weight OHWI [oc,kh,kw,ic]; DEPTHWISE weight
  * [kh,kw,ic,m] with oc = ic*m; bias [bias_len] (1 or oc) of out_dtype;
