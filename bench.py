@@ -2,27 +2,29 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl reference]
 
-Workloads (synthetic seeded inputs of the stated
-shapes and distributions):
-  matmul  config 2: batched int8 MATMUL A[8,1024,1024] x B[8,1024,1024], a/b zero
-          points in [-8,8], fused RESCALE (single multiplier, shift 35,
-          single_round) to int8. Metric: int8 TOPS (2*8*1024^3 ops per step).
-  conv    config 1: int8 CONV2D [1,56,56,64] x [64,3,3,64] pad 1, input_zp -3,
-          per-channel double-round RESCALE to int8 (output_zp 5).
+Workloads (synthetic seeded inputs of the stated shapes
+and distributions, random-init weights):
+  matmul       config 2: batched int8 MATMUL A[8,1024,1024] x B[8,1024,1024], a/b
+               zero points in [-8,8], fused RESCALE (single multiplier, shift 35,
+               single_round) to int8. Metric: int8 TOPS (2*8*1024^3 ops per step).
+  resnet50     config 4: the ResNet-50-shaped int8 TOSA graph (tosa_b200/graphs.py),
+               64 images per GPU, run by the graph runner (one CUDA graph per
+               step). Metric: images/s.
+  mobilenetv2  config 3: the MobileNetV2-shaped int8 graph, batch 64 per GPU.
 
-Multi-GPU (torchrun, one process per GPU): every rank runs its own copy of the
+Multi-GPU (torchrun, one process per GPU): every rank runs its own shard of the
 workload (weak scaling; the batch shards are independent, no collective on the
 data path). Timing: W untimed warm-up steps; K timed steps, each bracketed by
 CUDA events on the launching stream with the L2 flushed (a 256 MiB write)
 between steps; barrier + synchronize around the timed region; the max over
 ranks of the summed step time. `e2e` repeats the measurement through the same
-C-ABI entry point with the step's inputs copied from pinned host memory and
+public entry point with the step's inputs copied from pinned host memory and
 its output copied back inside the timed region.
 
 `--impl reference` times the reference's arithmetic on the host CPU cores
-instead: the C restatement of the reference loops (oracle/, the reference is
-Rust and cannot be built here), multi-threaded over output rows, each step a
-bounded sample of the workload.
+instead: the C restatement of the reference loops (oracle/; the reference is
+Rust and cannot be built here) on all host threads, each step a bounded sample
+of the workload.
 """
 
 from __future__ import annotations
@@ -58,8 +60,9 @@ class MatmulWorkload:
     unit = "TOPS"
     N, H, C, W = 8, 1024, 1024, 1024
     seed = 2
+    kernel = "tc_gemm_kernel"
 
-    def __init__(self):
+    def __init__(self, args):
         rng = np.random.default_rng(self.seed)
         self.a = rng.integers(-128, 128, (self.N, self.H, self.C), dtype=np.int8)
         self.b = rng.integers(-128, 128, (self.N, self.C, self.W), dtype=np.int8)
@@ -68,6 +71,7 @@ class MatmulWorkload:
         self.mult = int(rng.integers(1 << 30, 1 << 31))
         self.shift = 35
         self.ops = 2 * self.N * self.H * self.C * self.W
+        self.units_per_step = self.ops / 1e12  # TOPS
 
     def config(self):
         return {"workload": "config2: batched int8 MATMUL [8,1024,1024]x[8,1024,1024] + RESCALE(single_round, "
@@ -76,7 +80,7 @@ class MatmulWorkload:
                 "l2": "flushed between timed steps (256 MiB write)"}
 
     # -- GPU
-    def setup(self, L, ctx, torch):
+    def setup(self, L, ctx, torch, stream):
         self.L, self.torch = L, torch
         d = L.MatmulDesc(n=self.N, h=self.H, c=self.C, w=self.W, a_dtype=L.DT_INT8, b_dtype=L.DT_INT8,
                          out_dtype=L.DT_INT32, a_zp=self.za, b_zp=self.zb)
@@ -97,6 +101,7 @@ class MatmulWorkload:
         L = self.L
         L.check(L.load().tb_matmul_plan_run(self.plan, L.ptr(self.da), L.ptr(self.db), L.ptr(self.dout),
                                             L.stream_ptr(stream)))
+        return 1
 
     def step_e2e(self, stream):
         self.da.copy_(self.ha, non_blocking=True)
@@ -113,16 +118,28 @@ class MatmulWorkload:
         rc, exp = H.oracle_rescale(acc, 5, 3, [self.mult], [self.shift], 0, 0, 1, 1, 0)
         return rc == 0 and np.array_equal(got[:1, :rows].reshape(-1).astype(np.int64), exp)
 
+    def kernel_time(self, stream, flush, steps):
+        """Mean CUDA-event time of the dominant kernel (the step is one launch of it)."""
+        torch = self.torch
+        evs = []
+        for _ in range(steps):
+            flush.fill_(1)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            self.step(stream)
+            e.record(stream)
+            evs.append((s, e))
+        torch.cuda.synchronize()
+        ms = statistics.mean(s.elapsed_time(e) for s, e in evs)
+        return self.ops / (ms * 1e-3) / 1e12, "TOPS (int8)", ms, 1
+
     def close(self):
         self.L.load().tb_matmul_plan_destroy(self.plan)
-
-    # -- roofline of the dominant kernel
-    kernel_regex = "tc_gemm_kernel"
 
     # -- CPU (oracle restatement)
     def cpu_run(self, rows, threads):
         """MATMUL + RESCALE of the first `rows` rows of A (row-major over [N*H], so a
-        sample may span batches) against their batch's B; returns ops done."""
+        sample may span batches) against their batch's B; returns work done in units."""
         from oracle import oracle as O
         L = O.lib()
         p = lambda x: x.ctypes.data_as(ctypes.c_void_p)  # noqa: E731
@@ -148,7 +165,13 @@ class MatmulWorkload:
                           ctypes.c_int64(1), ctypes.c_int64(0), ctypes.c_int64(0), ctypes.c_int(1), ctypes.c_int(1),
                           ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0), p(res))
             done += nr
-        return 2 * rows * self.C * self.W
+        return 2 * rows * self.C * self.W / 1e12
+
+    def cpu_default(self, args):
+        return args.cpu_rows
+
+    def ref_default(self, args):
+        return args.ref_rows
 
     def cpu_sample_desc(self, rows, threads):
         return (f"first {rows} of the {self.N * self.H} rows of A[8,1024,1024] (row-major over batch) x their "
@@ -156,7 +179,144 @@ class MatmulWorkload:
                 f"reference loops")
 
 
-WORKLOADS = {"matmul": MatmulWorkload}
+def _oracle_image(data, image):
+    """Run one image through the oracle (a worker of the CPU baseline)."""
+    from oracle import oracle as O
+    block = O.read_graph(data).main_block
+    name = block.inputs[0]
+    return O.run_block(block, {name: O.T(3, list(image.shape), image.astype(np.int64).reshape(-1))})
+
+
+class GraphWorkload:
+    """A synthetic int8 TOSA graph run by the graph runner (configs 3 and 4)."""
+
+    unit = "img/s"
+    kernel = "tc_gemm_kernel"
+    batch = 64
+    seed = 21
+
+    def __init__(self, args):
+        from tosa_b200 import graphs
+        self.graphs = graphs
+        self.batch = args.batch or self.batch
+        self.data, self.info = self.builder(self.batch)
+        self.units_per_step = self.batch
+        rng = np.random.default_rng(self.seed)
+        self.images = rng.integers(-128, 128, (self.batch, 224, 224, 3), dtype=np.int8)
+
+    def config(self):
+        return {"workload": self.desc, "global_batch": self.batch, "batch_per_gpu": self.batch,
+                "int_ops_per_image": self.info["ops_per_image"],
+                "l2": "flushed between timed steps (256 MiB write); activations exceed L2"}
+
+    def setup(self, L, ctx, torch, stream):
+        from tosa_b200 import interpreter as I
+        self.L, self.torch, self.I = L, torch, I
+        self.ctx = ctx
+        self.dimg = torch.from_numpy(self.images).cuda()
+        self.himg = torch.from_numpy(self.images).pin_memory()
+        self.it = I.Interpreter(self.data, context=ctx, cuda_graph=True)
+        self.it.bind_device(self.info["input"], L.DT_INT8, list(self.images.shape), self.dimg.data_ptr())
+        self.out_name = self.info["output"]
+        self.h2d = self.images.nbytes
+        self.it.execute(stream=stream)  # compile + capture
+        info = L.TensorInfo()
+        L.check(L.load().tb_graph_get_output(self.it._h, self.out_name.encode(), ctypes.byref(info)))
+        self.out_ptr = info.data
+        self.out_bytes = int(np.prod([info.shape[i] for i in range(info.rank)])) * 4
+        self.hout = torch.empty(self.out_bytes, dtype=torch.uint8).pin_memory()
+        self.d2h = self.out_bytes
+
+    def step(self, stream):
+        self.it.execute(stream=stream)
+        return self.it.last_launches
+
+    def step_e2e(self, stream):
+        L = self.L
+        self.dimg.copy_(self.himg, non_blocking=True)
+        self.it.execute(stream=stream)
+        L.check(L.load().tb_memcpy_d2h(self.ctx.h, ctypes.c_void_p(self.hout.data_ptr()),
+                                       ctypes.c_void_p(self.out_ptr), self.out_bytes, L.stream_ptr(stream)))
+
+    def check(self):
+        """First image's logits bit-exact against the oracle."""
+        got = self.it.output(self.out_name).data.reshape(self.batch, -1)[0].astype(np.int64)
+        d1, _ = self.builder(1)
+        want = _oracle_image(d1, self.images[:1])
+        return bool(np.array_equal(next(iter(want.values())).values, got))
+
+    def kernel_time(self, stream, flush, steps):
+        """Per-operator CUDA-event times of an eager run; the dominant kernel is the
+        tensor-core implicit-GEMM convolution: achieved = its 2*MACs / its time."""
+        I = self.I
+        it = I.Interpreter(self.data, context=self.ctx, time_ops=True)
+        it.bind_device(self.info["input"], self.L.DT_INT8, list(self.images.shape), self.dimg.data_ptr())
+        it.execute(stream=stream)  # compile
+        block = self.graphs.TG.read_graph(self.data).main_block
+        conv_ops = [i for i, o in enumerate(block.operators) if o.name == "CONV2D"]
+        tc_ops = [i for i in conv_ops if block.tensor(block.operators[i].inputs[0]).shape[3] % 16 == 0]
+        tot_ms, tot_macs, all_ms, n = 0.0, 0, 0.0, 0
+        for _ in range(steps):
+            flush.fill_(1)
+            it.execute(stream=stream)
+            for i in range(len(block.operators)):
+                t = it.op_time_ms(i)
+                if t > 0:
+                    all_ms += t
+            for i in tc_ops:
+                tot_ms += it.op_time_ms(i)
+                tot_macs += self.info["op_macs"][i]
+            n += len(tc_ops)
+        it.close()
+        self.kernel_share = tot_ms / all_ms if all_ms else None
+        return 2 * tot_macs / (tot_ms * 1e-3) / 1e12, "TOPS (int8)", tot_ms / n, len(tc_ops)
+
+    def close(self):
+        self.it.close()
+
+    # -- CPU (oracle restatement): whole images through the graph
+    def cpu_run(self, images, threads):
+        d1, _ = self.builder(1)
+        imgs = [self.images[i % self.batch][None] for i in range(images)]
+        if threads > 1:
+            import multiprocessing as mp
+            with mp.get_context("spawn").Pool(threads) as pool:
+                pool.starmap(_oracle_image, [(d1, im) for im in imgs])
+        else:
+            for im in imgs:
+                _oracle_image(d1, im)
+        return images
+
+    def cpu_default(self, args):
+        return 1
+
+    def ref_default(self, args):
+        return os.cpu_count() or 1
+
+    def cpu_sample_desc(self, images, threads):
+        return (f"{images} image(s) through the whole {self.name} graph at batch 1 on {threads} "
+                f"process(es), C restatement of the reference loops")
+
+
+class ResNet50Workload(GraphWorkload):
+    name = "resnet50"
+    desc = ("config4: ResNet-50-shaped int8 TOSA graph (stem 7x7/s2, stages [3,4,6,3], RESCALE+CLAMP after "
+            "every conv, residual ADD via RESCALE to int32, AVG_POOL2D, 2048->1000 MATMUL), 224x224x3 int8")
+
+    def builder(self, batch):
+        return self.graphs.resnet50_int8(batch)
+
+
+class MobileNetV2Workload(GraphWorkload):
+    name = "mobilenetv2"
+    desc = ("config3: MobileNetV2-shaped int8 TOSA graph (17 inverted-residual blocks, expand x6, depthwise "
+            "3x3, RESCALE+CLAMP[0,127], residual ADD via RESCALE to int32, AVG_POOL2D, 1280->1000 MATMUL)")
+
+    def builder(self, batch):
+        return self.graphs.mobilenetv2_int8(batch)
+
+
+WORKLOADS = {"matmul": MatmulWorkload, "resnet50": ResNet50Workload, "mobilenetv2": MobileNetV2Workload}
 
 
 # ---------------------------------------------------------------------------
@@ -241,11 +401,11 @@ def measure_int8_peak(torch):
         return 4500.0, f"nominal dense int8 4.5 POPS (measurement failed: {ex})"
 
 
-def load_traffic(kernel_workload):
+def load_traffic(workload):
     path = os.path.join(ROOT, "profiles", "traffic.json")
     try:
         with open(path) as f:
-            return json.load(f).get(kernel_workload)
+            return json.load(f).get(workload)
     except (OSError, ValueError):
         return None
 
@@ -267,21 +427,21 @@ def run_reference(args, wl):
     if rank != 0:
         return 0
     threads = os.cpu_count() or 1
-    rows = args.ref_rows
+    sample = args.ref_sample or wl.ref_default(args)
     for _ in range(args.warmup):
-        wl.cpu_run(rows, threads)
+        wl.cpu_run(sample, threads)
     t0 = time.perf_counter()
-    ops = 0
+    units = 0.0
     for _ in range(args.steps):
-        ops += wl.cpu_run(rows, threads)
+        units += wl.cpu_run(sample, threads)
     dt = time.perf_counter() - t0
-    value = ops / dt / 1e12
+    value = units / dt
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": wl.unit, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
             "data": "synthetic", "config": wl.config(),
             "cpu_baseline": {"value": value, "unit": wl.unit, "cores": threads, "kind": "port",
-                             "sample": wl.cpu_sample_desc(rows, threads)},
+                             "sample": wl.cpu_sample_desc(sample, threads)},
             "e2e": {"value": value, "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
@@ -300,8 +460,9 @@ def run_gpu(args, wl):
     from tosa_b200 import _lib as L
 
     ctx = L.Context(local)
-    wl.setup(L, ctx, torch)
-    stream = torch.cuda.current_stream()
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    wl.setup(L, ctx, torch, stream)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
 
     def barrier():
@@ -316,12 +477,13 @@ def run_gpu(args, wl):
 
     def timed(fn):
         evs = []
+        launches = 0
         barrier()
         for _ in range(args.steps):
             flush.fill_(1)
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record(stream)
-            fn(stream)
+            launches += fn(stream) or 0
             e.record(stream)
             evs.append((s, e))
         barrier()
@@ -330,59 +492,46 @@ def run_gpu(args, wl):
             t = torch.tensor([ms], device="cuda")
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
             ms = float(t.item())
-        return ms
+        return ms, launches
 
     def soak(seconds):
         # keeps the GPU busy with the same step so the clock samples see load
         t0 = time.perf_counter()
         while time.perf_counter() - t0 < seconds:
-            for _ in range(50):
+            for _ in range(10):
                 wl.step(stream)
             torch.cuda.synchronize()
 
     clocks = ClockSampler(local)
     clocks.start()
     soak(0.6)
-    launches0 = ctx.launches
-    ms = timed(wl.step)
-    launches = ctx.launches - launches0
+    ms, launches = timed(wl.step)
     soak(0.6)
     clk = clocks.stop()
     ctx.synchronize(stream)
     for _ in range(args.warmup):
         wl.step_e2e(stream)
-    ms_e2e = timed(wl.step_e2e)
+    ms_e2e, _ = timed(lambda s: wl.step_e2e(s))
     ctx.synchronize(stream)
 
-    # roofline: the dominant kernel timed alone (same launch as a step)
-    peak, peak_src = (None, None)
-    kernel_ms = None
+    # roofline: the dominant kernel timed on its own stream with CUDA events
+    peak = peak_src = achieved = kunit = kms = None
     if rank == 0:
-        evs = []
-        for _ in range(args.steps):
-            flush.fill_(1)
-            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s.record(stream)
-            wl.step(stream)
-            e.record(stream)
-            evs.append((s, e))
-        torch.cuda.synchronize()
-        kernel_ms = statistics.mean(s.elapsed_time(e) for s, e in evs)
+        achieved, kunit, kms, _ = wl.kernel_time(stream, flush, max(3, min(args.steps, 10)))
         del flush
         peak, peak_src = measure_int8_peak(torch)
 
-    value = ws * wl.ops * args.steps / (ms * 1e-3) / 1e12
-    e2e = ws * wl.ops * args.steps / (ms_e2e * 1e-3) / 1e12
+    value = ws * wl.units_per_step * args.steps / (ms * 1e-3)
+    e2e = ws * wl.units_per_step * args.steps / (ms_e2e * 1e-3)
     if rank == 0:
         cpu = None
         if ws == 1 and not args.no_cpu:
-            rows = args.cpu_rows
+            sample = args.cpu_sample or wl.cpu_default(args)
             t0 = time.perf_counter()
-            ops = wl.cpu_run(rows, 1)  # ~10 s of single-thread work at the default size
+            done = wl.cpu_run(sample, 1)
             dt = time.perf_counter() - t0
-            cpu = {"value": ops / dt / 1e12, "unit": wl.unit, "cores": 1, "kind": "port",
-                   "sample": wl.cpu_sample_desc(rows, 1)}
-        achieved = wl.ops / (kernel_ms * 1e-3) / 1e12
+            cpu = {"value": done / dt, "unit": wl.unit, "cores": 1, "kind": "port",
+                   "sample": wl.cpu_sample_desc(sample, 1)}
         line = {
             "metric": METRIC, "value": value, "unit": wl.unit, "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
@@ -390,16 +539,18 @@ def run_gpu(args, wl):
             "parity_spot_check": bool(ok),
             "e2e": {"value": e2e, "unit": wl.unit, "h2d_bytes_per_step": wl.h2d, "d2h_bytes_per_step": wl.d2h},
             "gpu_launches": int(launches),
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOPS (int8)",
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": kunit,
                          "frac": achieved / peak if peak else None, "traffic": load_traffic(wl.name),
-                         "peak_source": peak_src,
-                         "note": "achieved = 2*M*N*K of one step / mean CUDA-event time of the step "
-                                 "(one GEMM launch with the zero-point column sums and RESCALE fused), "
-                                 "L2 flushed; clocks sampled during a 1.2 s soak of the same step around "
-                                 "the timed region"},
+                         "kernel": wl.kernel, "kernel_ms_per_launch": kms, "peak_source": peak_src,
+                         "note": "achieved = algorithmic int8 ops (2*MACs) of the dominant kernel's launches / "
+                                 "their CUDA-event time, L2 flushed; clocks sampled during a 1.2 s soak of the "
+                                 "same step around the timed region"},
             "cpu_baseline": cpu,
             "clocks": clk,
         }
+        share = getattr(wl, "kernel_share", None)
+        if share is not None:
+            line["roofline"]["kernel_share_of_step"] = share
         print(json.dumps(line), flush=True)
     wl.close()
     ctx.close()
@@ -415,12 +566,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="matmul", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="tosa_b200", choices=["tosa_b200", "reference"])
+    ap.add_argument("--batch", type=int, default=0, help="images per GPU for the graph workloads (default 64)")
     ap.add_argument("--cpu-rows", type=int, default=1536, help="rows of the single-thread CPU baseline sample")
     ap.add_argument("--ref-rows", type=int, default=1024, help="rows per step of the --impl reference arm")
+    ap.add_argument("--cpu-sample", type=int, default=0, help="override the CPU baseline sample size")
+    ap.add_argument("--ref-sample", type=int, default=0, help="override the reference arm's per-step sample")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    wl = WORKLOADS[args.workload]()
+    wl = WORKLOADS[args.workload](args)
     if args.impl == "reference":
         return run_reference(args, wl)
     return run_gpu(args, wl)

@@ -220,6 +220,95 @@ TB_API tb_status tb_avg_pool2d(tb_context *ctx, const tb_pool2d_desc *desc, cons
 TB_API tb_status tb_max_pool2d(tb_context *ctx, const tb_pool2d_desc *desc, const void *input, void *out,
                                void *stream);
 
+/* ---- graph runner ----------------------------------------------------------
+ * Runs a serialized TOSA graph (.tosa flatbuffer) on the device: the
+ * counterpart of Interpreter::from_flatbuffer + Interpreter::run
+ * (src/interpreter.rs:108-147, :154-253) and run_graph / run_graph_with_hooks
+ * (src/lib.rs:20-43). Operators execute in the reference's ready-queue order
+ * and every operator emits the reference's hook events (pre_op, then
+ * on_tensor_alloc for each output, then post_op; src/interpreter.rs:199-216),
+ * fused or not. The runner accepts CONST, CONST_SHAPE, IDENTITY, RESHAPE,
+ * TRANSPOSE, CONV2D, DEPTHWISE_CONV2D, MATMUL, RESCALE, CLAMP, ADD,
+ * AVG_POOL2D and MAX_POOL2D; a graph with any other operator is rejected
+ * with TB_ERR_UNSUPPORTED_OP at tb_graph_load (those graphs stay on the
+ * reference path).
+ *
+ * Fusion (off with TB_GRAPH_NO_FUSION): a contraction whose only consumer is
+ * a RESCALE (and that RESCALE's only consumer a CLAMP) runs as one kernel, and
+ * the residual chain RESCALE, RESCALE -> ADD -> RESCALE [-> CLAMP] runs as one
+ * elementwise pass. Intermediate tensors of a fused group are not
+ * materialised: their tb_tensor_info.data is NULL in hook callbacks.
+ *
+ * Tensor data in host and device buffers use one element per slot: INT8/BOOL
+ * 1 byte, INT4 1 byte per element (sign-extended, as the contraction entry
+ * points take INT4 weights), INT16/FP16/BF16 2, INT32/FP32 4, INT48/INT64/SHAPE
+ * 8 bytes, little-endian. TB_GRAPH_CUDA_GRAPH needs a non-default stream. */
+typedef struct tb_graph tb_graph;
+
+typedef struct tb_tensor_info {   /* a tensor as hooks see it (src/tensor.rs:228-249) */
+    const char *name;
+    int32_t dtype;                /* TB_DT_* (SHAPE values report TB_DT_INT64, like the reference) */
+    int32_t rank;
+    const int64_t *shape;
+    uint64_t bytes;               /* element_count (>= 1) * element size */
+    const void *data;             /* device pointer, NULL when fused away */
+} tb_tensor_info;
+
+typedef struct tb_op_info {       /* OpInfo (src/stats.rs:6-9) */
+    int32_t op;                   /* serialized Op code (schema/tosa.fbs:88-201) */
+    int32_t op_index;             /* index in the block's operator list */
+} tb_op_info;
+
+/* InterpreterHook (src/stats.rs:11-16); NULL members do nothing. Called on the
+ * thread that runs the graph. */
+typedef struct tb_hooks {
+    void *user;
+    void (*pre_op)(void *user, const tb_op_info *op, const tb_tensor_info *inputs, int32_t n_inputs);
+    void (*post_op)(void *user, const tb_op_info *op, const tb_tensor_info *inputs, int32_t n_inputs,
+                    const tb_tensor_info *outputs, int32_t n_outputs);
+    void (*on_tensor_alloc)(void *user, const char *name, const int64_t *shape, int32_t rank, int32_t dtype,
+                            uint64_t bytes);
+    void (*on_tensor_free)(void *user, const char *name, uint64_t bytes);
+} tb_hooks;
+
+enum {
+    TB_GRAPH_NO_FUSION = 1,   /* run every operator as its own kernel (every tensor materialised) */
+    TB_GRAPH_SYNC_EACH_OP = 2,/* synchronize the stream before each post_op (wall-clock timing hooks) */
+    TB_GRAPH_CUDA_GRAPH = 4,  /* capture the launches into a CUDA graph on the first run, replay it after */
+    TB_GRAPH_TIME_OPS = 8     /* CUDA-event device time of each operator's kernels (eager runs only) */
+};
+
+/* Parse `data` (Graph::from_flatbuffer, src/ir.rs:592-614) and check that
+ * every operator is one the runner executes. Plans, constants and device
+ * buffers are prepared on the first tb_graph_run for the bound input shapes. */
+TB_API tb_status tb_graph_load(tb_context *ctx, const void *data, size_t len, uint32_t flags, tb_graph **out);
+TB_API void tb_graph_destroy(tb_graph *graph);
+/* The main block's declared inputs / outputs (name, dtype, declared shape). */
+TB_API int32_t tb_graph_num_inputs(const tb_graph *graph);
+TB_API int32_t tb_graph_num_outputs(const tb_graph *graph);
+TB_API tb_status tb_graph_input_info(const tb_graph *graph, int32_t i, tb_tensor_info *info);
+TB_API tb_status tb_graph_output_info(const tb_graph *graph, int32_t i, tb_tensor_info *info);
+/* Bind one input tensor (an entry of the reference's `inputs` map). `data` is
+ * a host buffer (copied to the device before this returns) or, with
+ * on_device != 0, a device pointer used in place until the next bind. */
+TB_API tb_status tb_graph_set_input(tb_graph *graph, const char *name, int32_t dtype, const int64_t *shape,
+                                    int32_t rank, const void *data, uint64_t bytes, int32_t on_device, void *stream);
+/* Interpreter::run: execute the main block on `stream` with `hooks` (may be
+ * NULL), then wait for the stream and report data-dependent errors. */
+TB_API tb_status tb_graph_run(tb_graph *graph, const tb_hooks *hooks, void *stream);
+/* After a run: any tensor of the block by name (typically an output): its
+ * shape, dtype and device data (the runner's buffer, valid until the next
+ * run or bind; NULL when fused away). */
+TB_API tb_status tb_graph_get_output(tb_graph *graph, const char *name, tb_tensor_info *info);
+/* Copy that tensor's data to the host buffer `dst` (`bytes` >= its size). */
+TB_API tb_status tb_graph_read_output(tb_graph *graph, const char *name, void *dst, uint64_t bytes, void *stream);
+/* Kernels the last tb_graph_run launched (CUDA-graph replays count their nodes). */
+TB_API uint64_t tb_graph_last_launches(const tb_graph *graph);
+/* With TB_GRAPH_TIME_OPS: device milliseconds of the operator's kernels in the
+ * last run (a fused group's time is reported on its first operator); -1 when
+ * the operator launched nothing. */
+TB_API float tb_graph_op_time_ms(const tb_graph *graph, int32_t op_index);
+
 #ifdef __cplusplus
 }
 #endif

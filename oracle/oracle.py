@@ -781,9 +781,11 @@ EVAL = {
 }
 
 
-def run_block(block, inputs: dict):
+def run_block(block, inputs: dict, trace: list | None = None):
     """Dataflow execution in the reference's ready-queue order
-    (src/interpreter.rs:154-245). Returns {output name: T}."""
+    (src/interpreter.rs:154-245). Returns {output name: T}. With `trace`, appends
+    (op_index, op name, input shapes, output shapes) per executed operator --
+    the post_op events the reference's hooks see (src/interpreter.rs:199-216)."""
     st = State(block, inputs)
     available = set(st.tensors)
     ready = deque(i for i, op in enumerate(block.operators)
@@ -799,6 +801,9 @@ def run_block(block, inputs: dict):
             raise OracleError("UnsupportedOp", op.name)
         res = fn(st, op)
         st.tensors[op.outputs[0]] = res
+        if trace is not None:
+            trace.append((i, op.name, [list(st.tensors[n].shape) for n in op.inputs if n in st.tensors],
+                          [list(res.shape)]))
         executed[i] = True
         available.update(op.outputs)
         for j, nxt in enumerate(block.operators):

@@ -68,6 +68,30 @@ class Pool2dDesc(ctypes.Structure):
                 ("output_zp", ctypes.c_int32), ("nan_mode", ctypes.c_int32)]
 
 
+class TensorInfo(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("dtype", ctypes.c_int32), ("rank", ctypes.c_int32),
+                ("shape", ctypes.POINTER(ctypes.c_int64)), ("bytes", ctypes.c_uint64), ("data", ctypes.c_void_p)]
+
+
+class OpInfoC(ctypes.Structure):
+    _fields_ = [("op", ctypes.c_int32), ("op_index", ctypes.c_int32)]
+
+
+PRE_OP = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.POINTER(OpInfoC), ctypes.POINTER(TensorInfo), ctypes.c_int32)
+POST_OP = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.POINTER(OpInfoC), ctypes.POINTER(TensorInfo), ctypes.c_int32,
+                           ctypes.POINTER(TensorInfo), ctypes.c_int32)
+ON_ALLOC = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int64), ctypes.c_int32,
+                            ctypes.c_int32, ctypes.c_uint64)
+ON_FREE = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_char_p, ctypes.c_uint64)
+
+
+class Hooks(ctypes.Structure):
+    _fields_ = [("user", ctypes.c_void_p), ("pre_op", PRE_OP), ("post_op", POST_OP), ("on_tensor_alloc", ON_ALLOC),
+                ("on_tensor_free", ON_FREE)]
+
+
+GRAPH_NO_FUSION, GRAPH_SYNC_EACH_OP, GRAPH_CUDA_GRAPH, GRAPH_TIME_OPS = 1, 2, 4, 8
+
 _V = ctypes.c_void_p
 _P = ctypes.POINTER
 _I = ctypes.c_int32
@@ -101,6 +125,18 @@ SIGNATURES = [
     ("tb_add", _I, [_V, _I, _V, _V, _L, _V, _V]),
     ("tb_avg_pool2d", _I, [_V, _P(Pool2dDesc), _V, _V, _V]),
     ("tb_max_pool2d", _I, [_V, _P(Pool2dDesc), _V, _V, _V]),
+    ("tb_graph_load", _I, [_V, _V, ctypes.c_size_t, ctypes.c_uint32, _P(_V)]),
+    ("tb_graph_destroy", None, [_V]),
+    ("tb_graph_num_inputs", _I, [_V]),
+    ("tb_graph_num_outputs", _I, [_V]),
+    ("tb_graph_input_info", _I, [_V, _I, _P(TensorInfo)]),
+    ("tb_graph_output_info", _I, [_V, _I, _P(TensorInfo)]),
+    ("tb_graph_set_input", _I, [_V, ctypes.c_char_p, _I, _P(_L), _I, _V, ctypes.c_uint64, _I, _V]),
+    ("tb_graph_run", _I, [_V, _P(Hooks), _V]),
+    ("tb_graph_get_output", _I, [_V, ctypes.c_char_p, _P(TensorInfo)]),
+    ("tb_graph_read_output", _I, [_V, ctypes.c_char_p, _V, ctypes.c_uint64, _V]),
+    ("tb_graph_last_launches", ctypes.c_uint64, [_V]),
+    ("tb_graph_op_time_ms", ctypes.c_float, [_V, _I]),
 ]
 
 _lib = None

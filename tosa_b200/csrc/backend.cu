@@ -100,12 +100,6 @@ int grid_for(const tb_context* ctx, long long work, int block) {
     return static_cast<int>(g);
 }
 
-#define TB_LAUNCHED(ctx)                                                                               \
-    do {                                                                                               \
-        cudaError_t e_ = cudaGetLastError();                                                           \
-        if (e_ != cudaSuccess) return ::tb::fail(TB_ERR_CUDA, "kernel launch failed: %s", cudaGetErrorString(e_)); \
-        (ctx)->launches++;                                                                             \
-    } while (0)
 
 // ---------------------------------------------------------------------------
 // RESCALE validation (src/ops/type_conv.rs:128-171) and device plan
@@ -388,10 +382,12 @@ tb_status matmul_validate(const tb_matmul_desc* d, bool has_rescale, int* path, 
     // matmul_types (src/ops/matmul.rs:30-38), restricted to what runs here.
     const int at = d->a_dtype, bt = d->b_dtype, ot = d->out_dtype;
     const bool int8 = at == TB_DT_INT8 && bt == TB_DT_INT8 && ot == TB_DT_INT32;
-    const bool fl = (at == bt) && (at == TB_DT_BF16 || at == TB_DT_FP16) && ot == TB_DT_FP32;
+    const bool f32 = at == TB_DT_FP32 && bt == TB_DT_FP32 && ot == TB_DT_FP32;
+    const bool fl = ((at == bt) && (at == TB_DT_BF16 || at == TB_DT_FP16) && ot == TB_DT_FP32) || f32;
+    const bool fp8a = at == TB_DT_FP8E4M3 || at == TB_DT_FP8E5M2, fp8b = bt == TB_DT_FP8E4M3 || bt == TB_DT_FP8E5M2;
     const bool valid_other = (at == TB_DT_INT16 && bt == TB_DT_INT16 && ot == TB_DT_INT48) ||
                              (at == TB_DT_FP16 && bt == TB_DT_FP16 && ot == TB_DT_FP16) ||
-                             (at == TB_DT_FP32 && bt == TB_DT_FP32 && ot == TB_DT_FP32);
+                             (fp8a && fp8b && (ot == TB_DT_FP16 || ot == TB_DT_FP32));
     if (!int8 && !fl) {
         if (valid_other) return fail(TB_ERR_NOT_ACCELERATED, "MATMUL types %d x %d -> %d are not accelerated", at, bt, ot);
         return fail(TB_ERR_DTYPE_MISMATCH, "MATMUL: unsupported types a=%d b=%d output=%d", at, bt, ot);
@@ -406,7 +402,7 @@ tb_status matmul_validate(const tb_matmul_desc* d, bool has_rescale, int* path, 
     const int e = int8 ? 1 : 2;
     const bool tma_ok = (static_cast<long long>(d->c) * e) % 16 == 0 && (static_cast<long long>(d->w) * e) % 16 == 0 &&
                         d->c > 0 && d->w > 0 && d->h > 0 && d->n > 0;
-    *path = tma_ok ? (int8 ? 0 : 1) : (int8 ? 2 : 3);
+    *path = tma_ok && !f32 ? (int8 ? 0 : 1) : (int8 ? 2 : 3);
     *bn = d->w <= 128 ? 128 : 256;
     return TB_OK;
 }
@@ -501,7 +497,8 @@ extern "C" TB_API tb_status tb_matmul_plan_run(tb_matmul_plan* p, const void* a,
             cs.add = cst;
             cs.out = p->d_colterm;
             cs.counter = p->d_counter;
-            if (static_cast<unsigned long long>(p->epoch + 1) * cs.units >= (1ull << 31)) {
+            if (p->replayable || static_cast<unsigned long long>(p->epoch + 1) * cs.units >= (1ull << 31)) {
+                // replayable: the same counter target on every run, so a captured launch can be replayed
                 TB_CUDA(cudaMemsetAsync(p->d_counter, 0, sizeof(unsigned int), st));
                 p->epoch = 0;
             }
@@ -593,6 +590,29 @@ static void tap_range(int o, int stride, int pad, int dil, int k, int in, int* l
     *hi = h;
 }
 
+// The (input, weight, acc, output) combinations the reference admits:
+// conv2d_types (src/ops/conv.rs:375-385) and standard_types (:388-396).
+static bool conv_types_valid(bool depthwise, int i, int w, int a, int o) {
+    auto fp8 = [](int t) { return t == TB_DT_FP8E4M3 || t == TB_DT_FP8E5M2; };
+    if (i == TB_DT_INT8 && (w == TB_DT_INT8 || w == TB_DT_INT4) && a == TB_DT_INT32 && o == TB_DT_INT32) return true;
+    if (i == TB_DT_INT16 && w == TB_DT_INT8 && a == TB_DT_INT48 && o == TB_DT_INT48) return true;
+    if (!depthwise) {
+        auto any = [&](int t) { return fp8(t) || t == TB_DT_FP16 || t == TB_DT_BF16 || t == TB_DT_FP32; };
+        if (a == TB_DT_FP32 && o == TB_DT_FP32) return any(i) && any(w);
+        if ((a == TB_DT_FP16 || a == TB_DT_FP32) && o == TB_DT_FP16)
+            return (fp8(i) || i == TB_DT_FP16) && (fp8(w) || w == TB_DT_FP16);
+        if ((a == TB_DT_BF16 || a == TB_DT_FP32) && o == TB_DT_BF16)
+            return (fp8(i) || i == TB_DT_BF16) && (fp8(w) || w == TB_DT_BF16);
+        return false;
+    }
+    if (i == TB_DT_FP16 && w == TB_DT_FP16 && (a == TB_DT_FP16 || a == TB_DT_FP32) && o == TB_DT_FP16) return true;
+    if (i == TB_DT_BF16 && w == TB_DT_BF16 && a == TB_DT_FP32 && o == TB_DT_BF16) return true;
+    if (i == TB_DT_FP32 && w == TB_DT_FP32 && a == TB_DT_FP32 && o == TB_DT_FP32) return true;
+    if ((i == TB_DT_FP8E4M3 && w == TB_DT_FP8E4M3) || (i == TB_DT_FP8E5M2 && w == TB_DT_FP8E5M2))
+        return (a == TB_DT_FP16 && o == TB_DT_FP16) || (a == TB_DT_FP32 && o == TB_DT_FP32);
+    return false;
+}
+
 static tb_status conv_plan_create(tb_context* ctx, const tb_conv2d_desc* d, const void* weight, const void* bias,
                                   const tb_rescale_attr* rescale, bool depthwise, tb_conv2d_plan** out) {
     if (!ctx || !d || !out || !weight || !bias) return fail(TB_ERR_INVALID_ARGUMENT, "null argument");
@@ -617,12 +637,25 @@ static tb_status conv_plan_create(tb_context* ctx, const tb_conv2d_desc* d, cons
     const int it = d->in_dtype, wt = d->w_dtype, at = d->acc_dtype, ot = d->out_dtype;
     const bool int8 = it == TB_DT_INT8 && (wt == TB_DT_INT8 || wt == TB_DT_INT4) && at == TB_DT_INT32 &&
                       ot == TB_DT_INT32;
-    // float: the tables admit (F16,F16,F32,F16|F32) and (BF16,BF16,F32,BF16|F32) for CONV2D and
-    // (F16,F16,F32,F16), (BF16,BF16,F32,BF16) for DEPTHWISE; only fp32 accumulation runs here.
-    bool fl = it == wt && (it == TB_DT_BF16 || it == TB_DT_FP16) && at == TB_DT_FP32 &&
-              (ot == it || (!depthwise && ot == TB_DT_FP32));
-    if (!int8 && !fl) return fail(TB_ERR_NOT_ACCELERATED, "%s types in=%d w=%d acc=%d out=%d are not accelerated", op,
-                                  it, wt, at, ot);
+    // float, fp32 accumulation only (conv2d_types conv.rs:375-385, standard_types :388-396):
+    // CONV2D (F16|BF16|F32 mixed, F32, F32), (F16, F16, F32, F16), (BF16, BF16, F32, BF16);
+    // DEPTHWISE (F16, F16, F32, F16), (BF16, BF16, F32, BF16), (F32, F32, F32, F32).
+    auto f3 = [](int t) { return t == TB_DT_FP16 || t == TB_DT_BF16 || t == TB_DT_FP32; };
+    bool fl;
+    if (depthwise)
+        fl = it == wt && at == TB_DT_FP32 && ot == it && f3(it);
+    else
+        fl = at == TB_DT_FP32 && ((ot == TB_DT_FP32 && f3(it) && f3(wt)) ||
+                                  (it == wt && ot == it && (it == TB_DT_FP16 || it == TB_DT_BF16)));
+    // the tensor-core float path takes two 16-bit operands of one type
+    const bool tc_float = fl && it == wt && (it == TB_DT_FP16 || it == TB_DT_BF16);
+    if (!int8 && !fl) {
+        if (conv_types_valid(depthwise, it, wt, at, ot))
+            return fail(TB_ERR_NOT_ACCELERATED, "%s types in=%d w=%d acc=%d out=%d are not accelerated", op, it, wt,
+                        at, ot);
+        return fail(TB_ERR_DTYPE_MISMATCH, "%s: unsupported types input=%d weight=%d acc=%d output=%d", op, it, wt, at,
+                    ot);
+    }
     if (int8) {
         if (d->weight_zp != 0 && wt != TB_DT_INT8)
             return fail(TB_ERR_GRAPH, "%s: weight zero point must be zero for non-int8 weight", op);
@@ -659,7 +692,7 @@ static tb_status conv_plan_create(tb_context* ctx, const tb_conv2d_desc* d, cons
                         d->pad[0] <= 127 && d->pad[2] <= 127 && d->kw * d->dilation[1] < 256 &&
                         d->kh * d->dilation[0] < 256 && (taps * d->ic * e) % 16 == 0 && oh <= 255 && ow <= 255 &&
                         aligned16(weight);
-    p->path = tma_ok ? (int8 ? 0 : 1) : (int8 ? 2 : 3);
+    p->path = tma_ok && (int8 || tc_float) ? (int8 ? 0 : 1) : (int8 ? 2 : 3);
     if (p->path == 1) {
         // float bias widened once (the epilogue adds it in f32)
         cudaError_t ce = cudaMalloc(&p->d_fbias, sizeof(float) * d->bias_len);
@@ -1017,6 +1050,16 @@ static tb_status pool_geom(const char* op, const tb_pool2d_desc* d, PoolGeomDev*
     g->pad_t = d->pad[0]; g->pad_l = d->pad[2];
     return TB_OK;
 }
+
+namespace tb {
+tb_status pool_check(const char* op, const tb_pool2d_desc* d, int* oh, int* ow) {
+    PoolGeomDev g;
+    TB_TRY(pool_geom(op, d, &g));
+    *oh = g.oh;
+    *ow = g.ow;
+    return TB_OK;
+}
+}  // namespace tb
 
 extern "C" TB_API tb_status tb_avg_pool2d(tb_context* ctx, const tb_pool2d_desc* d, const void* input, void* out,
                                           void* stream_) {

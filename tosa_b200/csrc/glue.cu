@@ -1,0 +1,226 @@
+// Graph glue kernels used by the graph runner: TRANSPOSE, broadcasting ADD,
+// standalone RESCALE over a prepared plan (int8 lanes vectorised), and the
+// fused residual chain RESCALE(a) + RESCALE(b) -> ADD -> RESCALE [-> CLAMP]
+// that quantized residual networks emit around every skip connection.
+//
+// All of them are HBM-bound elementwise passes: grid-stride loops sized to a
+// multiple of the SM count, 4 int8 lanes per thread where the layout allows.
+// The arithmetic of every step is the reference's (RESCALE: type_conv.rs:168-190
+// through quant.cuh's rescale_value; ADD: elementwise.rs:395-397, int32 wrap);
+// only the intermediate tensors of the chain stay in registers.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "internal.hpp"
+#include "quant.cuh"
+
+namespace tb {
+namespace {
+
+__device__ __forceinline__ int32_t ld_int(const void* p, long long i, int dt, int uns) {
+    if (dt == DT_INT8) {
+        const int8_t v = static_cast<const int8_t*>(p)[i];
+        return uns ? static_cast<int32_t>(static_cast<uint8_t>(v)) : v;
+    }
+    if (dt == DT_INT16) {
+        const int16_t v = static_cast<const int16_t*>(p)[i];
+        return uns ? static_cast<int32_t>(static_cast<uint16_t>(v)) : v;
+    }
+    return static_cast<const int32_t*>(p)[i];
+}
+
+__device__ __forceinline__ void st_int(void* p, long long i, int dt, int32_t v) {
+    if (dt == DT_INT8) static_cast<int8_t*>(p)[i] = static_cast<int8_t>(v);
+    else if (dt == DT_INT16) static_cast<int16_t*>(p)[i] = static_cast<int16_t>(v);
+    else static_cast<int32_t*>(p)[i] = v;
+}
+
+__device__ __forceinline__ float ld_f(const void* p, long long i, int dt) {
+    if (dt == DT_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+    if (dt == DT_FP16) return __half2float(static_cast<const __half*>(p)[i]);
+    return static_cast<const float*>(p)[i];
+}
+
+__device__ __forceinline__ void st_f(void* p, long long i, int dt, float v) {
+    if (dt == DT_BF16) static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+    else if (dt == DT_FP16) static_cast<__half*>(p)[i] = __float2half_rn(v);
+    else static_cast<float*>(p)[i] = v;
+}
+
+__device__ __forceinline__ int64_t rescale_one(const RescaleArgs& r, int64_t x, int ch, uint32_t* err) {
+    const int c = r.per_channel ? ch : 0;
+    return rescale_value(x, r.multiplier[c], r.shift[c], r.rounding, r.scale32, r.out_zp, r.lo, r.hi, err);
+}
+
+// out[idx] = in[sum_d idx_d * in_stride[perm... ]]: the output walks its own
+// row-major index; `src_stride[d]` is the input stride of output dimension d.
+__global__ void transpose_nd(const void* __restrict__ in, void* __restrict__ out, int elem, long long total, int rank,
+                             NdMap map) {
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        long long rem = i, src = 0;
+        for (int d = rank - 1; d >= 0; --d) {
+            const long long q = rem / map.dims[d];
+            src += (rem - q * map.dims[d]) * map.a_stride[d];
+            rem = q;
+        }
+        switch (elem) {
+        case 1: static_cast<uint8_t*>(out)[i] = static_cast<const uint8_t*>(in)[src]; break;
+        case 2: static_cast<uint16_t*>(out)[i] = static_cast<const uint16_t*>(in)[src]; break;
+        case 4: static_cast<uint32_t*>(out)[i] = static_cast<const uint32_t*>(in)[src]; break;
+        default: static_cast<uint64_t*>(out)[i] = static_cast<const uint64_t*>(in)[src]; break;
+        }
+    }
+}
+
+__global__ void add_broadcast(const void* __restrict__ a, const void* __restrict__ b, int dt, long long total,
+                              int rank, NdMap map, void* __restrict__ out) {
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        long long rem = i, ia = 0, ib = 0;
+        for (int d = rank - 1; d >= 0; --d) {
+            const long long q = rem / map.dims[d];
+            const long long r = rem - q * map.dims[d];
+            ia += r * map.a_stride[d];
+            ib += r * map.b_stride[d];
+            rem = q;
+        }
+        if (dt == DT_INT32) {
+            static_cast<int32_t*>(out)[i] = static_cast<int32_t>(static_cast<uint32_t>(static_cast<const int32_t*>(a)[ia]) +
+                                                                 static_cast<uint32_t>(static_cast<const int32_t*>(b)[ib]));
+        } else {
+            st_f(out, i, dt, round_to_dtype(__fadd_rn(ld_f(a, ia, dt), ld_f(b, ib, dt)), dt));
+        }
+    }
+}
+
+// Standalone RESCALE. vec4: int8 input, 4 elements per thread (count % 4 == 0
+// and, when per channel, channels % 4 == 0).
+__global__ void rescale_plan_kernel(const void* __restrict__ in, int in_dt, int in_uns, int32_t izp, long long count,
+                                    int channels, RescaleArgs rs, int out_dt, int vec4, void* __restrict__ out,
+                                    uint32_t* err) {
+    uint32_t lerr = 0;
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    if (vec4) {
+        const long long n4 = count >> 2;
+        for (long long q = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; q < n4; q += stride) {
+            const char4 v = reinterpret_cast<const char4*>(in)[q];
+            const int c0 = rs.per_channel ? static_cast<int>((q << 2) % channels) : 0;
+            int32_t x[4] = {v.x, v.y, v.z, v.w};
+            int32_t r[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int32_t e = in_uns ? (x[k] & 0xff) : x[k];
+                r[k] = static_cast<int32_t>(rescale_one(rs, static_cast<int64_t>(e) - izp, c0 + k, &lerr));
+            }
+            if (out_dt == DT_INT8) {
+                reinterpret_cast<char4*>(out)[q] = make_char4(static_cast<signed char>(r[0]), static_cast<signed char>(r[1]),
+                                                              static_cast<signed char>(r[2]), static_cast<signed char>(r[3]));
+            } else if (out_dt == DT_INT32) {
+                reinterpret_cast<int4*>(out)[q] = make_int4(r[0], r[1], r[2], r[3]);
+            } else {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) st_int(out, (q << 2) + k, out_dt, r[k]);
+            }
+        }
+    } else {
+        for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < count; i += stride) {
+            const int64_t x = static_cast<int64_t>(ld_int(in, i, in_dt, in_uns)) - izp;
+            const int ch = rs.per_channel ? static_cast<int>(i % channels) : 0;
+            st_int(out, i, out_dt, static_cast<int32_t>(rescale_one(rs, x, ch, &lerr)));
+        }
+    }
+    if (lerr) atomicOr(err, lerr);
+}
+
+// Residual chain: o = RESCALE_o( wrap32( RESCALE_a(a - za) + RESCALE_b(b - zb) ) ) [clamped], where
+// RESCALE_a/b produce int32 (their clamp range is the int32 range) and RESCALE_o's
+// range is intersected with a following CLAMP. a and b have the same shape.
+__global__ void residual_chain(const void* __restrict__ a, int a_dt, int a_uns, int32_t za, RescaleArgs ra,
+                               const void* __restrict__ b, int b_dt, int b_uns, int32_t zb, RescaleArgs rb,
+                               RescaleArgs ro, int out_dt, long long count, int channels, int vec4,
+                               void* __restrict__ out, uint32_t* err) {
+    uint32_t lerr = 0;
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    auto one = [&](int32_t va, int32_t vb, int ch) -> int32_t {
+        const int32_t sa = static_cast<int32_t>(rescale_one(ra, static_cast<int64_t>(va) - za, ch, &lerr));
+        const int32_t sb = static_cast<int32_t>(rescale_one(rb, static_cast<int64_t>(vb) - zb, ch, &lerr));
+        const int32_t s = static_cast<int32_t>(static_cast<uint32_t>(sa) + static_cast<uint32_t>(sb));
+        return static_cast<int32_t>(rescale_one(ro, s, ch, &lerr));
+    };
+    if (vec4) {
+        const long long n4 = count >> 2;
+        for (long long q = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; q < n4; q += stride) {
+            const char4 x = reinterpret_cast<const char4*>(a)[q];
+            const char4 y = reinterpret_cast<const char4*>(b)[q];
+            const int c0 = static_cast<int>((q << 2) % channels);
+            const int32_t xa[4] = {x.x, x.y, x.z, x.w};
+            const int32_t yb[4] = {y.x, y.y, y.z, y.w};
+            int32_t r[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                r[k] = one(a_uns ? (xa[k] & 0xff) : xa[k], b_uns ? (yb[k] & 0xff) : yb[k], c0 + k);
+            if (out_dt == DT_INT8) {
+                reinterpret_cast<char4*>(out)[q] = make_char4(static_cast<signed char>(r[0]), static_cast<signed char>(r[1]),
+                                                              static_cast<signed char>(r[2]), static_cast<signed char>(r[3]));
+            } else {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) st_int(out, (q << 2) + k, out_dt, r[k]);
+            }
+        }
+    } else {
+        for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < count; i += stride) {
+            const int ch = static_cast<int>(i % channels);
+            st_int(out, i, out_dt, one(ld_int(a, i, a_dt, a_uns), ld_int(b, i, b_dt, b_uns), ch));
+        }
+    }
+    if (lerr) atomicOr(err, lerr);
+}
+
+}  // namespace
+
+tb_status launch_transpose(tb_context* ctx, const void* in, void* out, int elem, long long total, int rank,
+                           const NdMap& map, cudaStream_t st) {
+    if (total == 0) return TB_OK;
+    transpose_nd<<<grid_for(ctx, total), 256, 0, st>>>(in, out, elem, total, rank, map);
+    TB_LAUNCHED(ctx);
+    return TB_OK;
+}
+
+tb_status launch_add_broadcast(tb_context* ctx, int dtype, const void* a, const void* b, long long total, int rank,
+                               const NdMap& map, void* out, cudaStream_t st) {
+    if (total == 0) return TB_OK;
+    add_broadcast<<<grid_for(ctx, total), 256, 0, st>>>(a, b, dtype, total, rank, map, out);
+    TB_LAUNCHED(ctx);
+    return TB_OK;
+}
+
+tb_status launch_rescale(tb_context* ctx, const RescalePlan& r, int in_dtype, int in_uns, int32_t izp, const void* in,
+                         long long count, int channels, void* out, cudaStream_t st) {
+    if (count == 0) return TB_OK;
+    const bool vec4 = in_dtype == TB_DT_INT8 && count % 4 == 0 && (!r.per_channel || channels % 4 == 0) &&
+                      aligned16(in) && aligned16(out);
+    const long long work = vec4 ? count / 4 : count;
+    rescale_plan_kernel<<<grid_for(ctx, work), 256, 0, st>>>(in, in_dtype, in_uns, izp, count, channels,
+                                                             rescale_args(r), r.out_dtype, vec4 ? 1 : 0, out,
+                                                             ctx->dev_err);
+    TB_LAUNCHED(ctx);
+    return TB_OK;
+}
+
+tb_status launch_residual(tb_context* ctx, const void* a, int a_dt, int a_uns, int32_t za, const RescalePlan& ra,
+                          const void* b, int b_dt, int b_uns, int32_t zb, const RescalePlan& rb,
+                          const RescalePlan& ro, long long count, int channels, void* out, cudaStream_t st) {
+    if (count == 0) return TB_OK;
+    const bool vec4 = a_dt == TB_DT_INT8 && b_dt == TB_DT_INT8 && count % 4 == 0 && channels % 4 == 0 &&
+                      aligned16(a) && aligned16(b) && aligned16(out);
+    const long long work = vec4 ? count / 4 : count;
+    residual_chain<<<grid_for(ctx, work), 256, 0, st>>>(a, a_dt, a_uns, za, rescale_args(ra), b, b_dt, b_uns, zb,
+                                                        rescale_args(rb), rescale_args(ro), ro.out_dtype, count,
+                                                        channels, vec4 ? 1 : 0, out, ctx->dev_err);
+    TB_LAUNCHED(ctx);
+    return TB_OK;
+}
+
+}  // namespace tb

@@ -33,6 +33,14 @@ tb_status fail(tb_status st, const char* fmt, ...);
             return ::tb::fail(TB_ERR_CUDA, "%s failed: %s", #call, cudaGetErrorString(e_));    \
     } while (0)
 
+// After a kernel launch: report a launch error, else count the launch.
+#define TB_LAUNCHED(ctx)                                                                               \
+    do {                                                                                               \
+        cudaError_t e_ = cudaGetLastError();                                                           \
+        if (e_ != cudaSuccess) return ::tb::fail(TB_ERR_CUDA, "kernel launch failed: %s", cudaGetErrorString(e_)); \
+        (ctx)->launches++;                                                                             \
+    } while (0)
+
 #define TB_TRY(expr)                         \
     do {                                     \
         tb_status s_ = (expr);               \
@@ -87,6 +95,31 @@ void place_rescale(RescalePlan* r, int32_t* dev_blob);
 
 int grid_for(const tb_context* ctx, long long work, int block = 256);
 
+struct RescaleArgs;
+RescaleArgs rescale_args(const RescalePlan& r);
+
+// Index map of an N-d elementwise pass (rank <= 6): output dims, and the
+// element strides of operands a/b along each output dimension (0 = broadcast).
+struct NdMap {
+    long long dims[6];
+    long long a_stride[6];
+    long long b_stride[6];
+};
+
+// AVG_POOL2D / MAX_POOL2D geometry checks (src/ops/pool.rs:31-70).
+tb_status pool_check(const char* op, const tb_pool2d_desc* d, int* oh, int* ow);
+
+// Graph glue launchers (glue.cu).
+tb_status launch_transpose(tb_context* ctx, const void* in, void* out, int elem, long long total, int rank,
+                           const NdMap& map, cudaStream_t st);
+tb_status launch_add_broadcast(tb_context* ctx, int dtype, const void* a, const void* b, long long total, int rank,
+                               const NdMap& map, void* out, cudaStream_t st);
+tb_status launch_rescale(tb_context* ctx, const RescalePlan& r, int in_dtype, int in_uns, int32_t izp, const void* in,
+                         long long count, int channels, void* out, cudaStream_t st);
+tb_status launch_residual(tb_context* ctx, const void* a, int a_dt, int a_uns, int32_t za, const RescalePlan& ra,
+                          const void* b, int b_dt, int b_uns, int32_t zb, const RescalePlan& rb,
+                          const RescalePlan& ro, long long count, int channels, void* out, cudaStream_t st);
+
 // MATMUL static checks (src/ops/matmul.rs:112-153) and path choice:
 // path 0 tensor-core int8, 1 tensor-core f16/bf16, 2 direct int8, 3 direct float.
 tb_status matmul_validate(const tb_matmul_desc* d, bool has_rescale, int* path, int* bn);
@@ -103,6 +136,7 @@ struct tb_matmul_plan {
     int32_t* d_colterm = nullptr;  // [n][w] (+ one tile of padding) when a_zp != 0
     unsigned int* d_counter = nullptr;  // column-sum units finished, grows by `units` per run
     unsigned int epoch = 0;
+    bool replayable = false;  // reset the column-sum counter on every run (CUDA-graph replay)
     const void* a_cached = nullptr;
     const void* b_cached = nullptr;
     CUtensorMap tmA, tmB;

@@ -310,28 +310,36 @@ def read_graph(data: bytes) -> Graph:
 
 
 class _Builder:
-    """Minimal back-to-front flatbuffer builder (standard wire format)."""
+    """Minimal back-to-front flatbuffer builder (standard wire format).
+
+    The buffer grows at the front; pieces are kept in a list (last piece =
+    frontmost) and joined once at the end, so building is linear in size.
+    Offsets are measured from the end, as in the flatbuffers implementations."""
 
     def __init__(self):
-        self.buf = bytearray()  # grows at the front: data is stored reversed-relative
+        self.chunks: list = []
+        self.size = 0
         self.minalign = 1
 
-    # The builder keeps `buf` as the tail of the final buffer; offsets are
-    # measured from the end (as in the reference flatbuffers implementation).
     def off(self):
-        return len(self.buf)
+        return self.size
+
+    def _front(self, data: bytes):
+        self.chunks.append(data)
+        self.size += len(data)
 
     def pad(self, n):
-        self.buf[0:0] = b"\x00" * n
+        if n:
+            self._front(b"\x00" * n)
 
     def prep(self, size, additional):
         if size > self.minalign:
             self.minalign = size
-        align = (-(len(self.buf) + additional)) % size
+        align = (-(self.size + additional)) % size
         self.pad(align)
 
     def put(self, fmt, v):
-        self.buf[0:0] = struct.pack("<" + fmt, v)
+        self._front(struct.pack("<" + fmt, v))
 
     def add_scalar(self, fmt, v):
         sz = struct.calcsize(fmt)
@@ -348,21 +356,20 @@ class _Builder:
     def create_bytes(self, data: bytes, align=8):
         self.prep(max(4, align), len(data))
         self.prep(4, len(data))
-        self.buf[0:0] = bytes(data)
+        self._front(bytes(data))
         self.put("I", len(data))
         return self.off()
 
     def create_string(self, s: str):
         data = s.encode()
         self.prep(4, len(data) + 1)
-        self.buf[0:0] = data + b"\x00"
+        self._front(data + b"\x00")
         self.put("I", len(data))
         return self.off()
 
     def create_i32_vec(self, vals):
         self.prep(4, 4 * len(vals))
-        for v in reversed(vals):
-            self.put("i", int(v))
+        self._front(struct.pack(f"<{len(vals)}i", *[int(v) for v in vals]))
         self.put("I", len(vals))
         return self.off()
 
@@ -395,10 +402,9 @@ class _Builder:
                 pos[i] = self.add_scalar("i", int(v))
             elif kind == "u64":
                 pos[i] = self.add_scalar("Q", int(v))
-        # soffset to vtable
+        # soffset to the vtable, which is written immediately in front of the table
         self.prep(4, 0)
-        self.put("i", 0)
-        table_off = self.off()
+        table_off = self.off() + 4
         nf = len(fields)
         while nf and fields[nf - 1] is None:
             nf -= 1
@@ -407,19 +413,16 @@ class _Builder:
             vt[i] = table_off - p
         table_size = table_off - start
         vbytes = struct.pack(f"<HH{nf}H", 4 + 2 * nf, table_size, *vt)
-        self.buf[0:0] = vbytes  # vtable immediately precedes the table (2-byte aligned)
-        vt_off = self.off()
-        # patch soffset: vtable position = table position - soffset
-        tpos = len(self.buf) - table_off
-        struct.pack_into("<i", self.buf, tpos, vt_off - table_off)
-        # alignment of vtable is 2; keep 4 alignment for following data
+        # vtable position = table position - soffset (the vtable precedes the table)
+        self.put("i", len(vbytes))
+        self._front(vbytes)
         return table_off
 
     def finish(self, root, ident=b"TOSA"):
         self.prep(max(self.minalign, 8), 8)
-        self.buf[0:0] = ident
+        self._front(ident)
         self.add_uoffset(root)
-        return bytes(self.buf)
+        return b"".join(reversed(self.chunks))
 
 
 def _attr_fields(opname, attr, b: _Builder):
