@@ -189,6 +189,10 @@ CONV_CASES = [
     (2, 15, 15, 64, 128, 1, 1, (0, 0, 0, 0), (2, 2), (1, 1), -8, 8),
     (1, 13, 13, 16, 64, 5, 5, (2, 2, 2, 2), (2, 2), (1, 1), 4, -4),
     (1, 7, 7, 256, 320, 3, 3, (1, 1, 1, 1), (1, 1), (1, 1), 0, 0),
+    # few input channels: im2col rows + 1x1 tensor-core convolution (RGB stems)
+    (4, 64, 64, 3, 64, 7, 7, (2, 3, 2, 3), (2, 2), (1, 1), -5, 3),
+    (3, 96, 80, 3, 32, 3, 3, (0, 1, 0, 1), (2, 2), (1, 1), 6, 0),
+    (1, 72, 72, 4, 48, 5, 5, (2, 2, 1, 3), (1, 1), (1, 2), -128, -2),
 ]
 
 

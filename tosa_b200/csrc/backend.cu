@@ -382,27 +382,30 @@ tb_status matmul_validate(const tb_matmul_desc* d, bool has_rescale, int* path, 
     // matmul_types (src/ops/matmul.rs:30-38), restricted to what runs here.
     const int at = d->a_dtype, bt = d->b_dtype, ot = d->out_dtype;
     const bool int8 = at == TB_DT_INT8 && bt == TB_DT_INT8 && ot == TB_DT_INT32;
-    const bool f32 = at == TB_DT_FP32 && bt == TB_DT_FP32 && ot == TB_DT_FP32;
-    const bool fl = ((at == bt) && (at == TB_DT_BF16 || at == TB_DT_FP16) && ot == TB_DT_FP32) || f32;
+    const bool int16 = at == TB_DT_INT16 && bt == TB_DT_INT16 && ot == TB_DT_INT48;
     const bool fp8a = at == TB_DT_FP8E4M3 || at == TB_DT_FP8E5M2, fp8b = bt == TB_DT_FP8E4M3 || bt == TB_DT_FP8E5M2;
-    const bool valid_other = (at == TB_DT_INT16 && bt == TB_DT_INT16 && ot == TB_DT_INT48) ||
-                             (at == TB_DT_FP16 && bt == TB_DT_FP16 && ot == TB_DT_FP16) ||
-                             (fp8a && fp8b && (ot == TB_DT_FP16 || ot == TB_DT_FP32));
-    if (!int8 && !fl) {
-        if (valid_other) return fail(TB_ERR_NOT_ACCELERATED, "MATMUL types %d x %d -> %d are not accelerated", at, bt, ot);
-        return fail(TB_ERR_DTYPE_MISMATCH, "MATMUL: unsupported types a=%d b=%d output=%d", at, bt, ot);
-    }
-    if (int8) {
+    // (F16, F16, F16|F32), (BF16, BF16, F32), (F32, F32, F32), (FP8, FP8, F16|F32)
+    const bool fl = (at == TB_DT_FP16 && bt == TB_DT_FP16 && (ot == TB_DT_FP16 || ot == TB_DT_FP32)) ||
+                    (at == TB_DT_BF16 && bt == TB_DT_BF16 && ot == TB_DT_FP32) ||
+                    (at == TB_DT_FP32 && bt == TB_DT_FP32 && ot == TB_DT_FP32) ||
+                    (fp8a && fp8b && (ot == TB_DT_FP16 || ot == TB_DT_FP32));
+    if (!int8 && !int16 && !fl) return fail(TB_ERR_DTYPE_MISMATCH, "MATMUL: unsupported types a=%d b=%d output=%d", at, bt, ot);
+    if (int8 || int16) {
         if ((d->a_zp != 0 && at != TB_DT_INT8) || (d->b_zp != 0 && bt != TB_DT_INT8))
             return fail(TB_ERR_GRAPH, "MATMUL: zero points must be zero for non-int8 inputs");
     } else if (d->a_zp != 0 || d->b_zp != 0) {
         return fail(TB_ERR_GRAPH, "MATMUL: zero points must be zero for floating-point inputs");
     }
-    if (has_rescale && !int8) return fail(TB_ERR_DTYPE_MISMATCH, "MATMUL: RESCALE needs an integer result");
+    if (has_rescale && !int8) return fail(TB_ERR_DTYPE_MISMATCH, "MATMUL: RESCALE needs an int32 result");
     const int e = int8 ? 1 : 2;
     const bool tma_ok = (static_cast<long long>(d->c) * e) % 16 == 0 && (static_cast<long long>(d->w) * e) % 16 == 0 &&
                         d->c > 0 && d->w > 0 && d->h > 0 && d->n > 0;
-    *path = tma_ok && !f32 ? (int8 ? 0 : 1) : (int8 ? 2 : 3);
+    // tensor cores: int8 -> int32, and BF16/F16 pairs with an FP32 result; everything else runs
+    // the direct kernels in the reference's accumulation order (path 2 int8, 3 float, 4 int16)
+    const bool tc_float = at == bt && (at == TB_DT_BF16 || at == TB_DT_FP16) && ot == TB_DT_FP32;
+    if (int16) *path = 4;
+    else if (int8) *path = tma_ok ? 0 : 2;
+    else *path = tma_ok && tc_float ? 1 : 3;
     *bn = d->w <= 128 ? 128 : 256;
     return TB_OK;
 }
@@ -449,9 +452,13 @@ extern "C" TB_API tb_status tb_matmul_plan_run(tb_matmul_plan* p, const void* a,
             matmul_direct_int<<<grid_for(ctx, total), 256, 0, st>>>(d.n, d.h, d.c, d.w, static_cast<const int8_t*>(a),
                                                                     static_cast<const int8_t*>(b), d.a_zp, d.b_zp,
                                                                     int_epi(p->rs), out, ctx->dev_err);
+        } else if (d.a_dtype == TB_DT_INT16) {
+            matmul_direct_i48<<<grid_for(ctx, total), 256, 0, st>>>(d.n, d.h, d.c, d.w, static_cast<const int16_t*>(a),
+                                                                    static_cast<const int16_t*>(b),
+                                                                    static_cast<int64_t*>(out));
         } else {
-            matmul_direct_float<<<grid_for(ctx, total), 256, 0, st>>>(d.n, d.h, d.c, d.w, a, b, d.a_dtype,
-                                                                      TB_DT_FP32, out);
+            matmul_direct_float<<<grid_for(ctx, total), 256, 0, st>>>(d.n, d.h, d.c, d.w, a, b, d.a_dtype, d.b_dtype,
+                                                                      d.out_dtype, out);
         }
         TB_LAUNCHED(ctx);
         return TB_OK;
@@ -554,7 +561,8 @@ struct tb_conv2d_plan {
     tb_conv2d_desc d{};
     bool depthwise = false;
     int oh = 0, ow = 0;
-    int path = 0;  // 0 TC int8, 1 TC f16/bf16, 2 direct int, 3 direct float, 4 dw int vec4, 5 dw int, 6 dw float
+    int path = 0;  // 0 TC int8, 1 TC f16/bf16, 2 direct int, 3 direct float, 4 dw int vec4, 5 dw int, 6 dw float,
+                   // 7 direct INT16 x INT8 -> INT48 (conv or depthwise)
     const void* weight = nullptr;
     const void* bias = nullptr;
     RescalePlan rs;
@@ -569,6 +577,11 @@ struct tb_conv2d_plan {
     const void* in_cached = nullptr;
     CUtensorMap tmA, tmB;
     float* d_fbias = nullptr;  // float bias widened to f32
+    // path 8: im2col rows + a 1x1 tensor-core convolution over them
+    tb_conv2d_plan* inner = nullptr;
+    int8_t* d_rows = nullptr;       // [n*oh*ow][kp]
+    int8_t* d_wpad = nullptr;       // [oc][kp]
+    int kp = 0;
 };
 
 static tb_status conv_extent(const char* op, int in, int pb, int pa, int k, int dil, int stride, int* out) {
@@ -637,32 +650,25 @@ static tb_status conv_plan_create(tb_context* ctx, const tb_conv2d_desc* d, cons
     const int it = d->in_dtype, wt = d->w_dtype, at = d->acc_dtype, ot = d->out_dtype;
     const bool int8 = it == TB_DT_INT8 && (wt == TB_DT_INT8 || wt == TB_DT_INT4) && at == TB_DT_INT32 &&
                       ot == TB_DT_INT32;
-    // float, fp32 accumulation only (conv2d_types conv.rs:375-385, standard_types :388-396):
-    // CONV2D (F16|BF16|F32 mixed, F32, F32), (F16, F16, F32, F16), (BF16, BF16, F32, BF16);
-    // DEPTHWISE (F16, F16, F32, F16), (BF16, BF16, F32, BF16), (F32, F32, F32, F32).
-    auto f3 = [](int t) { return t == TB_DT_FP16 || t == TB_DT_BF16 || t == TB_DT_FP32; };
-    bool fl;
-    if (depthwise)
-        fl = it == wt && at == TB_DT_FP32 && ot == it && f3(it);
-    else
-        fl = at == TB_DT_FP32 && ((ot == TB_DT_FP32 && f3(it) && f3(wt)) ||
-                                  (it == wt && ot == it && (it == TB_DT_FP16 || it == TB_DT_BF16)));
-    // the tensor-core float path takes two 16-bit operands of one type
-    const bool tc_float = fl && it == wt && (it == TB_DT_FP16 || it == TB_DT_BF16);
-    if (!int8 && !fl) {
-        if (conv_types_valid(depthwise, it, wt, at, ot))
-            return fail(TB_ERR_NOT_ACCELERATED, "%s types in=%d w=%d acc=%d out=%d are not accelerated", op, it, wt,
-                        at, ot);
+    const bool int16 = it == TB_DT_INT16 && wt == TB_DT_INT8 && at == TB_DT_INT48 && ot == TB_DT_INT48;
+    // every type combination of the reference's tables runs: int8 and BF16/F16 pairs with
+    // fp32 accumulation on tensor cores where the layout allows, the rest (fp8 operands,
+    // mixed float types, f16/bf16 accumulators, INT16 x INT8 -> INT48) on the direct
+    // kernels in the reference's accumulation order
+    if (!conv_types_valid(depthwise, it, wt, at, ot))
         return fail(TB_ERR_DTYPE_MISMATCH, "%s: unsupported types input=%d weight=%d acc=%d output=%d", op, it, wt, at,
                     ot);
-    }
-    if (int8) {
+    const bool fl = !int8 && !int16;
+    const bool tc_float = fl && it == wt && (it == TB_DT_FP16 || it == TB_DT_BF16) && at == TB_DT_FP32;
+    if (int8 || int16) {
+        if (d->input_zp != 0 && it != TB_DT_INT8)
+            return fail(TB_ERR_GRAPH, "%s: input zero point must be zero for non-int8 input", op);
         if (d->weight_zp != 0 && wt != TB_DT_INT8)
             return fail(TB_ERR_GRAPH, "%s: weight zero point must be zero for non-int8 weight", op);
     } else if (d->input_zp != 0 || d->weight_zp != 0) {
         return fail(TB_ERR_GRAPH, "%s: zero points must be zero for floating-point operands", op);
     }
-    if (rescale && !int8) return fail(TB_ERR_DTYPE_MISMATCH, "%s: RESCALE needs an integer result", op);
+    if (rescale && !int8) return fail(TB_ERR_DTYPE_MISMATCH, "%s: RESCALE needs an int32 result", op);
 
     tb_conv2d_plan* p = new tb_conv2d_plan;
     p->ctx = ctx;
@@ -681,6 +687,11 @@ static tb_status conv_plan_create(tb_context* ctx, const tb_conv2d_desc* d, cons
         tb_status s = make_rescale_plan(ctx, rescale, TB_DT_INT32, oc, &p->rs);
         if (s != TB_OK) return bail(s);
     }
+    if (int16) {
+        p->path = 7;
+        *out = p;
+        return TB_OK;
+    }
     if (depthwise) {
         p->path = int8 ? ((d->m == 1 && d->ic % 4 == 0) ? 4 : 5) : 6;
         *out = p;
@@ -693,6 +704,36 @@ static tb_status conv_plan_create(tb_context* ctx, const tb_conv2d_desc* d, cons
                         d->kh * d->dilation[0] < 256 && (taps * d->ic * e) % 16 == 0 && oh <= 255 && ow <= 255 &&
                         aligned16(weight);
     p->path = tma_ok && (int8 || tc_float) ? (int8 ? 0 : 1) : (int8 ? 2 : 3);
+    // Few input channels (an RGB stem): gather im2col rows once and run them as a 1x1
+    // tensor-core convolution when the contraction is long enough to pay for the rows.
+    const long long kfull = taps * d->ic;
+    const long long m_rows = static_cast<long long>(d->n) * oh * ow;
+    if (p->path == 2 && wt == TB_DT_INT8 && kfull >= 16 && m_rows >= 4096 && aligned16(weight) &&
+        m_rows * ((kfull + 15) / 16 * 16) <= (4ll << 30)) {
+        p->path = 8;
+        p->kp = static_cast<int>((kfull + 15) / 16 * 16);
+        cudaError_t ce = cudaMalloc(&p->d_rows, static_cast<size_t>(m_rows) * p->kp);
+        if (ce == cudaSuccess) ce = cudaMalloc(&p->d_wpad, static_cast<size_t>(oc) * p->kp);
+        if (ce != cudaSuccess) return bail(fail(TB_ERR_CUDA, "im2col buffer allocation failed: %s", cudaGetErrorString(ce)));
+        pad_weight_rows_i8<<<grid_for(ctx, static_cast<long long>(oc) * p->kp), 256>>>(
+            oc, static_cast<int>(kfull), p->kp, static_cast<const int8_t*>(weight), p->d_wpad);
+        ce = cudaGetLastError();
+        if (ce == cudaSuccess) ce = cudaDeviceSynchronize();
+        if (ce != cudaSuccess) return bail(fail(TB_ERR_CUDA, "weight padding failed: %s", cudaGetErrorString(ce)));
+        ctx->launches++;
+        tb_conv2d_desc in = *d;
+        in.ih = oh;
+        in.iw = ow;
+        in.ic = p->kp;
+        in.kh = in.kw = 1;
+        for (int i = 0; i < 4; ++i) in.pad[i] = 0;
+        in.stride[0] = in.stride[1] = in.dilation[0] = in.dilation[1] = 1;
+        tb_status s2 = conv_plan_create(ctx, &in, p->d_wpad, bias, rescale, false, &p->inner);
+        if (s2 != TB_OK) return bail(s2);
+        if (p->inner->path != 0) return bail(fail(TB_ERR_NOT_ACCELERATED, "%s: im2col rows did not take the tensor cores", op));
+        *out = p;
+        return TB_OK;
+    }
     if (p->path == 1) {
         // float bias widened once (the epilogue adds it in f32)
         cudaError_t ce = cudaMalloc(&p->d_fbias, sizeof(float) * d->bias_len);
@@ -839,7 +880,7 @@ extern "C" TB_API tb_status tb_conv2d_plan_run(tb_conv2d_plan* p, const void* in
         return TB_OK;
     case 3:
         conv2d_direct_float<<<grid_for(ctx, total), 256, 0, st>>>(g, input, p->weight, p->bias, d.bias_len, d.in_dtype,
-                                                                  d.w_dtype, d.out_dtype, out);
+                                                                  d.w_dtype, d.acc_dtype, d.out_dtype, out);
         TB_LAUNCHED(ctx);
         return TB_OK;
     case 4:
@@ -860,7 +901,21 @@ extern "C" TB_API tb_status tb_conv2d_plan_run(tb_conv2d_plan* p, const void* in
         return TB_OK;
     case 6:
         depthwise_float<<<grid_for(ctx, total), 256, 0, st>>>(g, input, p->weight, p->bias, d.bias_len, d.in_dtype,
-                                                              d.out_dtype, out);
+                                                              d.w_dtype, d.acc_dtype, d.out_dtype, out);
+        TB_LAUNCHED(ctx);
+        return TB_OK;
+    case 8: {
+        im2col_rows_i8<<<grid_for(ctx, static_cast<long long>(d.n) * p->oh * p->ow * (p->kp / 16)), 256, 0, st>>>(
+            g, static_cast<const int8_t*>(input), d.kh * d.kw * d.ic, p->kp, static_cast<int8_t>(d.input_zp), p->d_rows);
+        TB_LAUNCHED(ctx);
+        return tb_conv2d_plan_run(p->inner, p->d_rows, out, stream_);
+    }
+    case 7:
+        conv2d_direct_i48<<<grid_for(ctx, total), 256, 0, st>>>(g, static_cast<const int16_t*>(input),
+                                                                static_cast<const int8_t*>(p->weight),
+                                                                static_cast<const int64_t*>(p->bias), d.bias_len,
+                                                                d.input_zp, d.weight_zp, p->depthwise ? 1 : 0,
+                                                                static_cast<int64_t*>(out));
         TB_LAUNCHED(ctx);
         return TB_OK;
     default: break;
@@ -934,6 +989,9 @@ extern "C" TB_API tb_status tb_conv2d_plan_run(tb_conv2d_plan* p, const void* in
 
 extern "C" TB_API void tb_conv2d_plan_destroy(tb_conv2d_plan* p) {
     if (!p) return;
+    if (p->inner) tb_conv2d_plan_destroy(p->inner);
+    if (p->d_rows) cudaFree(p->d_rows);
+    if (p->d_wpad) cudaFree(p->d_wpad);
     free_rescale_plan(&p->rs);
     if (p->d_colterm) cudaFree(p->d_colterm);
     if (p->d_ctdelta) cudaFree(p->d_ctdelta);
@@ -972,7 +1030,6 @@ extern "C" TB_API tb_status tb_depthwise_conv2d(tb_context* ctx, const tb_conv2d
 extern "C" TB_API tb_status tb_rescale(tb_context* ctx, const tb_rescale_attr* attr, int32_t in_dtype,
                                        const void* input, int64_t count, void* out, void* stream_) {
     if (!ctx || !attr || (count > 0 && (!input || !out))) return fail(TB_ERR_INVALID_ARGUMENT, "null argument");
-    if (in_dtype == TB_DT_INT48) return fail(TB_ERR_NOT_ACCELERATED, "RESCALE of INT48 input is not accelerated");
     TB_CUDA(cudaSetDevice(ctx->device));
     RescalePlan r;
     int64_t izp = 0, ozp = 0;
@@ -1067,10 +1124,12 @@ extern "C" TB_API tb_status tb_avg_pool2d(tb_context* ctx, const tb_pool2d_desc*
     PoolGeomDev g;
     TB_TRY(pool_geom("AVG_POOL2D", d, &g));
     const int dt = d->dtype, at = d->acc_dtype;
+    // (src/ops/pool.rs:182-187)
     const bool ok = ((dt == TB_DT_INT8 || dt == TB_DT_INT16) && at == TB_DT_INT32) ||
                     (dt == TB_DT_FP16 && (at == TB_DT_FP16 || at == TB_DT_FP32)) ||
-                    ((dt == TB_DT_BF16 || dt == TB_DT_FP32) && at == TB_DT_FP32);
-    if (!ok) return fail(TB_ERR_NOT_ACCELERATED, "AVG_POOL2D types %d/%d are not accelerated", dt, at);
+                    ((dt == TB_DT_BF16 || dt == TB_DT_FP32) && at == TB_DT_FP32) ||
+                    ((dt == TB_DT_FP8E4M3 || dt == TB_DT_FP8E5M2) && at == TB_DT_FP16);
+    if (!ok) return fail(TB_ERR_DTYPE_MISMATCH, "AVG_POOL2D: unsupported types input=%d acc=%d", dt, at);
     if (dt != TB_DT_INT8 && (d->input_zp != 0 || d->output_zp != 0))
         return fail(TB_ERR_GRAPH, "AVG_POOL2D: zero points must be zero for non-int8 data");
     const long long total = static_cast<long long>(g.n) * g.oh * g.ow * g.c;
@@ -1098,8 +1157,9 @@ extern "C" TB_API tb_status tb_max_pool2d(tb_context* ctx, const tb_pool2d_desc*
     const int dt = d->dtype;
     const long long total = static_cast<long long>(g.n) * g.oh * g.ow * g.c;
     cudaStream_t st = static_cast<cudaStream_t>(stream_);
-    if (!(dt == TB_DT_INT8 || dt == TB_DT_INT16 || dt == TB_DT_FP16 || dt == TB_DT_BF16 || dt == TB_DT_FP32))
-        return fail(TB_ERR_NOT_ACCELERATED, "MAX_POOL2D dtype %d is not accelerated", dt);
+    if (!(dt == TB_DT_INT8 || dt == TB_DT_INT16 || dt == TB_DT_FP16 || dt == TB_DT_BF16 || dt == TB_DT_FP32 ||
+          dt == TB_DT_FP8E4M3 || dt == TB_DT_FP8E5M2))
+        return fail(TB_ERR_DTYPE_MISMATCH, "MAX_POOL2D: unsupported dtype %d", dt);
     if (total == 0) return TB_OK;
     if (!input || !out) return fail(TB_ERR_INVALID_ARGUMENT, "null argument");
     if (dt == TB_DT_INT8 && g.c % 4 == 0 && aligned16(input))

@@ -18,7 +18,8 @@
 namespace tb {
 namespace {
 
-__device__ __forceinline__ int32_t ld_int(const void* p, long long i, int dt, int uns) {
+__device__ __forceinline__ int64_t ld_int(const void* p, long long i, int dt, int uns) {
+    if (dt == DT_INT48) return static_cast<const int64_t*>(p)[i];  // INT48 is stored as int64
     if (dt == DT_INT8) {
         const int8_t v = static_cast<const int8_t*>(p)[i];
         return uns ? static_cast<int32_t>(static_cast<uint8_t>(v)) : v;
@@ -126,7 +127,7 @@ __global__ void rescale_plan_kernel(const void* __restrict__ in, int in_dt, int 
         }
     } else {
         for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < count; i += stride) {
-            const int64_t x = static_cast<int64_t>(ld_int(in, i, in_dt, in_uns)) - izp;
+            const int64_t x = ld_int(in, i, in_dt, in_uns) - izp;
             const int ch = rs.per_channel ? static_cast<int>(i % channels) : 0;
             st_int(out, i, out_dt, static_cast<int32_t>(rescale_one(rs, x, ch, &lerr)));
         }
@@ -172,7 +173,8 @@ __global__ void residual_chain(const void* __restrict__ a, int a_dt, int a_uns, 
     } else {
         for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < count; i += stride) {
             const int ch = static_cast<int>(i % channels);
-            st_int(out, i, out_dt, one(ld_int(a, i, a_dt, a_uns), ld_int(b, i, b_dt, b_uns), ch));
+            st_int(out, i, out_dt, one(static_cast<int32_t>(ld_int(a, i, a_dt, a_uns)),
+                                       static_cast<int32_t>(ld_int(b, i, b_dt, b_uns)), ch));
         }
     }
     if (lerr) atomicOr(err, lerr);

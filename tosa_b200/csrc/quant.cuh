@@ -26,8 +26,62 @@ enum : int { ROUND_SINGLE = 1, ROUND_INEXACT = 2, ROUND_DOUBLE = 3 };
 // DType codes (schema DType enum).
 enum : int {
     DT_BOOL = 1, DT_INT4 = 2, DT_INT8 = 3, DT_INT16 = 4, DT_INT32 = 5, DT_INT48 = 6,
-    DT_FP32 = 7, DT_FP16 = 8, DT_BF16 = 9, DT_SHAPE = 10, DT_INT64 = 17,
+    DT_FP32 = 7, DT_FP16 = 8, DT_BF16 = 9, DT_SHAPE = 10, DT_FP8E4M3 = 11, DT_FP8E5M2 = 12, DT_INT64 = 17,
 };
+
+// FP8 formats (src/float8.rs): E4M3 (bias 7, no infinities, NaN = exponent and
+// mantissa all ones, overflow -> NaN) and E5M2 (bias 15, IEEE-style infinities
+// and NaNs, overflow -> infinity). Decoding is exact.
+__device__ __forceinline__ float fp8_decode(uint8_t bits, int dt) {
+    const int man_bits = dt == DT_FP8E4M3 ? 3 : 2;
+    const int bias = dt == DT_FP8E4M3 ? 7 : 15;
+    const unsigned maxe = (1u << (7 - man_bits)) - 1u, manm = (1u << man_bits) - 1u;
+    const unsigned e = (bits >> man_bits) & maxe, m = bits & manm;
+    const bool has_inf = dt == DT_FP8E5M2;
+    if (has_inf ? (e == maxe && m != 0) : (e == maxe && m == manm)) return __int_as_float(0x7fc00000);
+    const float sign = (bits & 0x80) ? -1.f : 1.f;
+    if (has_inf && e == maxe) return sign * __int_as_float(0x7f800000);
+    // value = m * 2^(1 - bias - man_bits) (subnormal) or (2^man_bits + m) * 2^(e - bias - man_bits)
+    const int expo = (e == 0 ? 1 : static_cast<int>(e)) - bias - man_bits;
+    const float mant = static_cast<float>(e == 0 ? m : ((1u << man_bits) | m));
+    return sign * mant * __int_as_float((127 + expo) << 23);
+}
+
+// Round-to-nearest-even encode with the format's overflow rule.
+__device__ __forceinline__ uint8_t fp8_encode(float x, int dt) {
+    const int man_bits = dt == DT_FP8E4M3 ? 3 : 2;
+    const int bias = dt == DT_FP8E4M3 ? 7 : 15;
+    const bool has_inf = dt == DT_FP8E5M2;
+    const unsigned maxe = (1u << (7 - man_bits)) - 1u, manm = (1u << man_bits) - 1u;
+    const uint8_t nanv = static_cast<uint8_t>((maxe << man_bits) | manm);
+    const uint32_t u = __float_as_uint(x);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return nanv;
+    const uint8_t sign = (u >> 31) ? 0x80 : 0;
+    const uint8_t overflow = has_inf ? static_cast<uint8_t>(sign | (maxe << man_bits)) : static_cast<uint8_t>(sign | nanv);
+    if ((u & 0x7fffffffu) == 0x7f800000u) return overflow;
+    const float a = __uint_as_float(u & 0x7fffffffu);
+    if (a == 0.f) return sign;
+    const int min_normal = 1 - bias;
+    int e = static_cast<int>((u >> 23) & 0xff) - 127;  // f32 subnormals fall in the fp8 subnormal branch
+    unsigned exp_field, man;
+    if (e < min_normal) {
+        // q = rint(a / 2^min_normal * 2^man_bits), exact scaling by a power of two
+        const unsigned q = static_cast<unsigned>(rintf(a * __int_as_float((127 - min_normal + man_bits) << 23)));
+        exp_field = q >> man_bits;
+        man = q & manm;
+    } else {
+        unsigned q = static_cast<unsigned>(rintf(a * __int_as_float((127 - e + man_bits) << 23)));
+        if (q == (2u << man_bits)) {
+            e += 1;
+            q = 1u << man_bits;
+        }
+        exp_field = static_cast<unsigned>(e + bias);
+        man = q & manm;
+    }
+    const bool exceeded = has_inf ? (exp_field >= maxe) : (exp_field > maxe || (exp_field == maxe && man == manm));
+    if (exceeded) return overflow;
+    return static_cast<uint8_t>(sign | ((exp_field << man_bits) | man));
+}
 
 struct RescaleArgs {
     const int32_t* multiplier;  // [channels] (scale32: int32 values; scale16: int16 values widened)
@@ -91,6 +145,7 @@ __device__ __forceinline__ int32_t rescale_fast(int32_t v, int32_t m, int32_t s,
 __device__ __forceinline__ float round_to_dtype(float x, int dtype) {
     if (dtype == DT_BF16) return __bfloat162float(__float2bfloat16_rn(x));
     if (dtype == DT_FP16) return __half2float(__float2half_rn(x));
+    if (dtype == DT_FP8E4M3 || dtype == DT_FP8E5M2) return fp8_decode(fp8_encode(x, dtype), dtype);
     return x;
 }
 

@@ -96,6 +96,19 @@ float f16_to_f32(uint16_t h) {
     return sign ? -v : v;
 }
 
+// FP8 E4M3 / E5M2 byte -> float (exact; src/float8.rs).
+float fp8_to_f32(uint8_t bits, int dt) {
+    const int man_bits = dt == TB_DT_FP8E4M3 ? 3 : 2, bias = dt == TB_DT_FP8E4M3 ? 7 : 15;
+    const unsigned maxe = (1u << (7 - man_bits)) - 1u, manm = (1u << man_bits) - 1u;
+    const unsigned e = (bits >> man_bits) & maxe, m = bits & manm;
+    const bool has_inf = dt == TB_DT_FP8E5M2;
+    if (has_inf ? (e == maxe && m != 0) : (e == maxe && m == manm)) return NAN;
+    const float sign = (bits & 0x80) ? -1.f : 1.f;
+    if (has_inf && e == maxe) return sign * INFINITY;
+    const int expo = (e == 0 ? 1 : static_cast<int>(e)) - bias - man_bits;
+    return sign * std::ldexp(static_cast<float>(e == 0 ? m : ((1u << man_bits) | m)), expo);
+}
+
 struct Tensor {
     std::string name;
     int dtype = 0;
@@ -401,7 +414,8 @@ class Compiler {
                 case TB_DT_FP32: { float v; std::memcpy(&v, p, 4); t->hf.push_back(v); break; }
                 case TB_DT_FP16: { uint16_t v; std::memcpy(&v, p, 2); t->hf.push_back(f16_to_f32(v)); break; }
                 case TB_DT_BF16: { uint16_t v; std::memcpy(&v, p, 2); t->hf.push_back(bf16_to_f32(v)); break; }
-                default: t->host = false; break;  // fp8: not needed on the host
+                case TB_DT_FP8E4M3: case TB_DT_FP8E5M2: t->hf.push_back(fp8_to_f32(*p, t->dtype)); break;
+                default: t->host = false; break;
                 }
                 if (!t->host) break;
             }
@@ -647,7 +661,6 @@ class Compiler {
             raise(TB_ERR_GRAPH, "%s: multiplier and shift must have %lld elements", op, static_cast<long long>(channels));
         if (!M.host || !S.host || !IZ.host || !OZ.host)
             raise(TB_ERR_NOT_ACCELERATED, "%s: multiplier, shift and zero points must be constants for this backend", op);
-        if (in_t == TB_DT_INT48) raise(TB_ERR_NOT_ACCELERATED, "%s: INT48 input is not accelerated", op);
         s.rmult.assign(M.hi.begin(), M.hi.end());
         s.rshift.assign(S.hi.begin(), S.hi.end());
         tb_rescale_attr& r = s.rattr;
@@ -809,8 +822,6 @@ class Compiler {
             if ((!iz.hf.empty() && iz.hf[0] != 0.f) || (!oz.hf.empty() && oz.hf[0] != 0.f))
                 raise(TB_ERR_GRAPH, "%s: zero points must be zero for float data", op);
         }
-        if (dt == TB_DT_FP8E4M3 || dt == TB_DT_FP8E5M2 || (dt == TB_DT_FP16 && at == TB_DT_FP16))
-            raise(TB_ERR_NOT_ACCELERATED, "%s: types %d/%d are not accelerated", op, dt, at);
         s.pool.acc_dtype = at;
         s.kind = K_AVGPOOL;
         s.in = {x, get(o.inputs[1]), get(o.inputs[2])};
@@ -833,7 +844,8 @@ class Compiler {
         const int dt = X.dtype;
         const int decl = declared(op, o.outputs[0], out);
         if (decl && decl != dt) raise(TB_ERR_DTYPE_MISMATCH, "%s: output dtype must match input dtype", op);
-        if (!(dt == TB_DT_INT8 || dt == TB_DT_INT16 || dt == TB_DT_FP16 || dt == TB_DT_BF16 || dt == TB_DT_FP32))
+        if (!(dt == TB_DT_INT8 || dt == TB_DT_INT16 || dt == TB_DT_FP16 || dt == TB_DT_BF16 || dt == TB_DT_FP32 ||
+              dt == TB_DT_FP8E4M3 || dt == TB_DT_FP8E5M2))
             raise(TB_ERR_DTYPE_MISMATCH, "%s: unsupported dtype", op);
         s.pool.nan_mode = o.attr.nan_mode;
         s.kind = K_MAXPOOL;

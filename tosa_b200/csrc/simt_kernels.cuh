@@ -51,12 +51,25 @@ __device__ __forceinline__ void finish_int(const IntEpiDev& e, int32_t v, int ch
 __device__ __forceinline__ float load_f(const void* p, long long i, int dt) {
     if (dt == DT_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
     if (dt == DT_FP16) return __half2float(static_cast<const __half*>(p)[i]);
+    if (dt == DT_FP8E4M3 || dt == DT_FP8E5M2) return fp8_decode(static_cast<const uint8_t*>(p)[i], dt);
     return static_cast<const float*>(p)[i];
 }
 __device__ __forceinline__ void store_f(void* p, long long i, int dt, float v) {
     if (dt == DT_BF16) static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
     else if (dt == DT_FP16) static_cast<__half*>(p)[i] = __float2half_rn(v);
+    else if (dt == DT_FP8E4M3 || dt == DT_FP8E5M2) static_cast<uint8_t*>(p)[i] = fp8_encode(v, dt);
     else static_cast<float*>(p)[i] = v;
+}
+
+// One multiply-accumulate in the reference's accumulator types (src/ops/accum.rs):
+// acc_dt FP32 -> acc + a*b (product and sum each rounded to f32, no fused
+// multiply-add); FP16 / BF16 -> the product rounded to the accumulator type, then
+// the sum rounded to it (`acc += a * b`); with unrounded_product (MATMUL's
+// `acc = acc + a * b`) only the sum is rounded.
+__device__ __forceinline__ float mac_acc(float acc, float a, float b, int acc_dt, bool unrounded_product = false) {
+    if (acc_dt == DT_FP32) return __fadd_rn(acc, __fmul_rn(a, b));
+    const float p = unrounded_product ? __fmul_rn(a, b) : round_to_dtype(__fmul_rn(a, b), acc_dt);
+    return round_to_dtype(__fadd_rn(acc, p), acc_dt);
 }
 
 // ---------------------------------------------------------------------------
@@ -97,8 +110,8 @@ __global__ void conv2d_direct_int(ConvGeomDev g, const int8_t* __restrict__ x, c
 }
 
 __global__ void conv2d_direct_float(ConvGeomDev g, const void* __restrict__ x, const void* __restrict__ w,
-                                    const void* __restrict__ bias, int bias_len, int in_dt, int w_dt, int out_dt,
-                                    void* out) {
+                                    const void* __restrict__ bias, int bias_len, int in_dt, int w_dt, int acc_dt,
+                                    int out_dt, void* out) {
     const long long total = static_cast<long long>(g.n) * g.oh * g.ow * g.oc;
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -118,11 +131,130 @@ __global__ void conv2d_direct_float(ConvGeomDev g, const void* __restrict__ x, c
                 const long long xb = ((static_cast<long long>(b) * g.ih + y) * g.iw + xx) * g.ic;
                 const long long wb = ((static_cast<long long>(oc) * g.kh + ky) * g.kw + kx) * g.ic;
                 for (int c = 0; c < g.ic; ++c)
-                    acc = __fadd_rn(acc, __fmul_rn(load_f(x, xb + c, in_dt), load_f(w, wb + c, w_dt)));
+                    acc = mac_acc(acc, load_f(x, xb + c, in_dt), load_f(w, wb + c, w_dt), acc_dt);
             }
         }
         const float bv = load_f(bias, bias_len == 1 ? 0 : oc, out_dt);
         store_f(out, i, out_dt, round_to_dtype(__fadd_rn(round_to_dtype(acc, out_dt), bv), out_dt));
+    }
+}
+
+// ---------------------------------------------------------------------------
+// im2col for convolutions whose input channels are too few for the im2col TMA
+// boxes (an RGB stem): rows [N*OH*OW][kp] of the taps in weight order (ky, kx,
+// c), padded taps and the K padding filled with the input zero point, so that
+// (x - zx) is 0 there and a 1x1 tensor-core convolution over the rows yields
+// the reference's sum over valid taps. 16 bytes per thread (kp % 16 == 0).
+// ---------------------------------------------------------------------------
+__global__ void im2col_rows_i8(ConvGeomDev g, const int8_t* __restrict__ x, int k_valid, int kp, int8_t zx,
+                               int8_t* __restrict__ rows) {
+    const int chunks = kp >> 4;
+    const long long total = static_cast<long long>(g.n) * g.oh * g.ow * chunks;
+    const int tap_c = g.kw * g.ic;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int chunk = static_cast<int>(i % chunks);
+        long long r = i / chunks;
+        const int ox = static_cast<int>(r % g.ow);
+        r /= g.ow;
+        const int oy = static_cast<int>(r % g.oh);
+        const int b = static_cast<int>(r / g.oh);
+        int k = chunk << 4;
+        int ky = k / tap_c, rem = k - ky * tap_c, kx = rem / g.ic, c = rem - kx * g.ic;
+        const int8_t* xb = x + static_cast<long long>(b) * g.ih * g.iw * g.ic;
+        uint32_t w4[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            uint32_t word = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                int8_t v = zx;
+                if (k < k_valid) {
+                    const int y = oy * g.sh + ky * g.dh - g.pad_t, xx = ox * g.sw + kx * g.dw - g.pad_l;
+                    if (y >= 0 && y < g.ih && xx >= 0 && xx < g.iw) v = xb[(static_cast<long long>(y) * g.iw + xx) * g.ic + c];
+                }
+                word |= static_cast<uint32_t>(static_cast<uint8_t>(v)) << (8 * j);
+                ++k;
+                if (++c == g.ic) {
+                    c = 0;
+                    if (++kx == g.kw) { kx = 0; ++ky; }
+                }
+            }
+            w4[q] = word;
+        }
+        reinterpret_cast<uint4*>(rows)[i] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+    }
+}
+
+// Weights [OC][K] -> [OC][kp], zero-padded.
+__global__ void pad_weight_rows_i8(int oc, int k, int kp, const int8_t* __restrict__ w, int8_t* __restrict__ out) {
+    const long long total = static_cast<long long>(oc) * kp;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int col = static_cast<int>(i % kp);
+        const long long row = i / kp;
+        out[i] = col < k ? w[row * k + col] : 0;
+    }
+}
+
+// INT16 x INT8 -> INT48 (AccI64, src/ops/accum.rs:43-56): int64 accumulation,
+// bias added with wrap-around, then clamped to 48 bits (src/ops/conv.rs:466-470).
+// INT48 values are stored as int64. depthwise: weight [KH,KW,C,M].
+__device__ __forceinline__ int64_t clamp48(int64_t v) {
+    const int64_t lo = -(1ll << 47), hi = (1ll << 47) - 1;
+    return v < lo ? lo : (v > hi ? hi : v);
+}
+
+__global__ void conv2d_direct_i48(ConvGeomDev g, const int16_t* __restrict__ x, const int8_t* __restrict__ w,
+                                  const int64_t* __restrict__ bias, int bias_len, int32_t zx, int32_t zw,
+                                  int depthwise, int64_t* __restrict__ out) {
+    const long long total = static_cast<long long>(g.n) * g.oh * g.ow * g.oc;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int oc = static_cast<int>(i % g.oc);
+        long long r = i / g.oc;
+        const int ox = static_cast<int>(r % g.ow);
+        r /= g.ow;
+        const int oy = static_cast<int>(r % g.oh);
+        const int b = static_cast<int>(r / g.oh);
+        uint64_t acc = 0;
+        for (int ky = 0; ky < g.kh; ++ky) {
+            const int y = oy * g.sh + ky * g.dh - g.pad_t;
+            if (y < 0 || y >= g.ih) continue;
+            for (int kx = 0; kx < g.kw; ++kx) {
+                const int xx = ox * g.sw + kx * g.dw - g.pad_l;
+                if (xx < 0 || xx >= g.iw) continue;
+                const int16_t* xp = x + ((static_cast<long long>(b) * g.ih + y) * g.iw + xx) * g.ic;
+                if (depthwise) {
+                    const int c = oc / g.m, mm = oc % g.m;
+                    const int64_t wv = w[((ky * g.kw + kx) * g.ic + c) * g.m + mm] - zw;
+                    acc += static_cast<uint64_t>((static_cast<int64_t>(xp[c]) - zx) * wv);
+                } else {
+                    const int8_t* wp = w + ((static_cast<long long>(oc) * g.kh + ky) * g.kw + kx) * g.ic;
+                    for (int c = 0; c < g.ic; ++c)
+                        acc += static_cast<uint64_t>((static_cast<int64_t>(xp[c]) - zx) *
+                                                     (static_cast<int64_t>(wp[c]) - zw));
+                }
+            }
+        }
+        acc += static_cast<uint64_t>(bias[bias_len == 1 ? 0 : oc]);
+        out[i] = clamp48(static_cast<int64_t>(acc));
+    }
+}
+
+__global__ void matmul_direct_i48(int n, int h, int c, int w, const int16_t* __restrict__ a,
+                                  const int16_t* __restrict__ bm, int64_t* __restrict__ out) {
+    const long long total = static_cast<long long>(n) * h * w;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int col = static_cast<int>(i % w);
+        const long long rowi = i / w;
+        const int bn = static_cast<int>(rowi / h);
+        uint64_t acc = 0;
+        for (int k = 0; k < c; ++k)
+            acc += static_cast<uint64_t>(static_cast<int64_t>(a[rowi * c + k]) *
+                                         bm[(static_cast<long long>(bn) * c + k) * w + col]);
+        out[i] = clamp48(static_cast<int64_t>(acc));
     }
 }
 
@@ -225,7 +357,8 @@ __global__ void depthwise_int_generic(ConvGeomDev g, const int8_t* __restrict__ 
 }
 
 __global__ void depthwise_float(ConvGeomDev g, const void* __restrict__ x, const void* __restrict__ w,
-                                const void* __restrict__ bias, int bias_len, int in_dt, int out_dt, void* out) {
+                                const void* __restrict__ bias, int bias_len, int in_dt, int w_dt, int acc_dt,
+                                int out_dt, void* out) {
     const int cm = g.ic * g.m;
     const long long total = static_cast<long long>(g.n) * g.oh * g.ow * cm;
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
@@ -245,8 +378,8 @@ __global__ void depthwise_float(ConvGeomDev g, const void* __restrict__ x, const
                 const int xx = ox * g.sw - g.pad_l + kx * g.dw;
                 if (xx < 0 || xx >= g.iw) continue;
                 const float xv = load_f(x, ((static_cast<long long>(b) * g.ih + y) * g.iw + xx) * g.ic + c, in_dt);
-                const float wv = load_f(w, ((ky * g.kw + kx) * g.ic + c) * g.m + mm, in_dt);
-                acc = __fadd_rn(acc, __fmul_rn(xv, wv));
+                const float wv = load_f(w, ((ky * g.kw + kx) * g.ic + c) * g.m + mm, w_dt);
+                acc = mac_acc(acc, xv, wv, acc_dt);
             }
         }
         const float bv = load_f(bias, bias_len == 1 ? 0 : oc, out_dt);
@@ -278,7 +411,7 @@ __global__ void matmul_direct_int(int n, int h, int c, int w, const int8_t* __re
 }
 
 __global__ void matmul_direct_float(int n, int h, int c, int w, const void* __restrict__ a, const void* __restrict__ bm,
-                                    int in_dt, int out_dt, void* out) {
+                                    int in_dt, int b_dt, int out_dt, void* out) {
     const long long total = static_cast<long long>(n) * h * w;
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -286,9 +419,10 @@ __global__ void matmul_direct_float(int n, int h, int c, int w, const void* __re
         const long long rowi = i / w;
         const int bn = static_cast<int>(rowi / h);
         float acc = 0.f;
+        // operands are first converted to the output type (exact for every admitted pair)
         for (int k = 0; k < c; ++k)
-            acc = __fadd_rn(acc, __fmul_rn(load_f(a, rowi * c + k, in_dt),
-                                           load_f(bm, (static_cast<long long>(bn) * c + k) * w + col, in_dt)));
+            acc = mac_acc(acc, load_f(a, rowi * c + k, in_dt),
+                          load_f(bm, (static_cast<long long>(bn) * c + k) * w + col, b_dt), out_dt, true);
         store_f(out, i, out_dt, acc);
     }
 }

@@ -213,6 +213,17 @@ __device__ __forceinline__ float nan_pick(float a, float b, int mode) {
     if (mode == 2) return isnan(a) ? b : a;
     return __int_as_float(0x7fc00000);
 }
+// The most negative finite value of a float type (the reference's float_lowest).
+__device__ __forceinline__ float float_lowest(int dt) {
+    switch (dt) {
+    case DT_FP16: return -65504.f;
+    case DT_BF16: return __uint_as_float(0xff7f0000u);
+    case DT_FP8E4M3: return -448.f;
+    case DT_FP8E5M2: return -57344.f;
+    default: return __uint_as_float(0xff7fffffu);
+    }
+}
+
 __device__ __forceinline__ float nan_max(float a, float b, int mode) {
     if (isnan(a) || isnan(b)) return nan_pick(a, b, mode);
     return a >= b ? a : b;
@@ -233,7 +244,7 @@ __global__ void max_pool_float(PoolGeomDev g, const void* __restrict__ x, int dt
         const int oy = static_cast<int>(r % g.oh);
         const int b = static_cast<int>(r / g.oh);
         const int iy0 = oy * g.sy - g.pad_t, ix0 = ox * g.sx - g.pad_l;
-        float m = nan_mode == 2 ? __int_as_float(0x7fc00000) : -INFINITY;
+        float m = nan_mode == 2 ? __int_as_float(0x7fc00000) : float_lowest(dt);
         for (int ky = 0; ky < g.ky; ++ky) {
             const int y = iy0 + ky;
             if (y < 0 || y >= g.ih) continue;
@@ -258,7 +269,7 @@ __global__ void rescale_elementwise(const void* __restrict__ in, int in_dt, int 
     uint32_t lerr = 0;
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < count;
          i += static_cast<long long>(gridDim.x) * blockDim.x) {
-        int64_t v = load_int(in, i, in_dt);
+        int64_t v = in_dt == DT_INT48 ? static_cast<const int64_t*>(in)[i] : load_int(in, i, in_dt);
         if (in_unsigned) v &= in_dt == DT_INT8 ? 0xff : 0xffff;
         const int64_t x = v - in_zp_ext;
         const int ch = rs.per_channel ? static_cast<int>(i % channels) : 0;
