@@ -60,6 +60,9 @@ MATMUL_SHAPES = [
     (3, 130, 256, 64, 3, 0),       # a_zp only
     (1, 64, 1024, 384, 0, -8),     # b_zp only, N spans 2 tiles
     (2, 257, 528, 272, -128, 127), # extreme zero points
+    # B rows not 16-byte multiples: copied into padded rows, then tensor cores
+    (1, 64, 2048, 1000, 5, -3),    # a classifier head: 1000 classes
+    (2, 96, 128, 20, -7, 0),
 ]
 
 
@@ -90,6 +93,22 @@ def test_matmul_int8_fused_rescale(ctx, rounding, per_channel):
     rc, exp = H.oracle_rescale(acc, L.DT_INT32, L.DT_INT8, mult, shift, 0, 5, 1, rounding, int(per_channel))
     assert rc == 0
     assert np.array_equal(got.reshape(-1).astype(np.int64), exp)
+
+
+def test_matmul_int8_padded_b_fused_rescale(ctx):
+    """The padded-B path with a fused per-channel RESCALE to int8 (rows of 1000
+    bytes: the epilogue stores unaligned chunks element by element)."""
+    rng = np.random.default_rng(99)
+    n, h, c, w = 1, 128, 256, 1000
+    a = rng.integers(-128, 128, (n, h, c), dtype=np.int64)
+    b = rng.integers(-128, 128, (n, c, w), dtype=np.int64)
+    mult = rng.integers(1 << 30, (1 << 31) - 1, w)
+    shift = rng.integers(32, 40, w)
+    attr = L.rescale_attr(mult, shift, rounding=L.ROUND_DOUBLE, output_zp=-3, out_dtype=L.DT_INT8)
+    got = run_matmul(ctx, a, b, 4, -2, rescale=attr)
+    acc = H.oracle_matmul_int(a, b, 4, -2)
+    rc, exp = H.oracle_rescale(acc, L.DT_INT32, L.DT_INT8, mult, shift, 0, -3, 1, L.ROUND_DOUBLE, 1)
+    assert rc == 0 and np.array_equal(got.reshape(-1).astype(np.int64), exp)
 
 
 def test_matmul_int8_rescale_small_shift_checks(ctx):
@@ -319,3 +338,54 @@ def test_depthwise_int8_fused_rescale_clamp(ctx):
     rc, r = H.oracle_rescale(acc, L.DT_INT32, L.DT_INT8, mult, shift, 0, 3, 1, L.ROUND_DOUBLE, 1)
     assert rc == 0
     assert np.array_equal(got.reshape(-1).astype(np.int64), np.clip(r, 0, 127))
+
+
+POOL_CASES = [
+    # (n, ih, iw, c, kernel, stride, pad)
+    (2, 17, 19, 32, (3, 3), (2, 2), (1, 1, 1, 1)),   # 16 channels per thread, borders
+    (1, 56, 56, 64, (2, 2), (2, 2), (0, 0, 0, 0)),   # a strided 2x2 shortcut pool
+    (2, 7, 7, 48, (7, 7), (1, 1), (0, 0, 0, 0)),     # global pool
+    (1, 9, 10, 12, (3, 2), (1, 2), (1, 0, 0, 0)),    # 4 channels per thread
+    (1, 6, 5, 7, (2, 3), (2, 1), (0, 0, 1, 1)),      # scalar
+]
+
+
+def _pool_desc(n, ih, iw, c, kernel, stride, pad, dtype, zi=0, zo=0):
+    d = L.Pool2dDesc()
+    d.n, d.ih, d.iw, d.c = n, ih, iw, c
+    d.kernel[0], d.kernel[1] = kernel
+    d.stride[0], d.stride[1] = stride
+    for i in range(4):
+        d.pad[i] = pad[i]
+    d.dtype, d.acc_dtype, d.input_zp, d.output_zp, d.nan_mode = dtype, L.DT_INT32, zi, zo, L.NAN_PROPAGATE
+    return d
+
+
+@pytest.mark.parametrize("case", POOL_CASES)
+def test_pool2d_int8(ctx, case):
+    """AVG_POOL2D (zero points, reciprocal_scale rounding) and MAX_POOL2D on int8
+    NHWC against the oracle, bit for bit."""
+    import ctypes as C
+    from oracle import oracle as O
+    n, ih, iw, c, kernel, stride, pad = case
+    rng = np.random.default_rng(ih * 7 + c)
+    x = rng.integers(-128, 128, (n, ih, iw, c), dtype=np.int8)
+    g = H.pool_geom(x.shape, kernel, stride, pad)
+    tx = torch.from_numpy(x).cuda()
+    out = torch.empty((n, g.oh, g.ow, c), dtype=torch.int8, device="cuda")
+    xi = np.ascontiguousarray(x, np.int64)
+    p = lambda a: a.ctypes.data_as(C.c_void_p)  # noqa: E731
+    for zi, zo in ((0, 0), (-7, 5)):
+        d = _pool_desc(n, ih, iw, c, kernel, stride, pad, L.DT_INT8, zi, zo)
+        L.check(L.load().tb_avg_pool2d(ctx.h, d, L.ptr(tx), L.ptr(out), L.stream_ptr()))
+        ctx.synchronize()
+        exp = np.zeros(out.numel(), dtype=np.int64)
+        assert O.lib().orc_avg_pool_int(C.byref(g), p(xi), C.c_int(L.DT_INT8), C.c_int64(zi), C.c_int64(zo),
+                                        p(exp)) == 0
+        assert np.array_equal(out.cpu().numpy().reshape(-1).astype(np.int64), exp)
+    d = _pool_desc(n, ih, iw, c, kernel, stride, pad, L.DT_INT8)
+    L.check(L.load().tb_max_pool2d(ctx.h, d, L.ptr(tx), L.ptr(out), L.stream_ptr()))
+    ctx.synchronize()
+    exp = np.zeros(out.numel(), dtype=np.int64)
+    O.lib().orc_max_pool_int(C.byref(g), p(xi), C.c_int(L.DT_INT8), p(exp))
+    assert np.array_equal(out.cpu().numpy().reshape(-1).astype(np.int64), exp)

@@ -403,8 +403,13 @@ tb_status matmul_validate(const tb_matmul_desc* d, bool has_rescale, int* path, 
     // tensor cores: int8 -> int32, and BF16/F16 pairs with an FP32 result; everything else runs
     // the direct kernels in the reference's accumulation order (path 2 int8, 3 float, 4 int16)
     const bool tc_float = at == bt && (at == TB_DT_BF16 || at == TB_DT_FP16) && ot == TB_DT_FP32;
+    // int8 with A rows TMA-addressable but B rows not (e.g. 1000 classes): B is copied
+    // into column-padded rows each run and the tensor cores take it (path 5)
+    // (w % 4 == 0: the in-kernel column sums of B read 4-byte words of its rows)
+    const bool pad_b = int8 && !tma_ok && d->c % 16 == 0 && d->c > 0 && d->h > 0 && d->n > 0 && d->w >= 16 &&
+                       d->w % 4 == 0 && static_cast<long long>(d->h) * d->n >= 64;
     if (int16) *path = 4;
-    else if (int8) *path = tma_ok ? 0 : 2;
+    else if (int8) *path = tma_ok ? 0 : (pad_b ? 5 : 2);
     else *path = tma_ok && tc_float ? 1 : 3;
     *bn = d->w <= 128 ? 128 : 256;
     return TB_OK;
@@ -428,7 +433,12 @@ extern "C" TB_API tb_status tb_matmul_plan_create(tb_context* ctx, const tb_matm
         tb_status s = make_rescale_plan(ctx, rescale, TB_DT_INT32, d->w, &p->rs);
         if (s != TB_OK) { delete p; return s; }
     }
-    if (p->path == 0 && d->a_zp != 0) {
+    if (p->path == 5) {
+        p->wp = (d->w + 15) / 16 * 16;
+        cudaError_t ce = cudaMalloc(&p->d_bpad, static_cast<size_t>(d->n) * d->c * p->wp);
+        if (ce != cudaSuccess) { free_rescale_plan(&p->rs); delete p; return fail(TB_ERR_CUDA, "B padding alloc failed"); }
+    }
+    if ((p->path == 0 || p->path == 5) && d->a_zp != 0) {
         // padded by one tile: the epilogue reads whole 16-column chunks without clamping
         cudaError_t ce = cudaMalloc(&p->d_colterm, sizeof(int32_t) * (static_cast<size_t>(d->n) * d->w + 256));
         if (ce == cudaSuccess) ce = cudaMalloc(&p->d_counter, sizeof(unsigned int));
@@ -447,7 +457,13 @@ extern "C" TB_API tb_status tb_matmul_plan_run(tb_matmul_plan* p, const void* a,
     const tb_matmul_desc& d = p->d;
     const long long total = static_cast<long long>(d.n) * d.h * d.w;
     if (total == 0) return TB_OK;
-    if (p->path >= 2 || !aligned16(a) || !aligned16(b)) {
+    const void* b_tma = b;
+    if (p->path == 5 && aligned16(a)) {
+        pad_weight_rows_i8<<<grid_for(ctx, static_cast<long long>(d.n) * d.c * p->wp), 256, 0, st>>>(
+            d.n * d.c, d.w, p->wp, static_cast<const int8_t*>(b), p->d_bpad);
+        TB_LAUNCHED(ctx);
+        b_tma = p->d_bpad;
+    } else if (p->path >= 2 || !aligned16(a) || !aligned16(b)) {
         if (d.a_dtype == TB_DT_INT8) {
             matmul_direct_int<<<grid_for(ctx, total), 256, 0, st>>>(d.n, d.h, d.c, d.w, static_cast<const int8_t*>(a),
                                                                     static_cast<const int8_t*>(b), d.a_zp, d.b_zp,
@@ -463,7 +479,8 @@ extern "C" TB_API tb_status tb_matmul_plan_run(tb_matmul_plan* p, const void* a,
         TB_LAUNCHED(ctx);
         return TB_OK;
     }
-    const int e = p->path == 0 ? 1 : 2;
+    const int e = p->path == 1 ? 2 : 1;
+    const int wt = p->path == 5 ? p->wp : d.w;  // B row length of the tensor map
     if (a != p->a_cached) {
         const uint64_t dims[3] = {static_cast<uint64_t>(d.c), static_cast<uint64_t>(d.h), static_cast<uint64_t>(d.n)};
         const uint64_t str[2] = {static_cast<uint64_t>(d.c) * e, static_cast<uint64_t>(d.c) * d.h * e};
@@ -471,12 +488,12 @@ extern "C" TB_API tb_status tb_matmul_plan_run(tb_matmul_plan* p, const void* a,
         TB_TRY(encode_tiled(&p->tmA, tmap_dtype(d.a_dtype), 3, a, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B));
         p->a_cached = a;
     }
-    if (b != p->b_cached) {
-        const uint64_t dims[3] = {static_cast<uint64_t>(d.w), static_cast<uint64_t>(d.c), static_cast<uint64_t>(d.n)};
-        const uint64_t str[2] = {static_cast<uint64_t>(d.w) * e, static_cast<uint64_t>(d.w) * d.c * e};
+    if (b_tma != p->b_cached) {
+        const uint64_t dims[3] = {static_cast<uint64_t>(wt), static_cast<uint64_t>(d.c), static_cast<uint64_t>(d.n)};
+        const uint64_t str[2] = {static_cast<uint64_t>(wt) * e, static_cast<uint64_t>(wt) * d.c * e};
         const uint32_t box[3] = {static_cast<uint32_t>(128 / e), static_cast<uint32_t>(128 / e), 1};
-        TB_TRY(encode_tiled(&p->tmB, tmap_dtype(d.b_dtype), 3, b, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B));
-        p->b_cached = b;
+        TB_TRY(encode_tiled(&p->tmB, tmap_dtype(d.b_dtype), 3, b_tma, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B));
+        p->b_cached = b_tma;
     }
     GemmParams gp{};
     gp.M = d.h;
@@ -489,7 +506,7 @@ extern "C" TB_API tb_status tb_matmul_plan_run(tb_matmul_plan* p, const void* a,
     gp.out_batch_stride = static_cast<long long>(d.h) * d.w;
     gp.ldo = d.w;
     GemmEpilogue& ep = gp.epi;
-    if (p->path == 0) {
+    if (p->path == 0 || p->path == 5) {
         if (d.a_zp != 0) {
             // colterm = -a_zp * colsum(B) + c * a_zp * b_zp, reduced inside the GEMM by the epilogue warps
             // during the first main loop (cooperative launch; see ColsumJob).
@@ -538,6 +555,7 @@ extern "C" TB_API void tb_matmul_plan_destroy(tb_matmul_plan* p) {
     free_rescale_plan(&p->rs);
     if (p->d_colterm) cudaFree(p->d_colterm);
     if (p->d_counter) cudaFree(p->d_counter);
+    if (p->d_bpad) cudaFree(p->d_bpad);
     delete p;
 }
 
@@ -1136,7 +1154,22 @@ extern "C" TB_API tb_status tb_avg_pool2d(tb_context* ctx, const tb_pool2d_desc*
     if (total == 0) return TB_OK;
     if (!input || !out) return fail(TB_ERR_INVALID_ARGUMENT, "null argument");
     cudaStream_t st = static_cast<cudaStream_t>(stream_);
-    if (dt == TB_DT_INT8 && g.c % 4 == 0 && aligned16(input))
+    if (dt == TB_DT_INT8 && g.c % 16 == 0 && aligned16(input) && aligned16(out) && total / 16 < (1ll << 31)) {
+        static RecipTable table = [] {
+            RecipTable t{};
+            for (int c = 1; c <= 64; ++c) {  // reciprocal_scale (src/ops/quant.rs:6-11)
+                const uint32_t v = static_cast<uint32_t>(c) - 1u;
+                const int k = v == 0 ? 0 : 32 - __builtin_clz(v);
+                const long long numerator = ((1ll << 30) + 1) << k;
+                t.m[c] = static_cast<int32_t>(numerator / c);
+                t.s[c] = 30 + k;
+            }
+            return t;
+        }();
+        avg_pool_i8_vec16<<<grid_for(ctx, total / 16), 256, 0, st>>>(g, static_cast<const int8_t*>(input),
+                                                                    d->input_zp, d->output_zp, table,
+                                                                    static_cast<int8_t*>(out), ctx->dev_err);
+    } else if (dt == TB_DT_INT8 && g.c % 4 == 0 && aligned16(input))
         avg_pool_i8_vec4<<<grid_for(ctx, total / 4), 256, 0, st>>>(g, static_cast<const int8_t*>(input), d->input_zp,
                                                                   d->output_zp, static_cast<int8_t*>(out), ctx->dev_err);
     else if (dt == TB_DT_INT8 || dt == TB_DT_INT16)
@@ -1162,7 +1195,10 @@ extern "C" TB_API tb_status tb_max_pool2d(tb_context* ctx, const tb_pool2d_desc*
         return fail(TB_ERR_DTYPE_MISMATCH, "MAX_POOL2D: unsupported dtype %d", dt);
     if (total == 0) return TB_OK;
     if (!input || !out) return fail(TB_ERR_INVALID_ARGUMENT, "null argument");
-    if (dt == TB_DT_INT8 && g.c % 4 == 0 && aligned16(input))
+    if (dt == TB_DT_INT8 && g.c % 16 == 0 && aligned16(input) && aligned16(out) && total / 16 < (1ll << 31))
+        max_pool_i8_vec16<<<grid_for(ctx, total / 16), 256, 0, st>>>(g, static_cast<const int8_t*>(input),
+                                                                    static_cast<int8_t*>(out));
+    else if (dt == TB_DT_INT8 && g.c % 4 == 0 && aligned16(input))
         max_pool_i8_vec4<<<grid_for(ctx, total / 4), 256, 0, st>>>(g, static_cast<const int8_t*>(input),
                                                                   static_cast<int8_t*>(out));
     else if (dt == TB_DT_INT8 || dt == TB_DT_INT16)

@@ -12,6 +12,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "internal.hpp"
 #include "quant.cuh"
 
@@ -180,7 +182,89 @@ __global__ void residual_chain(const void* __restrict__ a, int a_dt, int a_uns, 
     if (lerr) atomicOr(err, lerr);
 }
 
+__device__ __forceinline__ int32_t sext8(uint32_t word, int j) {
+    return static_cast<int32_t>(static_cast<int8_t>(static_cast<uint8_t>(word >> (8 * j))));
+}
+
+__device__ __forceinline__ int32_t small_rescale(int32_t x, int32_t m, int s, long long rpos, long long rneg) {
+    return static_cast<int32_t>((static_cast<long long>(x) * m + (x >= 0 ? rpos : rneg)) >> s);
+}
+
+// Residual chain, int8 in and out, 16 elements per thread. The two input
+// RESCALEs use the error-free constants of ResidualFast; the output RESCALE
+// uses the packed fast-path constants (every shift >= 32, multiplier >= 0:
+// r = ((v * m + R) >> 32) >> (s - 32) [+ zp], clamped), as in the GEMM epilogue.
+template <bool PC, bool DBL>
+__global__ void residual_fast_i8(const uint4* __restrict__ a, const uint4* __restrict__ b, ResidualFast f,
+                                 const int4* __restrict__ rq, int32_t lo, int32_t hi, int32_t add_zp, long long n16,
+                                 int channels, uint4* __restrict__ out) {
+    int4 P = __ldg(rq), Q = __ldg(rq + 1);
+    for (long long q = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; q < n16;
+         q += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const uint4 av = __ldg(a + q), bv = __ldg(b + q);
+        const uint32_t aw[4] = {av.x, av.y, av.z, av.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
+        const int c0 = PC ? static_cast<int>((static_cast<unsigned long long>(q) << 4) % static_cast<unsigned>(channels))
+                          : 0;
+        uint32_t ow[4];
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            uint32_t word = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int32_t xa = sext8(aw[w], j) - f.za, xb = sext8(bw[w], j) - f.zb;
+                const int32_t sum = static_cast<int32_t>(
+                    static_cast<uint32_t>(small_rescale(xa, f.ma, f.sa, f.ra_pos, f.ra_neg)) +
+                    static_cast<uint32_t>(small_rescale(xb, f.mb, f.sb, f.rb_pos, f.rb_neg)));
+                if (PC) {
+                    P = __ldg(rq + 2 * (c0 + 4 * w + j));
+                    if (DBL) Q = __ldg(rq + 2 * (c0 + 4 * w + j) + 1);
+                }
+                const bool neg = DBL && sum < 0;
+                const long long R = static_cast<long long>(
+                    (static_cast<unsigned long long>(static_cast<uint32_t>(neg ? Q.y : P.w)) << 32) |
+                    static_cast<uint32_t>(neg ? Q.x : P.z));
+                const int32_t hi32 = static_cast<int32_t>(
+                    static_cast<unsigned long long>(static_cast<long long>(sum) * P.x + R) >> 32);
+                int32_t r = (hi32 >> P.y) + add_zp;
+                r = min(max(r, lo), hi);
+                word |= static_cast<uint32_t>(static_cast<uint8_t>(r)) << (8 * j);
+            }
+            ow[w] = word;
+        }
+        out[q] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+    }
+}
+
 }  // namespace
+
+void residual_fast_constants(const tb_rescale_attr& a, int a_dt, const tb_rescale_attr& b, int b_dt, ResidualFast* f) {
+    f->ok = false;
+    auto one = [](const tb_rescale_attr& r, int dt, int32_t* m, int32_t* z, int32_t* s, long long* rp,
+                  long long* rn) {
+        if (dt != TB_DT_INT8 || !r.scale32 || r.per_channel || r.channels != 1 || r.input_unsigned ||
+            r.output_unsigned || r.out_dtype != TB_DT_INT32 || r.rounding_mode == TB_ROUND_INEXACT || r.output_zp != 0)
+            return false;
+        const long long mm = r.multiplier[0];
+        const int ss = r.shift[0];
+        if (mm < 0 || ss < 2 || ss > 62) return false;
+        const long long zp = r.input_zp;
+        const long long xmax = std::max(127 - zp, 128 + zp);  // |x - zp| over int8
+        if (xmax >= (1ll << (ss - 1))) return false;          // apply_scale_32's input range
+        const long long half = 1ll << (ss - 1);
+        const long long dr = (r.rounding_mode == TB_ROUND_DOUBLE && ss > 31) ? (1ll << 30) : 0;
+        // every result in int32: |(x * m + R) >> s| for |x| <= xmax
+        const long double big = static_cast<long double>(xmax) * mm + half + dr;
+        if (big / static_cast<long double>(1ll << ss) >= 2147483647.0L - 1) return false;
+        *m = static_cast<int32_t>(mm);
+        *z = static_cast<int32_t>(zp);
+        *s = ss;
+        *rp = half + dr;
+        *rn = half - dr;
+        return true;
+    };
+    f->ok = one(a, a_dt, &f->ma, &f->za, &f->sa, &f->ra_pos, &f->ra_neg) &&
+            one(b, b_dt, &f->mb, &f->zb, &f->sb, &f->rb_pos, &f->rb_neg);
+}
 
 tb_status launch_transpose(tb_context* ctx, const void* in, void* out, int elem, long long total, int rank,
                            const NdMap& map, cudaStream_t st) {
@@ -213,8 +297,29 @@ tb_status launch_rescale(tb_context* ctx, const RescalePlan& r, int in_dtype, in
 
 tb_status launch_residual(tb_context* ctx, const void* a, int a_dt, int a_uns, int32_t za, const RescalePlan& ra,
                           const void* b, int b_dt, int b_uns, int32_t zb, const RescalePlan& rb,
-                          const RescalePlan& ro, long long count, int channels, void* out, cudaStream_t st) {
+                          const RescalePlan& ro, const ResidualFast& fast, long long count, int channels, void* out,
+                          cudaStream_t st) {
     if (count == 0) return TB_OK;
+    if (fast.ok && ro.fast && ro.out_dtype == TB_DT_INT8 && count % 16 == 0 && (!ro.per_channel || channels % 16 == 0) &&
+        aligned16(a) && aligned16(b) && aligned16(out)) {
+        const long long n16 = count / 16;
+        const int32_t add_zp = ro.zp_folded ? 0 : ro.out_zp;
+        const int4* rq = reinterpret_cast<const int4*>(ro.d_rq);
+        const int grid = grid_for(ctx, n16);
+        const bool dbl = ro.rounding == TB_ROUND_DOUBLE;
+        auto A = static_cast<const uint4*>(a);
+        auto B = static_cast<const uint4*>(b);
+        auto O = static_cast<uint4*>(out);
+        if (ro.per_channel) {
+            if (dbl) residual_fast_i8<true, true><<<grid, 256, 0, st>>>(A, B, fast, rq, ro.lo, ro.hi, add_zp, n16, channels, O);
+            else residual_fast_i8<true, false><<<grid, 256, 0, st>>>(A, B, fast, rq, ro.lo, ro.hi, add_zp, n16, channels, O);
+        } else {
+            if (dbl) residual_fast_i8<false, true><<<grid, 256, 0, st>>>(A, B, fast, rq, ro.lo, ro.hi, add_zp, n16, channels, O);
+            else residual_fast_i8<false, false><<<grid, 256, 0, st>>>(A, B, fast, rq, ro.lo, ro.hi, add_zp, n16, channels, O);
+        }
+        TB_LAUNCHED(ctx);
+        return TB_OK;
+    }
     const bool vec4 = a_dt == TB_DT_INT8 && b_dt == TB_DT_INT8 && count % 4 == 0 && channels % 4 == 0 &&
                       aligned16(a) && aligned16(b) && aligned16(out);
     const long long work = vec4 ? count / 4 : count;

@@ -116,9 +116,21 @@ tb_status launch_add_broadcast(tb_context* ctx, int dtype, const void* a, const 
                                const NdMap& map, void* out, cudaStream_t st);
 tb_status launch_rescale(tb_context* ctx, const RescalePlan& r, int in_dtype, int in_uns, int32_t izp, const void* in,
                          long long count, int channels, void* out, cudaStream_t st);
+// Per-tensor constants of the residual chain's two input RESCALEs when neither can
+// raise an error (int8 inputs, scale32 single/double rounding, every |x - zp| below
+// 2^(shift-1) and every result inside int32): r = (x * m + R) >> shift, R chosen by
+// the sign of x. `ok` false: the general kernel runs.
+struct ResidualFast {
+    bool ok = false;
+    int32_t ma = 0, za = 0, sa = 0, mb = 0, zb = 0, sb = 0;
+    long long ra_pos = 0, ra_neg = 0, rb_pos = 0, rb_neg = 0;
+};
+// Fills `f` from host copies of the two RESCALE attributes (int8 inputs, int32 outputs).
+void residual_fast_constants(const tb_rescale_attr& a, int a_dt, const tb_rescale_attr& b, int b_dt, ResidualFast* f);
 tb_status launch_residual(tb_context* ctx, const void* a, int a_dt, int a_uns, int32_t za, const RescalePlan& ra,
                           const void* b, int b_dt, int b_uns, int32_t zb, const RescalePlan& rb,
-                          const RescalePlan& ro, long long count, int channels, void* out, cudaStream_t st);
+                          const RescalePlan& ro, const ResidualFast& fast, long long count, int channels, void* out,
+                          cudaStream_t st);
 
 // MATMUL static checks (src/ops/matmul.rs:112-153) and path choice:
 // path 0 tensor-core int8, 1 tensor-core f16/bf16, 2 direct int8, 3 direct float.
@@ -130,13 +142,15 @@ tb_status matmul_validate(const tb_matmul_desc* d, bool has_rescale, int* path, 
 struct tb_matmul_plan {
     tb_context* ctx = nullptr;
     tb_matmul_desc d{};
-    int path = 0;  // 0 TC int8, 1 TC f16/bf16, 2 direct int, 3 direct float
+    int path = 0;  // 0 TC int8, 1 TC f16/bf16, 2 direct int, 3 direct float, 4 direct int16, 5 TC int8, padded B
     tb::RescalePlan rs;
     int bn = 256;
     int32_t* d_colterm = nullptr;  // [n][w] (+ one tile of padding) when a_zp != 0
     unsigned int* d_counter = nullptr;  // column-sum units finished, grows by `units` per run
     unsigned int epoch = 0;
     bool replayable = false;  // reset the column-sum counter on every run (CUDA-graph replay)
+    int wp = 0;                // path 5: padded B row length
+    int8_t* d_bpad = nullptr;  // path 5: [n][c][wp] copy of B
     const void* a_cached = nullptr;
     const void* b_cached = nullptr;
     CUtensorMap tmA, tmB;

@@ -151,6 +151,7 @@ struct Step {
     bool has_rescale = false;
     // standalone RESCALE / residual chain
     RescalePlan rs, ra, rb;
+    ResidualFast rfast;
     int in_dtype = 0, in_uns = 0, b_dtype = 0, b_uns = 0;
     int32_t izp = 0, bzp = 0;
     int channels = 1;
@@ -1152,6 +1153,7 @@ tb_status do_compile(tb_graph* G) {
             st = make_rescale_plan(ctx, &a.rattr, a.in_dtype, a.channels, &s.ra);
             if (st == TB_OK) st = make_rescale_plan(ctx, &bb.rattr, bb.in_dtype, bb.channels, &s.rb);
             if (st == TB_OK) st = make_rescale_plan(ctx, &s.rattr, TB_DT_INT32, s.channels, &s.rs);
+            residual_fast_constants(a.rattr, a.in_dtype, bb.rattr, bb.in_dtype, &s.rfast);
             break;
         }
         default: break;
@@ -1205,7 +1207,7 @@ tb_status exec_step(tb_graph* G, Step& s, cudaStream_t st) {
         const Tensor& a = G->tensors[ra.in[0]];
         const Tensor& b = G->tensors[rb.in[0]];
         return launch_residual(ctx, a.dev, s.in_dtype, s.in_uns, s.izp, s.ra, b.dev, s.b_dtype, s.b_uns, s.bzp, s.rb,
-                               s.rs, a.count, s.channels, dev(s.exec_out), st);
+                               s.rs, s.rfast, a.count, s.channels, dev(s.exec_out), st);
     }
     case K_CLAMP: {
         const Tensor& x = G->tensors[s.in[0]];

@@ -122,6 +122,96 @@ __global__ void avg_pool_i8_vec4(PoolGeomDev g, const int8_t* __restrict__ x, in
     if (lerr) atomicOr(err, lerr);
 }
 
+// reciprocal_scale of every window size up to 64, computed once on the host.
+struct RecipTable {
+    int32_t m[65];
+    int32_t s[65];
+};
+
+// int8, C % 16 == 0, fewer than 2^31 output vectors: sixteen channels per thread
+// (16-byte loads), 32-bit index arithmetic, the reciprocal from the table.
+__global__ void avg_pool_i8_vec16(PoolGeomDev g, const int8_t* __restrict__ x, int32_t zi, int32_t zo,
+                                  RecipTable rt, int8_t* out, uint32_t* err) {
+    const int cg = g.c >> 4;
+    const int total = g.n * g.oh * g.ow * cg;
+    uint32_t lerr = 0;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        const int c16 = (i % cg) * 16;
+        int r = i / cg;
+        const int ox = r % g.ow;
+        r /= g.ow;
+        const int oy = r % g.oh;
+        const int b = r / g.oh;
+        const int iy0 = oy * g.sy - g.pad_t, ix0 = ox * g.sx - g.pad_l;
+        uint32_t acc[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc[j] = 0;
+        int count = 0;
+        for (int ky = 0; ky < g.ky; ++ky) {
+            const int y = iy0 + ky;
+            if (y < 0 || y >= g.ih) continue;
+            for (int kx = 0; kx < g.kx; ++kx) {
+                const int xx = ix0 + kx;
+                if (xx < 0 || xx >= g.iw) continue;
+                const uint4 v = __ldg(reinterpret_cast<const uint4*>(
+                    x + ((static_cast<long long>(b) * g.ih + y) * g.iw + xx) * g.c + c16));
+                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    acc[j] += static_cast<uint32_t>(static_cast<int32_t>(static_cast<int8_t>(w[j >> 2] >> (8 * (j & 3)))) - zi);
+                ++count;
+            }
+        }
+        int32_t m, sh;
+        if (count <= 64) {
+            m = rt.m[count];
+            sh = rt.s[count];
+        } else {
+            reciprocal_scale_dev(count, &m, &sh);
+        }
+        uint32_t o[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const int32_t q = static_cast<int32_t>(
+                rescale_value(static_cast<int32_t>(acc[j]), m, sh, ROUND_SINGLE, 1, zo, -128, 127, &lerr));
+            o[j >> 2] |= static_cast<uint32_t>(static_cast<uint8_t>(q)) << (8 * (j & 3));
+        }
+        reinterpret_cast<uint4*>(out)[i] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    if (lerr) atomicOr(err, lerr);
+}
+
+// int8, C % 16 == 0, fewer than 2^31 output vectors: byte-wise signed max of 16-byte words.
+__global__ void max_pool_i8_vec16(PoolGeomDev g, const int8_t* __restrict__ x, int8_t* out) {
+    const int cg = g.c >> 4;
+    const int total = g.n * g.oh * g.ow * cg;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        const int c16 = (i % cg) * 16;
+        int r = i / cg;
+        const int ox = r % g.ow;
+        r /= g.ow;
+        const int oy = r % g.oh;
+        const int b = r / g.oh;
+        const int iy0 = oy * g.sy - g.pad_t, ix0 = ox * g.sx - g.pad_l;
+        uint4 m = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);
+        for (int ky = 0; ky < g.ky; ++ky) {
+            const int y = iy0 + ky;
+            if (y < 0 || y >= g.ih) continue;
+            for (int kx = 0; kx < g.kx; ++kx) {
+                const int xx = ix0 + kx;
+                if (xx < 0 || xx >= g.iw) continue;
+                const uint4 v = __ldg(reinterpret_cast<const uint4*>(
+                    x + ((static_cast<long long>(b) * g.ih + y) * g.iw + xx) * g.c + c16));
+                m.x = __vmaxs4(m.x, v.x);
+                m.y = __vmaxs4(m.y, v.y);
+                m.z = __vmaxs4(m.z, v.z);
+                m.w = __vmaxs4(m.w, v.w);
+            }
+        }
+        reinterpret_cast<uint4*>(out)[i] = m;
+    }
+}
+
 // Float AVG_POOL2D: every add and the division rounded to acc_dt, the result
 // rounded to the data type (pool.rs:215-227).
 __global__ void avg_pool_float(PoolGeomDev g, const void* __restrict__ x, int dt, int acc_dt, void* out) {

@@ -3,8 +3,8 @@
 The reference ships no model files; these builders write seeded `.tosa`
 graphs with the shapes of BASELINE configs 3 (MobileNetV2-shaped, int8) and 4
 (ResNet-50-shaped, int8), plus small residual graphs for the tests. Weights
-are uniform int8 in [-127, 127], biases uniform int32, zero points uniform in
-[-8, 8]. Every contraction is followed by a per-channel RESCALE (scale32,
+are uniform int8 in [-127, 127], biases calibrated int32, zero points uniform
+in [-8, 8] (the ResNet-50 graph keeps weight zero points at 0). Every contraction is followed by a per-channel RESCALE (scale32,
 double rounding) to int8 and a CLAMP; residual additions follow the quantized
 pattern RESCALE(int8 -> int32) of both branches, ADD (int32), RESCALE
 (int32 -> int8), CLAMP.
@@ -31,8 +31,9 @@ D = TG.DTYPE
 
 
 class GraphBuilder:
-    def __init__(self, seed: int, batch: int):
+    def __init__(self, seed: int, batch: int, weight_zp: bool = True):
         self.rng = np.random.default_rng(seed)
+        self.weight_zp = weight_zp  # draw weight zero points (else symmetric weights, zero point 0)
         self.batch = batch
         self.ops: list = []
         self.tensors: dict = {}
@@ -97,7 +98,7 @@ class GraphBuilder:
         pt, pb, oh = self.same_pads(ih, k, stride)
         pl, pr, ow = self.same_pads(iw, k, stride)
         assert (ih - 1 + pt + pb - (k - 1)) % stride == 0 and (iw - 1 + pl + pr - (k - 1)) % stride == 0
-        w_zp = self.zp()
+        w_zp = self.zp() if self.weight_zp else 0
         if depthwise:
             w = self.rng.integers(-127, 128, (k, k, ic, 1), dtype=np.int8)
             oc = ic
@@ -142,7 +143,7 @@ class GraphBuilder:
     def matmul(self, a, a_zp, b_arr):
         n, h, c = self.shape(a)
         w = b_arr.shape[2]
-        b_zp = self.zp()
+        b_zp = self.zp() if self.weight_zp else 0
         out = self._name("mm")
         self._tensor(out, [n, h, w], D["INT32"])
         self.ops.append(TG.Operator(op=TG.OP["MATMUL"], inputs=[
@@ -265,8 +266,10 @@ def resnet50_int8(batch: int, seed: int = 4, image: int = 224, classes: int = 10
     [3, 4, 6, 3] with widths 64/128/256/512 (x4 out), RESCALE+CLAMP after every
     conv, residual ADD, AVG_POOL2D 7x7, 2048 -> 1000 MATMUL (int32 logits).
     Padding is TF 'SAME'; the strided projection shortcut is AVG_POOL2D 2x2/s2
-    followed by a 1x1 CONV2D. Returns (graph bytes, info dict)."""
-    g = GraphBuilder(seed, batch)
+    followed by a 1x1 CONV2D. Weights are symmetric (zero point 0, as int8
+    classifiers quantize them); activation zero points are drawn from [-8, 8].
+    Returns (graph bytes, info dict)."""
+    g = GraphBuilder(seed, batch, weight_zp=False)
     x = g.input("images", [batch, image, image, 3])
     x_zp = g.zp()
     # the stem conv has 3 input channels: pad 3
