@@ -181,47 +181,46 @@ tb_status prepare_rescale(const tb_rescale_attr* a, int in_t, int64_t shape_last
     for (int i = 0; i < a->channels; ++i) {
         m[i] = a->multiplier[i];
         s[i] = a->shift[i];
-        if (m[i] < 0 || s[i] < 32 || s[i] > 62) fast = false;
+        if (m[i] < 0 || s[i] < 33 || s[i] > 62) fast = false;
     }
     r->fast = fast;
-    // Blob layout (int32 words): [rq: 8 per padded channel (fast path only)] [multiplier] [shift].
+    // Blob layout (int32 words): [fast path: m, sh, hz, each padded to whole 256-channel tiles with
+    // channel 0] [multiplier] [shift].
+    //   With s >= 33 every int32 v is in apply_scale_32's range and
+    //   (v*m + 2^(s-1) +- 2^30) >> s == (hi32(v*m +- 2^30) + 2^(s-33)) >> (s-32)
+    // (adding a multiple of 2^32 to the 64-bit sum adds it to the high word; the nested floor is
+    // exact). The output zero point joins hz as zp * 2^(s-32) when that stays inside int32.
     const size_t padded = (static_cast<size_t>(a->channels) + 255) / 256 * 256;
-    const size_t rq_words = fast ? 8 * padded : 0;
-    blob->assign(rq_words + 2 * static_cast<size_t>(a->channels), 0);
+    const size_t fq_words = fast ? 3 * padded : 0;
+    blob->assign(fq_words + 2 * static_cast<size_t>(a->channels), 0);
     if (fast) {
-        // R = 2^(s-1) (+2^30 for v >= 0, -2^30 for v < 0 under double rounding) as 64-bit lo/hi words;
-        // when every shift is <= 55 the output zero point rides along as zp * 2^s (the 64-bit sum then
-        // stays below 2^63 and the shifted result gains exactly zp). Padded to whole 256-column tiles
-        // with channel 0 so the kernel needs no index clamp.
         bool fold = true;
-        for (int i = 0; i < a->channels; ++i)
-            if (s[i] > 55) fold = false;
+        for (int i = 0; i < a->channels; ++i) {
+            const long long hz = (1ll << (s[i] - 33)) + static_cast<long long>(ozp) * (1ll << (s[i] - 32));
+            if (hz < INT32_MIN || hz > INT32_MAX) fold = false;
+        }
         r->zp_folded = fold;
         for (size_t pi = 0; pi < padded; ++pi) {
             const int i = pi < static_cast<size_t>(a->channels) ? static_cast<int>(pi) : 0;
-            const int64_t base = (1ll << (s[i] - 1)) + (fold ? static_cast<int64_t>(ozp) * (1ll << s[i]) : 0);
-            const int64_t dr = a->rounding_mode == TB_ROUND_DOUBLE ? (1ll << 30) : 0;
-            const uint64_t rp = static_cast<uint64_t>(base + dr), rn = static_cast<uint64_t>(base - dr);
-            int32_t* q = &(*blob)[8 * pi];
-            q[0] = m[i];
-            q[1] = s[i] - 32;
-            q[2] = static_cast<int32_t>(rp & 0xffffffffu);
-            q[3] = static_cast<int32_t>(rp >> 32);
-            q[4] = static_cast<int32_t>(rn & 0xffffffffu);
-            q[5] = static_cast<int32_t>(rn >> 32);
+            const long long hz = (1ll << (s[i] - 33)) + (fold ? static_cast<long long>(ozp) * (1ll << (s[i] - 32)) : 0);
+            (*blob)[pi] = m[i];
+            (*blob)[padded + pi] = s[i] - 32;
+            (*blob)[2 * padded + pi] = static_cast<int32_t>(hz);
         }
     }
-    std::copy(m.begin(), m.end(), blob->begin() + rq_words);
-    std::copy(s.begin(), s.end(), blob->begin() + rq_words + a->channels);
+    std::copy(m.begin(), m.end(), blob->begin() + fq_words);
+    std::copy(s.begin(), s.end(), blob->begin() + fq_words + a->channels);
     return TB_OK;
 }
 
 void place_rescale(RescalePlan* r, int32_t* dev_blob) {
     const size_t padded = (static_cast<size_t>(r->channels) + 255) / 256 * 256;
-    const size_t rq_words = r->fast ? 8 * padded : 0;
-    r->d_rq = r->fast ? dev_blob : nullptr;
-    r->d_mult = dev_blob + rq_words;
-    r->d_shift = dev_blob + rq_words + r->channels;
+    const size_t fq_words = r->fast ? 3 * padded : 0;
+    r->fq_m = r->fast ? dev_blob : nullptr;
+    r->fq_sh = r->fast ? dev_blob + padded : nullptr;
+    r->fq_hz = r->fast ? dev_blob + 2 * padded : nullptr;
+    r->d_mult = dev_blob + fq_words;
+    r->d_shift = dev_blob + fq_words + r->channels;
 }
 
 tb_status make_rescale_plan(tb_context* ctx, const tb_rescale_attr* a, int in_t, int64_t shape_last, RescalePlan* r) {
@@ -237,7 +236,7 @@ tb_status make_rescale_plan(tb_context* ctx, const tb_rescale_attr* a, int in_t,
 void free_rescale_plan(RescalePlan* r) {
     if (r->d_blob) cudaFree(r->d_blob);
     r->d_blob = nullptr;
-    r->d_mult = r->d_shift = r->d_rq = nullptr;
+    r->d_mult = r->d_shift = r->fq_m = r->fq_sh = r->fq_hz = nullptr;
 }
 
 RescaleArgs rescale_args(const RescalePlan& r) {
@@ -537,7 +536,9 @@ extern "C" TB_API tb_status tb_matmul_plan_run(tb_matmul_plan* p, const void* a,
             ep.rs = rescale_args(p->rs);
             ep.rs_fast = p->rs.fast;
             ep.rs_zp_folded = p->rs.zp_folded;
-            ep.rq = reinterpret_cast<const int4*>(p->rs.d_rq);
+            ep.fq_m = p->rs.fq_m;
+            ep.fq_sh = p->rs.fq_sh;
+            ep.fq_hz = p->rs.fq_hz;
             ep.out_dtype = p->rs.out_dtype;
         } else {
             ep.mode = EPI_I32;
@@ -727,7 +728,7 @@ static tb_status conv_plan_create(tb_context* ctx, const tb_conv2d_desc* d, cons
     const long long kfull = taps * d->ic;
     const long long m_rows = static_cast<long long>(d->n) * oh * ow;
     if (p->path == 2 && wt == TB_DT_INT8 && kfull >= 16 && m_rows >= 4096 && aligned16(weight) &&
-        m_rows * ((kfull + 15) / 16 * 16) <= (4ll << 30)) {
+        m_rows * ((kfull + 15) / 16 * 16) <= (4ll << 30) && kfull <= 384) {
         p->path = 8;
         p->kp = static_cast<int>((kfull + 15) / 16 * 16);
         cudaError_t ce = cudaMalloc(&p->d_rows, static_cast<size_t>(m_rows) * p->kp);
@@ -923,7 +924,11 @@ extern "C" TB_API tb_status tb_conv2d_plan_run(tb_conv2d_plan* p, const void* in
         TB_LAUNCHED(ctx);
         return TB_OK;
     case 8: {
-        im2col_rows_i8<<<grid_for(ctx, static_cast<long long>(d.n) * p->oh * p->ow * (p->kp / 16)), 256, 0, st>>>(
+        const long long m_rows = static_cast<long long>(d.n) * p->oh * p->ow;
+        const int threads = 128;
+        long long blocks = (m_rows + threads - 1) / threads;
+        blocks = std::min<long long>(blocks, static_cast<long long>(ctx->num_sms) * 16);
+        im2col_rows_i8<<<static_cast<int>(blocks), threads, static_cast<size_t>(threads) * p->kp, st>>>(
             g, static_cast<const int8_t*>(input), d.kh * d.kw * d.ic, p->kp, static_cast<int8_t>(d.input_zp), p->d_rows);
         TB_LAUNCHED(ctx);
         return tb_conv2d_plan_run(p->inner, p->d_rows, out, stream_);
@@ -996,7 +1001,9 @@ extern "C" TB_API tb_status tb_conv2d_plan_run(tb_conv2d_plan* p, const void* in
         ep.rs = rescale_args(p->rs);
         ep.rs_fast = p->rs.fast;
         ep.rs_zp_folded = p->rs.zp_folded;
-        ep.rq = reinterpret_cast<const int4*>(p->rs.d_rq);
+        ep.fq_m = p->rs.fq_m;
+        ep.fq_sh = p->rs.fq_sh;
+        ep.fq_hz = p->rs.fq_hz;
         ep.out_dtype = p->rs.out_dtype;
     } else {
         ep.mode = EPI_I32;

@@ -192,46 +192,40 @@ __device__ __forceinline__ int32_t small_rescale(int32_t x, int32_t m, int s, lo
 
 // Residual chain, int8 in and out, 16 elements per thread. The two input
 // RESCALEs use the error-free constants of ResidualFast; the output RESCALE
-// uses the packed fast-path constants (every shift >= 32, multiplier >= 0:
-// r = ((v * m + R) >> 32) >> (s - 32) [+ zp], clamped), as in the GEMM epilogue.
+// uses the fast-path arrays (every shift in [33, 62], multiplier >= 0), as the
+// GEMM epilogue does; saturating packs and the fused CLAMP finish the range.
 template <bool PC, bool DBL>
 __global__ void residual_fast_i8(const uint4* __restrict__ a, const uint4* __restrict__ b, ResidualFast f,
-                                 const int4* __restrict__ rq, int32_t lo, int32_t hi, int32_t add_zp, long long n16,
-                                 int channels, uint4* __restrict__ out) {
-    int4 P = __ldg(rq), Q = __ldg(rq + 1);
+                                 const int32_t* __restrict__ fm, const int32_t* __restrict__ fsh,
+                                 const int32_t* __restrict__ fhz, int32_t lo, int32_t hi, int32_t add_zp,
+                                 long long n16, int channels, uint4* __restrict__ out) {
+    const int32_t m0 = __ldg(fm), sh0 = __ldg(fsh), hz0 = __ldg(fhz);
+    const bool clamp = lo > -128 || hi < 127;
     for (long long q = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; q < n16;
          q += static_cast<long long>(gridDim.x) * blockDim.x) {
         const uint4 av = __ldg(a + q), bv = __ldg(b + q);
         const uint32_t aw[4] = {av.x, av.y, av.z, av.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
         const int c0 = PC ? static_cast<int>((static_cast<unsigned long long>(q) << 4) % static_cast<unsigned>(channels))
                           : 0;
-        uint32_t ow[4];
+        int32_t r[16];
 #pragma unroll
         for (int w = 0; w < 4; ++w) {
-            uint32_t word = 0;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
+                const int k = 4 * w + j;
                 const int32_t xa = sext8(aw[w], j) - f.za, xb = sext8(bw[w], j) - f.zb;
                 const int32_t sum = static_cast<int32_t>(
                     static_cast<uint32_t>(small_rescale(xa, f.ma, f.sa, f.ra_pos, f.ra_neg)) +
                     static_cast<uint32_t>(small_rescale(xb, f.mb, f.sb, f.rb_pos, f.rb_neg)));
-                if (PC) {
-                    P = __ldg(rq + 2 * (c0 + 4 * w + j));
-                    if (DBL) Q = __ldg(rq + 2 * (c0 + 4 * w + j) + 1);
-                }
-                const bool neg = DBL && sum < 0;
-                const long long R = static_cast<long long>(
-                    (static_cast<unsigned long long>(static_cast<uint32_t>(neg ? Q.y : P.w)) << 32) |
-                    static_cast<uint32_t>(neg ? Q.x : P.z));
-                const int32_t hi32 = static_cast<int32_t>(
-                    static_cast<unsigned long long>(static_cast<long long>(sum) * P.x + R) >> 32);
-                int32_t r = (hi32 >> P.y) + add_zp;
-                r = min(max(r, lo), hi);
-                word |= static_cast<uint32_t>(static_cast<uint8_t>(r)) << (8 * j);
+                if (PC)
+                    r[k] = rescale_f2<DBL>(sum, __ldg(fm + c0 + k), __ldg(fsh + c0 + k), __ldg(fhz + c0 + k)) + add_zp;
+                else
+                    r[k] = rescale_f2<DBL>(sum, m0, sh0, hz0) + add_zp;
+                if (clamp) r[k] = min(max(r[k], lo), hi);
             }
-            ow[w] = word;
         }
-        out[q] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+        out[q] = make_uint4(pack4_sat_i8(r[0], r[1], r[2], r[3]), pack4_sat_i8(r[4], r[5], r[6], r[7]),
+                            pack4_sat_i8(r[8], r[9], r[10], r[11]), pack4_sat_i8(r[12], r[13], r[14], r[15]));
     }
 }
 
@@ -304,19 +298,22 @@ tb_status launch_residual(tb_context* ctx, const void* a, int a_dt, int a_uns, i
         aligned16(a) && aligned16(b) && aligned16(out)) {
         const long long n16 = count / 16;
         const int32_t add_zp = ro.zp_folded ? 0 : ro.out_zp;
-        const int4* rq = reinterpret_cast<const int4*>(ro.d_rq);
         const int grid = grid_for(ctx, n16);
         const bool dbl = ro.rounding == TB_ROUND_DOUBLE;
         auto A = static_cast<const uint4*>(a);
         auto B = static_cast<const uint4*>(b);
         auto O = static_cast<uint4*>(out);
+#define TB_RESID(PC, DBL)                                                                                      \
+    residual_fast_i8<PC, DBL><<<grid, 256, 0, st>>>(A, B, fast, ro.fq_m, ro.fq_sh, ro.fq_hz, ro.lo, ro.hi, add_zp, \
+                                                    n16, channels, O)
         if (ro.per_channel) {
-            if (dbl) residual_fast_i8<true, true><<<grid, 256, 0, st>>>(A, B, fast, rq, ro.lo, ro.hi, add_zp, n16, channels, O);
-            else residual_fast_i8<true, false><<<grid, 256, 0, st>>>(A, B, fast, rq, ro.lo, ro.hi, add_zp, n16, channels, O);
+            if (dbl) TB_RESID(true, true);
+            else TB_RESID(true, false);
         } else {
-            if (dbl) residual_fast_i8<false, true><<<grid, 256, 0, st>>>(A, B, fast, rq, ro.lo, ro.hi, add_zp, n16, channels, O);
-            else residual_fast_i8<false, false><<<grid, 256, 0, st>>>(A, B, fast, rq, ro.lo, ro.hi, add_zp, n16, channels, O);
+            if (dbl) TB_RESID(false, true);
+            else TB_RESID(false, false);
         }
+#undef TB_RESID
         TB_LAUNCHED(ctx);
         return TB_OK;
     }

@@ -71,12 +71,17 @@ struct RescalePlan {
     int scale32 = 1, rounding = 1, per_channel = 0, channels = 1;
     int32_t out_zp = 0, lo = 0, hi = 0;
     int out_dtype = TB_DT_INT32;
-    bool fast = false;             // every shift >= 32 and multiplier >= 0 (scale32 single/double)
-    bool zp_folded = false;        // output zero point folded into the packed rounding constants
+    bool fast = false;             // every shift in [33, 62], multiplier >= 0 (scale32 single/double)
+    bool zp_folded = false;        // the output zero point rides in fq_hz
     int32_t* d_mult = nullptr;     // [channels]
     int32_t* d_shift = nullptr;    // [channels]
-    int32_t* d_rq = nullptr;       // fast path: [channels][8] {m, s-32, rp_lo, rp_hi, rn_lo, rn_hi, 0, 0}
-    int32_t* d_blob = nullptr;     // owned allocation holding rq, multiplier and shift
+    // Fast path, three arrays of `padded` (channels rounded up to 256) words:
+    //   fq_m  multiplier, fq_sh  shift - 32, fq_hz  2^(shift-33) (+ out_zp * 2^(shift-32) when folded)
+    // r = ((high word of v*m [+-2^30 by the sign of v under double rounding]) + hz) >> sh [+ out_zp]
+    int32_t* fq_m = nullptr;
+    int32_t* fq_sh = nullptr;
+    int32_t* fq_hz = nullptr;
+    int32_t* d_blob = nullptr;     // owned allocation holding the fast arrays, multiplier and shift
 };
 
 // Validate a fused/standalone RESCALE (src/ops/type_conv.rs:128-171) for

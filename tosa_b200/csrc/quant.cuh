@@ -141,6 +141,31 @@ __device__ __forceinline__ int32_t rescale_fast(int32_t v, int32_t m, int32_t s,
     return r;
 }
 
+// Four int32 -> four saturated int8 in one word, v0 in the lowest byte
+// (cvt.pack.sat: d = c << 16 | sat(a) << 8 | sat(b)).
+__device__ __forceinline__ uint32_t pack4_sat_i8(int32_t v0, int32_t v1, int32_t v2, int32_t v3) {
+    uint32_t t, d;
+    asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(t) : "r"(v3), "r"(v2), "r"(0));
+    asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(v1), "r"(v0), "r"(t));
+    return d;
+}
+
+// The fast RESCALE of one value (every shift s in [33, 62], m >= 0, checked on the
+// host): apply_scale_32's (v*m + 2^(s-1) [+-2^30]) >> s as the high word of
+// v*m [+-2^30 by the sign of v] plus hz = 2^(s-33) (+ zp * 2^(s-32)), shifted by
+// s - 32; |high word| <= 2^30 and |hz| < 2^30 keep the sum inside int32.
+template <bool DBL>
+__device__ __forceinline__ int32_t rescale_f2(int32_t v, int32_t m, int32_t sh, int32_t hz) {
+    int32_t h;
+    if (DBL) {
+        const long long R = (static_cast<long long>(v >> 31) << 31) | 0x40000000ll;  // +2^30, or -2^30 for v < 0
+        h = static_cast<int32_t>((static_cast<long long>(v) * m + R) >> 32);
+    } else {
+        h = __mulhi(v, m);
+    }
+    return (h + hz) >> sh;
+}
+
 // f32 -> dtype -> f32 rounding (round to nearest even).
 __device__ __forceinline__ float round_to_dtype(float x, int dtype) {
     if (dtype == DT_BF16) return __bfloat162float(__float2bfloat16_rn(x));

@@ -148,41 +148,44 @@ __global__ void conv2d_direct_float(ConvGeomDev g, const void* __restrict__ x, c
 // ---------------------------------------------------------------------------
 __global__ void im2col_rows_i8(ConvGeomDev g, const int8_t* __restrict__ x, int k_valid, int kp, int8_t zx,
                                int8_t* __restrict__ rows) {
+    // One thread per output pixel assembles its row in shared memory (taps in
+    // weight order, runs of kw * ic contiguous input bytes per kernel row), then
+    // the block writes its rows out with 16-byte stores.
+    extern __shared__ __align__(16) int8_t srow[];
+    const long long m_total = static_cast<long long>(g.n) * g.oh * g.ow;
     const int chunks = kp >> 4;
-    const long long total = static_cast<long long>(g.n) * g.oh * g.ow * chunks;
-    const int tap_c = g.kw * g.ic;
-    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-         i += static_cast<long long>(gridDim.x) * blockDim.x) {
-        const int chunk = static_cast<int>(i % chunks);
-        long long r = i / chunks;
-        const int ox = static_cast<int>(r % g.ow);
-        r /= g.ow;
-        const int oy = static_cast<int>(r % g.oh);
-        const int b = static_cast<int>(r / g.oh);
-        int k = chunk << 4;
-        int ky = k / tap_c, rem = k - ky * tap_c, kx = rem / g.ic, c = rem - kx * g.ic;
-        const int8_t* xb = x + static_cast<long long>(b) * g.ih * g.iw * g.ic;
-        uint32_t w4[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            uint32_t word = 0;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                int8_t v = zx;
-                if (k < k_valid) {
-                    const int y = oy * g.sh + ky * g.dh - g.pad_t, xx = ox * g.sw + kx * g.dw - g.pad_l;
-                    if (y >= 0 && y < g.ih && xx >= 0 && xx < g.iw) v = xb[(static_cast<long long>(y) * g.iw + xx) * g.ic + c];
-                }
-                word |= static_cast<uint32_t>(static_cast<uint8_t>(v)) << (8 * j);
-                ++k;
-                if (++c == g.ic) {
-                    c = 0;
-                    if (++kx == g.kw) { kx = 0; ++ky; }
+    for (long long m0 = static_cast<long long>(blockIdx.x) * blockDim.x; m0 < m_total;
+         m0 += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long m = m0 + threadIdx.x;
+        int8_t* my = srow + threadIdx.x * kp;
+        if (m < m_total) {
+            const int ox = static_cast<int>(m % g.ow);
+            const long long r = m / g.ow;
+            const int oy = static_cast<int>(r % g.oh);
+            const int b = static_cast<int>(r / g.oh);
+            const int8_t* xb = x + static_cast<long long>(b) * g.ih * g.iw * g.ic;
+            int k = 0;
+            for (int ky = 0; ky < g.kh; ++ky) {
+                const int y = oy * g.sh + ky * g.dh - g.pad_t;
+                const bool yok = y >= 0 && y < g.ih;
+                for (int kx = 0; kx < g.kw; ++kx) {
+                    const int xx = ox * g.sw + kx * g.dw - g.pad_l;
+                    const bool ok = yok && xx >= 0 && xx < g.iw;
+                    const int8_t* src = xb + (static_cast<long long>(y) * g.iw + xx) * g.ic;
+                    for (int c = 0; c < g.ic; ++c) my[k++] = ok ? __ldg(src + c) : zx;
                 }
             }
-            w4[q] = word;
+            for (; k < kp; ++k) my[k] = zx;
+            (void)k_valid;
         }
-        reinterpret_cast<uint4*>(rows)[i] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+        __syncthreads();
+        // cooperative copy of the block's rows: rows are contiguous in global memory
+        const long long rows_here = m_total - m0 < blockDim.x ? m_total - m0 : blockDim.x;
+        const int vecs = static_cast<int>(rows_here) * chunks;
+        uint4* dst = reinterpret_cast<uint4*>(rows + m0 * kp);
+        const uint4* s4 = reinterpret_cast<const uint4*>(srow);
+        for (int v = threadIdx.x; v < vecs; v += blockDim.x) dst[v] = s4[v];
+        __syncthreads();
     }
 }
 

@@ -85,9 +85,12 @@ struct GemmEpilogue {
     int n_col_classes;
     // RESCALE
     RescaleArgs rs;
-    int rs_fast;               // every shift in [32, 62], multipliers >= 0 (host-verified)
-    int rs_zp_folded;          // out_zp is inside the packed R constants
-    const int4* rq;            // fast path: [channels padded][2]: {m, s-32, rp_lo, rp_hi}, {rn_lo, rn_hi, -, -}
+    int rs_fast;               // every shift in [33, 62], multipliers >= 0 (host-verified)
+    int rs_zp_folded;          // out_zp rides in fq_hz
+    // fast path, [channels padded to 256]: multiplier, shift - 32, 2^(shift-33) (+ out_zp * 2^(shift-32))
+    const int32_t* fq_m;
+    const int32_t* fq_sh;
+    const int32_t* fq_hz;
     int out_dtype;             // DT_INT8 / DT_INT16 / DT_INT32 / DT_FP32 / DT_BF16 / DT_FP16
     // Float convolution: out = round(round(acc) + fbias[n])
     const float* fbias;        // [N] or [1]
@@ -157,7 +160,7 @@ struct GemmCfg {
     static constexpr int B_MN_CHUNK = 128 / kElem;                  // N elements per box
     static constexpr int B_MN_BOX_BYTES = BK * 128;                 // BK k-rows x 128 bytes
     static constexpr int TMEM_COLS = 2 * BN <= 32 ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
-    static constexpr int SCRATCH_BYTES = 8192;  // epilogue: column-sum reduction and staged column terms
+    static constexpr int SCRATCH_BYTES = 12288;  // epilogue: column-sum reduction, staged per-tile column constants
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 2048 /*barriers, row sums*/ + SCRATCH_BYTES;
     static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "UMMA N for M=128; each epilogue half walks pairs of 16-column chunks");
     static_assert(!B_MN_MAJOR || BK_BYTES == 128, "MN-major B uses 128-byte K blocks");
@@ -190,39 +193,18 @@ __device__ __forceinline__ uint32_t pack4_i8(int32_t a, int32_t b, int32_t c, in
     return __byte_perm(lo, hi, 0x5410);
 }
 
-// High word of the 64-bit sum v*m + (rhi:rlo), v and m signed 32-bit.
-__device__ __forceinline__ int32_t mad_wide_hi(int32_t v, int32_t m, uint32_t rlo, uint32_t rhi) {
-    const int64_t r = static_cast<int64_t>((static_cast<uint64_t>(rhi) << 32) | rlo);
-    const int64_t t = static_cast<int64_t>(v) * m + r;  // one wide multiply-add with a 64-bit addend
-    return static_cast<int32_t>(static_cast<uint64_t>(t) >> 32);
-}
-
-template <bool PC, bool DBL>
-__device__ __forceinline__ void rescale_fast(const int32_t (&v)[kChunk], int32_t (&res)[kChunk],
-                                             const int4* __restrict__ rq, int4 P, int4 Q, int n0, int32_t lo,
-                                             int32_t hi, int32_t add_zp) {
-#pragma unroll
-    for (int j = 0; j < kChunk; ++j) {
-        if (PC) {
-            P = __ldg(rq + 2 * (n0 + j));
-            if (DBL) Q = __ldg(rq + 2 * (n0 + j) + 1);
-        }
-        uint32_t rlo = static_cast<uint32_t>(P.z), rhi = static_cast<uint32_t>(P.w);
-        if (DBL) {
-            const bool neg = v[j] < 0;
-            rlo = neg ? static_cast<uint32_t>(Q.x) : rlo;
-            rhi = neg ? static_cast<uint32_t>(Q.y) : rhi;
-        }
-        const int32_t y = (mad_wide_hi(v[j], P.x, rlo, rhi) >> P.y) + add_zp;
-        res[j] = min(max(y, lo), hi);
-    }
-}
-
 // Epilogue for kChunk consecutive output columns n0.. of one row (one thread).
+// Per-tensor fast RESCALE constants (channel 0) and the clamp decision, loaded once.
+struct FastConst {
+    int32_t m, sh, hz, add_zp;
+    bool clamp;  // the range is narrower than int8's (a fused CLAMP): saturation alone does not do it
+};
+
 template <int EK>
 __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, const uint32_t (&acc)[kChunk], int n0,
                                                long long orow, int32_t rowterm, const int32_t* colterm,
-                                               const int32_t* delta, int4 P0, int4 Q0, uint32_t& err) {
+                                               const int32_t* delta, const int32_t* fm, const int32_t* fsh,
+                                               const int32_t* fhz, const FastConst& fk, uint32_t& err) {
     const GemmEpilogue& e = p.epi;
     uint8_t* outp = reinterpret_cast<uint8_t*>(p.out);
     const int ncols = min(kChunk, p.N - n0);
@@ -304,16 +286,41 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, const uint32
     if constexpr (EK >= EK_FAST_T_S && EK <= EK_FAST_PC_D) {
         constexpr bool PC = EK == EK_FAST_PC_S || EK == EK_FAST_PC_D;
         constexpr bool DBL = EK == EK_FAST_T_D || EK == EK_FAST_PC_D;
-        rescale_fast<PC, DBL>(v, res, e.rq, P0, Q0, n0, r.lo, r.hi, e.rs_zp_folded ? 0 : r.out_zp);
-        int8_t* o = reinterpret_cast<int8_t*>(outp) + orow + n0;
-        if (ncols == kChunk && ((reinterpret_cast<uintptr_t>(o) & 15) == 0)) {
-            *reinterpret_cast<uint4*>(o) = make_uint4(pack4_i8(res[0], res[1], res[2], res[3]),
-                                                      pack4_i8(res[4], res[5], res[6], res[7]),
-                                                      pack4_i8(res[8], res[9], res[10], res[11]),
-                                                      pack4_i8(res[12], res[13], res[14], res[15]));
+        if constexpr (PC) {
+            // per-channel constants of this chunk, staged in shared memory for the tile
+#pragma unroll
+            for (int j = 0; j < kChunk; j += 4) {
+                const int4 m4 = *reinterpret_cast<const int4*>(fm + n0 + j);
+                const int4 s4 = *reinterpret_cast<const int4*>(fsh + n0 + j);
+                const int4 h4 = *reinterpret_cast<const int4*>(fhz + n0 + j);
+                res[j + 0] = rescale_f2<DBL>(v[j + 0], m4.x, s4.x, h4.x);
+                res[j + 1] = rescale_f2<DBL>(v[j + 1], m4.y, s4.y, h4.y);
+                res[j + 2] = rescale_f2<DBL>(v[j + 2], m4.z, s4.z, h4.z);
+                res[j + 3] = rescale_f2<DBL>(v[j + 3], m4.w, s4.w, h4.w);
+            }
         } else {
 #pragma unroll
-            for (int j = 0; j < kChunk; ++j) if (j < ncols) o[j] = static_cast<int8_t>(res[j]);
+            for (int j = 0; j < kChunk; ++j) res[j] = rescale_f2<DBL>(v[j], fk.m, fk.sh, fk.hz);
+        }
+        if (fk.add_zp != 0) {
+#pragma unroll
+            for (int j = 0; j < kChunk; ++j) res[j] += fk.add_zp;
+        }
+        if (fk.clamp) {
+#pragma unroll
+            for (int j = 0; j < kChunk; ++j) res[j] = min(max(res[j], r.lo), r.hi);
+        }
+        int8_t* o = reinterpret_cast<int8_t*>(outp) + orow + n0;
+        if (ncols == kChunk && ((reinterpret_cast<uintptr_t>(o) & 15) == 0)) {
+            // saturating packs complete the clamp to the int8 range
+            *reinterpret_cast<uint4*>(o) = make_uint4(pack4_sat_i8(res[0], res[1], res[2], res[3]),
+                                                      pack4_sat_i8(res[4], res[5], res[6], res[7]),
+                                                      pack4_sat_i8(res[8], res[9], res[10], res[11]),
+                                                      pack4_sat_i8(res[12], res[13], res[14], res[15]));
+        } else {
+#pragma unroll
+            for (int j = 0; j < kChunk; ++j)
+                if (j < ncols) o[j] = static_cast<int8_t>(min(max(res[j], r.lo), r.hi));
         }
         return;
     } else {
@@ -565,7 +572,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             ephase ^= 1;
             return done;
         };
-        int32_t* ct_stage = scratch + 1024;     // [2][256] column terms of the current tile
+        // [2 buffers][column terms, multiplier, shift - 32, hz][256] of the current tile
+        int32_t* ct_stage = scratch + 1024;
+        constexpr bool kPC = EK == EK_FAST_PC_S || EK == EK_FAST_PC_D;
         bool ok = true;
         if (p.cs.b != nullptr) {
             // ---- column sums of B (MATMUL a_zp): 16 column groups of 4 bytes x 16 row slices
@@ -629,8 +638,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const int m = mt * BM + row;
             const bool row_ok = m < p.M;
             const int32_t* colterm = nullptr;
-            if (e.colterm != nullptr) {
-                if (p.cs.b != nullptr && tcount == 0) {
+            const int32_t *fm = nullptr, *fsh = nullptr, *fhz = nullptr;
+            if (e.colterm != nullptr || kPC) {
+                if (e.colterm != nullptr && p.cs.b != nullptr && tcount == 0) {
                     // all column sums published (bounded wait on the cross-CTA counter)
                     const long long t0 = clock64();
                     while (*reinterpret_cast<volatile unsigned int*>(p.cs.counter) < p.cs.target) {
@@ -639,11 +649,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     __threadfence();
                     if (!ok) break;
                 }
-                // stage this tile's column terms in shared memory
-                int32_t* cst = ct_stage + (tcount & 1) * 256;
-                if (et < BN) cst[et] = e.colterm[b * e.colterm_bstride + nt * BN + et];
+                // stage this tile's column constants in shared memory (the tables are padded to
+                // whole 256-column tiles)
+                int32_t* cst = ct_stage + (tcount & 1) * 1024;
+                if (et < BN) {
+                    const int n = nt * BN + et;
+                    if (e.colterm != nullptr) cst[et] = e.colterm[b * e.colterm_bstride + n];
+                    if constexpr (kPC) {
+                        cst[256 + et] = __ldg(e.fq_m + n);
+                        cst[512 + et] = __ldg(e.fq_sh + n);
+                        cst[768 + et] = __ldg(e.fq_hz + n);
+                    }
+                }
                 if (!epi_sync()) { ok = false; break; }
-                colterm = cst - nt * BN;
+                if (e.colterm != nullptr) colterm = cst - nt * BN;
+                fm = cst + 256 - nt * BN;
+                fsh = cst + 512 - nt * BN;
+                fhz = cst + 768 - nt * BN;
             }
             const int32_t* delta = nullptr;
             if (e.rowclass != nullptr && row_ok) {
@@ -658,10 +680,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const long long orow = static_cast<long long>(b) * p.out_batch_stride + static_cast<long long>(m) * p.ldo;
             const int nb = nt * BN + cbase;
             // Per-tensor rescale constants (channel 0), loaded once per tile.
-            int4 P0 = make_int4(0, 0, 0, 0), Q0 = make_int4(0, 0, 0, 0);
+            FastConst fk{0, 0, 0, 0, false};
             if constexpr (EK >= EK_FAST_T_S && EK <= EK_FAST_PC_D) {
-                P0 = __ldg(e.rq);
-                Q0 = __ldg(e.rq + 1);
+                fk.m = __ldg(e.fq_m);
+                fk.sh = __ldg(e.fq_sh);
+                fk.hz = __ldg(e.fq_hz);
+                fk.add_zp = e.rs_zp_folded ? 0 : e.rs.out_zp;
+                fk.clamp = e.rs.lo > -128 || e.rs.hi < 127;
             }
             // Two register sets: the next chunk's TMEM load overlaps this chunk's epilogue.
             uint32_t accA[kChunk], accB[kChunk];
@@ -674,13 +699,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 if (tr) p.trace[408 + (c0 / kChunk) * 2] = clock64();
                 __syncwarp();
                 tmem_ld_32x32b_x16(taddr + c0 + kChunk, accB);
-                if (row_ok && nb + c0 < p.N) epilogue_chunk<EK>(p, accA, nb + c0, orow, rowterm, colterm, delta, P0, Q0, err);
+                if (row_ok && nb + c0 < p.N)
+                    epilogue_chunk<EK>(p, accA, nb + c0, orow, rowterm, colterm, delta, fm, fsh, fhz, fk, err);
                 if (tr) p.trace[409 + (c0 / kChunk) * 2] = clock64();
                 __syncwarp();
                 tmem_wait_regs(accB);
                 if (c0 + 2 * kChunk < HALF) tmem_ld_32x32b_x16(taddr + c0 + 2 * kChunk, accA);
                 if (row_ok && nb + c0 + kChunk < p.N)
-                    epilogue_chunk<EK>(p, accB, nb + c0 + kChunk, orow, rowterm, colterm, delta, P0, Q0, err);
+                    epilogue_chunk<EK>(p, accB, nb + c0 + kChunk, orow, rowterm, colterm, delta, fm, fsh, fhz, fk,
+                                       err);
                 __syncwarp();
                 if (c0 + 2 * kChunk < HALF) tmem_wait_regs(accA);
             }
