@@ -191,14 +191,26 @@ __device__ __forceinline__ int32_t small_rescale(int32_t x, int32_t m, int s, lo
 }
 
 // Residual chain, int8 in and out, 16 elements per thread. The two input
-// RESCALEs use the error-free constants of ResidualFast; the output RESCALE
-// uses the fast-path arrays (every shift in [33, 62], multiplier >= 0), as the
-// GEMM epilogue does; saturating packs and the fused CLAMP finish the range.
+// RESCALEs are functions of one int8 value each: every block tabulates them
+// (256 int32 entries apiece, indexed by the input byte, error-free constants of
+// ResidualFast) in shared memory. The output RESCALE uses the fast-path arrays
+// (every shift in [33, 62], multiplier >= 0), as the GEMM epilogue does;
+// saturating packs and the fused CLAMP finish the range.
 template <bool PC, bool DBL>
-__global__ void residual_fast_i8(const uint4* __restrict__ a, const uint4* __restrict__ b, ResidualFast f,
-                                 const int32_t* __restrict__ fm, const int32_t* __restrict__ fsh,
-                                 const int32_t* __restrict__ fhz, int32_t lo, int32_t hi, int32_t add_zp,
-                                 long long n16, int channels, uint4* __restrict__ out) {
+__global__ void __launch_bounds__(256) residual_fast_i8(const uint4* __restrict__ a, const uint4* __restrict__ b,
+                                                        ResidualFast f, const int32_t* __restrict__ fm,
+                                                        const int32_t* __restrict__ fsh,
+                                                        const int32_t* __restrict__ fhz, int32_t lo, int32_t hi,
+                                                        int32_t add_zp, long long n16, int channels,
+                                                        uint4* __restrict__ out) {
+    __shared__ int32_t lut_a[256], lut_b[256];
+    {
+        const int u = threadIdx.x;  // blockDim.x == 256: one table entry per thread
+        const int32_t v = static_cast<int8_t>(static_cast<uint8_t>(u));
+        lut_a[u] = small_rescale(v - f.za, f.ma, f.sa, f.ra_pos, f.ra_neg);
+        lut_b[u] = small_rescale(v - f.zb, f.mb, f.sb, f.rb_pos, f.rb_neg);
+    }
+    __syncthreads();
     const int32_t m0 = __ldg(fm), sh0 = __ldg(fsh), hz0 = __ldg(fhz);
     const bool clamp = lo > -128 || hi < 127;
     for (long long q = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; q < n16;
@@ -213,10 +225,8 @@ __global__ void residual_fast_i8(const uint4* __restrict__ a, const uint4* __res
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const int k = 4 * w + j;
-                const int32_t xa = sext8(aw[w], j) - f.za, xb = sext8(bw[w], j) - f.zb;
-                const int32_t sum = static_cast<int32_t>(
-                    static_cast<uint32_t>(small_rescale(xa, f.ma, f.sa, f.ra_pos, f.ra_neg)) +
-                    static_cast<uint32_t>(small_rescale(xb, f.mb, f.sb, f.rb_pos, f.rb_neg)));
+                const int32_t sum = static_cast<int32_t>(static_cast<uint32_t>(lut_a[(aw[w] >> (8 * j)) & 0xff]) +
+                                                         static_cast<uint32_t>(lut_b[(bw[w] >> (8 * j)) & 0xff]));
                 if (PC)
                     r[k] = rescale_f2<DBL>(sum, __ldg(fm + c0 + k), __ldg(fsh + c0 + k), __ldg(fhz + c0 + k)) + add_zp;
                 else

@@ -45,15 +45,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait: spins until the phase with `parity` completes or the shared
-// abort flag (when given) is raised or `limit` clock cycles pass. Returns false when it
-// gave up (the caller then records ERR_TIMEOUT and unwinds).
+// try_wait that may suspend the thread until the phase completes, for at most about
+// `hint_ns` nanoseconds: a waiting warp then takes no issue slots from the warps that work.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: waits (suspended between checks) until the phase with `parity`
+// completes or the shared abort flag (when given) is raised or `limit` clock cycles
+// pass. Returns false when it gave up (the caller then records ERR_TIMEOUT and unwinds).
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                                   long long limit) {
     if (mbar_try_wait(bar, parity)) return true;
     long long t0 = clock64();
     while (true) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait_suspend(bar, parity, 20000u)) return true;
         if (abort_flag != nullptr && *abort_flag) return false;
         if (clock64() - t0 > limit) return false;
     }

@@ -160,7 +160,9 @@ struct GemmCfg {
     static constexpr int B_MN_CHUNK = 128 / kElem;                  // N elements per box
     static constexpr int B_MN_BOX_BYTES = BK * 128;                 // BK k-rows x 128 bytes
     static constexpr int TMEM_COLS = 2 * BN <= 32 ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
-    static constexpr int SCRATCH_BYTES = 12288;  // epilogue: column-sum reduction, staged per-tile column constants
+    // epilogue: column-sum reduction and staged per-tile column constants (12 KB), then a 2 KB
+    // output staging buffer per epilogue warp (16 KB)
+    static constexpr int SCRATCH_BYTES = 12288 + 16384;
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 2048 /*barriers, row sums*/ + SCRATCH_BYTES;
     static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "UMMA N for M=128; each epilogue half walks pairs of 16-column chunks");
     static_assert(!B_MN_MAJOR || BK_BYTES == 128, "MN-major B uses 128-byte K blocks");
@@ -185,7 +187,17 @@ __device__ __forceinline__ void tmem_wait_regs(uint32_t (&r)[16]) {
                    "+r"(r[15]));
 }
 
-constexpr int kChunk = 16;  // output columns per thread per TMEM load
+__device__ __forceinline__ void tmem_wait_regs(uint32_t (&r)[32]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                   "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                   "+r"(r[29]), "+r"(r[30]), "+r"(r[31]));
+}
+
+constexpr int kChunk = 16;   // output columns per thread per TMEM load (general epilogue)
+constexpr int kChunkF = 32;  // the same for the fast int8 RESCALE epilogue
 
 __device__ __forceinline__ uint32_t pack4_i8(int32_t a, int32_t b, int32_t c, int32_t d) {
     const uint32_t lo = __byte_perm(static_cast<uint32_t>(a), static_cast<uint32_t>(b), 0x0040);
@@ -194,6 +206,41 @@ __device__ __forceinline__ uint32_t pack4_i8(int32_t a, int32_t b, int32_t c, in
 }
 
 // Epilogue for kChunk consecutive output columns n0.. of one row (one thread).
+// v = acc + column terms (+ border-class delta) + row term, the zero-point and bias
+// terms of the integer contraction. colterm / delta are padded by the host to
+// whole tiles, so n0 + j needs no clamp.
+template <int W = kChunk>
+__device__ __forceinline__ void int_terms(const uint32_t (&acc)[W], int n0, int32_t rowterm,
+                                          const int32_t* colterm, const int32_t* delta, int32_t (&v)[W]) {
+    if (colterm != nullptr) {
+        // 16-byte loads of the column terms (tables are 16-byte aligned and padded to whole tiles)
+        // column terms staged in shared memory for the tile (16-byte loads)
+        const int4* ct4 = reinterpret_cast<const int4*>(colterm + n0);
+#pragma unroll
+        for (int j = 0; j < W; j += 4) {
+            const int4 c = ct4[j / 4];
+            v[j + 0] = static_cast<int32_t>(acc[j + 0] + static_cast<uint32_t>(c.x) + static_cast<uint32_t>(rowterm));
+            v[j + 1] = static_cast<int32_t>(acc[j + 1] + static_cast<uint32_t>(c.y) + static_cast<uint32_t>(rowterm));
+            v[j + 2] = static_cast<int32_t>(acc[j + 2] + static_cast<uint32_t>(c.z) + static_cast<uint32_t>(rowterm));
+            v[j + 3] = static_cast<int32_t>(acc[j + 3] + static_cast<uint32_t>(c.w) + static_cast<uint32_t>(rowterm));
+        }
+        if (delta != nullptr) {
+            const int4* d4 = reinterpret_cast<const int4*>(delta + n0);
+#pragma unroll
+            for (int j = 0; j < W; j += 4) {
+                const int4 c = __ldg(d4 + j / 4);
+                v[j + 0] = static_cast<int32_t>(static_cast<uint32_t>(v[j + 0]) + static_cast<uint32_t>(c.x));
+                v[j + 1] = static_cast<int32_t>(static_cast<uint32_t>(v[j + 1]) + static_cast<uint32_t>(c.y));
+                v[j + 2] = static_cast<int32_t>(static_cast<uint32_t>(v[j + 2]) + static_cast<uint32_t>(c.z));
+                v[j + 3] = static_cast<int32_t>(static_cast<uint32_t>(v[j + 3]) + static_cast<uint32_t>(c.w));
+            }
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < W; ++j) v[j] = static_cast<int32_t>(acc[j] + static_cast<uint32_t>(rowterm));
+    }
+}
+
 // Per-tensor fast RESCALE constants (channel 0) and the clamp decision, loaded once.
 struct FastConst {
     int32_t m, sh, hz, add_zp;
@@ -240,35 +287,8 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, const uint32
         }
         return;
     } else {
-    // colterm / delta are padded by the host to whole tiles, so n0 + j needs no clamp.
     int32_t v[kChunk];
-    if (colterm != nullptr) {
-        // 16-byte loads of the column terms (tables are 16-byte aligned and padded to whole tiles)
-        // column terms staged in shared memory for the tile (16-byte loads)
-        const int4* ct4 = reinterpret_cast<const int4*>(colterm + n0);
-#pragma unroll
-        for (int j = 0; j < kChunk; j += 4) {
-            const int4 c = ct4[j / 4];
-            v[j + 0] = static_cast<int32_t>(acc[j + 0] + static_cast<uint32_t>(c.x) + static_cast<uint32_t>(rowterm));
-            v[j + 1] = static_cast<int32_t>(acc[j + 1] + static_cast<uint32_t>(c.y) + static_cast<uint32_t>(rowterm));
-            v[j + 2] = static_cast<int32_t>(acc[j + 2] + static_cast<uint32_t>(c.z) + static_cast<uint32_t>(rowterm));
-            v[j + 3] = static_cast<int32_t>(acc[j + 3] + static_cast<uint32_t>(c.w) + static_cast<uint32_t>(rowterm));
-        }
-        if (delta != nullptr) {
-            const int4* d4 = reinterpret_cast<const int4*>(delta + n0);
-#pragma unroll
-            for (int j = 0; j < kChunk; j += 4) {
-                const int4 c = __ldg(d4 + j / 4);
-                v[j + 0] = static_cast<int32_t>(static_cast<uint32_t>(v[j + 0]) + static_cast<uint32_t>(c.x));
-                v[j + 1] = static_cast<int32_t>(static_cast<uint32_t>(v[j + 1]) + static_cast<uint32_t>(c.y));
-                v[j + 2] = static_cast<int32_t>(static_cast<uint32_t>(v[j + 2]) + static_cast<uint32_t>(c.z));
-                v[j + 3] = static_cast<int32_t>(static_cast<uint32_t>(v[j + 3]) + static_cast<uint32_t>(c.w));
-            }
-        }
-    } else {
-#pragma unroll
-        for (int j = 0; j < kChunk; ++j) v[j] = static_cast<int32_t>(acc[j] + static_cast<uint32_t>(rowterm));
-    }
+    int_terms(acc, n0, rowterm, colterm, delta, v);
     if constexpr (EK == EK_I32) {
         int32_t* o = reinterpret_cast<int32_t*>(outp) + orow + n0;
         if (ncols == kChunk && ((reinterpret_cast<uintptr_t>(o) & 15) == 0)) {
@@ -357,12 +377,57 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, const uint32
     }
 }
 
+// Fast int8 RESCALE of W consecutive columns, W/16 x 16 packed bytes into out16[].
+template <int EK, int W>
+__device__ __forceinline__ void fast_chunk_i8(const GemmParams& p, const uint32_t (&acc)[W], int n0, int32_t rowterm,
+                                              const int32_t* colterm, const int32_t* delta, const int32_t* fm,
+                                              const int32_t* fsh, const int32_t* fhz, const FastConst& fk,
+                                              uint4 (&out16)[W / 16]) {
+    constexpr bool PC = EK == EK_FAST_PC_S || EK == EK_FAST_PC_D;
+    constexpr bool DBL = EK == EK_FAST_T_D || EK == EK_FAST_PC_D;
+    int32_t v[W];
+    int_terms<W>(acc, n0, rowterm, colterm, delta, v);
+    if constexpr (PC) {
+#pragma unroll
+        for (int j = 0; j < W; j += 4) {
+            const int4 m4 = *reinterpret_cast<const int4*>(fm + n0 + j);
+            const int4 s4 = *reinterpret_cast<const int4*>(fsh + n0 + j);
+            const int4 h4 = *reinterpret_cast<const int4*>(fhz + n0 + j);
+            v[j + 0] = rescale_f2<DBL>(v[j + 0], m4.x, s4.x, h4.x);
+            v[j + 1] = rescale_f2<DBL>(v[j + 1], m4.y, s4.y, h4.y);
+            v[j + 2] = rescale_f2<DBL>(v[j + 2], m4.z, s4.z, h4.z);
+            v[j + 3] = rescale_f2<DBL>(v[j + 3], m4.w, s4.w, h4.w);
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < W; ++j) v[j] = rescale_f2<DBL>(v[j], fk.m, fk.sh, fk.hz);
+    }
+    if (fk.add_zp != 0) {
+#pragma unroll
+        for (int j = 0; j < W; ++j) v[j] += fk.add_zp;
+    }
+    if (fk.clamp) {
+        const RescaleArgs& r = p.epi.rs;
+#pragma unroll
+        for (int j = 0; j < W; ++j) v[j] = min(max(v[j], r.lo), r.hi);
+    }
+    // saturating packs complete the clamp to the int8 range
+#pragma unroll
+    for (int q = 0; q < W / 16; ++q)
+        out16[q] = make_uint4(pack4_sat_i8(v[16 * q + 0], v[16 * q + 1], v[16 * q + 2], v[16 * q + 3]),
+                              pack4_sat_i8(v[16 * q + 4], v[16 * q + 5], v[16 * q + 6], v[16 * q + 7]),
+                              pack4_sat_i8(v[16 * q + 8], v[16 * q + 9], v[16 * q + 10], v[16 * q + 11]),
+                              pack4_sat_i8(v[16 * q + 12], v[16 * q + 13], v[16 * q + 14], v[16 * q + 15]));
+}
+
 template <class Cfg, int EK>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
     constexpr int BM = Cfg::BM, BN = Cfg::kBN, S = Cfg::kStages;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // 1024-byte alignment by an offset into the shared array: pointer arithmetic on smem_raw keeps the
+    // shared address space visible to the compiler (shared loads/stores rather than generic ones).
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t* stage_base = smem;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::STAGE_BYTES);
     uint64_t* full = bars;               // [S]
@@ -688,6 +753,68 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 fk.add_zp = e.rs_zp_folded ? 0 : e.rs.out_zp;
                 fk.clamp = e.rs.lo > -128 || e.rs.hi < 127;
             }
+            if constexpr (EK >= EK_FAST_T_S && EK <= EK_FAST_PC_D) {
+                // int8 results pass through a per-warp shared buffer [32 rows][4 x 16 B] (16-byte slots
+                // swizzled by row) so that the global stores are row-contiguous: a warp writes 8 rows x
+                // 64 B per store instead of 32 scattered 16 B pieces.
+                uint4* wst = reinterpret_cast<uint4*>(scratch + 3072) + (warp - 4) * 128;
+                constexpr int GW = HALF < 64 ? HALF : 64;  // columns per staging group
+                constexpr int CPG = GW / kChunk;           // 16-byte slots per row and group: 2 or 4
+                int8_t* obase = reinterpret_cast<int8_t*>(p.out) + static_cast<long long>(b) * p.out_batch_stride;
+                const bool vec_ok = (p.ldo & 15) == 0 && (p.out_batch_stride & 15) == 0 &&
+                                    (reinterpret_cast<uintptr_t>(p.out) & 15) == 0;
+                const int mrow0 = mt * BM + q * 32;
+                const int swz = (lane >> 1) & 3;
+                uint32_t fA[kChunkF], fB[kChunkF];
+                __syncwarp();
+                tmem_ld_32x32b_x32(taddr, fA);
+                tmem_wait_regs(fA);
+#pragma unroll 1
+                for (int g0 = 0; g0 < HALF; g0 += GW) {
+                    uint4 pk[2];
+                    if constexpr (GW == 64) {
+                        __syncwarp();
+                        tmem_ld_32x32b_x32(taddr + g0 + kChunkF, fB);
+                        fast_chunk_i8<EK, kChunkF>(p, fA, nb + g0, rowterm, colterm, delta, fm, fsh, fhz, fk, pk);
+                        wst[lane * 4 + (0 ^ swz)] = pk[0];
+                        wst[lane * 4 + (1 ^ swz)] = pk[1];
+                        __syncwarp();
+                        tmem_wait_regs(fB);
+                        if (g0 + GW < HALF) tmem_ld_32x32b_x32(taddr + g0 + GW, fA);
+                        fast_chunk_i8<EK, kChunkF>(p, fB, nb + g0 + kChunkF, rowterm, colterm, delta, fm, fsh, fhz,
+                                                   fk, pk);
+                        wst[lane * 4 + (2 ^ swz)] = pk[0];
+                        wst[lane * 4 + (3 ^ swz)] = pk[1];
+                        __syncwarp();
+                        if (g0 + GW < HALF) tmem_wait_regs(fA);
+                    } else {
+                        fast_chunk_i8<EK, kChunkF>(p, fA, nb + g0, rowterm, colterm, delta, fm, fsh, fhz, fk, pk);
+                        wst[lane * 4 + (0 ^ swz)] = pk[0];
+                        wst[lane * 4 + (1 ^ swz)] = pk[1];
+                    }
+                    __syncwarp();
+#pragma unroll
+                    for (int it = 0; it < CPG; ++it) {
+                        const int idx = it * 32 + lane;
+                        const int r = idx / CPG, k = idx % CPG;
+                        const uint4 pk = wst[r * 4 + (k ^ ((r >> 1) & 3))];
+                        const int mr = mrow0 + r;
+                        const int n = nb + g0 + k * kChunk;
+                        if (mr < p.M && n < p.N) {
+                            int8_t* o = obase + static_cast<long long>(mr) * p.ldo + n;
+                            if (vec_ok && n + kChunk <= p.N) {
+                                *reinterpret_cast<uint4*>(o) = pk;
+                            } else {
+                                const uint32_t w4[4] = {pk.x, pk.y, pk.z, pk.w};
+#pragma unroll
+                                for (int j = 0; j < kChunk; ++j)
+                                    if (n + j < p.N) o[j] = static_cast<int8_t>(w4[j >> 2] >> (8 * (j & 3)));
+                            }
+                        }
+                    }
+                    __syncwarp();
+                }
+            } else {
             // Two register sets: the next chunk's TMEM load overlaps this chunk's epilogue.
             uint32_t accA[kChunk], accB[kChunk];
             __syncwarp();
@@ -710,6 +837,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                        err);
                 __syncwarp();
                 if (c0 + 2 * kChunk < HALF) tmem_wait_regs(accA);
+            }
             }
             tc_fence_before();
             __syncwarp();
