@@ -158,8 +158,19 @@ template <bool DBL>
 __device__ __forceinline__ int32_t rescale_f2(int32_t v, int32_t m, int32_t sh, int32_t hz) {
     int32_t h;
     if (DBL) {
-        const long long R = (static_cast<long long>(v >> 31) << 31) | 0x40000000ll;  // +2^30, or -2^30 for v < 0
-        h = static_cast<int32_t>((static_cast<long long>(v) * m + R) >> 32);
+        // R = +2^30, or -2^30 for v < 0, as the 64-bit pair {lo, hi}:
+        // hi = v >> 31 (sign), lo = (v & 2^31) ^ 2^30; then one wide multiply-add.
+        asm("{\n\t"
+            ".reg .b32 s, lo, dlo;\n\t"
+            ".reg .b64 r, t;\n\t"
+            "shr.s32 s, %1, 31;\n\t"
+            "lop3.b32 lo, %1, 0x80000000, 0x40000000, 0x6a;\n\t"
+            "mov.b64 r, {lo, s};\n\t"
+            "mad.wide.s32 t, %1, %2, r;\n\t"
+            "mov.b64 {dlo, %0}, t;\n\t"
+            "}"
+            : "=r"(h)
+            : "r"(v), "r"(m));
     } else {
         h = __mulhi(v, m);
     }

@@ -244,7 +244,9 @@ __device__ __forceinline__ void int_terms(const uint32_t (&acc)[W], int n0, int3
 // Per-tensor fast RESCALE constants (channel 0) and the clamp decision, loaded once.
 struct FastConst {
     int32_t m, sh, hz, add_zp;
-    bool clamp;  // the range is narrower than int8's (a fused CLAMP): saturation alone does not do it
+    bool clamp;     // the range is narrower than int8's (a fused CLAMP): saturation alone does not do it
+    bool clamp_lo;  // lower bound above -128
+    bool clamp_hi;  // upper bound below 127
 };
 
 template <int EK>
@@ -385,8 +387,28 @@ __device__ __forceinline__ void fast_chunk_i8(const GemmParams& p, const uint32_
                                               uint4 (&out16)[W / 16]) {
     constexpr bool PC = EK == EK_FAST_PC_S || EK == EK_FAST_PC_D;
     constexpr bool DBL = EK == EK_FAST_T_D || EK == EK_FAST_PC_D;
+    // v = acc + column term + row term (+ border-class delta); the column terms are always
+    // staged in shared memory here (zeros when the contraction has none)
     int32_t v[W];
-    int_terms<W>(acc, n0, rowterm, colterm, delta, v);
+#pragma unroll
+    for (int j = 0; j < W; j += 4) {
+        const int4 c = *reinterpret_cast<const int4*>(colterm + n0 + j);
+        v[j + 0] = static_cast<int32_t>(acc[j + 0] + static_cast<uint32_t>(c.x) + static_cast<uint32_t>(rowterm));
+        v[j + 1] = static_cast<int32_t>(acc[j + 1] + static_cast<uint32_t>(c.y) + static_cast<uint32_t>(rowterm));
+        v[j + 2] = static_cast<int32_t>(acc[j + 2] + static_cast<uint32_t>(c.z) + static_cast<uint32_t>(rowterm));
+        v[j + 3] = static_cast<int32_t>(acc[j + 3] + static_cast<uint32_t>(c.w) + static_cast<uint32_t>(rowterm));
+    }
+    if (delta != nullptr) {
+        const int4* d4 = reinterpret_cast<const int4*>(delta + n0);
+#pragma unroll
+        for (int j = 0; j < W; j += 4) {
+            const int4 c = __ldg(d4 + j / 4);
+            v[j + 0] = static_cast<int32_t>(static_cast<uint32_t>(v[j + 0]) + static_cast<uint32_t>(c.x));
+            v[j + 1] = static_cast<int32_t>(static_cast<uint32_t>(v[j + 1]) + static_cast<uint32_t>(c.y));
+            v[j + 2] = static_cast<int32_t>(static_cast<uint32_t>(v[j + 2]) + static_cast<uint32_t>(c.z));
+            v[j + 3] = static_cast<int32_t>(static_cast<uint32_t>(v[j + 3]) + static_cast<uint32_t>(c.w));
+        }
+    }
     if constexpr (PC) {
 #pragma unroll
         for (int j = 0; j < W; j += 4) {
@@ -406,10 +428,16 @@ __device__ __forceinline__ void fast_chunk_i8(const GemmParams& p, const uint32_
 #pragma unroll
         for (int j = 0; j < W; ++j) v[j] += fk.add_zp;
     }
-    if (fk.clamp) {
-        const RescaleArgs& r = p.epi.rs;
+    // a bound at the int8 limit is left to the saturating packs
+    if (fk.clamp_lo) {
+        const int32_t lo = p.epi.rs.lo;
 #pragma unroll
-        for (int j = 0; j < W; ++j) v[j] = min(max(v[j], r.lo), r.hi);
+        for (int j = 0; j < W; ++j) v[j] = max(v[j], lo);
+    }
+    if (fk.clamp_hi) {
+        const int32_t hi = p.epi.rs.hi;
+#pragma unroll
+        for (int j = 0; j < W; ++j) v[j] = min(v[j], hi);
     }
     // saturating packs complete the clamp to the int8 range
 #pragma unroll
@@ -684,11 +712,85 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         uint32_t tcount = 0;
         uint32_t err = 0;
         constexpr int HALF = BN / 2;
+        constexpr bool kFast = EK >= EK_FAST_T_S && EK <= EK_FAST_PC_D;
+        // Tile-invariant RESCALE constants (per-tensor values are channel 0's).
+        FastConst fk{0, 0, 0, 0, false, false, false};
+        if constexpr (kFast) {
+            fk.m = __ldg(e.fq_m);
+            fk.sh = __ldg(e.fq_sh);
+            fk.hz = __ldg(e.fq_hz);
+            fk.add_zp = e.rs_zp_folded ? 0 : e.rs.out_zp;
+            fk.clamp_lo = e.rs.lo > -128;
+            fk.clamp_hi = e.rs.hi < 127;
+            fk.clamp = fk.clamp_lo || fk.clamp_hi;
+        }
+        // Border-class tables of a convolution, copied to shared memory once (the column-sum
+        // reduction area is free when there is no column-sum job).
+        const uint8_t* rcls = e.rowclass;
+        const uint8_t* ccls = e.colclass;
+        if (e.rowclass != nullptr && p.cs.b == nullptr) {
+            const int oh = p.conv_OHOW / p.conv_OW, ow = p.conv_OW;
+            uint8_t* cl = reinterpret_cast<uint8_t*>(scratch);
+            if (oh + ow <= 4096) {
+                for (int i = et; i < oh; i += kEpiWarps * 32) cl[i] = e.rowclass[i];
+                for (int i = et; i < ow; i += kEpiWarps * 32) cl[oh + i] = e.colclass[i];
+                if (!epi_sync()) ok = false;
+                rcls = cl;
+                ccls = cl + oh;
+            }
+        }
+        // Column constants (column terms and per-channel multiplier, shift - 32, hz) of the
+        // current (batch, N tile) in shared memory; restaged only when the tile's batch or N
+        // block changes (tiles walk M fastest). Two buffers: a warp that runs ahead writes
+        // the other one; it cannot lap, as each staging ends in a barrier of all 8 warps.
+        // The fast path always stages (zero column terms when there are none), so its
+        // pointers are plain shared-memory pointers.
+        const bool stage_cols = kFast || kPC || e.colterm != nullptr;
+        int staged_key = -1;
+        int sbuf = 0;
         for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++tcount) {
             int b, mt, nt;
             tile_coords(p, tile, b, mt, nt);
             const int buf = tcount & 1;
             const uint32_t tph = (tcount >> 1) & 1;
+            const int key = b * p.n_tiles + nt;
+            if (stage_cols && key != staged_key) {
+                if (e.colterm != nullptr && p.cs.b != nullptr && staged_key < 0) {
+                    // all column sums published (bounded wait on the cross-CTA counter)
+                    const long long t0 = clock64();
+                    while (*reinterpret_cast<volatile unsigned int*>(p.cs.counter) < p.cs.target) {
+                        if (*abort_flag || clock64() - t0 > limit) { ok = false; break; }
+                    }
+                    __threadfence();
+                    if (!ok) break;
+                }
+                sbuf ^= 1;
+                int32_t* cst = ct_stage + sbuf * 1024;
+                // (the tables are padded to whole 256-column tiles)
+                if (et < BN) {
+                    const int n = nt * BN + et;
+                    cst[et] = e.colterm != nullptr ? e.colterm[b * e.colterm_bstride + n] : 0;
+                    if constexpr (kPC) {
+                        cst[256 + et] = __ldg(e.fq_m + n);
+                        cst[512 + et] = __ldg(e.fq_sh + n);
+                        cst[768 + et] = __ldg(e.fq_hz + n);
+                    }
+                }
+                if (!epi_sync()) { ok = false; break; }
+                staged_key = key;
+            }
+            // Pointers indexed by the absolute output column.
+            const int32_t* cst_n = ct_stage + sbuf * 1024 - nt * BN;
+            // Border class of this thread's row (before the accumulator wait: the lookups overlap it).
+            const int m = mt * BM + row;
+            const bool row_ok = m < p.M;
+            const int32_t* delta = nullptr;
+            if (rcls != nullptr && row_ok) {
+                const int rem = m % p.conv_OHOW;
+                const int oy = rem / p.conv_OW, ox = rem - oy * p.conv_OW;
+                const int cls = rcls[oy] * e.n_col_classes + ccls[ox];
+                if (cls != e.base_class) delta = e.ct_delta + static_cast<long long>(cls) * e.ct_ld;
+            }
             if (!mbar_wait_bounded(&tfull[buf], tph, abort_flag, limit)) { ok = false; break; }
             tc_fence_after();
             if (p.trace && blockIdx.x == 0 && tcount < 8 && threadIdx.x == 128) p.trace[384 + 2 * tcount] = clock64();
@@ -700,59 +802,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&rsempty[buf]);
             }
-            const int m = mt * BM + row;
-            const bool row_ok = m < p.M;
-            const int32_t* colterm = nullptr;
-            const int32_t *fm = nullptr, *fsh = nullptr, *fhz = nullptr;
-            if (e.colterm != nullptr || kPC) {
-                if (e.colterm != nullptr && p.cs.b != nullptr && tcount == 0) {
-                    // all column sums published (bounded wait on the cross-CTA counter)
-                    const long long t0 = clock64();
-                    while (*reinterpret_cast<volatile unsigned int*>(p.cs.counter) < p.cs.target) {
-                        if (*abort_flag || clock64() - t0 > limit) { ok = false; break; }
-                    }
-                    __threadfence();
-                    if (!ok) break;
-                }
-                // stage this tile's column constants in shared memory (the tables are padded to
-                // whole 256-column tiles)
-                int32_t* cst = ct_stage + (tcount & 1) * 1024;
-                if (et < BN) {
-                    const int n = nt * BN + et;
-                    if (e.colterm != nullptr) cst[et] = e.colterm[b * e.colterm_bstride + n];
-                    if constexpr (kPC) {
-                        cst[256 + et] = __ldg(e.fq_m + n);
-                        cst[512 + et] = __ldg(e.fq_sh + n);
-                        cst[768 + et] = __ldg(e.fq_hz + n);
-                    }
-                }
-                if (!epi_sync()) { ok = false; break; }
-                if (e.colterm != nullptr) colterm = cst - nt * BN;
-                fm = cst + 256 - nt * BN;
-                fsh = cst + 512 - nt * BN;
-                fhz = cst + 768 - nt * BN;
-            }
-            const int32_t* delta = nullptr;
-            if (e.rowclass != nullptr && row_ok) {
-                const int rem = m % p.conv_OHOW;
-                const int oy = rem / p.conv_OW, ox = rem % p.conv_OW;
-                const int cls = e.rowclass[oy] * e.n_col_classes + e.colclass[ox];
-                if (cls != e.base_class) delta = e.ct_delta + static_cast<long long>(cls) * e.ct_ld;
-            }
+            const int32_t* colterm = e.colterm != nullptr ? cst_n : nullptr;
+            const int32_t* fm = cst_n + 256;
+            const int32_t* fsh = cst_n + 512;
+            const int32_t* fhz = cst_n + 768;
             const int cbase = half * HALF;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                                    static_cast<uint32_t>(buf * BN + cbase);
             const long long orow = static_cast<long long>(b) * p.out_batch_stride + static_cast<long long>(m) * p.ldo;
             const int nb = nt * BN + cbase;
-            // Per-tensor rescale constants (channel 0), loaded once per tile.
-            FastConst fk{0, 0, 0, 0, false};
-            if constexpr (EK >= EK_FAST_T_S && EK <= EK_FAST_PC_D) {
-                fk.m = __ldg(e.fq_m);
-                fk.sh = __ldg(e.fq_sh);
-                fk.hz = __ldg(e.fq_hz);
-                fk.add_zp = e.rs_zp_folded ? 0 : e.rs.out_zp;
-                fk.clamp = e.rs.lo > -128 || e.rs.hi < 127;
-            }
             if constexpr (EK >= EK_FAST_T_S && EK <= EK_FAST_PC_D) {
                 // int8 results pass through a per-warp shared buffer [32 rows][4 x 16 B] (16-byte slots
                 // swizzled by row) so that the global stores are row-contiguous: a warp writes 8 rows x
@@ -775,20 +833,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     if constexpr (GW == 64) {
                         __syncwarp();
                         tmem_ld_32x32b_x32(taddr + g0 + kChunkF, fB);
-                        fast_chunk_i8<EK, kChunkF>(p, fA, nb + g0, rowterm, colterm, delta, fm, fsh, fhz, fk, pk);
+                        fast_chunk_i8<EK, kChunkF>(p, fA, nb + g0, rowterm, cst_n, delta, fm, fsh, fhz, fk, pk);
                         wst[lane * 4 + (0 ^ swz)] = pk[0];
                         wst[lane * 4 + (1 ^ swz)] = pk[1];
                         __syncwarp();
                         tmem_wait_regs(fB);
                         if (g0 + GW < HALF) tmem_ld_32x32b_x32(taddr + g0 + GW, fA);
-                        fast_chunk_i8<EK, kChunkF>(p, fB, nb + g0 + kChunkF, rowterm, colterm, delta, fm, fsh, fhz,
-                                                   fk, pk);
+                        fast_chunk_i8<EK, kChunkF>(p, fB, nb + g0 + kChunkF, rowterm, cst_n, delta, fm, fsh,
+                                                   fhz, fk, pk);
                         wst[lane * 4 + (2 ^ swz)] = pk[0];
                         wst[lane * 4 + (3 ^ swz)] = pk[1];
                         __syncwarp();
                         if (g0 + GW < HALF) tmem_wait_regs(fA);
                     } else {
-                        fast_chunk_i8<EK, kChunkF>(p, fA, nb + g0, rowterm, colterm, delta, fm, fsh, fhz, fk, pk);
+                        fast_chunk_i8<EK, kChunkF>(p, fA, nb + g0, rowterm, cst_n, delta, fm, fsh, fhz, fk, pk);
                         wst[lane * 4 + (0 ^ swz)] = pk[0];
                         wst[lane * 4 + (1 ^ swz)] = pk[1];
                     }
