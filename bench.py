@@ -4,17 +4,18 @@
 
 Workloads (synthetic seeded inputs of the stated shapes
 and distributions, random-init weights):
+  resnet50     (default) config 4: the ResNet-50-shaped int8 TOSA graph
+               (tosa_b200/graphs.py), 64 images per GPU, run by the graph runner
+               (one CUDA graph per step). Metric: images/s; the roofline line
+               reports the int8 TOPS of its tensor-core convolutions.
   matmul       config 2: batched int8 MATMUL A[8,1024,1024] x B[8,1024,1024], a/b
                zero points in [-8,8], fused RESCALE (single multiplier, shift 35,
                single_round) to int8. Metric: int8 TOPS (2*8*1024^3 ops per step).
-  resnet50     config 4: the ResNet-50-shaped int8 TOSA graph (tosa_b200/graphs.py),
-               64 images per GPU, run by the graph runner (one CUDA graph per
-               step). Metric: images/s.
   mobilenetv2  config 3: the MobileNetV2-shaped int8 graph, batch 64 per GPU.
 
 Multi-GPU (torchrun, one process per GPU): every rank runs its own shard of the
-workload (weak scaling; the batch shards are independent, no collective on the
-data path). Timing: W untimed warm-up steps; K timed steps, each bracketed by
+workload (weak scaling: 64 images per GPU, the global batch 64 x N; the shards
+are independent, no collective on the data path). Timing: W untimed warm-up steps; K timed steps, each bracketed by
 CUDA events on the launching stream with the L2 flushed (a 256 MiB write)
 between steps; barrier + synchronize around the timed region; the max over
 ranks of the summed step time. `e2e` repeats the measurement through the same
@@ -201,11 +202,14 @@ class GraphWorkload:
         self.batch = args.batch or self.batch
         self.data, self.info = self.builder(self.batch)
         self.units_per_step = self.batch
-        rng = np.random.default_rng(self.seed)
+        rank = int(os.environ.get("RANK", "0"))
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        rng = np.random.default_rng(self.seed + rank)  # this rank's shard of the global batch
         self.images = rng.integers(-128, 128, (self.batch, 224, 224, 3), dtype=np.int8)
 
     def config(self):
-        return {"workload": self.desc, "global_batch": self.batch, "batch_per_gpu": self.batch,
+        return {"workload": self.desc, "global_batch": self.batch * self.world, "batch_per_gpu": self.batch,
+                "parallelism": f"dp{self.world} (batch sharded, no collective on the data path)",
                 "int_ops_per_image": self.info["ops_per_image"],
                 "l2": "flushed between timed steps (256 MiB write); activations exceed L2"}
 
@@ -458,6 +462,7 @@ def run_gpu(args, wl):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     from tosa_b200 import _lib as L
+    from tosa_b200 import parallel as P
 
     ctx = L.Context(local)
     stream = torch.cuda.Stream()
@@ -487,11 +492,7 @@ def run_gpu(args, wl):
             e.record(stream)
             evs.append((s, e))
         barrier()
-        ms = sum(s.elapsed_time(e) for s, e in evs)
-        if ws > 1:
-            t = torch.tensor([ms], device="cuda")
-            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-            ms = float(t.item())
+        ms = P.max_over_ranks(sum(s.elapsed_time(e) for s, e in evs))
         return ms, launches
 
     def soak(seconds):
@@ -564,7 +565,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="matmul", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="resnet50", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="tosa_b200", choices=["tosa_b200", "reference"])
     ap.add_argument("--batch", type=int, default=0, help="images per GPU for the graph workloads (default 64)")
     ap.add_argument("--cpu-rows", type=int, default=1536, help="rows of the single-thread CPU baseline sample")

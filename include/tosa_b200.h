@@ -140,6 +140,14 @@ typedef struct tb_matmul_plan tb_matmul_plan;
 TB_API tb_status tb_matmul_plan_create(tb_context *ctx, const tb_matmul_desc *desc, const tb_rescale_attr *rescale,
                                        tb_matmul_plan **out);
 TB_API tb_status tb_matmul_plan_run(tb_matmul_plan *plan, const void *a, const void *b, void *out, void *stream);
+/* Declares `b` (device) constant for this plan, as a MATMUL whose B operand is a
+ * CONST tensor of the graph: its column sums (the a_zp term) and, when its rows
+ * need it, its 16-byte-padded copy are computed now, once; later runs with this
+ * same pointer reuse them (a run with another B discards them). The data must
+ * not change while the plan is used with it. Returns after the work on `stream`
+ * finished. No-op for plans that keep nothing per B (float, direct and
+ * zero-a_zp unpadded paths). */
+TB_API tb_status tb_matmul_plan_set_constant_b(tb_matmul_plan *plan, const void *b, void *stream);
 TB_API void tb_matmul_plan_destroy(tb_matmul_plan *plan);
 TB_API tb_status tb_matmul(tb_context *ctx, const tb_matmul_desc *desc, const tb_rescale_attr *rescale,
                            const void *a, const void *b, void *out, void *stream);

@@ -111,6 +111,41 @@ def test_matmul_int8_padded_b_fused_rescale(ctx):
     assert rc == 0 and np.array_equal(got.reshape(-1).astype(np.int64), exp)
 
 
+@pytest.mark.parametrize("w", [256, 1000])
+def test_matmul_int8_constant_b(ctx, w):
+    """A plan told that B is constant (graph CONST weights) keeps B's column terms
+    (and padded rows): runs with that B are exact, a run with another B computes
+    its own (and discards the kept ones), and B is prepared again afterwards."""
+    import ctypes
+    rng = np.random.default_rng(w)
+    n, h, c = 1, 64, 512
+    a = rng.integers(-128, 128, (n, h, c), dtype=np.int64)
+    bs = [rng.integers(-128, 128, (n, c, w), dtype=np.int64) for _ in range(2)]
+    mult = rng.integers(1 << 30, (1 << 31) - 1, w)
+    shift = rng.integers(33, 40, w)
+    attr = L.rescale_attr(mult, shift, rounding=L.ROUND_DOUBLE, output_zp=4, out_dtype=L.DT_INT8)
+    za, zb = -5, 3
+    d = L.MatmulDesc(n=n, h=h, c=c, w=w, a_dtype=L.DT_INT8, b_dtype=L.DT_INT8, out_dtype=L.DT_INT32, a_zp=za, b_zp=zb)
+    plan = ctypes.c_void_p()
+    L.check(L.load().tb_matmul_plan_create(ctx.h, d, attr, ctypes.byref(plan)))
+    try:
+        ta = torch.from_numpy(a.astype(np.int8)).cuda()
+        tb = [torch.from_numpy(b.astype(np.int8)).cuda() for b in bs]
+        out = torch.empty((n, h, w), dtype=torch.int8, device="cuda")
+        L.check(L.load().tb_matmul_plan_set_constant_b(plan, L.ptr(tb[0]), L.stream_ptr()))
+        for k in (0, 0, 1, 0, -1, 0):
+            if k < 0:
+                L.check(L.load().tb_matmul_plan_set_constant_b(plan, L.ptr(tb[0]), L.stream_ptr()))
+                continue
+            L.check(L.load().tb_matmul_plan_run(plan, L.ptr(ta), L.ptr(tb[k]), L.ptr(out), L.stream_ptr()))
+            ctx.synchronize()
+            acc = H.oracle_matmul_int(a, bs[k], za, zb)
+            rc, exp = H.oracle_rescale(acc, L.DT_INT32, L.DT_INT8, mult, shift, 0, 4, 1, L.ROUND_DOUBLE, 1)
+            assert rc == 0 and np.array_equal(out.cpu().numpy().reshape(-1).astype(np.int64), exp), k
+    finally:
+        L.load().tb_matmul_plan_destroy(plan)
+
+
 def test_matmul_int8_rescale_small_shift_checks(ctx):
     """Shifts below 32 take the checked epilogue: in-range values are exact,
     out-of-range values are reported as GraphError (quant.rs:21-25)."""
@@ -347,6 +382,8 @@ POOL_CASES = [
     (2, 7, 7, 48, (7, 7), (1, 1), (0, 0, 0, 0)),     # global pool
     (1, 9, 10, 12, (3, 2), (1, 2), (1, 0, 0, 0)),    # 4 channels per thread
     (1, 6, 5, 7, (2, 3), (2, 1), (0, 0, 1, 1)),      # scalar
+    (1, 8, 8, 4096, (3, 3), (1, 1), (1, 1, 1, 1)),   # 256 channel groups: one pixel per block
+    (2, 10, 10, 32, (8, 8), (2, 2), (3, 3, 3, 3)),   # 64 taps (the widest 16-bit-lane window), borders
 ]
 
 
@@ -375,7 +412,7 @@ def test_pool2d_int8(ctx, case):
     out = torch.empty((n, g.oh, g.ow, c), dtype=torch.int8, device="cuda")
     xi = np.ascontiguousarray(x, np.int64)
     p = lambda a: a.ctypes.data_as(C.c_void_p)  # noqa: E731
-    for zi, zo in ((0, 0), (-7, 5)):
+    for zi, zo in ((0, 0), (-7, 5), (-128, 127), (127, -128)):
         d = _pool_desc(n, ih, iw, c, kernel, stride, pad, L.DT_INT8, zi, zo)
         L.check(L.load().tb_avg_pool2d(ctx.h, d, L.ptr(tx), L.ptr(out), L.stream_ptr()))
         ctx.synchronize()

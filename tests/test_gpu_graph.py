@@ -296,6 +296,35 @@ def _oracle_run(data, inputs):
     return O.run_block(block, ins)
 
 
+@pytest.mark.parametrize("rounding", ["SINGLE_ROUND", "DOUBLE_ROUND"])
+@pytest.mark.parametrize("clamp", [None, "relu", (-20, 90)])
+def test_residual_chain_int8(ctx, rounding, clamp):
+    """The fused residual chain (two int8 -> int32 RESCALEs, ADD, int32 -> int8
+    RESCALE, optional CLAMP) against the oracle, both roundings of the output RESCALE."""
+    from tosa_b200 import graphs
+    g = graphs.GraphBuilder(5, 2)
+    shape = [2, 12, 10, 48]
+    x = g.input("x", shape)
+    y = g.input("y", shape)
+    q, _ = g.residual(x, -3, y, 6, relu=clamp == "relu", clamp=None if clamp in (None, "relu") else clamp,
+                      rounding=rounding)
+    g.outputs.append(q)
+    data = g.build()
+    block = O.read_graph(data).main_block
+    rng = np.random.default_rng(3)
+    inputs = {nm: I.Tensor.from_numpy(nm, rng.integers(-128, 128, shape).astype(np.int8), block.tensor(nm).dtype)
+              for nm in block.inputs}
+    want = _oracle_run(data, inputs)
+    it = I.Interpreter(data, context=ctx)
+    try:
+        got = it.run(inputs)
+        assert it.last_launches == 1  # the whole chain in one kernel
+    finally:
+        it.close()
+    for nm in block.outputs:
+        assert np.array_equal(np.asarray(got[nm].data).astype(np.int64).reshape(-1), want[nm].values)
+
+
 @pytest.mark.parametrize("name", ["residual", "mobilenetv2", "resnet50"])
 @pytest.mark.parametrize("mode", ["fused", "unfused", "cuda_graph"])
 def test_synthetic_int8_graph_bit_exact(ctx, name, mode):
@@ -328,3 +357,28 @@ def test_synthetic_int8_graph_bit_exact(ctx, name, mode):
         assert got[nm].shape == want[nm].shape
         bad = np.nonzero(g != want[nm].values)[0]
         assert bad.size == 0, f"{nm}: {bad.size}/{g.size} differ, first at {bad[:5]}"
+
+
+def test_sharded_interpreter_matches_whole_batch():
+    """ShardedInterpreter: the batch split over two replicas (two GPUs when the
+    box has them, else two contexts on one), one host thread each; the gathered
+    outputs equal the oracle's whole-batch run bit for bit."""
+    from tosa_b200 import graphs
+    from tosa_b200 import parallel as P
+    devices = [0, 1] if torch.cuda.device_count() >= 2 else [0, 0]
+    per, world = 2, 2
+    data1, _ = graphs.residual_block_int8(batch=per)
+    dataw, _ = graphs.residual_block_int8(batch=per * world)
+    rng = np.random.default_rng(9)
+    x = rng.integers(-128, 128, (per * world, 14, 14, 64)).astype(np.int8)
+    inputs = {"x": I.Tensor.from_numpy("x", x, L.DT_INT8)}
+    want = _oracle_run(dataw, inputs)
+    si = P.ShardedInterpreter(data1, devices)
+    try:
+        for _ in range(2):
+            got = si.run(inputs)
+            for nm, w in want.items():
+                assert got[nm].shape == w.shape, nm
+                assert np.array_equal(np.asarray(got[nm].data).astype(np.int64).reshape(-1), w.values), nm
+    finally:
+        si.close()

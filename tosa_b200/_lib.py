@@ -111,6 +111,7 @@ SIGNATURES = [
     ("tb_debug_trace", _I, [_V, _P(ctypes.c_longlong)]),
     ("tb_matmul_plan_create", _I, [_V, _P(MatmulDesc), _P(RescaleAttr), _P(_V)]),
     ("tb_matmul_plan_run", _I, [_V, _V, _V, _V, _V]),
+    ("tb_matmul_plan_set_constant_b", _I, [_V, _V, _V]),
     ("tb_matmul_plan_destroy", None, [_V]),
     ("tb_matmul", _I, [_V, _P(MatmulDesc), _P(RescaleAttr), _V, _V, _V, _V]),
     ("tb_matmul_i8_noalloc", _I, [_P(MatmulDesc), _P(RescaleAttr), _V, _V, _V, _V]),

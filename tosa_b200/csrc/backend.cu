@@ -457,10 +457,15 @@ extern "C" TB_API tb_status tb_matmul_plan_run(tb_matmul_plan* p, const void* a,
     const long long total = static_cast<long long>(d.n) * d.h * d.w;
     if (total == 0) return TB_OK;
     const void* b_tma = b;
+    const bool b_prepared = p->b_const != nullptr && b == p->b_const;  // column terms / padded rows kept
+    // another B overwrites the kept buffers below: the constant one must be prepared again
+    if (!b_prepared) p->b_const = nullptr;
     if (p->path == 5 && aligned16(a)) {
-        pad_weight_rows_i8<<<grid_for(ctx, static_cast<long long>(d.n) * d.c * p->wp), 256, 0, st>>>(
-            d.n * d.c, d.w, p->wp, static_cast<const int8_t*>(b), p->d_bpad);
-        TB_LAUNCHED(ctx);
+        if (!b_prepared) {
+            pad_weight_rows_i8<<<grid_for(ctx, static_cast<long long>(d.n) * d.c * p->wp), 256, 0, st>>>(
+                d.n * d.c, d.w, p->wp, static_cast<const int8_t*>(b), p->d_bpad);
+            TB_LAUNCHED(ctx);
+        }
         b_tma = p->d_bpad;
     } else if (p->path >= 2 || !aligned16(a) || !aligned16(b)) {
         if (d.a_dtype == TB_DT_INT8) {
@@ -506,7 +511,10 @@ extern "C" TB_API tb_status tb_matmul_plan_run(tb_matmul_plan* p, const void* a,
     gp.ldo = d.w;
     GemmEpilogue& ep = gp.epi;
     if (p->path == 0 || p->path == 5) {
-        if (d.a_zp != 0) {
+        if (d.a_zp != 0 && b_prepared) {
+            ep.colterm = p->d_colterm;
+            ep.colterm_bstride = d.w;
+        } else if (d.a_zp != 0) {
             // colterm = -a_zp * colsum(B) + c * a_zp * b_zp, reduced inside the GEMM by the epilogue warps
             // during the first main loop (cooperative launch; see ColsumJob).
             const int32_t cst = static_cast<int32_t>(static_cast<uint32_t>(d.c) * static_cast<uint32_t>(d.a_zp) *
@@ -549,6 +557,33 @@ extern "C" TB_API tb_status tb_matmul_plan_run(tb_matmul_plan* p, const void* a,
     ep.mode = EPI_F32;
     ep.out_dtype = TB_DT_FP32;
     return launch_f16_matmul(ctx, p->bn, p->tmA, p->tmB, gp, st);
+}
+
+extern "C" TB_API tb_status tb_matmul_plan_set_constant_b(tb_matmul_plan* p, const void* b, void* stream_) {
+    if (!p || !b) return fail(TB_ERR_INVALID_ARGUMENT, "null argument");
+    tb_context* ctx = p->ctx;
+    const tb_matmul_desc& d = p->d;
+    p->b_const = nullptr;
+    if (!(p->path == 0 || p->path == 5) || (p->path == 0 && d.a_zp == 0)) return TB_OK;
+    TB_CUDA(cudaSetDevice(ctx->device));
+    cudaStream_t st = static_cast<cudaStream_t>(stream_);
+    if (static_cast<long long>(d.n) * d.c * d.w == 0) return TB_OK;
+    if (p->path == 5) {
+        pad_weight_rows_i8<<<grid_for(ctx, static_cast<long long>(d.n) * d.c * p->wp), 256, 0, st>>>(
+            d.n * d.c, d.w, p->wp, static_cast<const int8_t*>(b), p->d_bpad);
+        TB_LAUNCHED(ctx);
+    }
+    if (d.a_zp != 0) {
+        // colterm = -a_zp * colsum(B) + c * a_zp * b_zp (the in-GEMM column-sum job's values)
+        const int32_t add = static_cast<int32_t>(static_cast<uint32_t>(d.c) * static_cast<uint32_t>(d.a_zp) *
+                                                 static_cast<uint32_t>(d.b_zp));
+        colterm_const_i8<<<dim3((d.w + 31) / 32, d.n), dim3(32, 8), 0, st>>>(d.c, d.w, static_cast<const int8_t*>(b),
+                                                                            -d.a_zp, add, p->d_colterm);
+        TB_LAUNCHED(ctx);
+    }
+    TB_CUDA(cudaStreamSynchronize(st));
+    p->b_const = b;
+    return TB_OK;
 }
 
 extern "C" TB_API void tb_matmul_plan_destroy(tb_matmul_plan* p) {
@@ -1161,7 +1196,8 @@ extern "C" TB_API tb_status tb_avg_pool2d(tb_context* ctx, const tb_pool2d_desc*
     if (total == 0) return TB_OK;
     if (!input || !out) return fail(TB_ERR_INVALID_ARGUMENT, "null argument");
     cudaStream_t st = static_cast<cudaStream_t>(stream_);
-    if (dt == TB_DT_INT8 && g.c % 16 == 0 && aligned16(input) && aligned16(out) && total / 16 < (1ll << 31)) {
+    if (dt == TB_DT_INT8 && g.c % 16 == 0 && aligned16(input) && aligned16(out) && g.kx * g.ky <= 64 &&
+        g.oh <= 65535 && g.n <= 65535) {
         static RecipTable table = [] {
             RecipTable t{};
             for (int c = 1; c <= 64; ++c) {  // reciprocal_scale (src/ops/quant.rs:6-11)
@@ -1173,9 +1209,15 @@ extern "C" TB_API tb_status tb_avg_pool2d(tb_context* ctx, const tb_pool2d_desc*
             }
             return t;
         }();
-        avg_pool_i8_vec16<<<grid_for(ctx, total / 16), 256, 0, st>>>(g, static_cast<const int8_t*>(input),
-                                                                    d->input_zp, d->output_zp, table,
-                                                                    static_cast<int8_t*>(out), ctx->dev_err);
+        const PoolTile pt = pool_tile(g.c, g.ow);
+        const dim3 grid((g.ow + pt.ppb - 1) / pt.ppb, g.oh, g.n);
+        // taps one at a time for small windows (occupancy hides latency), eight in flight for wide ones
+        if (g.kx >= 6)
+            avg_pool_i8_vec16<8><<<grid, pool_block(pt), 0, st>>>(g, pt, static_cast<const int8_t*>(input), d->input_zp,
+                                                                  d->output_zp, table, static_cast<int8_t*>(out));
+        else
+            avg_pool_i8_vec16<1><<<grid, pool_block(pt), 0, st>>>(g, pt, static_cast<const int8_t*>(input), d->input_zp,
+                                                                  d->output_zp, table, static_cast<int8_t*>(out));
     } else if (dt == TB_DT_INT8 && g.c % 4 == 0 && aligned16(input))
         avg_pool_i8_vec4<<<grid_for(ctx, total / 4), 256, 0, st>>>(g, static_cast<const int8_t*>(input), d->input_zp,
                                                                   d->output_zp, static_cast<int8_t*>(out), ctx->dev_err);
@@ -1202,9 +1244,16 @@ extern "C" TB_API tb_status tb_max_pool2d(tb_context* ctx, const tb_pool2d_desc*
         return fail(TB_ERR_DTYPE_MISMATCH, "MAX_POOL2D: unsupported dtype %d", dt);
     if (total == 0) return TB_OK;
     if (!input || !out) return fail(TB_ERR_INVALID_ARGUMENT, "null argument");
-    if (dt == TB_DT_INT8 && g.c % 16 == 0 && aligned16(input) && aligned16(out) && total / 16 < (1ll << 31))
-        max_pool_i8_vec16<<<grid_for(ctx, total / 16), 256, 0, st>>>(g, static_cast<const int8_t*>(input),
-                                                                    static_cast<int8_t*>(out));
+    if (dt == TB_DT_INT8 && g.c % 16 == 0 && aligned16(input) && aligned16(out) && g.oh <= 65535 && g.n <= 65535) {
+        const PoolTile pt = pool_tile(g.c, g.ow);
+        const dim3 grid((g.ow + pt.ppb - 1) / pt.ppb, g.oh, g.n);
+        if (g.kx >= 6)
+            max_pool_i8_vec16<8><<<grid, pool_block(pt), 0, st>>>(g, pt, static_cast<const int8_t*>(input),
+                                                                  static_cast<int8_t*>(out));
+        else
+            max_pool_i8_vec16<1><<<grid, pool_block(pt), 0, st>>>(g, pt, static_cast<const int8_t*>(input),
+                                                                  static_cast<int8_t*>(out));
+    }
     else if (dt == TB_DT_INT8 && g.c % 4 == 0 && aligned16(input))
         max_pool_i8_vec4<<<grid_for(ctx, total / 4), 256, 0, st>>>(g, static_cast<const int8_t*>(input),
                                                                   static_cast<int8_t*>(out));

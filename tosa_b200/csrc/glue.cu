@@ -182,40 +182,42 @@ __global__ void residual_chain(const void* __restrict__ a, int a_dt, int a_uns, 
     if (lerr) atomicOr(err, lerr);
 }
 
-__device__ __forceinline__ int32_t sext8(uint32_t word, int j) {
-    return static_cast<int32_t>(static_cast<int8_t>(static_cast<uint8_t>(word >> (8 * j))));
-}
-
 __device__ __forceinline__ int32_t small_rescale(int32_t x, int32_t m, int s, long long rpos, long long rneg) {
     return static_cast<int32_t>((static_cast<long long>(x) * m + (x >= 0 ? rpos : rneg)) >> s);
 }
 
-// Residual chain, int8 in and out, 16 elements per thread. The two input
-// RESCALEs are functions of one int8 value each: every block tabulates them
-// (256 int32 entries apiece, indexed by the input byte, error-free constants of
-// ResidualFast) in shared memory. The output RESCALE uses the fast-path arrays
-// (every shift in [33, 62], multiplier >= 0), as the GEMM epilogue does;
-// saturating packs and the fused CLAMP finish the range.
-template <bool PC, bool DBL>
+// Residual chain, int8 in and out, 16 elements per thread and step. The two input
+// RESCALEs are functions of one int8 value each, tabulated per block in shared
+// memory (error-free constants of ResidualFast): entry e (the input byte) holds
+// 32 copies of table a's value then 32 copies of table b's, 256 bytes per entry, so
+// lane l reads word l of the copies (bank l, conflict-free) at the byte address
+// e * 256 + [128] + 4 l, which one byte permute builds from the input word. The
+// output RESCALE uses the fast-path arrays (every shift in [33, 62], multiplier
+// >= 0), as the GEMM epilogue does; saturating packs and the fused CLAMP finish
+// the range. Two steps are loaded before either is processed (more bytes in flight).
+constexpr int kResidLutBytes = 256 * 256;
+
+template <bool PC, bool DBL, bool SMALL>
 __global__ void __launch_bounds__(256) residual_fast_i8(const uint4* __restrict__ a, const uint4* __restrict__ b,
                                                         ResidualFast f, const int32_t* __restrict__ fm,
                                                         const int32_t* __restrict__ fsh,
                                                         const int32_t* __restrict__ fhz, int32_t lo, int32_t hi,
                                                         int32_t add_zp, long long n16, int channels,
                                                         uint4* __restrict__ out) {
-    __shared__ int32_t lut_a[256], lut_b[256];
-    {
-        const int u = threadIdx.x;  // blockDim.x == 256: one table entry per thread
-        const int32_t v = static_cast<int8_t>(static_cast<uint8_t>(u));
-        lut_a[u] = small_rescale(v - f.za, f.ma, f.sa, f.ra_pos, f.ra_neg);
-        lut_b[u] = small_rescale(v - f.zb, f.mb, f.sb, f.rb_pos, f.rb_neg);
+    extern __shared__ __align__(16) int32_t lut[];  // [256 entries][a x 32 | b x 32]
+    for (int i = threadIdx.x; i < 256 * 32; i += blockDim.x) {
+        const int e = i >> 5, c = i & 31;
+        const int32_t v = static_cast<int8_t>(static_cast<uint8_t>(e));
+        const int ks = SMALL ? f.k : 0;  // small-range path: values pre-shifted (no overflow by the host's bound)
+        lut[e * 64 + c] = static_cast<int32_t>(static_cast<uint32_t>(small_rescale(v - f.za, f.ma, f.sa, f.ra_pos, f.ra_neg)) << ks);
+        lut[e * 64 + 32 + c] = static_cast<int32_t>(static_cast<uint32_t>(small_rescale(v - f.zb, f.mb, f.sb, f.rb_pos, f.rb_neg)) << ks);
     }
     __syncthreads();
+    const char* lut_b8 = reinterpret_cast<const char*>(lut);
+    const uint32_t la = (threadIdx.x & 31) * 4u, lb = la + 128u;
     const int32_t m0 = __ldg(fm), sh0 = __ldg(fsh), hz0 = __ldg(fhz);
-    const bool clamp = lo > -128 || hi < 127;
-    for (long long q = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; q < n16;
-         q += static_cast<long long>(gridDim.x) * blockDim.x) {
-        const uint4 av = __ldg(a + q), bv = __ldg(b + q);
+    const bool clamp_lo = lo > -128, clamp_hi = hi < 127;
+    auto step = [&](long long q, const uint4& av, const uint4& bv) {
         const uint32_t aw[4] = {av.x, av.y, av.z, av.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
         const int c0 = PC ? static_cast<int>((static_cast<unsigned long long>(q) << 4) % static_cast<unsigned>(channels))
                           : 0;
@@ -225,23 +227,44 @@ __global__ void __launch_bounds__(256) residual_fast_i8(const uint4* __restrict_
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const int k = 4 * w + j;
-                const int32_t sum = static_cast<int32_t>(static_cast<uint32_t>(lut_a[(aw[w] >> (8 * j)) & 0xff]) +
-                                                         static_cast<uint32_t>(lut_b[(bw[w] >> (8 * j)) & 0xff]));
-                if (PC)
+                // byte 0 = the lane's word offset, byte 1 = the input byte (the entry), bytes 2-3 = 0
+                const uint32_t sel = 0x5504u | (static_cast<uint32_t>(j) << 4);
+                const int32_t ta = *reinterpret_cast<const int32_t*>(lut_b8 + __byte_perm(aw[w], la, sel));
+                const int32_t tb = *reinterpret_cast<const int32_t*>(lut_b8 + __byte_perm(bw[w], lb, sel));
+                const int32_t sum = static_cast<int32_t>(static_cast<uint32_t>(ta) + static_cast<uint32_t>(tb));
+                if (SMALL) {
+                    int32_t x = f.oc;
+                    if (DBL) x += (sum >> 31) * f.ok2;  // -2^(31-d) for a negative sum
+                    int32_t h;
+                    asm("mad.hi.s32 %0, %1, %2, %3;" : "=r"(h) : "r"(sum), "r"(f.om), "r"(x));
+                    r[k] = (h >> f.osh) + f.ozp_add;
+                } else if (PC) {
                     r[k] = rescale_f2<DBL>(sum, __ldg(fm + c0 + k), __ldg(fsh + c0 + k), __ldg(fhz + c0 + k)) + add_zp;
-                else
+                } else {
                     r[k] = rescale_f2<DBL>(sum, m0, sh0, hz0) + add_zp;
-                if (clamp) r[k] = min(max(r[k], lo), hi);
+                }
+                if (clamp_lo) r[k] = max(r[k], lo);
+                if (clamp_hi) r[k] = min(r[k], hi);
             }
         }
         out[q] = make_uint4(pack4_sat_i8(r[0], r[1], r[2], r[3]), pack4_sat_i8(r[4], r[5], r[6], r[7]),
                             pack4_sat_i8(r[8], r[9], r[10], r[11]), pack4_sat_i8(r[12], r[13], r[14], r[15]));
+    };
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    long long q = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+    for (; q + stride < n16; q += 2 * stride) {
+        const uint4 a0 = __ldg(a + q), b0 = __ldg(b + q);
+        const uint4 a1 = __ldg(a + q + stride), b1 = __ldg(b + q + stride);
+        step(q, a0, b0);
+        step(q + stride, a1, b1);
     }
+    if (q < n16) step(q, __ldg(a + q), __ldg(b + q));
 }
 
 }  // namespace
 
-void residual_fast_constants(const tb_rescale_attr& a, int a_dt, const tb_rescale_attr& b, int b_dt, ResidualFast* f) {
+void residual_fast_constants(const tb_rescale_attr& a, int a_dt, const tb_rescale_attr& b, int b_dt,
+                             const tb_rescale_attr& o, ResidualFast* f) {
     f->ok = false;
     auto one = [](const tb_rescale_attr& r, int dt, int32_t* m, int32_t* z, int32_t* s, long long* rp,
                   long long* rn) {
@@ -268,6 +291,46 @@ void residual_fast_constants(const tb_rescale_attr& a, int a_dt, const tb_rescal
     };
     f->ok = one(a, a_dt, &f->ma, &f->za, &f->sa, &f->ra_pos, &f->ra_neg) &&
             one(b, b_dt, &f->mb, &f->zb, &f->sb, &f->rb_pos, &f->rb_neg);
+    f->small = false;
+    if (!f->ok) return;
+    // small-range output path: per-tensor int32 -> int8, scale32, shift in [33, 62]
+    if (!o.scale32 || o.per_channel || o.channels != 1 || o.input_unsigned || o.output_unsigned ||
+        o.out_dtype != TB_DT_INT8 || o.rounding_mode == TB_ROUND_INEXACT || o.input_zp != 0)
+        return;
+    const long long om = o.multiplier[0];
+    const int os = o.shift[0];
+    if (om < 0 || os < 33 || os > 62) return;
+    auto host_rescale = [](long long x, long long m, int s, long long rp, long long rn) {
+        return (x * m + (x >= 0 ? rp : rn)) >> s;
+    };
+    long long amax = 0, bmax = 0;
+    for (int e = 0; e < 256; ++e) {
+        const long long v = static_cast<int8_t>(static_cast<uint8_t>(e));
+        amax = std::max(amax, std::llabs(host_rescale(v - f->za, f->ma, f->sa, f->ra_pos, f->ra_neg)));
+        bmax = std::max(bmax, std::llabs(host_rescale(v - f->zb, f->mb, f->sb, f->rb_pos, f->rb_neg)));
+    }
+    const long long bound = std::max(amax + bmax, 1ll);
+    int k = 0;
+    while (k < 30 && (bound << (k + 1)) <= 2147483647ll) ++k;
+    const bool dbl = o.rounding_mode == TB_ROUND_DOUBLE;
+    const int d = 32 - k;
+    if ((dbl && k < 2) || os - 1 < d) return;
+    const long long k2 = dbl ? (1ll << (31 - d)) : 0;
+    long long c = (1ll << (os - 1 - d)) + (dbl ? (1ll << (30 - d)) : 0);
+    long long zp_add = o.output_zp;
+    if (std::llabs(c + static_cast<long long>(o.output_zp) * (1ll << (os - d))) + k2 < (1ll << 30)) {
+        c += static_cast<long long>(o.output_zp) * (1ll << (os - d));
+        zp_add = 0;
+    }
+    // |mulhi| <= 2^30 and |oc| + ok2 < 2^30 keep the sum in int32
+    if (std::llabs(c) + k2 >= (1ll << 30)) return;
+    f->small = true;
+    f->k = k;
+    f->om = static_cast<int32_t>(om);
+    f->osh = os - d;
+    f->oc = static_cast<int32_t>(c);
+    f->ok2 = static_cast<int32_t>(k2);
+    f->ozp_add = static_cast<int32_t>(zp_add);
 }
 
 tb_status launch_transpose(tb_context* ctx, const void* in, void* out, int elem, long long total, int rank,
@@ -308,20 +371,32 @@ tb_status launch_residual(tb_context* ctx, const void* a, int a_dt, int a_uns, i
         aligned16(a) && aligned16(b) && aligned16(out)) {
         const long long n16 = count / 16;
         const int32_t add_zp = ro.zp_folded ? 0 : ro.out_zp;
-        const int grid = grid_for(ctx, n16);
+        // persistent: three 64 KB-table blocks per SM, each thread two 16-element steps per pass
+        const int grid = static_cast<int>(std::min<long long>((n16 + 511) / 512, 3ll * ctx->num_sms));
         const bool dbl = ro.rounding == TB_ROUND_DOUBLE;
         auto A = static_cast<const uint4*>(a);
         auto B = static_cast<const uint4*>(b);
         auto O = static_cast<uint4*>(out);
-#define TB_RESID(PC, DBL)                                                                                      \
-    residual_fast_i8<PC, DBL><<<grid, 256, 0, st>>>(A, B, fast, ro.fq_m, ro.fq_sh, ro.fq_hz, ro.lo, ro.hi, add_zp, \
-                                                    n16, channels, O)
+#define TB_RESID(PC, DBL, SMALL)                                                                                  \
+    do {                                                                                                     \
+        static bool attr_set = false;                                                                        \
+        if (!attr_set) {                                                                                     \
+            TB_CUDA(cudaFuncSetAttribute(residual_fast_i8<PC, DBL, SMALL>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                         kResidLutBytes));                                                   \
+            attr_set = true;                                                                                 \
+        }                                                                                                    \
+        residual_fast_i8<PC, DBL, SMALL><<<grid, 256, kResidLutBytes, st>>>(A, B, fast, ro.fq_m, ro.fq_sh, ro.fq_hz, \
+                                                                            ro.lo, ro.hi, add_zp, n16, channels, O); \
+    } while (0)
         if (ro.per_channel) {
-            if (dbl) TB_RESID(true, true);
-            else TB_RESID(true, false);
+            if (dbl) TB_RESID(true, true, false);
+            else TB_RESID(true, false, false);
+        } else if (fast.small) {
+            if (dbl) TB_RESID(false, true, true);
+            else TB_RESID(false, false, true);
         } else {
-            if (dbl) TB_RESID(false, true);
-            else TB_RESID(false, false);
+            if (dbl) TB_RESID(false, true, false);
+            else TB_RESID(false, false, false);
         }
 #undef TB_RESID
         TB_LAUNCHED(ctx);

@@ -129,9 +129,18 @@ struct ResidualFast {
     bool ok = false;
     int32_t ma = 0, za = 0, sa = 0, mb = 0, zb = 0, sb = 0;
     long long ra_pos = 0, ra_neg = 0, rb_pos = 0, rb_neg = 0;
+    // Small-range output RESCALE (per-tensor, shift in [33, 62]): every table value is
+    // pre-shifted by k (|a| + |b| < 2^(31-k)), so sum' = sum * 2^k, and with d = 32 - k
+    // r = (mulhi(sum', om) + oc [- ok2 when sum' < 0, double rounding]) >> osh [+ ozp_add],
+    // oc = 2^(s-1-d) [+ 2^(30-d)] [+ zp * 2^(s-d)], ok2 = 2^(31-d), osh = s - d.
+    bool small = false;
+    int k = 0;
+    int32_t om = 0, osh = 0, oc = 0, ok2 = 0, ozp_add = 0;
 };
-// Fills `f` from host copies of the two RESCALE attributes (int8 inputs, int32 outputs).
-void residual_fast_constants(const tb_rescale_attr& a, int a_dt, const tb_rescale_attr& b, int b_dt, ResidualFast* f);
+// Fills `f` from host copies of the two input RESCALE attributes (int8 inputs, int32
+// outputs) and of the output RESCALE (int32 -> int8).
+void residual_fast_constants(const tb_rescale_attr& a, int a_dt, const tb_rescale_attr& b, int b_dt,
+                             const tb_rescale_attr& o, ResidualFast* f);
 tb_status launch_residual(tb_context* ctx, const void* a, int a_dt, int a_uns, int32_t za, const RescalePlan& ra,
                           const void* b, int b_dt, int b_uns, int32_t zb, const RescalePlan& rb,
                           const RescalePlan& ro, const ResidualFast& fast, long long count, int channels, void* out,
@@ -158,5 +167,6 @@ struct tb_matmul_plan {
     int8_t* d_bpad = nullptr;  // path 5: [n][c][wp] copy of B
     const void* a_cached = nullptr;
     const void* b_cached = nullptr;
+    const void* b_const = nullptr;  // B declared constant: d_colterm / d_bpad hold its column terms / padded rows
     CUtensorMap tmA, tmB;
 };

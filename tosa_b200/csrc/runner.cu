@@ -1143,6 +1143,8 @@ tb_status do_compile(tb_graph* G) {
         case K_MATMUL:
             st = tb_matmul_plan_create(ctx, &s.mdesc, s.has_rescale ? &s.rattr : nullptr, &s.mm);
             if (st == TB_OK) s.mm->replayable = (G->flags & TB_GRAPH_CUDA_GRAPH) != 0;
+            if (st == TB_OK && G->tensors[s.in[1]].is_static && G->tensors[s.in[1]].dev != nullptr)
+                st = tb_matmul_plan_set_constant_b(s.mm, G->tensors[s.in[1]].dev, nullptr);  // e.g. FC weights
             break;
         case K_RESCALE:
             st = make_rescale_plan(ctx, &s.rattr, s.in_dtype, s.channels, &s.rs);
@@ -1153,7 +1155,7 @@ tb_status do_compile(tb_graph* G) {
             st = make_rescale_plan(ctx, &a.rattr, a.in_dtype, a.channels, &s.ra);
             if (st == TB_OK) st = make_rescale_plan(ctx, &bb.rattr, bb.in_dtype, bb.channels, &s.rb);
             if (st == TB_OK) st = make_rescale_plan(ctx, &s.rattr, TB_DT_INT32, s.channels, &s.rs);
-            residual_fast_constants(a.rattr, a.in_dtype, bb.rattr, bb.in_dtype, &s.rfast);
+            residual_fast_constants(a.rattr, a.in_dtype, bb.rattr, bb.in_dtype, s.rattr, &s.rfast);
             break;
         }
         default: break;

@@ -200,6 +200,27 @@ __global__ void pad_weight_rows_i8(int oc, int k, int kp, const int8_t* __restri
     }
 }
 
+// Column terms of a constant MATMUL B [n][c][w]: out[bn][x] = scale * sum_c B[bn][c][x] + add
+// (int32 wrap-around, as the in-GEMM column-sum job). Block (32, 8): 32 columns, 8 row
+// slices reduced in shared memory; grid (ceil(w / 32), n).
+__global__ void colterm_const_i8(int c, int w, const int8_t* __restrict__ b, int32_t scale, int32_t add,
+                                 int32_t* __restrict__ out) {
+    __shared__ int32_t part[8][33];
+    const int x = blockIdx.x * 32 + threadIdx.x, bn = blockIdx.y;
+    int32_t sum = 0;
+    if (x < w)
+        for (int k = threadIdx.y; k < c; k += 8) sum += b[(static_cast<long long>(bn) * c + k) * w + x];
+    part[threadIdx.y][threadIdx.x] = sum;
+    __syncthreads();
+    if (threadIdx.y == 0 && x < w) {
+        int32_t t = 0;
+#pragma unroll
+        for (int r = 0; r < 8; ++r) t += part[r][threadIdx.x];
+        out[static_cast<long long>(bn) * w + x] =
+            static_cast<int32_t>(static_cast<uint32_t>(scale) * static_cast<uint32_t>(t) + static_cast<uint32_t>(add));
+    }
+}
+
 // INT16 x INT8 -> INT48 (AccI64, src/ops/accum.rs:43-56): int64 accumulation,
 // bias added with wrap-around, then clamped to 48 bits (src/ops/conv.rs:466-470).
 // INT48 values are stored as int64. depthwise: weight [KH,KW,C,M].

@@ -128,87 +128,133 @@ struct RecipTable {
     int32_t s[65];
 };
 
-// int8, C % 16 == 0, fewer than 2^31 output vectors: sixteen channels per thread
-// (16-byte loads), 32-bit index arithmetic, the reciprocal from the table.
-__global__ void avg_pool_i8_vec16(PoolGeomDev g, const int8_t* __restrict__ x, int32_t zi, int32_t zo,
-                                  RecipTable rt, int8_t* out, uint32_t* err) {
-    const int cg = g.c >> 4;
-    const int total = g.n * g.oh * g.ow * cg;
-    uint32_t lerr = 0;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
-        const int c16 = (i % cg) * 16;
-        int r = i / cg;
-        const int ox = r % g.ow;
-        r /= g.ow;
-        const int oy = r % g.oh;
-        const int b = r / g.oh;
-        const int iy0 = oy * g.sy - g.pad_t, ix0 = ox * g.sx - g.pad_l;
-        uint32_t acc[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) acc[j] = 0;
-        int count = 0;
-        for (int ky = 0; ky < g.ky; ++ky) {
-            const int y = iy0 + ky;
-            if (y < 0 || y >= g.ih) continue;
-            for (int kx = 0; kx < g.kx; ++kx) {
-                const int xx = ix0 + kx;
-                if (xx < 0 || xx >= g.iw) continue;
-                const uint4 v = __ldg(reinterpret_cast<const uint4*>(
-                    x + ((static_cast<long long>(b) * g.ih + y) * g.iw + xx) * g.c + c16));
-                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                for (int j = 0; j < 16; ++j)
-                    acc[j] += static_cast<uint32_t>(static_cast<int32_t>(static_cast<int8_t>(w[j >> 2] >> (8 * (j & 3)))) - zi);
-                ++count;
-            }
-        }
-        int32_t m, sh;
-        if (count <= 64) {
-            m = rt.m[count];
-            sh = rt.s[count];
-        } else {
-            reciprocal_scale_dev(count, &m, &sh);
-        }
-        uint32_t o[4] = {0, 0, 0, 0};
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            const int32_t q = static_cast<int32_t>(
-                rescale_value(static_cast<int32_t>(acc[j]), m, sh, ROUND_SINGLE, 1, zo, -128, 127, &lerr));
-            o[j >> 2] |= static_cast<uint32_t>(static_cast<uint8_t>(q)) << (8 * (j & 3));
-        }
-        reinterpret_cast<uint4*>(out)[i] = make_uint4(o[0], o[1], o[2], o[3]);
-    }
-    if (lerr) atomicOr(err, lerr);
+// int8 pooling, C % 16 == 0: sixteen channels (one 16-byte word) per work item. A block
+// covers ppb = max(1, 256 / (C/16)) consecutive output pixels of one output row:
+// grid (ceil(OW / ppb), OH, N), so pixel coordinates come from the block index.
+struct PoolTile {
+    int cg;   // 16-channel groups per pixel
+    int ppb;  // output pixels per block
+};
+
+__host__ __device__ inline PoolTile pool_tile(int c, int ow) {
+    const int cg = c >> 4;
+    const int ppb = cg >= 256 ? 1 : 256 / cg;
+    return PoolTile{cg, ppb < ow ? ppb : ow};
 }
 
-// int8, C % 16 == 0, fewer than 2^31 output vectors: byte-wise signed max of 16-byte words.
-__global__ void max_pool_i8_vec16(PoolGeomDev g, const int8_t* __restrict__ x, int8_t* out) {
-    const int cg = g.c >> 4;
-    const int total = g.n * g.oh * g.ow * cg;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
-        const int c16 = (i % cg) * 16;
-        int r = i / cg;
-        const int ox = r % g.ow;
-        r /= g.ow;
-        const int oy = r % g.oh;
-        const int b = r / g.oh;
-        const int iy0 = oy * g.sy - g.pad_t, ix0 = ox * g.sx - g.pad_l;
-        uint4 m = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);
-        for (int ky = 0; ky < g.ky; ++ky) {
-            const int y = iy0 + ky;
-            if (y < 0 || y >= g.ih) continue;
-            for (int kx = 0; kx < g.kx; ++kx) {
-                const int xx = ix0 + kx;
-                if (xx < 0 || xx >= g.iw) continue;
-                const uint4 v = __ldg(reinterpret_cast<const uint4*>(
-                    x + ((static_cast<long long>(b) * g.ih + y) * g.iw + xx) * g.c + c16));
-                m.x = __vmaxs4(m.x, v.x);
-                m.y = __vmaxs4(m.y, v.y);
-                m.z = __vmaxs4(m.z, v.z);
-                m.w = __vmaxs4(m.w, v.w);
+// Threads of a pooling block: the tile's work items rounded up to whole warps, at most 256.
+__host__ __device__ inline int pool_block(const PoolTile& pt) {
+    const int items = pt.ppb * pt.cg;
+    return items >= 256 ? 256 : (items + 31) / 32 * 32;
+}
+
+// AVG_POOL2D int8 with at most 64 taps: the window is summed as biased bytes (x + 128)
+// in 16-bit lanes of 32-bit registers (at most 64 * 255 per lane, no carry between
+// lanes), and sum(x - zi) = sum(x + 128) - count * (128 + zi). apply_scale_32 with
+// single rounding of |sum| < 2^14 by the reciprocal (m, s = 30 + k), exactly:
+// floor((sum * m + 2^(s-1)) / 2^s) + zo = (mulhi(sum * 2^16, m) + 2^(s-17) + zo * 2^(s-16))
+// >> (s - 16), the inner floor division being exact for whole multiples; no
+// apply_scale_32 range check can fail for these inputs. Saturating packs give the int8 clamp.
+template <int BATCH>
+__global__ void avg_pool_i8_vec16(PoolGeomDev g, PoolTile pt, const int8_t* __restrict__ x, int32_t zi, int32_t zo,
+                                  RecipTable rt, int8_t* out) {
+    const int oy = blockIdx.y, b = blockIdx.z;
+    const int iy0 = oy * g.sy - g.pad_t;
+    const int ky0 = max(0, -iy0), ky1 = min(g.ky, g.ih - iy0);
+    for (int item = threadIdx.x; item < pt.ppb * pt.cg; item += blockDim.x) {
+        const int px = item / pt.cg, c16 = (item - px * pt.cg) * 16;
+        const int ox = blockIdx.x * pt.ppb + px;
+        if (ox >= g.ow) break;
+        const int ix0 = ox * g.sx - g.pad_l;
+        const int kx0 = max(0, -ix0), kx1 = min(g.kx, g.iw - ix0);
+        uint32_t lo[4] = {0, 0, 0, 0}, hi[4] = {0, 0, 0, 0};
+        for (int ky = ky0; ky < ky1; ++ky) {
+            const uint4* row = reinterpret_cast<const uint4*>(
+                x + ((static_cast<long long>(b) * g.ih + iy0 + ky) * g.iw + ix0) * g.c + c16);
+            for (int kb = kx0; kb < kx1; kb += BATCH) {
+                uint4 v[BATCH];  // BATCH taps of the row in flight (wide windows over few outputs)
+#pragma unroll
+                for (int j = 0; j < BATCH; ++j)
+                    if (kb + j < kx1) v[j] = __ldg(row + static_cast<long long>(kb + j) * pt.cg);
+#pragma unroll
+                for (int j = 0; j < BATCH; ++j) {
+                    if (kb + j >= kx1) break;
+                    const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        lo[q] += (w[q] ^ 0x80808080u) & 0x00ff00ffu;
+                        hi[q] += ((w[q] >> 8) ^ 0x00808080u) & 0x00ff00ffu;
+                    }
+                }
             }
         }
-        reinterpret_cast<uint4*>(out)[i] = m;
+        const int count = (ky1 - ky0) * (kx1 - kx0);
+        if (count <= 0) break;  // cannot happen for a valid geometry (pads smaller than the kernel)
+        const int32_t m = rt.m[count], sh = rt.s[count] - 16;
+        const int32_t bias16 = count * (128 + zi) * 65536;
+        const int32_t cst = (1 << (sh - 1)) + zo * (1 << sh);
+        int32_t r[16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int32_t s0 = static_cast<int32_t>(lo[q] << 16) - bias16;          // byte 0
+            const int32_t s2 = static_cast<int32_t>(lo[q] & 0xffff0000u) - bias16;  // byte 2
+            const int32_t s1 = static_cast<int32_t>(hi[q] << 16) - bias16;          // byte 1
+            const int32_t s3 = static_cast<int32_t>(hi[q] & 0xffff0000u) - bias16;  // byte 3
+            r[4 * q + 0] = (__mulhi(s0, m) + cst) >> sh;
+            r[4 * q + 1] = (__mulhi(s1, m) + cst) >> sh;
+            r[4 * q + 2] = (__mulhi(s2, m) + cst) >> sh;
+            r[4 * q + 3] = (__mulhi(s3, m) + cst) >> sh;
+        }
+        reinterpret_cast<uint4*>(out)[((static_cast<long long>(b) * g.oh + oy) * g.ow + ox) * pt.cg + (c16 >> 4)] =
+            make_uint4(pack4_sat_i8(r[0], r[1], r[2], r[3]), pack4_sat_i8(r[4], r[5], r[6], r[7]),
+                       pack4_sat_i8(r[8], r[9], r[10], r[11]), pack4_sat_i8(r[12], r[13], r[14], r[15]));
+    }
+}
+
+__device__ __forceinline__ uint32_t max_u16x2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("max.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+// MAX_POOL2D int8, C % 16 == 0 (same tiling): the bytes, biased to unsigned (x + 128),
+// are split into even and odd bytes held in 16-bit lanes, and the lanes take packed
+// unsigned 16-bit maxima; the bytes are rejoined and unbiased at the end.
+template <int BATCH>
+__global__ void max_pool_i8_vec16(PoolGeomDev g, PoolTile pt, const int8_t* __restrict__ x, int8_t* out) {
+    const int oy = blockIdx.y, b = blockIdx.z;
+    const int iy0 = oy * g.sy - g.pad_t;
+    const int ky0 = max(0, -iy0), ky1 = min(g.ky, g.ih - iy0);
+    for (int item = threadIdx.x; item < pt.ppb * pt.cg; item += blockDim.x) {
+        const int px = item / pt.cg, c16 = (item - px * pt.cg) * 16;
+        const int ox = blockIdx.x * pt.ppb + px;
+        if (ox >= g.ow) break;
+        const int ix0 = ox * g.sx - g.pad_l;
+        const int kx0 = max(0, -ix0), kx1 = min(g.kx, g.iw - ix0);
+        uint32_t lo[4] = {0, 0, 0, 0}, hi[4] = {0, 0, 0, 0};  // biased -128
+        for (int ky = ky0; ky < ky1; ++ky) {
+            const uint4* row = reinterpret_cast<const uint4*>(
+                x + ((static_cast<long long>(b) * g.ih + iy0 + ky) * g.iw + ix0) * g.c + c16);
+            for (int kb = kx0; kb < kx1; kb += BATCH) {
+                uint4 v[BATCH];  // BATCH taps of the row in flight (wide windows over few outputs)
+#pragma unroll
+                for (int j = 0; j < BATCH; ++j)
+                    if (kb + j < kx1) v[j] = __ldg(row + static_cast<long long>(kb + j) * pt.cg);
+#pragma unroll
+                for (int j = 0; j < BATCH; ++j) {
+                    if (kb + j >= kx1) break;
+                    const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        lo[q] = max_u16x2(lo[q], (w[q] ^ 0x80808080u) & 0x00ff00ffu);
+                        hi[q] = max_u16x2(hi[q], ((w[q] >> 8) ^ 0x00808080u) & 0x00ff00ffu);
+                    }
+                }
+            }
+        }
+        reinterpret_cast<uint4*>(out)[((static_cast<long long>(b) * g.oh + oy) * g.ow + ox) * pt.cg + (c16 >> 4)] =
+            make_uint4((lo[0] | (hi[0] << 8)) ^ 0x80808080u, (lo[1] | (hi[1] << 8)) ^ 0x80808080u,
+                       (lo[2] | (hi[2] << 8)) ^ 0x80808080u, (lo[3] | (hi[3] << 8)) ^ 0x80808080u);
     }
 }
 

@@ -205,7 +205,7 @@ class GraphBuilder:
             q = self.clamp(q, lo, hi)
         return q, out_zp
 
-    def residual(self, a, a_zp, b, b_zp, relu=True, clamp=None):
+    def residual(self, a, a_zp, b, b_zp, relu=True, clamp=None, rounding="DOUBLE_ROUND"):
         """RESCALE(a), RESCALE(b) to int32 -> ADD -> RESCALE to int8 [-> CLAMP]."""
         ra = self.rescale(a, a_zp, D["INT32"], 0, 2.0 ** 10, per_channel=False, rounding="SINGLE_ROUND")
         rb = self.rescale(b, b_zp, D["INT32"], 0, 2.0 ** 10 * 0.9, per_channel=False, rounding="SINGLE_ROUND")
@@ -216,7 +216,7 @@ class GraphBuilder:
         out_zp = self.zp()
         centre = self.sh[s].mean(axis=(0, 1))
         spread = max(float(np.sqrt(((self.sh[s] - centre) ** 2).mean() + (centre ** 2).mean())), 1.0)
-        q = self.rescale(s, 0, D["INT8"], out_zp, 24.0 / spread, per_channel=False)
+        q = self.rescale(s, 0, D["INT8"], out_zp, 24.0 / spread, per_channel=False, rounding=rounding)
         if relu or clamp is not None:
             lo, hi = clamp if clamp is not None else (out_zp, 127)
             q = self.clamp(q, lo, hi)
