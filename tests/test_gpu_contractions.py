@@ -243,10 +243,17 @@ CONV_CASES = [
     (2, 15, 15, 64, 128, 1, 1, (0, 0, 0, 0), (2, 2), (1, 1), -8, 8),
     (1, 13, 13, 16, 64, 5, 5, (2, 2, 2, 2), (2, 2), (1, 1), 4, -4),
     (1, 7, 7, 256, 320, 3, 3, (1, 1, 1, 1), (1, 1), (1, 1), 0, 0),
+    (1, 5, 200, 16, 32, 3, 3, (1, 1, 1, 1), (1, 1), (1, 1), 3, -2),     # wide rows
+    (2, 23, 19, 48, 64, 3, 3, (1, 1, 1, 1), (1, 1), (1, 1), -7, 2),     # odd extents, a partial last tile
+    (3, 31, 29, 32, 48, 1, 1, (0, 0, 0, 0), (2, 2), (1, 1), 11, 0),     # strided 1x1
     # few input channels: im2col rows + 1x1 tensor-core convolution (RGB stems)
     (4, 64, 64, 3, 64, 7, 7, (2, 3, 2, 3), (2, 2), (1, 1), -5, 3),
     (3, 96, 80, 3, 32, 3, 3, (0, 1, 0, 1), (2, 2), (1, 1), 6, 0),
+    (8, 57, 45, 3, 64, 7, 7, (2, 2, 2, 2), (2, 2), (1, 1), 127, -128),   # odd input extents
+    (11, 40, 40, 4, 32, 5, 5, (2, 1, 2, 1), (2, 2), (1, 1), -128, 5),
+    (5, 64, 66, 1, 16, 4, 4, (0, 0, 2, 2), (2, 2), (1, 1), 9, -7),      # even kernel, one channel
     (1, 72, 72, 4, 48, 5, 5, (2, 2, 1, 3), (1, 1), (1, 2), -128, -2),
+    (7, 50, 50, 3, 32, 7, 7, (3, 2, 3, 2), (2, 2), (1, 1), 2, 1),       # odd pads
 ]
 
 

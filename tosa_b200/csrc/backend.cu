@@ -962,9 +962,18 @@ extern "C" TB_API tb_status tb_conv2d_plan_run(tb_conv2d_plan* p, const void* in
         const long long m_rows = static_cast<long long>(d.n) * p->oh * p->ow;
         const int threads = 128;
         long long blocks = (m_rows + threads - 1) / threads;
-        blocks = std::min<long long>(blocks, static_cast<long long>(ctx->num_sms) * 16);
-        im2col_rows_i8<<<static_cast<int>(blocks), threads, static_cast<size_t>(threads) * p->kp, st>>>(
-            g, static_cast<const int8_t*>(input), d.kh * d.kw * d.ic, p->kp, static_cast<int8_t>(d.input_zp), p->d_rows);
+        blocks = std::min<long long>(blocks, static_cast<long long>(ctx->num_sms) * 64);
+        const size_t smem = static_cast<size_t>(threads) * p->kp;
+        auto x = static_cast<const int8_t*>(input);
+        const int8_t zx = static_cast<int8_t>(d.input_zp);
+        const int bl = static_cast<int>(blocks);
+        // unrolled taps for the common stem shapes (3 or 4 channels, filter rows of 3, 5 or 7)
+#define TB_IM2COL(IC_, KW_) \
+    else if (d.ic == IC_ && d.kw == KW_) im2col_rows_i8_t<IC_, KW_><<<bl, threads, smem, st>>>(g, x, p->kp, zx, p->d_rows)
+        if (false) {}
+        TB_IM2COL(3, 7); TB_IM2COL(3, 5); TB_IM2COL(3, 3); TB_IM2COL(4, 7); TB_IM2COL(4, 5); TB_IM2COL(4, 3);
+        else im2col_rows_i8<<<bl, threads, smem, st>>>(g, x, d.kh * d.kw * d.ic, p->kp, zx, p->d_rows);
+#undef TB_IM2COL
         TB_LAUNCHED(ctx);
         return tb_conv2d_plan_run(p->inner, p->d_rows, out, stream_);
     }

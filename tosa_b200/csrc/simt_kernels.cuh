@@ -200,6 +200,60 @@ __global__ void pad_weight_rows_i8(int oc, int k, int kp, const int8_t* __restri
     }
 }
 
+// The same rows for the common stems, with the tap loops unrolled (IC channels,
+// KW taps per filter row known at compile time): a thread's IC * KW loads of a
+// filter row are independent and in flight together; rows are assembled in
+// shared memory (IC * KW bytes per filter row, kp bytes per output pixel) and
+// written out by the block with 16-byte stores.
+template <int IC, int KW>
+__global__ void __launch_bounds__(128) im2col_rows_i8_t(ConvGeomDev g, const int8_t* __restrict__ x, int kp, int8_t zx,
+                                                         int8_t* __restrict__ rows) {
+    extern __shared__ __align__(16) int8_t srow[];
+    const long long m_total = static_cast<long long>(g.n) * g.oh * g.ow;
+    const int chunks = kp >> 4;
+    const int kfull = g.kh * KW * IC;
+    for (long long m0 = static_cast<long long>(blockIdx.x) * blockDim.x; m0 < m_total;
+         m0 += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long m = m0 + threadIdx.x;
+        int8_t* my = srow + threadIdx.x * kp;
+        if (m < m_total) {
+            const int ox = static_cast<int>(m % g.ow);
+            const long long r = m / g.ow;
+            const int oy = static_cast<int>(r % g.oh);
+            const int b = static_cast<int>(r / g.oh);
+            const int8_t* xb = x + static_cast<long long>(b) * g.ih * g.iw * IC;
+            const int x0 = ox * g.sw - g.pad_l;
+            bool xok[KW];
+#pragma unroll
+            for (int kx = 0; kx < KW; ++kx) {
+                const int xx = x0 + kx * g.dw;
+                xok[kx] = xx >= 0 && xx < g.iw;
+            }
+            for (int ky = 0; ky < g.kh; ++ky) {
+                const int y = oy * g.sh + ky * g.dh - g.pad_t;
+                const bool yok = y >= 0 && y < g.ih;
+                const int8_t* src = xb + (static_cast<long long>(y) * g.iw + x0) * IC;
+                int8_t v[KW * IC];
+#pragma unroll
+                for (int kx = 0; kx < KW; ++kx)
+#pragma unroll
+                    for (int c = 0; c < IC; ++c)
+                        v[kx * IC + c] = (yok && xok[kx]) ? __ldg(src + kx * g.dw * IC + c) : zx;
+#pragma unroll
+                for (int j = 0; j < KW * IC; ++j) my[ky * KW * IC + j] = v[j];
+            }
+            for (int k = kfull; k < kp; ++k) my[k] = zx;
+        }
+        __syncthreads();
+        const long long rows_here = m_total - m0 < blockDim.x ? m_total - m0 : blockDim.x;
+        const int vecs = static_cast<int>(rows_here) * chunks;
+        uint4* dst = reinterpret_cast<uint4*>(rows + m0 * kp);
+        const uint4* s4 = reinterpret_cast<const uint4*>(srow);
+        for (int v = threadIdx.x; v < vecs; v += blockDim.x) dst[v] = s4[v];
+        __syncthreads();
+    }
+}
+
 // Column terms of a constant MATMUL B [n][c][w]: out[bn][x] = scale * sum_c B[bn][c][x] + add
 // (int32 wrap-around, as the in-GEMM column-sum job). Block (32, 8): 32 columns, 8 row
 // slices reduced in shared memory; grid (ceil(w / 32), n).
