@@ -636,6 +636,7 @@ struct tb_conv2d_plan {
     int8_t* d_rows = nullptr;       // [n*oh*ow][kp]
     int8_t* d_wpad = nullptr;       // [oc][kp]
     int kp = 0;
+    int segp = 0;                   // path 8: bytes per filter-row segment of a row (KW * IC rounded up to words)
 };
 
 static tb_status conv_extent(const char* op, int in, int pb, int pa, int k, int dil, int stride, int* out) {
@@ -762,15 +763,19 @@ static tb_status conv_plan_create(tb_context* ctx, const tb_conv2d_desc* d, cons
     // tensor-core convolution when the contraction is long enough to pay for the rows.
     const long long kfull = taps * d->ic;
     const long long m_rows = static_cast<long long>(d->n) * oh * ow;
+    // rows of KH segments (one per filter row, KW * IC bytes padded to whole words)
+    const int seg = d->kw * d->ic, segp = (seg + 3) / 4 * 4;
+    const long long kpad = (static_cast<long long>(d->kh) * segp + 15) / 16 * 16;
     if (p->path == 2 && wt == TB_DT_INT8 && kfull >= 16 && m_rows >= 4096 && aligned16(weight) &&
-        m_rows * ((kfull + 15) / 16 * 16) <= (4ll << 30) && kfull <= 384) {
+        m_rows * kpad <= (4ll << 30) && kpad <= 384) {
         p->path = 8;
-        p->kp = static_cast<int>((kfull + 15) / 16 * 16);
+        p->kp = static_cast<int>(kpad);
+        p->segp = segp;
         cudaError_t ce = cudaMalloc(&p->d_rows, static_cast<size_t>(m_rows) * p->kp);
         if (ce == cudaSuccess) ce = cudaMalloc(&p->d_wpad, static_cast<size_t>(oc) * p->kp);
         if (ce != cudaSuccess) return bail(fail(TB_ERR_CUDA, "im2col buffer allocation failed: %s", cudaGetErrorString(ce)));
-        pad_weight_rows_i8<<<grid_for(ctx, static_cast<long long>(oc) * p->kp), 256>>>(
-            oc, static_cast<int>(kfull), p->kp, static_cast<const int8_t*>(weight), p->d_wpad);
+        pad_weight_segments_i8<<<grid_for(ctx, static_cast<long long>(oc) * p->kp), 256>>>(
+            oc, d->kh, seg, segp, p->kp, static_cast<const int8_t*>(weight), p->d_wpad);
         ce = cudaGetLastError();
         if (ce == cudaSuccess) ce = cudaDeviceSynchronize();
         if (ce != cudaSuccess) return bail(fail(TB_ERR_CUDA, "weight padding failed: %s", cudaGetErrorString(ce)));
@@ -968,11 +973,13 @@ extern "C" TB_API tb_status tb_conv2d_plan_run(tb_conv2d_plan* p, const void* in
         const int8_t zx = static_cast<int8_t>(d.input_zp);
         const int bl = static_cast<int>(blocks);
         // unrolled taps for the common stem shapes (3 or 4 channels, filter rows of 3, 5 or 7)
-#define TB_IM2COL(IC_, KW_) \
-    else if (d.ic == IC_ && d.kw == KW_) im2col_rows_i8_t<IC_, KW_><<<bl, threads, smem, st>>>(g, x, p->kp, zx, p->d_rows)
+        const long long x_bytes = static_cast<long long>(d.n) * d.ih * d.iw * d.ic;
+#define TB_IM2COL(IC_, KW_)                                                                               \
+    else if (d.ic == IC_ && d.kw == KW_ && d.dilation[1] == 1)                                           \
+        im2col_rows_i8_t<IC_, KW_><<<bl, threads, smem, st>>>(g, x, x_bytes, p->segp, p->kp, zx, p->d_rows)
         if (false) {}
         TB_IM2COL(3, 7); TB_IM2COL(3, 5); TB_IM2COL(3, 3); TB_IM2COL(4, 7); TB_IM2COL(4, 5); TB_IM2COL(4, 3);
-        else im2col_rows_i8<<<bl, threads, smem, st>>>(g, x, d.kh * d.kw * d.ic, p->kp, zx, p->d_rows);
+        else im2col_rows_i8<<<bl, threads, smem, st>>>(g, x, p->segp, p->kp, zx, p->d_rows);
 #undef TB_IM2COL
         TB_LAUNCHED(ctx);
         return tb_conv2d_plan_run(p->inner, p->d_rows, out, stream_);

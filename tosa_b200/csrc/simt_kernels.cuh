@@ -141,16 +141,17 @@ __global__ void conv2d_direct_float(ConvGeomDev g, const void* __restrict__ x, c
 
 // ---------------------------------------------------------------------------
 // im2col for convolutions whose input channels are too few for the im2col TMA
-// boxes (an RGB stem): rows [N*OH*OW][kp] of the taps in weight order (ky, kx,
-// c), padded taps and the K padding filled with the input zero point, so that
-// (x - zx) is 0 there and a 1x1 tensor-core convolution over the rows yields
-// the reference's sum over valid taps. 16 bytes per thread (kp % 16 == 0).
+// boxes (an RGB stem): rows [N*OH*OW][kp], one segment of segp bytes per filter
+// row ky (its KW taps x IC channels in weight order, padded to whole 32-bit
+// words), padded taps and all padding filled with the input zero point, so that
+// (x - zx) is 0 there and a 1x1 tensor-core convolution over the rows yields the
+// reference's sum over valid taps. The weights are laid out to match
+// (pad_weight_segments_i8).
 // ---------------------------------------------------------------------------
-__global__ void im2col_rows_i8(ConvGeomDev g, const int8_t* __restrict__ x, int k_valid, int kp, int8_t zx,
+__global__ void im2col_rows_i8(ConvGeomDev g, const int8_t* __restrict__ x, int segp, int kp, int8_t zx,
                                int8_t* __restrict__ rows) {
-    // One thread per output pixel assembles its row in shared memory (taps in
-    // weight order, runs of kw * ic contiguous input bytes per kernel row), then
-    // the block writes its rows out with 16-byte stores.
+    // One thread per output pixel assembles its row in shared memory, then the
+    // block writes its rows out with 16-byte stores.
     extern __shared__ __align__(16) int8_t srow[];
     const long long m_total = static_cast<long long>(g.n) * g.oh * g.ow;
     const int chunks = kp >> 4;
@@ -164,19 +165,17 @@ __global__ void im2col_rows_i8(ConvGeomDev g, const int8_t* __restrict__ x, int 
             const int oy = static_cast<int>(r % g.oh);
             const int b = static_cast<int>(r / g.oh);
             const int8_t* xb = x + static_cast<long long>(b) * g.ih * g.iw * g.ic;
-            int k = 0;
+            for (int k = 0; k < kp; ++k) my[k] = zx;
             for (int ky = 0; ky < g.kh; ++ky) {
                 const int y = oy * g.sh + ky * g.dh - g.pad_t;
-                const bool yok = y >= 0 && y < g.ih;
+                if (y < 0 || y >= g.ih) continue;
                 for (int kx = 0; kx < g.kw; ++kx) {
                     const int xx = ox * g.sw + kx * g.dw - g.pad_l;
-                    const bool ok = yok && xx >= 0 && xx < g.iw;
+                    if (xx < 0 || xx >= g.iw) continue;
                     const int8_t* src = xb + (static_cast<long long>(y) * g.iw + xx) * g.ic;
-                    for (int c = 0; c < g.ic; ++c) my[k++] = ok ? __ldg(src + c) : zx;
+                    for (int c = 0; c < g.ic; ++c) my[ky * segp + kx * g.ic + c] = __ldg(src + c);
                 }
             }
-            for (; k < kp; ++k) my[k] = zx;
-            (void)k_valid;
         }
         __syncthreads();
         // cooperative copy of the block's rows: rows are contiguous in global memory
@@ -189,60 +188,68 @@ __global__ void im2col_rows_i8(ConvGeomDev g, const int8_t* __restrict__ x, int 
     }
 }
 
-// Weights [OC][K] -> [OC][kp], zero-padded.
-__global__ void pad_weight_rows_i8(int oc, int k, int kp, const int8_t* __restrict__ w, int8_t* __restrict__ out) {
-    const long long total = static_cast<long long>(oc) * kp;
-    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-         i += static_cast<long long>(gridDim.x) * blockDim.x) {
-        const int col = static_cast<int>(i % kp);
-        const long long row = i / kp;
-        out[i] = col < k ? w[row * k + col] : 0;
-    }
-}
-
-// The same rows for the common stems, with the tap loops unrolled (IC channels,
-// KW taps per filter row known at compile time): a thread's IC * KW loads of a
-// filter row are independent and in flight together; rows are assembled in
-// shared memory (IC * KW bytes per filter row, kp bytes per output pixel) and
-// written out by the block with 16-byte stores.
+// The same rows for the common stems (IC channels, KW taps per filter row known at
+// compile time, no horizontal dilation): a filter row's KW * IC input bytes are
+// contiguous, so an interior segment is read as the aligned 32-bit words covering
+// it and funnel-shifted into place (word loads and stores instead of byte ones);
+// segments touching the image border take bytes one by one.
 template <int IC, int KW>
-__global__ void __launch_bounds__(128) im2col_rows_i8_t(ConvGeomDev g, const int8_t* __restrict__ x, int kp, int8_t zx,
+__global__ void __launch_bounds__(128) im2col_rows_i8_t(ConvGeomDev g, const int8_t* __restrict__ x,
+                                                         long long x_bytes, int segp, int kp, int8_t zx,
                                                          int8_t* __restrict__ rows) {
+    constexpr int L = KW * IC, LW = (L + 3) / 4;  // segment bytes and words
     extern __shared__ __align__(16) int8_t srow[];
     const long long m_total = static_cast<long long>(g.n) * g.oh * g.ow;
     const int chunks = kp >> 4;
-    const int kfull = g.kh * KW * IC;
+    const uint32_t fill = static_cast<uint8_t>(zx) * 0x01010101u;
     for (long long m0 = static_cast<long long>(blockIdx.x) * blockDim.x; m0 < m_total;
          m0 += static_cast<long long>(gridDim.x) * blockDim.x) {
         const long long m = m0 + threadIdx.x;
-        int8_t* my = srow + threadIdx.x * kp;
+        uint32_t* my = reinterpret_cast<uint32_t*>(srow + threadIdx.x * kp);
         if (m < m_total) {
             const int ox = static_cast<int>(m % g.ow);
             const long long r = m / g.ow;
             const int oy = static_cast<int>(r % g.oh);
             const int b = static_cast<int>(r / g.oh);
-            const int8_t* xb = x + static_cast<long long>(b) * g.ih * g.iw * IC;
+            const long long xb = static_cast<long long>(b) * g.ih * g.iw * IC;
             const int x0 = ox * g.sw - g.pad_l;
-            bool xok[KW];
-#pragma unroll
-            for (int kx = 0; kx < KW; ++kx) {
-                const int xx = x0 + kx * g.dw;
-                xok[kx] = xx >= 0 && xx < g.iw;
-            }
+            const bool x_in = x0 >= 0 && x0 + KW <= g.iw;
+            for (int k = g.kh * (segp >> 2); k < (kp >> 2); ++k) my[k] = fill;
             for (int ky = 0; ky < g.kh; ++ky) {
                 const int y = oy * g.sh + ky * g.dh - g.pad_t;
-                const bool yok = y >= 0 && y < g.ih;
-                const int8_t* src = xb + (static_cast<long long>(y) * g.iw + x0) * IC;
-                int8_t v[KW * IC];
+                uint32_t* dst = my + ky * (segp >> 2);
+                const long long a = xb + (static_cast<long long>(y) * g.iw + x0) * IC;  // first byte
+                const long long a0 = a & ~3ll;
+                if (y >= 0 && y < g.ih && x_in && a0 + 4 * (LW + 1) <= x_bytes) {
+                    const uint32_t* w = reinterpret_cast<const uint32_t*>(x + a0);
+                    uint32_t in[LW + 1];
 #pragma unroll
-                for (int kx = 0; kx < KW; ++kx)
+                    for (int j = 0; j <= LW; ++j) in[j] = __ldg(w + j);
+                    const uint32_t sh = static_cast<uint32_t>(a - a0) * 8;
 #pragma unroll
-                    for (int c = 0; c < IC; ++c)
-                        v[kx * IC + c] = (yok && xok[kx]) ? __ldg(src + kx * g.dw * IC + c) : zx;
+                    for (int j = 0; j < LW; ++j) {
+                        uint32_t v = __funnelshift_r(in[j], in[j + 1], sh);
+                        if (4 * j + 4 > L) {  // the segment's last word: bytes past it hold zx
+                            const uint32_t keep = 0xffffffffu >> (8 * (4 * j + 4 - L));
+                            v = (v & keep) | (fill & ~keep);
+                        }
+                        dst[j] = v;
+                    }
+                } else {
+                    uint8_t* db = reinterpret_cast<uint8_t*>(dst);
+                    const bool yok = y >= 0 && y < g.ih;
 #pragma unroll
-                for (int j = 0; j < KW * IC; ++j) my[ky * KW * IC + j] = v[j];
+                    for (int kx = 0; kx < KW; ++kx) {
+                        const bool ok = yok && x0 + kx >= 0 && x0 + kx < g.iw;
+#pragma unroll
+                        for (int c = 0; c < IC; ++c)
+                            db[kx * IC + c] = ok ? static_cast<uint8_t>(__ldg(x + a + kx * IC + c)) : static_cast<uint8_t>(zx);
+                    }
+#pragma unroll
+                    for (int j = L; j < 4 * LW; ++j) db[j] = static_cast<uint8_t>(zx);
+                }
+                for (int j = LW; j < (segp >> 2); ++j) dst[j] = fill;
             }
-            for (int k = kfull; k < kp; ++k) my[k] = zx;
         }
         __syncthreads();
         const long long rows_here = m_total - m0 < blockDim.x ? m_total - m0 : blockDim.x;
@@ -251,6 +258,32 @@ __global__ void __launch_bounds__(128) im2col_rows_i8_t(ConvGeomDev g, const int
         const uint4* s4 = reinterpret_cast<const uint4*>(srow);
         for (int v = threadIdx.x; v < vecs; v += blockDim.x) dst[v] = s4[v];
         __syncthreads();
+    }
+}
+
+// Weights [oc][KH][KW*IC] -> [oc][kp] in the rows' layout: segment ky at ky * segp,
+// zeros in the padding (the rows hold the input zero point there, so any weight
+// value gives (x - zx) * (w - zw) = 0).
+__global__ void pad_weight_segments_i8(int oc, int kh, int seg, int segp, int kp, const int8_t* __restrict__ w,
+                                       int8_t* __restrict__ out) {
+    const long long total = static_cast<long long>(oc) * kp;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int col = static_cast<int>(i % kp);
+        const long long o = i / kp;
+        const int ky = col / segp, j = col - ky * segp;
+        out[i] = (ky < kh && j < seg) ? w[(o * kh + ky) * seg + j] : 0;
+    }
+}
+
+// Weights [OC][K] -> [OC][kp], zero-padded.
+__global__ void pad_weight_rows_i8(int oc, int k, int kp, const int8_t* __restrict__ w, int8_t* __restrict__ out) {
+    const long long total = static_cast<long long>(oc) * kp;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int col = static_cast<int>(i % kp);
+        const long long row = i / kp;
+        out[i] = col < k ? w[row * k + col] : 0;
     }
 }
 
