@@ -21,6 +21,17 @@ namespace tb {
         (ctx)->launches++;                                                                             \
     } while (0)
 
+// Host side of FastDiv (tc_gemm.cuh): s = ceil(log2 d), m = floor(2^32 (2^s - d) / d) + 1.
+inline FastDiv make_fastdiv(int d) {
+    FastDiv f{};
+    f.d = static_cast<uint32_t>(d < 1 ? 1 : d);
+    int s = 0;
+    while ((1ull << s) < f.d) ++s;
+    f.s = s;
+    f.m = static_cast<uint32_t>(((1ull << 32) * ((1ull << s) - f.d)) / f.d + 1);
+    return f;
+}
+
 template <class Cfg, int EK>
 tb_status launch_gemm(tb_context* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB, GemmParams p,
                       cudaStream_t stream) {
@@ -33,6 +44,10 @@ tb_status launch_gemm(tb_context* ctx, const CUtensorMap& tmA, const CUtensorMap
     p.m_tiles = (p.M + Cfg::BM - 1) / Cfg::BM;
     p.n_tiles = (p.N + Cfg::kBN - 1) / Cfg::kBN;
     p.total_tiles = p.batch * p.m_tiles * p.n_tiles;
+    p.fd_mtiles = make_fastdiv(p.m_tiles);
+    p.fd_ntiles = make_fastdiv(p.n_tiles);
+    p.fd_ow = make_fastdiv(p.conv_OW);
+    p.fd_ohow = make_fastdiv(p.conv_OHOW);
     p.err = ctx->dev_err;
     p.timeout_cycles = ctx->timeout_cycles;
     p.trace = ctx->trace;

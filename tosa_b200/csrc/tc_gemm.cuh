@@ -113,6 +113,18 @@ struct ColsumJob {
     unsigned int target;
 };
 
+// Division by a runtime constant d as a multiply-high (Granlund-Montgomery): with
+// s = ceil(log2 d) and m = floor(2^32 (2^s - d) / d) + 1, n / d = (mulhi(n, m) + n) >> s
+// for 0 <= n < 2^31. The host fills it (make_fastdiv).
+struct FastDiv {
+    uint32_t d, m;
+    int s;
+};
+
+__device__ __forceinline__ int fdiv(int n, const FastDiv& f) {
+    return static_cast<int>((__umulhi(static_cast<uint32_t>(n), f.m) + static_cast<uint32_t>(n)) >> f.s);
+}
+
 struct GemmParams {
     int M, N, K;               // per batch
     int batch;
@@ -121,6 +133,7 @@ struct GemmParams {
     int total_tiles;
     // im2col geometry (CONV2D)
     int conv_OW, conv_OHOW;
+    FastDiv fd_mtiles, fd_ntiles, fd_ow, fd_ohow;  // the divisions of the per-tile index arithmetic
     int stride_h, stride_w, pad_t, pad_l;
     int KW, dil_h, dil_w;
     int c_blocks;              // k blocks per filter tap
@@ -172,10 +185,10 @@ struct GemmCfg {
 
 __device__ __forceinline__ void tile_coords(const GemmParams& p, int tile, int& b, int& mt, int& nt) {
     // m fastest so CTAs running concurrently share the B tile in L2.
-    mt = tile % p.m_tiles;
-    int rest = tile / p.m_tiles;
-    nt = rest % p.n_tiles;
-    b = rest / p.n_tiles;
+    const int rest = fdiv(tile, p.fd_mtiles);
+    mt = tile - rest * p.m_tiles;
+    b = fdiv(rest, p.fd_ntiles);
+    nt = rest - b * p.n_tiles;
 }
 
 // Makes the 16 registers of a finished tcgen05.ld visible only after the
@@ -517,12 +530,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 const int m0 = mt * BM, n0 = nt * BN;
                 int img = 0, wb = 0, hb = 0;
                 if constexpr (Cfg::kIm2col) {
-                    img = m0 / p.conv_OHOW;
+                    img = fdiv(m0, p.fd_ohow);
                     const int rem = m0 - img * p.conv_OHOW;
-                    const int oy = rem / p.conv_OW, ox = rem - oy * p.conv_OW;
+                    const int oy = fdiv(rem, p.fd_ow), ox = rem - oy * p.conv_OW;
                     wb = ox * p.stride_w - p.pad_l;
                     hb = oy * p.stride_h - p.pad_t;
                 }
+                int cb = 0, kx = 0, ky = 0, tap = 0;  // k block kb = (ky * KW + kx) * c_blocks + cb, stepped
                 for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
                     const int s = it % S;
                     const uint32_t ph = (it / S) & 1;
@@ -532,11 +546,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     if (p.trace && blockIdx.x == 0 && it < 128) p.trace[it] = clock64();
                     mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
                     if constexpr (Cfg::kIm2col) {
-                        const int tap = kb / p.c_blocks, cb = kb - tap * p.c_blocks;
-                        const int ky = tap / p.KW, kx = tap - ky * p.KW;
                         tma_load_im2col_4d(sa, &tmA, &full[s], cb * Cfg::BK, wb, hb, img,
                                            static_cast<uint16_t>(kx * p.dil_w), static_cast<uint16_t>(ky * p.dil_h));
                         tma_load_3d(sb, &tmB, &full[s], tap * p.IC + cb * Cfg::BK, n0, 0);
+                        if (++cb == p.c_blocks) {
+                            cb = 0;
+                            ++tap;
+                            if (++kx == p.KW) {
+                                kx = 0;
+                                ++ky;
+                            }
+                        }
                     } else {
                         tma_load_3d(sa, &tmA, &full[s], kb * Cfg::BK, m0, b);
                         if constexpr (Cfg::kBMN) {
@@ -786,8 +806,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const bool row_ok = m < p.M;
             const int32_t* delta = nullptr;
             if (rcls != nullptr && row_ok) {
-                const int rem = m % p.conv_OHOW;
-                const int oy = rem / p.conv_OW, ox = rem - oy * p.conv_OW;
+                const int rem = m - fdiv(m, p.fd_ohow) * p.conv_OHOW;
+                const int oy = fdiv(rem, p.fd_ow), ox = rem - oy * p.conv_OW;
                 const int cls = rcls[oy] * e.n_col_classes + ccls[ox];
                 if (cls != e.base_class) delta = e.ct_delta + static_cast<long long>(cls) * e.ct_ld;
             }
