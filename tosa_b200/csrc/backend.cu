@@ -233,10 +233,82 @@ tb_status make_rescale_plan(tb_context* ctx, const tb_rescale_attr* a, int in_t,
     return TB_OK;
 }
 
+void prepare_small_range(const tb_rescale_attr& a, const RescalePlan& rs, long long bound, SmallRange* sr,
+                         std::vector<int32_t>* blob) {
+    *sr = SmallRange{};
+    blob->clear();
+    if (!rs.enabled || !rs.fast || rs.out_dtype != TB_DT_INT8 || bound < 0) return;
+    int k = 0;
+    while (k < 30 && (std::max(bound, 1ll) << (k + 1)) <= 2147483647ll) ++k;
+    if ((std::max(bound, 1ll) << k) > 2147483647ll) return;
+    const bool dbl = rs.rounding == TB_ROUND_DOUBLE;
+    if (dbl && k < 2) return;
+    const int d = 32 - k;
+    const long long k2 = dbl ? (1ll << (31 - d)) : 0;
+    const int ch = a.channels;
+    auto cterm = [&](int i, bool fold) {
+        const int s = a.shift[i];
+        return (1ll << (s - 1 - d)) + (dbl ? (1ll << (30 - d)) : 0) +
+               (fold ? static_cast<long long>(rs.out_zp) * (1ll << (s - d)) : 0);
+    };
+    bool fold = true, plain = true;
+    for (int i = 0; i < ch; ++i) {
+        if (a.shift[i] - 1 < d) return;
+        if (std::llabs(cterm(i, true)) + k2 >= (1ll << 30)) fold = false;
+        if (std::llabs(cterm(i, false)) + k2 >= (1ll << 30)) plain = false;
+    }
+    if (!fold && !plain) return;
+    const size_t padded = (static_cast<size_t>(ch) + 255) / 256 * 256;
+    blob->assign(2 * padded, 0);
+    for (size_t pi = 0; pi < padded; ++pi) {
+        const int i = pi < static_cast<size_t>(ch) ? static_cast<int>(pi) : 0;
+        (*blob)[pi] = std::min(a.shift[i] - d, 31);
+        (*blob)[padded + pi] = static_cast<int32_t>(cterm(i, fold));
+    }
+    sr->ok = true;
+    sr->k = k;
+    sr->mul = static_cast<int32_t>(1u << k);
+    sr->k2 = static_cast<int32_t>(k2);
+    sr->zp_folded = fold;
+}
+
+void place_small_range(SmallRange* sr, int32_t* dev_blob, int channels) {
+    const size_t padded = (static_cast<size_t>(channels) + 255) / 256 * 256;
+    sr->d_sh = dev_blob;
+    sr->d_c = dev_blob + padded;
+}
+
+tb_status make_small_range(const tb_rescale_attr& a, const RescalePlan& rs, long long bound, SmallRange* sr) {
+    std::vector<int32_t> blob;
+    prepare_small_range(a, rs, bound, sr, &blob);
+    if (!sr->ok) return TB_OK;
+    TB_CUDA(cudaMalloc(&sr->d_blob, sizeof(int32_t) * blob.size()));
+    TB_CUDA(cudaMemcpy(sr->d_blob, blob.data(), sizeof(int32_t) * blob.size(), cudaMemcpyHostToDevice));
+    place_small_range(sr, sr->d_blob, a.channels);
+    return TB_OK;
+}
+
+void free_small_range(SmallRange* sr) {
+    if (sr->d_blob) cudaFree(sr->d_blob);
+    *sr = SmallRange{};
+}
+
 void free_rescale_plan(RescalePlan* r) {
     if (r->d_blob) cudaFree(r->d_blob);
     r->d_blob = nullptr;
     r->d_mult = r->d_shift = r->fq_m = r->fq_sh = r->fq_hz = nullptr;
+}
+
+// The GEMM's fast int8 RESCALE (small-range form) when both the plan's RESCALE and its
+// bound allow it; otherwise the general epilogue (rs_fast = 0) with unscaled terms.
+static void set_fast_epilogue(GemmEpilogue* ep, const RescalePlan& rs, const SmallRange& sr) {
+    ep->rs_fast = rs.fast && sr.ok;
+    ep->rs_zp_folded = sr.zp_folded;
+    ep->sr_mul = sr.ok ? sr.mul : 1;
+    ep->sr_k2 = sr.k2;
+    ep->fq_m = rs.fq_m;
+    ep->sr_sh = sr.d_sh;
+    ep->sr_c = sr.d_c;
 }
 
 RescaleArgs rescale_args(const RescalePlan& r) {
@@ -431,6 +503,12 @@ extern "C" TB_API tb_status tb_matmul_plan_create(tb_context* ctx, const tb_matm
     if (rescale) {
         tb_status s = make_rescale_plan(ctx, rescale, TB_DT_INT32, d->w, &p->rs);
         if (s != TB_OK) { delete p; return s; }
+        if (d->a_dtype == TB_DT_INT8 && d->b_dtype == TB_DT_INT8) {
+            // |sum (a - za)(b - zb)| <= c * (128 + |za|) * (128 + |zb|)
+            const long long bound = static_cast<long long>(d->c) * (128 + std::abs(d->a_zp)) * (128 + std::abs(d->b_zp));
+            s = make_small_range(*rescale, p->rs, bound, &p->sr);
+            if (s != TB_OK) { free_rescale_plan(&p->rs); delete p; return s; }
+        }
     }
     if (p->path == 5) {
         p->wp = (d->w + 15) / 16 * 16;
@@ -510,6 +588,8 @@ extern "C" TB_API tb_status tb_matmul_plan_run(tb_matmul_plan* p, const void* a,
     gp.out_batch_stride = static_cast<long long>(d.h) * d.w;
     gp.ldo = d.w;
     GemmEpilogue& ep = gp.epi;
+    // the small-range epilogue takes its integer terms pre-multiplied by 2^k
+    const uint32_t tmul = p->sr.ok ? static_cast<uint32_t>(p->sr.mul) : 1u;
     if (p->path == 0 || p->path == 5) {
         if (d.a_zp != 0 && b_prepared) {
             ep.colterm = p->d_colterm;
@@ -517,15 +597,15 @@ extern "C" TB_API tb_status tb_matmul_plan_run(tb_matmul_plan* p, const void* a,
         } else if (d.a_zp != 0) {
             // colterm = -a_zp * colsum(B) + c * a_zp * b_zp, reduced inside the GEMM by the epilogue warps
             // during the first main loop (cooperative launch; see ColsumJob).
-            const int32_t cst = static_cast<int32_t>(static_cast<uint32_t>(d.c) * static_cast<uint32_t>(d.a_zp) *
-                                                     static_cast<uint32_t>(d.b_zp));
+            const uint32_t cst = static_cast<uint32_t>(d.c) * static_cast<uint32_t>(d.a_zp) *
+                                 static_cast<uint32_t>(d.b_zp);
             ColsumJob& cs = gp.cs;
             cs.b = static_cast<const int8_t*>(b);
             cs.c = d.c;
             cs.w = d.w;
             cs.units = d.n * ((d.w + 63) / 64);
-            cs.scale = -d.a_zp;
-            cs.add = cst;
+            cs.scale = static_cast<int32_t>(static_cast<uint32_t>(-d.a_zp) * tmul);
+            cs.add = static_cast<int32_t>(cst * tmul);
             cs.out = p->d_colterm;
             cs.counter = p->d_counter;
             if (p->replayable || static_cast<unsigned long long>(p->epoch + 1) * cs.units >= (1ull << 31)) {
@@ -538,15 +618,11 @@ extern "C" TB_API tb_status tb_matmul_plan_run(tb_matmul_plan* p, const void* a,
             ep.colterm = p->d_colterm;
             ep.colterm_bstride = d.w;
         }
-        ep.row_zp_neg = -d.b_zp;
+        ep.row_zp_neg = static_cast<int32_t>(static_cast<uint32_t>(-d.b_zp) * tmul);
         if (p->rs.enabled) {
             ep.mode = EPI_RESCALE;
             ep.rs = rescale_args(p->rs);
-            ep.rs_fast = p->rs.fast;
-            ep.rs_zp_folded = p->rs.zp_folded;
-            ep.fq_m = p->rs.fq_m;
-            ep.fq_sh = p->rs.fq_sh;
-            ep.fq_hz = p->rs.fq_hz;
+            set_fast_epilogue(&ep, p->rs, p->sr);
             ep.out_dtype = p->rs.out_dtype;
         } else {
             ep.mode = EPI_I32;
@@ -575,10 +651,12 @@ extern "C" TB_API tb_status tb_matmul_plan_set_constant_b(tb_matmul_plan* p, con
     }
     if (d.a_zp != 0) {
         // colterm = -a_zp * colsum(B) + c * a_zp * b_zp (the in-GEMM column-sum job's values)
+        const uint32_t tmul = p->sr.ok ? static_cast<uint32_t>(p->sr.mul) : 1u;  // small-range epilogue: x 2^k
         const int32_t add = static_cast<int32_t>(static_cast<uint32_t>(d.c) * static_cast<uint32_t>(d.a_zp) *
-                                                 static_cast<uint32_t>(d.b_zp));
-        colterm_const_i8<<<dim3((d.w + 31) / 32, d.n), dim3(32, 8), 0, st>>>(d.c, d.w, static_cast<const int8_t*>(b),
-                                                                            -d.a_zp, add, p->d_colterm);
+                                                 static_cast<uint32_t>(d.b_zp) * tmul);
+        colterm_const_i8<<<dim3((d.w + 31) / 32, d.n), dim3(32, 8), 0, st>>>(
+            d.c, d.w, static_cast<const int8_t*>(b), static_cast<int32_t>(static_cast<uint32_t>(-d.a_zp) * tmul), add,
+            p->d_colterm);
         TB_LAUNCHED(ctx);
     }
     TB_CUDA(cudaStreamSynchronize(st));
@@ -589,6 +667,7 @@ extern "C" TB_API tb_status tb_matmul_plan_set_constant_b(tb_matmul_plan* p, con
 extern "C" TB_API void tb_matmul_plan_destroy(tb_matmul_plan* p) {
     if (!p) return;
     free_rescale_plan(&p->rs);
+    free_small_range(&p->sr);
     if (p->d_colterm) cudaFree(p->d_colterm);
     if (p->d_counter) cudaFree(p->d_counter);
     if (p->d_bpad) cudaFree(p->d_bpad);
@@ -620,6 +699,7 @@ struct tb_conv2d_plan {
     const void* weight = nullptr;
     const void* bias = nullptr;
     RescalePlan rs;
+    SmallRange sr;                  // tensor-core int8 path: small-range RESCALE constants
     int bn = 64, bk = 128;
     int32_t* d_colterm = nullptr;   // [n_classes][ct_ld] column terms of each border class
     int32_t* d_ctdelta = nullptr;   // [n_classes][ct_ld] class terms minus the base class's
@@ -838,6 +918,24 @@ static tb_status conv_plan_create(tb_context* ctx, const tb_conv2d_desc* d, cons
         *out = p;
         return TB_OK;
     }
+    // Small-range RESCALE: |v| <= (128 + |zx|) * sum_k |w - zw| + |bias| per output channel.
+    if (rescale && int8) {
+        const size_t kk = static_cast<size_t>(taps) * d->ic;
+        std::vector<int8_t> hw(static_cast<size_t>(oc) * kk);
+        std::vector<int32_t> hb(d->bias_len);
+        cudaError_t ce = cudaMemcpy(hw.data(), weight, hw.size(), cudaMemcpyDeviceToHost);
+        if (ce == cudaSuccess) ce = cudaMemcpy(hb.data(), bias, sizeof(int32_t) * hb.size(), cudaMemcpyDeviceToHost);
+        if (ce != cudaSuccess) return bail(fail(TB_ERR_CUDA, "weight read failed: %s", cudaGetErrorString(ce)));
+        long long bound = 0;
+        for (int o = 0; o < oc; ++o) {
+            long long sw = 0;
+            for (size_t k = 0; k < kk; ++k) sw += std::abs(static_cast<int>(hw[o * kk + k]) - d->weight_zp);
+            const long long b = std::llabs(static_cast<long long>(hb[d->bias_len == 1 ? 0 : o]));
+            bound = std::max(bound, (128ll + std::abs(d->input_zp)) * sw + b);
+        }
+        tb_status s2 = make_small_range(*rescale, p->rs, bound, &p->sr);
+        if (s2 != TB_OK) return bail(s2);
+    }
     // Integer: border classes and the per-class column terms.
     std::vector<int> ky_r, kx_r;
     std::vector<uint8_t> rowc(oh), colc(ow);
@@ -892,7 +990,8 @@ static tb_status conv_plan_create(tb_context* ctx, const tb_conv2d_desc* d, cons
                                                             static_cast<const int8_t*>(weight), d_wsum);
     conv_colterm<<<grid_for(ctx, static_cast<long long>(n_ry) * n_rx * p->ct_ld), 256>>>(
         oc, p->ct_ld, d->kh, d->kw, d->ic, n_ry, n_rx, p->base_class, d_ranges, d_ranges + ky_r.size(), d_wsum,
-        static_cast<const int32_t*>(bias), d->bias_len, d->input_zp, d->weight_zp, p->d_colterm, p->d_ctdelta);
+        static_cast<const int32_t*>(bias), d->bias_len, d->input_zp, d->weight_zp,
+        p->sr.ok ? static_cast<uint32_t>(p->sr.mul) : 1u, p->d_colterm, p->d_ctdelta);
     ce = cudaDeviceSynchronize();
     cudaFree(d_wsum);
     cudaFree(d_ranges);
@@ -1046,15 +1145,12 @@ extern "C" TB_API tb_status tb_conv2d_plan_run(tb_conv2d_plan* p, const void* in
     ep.rowclass = p->d_rowclass;
     ep.colclass = p->d_colclass;
     ep.n_col_classes = p->n_cx;
-    ep.row_zp_neg = -d.weight_zp;
+    ep.row_zp_neg = static_cast<int32_t>(static_cast<uint32_t>(-d.weight_zp) *
+                                         (p->sr.ok ? static_cast<uint32_t>(p->sr.mul) : 1u));
     if (p->rs.enabled) {
         ep.mode = EPI_RESCALE;
         ep.rs = rescale_args(p->rs);
-        ep.rs_fast = p->rs.fast;
-        ep.rs_zp_folded = p->rs.zp_folded;
-        ep.fq_m = p->rs.fq_m;
-        ep.fq_sh = p->rs.fq_sh;
-        ep.fq_hz = p->rs.fq_hz;
+        set_fast_epilogue(&ep, p->rs, p->sr);
         ep.out_dtype = p->rs.out_dtype;
     } else {
         ep.mode = EPI_I32;
@@ -1069,6 +1165,7 @@ extern "C" TB_API void tb_conv2d_plan_destroy(tb_conv2d_plan* p) {
     if (p->d_rows) cudaFree(p->d_rows);
     if (p->d_wpad) cudaFree(p->d_wpad);
     free_rescale_plan(&p->rs);
+    free_small_range(&p->sr);
     if (p->d_colterm) cudaFree(p->d_colterm);
     if (p->d_ctdelta) cudaFree(p->d_ctdelta);
     if (p->d_rowclass) cudaFree(p->d_rowclass);

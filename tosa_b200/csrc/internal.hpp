@@ -84,6 +84,25 @@ struct RescalePlan {
     int32_t* d_blob = nullptr;     // owned allocation holding the fast arrays, multiplier and shift
 };
 
+// Small-range constants of a GEMM's fused int8 RESCALE (tc_gemm.cuh GemmEpilogue): with a
+// host bound |v| <= bound on the int32 value, k = the largest shift with bound * 2^k < 2^31,
+// d = 32 - k, per channel sh = s - d and c = 2^(s-1-d) [+ 2^(30-d)] [+ zp * 2^(s-d)].
+struct SmallRange {
+    bool ok = false;
+    int k = 0;
+    int32_t mul = 1, k2 = 0;
+    bool zp_folded = false;
+    int32_t* d_blob = nullptr;  // owned (make_small_range): sh then c, each padded to 256 channels
+    int32_t* d_sh = nullptr;
+    int32_t* d_c = nullptr;
+};
+// Host half: fills sr (ok = false when the form does not apply) and the blob words.
+void prepare_small_range(const tb_rescale_attr& a, const RescalePlan& rs, long long bound, SmallRange* sr,
+                         std::vector<int32_t>* blob);
+void place_small_range(SmallRange* sr, int32_t* dev_blob, int channels);
+tb_status make_small_range(const tb_rescale_attr& a, const RescalePlan& rs, long long bound, SmallRange* sr);
+void free_small_range(SmallRange* sr);
+
 // Validate a fused/standalone RESCALE (src/ops/type_conv.rs:128-171) for
 // input type in_dtype with `shape_last` as the last dimension.
 tb_status check_rescale(const tb_rescale_attr* a, int in_dtype, int64_t shape_last, int64_t* in_zp_ext,
@@ -158,6 +177,7 @@ struct tb_matmul_plan {
     tb_matmul_desc d{};
     int path = 0;  // 0 TC int8, 1 TC f16/bf16, 2 direct int, 3 direct float, 4 direct int16, 5 TC int8, padded B
     tb::RescalePlan rs;
+    tb::SmallRange sr;
     int bn = 256;
     int32_t* d_colterm = nullptr;  // [n][w] (+ one tile of padding) when a_zp != 0
     unsigned int* d_counter = nullptr;  // column-sum units finished, grows by `units` per run

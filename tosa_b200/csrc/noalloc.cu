@@ -102,15 +102,24 @@ extern "C" TB_API tb_status tb_matmul_i8_noalloc(const tb_matmul_desc* d, const 
     plan.d = *d;
     plan.path = path;
     plan.bn = bn;
+    std::vector<int32_t> blob, sr_blob;  // host copies stay alive until the call synchronizes
     if (rescale) {
-        std::vector<int32_t> blob;
         TB_TRY(prepare_rescale(rescale, TB_DT_INT32, d->w, &plan.rs, &blob));
-        if (blob.size() > kMaxBlobWords)
+        // the small-range epilogue constants (as tb_matmul_plan_create makes them)
+        const long long bound = static_cast<long long>(d->c) * (128 + std::abs(d->a_zp)) * (128 + std::abs(d->b_zp));
+        prepare_small_range(*rescale, plan.rs, bound, &plan.sr, &sr_blob);
+        if (blob.size() + sr_blob.size() > kMaxBlobWords)
             return fail(TB_ERR_INVALID_ARGUMENT, "tb_matmul_i8_noalloc: %d rescale channels exceed the scratch limit",
                         rescale->channels);
         int32_t* dev_blob = reinterpret_cast<int32_t*>(su.scratch + kBlobOffset);
         TB_CUDA(cudaMemcpyAsync(dev_blob, blob.data(), sizeof(int32_t) * blob.size(), cudaMemcpyHostToDevice, st));
         place_rescale(&plan.rs, dev_blob);
+        if (plan.sr.ok) {
+            int32_t* dev_sr = dev_blob + blob.size();
+            TB_CUDA(cudaMemcpyAsync(dev_sr, sr_blob.data(), sizeof(int32_t) * sr_blob.size(), cudaMemcpyHostToDevice,
+                                    st));
+            place_small_range(&plan.sr, dev_sr, rescale->channels);
+        }
     }
     if (path == 0 && d->a_zp != 0) {
         plan.d_colterm = reinterpret_cast<int32_t*>(su.scratch + kColtermOffset);
@@ -124,6 +133,7 @@ extern "C" TB_API tb_status tb_matmul_i8_noalloc(const tb_matmul_desc* d, const 
     TB_CUDA(cudaMemcpyAsync(&word, su.scratch, sizeof word, cudaMemcpyDeviceToHost, st));
     TB_CUDA(cudaStreamSynchronize(st));
     plan.rs.d_blob = nullptr;  // nothing owned
+    plan.sr.d_blob = nullptr;
     if (word & DEV_ERR_TIMEOUT) return fail(TB_ERR_TIMEOUT, "a device wait timed out");
     if (word) return fail(TB_ERR_GRAPH, "apply_scale: value out of range for the shift, or result exceeds int32");
     return TB_OK;

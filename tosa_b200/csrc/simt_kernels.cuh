@@ -631,7 +631,8 @@ __device__ __forceinline__ uint32_t conv_class_term(int o, int cls, int n_rx, in
 __global__ void conv_colterm(int oc, long long ld, int kh, int kw, int ic, int n_ry, int n_rx, int base,
                              const int* __restrict__ ky_range, const int* __restrict__ kx_range,
                              const int32_t* __restrict__ wsum, const int32_t* __restrict__ bias, int bias_len,
-                             int32_t zx, int32_t zw, int32_t* __restrict__ colterm, int32_t* __restrict__ delta) {
+                             int32_t zx, int32_t zw, uint32_t mul, int32_t* __restrict__ colterm,
+                             int32_t* __restrict__ delta) {
     const long long total = static_cast<long long>(n_ry) * n_rx * ld;
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -644,8 +645,9 @@ __global__ void conv_colterm(int oc, long long ld, int kh, int kw, int ic, int n
         }
         const uint32_t t = conv_class_term(o, cls, n_rx, kh, kw, ic, ky_range, kx_range, wsum, bias, bias_len, zx, zw);
         const uint32_t tb = conv_class_term(o, base, n_rx, kh, kw, ic, ky_range, kx_range, wsum, bias, bias_len, zx, zw);
-        colterm[i] = static_cast<int32_t>(t);
-        delta[i] = static_cast<int32_t>(t - tb);
+        // mul: 2^k of the small-range epilogue (1 otherwise), wrap-around
+        colterm[i] = static_cast<int32_t>(t * mul);
+        delta[i] = static_cast<int32_t>((t - tb) * mul);
     }
 }
 

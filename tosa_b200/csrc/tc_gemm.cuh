@@ -85,12 +85,19 @@ struct GemmEpilogue {
     int n_col_classes;
     // RESCALE
     RescaleArgs rs;
-    int rs_fast;               // every shift in [33, 62], multipliers >= 0 (host-verified)
-    int rs_zp_folded;          // out_zp rides in fq_hz
-    // fast path, [channels padded to 256]: multiplier, shift - 32, 2^(shift-33) (+ out_zp * 2^(shift-32))
+    // Fast RESCALE to int8 (every shift s in [33, 62], multipliers >= 0), small-range form: the
+    // column terms, deltas and row_zp_neg arrive multiplied by sr_mul = 2^k and the host bounds
+    // |v| < 2^(31-k), so v' = v * 2^k is exact; with d = 32 - k
+    //   r = (mulhi(v', m) + sr_c [- sr_k2 when v' < 0, double rounding]) >> sr_sh [+ out_zp],
+    // the exact apply_scale_32 (floor((v m + 2^(s-1) [+-2^30]) / 2^s); the added terms are
+    // whole multiples of 2^d, so the inner floor division by 2^d is exact).
+    int rs_fast;
+    int rs_zp_folded;          // out_zp rides in sr_c
+    int32_t sr_mul, sr_k2;
+    // [channels padded to 256]: multiplier, s - d (at most 31), 2^(s-1-d) [+ 2^(30-d)] [+ zp 2^(s-d)]
     const int32_t* fq_m;
-    const int32_t* fq_sh;
-    const int32_t* fq_hz;
+    const int32_t* sr_sh;
+    const int32_t* sr_c;
     int out_dtype;             // DT_INT8 / DT_INT16 / DT_INT32 / DT_FP32 / DT_BF16 / DT_FP16
     // Float convolution: out = round(round(acc) + fbias[n])
     const float* fbias;        // [N] or [1]
@@ -256,7 +263,7 @@ __device__ __forceinline__ void int_terms(const uint32_t (&acc)[W], int n0, int3
 
 // Per-tensor fast RESCALE constants (channel 0) and the clamp decision, loaded once.
 struct FastConst {
-    int32_t m, sh, hz, add_zp;
+    int32_t m, sh, c, add_zp;
     bool clamp;     // the range is narrower than int8's (a fused CLAMP): saturation alone does not do it
     bool clamp_lo;  // lower bound above -128
     bool clamp_hi;  // upper bound below 127
@@ -318,47 +325,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, const uint32
     // RESCALE (+ fused CLAMP through r.lo / r.hi)
     const RescaleArgs& r = e.rs;
     int32_t res[kChunk];
-    if constexpr (EK >= EK_FAST_T_S && EK <= EK_FAST_PC_D) {
-        constexpr bool PC = EK == EK_FAST_PC_S || EK == EK_FAST_PC_D;
-        constexpr bool DBL = EK == EK_FAST_T_D || EK == EK_FAST_PC_D;
-        if constexpr (PC) {
-            // per-channel constants of this chunk, staged in shared memory for the tile
-#pragma unroll
-            for (int j = 0; j < kChunk; j += 4) {
-                const int4 m4 = *reinterpret_cast<const int4*>(fm + n0 + j);
-                const int4 s4 = *reinterpret_cast<const int4*>(fsh + n0 + j);
-                const int4 h4 = *reinterpret_cast<const int4*>(fhz + n0 + j);
-                res[j + 0] = rescale_f2<DBL>(v[j + 0], m4.x, s4.x, h4.x);
-                res[j + 1] = rescale_f2<DBL>(v[j + 1], m4.y, s4.y, h4.y);
-                res[j + 2] = rescale_f2<DBL>(v[j + 2], m4.z, s4.z, h4.z);
-                res[j + 3] = rescale_f2<DBL>(v[j + 3], m4.w, s4.w, h4.w);
-            }
-        } else {
-#pragma unroll
-            for (int j = 0; j < kChunk; ++j) res[j] = rescale_f2<DBL>(v[j], fk.m, fk.sh, fk.hz);
-        }
-        if (fk.add_zp != 0) {
-#pragma unroll
-            for (int j = 0; j < kChunk; ++j) res[j] += fk.add_zp;
-        }
-        if (fk.clamp) {
-#pragma unroll
-            for (int j = 0; j < kChunk; ++j) res[j] = min(max(res[j], r.lo), r.hi);
-        }
-        int8_t* o = reinterpret_cast<int8_t*>(outp) + orow + n0;
-        if (ncols == kChunk && ((reinterpret_cast<uintptr_t>(o) & 15) == 0)) {
-            // saturating packs complete the clamp to the int8 range
-            *reinterpret_cast<uint4*>(o) = make_uint4(pack4_sat_i8(res[0], res[1], res[2], res[3]),
-                                                      pack4_sat_i8(res[4], res[5], res[6], res[7]),
-                                                      pack4_sat_i8(res[8], res[9], res[10], res[11]),
-                                                      pack4_sat_i8(res[12], res[13], res[14], res[15]));
-        } else {
-#pragma unroll
-            for (int j = 0; j < kChunk; ++j)
-                if (j < ncols) o[j] = static_cast<int8_t>(min(max(res[j], r.lo), r.hi));
-        }
-        return;
-    } else {
+    {
         // General apply_scale semantics with range checks (shifts below 32, inexact rounding, scale16).
         uint32_t dummy = 0;
 #pragma unroll
@@ -392,24 +359,30 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, const uint32
     }
 }
 
-// Fast int8 RESCALE of W consecutive columns, W/16 x 16 packed bytes into out16[].
+// Fast int8 RESCALE of W consecutive columns, W/16 x 16 packed bytes into out16[]
+// (small-range form, see GemmEpilogue): v' = acc * 2^k + column term [+ row term]
+// [+ border-class delta], all terms pre-multiplied by 2^k (int32 wrap-around; the
+// host's bound makes the sum exact), then r = (mulhi(v', m) + c [- k2 if v' < 0]) >> sh.
 template <int EK, int W>
 __device__ __forceinline__ void fast_chunk_i8(const GemmParams& p, const uint32_t (&acc)[W], int n0, int32_t rowterm,
-                                              const int32_t* colterm, const int32_t* delta, const int32_t* fm,
-                                              const int32_t* fsh, const int32_t* fhz, const FastConst& fk,
-                                              uint4 (&out16)[W / 16]) {
+                                              bool has_rowterm, const int32_t* colterm, const int32_t* delta,
+                                              const int32_t* fm, const int32_t* fsh, const int32_t* fc,
+                                              const FastConst& fk, uint4 (&out16)[W / 16]) {
     constexpr bool PC = EK == EK_FAST_PC_S || EK == EK_FAST_PC_D;
     constexpr bool DBL = EK == EK_FAST_T_D || EK == EK_FAST_PC_D;
-    // v = acc + column term + row term (+ border-class delta); the column terms are always
-    // staged in shared memory here (zeros when the contraction has none)
+    const uint32_t mul = static_cast<uint32_t>(p.epi.sr_mul);
     int32_t v[W];
 #pragma unroll
     for (int j = 0; j < W; j += 4) {
         const int4 c = *reinterpret_cast<const int4*>(colterm + n0 + j);
-        v[j + 0] = static_cast<int32_t>(acc[j + 0] + static_cast<uint32_t>(c.x) + static_cast<uint32_t>(rowterm));
-        v[j + 1] = static_cast<int32_t>(acc[j + 1] + static_cast<uint32_t>(c.y) + static_cast<uint32_t>(rowterm));
-        v[j + 2] = static_cast<int32_t>(acc[j + 2] + static_cast<uint32_t>(c.z) + static_cast<uint32_t>(rowterm));
-        v[j + 3] = static_cast<int32_t>(acc[j + 3] + static_cast<uint32_t>(c.w) + static_cast<uint32_t>(rowterm));
+        v[j + 0] = static_cast<int32_t>(acc[j + 0] * mul + static_cast<uint32_t>(c.x));
+        v[j + 1] = static_cast<int32_t>(acc[j + 1] * mul + static_cast<uint32_t>(c.y));
+        v[j + 2] = static_cast<int32_t>(acc[j + 2] * mul + static_cast<uint32_t>(c.z));
+        v[j + 3] = static_cast<int32_t>(acc[j + 3] * mul + static_cast<uint32_t>(c.w));
+    }
+    if (has_rowterm) {
+#pragma unroll
+        for (int j = 0; j < W; ++j) v[j] = static_cast<int32_t>(static_cast<uint32_t>(v[j]) + static_cast<uint32_t>(rowterm));
     }
     if (delta != nullptr) {
         const int4* d4 = reinterpret_cast<const int4*>(delta + n0);
@@ -422,20 +395,28 @@ __device__ __forceinline__ void fast_chunk_i8(const GemmParams& p, const uint32_
             v[j + 3] = static_cast<int32_t>(static_cast<uint32_t>(v[j + 3]) + static_cast<uint32_t>(c.w));
         }
     }
+    const int32_t k2 = p.epi.sr_k2;
+    auto one = [&](int32_t x, int32_t m, int32_t sh, int32_t c) -> int32_t {
+        int32_t add = c;
+        if (DBL) add += (x >> 31) * k2;  // -2^(31-d) for a negative value
+        int32_t h;
+        asm("mad.hi.s32 %0, %1, %2, %3;" : "=r"(h) : "r"(x), "r"(m), "r"(add));
+        return h >> sh;
+    };
     if constexpr (PC) {
 #pragma unroll
         for (int j = 0; j < W; j += 4) {
             const int4 m4 = *reinterpret_cast<const int4*>(fm + n0 + j);
             const int4 s4 = *reinterpret_cast<const int4*>(fsh + n0 + j);
-            const int4 h4 = *reinterpret_cast<const int4*>(fhz + n0 + j);
-            v[j + 0] = rescale_f2<DBL>(v[j + 0], m4.x, s4.x, h4.x);
-            v[j + 1] = rescale_f2<DBL>(v[j + 1], m4.y, s4.y, h4.y);
-            v[j + 2] = rescale_f2<DBL>(v[j + 2], m4.z, s4.z, h4.z);
-            v[j + 3] = rescale_f2<DBL>(v[j + 3], m4.w, s4.w, h4.w);
+            const int4 c4 = *reinterpret_cast<const int4*>(fc + n0 + j);
+            v[j + 0] = one(v[j + 0], m4.x, s4.x, c4.x);
+            v[j + 1] = one(v[j + 1], m4.y, s4.y, c4.y);
+            v[j + 2] = one(v[j + 2], m4.z, s4.z, c4.z);
+            v[j + 3] = one(v[j + 3], m4.w, s4.w, c4.w);
         }
     } else {
 #pragma unroll
-        for (int j = 0; j < W; ++j) v[j] = rescale_f2<DBL>(v[j], fk.m, fk.sh, fk.hz);
+        for (int j = 0; j < W; ++j) v[j] = one(v[j], fk.m, fk.sh, fk.c);
     }
     if (fk.add_zp != 0) {
 #pragma unroll
@@ -737,8 +718,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         FastConst fk{0, 0, 0, 0, false, false, false};
         if constexpr (kFast) {
             fk.m = __ldg(e.fq_m);
-            fk.sh = __ldg(e.fq_sh);
-            fk.hz = __ldg(e.fq_hz);
+            fk.sh = __ldg(e.sr_sh);
+            fk.c = __ldg(e.sr_c);
             fk.add_zp = e.rs_zp_folded ? 0 : e.rs.out_zp;
             fk.clamp_lo = e.rs.lo > -128;
             fk.clamp_hi = e.rs.hi < 127;
@@ -792,8 +773,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     cst[et] = e.colterm != nullptr ? e.colterm[b * e.colterm_bstride + n] : 0;
                     if constexpr (kPC) {
                         cst[256 + et] = __ldg(e.fq_m + n);
-                        cst[512 + et] = __ldg(e.fq_sh + n);
-                        cst[768 + et] = __ldg(e.fq_hz + n);
+                        cst[512 + et] = __ldg(e.sr_sh + n);
+                        cst[768 + et] = __ldg(e.sr_c + n);
                     }
                 }
                 if (!epi_sync()) { ok = false; break; }
@@ -853,20 +834,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     if constexpr (GW == 64) {
                         __syncwarp();
                         tmem_ld_32x32b_x32(taddr + g0 + kChunkF, fB);
-                        fast_chunk_i8<EK, kChunkF>(p, fA, nb + g0, rowterm, cst_n, delta, fm, fsh, fhz, fk, pk);
+                        fast_chunk_i8<EK, kChunkF>(p, fA, nb + g0, rowterm, need_rowsum, cst_n, delta, fm, fsh, fhz, fk, pk);
                         wst[lane * 4 + (0 ^ swz)] = pk[0];
                         wst[lane * 4 + (1 ^ swz)] = pk[1];
                         __syncwarp();
                         tmem_wait_regs(fB);
                         if (g0 + GW < HALF) tmem_ld_32x32b_x32(taddr + g0 + GW, fA);
-                        fast_chunk_i8<EK, kChunkF>(p, fB, nb + g0 + kChunkF, rowterm, cst_n, delta, fm, fsh,
-                                                   fhz, fk, pk);
+                        fast_chunk_i8<EK, kChunkF>(p, fB, nb + g0 + kChunkF, rowterm, need_rowsum, cst_n, delta, fm,
+                                                   fsh, fhz, fk, pk);
                         wst[lane * 4 + (2 ^ swz)] = pk[0];
                         wst[lane * 4 + (3 ^ swz)] = pk[1];
                         __syncwarp();
                         if (g0 + GW < HALF) tmem_wait_regs(fA);
                     } else {
-                        fast_chunk_i8<EK, kChunkF>(p, fA, nb + g0, rowterm, cst_n, delta, fm, fsh, fhz, fk, pk);
+                        fast_chunk_i8<EK, kChunkF>(p, fA, nb + g0, rowterm, need_rowsum, cst_n, delta, fm, fsh, fhz, fk, pk);
                         wst[lane * 4 + (0 ^ swz)] = pk[0];
                         wst[lane * 4 + (1 ^ swz)] = pk[1];
                     }
