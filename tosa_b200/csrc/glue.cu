@@ -189,13 +189,14 @@ __device__ __forceinline__ int32_t small_rescale(int32_t x, int32_t m, int s, lo
 // Residual chain, int8 in and out, 16 elements per thread and step. The two input
 // RESCALEs are functions of one int8 value each, tabulated per block in shared
 // memory (error-free constants of ResidualFast): entry e (the input byte) holds
-// 32 copies of table a's value then 32 copies of table b's, 256 bytes per entry, so
-// lane l reads word l of the copies (bank l, conflict-free) at the byte address
-// e * 256 + [128] + 4 l, which one byte permute builds from the input word. The
+// 16 copies of table a's value then 16 copies of table b's, 128 bytes per entry, so
+// lane l reads word l % 16 of the copies (at most two lanes per bank) at the byte
+// address e * 128 + [64] + 4 (l % 16), one shift and one bit-select from the input
+// word; 32 KB per block (more resident blocks than 64 KB tables allow). The
 // output RESCALE uses the fast-path arrays (every shift in [33, 62], multiplier
 // >= 0), as the GEMM epilogue does; saturating packs and the fused CLAMP finish
 // the range. Two steps are loaded before either is processed (more bytes in flight).
-constexpr int kResidLutBytes = 256 * 256;
+constexpr int kResidLutBytes = 256 * 128;
 
 template <bool PC, bool DBL, bool SMALL>
 __global__ void __launch_bounds__(256) residual_fast_i8(const uint4* __restrict__ a, const uint4* __restrict__ b,
@@ -204,17 +205,17 @@ __global__ void __launch_bounds__(256) residual_fast_i8(const uint4* __restrict_
                                                         const int32_t* __restrict__ fhz, int32_t lo, int32_t hi,
                                                         int32_t add_zp, long long n16, int channels,
                                                         uint4* __restrict__ out) {
-    extern __shared__ __align__(16) int32_t lut[];  // [256 entries][a x 32 | b x 32]
-    for (int i = threadIdx.x; i < 256 * 32; i += blockDim.x) {
-        const int e = i >> 5, c = i & 31;
+    extern __shared__ __align__(16) int32_t lut[];  // [256 entries][a x 16 | b x 16]
+    for (int i = threadIdx.x; i < 256 * 16; i += blockDim.x) {
+        const int e = i >> 4, c = i & 15;
         const int32_t v = static_cast<int8_t>(static_cast<uint8_t>(e));
         const int ks = SMALL ? f.k : 0;  // small-range path: values pre-shifted (no overflow by the host's bound)
-        lut[e * 64 + c] = static_cast<int32_t>(static_cast<uint32_t>(small_rescale(v - f.za, f.ma, f.sa, f.ra_pos, f.ra_neg)) << ks);
-        lut[e * 64 + 32 + c] = static_cast<int32_t>(static_cast<uint32_t>(small_rescale(v - f.zb, f.mb, f.sb, f.rb_pos, f.rb_neg)) << ks);
+        lut[e * 32 + c] = static_cast<int32_t>(static_cast<uint32_t>(small_rescale(v - f.za, f.ma, f.sa, f.ra_pos, f.ra_neg)) << ks);
+        lut[e * 32 + 16 + c] = static_cast<int32_t>(static_cast<uint32_t>(small_rescale(v - f.zb, f.mb, f.sb, f.rb_pos, f.rb_neg)) << ks);
     }
     __syncthreads();
     const char* lut_b8 = reinterpret_cast<const char*>(lut);
-    const uint32_t la = (threadIdx.x & 31) * 4u, lb = la + 128u;
+    const uint32_t la = (threadIdx.x & 15) * 4u, lb = la + 64u;
     const int32_t m0 = __ldg(fm), sh0 = __ldg(fsh), hz0 = __ldg(fhz);
     const bool clamp_lo = lo > -128, clamp_hi = hi < 127;
     auto step = [&](long long q, const uint4& av, const uint4& bv) {
@@ -228,9 +229,11 @@ __global__ void __launch_bounds__(256) residual_fast_i8(const uint4* __restrict_
             for (int j = 0; j < 4; ++j) {
                 const int k = 4 * w + j;
                 // byte 0 = the lane's word offset, byte 1 = the input byte (the entry), bytes 2-3 = 0
-                const uint32_t sel = 0x5504u | (static_cast<uint32_t>(j) << 4);
-                const int32_t ta = *reinterpret_cast<const int32_t*>(lut_b8 + __byte_perm(aw[w], la, sel));
-                const int32_t tb = *reinterpret_cast<const int32_t*>(lut_b8 + __byte_perm(bw[w], lb, sel));
+                // byte j of the word times 128: bits 7..14, then the lane's word offset
+                const uint32_t ea = j == 0 ? aw[w] << 7 : aw[w] >> (8 * j - 7);
+                const uint32_t eb = j == 0 ? bw[w] << 7 : bw[w] >> (8 * j - 7);
+                const int32_t ta = *reinterpret_cast<const int32_t*>(lut_b8 + ((ea & 0x7f80u) | la));
+                const int32_t tb = *reinterpret_cast<const int32_t*>(lut_b8 + ((eb & 0x7f80u) | lb));
                 const int32_t sum = static_cast<int32_t>(static_cast<uint32_t>(ta) + static_cast<uint32_t>(tb));
                 if (SMALL) {
                     int32_t x = f.oc;
@@ -371,8 +374,8 @@ tb_status launch_residual(tb_context* ctx, const void* a, int a_dt, int a_uns, i
         aligned16(a) && aligned16(b) && aligned16(out)) {
         const long long n16 = count / 16;
         const int32_t add_zp = ro.zp_folded ? 0 : ro.out_zp;
-        // persistent: three 64 KB-table blocks per SM, each thread two 16-element steps per pass
-        const int grid = static_cast<int>(std::min<long long>((n16 + 511) / 512, 3ll * ctx->num_sms));
+        // persistent: four blocks per SM (the register file's limit at 64 registers), two 16-element steps per pass
+        const int grid = static_cast<int>(std::min<long long>((n16 + 511) / 512, 4ll * ctx->num_sms));
         const bool dbl = ro.rounding == TB_ROUND_DOUBLE;
         auto A = static_cast<const uint4*>(a);
         auto B = static_cast<const uint4*>(b);
