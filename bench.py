@@ -135,7 +135,9 @@ class MatmulWorkload:
         return self.ops / (ms * 1e-3) / 1e12, "TOPS (int8)", ms, 1
 
     def close(self):
-        self.L.load().tb_matmul_plan_destroy(self.plan)
+        if getattr(self, "plan", None) is not None:
+            self.L.load().tb_matmul_plan_destroy(self.plan)
+            self.plan = None
 
     # -- CPU (oracle restatement)
     def cpu_run(self, rows, threads):
@@ -276,23 +278,30 @@ class GraphWorkload:
         return 2 * tot_macs / (tot_ms * 1e-3) / 1e12, "TOPS (int8)", tot_ms / n, len(tc_ops)
 
     def close(self):
-        self.it.close()
+        if getattr(self, "it", None) is not None:
+            self.it.close()
+        if getattr(self, "_pool", None) is not None:
+            self._pool.close()
+            self._pool.join()
+            self._pool = None
 
     # -- CPU (oracle restatement): whole images through the graph
     def cpu_run(self, images, threads):
-        d1, _ = self.builder(1)
+        if not hasattr(self, "_d1"):
+            self._d1, _ = self.builder(1)
         imgs = [self.images[i % self.batch][None] for i in range(images)]
         if threads > 1:
-            import multiprocessing as mp
-            with mp.get_context("spawn").Pool(threads) as pool:
-                pool.starmap(_oracle_image, [(d1, im) for im in imgs])
+            if getattr(self, "_pool", None) is None:
+                import multiprocessing as mp
+                self._pool = mp.get_context("spawn").Pool(threads)  # kept for every step of the run
+            self._pool.starmap(_oracle_image, [(self._d1, im) for im in imgs])
         else:
             for im in imgs:
-                _oracle_image(d1, im)
+                _oracle_image(self._d1, im)
         return images
 
     def cpu_default(self, args):
-        return 1
+        return 3  # about 15 s of single-core work
 
     def ref_default(self, args):
         return os.cpu_count() or 1
@@ -448,6 +457,8 @@ def run_reference(args, wl):
                              "sample": wl.cpu_sample_desc(sample, threads)},
             "e2e": {"value": value, "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+    if hasattr(wl, "close"):
+        wl.close()
     return 0
 
 
