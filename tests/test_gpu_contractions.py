@@ -354,6 +354,14 @@ def test_conv2d_float_tensor_core(ctx, dt, out_dt):
     (2, 28, 28, 96, 1, 3, 3, (1, 1, 1, 1), (1, 1), (1, 1), -5, 3),
     (1, 16, 16, 64, 1, 3, 3, (0, 1, 0, 1), (2, 2), (1, 1), 7, 0),
     (2, 5, 6, 2, 3, 3, 3, (1, 1, 0, 1), (2, 2), (1, 2), 53, 39),
+    # dp2a kernel: 4 pixels x 4 channels per thread, 3- and 5-wide rows, strides 1 and 2
+    (3, 19, 23, 32, 1, 3, 3, (1, 1, 1, 1), (1, 1), (1, 1), -128, 0),   # a partial last pixel group
+    (2, 21, 17, 48, 1, 5, 5, (2, 2, 2, 2), (1, 1), (1, 1), 127, -1),
+    (2, 22, 26, 80, 1, 5, 5, (1, 2, 2, 1), (2, 2), (1, 1), 9, 2),       # asymmetric pads
+    (1, 13, 13, 1040, 1, 3, 3, (1, 1, 1, 1), (2, 1), (1, 1), -3, 0),   # 260 channel words: two chunks
+    (2, 14, 15, 16, 1, 3, 3, (2, 2, 1, 1), (1, 2), (2, 1), 4, 1),       # vertical dilation
+    (1, 9, 9, 24, 1, 3, 3, (0, 0, 0, 0), (1, 1), (1, 1), 6, -100),     # w - zw beyond a byte (9 bits)
+    (1, 9, 11, 8, 1, 3, 5, (1, 1, 2, 2), (1, 1), (1, 2), -1, 1),       # horizontal dilation: vec4 kernel
 ])
 def test_depthwise_int8(ctx, case):
     n, ih, iw, c, m, kh, kw, pad, stride, dil, zx, zw = case
@@ -380,6 +388,58 @@ def test_depthwise_int8_fused_rescale_clamp(ctx):
     rc, r = H.oracle_rescale(acc, L.DT_INT32, L.DT_INT8, mult, shift, 0, 3, 1, L.ROUND_DOUBLE, 1)
     assert rc == 0
     assert np.array_equal(got.reshape(-1).astype(np.int64), np.clip(r, 0, 127))
+
+
+@pytest.mark.parametrize("case", [
+    # (n, ih, iw, c, k, stride, pad, zx, zw, per_channel, rounding, shift range, out_dtype, bias_len)
+    (2, 30, 30, 96, 3, 1, 1, -128, 0, True, L.ROUND_DOUBLE, (33, 38), L.DT_INT8, 96),
+    (1, 27, 29, 64, 5, 2, 2, 17, 0, False, L.ROUND_SINGLE, (35, 36), L.DT_INT8, 1),
+    (2, 17, 19, 32, 3, 2, 1, 3, -2, True, L.ROUND_SINGLE, (40, 46), L.DT_INT8, 32),
+    (1, 13, 14, 40, 3, 1, 1, -7, 0, True, L.ROUND_DOUBLE, (20, 30), L.DT_INT8, 40),   # shifts below 33: general form
+    (1, 12, 11, 24, 5, 1, 2, 5, 1, True, L.ROUND_DOUBLE, (33, 40), L.DT_INT16, 24),
+])
+def test_depthwise_int8_rescale_forms(ctx, case):
+    n, ih, iw, c, k, st, pd, zx, zw, pc, rnd, srange, odt, blen = case
+    rng = np.random.default_rng(n * 1000 + c + k)
+    x = rng.integers(-128, 128, (n, ih, iw, c), dtype=np.int64)
+    w = rng.integers(-127, 128, (k, k, c, 1), dtype=np.int64)
+    bias = rng.integers(-20000, 20000, blen, dtype=np.int64)
+    nch = c if pc else 1
+    mult = rng.integers(1 << 30, (1 << 31) - 1, nch)
+    shift = rng.integers(srange[0], srange[1] + 1, nch)
+    ozp = -4 if odt == L.DT_INT8 else 0  # RESCALE allows an output zero point on int8 only
+    lo, hi = (-120, 110) if odt == L.DT_INT8 else (-32768, 32767)
+    attr = L.rescale_attr(mult, shift, rounding=rnd, output_zp=ozp, out_dtype=odt, clamp=(lo, hi))
+    pad, stride = (pd, pd, pd, pd), (st, st)
+    got = run_conv(ctx, x, w, bias, zx, zw, pad, stride, (1, 1), rescale=attr, depthwise=True)
+    acc = H.oracle_conv_int(x, w, bias, zx, zw, pad, stride, (1, 1), depthwise=True)
+    rc, r = H.oracle_rescale(acc, L.DT_INT32, odt, mult, shift, 0, ozp, 1, rnd, int(pc))
+    assert rc == 0
+    assert np.array_equal(got.reshape(-1).astype(np.int64), np.clip(r, lo, hi))
+
+
+@pytest.mark.parametrize("rows", [1, 2, 3, 4, 5, 8])
+@pytest.mark.parametrize("stride", [1, 2])
+def test_depthwise_int8_strips(ctx, monkeypatch, rows, stride):
+    """3x3 strips of several output rows per block: every phase of the row-buffer rotation,
+    loop-back and a remainder strip, against the oracle (int32 and fused int8 RESCALE)."""
+    monkeypatch.setenv("TB_DEPTHWISE_STRIP_ROWS", str(rows))
+    rng = np.random.default_rng(rows * 10 + stride)
+    n, ih, iw, c = 2, 19, 21, 40
+    pad = (1, 1, 1, 1)
+    x = rng.integers(-128, 128, (n, ih, iw, c), dtype=np.int64)
+    w = rng.integers(-127, 128, (3, 3, c, 1), dtype=np.int64)
+    bias = rng.integers(-20000, 20000, c, dtype=np.int64)
+    got = run_conv(ctx, x, w, bias, -9, 4, pad, (stride, stride), (1, 1), depthwise=True)
+    acc = H.oracle_conv_int(x, w, bias, -9, 4, pad, (stride, stride), (1, 1), depthwise=True)
+    assert np.array_equal(got.astype(np.int64), acc)
+    mult = rng.integers(1 << 30, (1 << 31) - 1, c)
+    shift = rng.integers(34, 39, c)
+    attr = L.rescale_attr(mult, shift, rounding=L.ROUND_DOUBLE, output_zp=-2, out_dtype=L.DT_INT8, clamp=(-100, 127))
+    got = run_conv(ctx, x, w, bias, -9, 4, pad, (stride, stride), (1, 1), rescale=attr, depthwise=True)
+    rc, r = H.oracle_rescale(acc, L.DT_INT32, L.DT_INT8, mult, shift, 0, -2, 1, L.ROUND_DOUBLE, 1)
+    assert rc == 0
+    assert np.array_equal(got.reshape(-1).astype(np.int64), np.clip(r, -100, 127))
 
 
 POOL_CASES = [

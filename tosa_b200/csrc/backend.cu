@@ -695,7 +695,8 @@ struct tb_conv2d_plan {
     bool depthwise = false;
     int oh = 0, ow = 0;
     int path = 0;  // 0 TC int8, 1 TC f16/bf16, 2 direct int, 3 direct float, 4 dw int vec4, 5 dw int, 6 dw float,
-                   // 7 direct INT16 x INT8 -> INT48 (conv or depthwise)
+                   // 7 direct INT16 x INT8 -> INT48 (conv or depthwise), 8 im2col rows + 1x1 TC int8,
+                   // 9 dw int8 on dp2a (depthwise_i8_dp2a)
     const void* weight = nullptr;
     const void* bias = nullptr;
     RescalePlan rs;
@@ -717,7 +718,53 @@ struct tb_conv2d_plan {
     int8_t* d_wpad = nullptr;       // [oc][kp]
     int kp = 0;
     int segp = 0;                   // path 8: bytes per filter-row segment of a row (KW * IC rounded up to words)
+    // path 9 (depthwise int8 on dp2a): [taps][ic] masked weight words, then bias2 [ic]
+    uint32_t* d_dw = nullptr;
+    int strip_rows = 0;             // output rows per block of the 3x3 strip kernel (0: chosen per launch)
 };
+
+// Path 9 tables (depthwise_i8_dp2a): the masked 16-bit weight words and the bias with the
+// input zero point's terms taken out, from the weight and bias contents at plan creation.
+// Leaves the plan on path 4 when the input zero point does not fit a signed byte.
+static tb_status prepare_dw_dp2a(tb_conv2d_plan* p) {
+    const tb_conv2d_desc& d = p->d;
+    const int c = d.ic;
+    const long long taps = static_cast<long long>(d.kh) * d.kw;
+    if (d.input_zp < -128 || d.input_zp > 127) return TB_OK;
+    std::vector<int8_t> w(static_cast<size_t>(taps * c));
+    std::vector<int32_t> bias(static_cast<size_t>(d.bias_len));
+    TB_CUDA(cudaMemcpy(w.data(), p->weight, w.size(), cudaMemcpyDeviceToHost));
+    TB_CUDA(cudaMemcpy(bias.data(), p->bias, sizeof(int32_t) * bias.size(), cudaMemcpyDeviceToHost));
+    std::vector<uint32_t> blob(static_cast<size_t>(taps * c + c), 0);
+    std::vector<long long> wsum(c, 0);
+    for (long long t = 0; t < taps; ++t)
+        for (int ch = 0; ch < c; ++ch) {
+            const int wv = w[static_cast<size_t>(t * c + ch)] - d.weight_zp;
+            if (wv < -32768 || wv > 32767) return TB_OK;
+            wsum[ch] += wv;
+            blob[static_cast<size_t>(t * c + ch)] = static_cast<uint32_t>(static_cast<uint16_t>(wv)) << (16 * (ch & 1));
+        }
+    for (int ch = 0; ch < c; ++ch) {
+        const long long b = bias[d.bias_len == 1 ? 0 : ch];
+        blob[static_cast<size_t>(taps * c + ch)] =
+            static_cast<uint32_t>(static_cast<unsigned long long>(b - static_cast<long long>(d.input_zp) * wsum[ch]));
+    }
+    TB_CUDA(cudaMalloc(&p->d_dw, sizeof(uint32_t) * blob.size()));
+    TB_CUDA(cudaMemcpy(p->d_dw, blob.data(), sizeof(uint32_t) * blob.size(), cudaMemcpyHostToDevice));
+    // strip height override (tests use it to run several rows per block on small shapes)
+    if (const char* ev = std::getenv("TB_DEPTHWISE_STRIP_ROWS")) p->strip_rows = std::max(0, std::atoi(ev));
+    p->path = 9;
+    return TB_OK;
+}
+
+template <int K, int SW>
+static void launch_dw_dp2a(int ek, dim3 grid, dim3 block, cudaStream_t st, const DwGeom& g, const uint32_t* x,
+                           const uint4* wm, const int32_t* b2, uint32_t zxw, const DwEpi& e, void* out,
+                           uint32_t* err) {
+    if (ek == 2) depthwise_i8_dp2a<K, SW, 2><<<grid, block, 0, st>>>(g, x, wm, b2, zxw, e, out, err);
+    else if (ek == 1) depthwise_i8_dp2a<K, SW, 1><<<grid, block, 0, st>>>(g, x, wm, b2, zxw, e, out, err);
+    else depthwise_i8_dp2a<K, SW, 0><<<grid, block, 0, st>>>(g, x, wm, b2, zxw, e, out, err);
+}
 
 static tb_status conv_extent(const char* op, int in, int pb, int pa, int k, int dil, int stride, int* out) {
     // src/ops/conv.rs:54-75
@@ -829,6 +876,11 @@ static tb_status conv_plan_create(tb_context* ctx, const tb_conv2d_desc* d, cons
     }
     if (depthwise) {
         p->path = int8 ? ((d->m == 1 && d->ic % 4 == 0) ? 4 : 5) : 6;
+        if (p->path == 4 && d->dilation[1] == 1 && (d->kw == 3 || d->kw == 5) && d->kh == d->kw &&
+            (d->stride[1] == 1 || d->stride[1] == 2) && d->n <= 65535 && oh <= 65535) {
+            tb_status s = prepare_dw_dp2a(p);
+            if (s != TB_OK) return bail(s);
+        }
         *out = p;
         return TB_OK;
     }
@@ -1027,6 +1079,9 @@ extern "C" TB_API tb_status tb_conv2d_plan_run(tb_conv2d_plan* p, const void* in
     if (total == 0) return TB_OK;
     int path = p->path;
     if (path <= 1 && !aligned16(input)) path = path == 0 ? 2 : 3;
+    // word loads and stores of the vectorised depthwise kernels
+    if ((path == 4 || path == 9) && ((reinterpret_cast<uintptr_t>(input) | reinterpret_cast<uintptr_t>(out)) & 3u))
+        path = 5;
     switch (path) {
     case 2:
         conv2d_direct_int<<<grid_for(ctx, total), 256, 0, st>>>(g, static_cast<const int8_t*>(input),
@@ -1049,6 +1104,64 @@ extern "C" TB_API tb_status tb_conv2d_plan_run(tb_conv2d_plan* p, const void* in
                                                                     ctx->dev_err);
         TB_LAUNCHED(ctx);
         return TB_OK;
+    case 9: {
+        DwGeom dg;
+        dg.ih = d.ih; dg.iw = d.iw; dg.c4 = d.ic / 4; dg.oh = p->oh; dg.ow = p->ow; dg.kh = d.kh;
+        dg.pad_t = d.pad[0]; dg.pad_l = d.pad[2]; dg.sh = d.stride[0]; dg.dh = d.dilation[0];
+        dg.rows = 1;
+        const int cx = std::min(dg.c4, 256);
+        dg.chunks = (dg.c4 + cx - 1) / cx;
+        const int groups = (p->ow + kDwPix - 1) / kDwPix;
+        const int ng = std::min(std::max(1, 256 / cx), groups);
+        const dim3 block(cx, ng);
+        const dim3 grid(dg.chunks * ((groups + ng - 1) / ng), p->oh, d.n);
+        DwEpi e;
+        e.gen = int_epi(p->rs);
+        e.fq_m = p->rs.fq_m;
+        e.fq_sh = p->rs.fq_sh;
+        e.fq_hz = p->rs.fq_hz;
+        e.per_channel = p->rs.per_channel;
+        e.zp_add = p->rs.zp_folded ? 0 : p->rs.out_zp;
+        e.lo = p->rs.lo;
+        e.hi = p->rs.hi;
+        const int ek = (p->rs.enabled && p->rs.fast && p->rs.out_dtype == TB_DT_INT8)
+                           ? (p->rs.rounding == ROUND_DOUBLE ? 2 : 1)
+                           : 0;
+        const uint32_t zxw = static_cast<uint32_t>(static_cast<uint8_t>(d.input_zp)) * 0x01010101u;
+        auto x = static_cast<const uint32_t*>(input);
+        auto wm = reinterpret_cast<const uint4*>(p->d_dw);
+        const int32_t* b2 = reinterpret_cast<const int32_t*>(p->d_dw) + static_cast<long long>(d.kh) * d.kw * d.ic;
+        if (d.kh == 3 && d.stride[0] == d.stride[1] && d.stride[0] <= 2 && d.dilation[0] == 1) {
+            // strips of output rows: about four blocks per SM, at most 16 rows each (longer
+            // strips load fewer rows twice; measured on B200, shorter ones were not faster)
+            const long long row_blocks = static_cast<long long>(grid.x) * d.n;
+            const long long want = 4ll * ctx->num_sms;
+            long long rows = (static_cast<long long>(p->oh) * row_blocks) / std::max(want, 1ll);
+            rows = std::max(1ll, std::min<long long>(rows, std::min(16, p->oh)));
+            if (p->strip_rows > 0) rows = std::min(p->strip_rows, p->oh);
+            dg.rows = static_cast<int>(rows);
+            const dim3 sgrid(grid.x, (p->oh + dg.rows - 1) / dg.rows, d.n);
+            auto x4 = x;
+            if (d.stride[0] == 1) {
+                if (ek == 2) depthwise_i8_dp2a_strip<1, 2><<<sgrid, block, 0, st>>>(dg, x4, wm, b2, zxw, e, out, ctx->dev_err);
+                else if (ek == 1) depthwise_i8_dp2a_strip<1, 1><<<sgrid, block, 0, st>>>(dg, x4, wm, b2, zxw, e, out, ctx->dev_err);
+                else depthwise_i8_dp2a_strip<1, 0><<<sgrid, block, 0, st>>>(dg, x4, wm, b2, zxw, e, out, ctx->dev_err);
+            } else {
+                if (ek == 2) depthwise_i8_dp2a_strip<2, 2><<<sgrid, block, 0, st>>>(dg, x4, wm, b2, zxw, e, out, ctx->dev_err);
+                else if (ek == 1) depthwise_i8_dp2a_strip<2, 1><<<sgrid, block, 0, st>>>(dg, x4, wm, b2, zxw, e, out, ctx->dev_err);
+                else depthwise_i8_dp2a_strip<2, 0><<<sgrid, block, 0, st>>>(dg, x4, wm, b2, zxw, e, out, ctx->dev_err);
+            }
+            TB_LAUNCHED(ctx);
+            return TB_OK;
+        }
+        const int key = d.kw * 10 + d.stride[1];
+        if (key == 31) launch_dw_dp2a<3, 1>(ek, grid, block, st, dg, x, wm, b2, zxw, e, out, ctx->dev_err);
+        else if (key == 32) launch_dw_dp2a<3, 2>(ek, grid, block, st, dg, x, wm, b2, zxw, e, out, ctx->dev_err);
+        else if (key == 51) launch_dw_dp2a<5, 1>(ek, grid, block, st, dg, x, wm, b2, zxw, e, out, ctx->dev_err);
+        else launch_dw_dp2a<5, 2>(ek, grid, block, st, dg, x, wm, b2, zxw, e, out, ctx->dev_err);
+        TB_LAUNCHED(ctx);
+        return TB_OK;
+    }
     case 5:
         depthwise_int_generic<<<grid_for(ctx, total), 256, 0, st>>>(g, static_cast<const int8_t*>(input),
                                                                    static_cast<const int8_t*>(p->weight),
@@ -1171,6 +1284,7 @@ extern "C" TB_API void tb_conv2d_plan_destroy(tb_conv2d_plan* p) {
     if (p->d_rowclass) cudaFree(p->d_rowclass);
     if (p->d_colclass) cudaFree(p->d_colclass);
     if (p->d_fbias) cudaFree(p->d_fbias);
+    if (p->d_dw) cudaFree(p->d_dw);
     delete p;
 }
 

@@ -434,6 +434,307 @@ __global__ void depthwise_int_vec4(ConvGeomDev g, const int8_t* __restrict__ x, 
     if (lerr) atomicOr(err, lerr);
 }
 
+// DEPTHWISE_CONV2D int8 with multiplier 1, channels a multiple of 4 and no horizontal
+// dilation: one thread computes 4 channels (one input word) of kDwPix consecutive output
+// pixels of a row, with dp2a (two 16-bit x 8-bit products) doing the multiplies. The weight
+// table wm is built on the host when the plan is created: for tap t and channel c, word
+// (t, c) holds w[t][c] - weight_zp (up to 9 bits) as a 16-bit lane, lane c % 2, the other
+// lane zero; dp2a.lo against an input word then adds exactly channel c's product for
+// c % 4 < 2 (input bytes 0 and 1) and dp2a.hi for c % 4 >= 2. Taps that fall outside the input
+// read the input zero point zx instead of being skipped, and
+// bias2[c] = bias[c] - zx * sum_t (w[t][c] - weight_zp) takes those terms back out:
+//   sum over valid taps of (x - zx)(w - zw) = sum over all taps of x~ (w - zw) - zx sum_t (w - zw).
+struct DwGeom {
+    int ih, iw, c4, oh, ow, kh;
+    int pad_t, pad_l, sh, dh;
+    int chunks;  // channel chunks of blockDim.x words per pixel group
+    int rows;    // output rows per block (strip kernel)
+};
+
+// Epilogue of the dp2a depthwise kernel: the general RESCALE (per value) or the fast form
+// of rescale_f2 with the plan's fq arrays (per channel when per_channel, else entry 0).
+struct DwEpi {
+    IntEpiDev gen;
+    const int32_t* fq_m;
+    const int32_t* fq_sh;
+    const int32_t* fq_hz;
+    int per_channel;
+    int32_t zp_add;  // the output zero point when it is not folded into fq_hz
+    int32_t lo, hi;
+};
+
+constexpr int kDwPix = 4;
+
+// Multiply-accumulates of one thread's K x K window (rows ky, columns kx) into acc. CHECK:
+// the window may cross the input's border (positions outside read the zero-point word).
+template <int K, int SW, bool CHECK>
+__device__ __forceinline__ void dw_window(int (&acc)[kDwPix][4], const uint32_t* __restrict__ xb,
+                                          const uint4* __restrict__ wb, long long row_step, int cw, int iy0,
+                                          int dh, int ih, uint32_t colmask, uint32_t zxw) {
+    constexpr int P = kDwPix;
+    constexpr int NC = (P - 1) * SW + K;
+    int coff[NC];
+#pragma unroll
+    for (int j = 0; j < NC; ++j) coff[j] = j * cw;
+#pragma unroll
+    for (int ky = 0; ky < K; ++ky) {
+        const uint32_t* xr = xb + ky * row_step;
+        const bool row_ok = !CHECK || static_cast<unsigned>(iy0 + ky * dh) < static_cast<unsigned>(ih);
+        uint32_t xw[NC];
+#pragma unroll
+        for (int j = 0; j < NC; ++j) {
+            if (CHECK) xw[j] = (row_ok && ((colmask >> j) & 1u)) ? __ldg(xr + coff[j]) : zxw;
+            else xw[j] = __ldg(xr + coff[j]);
+        }
+        uint4 wq[K];
+#pragma unroll
+        for (int kx = 0; kx < K; ++kx) wq[kx] = __ldg(wb + (ky * K + kx) * cw);
+#pragma unroll
+        for (int p = 0; p < P; ++p)
+#pragma unroll
+            for (int kx = 0; kx < K; ++kx) {
+                const int xv = static_cast<int>(xw[p * SW + kx]);
+                acc[p][0] = __dp2a_lo(static_cast<int>(wq[kx].x), xv, acc[p][0]);
+                acc[p][1] = __dp2a_lo(static_cast<int>(wq[kx].y), xv, acc[p][1]);
+                acc[p][2] = __dp2a_hi(static_cast<int>(wq[kx].z), xv, acc[p][2]);
+                acc[p][3] = __dp2a_hi(static_cast<int>(wq[kx].w), xv, acc[p][3]);
+            }
+    }
+}
+
+// K x K window (K = 3 or 5), horizontal stride SW. EK: 0 general epilogue (any output type),
+// 1 fast RESCALE to int8 with single rounding, 2 fast RESCALE to int8 with double rounding.
+template <int K, int SW, int EK>
+__global__ void depthwise_i8_dp2a(DwGeom g, const uint32_t* __restrict__ x, const uint4* __restrict__ wm,
+                                  const int32_t* __restrict__ bias2, uint32_t zxw, DwEpi e, void* out,
+                                  uint32_t* err) {
+    constexpr int P = kDwPix;
+    constexpr int NC = (P - 1) * SW + K;  // input columns under P output pixels
+    const int c4 = (blockIdx.x % g.chunks) * blockDim.x + threadIdx.x;
+    const int ox0 = ((blockIdx.x / g.chunks) * blockDim.y + threadIdx.y) * P;
+    if (c4 >= g.c4 || ox0 >= g.ow) return;
+    const int oy = blockIdx.y, b = blockIdx.z;
+    const int cw = g.c4;
+    const int iy0 = oy * g.sh - g.pad_t, ix0 = ox0 * SW - g.pad_l;
+    // the accumulators start from the bias (with the input zero point's terms taken out)
+    const int4 bz = __ldg(reinterpret_cast<const int4*>(bias2) + c4);
+    int acc[P][4];
+#pragma unroll
+    for (int p = 0; p < P; ++p) {
+        acc[p][0] = bz.x;
+        acc[p][1] = bz.y;
+        acc[p][2] = bz.z;
+        acc[p][3] = bz.w;
+    }
+    // word (b, iy0, ix0, c4); only positions inside the input are read through it
+    const long long base = ((static_cast<long long>(b) * g.ih + iy0) * g.iw + ix0) * cw + c4;
+    const long long row_step = static_cast<long long>(g.dh) * g.iw * cw;
+    const uint4* wb = wm + c4;
+    const bool interior = iy0 >= 0 && iy0 + (K - 1) * g.dh < g.ih && ix0 >= 0 && ix0 + NC <= g.iw;
+    if (interior) {
+        dw_window<K, SW, false>(acc, x + base, wb, row_step, cw, iy0, g.dh, g.ih, 0u, zxw);
+    } else {
+        uint32_t colmask = 0;
+#pragma unroll
+        for (int j = 0; j < NC; ++j)
+            colmask |= static_cast<uint32_t>(static_cast<unsigned>(ix0 + j) < static_cast<unsigned>(g.iw)) << j;
+        dw_window<K, SW, true>(acc, x + base, wb, row_step, cw, iy0, g.dh, g.ih, colmask, zxw);
+    }
+    const long long pix0 = (static_cast<long long>(b) * g.oh + oy) * g.ow + ox0;
+    if (EK == 0) {
+        uint32_t lerr = 0;
+        const int c0 = c4 * 4;
+        const long long cn = static_cast<long long>(cw) * 4;
+#pragma unroll
+        for (int p = 0; p < P; ++p) {
+            if (ox0 + p >= g.ow) break;
+            const long long o = (pix0 + p) * cn + c0;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) finish_int(e.gen, acc[p][q], c0 + q, out, o + q, &lerr);
+        }
+        if (lerr) atomicOr(err, lerr);
+    } else {
+        const int pc = e.per_channel ? c4 : 0;
+        const int4 m = __ldg(reinterpret_cast<const int4*>(e.fq_m) + pc);
+        const int4 sh = __ldg(reinterpret_cast<const int4*>(e.fq_sh) + pc);
+        const int4 hz = __ldg(reinterpret_cast<const int4*>(e.fq_hz) + pc);
+        uint32_t* o = static_cast<uint32_t*>(out) + pix0 * cw + c4;
+#pragma unroll
+        for (int p = 0; p < P; ++p) {
+            if (ox0 + p >= g.ow) break;
+            int32_t r[4];
+            r[0] = rescale_f2<EK == 2>(acc[p][0], m.x, sh.x, hz.x);
+            r[1] = rescale_f2<EK == 2>(acc[p][1], m.y, sh.y, hz.y);
+            r[2] = rescale_f2<EK == 2>(acc[p][2], m.z, sh.z, hz.z);
+            r[3] = rescale_f2<EK == 2>(acc[p][3], m.w, sh.w, hz.w);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) r[q] = min(max(r[q] + e.zp_add, e.lo), e.hi);
+            o[p * cw] = pack4_sat_i8(r[0], r[1], r[2], r[3]);
+        }
+    }
+}
+
+// 3x3 windows with equal strides S (1 or 2) and no dilation: a thread keeps its 4 channels'
+// 9 weight words in registers and walks down a strip of g.rows output rows, loading per
+// output row only the S input rows that enter the window. The three row buffers rotate
+// roles with period 3, written out as one call per role so that no buffer is ever copied.
+template <int S>
+struct DwStrip {
+    static constexpr int P = kDwPix;
+    static constexpr int NC = (P - 1) * S + 3;
+};
+
+template <int S>
+__device__ __forceinline__ void dw_load_row(uint32_t (&r)[DwStrip<S>::NC], const uint32_t* __restrict__ xc, int iy,
+                                            const DwGeom& g, long long row_words, bool cols_ok, uint32_t colmask,
+                                            uint32_t zxw) {
+    constexpr int NC = DwStrip<S>::NC;
+    if (static_cast<unsigned>(iy) < static_cast<unsigned>(g.ih)) {
+        const uint32_t* xr = xc + iy * row_words;
+        if (cols_ok) {
+#pragma unroll
+            for (int j = 0; j < NC; ++j) r[j] = __ldg(xr + j * g.c4);
+        } else {
+#pragma unroll
+            for (int j = 0; j < NC; ++j) r[j] = ((colmask >> j) & 1u) ? __ldg(xr + j * g.c4) : zxw;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < NC; ++j) r[j] = zxw;
+    }
+}
+
+// One window row's taps (weights w0, w1, w2) into the P pixels' accumulators.
+template <int S>
+__device__ __forceinline__ void dw_row_mac(int (&acc)[kDwPix][4], const uint32_t (&r)[DwStrip<S>::NC],
+                                           const uint4& w0, const uint4& w1, const uint4& w2) {
+#pragma unroll
+    for (int p = 0; p < kDwPix; ++p)
+#pragma unroll
+        for (int kx = 0; kx < 3; ++kx) {
+            const int xv = static_cast<int>(r[p * S + kx]);
+            const uint4& wq = kx == 0 ? w0 : (kx == 1 ? w1 : w2);
+            acc[p][0] = __dp2a_lo(static_cast<int>(wq.x), xv, acc[p][0]);
+            acc[p][1] = __dp2a_lo(static_cast<int>(wq.y), xv, acc[p][1]);
+            acc[p][2] = __dp2a_hi(static_cast<int>(wq.z), xv, acc[p][2]);
+            acc[p][3] = __dp2a_hi(static_cast<int>(wq.w), xv, acc[p][3]);
+        }
+}
+
+template <int S, int EK>
+__device__ __forceinline__ void dw_strip_row(const uint32_t (&top)[DwStrip<S>::NC], const uint32_t (&mid)[DwStrip<S>::NC],
+                                             const uint32_t (&bot)[DwStrip<S>::NC], const uint4 (&w)[9],
+                                             const int4& bz, const DwEpi& e, const DwGeom& g, int c4, int ox0,
+                                             long long pix0, void* out, uint32_t* lerr) {
+    constexpr int P = DwStrip<S>::P;
+    int acc[P][4];
+#pragma unroll
+    for (int p = 0; p < P; ++p) {
+        acc[p][0] = bz.x;
+        acc[p][1] = bz.y;
+        acc[p][2] = bz.z;
+        acc[p][3] = bz.w;
+    }
+    dw_row_mac<S>(acc, top, w[0], w[1], w[2]);
+    dw_row_mac<S>(acc, mid, w[3], w[4], w[5]);
+    dw_row_mac<S>(acc, bot, w[6], w[7], w[8]);
+    if (EK == 0) {
+        const int c0 = c4 * 4;
+        const long long cn = static_cast<long long>(g.c4) * 4;
+#pragma unroll
+        for (int p = 0; p < P; ++p) {
+            if (ox0 + p >= g.ow) break;
+            const long long o = (pix0 + p) * cn + c0;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) finish_int(e.gen, acc[p][q], c0 + q, out, o + q, lerr);
+        }
+    } else {
+        const int pc = e.per_channel ? c4 : 0;
+        const int4 m = __ldg(reinterpret_cast<const int4*>(e.fq_m) + pc);
+        const int4 sh = __ldg(reinterpret_cast<const int4*>(e.fq_sh) + pc);
+        const int4 hz = __ldg(reinterpret_cast<const int4*>(e.fq_hz) + pc);
+        uint32_t* o = static_cast<uint32_t*>(out) + pix0 * g.c4 + c4;
+#pragma unroll
+        for (int p = 0; p < P; ++p) {
+            if (ox0 + p >= g.ow) break;
+            int32_t v[4];
+            v[0] = rescale_f2<EK == 2>(acc[p][0], m.x, sh.x, hz.x);
+            v[1] = rescale_f2<EK == 2>(acc[p][1], m.y, sh.y, hz.y);
+            v[2] = rescale_f2<EK == 2>(acc[p][2], m.z, sh.z, hz.z);
+            v[3] = rescale_f2<EK == 2>(acc[p][3], m.w, sh.w, hz.w);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) v[q] = min(max(v[q] + e.zp_add, e.lo), e.hi);
+            o[p * g.c4] = pack4_sat_i8(v[0], v[1], v[2], v[3]);
+        }
+    }
+}
+
+template <int S, int EK>
+__global__ void depthwise_i8_dp2a_strip(DwGeom g, const uint32_t* __restrict__ x, const uint4* __restrict__ wm,
+                                        const int32_t* __restrict__ bias2, uint32_t zxw, DwEpi e, void* out,
+                                        uint32_t* err) {
+    constexpr int NC = DwStrip<S>::NC;
+    const int c4 = (blockIdx.x % g.chunks) * blockDim.x + threadIdx.x;
+    const int ox0 = ((blockIdx.x / g.chunks) * blockDim.y + threadIdx.y) * DwStrip<S>::P;
+    if (c4 >= g.c4 || ox0 >= g.ow) return;
+    const int b = blockIdx.z;
+    const int oy0 = blockIdx.y * g.rows;
+    const int oy1 = min(oy0 + g.rows, g.oh);
+    const int ix0 = ox0 * S - g.pad_l;
+    uint32_t colmask = 0;
+#pragma unroll
+    for (int j = 0; j < NC; ++j)
+        colmask |= static_cast<uint32_t>(static_cast<unsigned>(ix0 + j) < static_cast<unsigned>(g.iw)) << j;
+    const bool cols_ok = colmask == (1u << NC) - 1;
+    uint4 w[9];
+#pragma unroll
+    for (int t = 0; t < 9; ++t) w[t] = __ldg(wm + t * g.c4 + c4);
+    const int4 bz = __ldg(reinterpret_cast<const int4*>(bias2) + c4);
+    const long long row_words = static_cast<long long>(g.iw) * g.c4;
+    // column ix0 of row 0 of image b, channel word c4 (read only at columns inside the input)
+    const uint32_t* xc = x + static_cast<long long>(b) * g.ih * row_words + static_cast<long long>(ix0) * g.c4 + c4;
+    long long pix0 = (static_cast<long long>(b) * g.oh + oy0) * g.ow + ox0;
+    int iy = oy0 * S - g.pad_t;  // top input row of the window
+    uint32_t lerr = 0;
+    // window rows (top, mid, bot) rotate with period 3: stride 1 brings one new row per
+    // output row, stride 2 two
+    uint32_t r0[NC], r1[NC], r2[NC];
+    dw_load_row<S>(r0, xc, iy, g, row_words, cols_ok, colmask, zxw);
+    if (S == 1) dw_load_row<S>(r1, xc, iy + 1, g, row_words, cols_ok, colmask, zxw);
+    for (int oy = oy0;;) {
+        // (r0, r1, r2)
+        if (S == 2) dw_load_row<S>(r1, xc, iy + 1, g, row_words, cols_ok, colmask, zxw);
+        dw_load_row<S>(r2, xc, iy + 2, g, row_words, cols_ok, colmask, zxw);
+        dw_strip_row<S, EK>(r0, r1, r2, w, bz, e, g, c4, ox0, pix0, out, &lerr);
+        if (++oy >= oy1) break;
+        iy += S;
+        pix0 += g.ow;
+        if (S == 1) {  // (r1, r2, r0)
+            dw_load_row<S>(r0, xc, iy + 2, g, row_words, cols_ok, colmask, zxw);
+            dw_strip_row<S, EK>(r1, r2, r0, w, bz, e, g, c4, ox0, pix0, out, &lerr);
+        } else {  // (r2, r0, r1)
+            dw_load_row<S>(r0, xc, iy + 1, g, row_words, cols_ok, colmask, zxw);
+            dw_load_row<S>(r1, xc, iy + 2, g, row_words, cols_ok, colmask, zxw);
+            dw_strip_row<S, EK>(r2, r0, r1, w, bz, e, g, c4, ox0, pix0, out, &lerr);
+        }
+        if (++oy >= oy1) break;
+        iy += S;
+        pix0 += g.ow;
+        if (S == 1) {  // (r2, r0, r1)
+            dw_load_row<S>(r1, xc, iy + 2, g, row_words, cols_ok, colmask, zxw);
+            dw_strip_row<S, EK>(r2, r0, r1, w, bz, e, g, c4, ox0, pix0, out, &lerr);
+        } else {  // (r1, r2, r0)
+            dw_load_row<S>(r2, xc, iy + 1, g, row_words, cols_ok, colmask, zxw);
+            dw_load_row<S>(r0, xc, iy + 2, g, row_words, cols_ok, colmask, zxw);
+            dw_strip_row<S, EK>(r1, r2, r0, w, bz, e, g, c4, ox0, pix0, out, &lerr);
+        }
+        if (++oy >= oy1) break;
+        iy += S;
+        pix0 += g.ow;
+    }
+    if (EK == 0 && lerr) atomicOr(err, lerr);
+}
+
 __global__ void depthwise_int_generic(ConvGeomDev g, const int8_t* __restrict__ x, const int8_t* __restrict__ w,
                                       const int32_t* __restrict__ bias, int bias_len, int32_t zx, int32_t zw,
                                       IntEpiDev e, void* out, uint32_t* err) {
