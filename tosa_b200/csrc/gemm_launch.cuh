@@ -1,6 +1,6 @@
 // Launch helpers of the tensor-core GEMM: one template instantiation per tile
-// configuration and epilogue kind. The instantiations are spread over
-// gemm_i8_mm.cu, gemm_i8_conv.cu and gemm_f16.cu, which expose the plain
+// configuration and epilogue kind. The instantiations are spread over gemm_i8_mm.cu,
+// gemm_i8_conv.cu, gemm_i8_conv_k128.cu and gemm_f16.cu, which expose the plain
 // functions declared at the bottom.
 #pragma once
 
@@ -32,12 +32,12 @@ inline FastDiv make_fastdiv(int d) {
     return f;
 }
 
-template <class Cfg, int EK>
+template <class Cfg, int EK, int EF = 0>
 tb_status launch_gemm(tb_context* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB, GemmParams p,
                       cudaStream_t stream) {
     static bool attr_set = false;  // the attribute is per function and process-wide
     if (!attr_set) {
-        TB_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<Cfg, EK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        TB_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<Cfg, EK, EF>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      Cfg::SMEM_BYTES));
         attr_set = true;
     }
@@ -72,7 +72,7 @@ tb_status launch_gemm(tb_context* ctx, const CUtensorMap& tmA, const CUtensorMap
     }
     cfg.attrs = attr;
     cfg.numAttrs = na;
-    TB_CUDA(cudaLaunchKernelEx(&cfg, tc_gemm_kernel<Cfg, EK>, tmA, tmB, p));
+    TB_CUDA(cudaLaunchKernelEx(&cfg, tc_gemm_kernel<Cfg, EK, EF>, tmA, tmB, p));
     TB_GEMM_LAUNCHED(ctx);
     return TB_OK;
 }
@@ -90,26 +90,43 @@ inline int epilogue_kind(const GemmEpilogue& e) {
     return dbl ? EK_FAST_T_D : EK_FAST_T_S;
 }
 
+// The fast int8 epilogue kind EK with its flags: row terms when B has a zero point, border
+// deltas when the convolution has border classes (CONV: only convolutions have them).
+template <class Cfg, int EK, bool CONV>
+tb_status launch_fast_ek(tb_context* ctx, const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p,
+                         cudaStream_t st) {
+    const bool row = p.epi.row_zp_neg != 0;
+    if constexpr (CONV) {
+        if (p.epi.rowclass != nullptr) {
+            return row ? launch_gemm<Cfg, EK, kEfRow | kEfDelta>(ctx, a, b, p, st)
+                       : launch_gemm<Cfg, EK, kEfDelta>(ctx, a, b, p, st);
+        }
+    }
+    return row ? launch_gemm<Cfg, EK, kEfRow>(ctx, a, b, p, st) : launch_gemm<Cfg, EK, 0>(ctx, a, b, p, st);
+}
+
 // Switch over the integer epilogue kinds for one tile configuration.
-template <class Cfg>
+template <class Cfg, bool CONV>
 tb_status launch_int_ek(tb_context* ctx, int ek, const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p,
                         cudaStream_t st) {
     switch (ek) {
     case EK_I32: return launch_gemm<Cfg, EK_I32>(ctx, a, b, p, st);
     case EK_SLOW: return launch_gemm<Cfg, EK_SLOW>(ctx, a, b, p, st);
-    case EK_FAST_T_S: return launch_gemm<Cfg, EK_FAST_T_S>(ctx, a, b, p, st);
-    case EK_FAST_T_D: return launch_gemm<Cfg, EK_FAST_T_D>(ctx, a, b, p, st);
-    case EK_FAST_PC_S: return launch_gemm<Cfg, EK_FAST_PC_S>(ctx, a, b, p, st);
-    case EK_FAST_PC_D: return launch_gemm<Cfg, EK_FAST_PC_D>(ctx, a, b, p, st);
+    case EK_FAST_T_S: return launch_fast_ek<Cfg, EK_FAST_T_S, CONV>(ctx, a, b, p, st);
+    case EK_FAST_T_D: return launch_fast_ek<Cfg, EK_FAST_T_D, CONV>(ctx, a, b, p, st);
+    case EK_FAST_PC_S: return launch_fast_ek<Cfg, EK_FAST_PC_S, CONV>(ctx, a, b, p, st);
+    case EK_FAST_PC_D: return launch_fast_ek<Cfg, EK_FAST_PC_D, CONV>(ctx, a, b, p, st);
     default: return fail(TB_ERR_NOT_ACCELERATED, "no integer epilogue kind %d", ek);
     }
 }
 
-// Implemented in gemm_i8_mm.cu / gemm_i8_conv.cu / gemm_f16.cu.
+// Implemented in gemm_i8_mm.cu / gemm_i8_conv.cu / gemm_i8_conv_k128.cu / gemm_f16.cu.
 tb_status launch_i8_matmul(tb_context* ctx, int bn, int ek, const CUtensorMap& a, const CUtensorMap& b,
                            const GemmParams& p, cudaStream_t st);
 tb_status launch_i8_conv(tb_context* ctx, int bn, int bk, int ek, const CUtensorMap& a, const CUtensorMap& b,
                          const GemmParams& p, cudaStream_t st);
+tb_status launch_i8_conv_k128(tb_context* ctx, int bn, int ek, const CUtensorMap& a, const CUtensorMap& b,
+                              const GemmParams& p, cudaStream_t st);
 tb_status launch_f16_matmul(tb_context* ctx, int bn, const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p,
                             cudaStream_t st);
 tb_status launch_f16_conv(tb_context* ctx, int bn, const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p,

@@ -362,12 +362,18 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, const uint32
 // Fast int8 RESCALE of W consecutive columns, W/16 x 16 packed bytes into out16[]
 // (small-range form, see GemmEpilogue): v' = acc * 2^k + column term [+ row term]
 // [+ border-class delta], all terms pre-multiplied by 2^k (int32 wrap-around; the
-// host's bound makes the sum exact), then r = (mulhi(v', m) + c [- k2 if v' < 0]) >> sh.
-template <int EK, int W>
+// host's bound makes the sum exact), then r = (mulhi(v', m) + c [- k2 if v' < 0]) >> sh,
+// then max(r + zp, lo) [min(., hi)] and saturating packs. ROW (a B zero point) and DELTA
+// (a convolution with border classes) are kernel template flags, so kernels without them
+// carry no code for them; the remaining conditions are uniform across the warp.
+constexpr int kEfRow = 1;
+constexpr int kEfDelta = 2;
+
+template <int EK, int W, bool ROW, bool DELTA>
 __device__ __forceinline__ void fast_chunk_i8(const GemmParams& p, const uint32_t (&acc)[W], int n0, int32_t rowterm,
-                                              bool has_rowterm, const int32_t* colterm, const int32_t* delta,
-                                              const int32_t* fm, const int32_t* fsh, const int32_t* fc,
-                                              const FastConst& fk, uint4 (&out16)[W / 16]) {
+                                              const int32_t* colterm, const int32_t* delta, const int32_t* fm,
+                                              const int32_t* fsh, const int32_t* fc, const FastConst& fk,
+                                              uint4 (&out16)[W / 16]) {
     constexpr bool PC = EK == EK_FAST_PC_S || EK == EK_FAST_PC_D;
     constexpr bool DBL = EK == EK_FAST_T_D || EK == EK_FAST_PC_D;
     const uint32_t mul = static_cast<uint32_t>(p.epi.sr_mul);
@@ -380,11 +386,11 @@ __device__ __forceinline__ void fast_chunk_i8(const GemmParams& p, const uint32_
         v[j + 2] = static_cast<int32_t>(acc[j + 2] * mul + static_cast<uint32_t>(c.z));
         v[j + 3] = static_cast<int32_t>(acc[j + 3] * mul + static_cast<uint32_t>(c.w));
     }
-    if (has_rowterm) {
+    if constexpr (ROW) {
 #pragma unroll
         for (int j = 0; j < W; ++j) v[j] = static_cast<int32_t>(static_cast<uint32_t>(v[j]) + static_cast<uint32_t>(rowterm));
     }
-    if (delta != nullptr) {
+    if (DELTA && delta != nullptr) {  // warp-uniform: null for a warp without border rows
         const int4* d4 = reinterpret_cast<const int4*>(delta + n0);
 #pragma unroll
         for (int j = 0; j < W; j += 4) {
@@ -418,22 +424,16 @@ __device__ __forceinline__ void fast_chunk_i8(const GemmParams& p, const uint32_
 #pragma unroll
         for (int j = 0; j < W; ++j) v[j] = one(v[j], fk.m, fk.sh, fk.c);
     }
-    if (fk.add_zp != 0) {
+    // output zero point (when not folded into c) and the lower clamp in one add-max; the
+    // saturating packs complete the clamp to the int8 range
+    const int32_t zp = fk.add_zp, lo = p.epi.rs.lo;
 #pragma unroll
-        for (int j = 0; j < W; ++j) v[j] += fk.add_zp;
-    }
-    // a bound at the int8 limit is left to the saturating packs
-    if (fk.clamp_lo) {
-        const int32_t lo = p.epi.rs.lo;
-#pragma unroll
-        for (int j = 0; j < W; ++j) v[j] = max(v[j], lo);
-    }
-    if (fk.clamp_hi) {
+    for (int j = 0; j < W; ++j) v[j] = max(v[j] + zp, lo);
+    if (fk.clamp_hi) {  // an upper bound below 127 (uniform; rare)
         const int32_t hi = p.epi.rs.hi;
 #pragma unroll
         for (int j = 0; j < W; ++j) v[j] = min(v[j], hi);
     }
-    // saturating packs complete the clamp to the int8 range
 #pragma unroll
     for (int q = 0; q < W / 16; ++q)
         out16[q] = make_uint4(pack4_sat_i8(v[16 * q + 0], v[16 * q + 1], v[16 * q + 2], v[16 * q + 3]),
@@ -442,7 +442,98 @@ __device__ __forceinline__ void fast_chunk_i8(const GemmParams& p, const uint32_
                               pack4_sat_i8(v[16 * q + 12], v[16 * q + 13], v[16 * q + 14], v[16 * q + 15]));
 }
 
-template <class Cfg, int EK>
+// One epilogue warp's pass over its half of a tile (32 rows x HALF columns) in the fast
+// int8 form: TMEM loads of 32 columns (the next one in flight while this one is rescaled),
+// packing into the warp's shared staging buffer, and row-contiguous stores of 64-byte groups.
+struct FastHalf {
+    uint32_t taddr;         // TMEM address of the half's first column (lane quadrant in the high half)
+    int n_end;              // columns of the half that exist (N - first column)
+    int nb;                 // absolute output column of the half's first column
+    int32_t rowterm;
+    const int32_t* cst_n;   // staged column terms, indexed by absolute column
+    const int32_t* delta;   // border-class delta row, or null when no row of the warp is on a border
+    const int32_t* fm;
+    const int32_t* fsh;
+    const int32_t* fc;
+    uint4* wst;             // the warp's staging buffer [32 rows][4 x 16 B]
+    int lane, swz, mrow0;
+    int8_t* obase;
+    bool vec_ok;
+    long long* ftr;         // trace slots (CTA 0, first tiles) or null
+};
+
+template <int EK, int HALF, bool ROW, bool DELTA>
+__device__ __forceinline__ void fast_half_pass(const GemmParams& p, const FastConst& fk, const FastHalf& h) {
+    constexpr int FW = kChunkF;                // columns per TMEM load
+    constexpr int FPK = FW / 16;               // 16-byte packs per chunk
+    constexpr int GW = HALF < 64 ? HALF : 64;  // columns per staging group
+    constexpr int CPG = GW / kChunk;           // 16-byte slots per row and group: 2 or 4
+    const int lane = h.lane, swz = h.swz;
+    uint32_t fA[FW], fB[FW];
+    __syncwarp();
+    if (h.n_end > 0) {
+        tmem_ld_32x32b(h.taddr, fA);
+        tmem_wait_regs(fA);
+    }
+#pragma unroll 1
+    for (int g0 = 0; g0 < HALF && g0 < h.n_end; g0 += GW) {
+        uint4 pk[FPK];
+        if (h.ftr && g0 / GW < 8) h.ftr[3 * (g0 / GW)] = clock64();
+        if constexpr (GW == 2 * FW) {
+            const bool second = g0 + FW < h.n_end;
+            const bool next = g0 + GW < HALF && g0 + GW < h.n_end;
+            __syncwarp();
+            if (second) tmem_ld_32x32b(h.taddr + g0 + FW, fB);
+            fast_chunk_i8<EK, FW, ROW, DELTA>(p, fA, h.nb + g0, h.rowterm, h.cst_n, h.delta, h.fm, h.fsh, h.fc,
+                                                   fk, pk);
+#pragma unroll
+            for (int j = 0; j < FPK; ++j) h.wst[lane * 4 + (j ^ swz)] = pk[j];
+            __syncwarp();
+            if (second) {
+                tmem_wait_regs(fB);
+                if (next) tmem_ld_32x32b(h.taddr + g0 + GW, fA);
+                fast_chunk_i8<EK, FW, ROW, DELTA>(p, fB, h.nb + g0 + FW, h.rowterm, h.cst_n, h.delta, h.fm,
+                                                       h.fsh, h.fc, fk, pk);
+#pragma unroll
+                for (int j = 0; j < FPK; ++j) h.wst[lane * 4 + ((FPK + j) ^ swz)] = pk[j];
+            }
+            __syncwarp();
+            if (next) tmem_wait_regs(fA);
+        } else {
+            fast_chunk_i8<EK, FW, ROW, DELTA>(p, fA, h.nb + g0, h.rowterm, h.cst_n, h.delta, h.fm, h.fsh, h.fc,
+                                                   fk, pk);
+#pragma unroll
+            for (int j = 0; j < FPK; ++j) h.wst[lane * 4 + (j ^ swz)] = pk[j];
+        }
+        if (h.ftr && g0 / GW < 8) h.ftr[3 * (g0 / GW) + 1] = clock64();
+        __syncwarp();
+#pragma unroll
+        for (int it = 0; it < CPG; ++it) {
+            const int idx = it * 32 + lane;
+            const int r = idx / CPG, k = idx % CPG;
+            const uint4 pv = h.wst[r * 4 + (k ^ ((r >> 1) & 3))];
+            const int mr = h.mrow0 + r;
+            const int n = h.nb + g0 + k * kChunk;
+            if (mr < p.M && n < p.N) {
+                int8_t* o = h.obase + static_cast<long long>(mr) * p.ldo + n;
+                if (h.vec_ok && n + kChunk <= p.N) {
+                    *reinterpret_cast<uint4*>(o) = pv;
+                } else {
+                    const uint32_t w4[4] = {pv.x, pv.y, pv.z, pv.w};
+#pragma unroll
+                    for (int j = 0; j < kChunk; ++j)
+                        if (n + j < p.N) o[j] = static_cast<int8_t>(w4[j >> 2] >> (8 * (j & 3)));
+                }
+            }
+        }
+        if (h.ftr && g0 / GW < 8) h.ftr[3 * (g0 / GW) + 2] = clock64();
+        __syncwarp();
+    }
+}
+
+// EF: flags of the fast int8 epilogue (kEfRow: B zero point row terms; kEfDelta: convolution
+// border classes); 0 for the other epilogue kinds.
+template <class Cfg, int EK, int EF>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
     constexpr int BM = Cfg::BM, BN = Cfg::kBN, S = Cfg::kStages;
@@ -785,13 +876,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             // Border class of this thread's row (before the accumulator wait: the lookups overlap it).
             const int m = mt * BM + row;
             const bool row_ok = m < p.M;
-            const int32_t* delta = nullptr;
-            if (rcls != nullptr && row_ok) {
-                const int rem = m - fdiv(m, p.fd_ohow) * p.conv_OHOW;
-                const int oy = fdiv(rem, p.fd_ow), ox = rem - oy * p.conv_OW;
-                const int cls = rcls[oy] * e.n_col_classes + ccls[ox];
-                if (cls != e.base_class) delta = e.ct_delta + static_cast<long long>(cls) * e.ct_ld;
+            const int32_t* delta = nullptr;       // general epilogue: null for the interior class
+            const int32_t* delta_fast = nullptr;  // fast epilogue: the interior class's row is all zeros
+            if (rcls != nullptr) {
+                int cls = e.base_class;
+                if (row_ok) {
+                    const int rem = m - fdiv(m, p.fd_ohow) * p.conv_OHOW;
+                    const int oy = fdiv(rem, p.fd_ow), ox = rem - oy * p.conv_OW;
+                    cls = rcls[oy] * e.n_col_classes + ccls[ox];
+                }
+                delta_fast = e.ct_delta + static_cast<long long>(cls) * e.ct_ld;
+                if (cls != e.base_class) delta = delta_fast;
             }
+            // whether any row of this warp lies on a border (warp-uniform choice of the fast path)
+            bool warp_delta = false;
+            if constexpr ((EF & kEfDelta) != 0) warp_delta = __any_sync(0xffffffffu, delta != nullptr);
             if (!mbar_wait_bounded(&tfull[buf], tph, abort_flag, limit)) { ok = false; break; }
             tc_fence_after();
             if (p.trace && blockIdx.x == 0 && tcount < 8 && threadIdx.x == 128) p.trace[384 + 2 * tcount] = clock64();
@@ -817,62 +916,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 // swizzled by row) so that the global stores are row-contiguous: a warp writes 8 rows x
                 // 64 B per store instead of 32 scattered 16 B pieces.
                 uint4* wst = reinterpret_cast<uint4*>(scratch + 3072) + (warp - 4) * 128;
-                constexpr int GW = HALF < 64 ? HALF : 64;  // columns per staging group
-                constexpr int CPG = GW / kChunk;           // 16-byte slots per row and group: 2 or 4
                 int8_t* obase = reinterpret_cast<int8_t*>(p.out) + static_cast<long long>(b) * p.out_batch_stride;
                 const bool vec_ok = (p.ldo & 15) == 0 && (p.out_batch_stride & 15) == 0 &&
                                     (reinterpret_cast<uintptr_t>(p.out) & 15) == 0;
                 const int mrow0 = mt * BM + q * 32;
                 const int swz = (lane >> 1) & 3;
-                uint32_t fA[kChunkF], fB[kChunkF];
-                __syncwarp();
-                tmem_ld_32x32b_x32(taddr, fA);
-                tmem_wait_regs(fA);
-#pragma unroll 1
-                for (int g0 = 0; g0 < HALF; g0 += GW) {
-                    uint4 pk[2];
-                    if constexpr (GW == 64) {
-                        __syncwarp();
-                        tmem_ld_32x32b_x32(taddr + g0 + kChunkF, fB);
-                        fast_chunk_i8<EK, kChunkF>(p, fA, nb + g0, rowterm, need_rowsum, cst_n, delta, fm, fsh, fhz, fk, pk);
-                        wst[lane * 4 + (0 ^ swz)] = pk[0];
-                        wst[lane * 4 + (1 ^ swz)] = pk[1];
-                        __syncwarp();
-                        tmem_wait_regs(fB);
-                        if (g0 + GW < HALF) tmem_ld_32x32b_x32(taddr + g0 + GW, fA);
-                        fast_chunk_i8<EK, kChunkF>(p, fB, nb + g0 + kChunkF, rowterm, need_rowsum, cst_n, delta, fm,
-                                                   fsh, fhz, fk, pk);
-                        wst[lane * 4 + (2 ^ swz)] = pk[0];
-                        wst[lane * 4 + (3 ^ swz)] = pk[1];
-                        __syncwarp();
-                        if (g0 + GW < HALF) tmem_wait_regs(fA);
-                    } else {
-                        fast_chunk_i8<EK, kChunkF>(p, fA, nb + g0, rowterm, need_rowsum, cst_n, delta, fm, fsh, fhz, fk, pk);
-                        wst[lane * 4 + (0 ^ swz)] = pk[0];
-                        wst[lane * 4 + (1 ^ swz)] = pk[1];
-                    }
-                    __syncwarp();
-#pragma unroll
-                    for (int it = 0; it < CPG; ++it) {
-                        const int idx = it * 32 + lane;
-                        const int r = idx / CPG, k = idx % CPG;
-                        const uint4 pk = wst[r * 4 + (k ^ ((r >> 1) & 3))];
-                        const int mr = mrow0 + r;
-                        const int n = nb + g0 + k * kChunk;
-                        if (mr < p.M && n < p.N) {
-                            int8_t* o = obase + static_cast<long long>(mr) * p.ldo + n;
-                            if (vec_ok && n + kChunk <= p.N) {
-                                *reinterpret_cast<uint4*>(o) = pk;
-                            } else {
-                                const uint32_t w4[4] = {pk.x, pk.y, pk.z, pk.w};
-#pragma unroll
-                                for (int j = 0; j < kChunk; ++j)
-                                    if (n + j < p.N) o[j] = static_cast<int8_t>(w4[j >> 2] >> (8 * (j & 3)));
-                            }
-                        }
-                    }
-                    __syncwarp();
-                }
+                // chunks that start at or beyond N (a partial last N tile) are skipped (the
+                // conditions are warp-uniform, so the TMEM loads stay warp-collective)
+                const int n_end = p.N - nb;  // columns of this half that exist
+                // trace slots 416..479: per staging group, start / chunks done / stores done (CTA 0, tiles 0-1)
+                long long* ftr = (p.trace && blockIdx.x == 0 && tcount < 2 && threadIdx.x == 128)
+                                     ? p.trace + 416 + 32 * tcount : nullptr;
+                // a warp with a border row adds every row's delta (zeros for interior rows)
+                const FastHalf h{taddr, n_end, nb, rowterm, cst_n, warp_delta ? delta_fast : nullptr,
+                                 fm, fsh, fhz, wst, lane, swz, mrow0, obase, vec_ok, ftr};
+                fast_half_pass<EK, HALF, (EF & kEfRow) != 0, (EF & kEfDelta) != 0>(p, fk, h);
             } else {
             // Two register sets: the next chunk's TMEM load overlaps this chunk's epilogue.
             uint32_t accA[kChunk], accB[kChunk];
