@@ -13,6 +13,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <vector>
 
 #include "internal.hpp"
 #include "quant.cuh"
@@ -264,6 +265,48 @@ __global__ void __launch_bounds__(256) residual_fast_i8(const uint4* __restrict_
     if (q < n16) step(q, __ldg(a + q), __ldg(b + q));
 }
 
+// Residual chain through the table of its int8 x int8 -> int8 function (ResidualFast::d_table),
+// staged in shared memory per block: four results per pair of input words from byte permutes
+// and one shared-memory byte load each. HBM-bound. The entry of bytes (a, b) sits at
+// a * 256 + (b ^ ((a & 31) << 2)): its bank, ((b >> 2) ^ a) & 31, spreads the rows of one b
+// value (activations cluster on few values; unswizzled, all rows of a b share one bank).
+constexpr int kResidTableBytes = 65536;
+
+__host__ __device__ inline int residual_table_index(int a, int b) { return a * 256 + (b ^ ((a & 31) << 2)); }
+
+__device__ __forceinline__ uint32_t residual_table_word(const uint8_t* tab, uint32_t wa, uint32_t wb) {
+    wb ^= (wa << 2) & 0x7c7c7c7cu;  // the swizzle, four bytes at once (no carries between bytes)
+    const uint32_t ae = wa & 0x00ff00ffu, be = wb & 0x00ff00ffu;               // bytes 0 and 2
+    const uint32_t ao = (wa >> 8) & 0x00ff00ffu, bo = (wb >> 8) & 0x00ff00ffu;  // bytes 1 and 3
+    const uint32_t r0 = tab[__byte_perm(be, ae, 0x5140)];
+    const uint32_t r2 = tab[__byte_perm(be, ae, 0x7362)];
+    const uint32_t r1 = tab[__byte_perm(bo, ao, 0x5140)];
+    const uint32_t r3 = tab[__byte_perm(bo, ao, 0x7362)];
+    return __byte_perm(__byte_perm(r0, r1, 0x0040), __byte_perm(r2, r3, 0x0040), 0x5410);
+}
+
+__global__ void __launch_bounds__(512) residual_table_i8(const uint4* __restrict__ a, const uint4* __restrict__ b,
+                                                         const uint4* __restrict__ table, long long n16,
+                                                         uint4* __restrict__ out) {
+    extern __shared__ __align__(16) uint8_t tab[];
+    for (int i = threadIdx.x; i < kResidTableBytes / 16; i += blockDim.x)
+        reinterpret_cast<uint4*>(tab)[i] = __ldg(table + i);
+    __syncthreads();
+    auto step = [&](long long q, const uint4& av, const uint4& bv) {
+        out[q] = make_uint4(residual_table_word(tab, av.x, bv.x), residual_table_word(tab, av.y, bv.y),
+                            residual_table_word(tab, av.z, bv.z), residual_table_word(tab, av.w, bv.w));
+    };
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    long long q = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+    for (; q + stride < n16; q += 2 * stride) {
+        const uint4 a0 = __ldg(a + q), b0 = __ldg(b + q);
+        const uint4 a1 = __ldg(a + q + stride), b1 = __ldg(b + q + stride);
+        step(q, a0, b0);
+        step(q + stride, a1, b1);
+    }
+    if (q < n16) step(q, __ldg(a + q), __ldg(b + q));
+}
+
 }  // namespace
 
 void residual_fast_constants(const tb_rescale_attr& a, int a_dt, const tb_rescale_attr& b, int b_dt,
@@ -336,6 +379,56 @@ void residual_fast_constants(const tb_rescale_attr& a, int a_dt, const tb_rescal
     f->ozp_add = static_cast<int32_t>(zp_add);
 }
 
+void free_residual_table(ResidualFast* f) {
+    if (f->d_table) cudaFree(f->d_table);
+    f->d_table = nullptr;
+}
+
+tb_status make_residual_table(const tb_rescale_attr& o, const RescalePlan& ro, ResidualFast* f) {
+    free_residual_table(f);
+    if (!f->ok || !o.scale32 || o.per_channel || o.channels != 1 || o.input_unsigned || o.output_unsigned ||
+        o.out_dtype != TB_DT_INT8 || o.rounding_mode == TB_ROUND_INEXACT || o.input_zp != 0)
+        return TB_OK;
+    const long long om = o.multiplier[0];
+    const int os = o.shift[0];
+    if (om < 0 || os < 2 || os > 62) return TB_OK;
+    const bool dbl = o.rounding_mode == TB_ROUND_DOUBLE && os > 31;
+    // the input RESCALEs (type_conv.rs:111-191 with apply_scale_32, quant.rs:6-20), exact in 64 bits
+    auto in_rescale = [](long long x, long long m, int s, long long rp, long long rn) {
+        return (x * m + (x >= 0 ? rp : rn)) >> s;
+    };
+    long long ta[256], tb[256];
+    for (int e = 0; e < 256; ++e) {
+        const long long v = static_cast<int8_t>(static_cast<uint8_t>(e));
+        ta[e] = in_rescale(v - f->za, f->ma, f->sa, f->ra_pos, f->ra_neg);
+        tb[e] = in_rescale(v - f->zb, f->mb, f->sb, f->rb_pos, f->rb_neg);
+    }
+    std::vector<uint8_t> t(kResidTableBytes);
+    const long long lim = 1ll << (os - 1);
+    for (int ea = 0; ea < 256; ++ea)
+        for (int eb = 0; eb < 256; ++eb) {
+            const long long sum = ta[ea] + tb[eb];  // ADD of two int32 values (elementwise.rs:395-397)
+            if (sum < INT32_MIN || sum > INT32_MAX) return TB_OK;
+            // apply_scale_32's input range; outside it the reference reports an error, which only
+            // the per-element kernels report (for the values that actually occur)
+            if (sum < -lim || sum >= lim) return TB_OK;
+            const long long r = (sum * om + lim + (dbl ? (sum >= 0 ? (1ll << 30) : -(1ll << 30)) : 0)) >> os;
+            if (r < INT32_MIN || r > INT32_MAX) return TB_OK;
+            long long y = r + o.output_zp;
+            y = std::min<long long>(std::max<long long>(y, -128), 127);  // the int8 output range
+            y = std::min<long long>(std::max<long long>(y, ro.lo), ro.hi);  // the fused CLAMP
+            t[static_cast<size_t>(residual_table_index(ea, eb))] = static_cast<uint8_t>(static_cast<int8_t>(y));
+        }
+    TB_CUDA(cudaMalloc(&f->d_table, t.size()));
+    const cudaError_t ce = cudaMemcpy(f->d_table, t.data(), t.size(), cudaMemcpyHostToDevice);
+    if (ce != cudaSuccess) {
+        cudaFree(f->d_table);
+        f->d_table = nullptr;
+        return fail(TB_ERR_CUDA, "residual table upload failed: %s", cudaGetErrorString(ce));
+    }
+    return TB_OK;
+}
+
 tb_status launch_transpose(tb_context* ctx, const void* in, void* out, int elem, long long total, int rank,
                            const NdMap& map, cudaStream_t st) {
     if (total == 0) return TB_OK;
@@ -370,6 +463,25 @@ tb_status launch_residual(tb_context* ctx, const void* a, int a_dt, int a_uns, i
                           const RescalePlan& ro, const ResidualFast& fast, long long count, int channels, void* out,
                           cudaStream_t st) {
     if (count == 0) return TB_OK;
+    if (fast.d_table != nullptr && count % 16 == 0 && aligned16(a) && aligned16(b) && aligned16(out)) {
+        const long long n16 = count / 16;
+        // at most three blocks per SM (64 KB of table each), about two 16-byte steps per thread
+        // (small tensors: many blocks, so the per-block table load is spread over the SMs)
+        const int grid = static_cast<int>(std::max<long long>(
+            1, std::min<long long>((n16 + 1023) / 1024, 3ll * ctx->num_sms)));
+        static bool attr_set = false;
+        if (!attr_set) {
+            TB_CUDA(cudaFuncSetAttribute(residual_table_i8, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kResidTableBytes));
+            attr_set = true;
+        }
+        residual_table_i8<<<grid, 512, kResidTableBytes, st>>>(static_cast<const uint4*>(a),
+                                                               static_cast<const uint4*>(b),
+                                                               reinterpret_cast<const uint4*>(fast.d_table), n16,
+                                                               static_cast<uint4*>(out));
+        TB_LAUNCHED(ctx);
+        return TB_OK;
+    }
     if (fast.ok && ro.fast && ro.out_dtype == TB_DT_INT8 && count % 16 == 0 && (!ro.per_channel || channels % 16 == 0) &&
         aligned16(a) && aligned16(b) && aligned16(out)) {
         const long long n16 = count / 16;

@@ -155,11 +155,20 @@ struct ResidualFast {
     bool small = false;
     int k = 0;
     int32_t om = 0, osh = 0, oc = 0, ok2 = 0, ozp_add = 0;
+    // With a per-tensor output RESCALE the whole chain is a function of the two input bytes:
+    // d_table holds its int8 result for every byte pair, at a * 256 + (b ^ ((a & 31) << 2))
+    // (bank swizzle; glue.cu) (owned; null when not built).
+    uint8_t* d_table = nullptr;
 };
 // Fills `f` from host copies of the two input RESCALE attributes (int8 inputs, int32
 // outputs) and of the output RESCALE (int32 -> int8).
 void residual_fast_constants(const tb_rescale_attr& a, int a_dt, const tb_rescale_attr& b, int b_dt,
                              const tb_rescale_attr& o, ResidualFast* f);
+// Builds f->d_table (see ResidualFast) when f->ok, the output RESCALE `o` is per-tensor
+// int32 -> int8 with a 32-bit multiplier and no entry of the table raises a RESCALE error;
+// `ro` supplies the combined clamp. Leaves d_table null otherwise.
+tb_status make_residual_table(const tb_rescale_attr& o, const RescalePlan& ro, ResidualFast* f);
+void free_residual_table(ResidualFast* f);
 tb_status launch_residual(tb_context* ctx, const void* a, int a_dt, int a_uns, int32_t za, const RescalePlan& ra,
                           const void* b, int b_dt, int b_uns, int32_t zb, const RescalePlan& rb,
                           const RescalePlan& ro, const ResidualFast& fast, long long count, int channels, void* out,

@@ -225,6 +225,7 @@ struct tb_graph {
             free_rescale_plan(&s.rs);
             free_rescale_plan(&s.ra);
             free_rescale_plan(&s.rb);
+            free_residual_table(&s.rfast);
         }
         steps.clear();
         for (void* p : buffers) cudaFree(p);
@@ -1156,6 +1157,7 @@ tb_status do_compile(tb_graph* G) {
             if (st == TB_OK) st = make_rescale_plan(ctx, &bb.rattr, bb.in_dtype, bb.channels, &s.rb);
             if (st == TB_OK) st = make_rescale_plan(ctx, &s.rattr, TB_DT_INT32, s.channels, &s.rs);
             residual_fast_constants(a.rattr, a.in_dtype, bb.rattr, bb.in_dtype, s.rattr, &s.rfast);
+            if (st == TB_OK) st = make_residual_table(s.rattr, s.rs, &s.rfast);
             break;
         }
         default: break;
