@@ -11,13 +11,14 @@
 //               sum every A row of each stage from shared memory (dp4a, bank-
 //               conflict-free chunk order) so the epilogue can apply
 //               -zp_b * rowsum(A). 64 rows per warp.
-//   warps 4-11  epilogue, two warps per SM sub-partition: warp w reads TMEM
-//               lanes 32*(w%4)..+31 (one output row per thread) and the half
-//               (w-4)/4 of the tile's columns; the next 16 columns are loaded
-//               from TMEM while the current ones are processed.
+//   warps 4-11  epilogue, two warps per SM sub-partition in two groups of four:
+//               group (w-4)/4 takes the tiles of its parity (its accumulator
+//               buffer), warp w reads TMEM lanes 32*(w%4)..+31 (one output row
+//               per thread) and every column of the tile; the next columns are
+//               loaded from TMEM while the current ones are processed.
 //
 // The accumulator is double-buffered in TMEM, so the epilogue of tile t
-// overlaps the main loop of tile t+1. All waits are bounded: a wait that
+// overlaps the main loop of tile t+1 and the epilogue of tile t-1 (the other group). All waits are bounded: a wait that
 // gives up sets DEV_ERR_TIMEOUT in the device error word and the CTA unwinds.
 //
 // Arithmetic contract (integer): the tensor core forms sum(a*b) over raw
@@ -157,6 +158,9 @@ struct GemmParams {
     // [256,384) row-sum per stage done, [384,400) epilogue tile start/end.
     long long* trace;
     ColsumJob cs;
+    // epilogue warps in two groups taking alternate tiles (set by the launcher when every CTA
+    // has many tiles; otherwise both groups share each tile by column halves)
+    int epi_groups;
 };
 
 template <int KIND, int BN, int BK_BYTES, bool B_MN_MAJOR, bool IM2COL, int STAGES>
@@ -184,7 +188,7 @@ struct GemmCfg {
     // output staging buffer per epilogue warp (16 KB)
     static constexpr int SCRATCH_BYTES = 12288 + 16384;
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 2048 /*barriers, row sums*/ + SCRATCH_BYTES;
-    static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "UMMA N for M=128; each epilogue half walks pairs of 16-column chunks");
+    static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "UMMA N for M=128; each epilogue warp walks pairs of 16-column chunks");
     static_assert(!B_MN_MAJOR || BK_BYTES == 128, "MN-major B uses 128-byte K blocks");
 };
 
@@ -442,13 +446,14 @@ __device__ __forceinline__ void fast_chunk_i8(const GemmParams& p, const uint32_
                               pack4_sat_i8(v[16 * q + 12], v[16 * q + 13], v[16 * q + 14], v[16 * q + 15]));
 }
 
-// One epilogue warp's pass over its half of a tile (32 rows x HALF columns) in the fast
+// One epilogue warp's pass over its part of a tile (32 rows x h.cols columns) in the fast
 // int8 form: TMEM loads of 32 columns (the next one in flight while this one is rescaled),
 // packing into the warp's shared staging buffer, and row-contiguous stores of 64-byte groups.
-struct FastHalf {
-    uint32_t taddr;         // TMEM address of the half's first column (lane quadrant in the high half)
-    int n_end;              // columns of the half that exist (N - first column)
-    int nb;                 // absolute output column of the half's first column
+struct FastTile {
+    uint32_t taddr;         // TMEM address of the warp's first column (lane quadrant in the high half)
+    int cols;               // columns of the tile this warp covers (BN or BN / 2)
+    int n_end;              // of them, the ones that exist (N - first column)
+    int nb;                 // absolute output column of the warp's first column
     int32_t rowterm;
     const int32_t* cst_n;   // staged column terms, indexed by absolute column
     const int32_t* delta;   // border-class delta row, or null when no row of the warp is on a border
@@ -462,11 +467,12 @@ struct FastHalf {
     long long* ftr;         // trace slots (CTA 0, first tiles) or null
 };
 
-template <int EK, int HALF, bool ROW, bool DELTA>
-__device__ __forceinline__ void fast_half_pass(const GemmParams& p, const FastConst& fk, const FastHalf& h) {
+template <int EK, int GW, bool ROW, bool DELTA>
+__device__ __forceinline__ void fast_tile_pass(const GemmParams& p, const FastConst& fk, const FastTile& h) {
     constexpr int FW = kChunkF;                // columns per TMEM load
     constexpr int FPK = FW / 16;               // 16-byte packs per chunk
-    constexpr int GW = HALF < 64 ? HALF : 64;  // columns per staging group
+    // GW: columns per staging group (32 or 64)
+    const int COLS = h.cols;
     constexpr int CPG = GW / kChunk;           // 16-byte slots per row and group: 2 or 4
     const int lane = h.lane, swz = h.swz;
     uint32_t fA[FW], fB[FW];
@@ -476,12 +482,12 @@ __device__ __forceinline__ void fast_half_pass(const GemmParams& p, const FastCo
         tmem_wait_regs(fA);
     }
 #pragma unroll 1
-    for (int g0 = 0; g0 < HALF && g0 < h.n_end; g0 += GW) {
+    for (int g0 = 0; g0 < COLS && g0 < h.n_end; g0 += GW) {
         uint4 pk[FPK];
         if (h.ftr && g0 / GW < 8) h.ftr[3 * (g0 / GW)] = clock64();
         if constexpr (GW == 2 * FW) {
             const bool second = g0 + FW < h.n_end;
-            const bool next = g0 + GW < HALF && g0 + GW < h.n_end;
+            const bool next = g0 + GW < COLS && g0 + GW < h.n_end;
             __syncwarp();
             if (second) tmem_ld_32x32b(h.taddr + g0 + FW, fB);
             fast_chunk_i8<EK, FW, ROW, DELTA>(p, fA, h.nb + g0, h.rowterm, h.cst_n, h.delta, h.fm, h.fsh, h.fc,
@@ -560,6 +566,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int lane = threadIdx.x & 31;
     const bool need_rowsum = Cfg::kKind == 0 && p.epi.row_zp_neg != 0;
 
+    // epilogue warps that release each accumulator buffer: 4 (the owning group) or all 8
+    const uint32_t epi_arrivals = p.epi_groups ? kEpiWarps / 2 : kEpiWarps;
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
@@ -567,9 +575,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], kEpiWarps);
+            mbar_init(&tempty[b], epi_arrivals);
             mbar_init(&rsfull[b], 2);
-            mbar_init(&rsempty[b], kEpiWarps);
+            mbar_init(&rsempty[b], epi_arrivals);
         }
         mbar_init(&mdrain[0], 1);
         mbar_init(&ebar[0], kEpiWarps);
@@ -742,8 +750,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
     } else {
         // ------------------------------------------------------------ epilogue (warps 4..11)
+        // Two groups of 4 warps (one per TMEM lane quadrant). With p.epi_groups (many tiles per
+        // CTA) group g takes the tiles with tcount % 2 == g (accumulator buffer g) and every
+        // column of them, so one group's per-tile waits overlap the other group's work;
+        // otherwise both groups share every tile, group g taking half g of its columns.
         const int q = warp & 3;                 // TMEM lane quadrant
-        const int half = (warp - 4) >> 2;       // which half of the tile's columns
+        const int grp = (warp - 4) >> 2;
+        const int cols = p.epi_groups ? BN : BN / 2;      // columns per warp and tile
+        const int cbase = p.epi_groups ? 0 : grp * (BN / 2);
         const int row = q * 32 + lane;          // row within the tile
         const GemmEpilogue& e = p.epi;
         if (e.pdl_wait) grid_dependency_wait();
@@ -803,7 +817,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         uint32_t tcount = 0;
         uint32_t err = 0;
-        constexpr int HALF = BN / 2;
         constexpr bool kFast = EK >= EK_FAST_T_S && EK <= EK_FAST_PC_D;
         // Tile-invariant RESCALE constants (per-tensor values are channel 0's).
         FastConst fk{0, 0, 0, 0, false, false, false};
@@ -871,6 +884,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 if (!epi_sync()) { ok = false; break; }
                 staged_key = key;
             }
+            // (the column-constant staging above is shared by both groups: every warp passes
+            // every tile's key check, so the staging barriers pair up)
+            if (p.epi_groups && buf != grp) continue;
             // Pointers indexed by the absolute output column.
             const int32_t* cst_n = ct_stage + sbuf * 1024 - nt * BN;
             // Border class of this thread's row (before the accumulator wait: the lookups overlap it).
@@ -906,7 +922,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const int32_t* fm = cst_n + 256;
             const int32_t* fsh = cst_n + 512;
             const int32_t* fhz = cst_n + 768;
-            const int cbase = half * HALF;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                                    static_cast<uint32_t>(buf * BN + cbase);
             const long long orow = static_cast<long long>(b) * p.out_batch_stride + static_cast<long long>(m) * p.ldo;
@@ -923,14 +938,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 const int swz = (lane >> 1) & 3;
                 // chunks that start at or beyond N (a partial last N tile) are skipped (the
                 // conditions are warp-uniform, so the TMEM loads stay warp-collective)
-                const int n_end = p.N - nb;  // columns of this half that exist
+                const int n_end = p.N - nb;  // columns of this warp's part that exist
                 // trace slots 416..479: per staging group, start / chunks done / stores done (CTA 0, tiles 0-1)
                 long long* ftr = (p.trace && blockIdx.x == 0 && tcount < 2 && threadIdx.x == 128)
                                      ? p.trace + 416 + 32 * tcount : nullptr;
                 // a warp with a border row adds every row's delta (zeros for interior rows)
-                const FastHalf h{taddr, n_end, nb, rowterm, cst_n, warp_delta ? delta_fast : nullptr,
+                const FastTile h{taddr, cols, n_end, nb, rowterm, cst_n, warp_delta ? delta_fast : nullptr,
                                  fm, fsh, fhz, wst, lane, swz, mrow0, obase, vec_ok, ftr};
-                fast_half_pass<EK, HALF, (EF & kEfRow) != 0, (EF & kEfDelta) != 0>(p, fk, h);
+                fast_tile_pass<EK, (BN / 2 < 64 ? BN / 2 : 64), (EF & kEfRow) != 0, (EF & kEfDelta) != 0>(p, fk, h);
             } else {
             // Two register sets: the next chunk's TMEM load overlaps this chunk's epilogue.
             uint32_t accA[kChunk], accB[kChunk];
@@ -938,7 +953,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             tmem_ld_32x32b_x16(taddr, accA);
             tmem_wait_regs(accA);
 #pragma unroll 1
-            for (int c0 = 0; c0 < HALF; c0 += 2 * kChunk) {
+            for (int c0 = 0; c0 < cols; c0 += 2 * kChunk) {
                 const bool tr = p.trace && blockIdx.x == 0 && tcount == 0 && threadIdx.x == 128;
                 if (tr) p.trace[408 + (c0 / kChunk) * 2] = clock64();
                 __syncwarp();
@@ -948,12 +963,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 if (tr) p.trace[409 + (c0 / kChunk) * 2] = clock64();
                 __syncwarp();
                 tmem_wait_regs(accB);
-                if (c0 + 2 * kChunk < HALF) tmem_ld_32x32b_x16(taddr + c0 + 2 * kChunk, accA);
+                if (c0 + 2 * kChunk < cols) tmem_ld_32x32b_x16(taddr + c0 + 2 * kChunk, accA);
                 if (row_ok && nb + c0 + kChunk < p.N)
                     epilogue_chunk<EK>(p, accB, nb + c0 + kChunk, orow, rowterm, colterm, delta, fm, fsh, fhz, fk,
                                        err);
                 __syncwarp();
-                if (c0 + 2 * kChunk < HALF) tmem_wait_regs(accA);
+                if (c0 + 2 * kChunk < cols) tmem_wait_regs(accA);
             }
             }
             tc_fence_before();
