@@ -254,6 +254,11 @@ CONV_CASES = [
     (5, 64, 66, 1, 16, 4, 4, (0, 0, 2, 2), (2, 2), (1, 1), 9, -7),      # even kernel, one channel
     (1, 72, 72, 4, 48, 5, 5, (2, 2, 1, 3), (1, 1), (1, 2), -128, -2),
     (7, 50, 50, 3, 32, 7, 7, (3, 2, 3, 2), (2, 2), (1, 1), 2, 1),       # odd pads
+    # 64 input channels: two filter taps per stage (odd tap counts end on a one-tap stage)
+    (2, 14, 14, 64, 96, 3, 3, (1, 1, 1, 1), (1, 1), (1, 1), 5, -2),     # weight zero point: row sums of both taps
+    (1, 13, 13, 64, 64, 5, 5, (2, 2, 2, 2), (2, 2), (1, 1), 4, -4),
+    (2, 10, 11, 64, 40, 3, 3, (1, 0, 2, 1), (2, 1), (2, 1), -49, 1),    # vertical dilation, asymmetric pads
+    (1, 9, 12, 64, 64, 1, 3, (0, 0, 1, 1), (1, 1), (1, 1), 2, 3),       # three taps in one row
 ]
 
 

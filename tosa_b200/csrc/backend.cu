@@ -702,6 +702,7 @@ struct tb_conv2d_plan {
     RescalePlan rs;
     SmallRange sr;                  // tensor-core int8 path: small-range RESCALE constants
     int bn = 64, bk = 128;
+    bool tap2 = false;              // int8 tensor-core path: two filter taps per stage (64 input channels)
     int32_t* d_colterm = nullptr;   // [n_classes][ct_ld] column terms of each border class
     int32_t* d_ctdelta = nullptr;   // [n_classes][ct_ld] class terms minus the base class's
     long long ct_ld = 0;            // output channels padded to whole 256-column tiles
@@ -934,15 +935,17 @@ static tb_status conv_plan_create(tb_context* ctx, const tb_conv2d_desc* d, cons
 
     p->bn = oc <= 64 ? 64 : oc <= 128 ? 128 : 256;
     p->bk = (int8 && d->ic <= 64) ? 64 : 128;
+    p->tap2 = p->path == 0 && int8 && d->ic == 64 && taps >= 2 && p->bn <= 128;
     const int bke = p->bk / e;
     // Weight tensor map: [OC][KH*KW*IC], K-major.
     {
         const uint64_t K = static_cast<uint64_t>(taps) * d->ic;
         const uint64_t dims[3] = {K, static_cast<uint64_t>(oc), 1};
         const uint64_t str[2] = {K * e, K * e * oc};
-        const uint32_t box[3] = {static_cast<uint32_t>(bke), static_cast<uint32_t>(p->bn), 1};
+        // two taps per stage: one 128-byte box covers both taps' weights (adjacent in K)
+        const uint32_t box[3] = {static_cast<uint32_t>(p->tap2 ? 2 * bke : bke), static_cast<uint32_t>(p->bn), 1};
         tb_status s = encode_tiled(&p->tmB, tmap_dtype(wt), 3, weight, dims, str, box,
-                                   p->bk == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+                                   (p->bk == 128 || p->tap2) ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
         if (s != TB_OK) return bail(s);
     }
     if (p->path == 1) {
@@ -1228,7 +1231,8 @@ extern "C" TB_API tb_status tb_conv2d_plan_run(tb_conv2d_plan* p, const void* in
     gp.batch = 1;
     gp.in_bf16 = d.in_dtype == TB_DT_BF16;
     gp.c_blocks = (d.ic + bke - 1) / bke;
-    gp.k_blocks = d.kh * d.kw * gp.c_blocks;
+    gp.taps = d.kh * d.kw;
+    gp.k_blocks = p->tap2 ? (gp.taps + 1) / 2 : gp.taps * gp.c_blocks;
     gp.conv_OW = p->ow;
     gp.conv_OHOW = p->oh * p->ow;
     gp.stride_h = d.stride[0];
@@ -1269,6 +1273,7 @@ extern "C" TB_API tb_status tb_conv2d_plan_run(tb_conv2d_plan* p, const void* in
         ep.mode = EPI_I32;
         ep.out_dtype = TB_DT_INT32;
     }
+    if (p->tap2) return launch_i8_conv_tap2(ctx, p->bn, epilogue_kind(ep), p->tmA, p->tmB, gp, st);
     return launch_i8_conv(ctx, p->bn, p->bk, epilogue_kind(ep), p->tmA, p->tmB, gp, st);
 }
 
@@ -1438,8 +1443,13 @@ extern "C" TB_API tb_status tb_avg_pool2d(tb_context* ctx, const tb_pool2d_desc*
         }();
         const PoolTile pt = pool_tile(g.c, g.ow);
         const dim3 grid((g.ow + pt.ppb - 1) / pt.ppb, g.oh, g.n);
-        // taps one at a time for small windows (occupancy hides latency), eight in flight for wide ones
-        if (g.kx >= 6)
+        // taps in flight per thread: a window of up to 4 taps in one batch, eight at a time for wide
+        // windows, one at a time in between (measured on B200: batches of 8 over a 3x3 window cost
+        // more occupancy than they hide latency)
+        if (g.kx * g.ky <= 4)
+            avg_pool_i8_vec16<4><<<grid, pool_block(pt), 0, st>>>(g, pt, static_cast<const int8_t*>(input), d->input_zp,
+                                                                  d->output_zp, table, static_cast<int8_t*>(out));
+        else if (g.kx >= 6)
             avg_pool_i8_vec16<8><<<grid, pool_block(pt), 0, st>>>(g, pt, static_cast<const int8_t*>(input), d->input_zp,
                                                                   d->output_zp, table, static_cast<int8_t*>(out));
         else
@@ -1474,7 +1484,11 @@ extern "C" TB_API tb_status tb_max_pool2d(tb_context* ctx, const tb_pool2d_desc*
     if (dt == TB_DT_INT8 && g.c % 16 == 0 && aligned16(input) && aligned16(out) && g.oh <= 65535 && g.n <= 65535) {
         const PoolTile pt = pool_tile(g.c, g.ow);
         const dim3 grid((g.ow + pt.ppb - 1) / pt.ppb, g.oh, g.n);
-        if (g.kx >= 6)
+        // taps in flight per thread, as for AVG_POOL2D
+        if (g.kx * g.ky <= 4)
+            max_pool_i8_vec16<4><<<grid, pool_block(pt), 0, st>>>(g, pt, static_cast<const int8_t*>(input),
+                                                                  static_cast<int8_t*>(out));
+        else if (g.kx >= 6)
             max_pool_i8_vec16<8><<<grid, pool_block(pt), 0, st>>>(g, pt, static_cast<const int8_t*>(input),
                                                                   static_cast<int8_t*>(out));
         else

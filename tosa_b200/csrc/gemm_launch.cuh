@@ -1,6 +1,6 @@
 // Launch helpers of the tensor-core GEMM: one template instantiation per tile
 // configuration and epilogue kind. The instantiations are spread over gemm_i8_mm.cu,
-// gemm_i8_conv.cu, gemm_i8_conv_k128.cu and gemm_f16.cu, which expose the plain
+// gemm_i8_conv.cu, gemm_i8_conv_k128.cu, gemm_i8_conv_tap2.cu and gemm_f16.cu, which expose the plain
 // functions declared at the bottom.
 #pragma once
 
@@ -81,6 +81,8 @@ tb_status launch_gemm(tb_context* ctx, const CUtensorMap& tmA, const CUtensorMap
 }
 
 constexpr int gemm_stages(int bn, int bk) { return (196608 / ((128 + bn) * bk)) < 8 ? (196608 / ((128 + bn) * bk)) : 8; }
+// Stages with two taps per stage (A: two 64-byte boxes, B: one 128-byte box).
+constexpr int gemm_stages_tap2(int bn) { return (196608 / ((128 + bn) * 128)) < 8 ? (196608 / ((128 + bn) * 128)) : 8; }
 
 // Epilogue kind for a prepared epilogue.
 inline int epilogue_kind(const GemmEpilogue& e) {
@@ -123,12 +125,14 @@ tb_status launch_int_ek(tb_context* ctx, int ek, const CUtensorMap& a, const CUt
     }
 }
 
-// Implemented in gemm_i8_mm.cu / gemm_i8_conv.cu / gemm_i8_conv_k128.cu / gemm_f16.cu.
+// Implemented in gemm_i8_mm.cu / gemm_i8_conv*.cu / gemm_f16.cu.
 tb_status launch_i8_matmul(tb_context* ctx, int bn, int ek, const CUtensorMap& a, const CUtensorMap& b,
                            const GemmParams& p, cudaStream_t st);
 tb_status launch_i8_conv(tb_context* ctx, int bn, int bk, int ek, const CUtensorMap& a, const CUtensorMap& b,
                          const GemmParams& p, cudaStream_t st);
 tb_status launch_i8_conv_k128(tb_context* ctx, int bn, int ek, const CUtensorMap& a, const CUtensorMap& b,
+                              const GemmParams& p, cudaStream_t st);
+tb_status launch_i8_conv_tap2(tb_context* ctx, int bn, int ek, const CUtensorMap& a, const CUtensorMap& b,
                               const GemmParams& p, cudaStream_t st);
 tb_status launch_f16_matmul(tb_context* ctx, int bn, const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p,
                             cudaStream_t st);

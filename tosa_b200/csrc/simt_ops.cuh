@@ -168,23 +168,28 @@ __global__ void avg_pool_i8_vec16(PoolGeomDev g, PoolTile pt, const int8_t* __re
         const int ix0 = ox * g.sx - g.pad_l;
         const int kx0 = max(0, -ix0), kx1 = min(g.kx, g.iw - ix0);
         uint32_t lo[4] = {0, 0, 0, 0}, hi[4] = {0, 0, 0, 0};
-        for (int ky = ky0; ky < ky1; ++ky) {
-            const uint4* row = reinterpret_cast<const uint4*>(
-                x + ((static_cast<long long>(b) * g.ih + iy0 + ky) * g.iw + ix0) * g.c + c16);
-            for (int kb = kx0; kb < kx1; kb += BATCH) {
-                uint4 v[BATCH];  // BATCH taps of the row in flight (wide windows over few outputs)
+        const uint4* xb = reinterpret_cast<const uint4*>(x + static_cast<long long>(b) * g.ih * g.iw * g.c + c16);
+        const int nkx = kx1 - kx0, ntaps = (ky1 - ky0) * nkx;
+        int ky = ky0, kx = kx0;
+        for (int t0 = 0; t0 < ntaps; t0 += BATCH) {
+            uint4 v[BATCH];  // BATCH taps of the window in flight, across its rows
 #pragma unroll
-                for (int j = 0; j < BATCH; ++j)
-                    if (kb + j < kx1) v[j] = __ldg(row + static_cast<long long>(kb + j) * pt.cg);
-#pragma unroll
-                for (int j = 0; j < BATCH; ++j) {
-                    if (kb + j >= kx1) break;
-                    const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        lo[q] += (w[q] ^ 0x80808080u) & 0x00ff00ffu;
-                        hi[q] += ((w[q] >> 8) ^ 0x00808080u) & 0x00ff00ffu;
+            for (int j = 0; j < BATCH; ++j)
+                if (t0 + j < ntaps) {
+                    v[j] = __ldg(xb + static_cast<long long>((iy0 + ky) * g.iw + ix0 + kx) * pt.cg);
+                    if (++kx == kx1) {
+                        kx = kx0;
+                        ++ky;
                     }
+                }
+#pragma unroll
+            for (int j = 0; j < BATCH; ++j) {
+                if (t0 + j >= ntaps) break;
+                const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    lo[q] += (w[q] ^ 0x80808080u) & 0x00ff00ffu;
+                    hi[q] += ((w[q] >> 8) ^ 0x00808080u) & 0x00ff00ffu;
                 }
             }
         }
@@ -232,23 +237,28 @@ __global__ void max_pool_i8_vec16(PoolGeomDev g, PoolTile pt, const int8_t* __re
         const int ix0 = ox * g.sx - g.pad_l;
         const int kx0 = max(0, -ix0), kx1 = min(g.kx, g.iw - ix0);
         uint32_t lo[4] = {0, 0, 0, 0}, hi[4] = {0, 0, 0, 0};  // biased -128
-        for (int ky = ky0; ky < ky1; ++ky) {
-            const uint4* row = reinterpret_cast<const uint4*>(
-                x + ((static_cast<long long>(b) * g.ih + iy0 + ky) * g.iw + ix0) * g.c + c16);
-            for (int kb = kx0; kb < kx1; kb += BATCH) {
-                uint4 v[BATCH];  // BATCH taps of the row in flight (wide windows over few outputs)
+        const uint4* xb = reinterpret_cast<const uint4*>(x + static_cast<long long>(b) * g.ih * g.iw * g.c + c16);
+        const int nkx = kx1 - kx0, ntaps = (ky1 - ky0) * nkx;
+        int ky = ky0, kx = kx0;
+        for (int t0 = 0; t0 < ntaps; t0 += BATCH) {
+            uint4 v[BATCH];  // BATCH taps of the window in flight, across its rows
 #pragma unroll
-                for (int j = 0; j < BATCH; ++j)
-                    if (kb + j < kx1) v[j] = __ldg(row + static_cast<long long>(kb + j) * pt.cg);
-#pragma unroll
-                for (int j = 0; j < BATCH; ++j) {
-                    if (kb + j >= kx1) break;
-                    const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        lo[q] = max_u16x2(lo[q], (w[q] ^ 0x80808080u) & 0x00ff00ffu);
-                        hi[q] = max_u16x2(hi[q], ((w[q] >> 8) ^ 0x00808080u) & 0x00ff00ffu);
+            for (int j = 0; j < BATCH; ++j)
+                if (t0 + j < ntaps) {
+                    v[j] = __ldg(xb + static_cast<long long>((iy0 + ky) * g.iw + ix0 + kx) * pt.cg);
+                    if (++kx == kx1) {
+                        kx = kx0;
+                        ++ky;
                     }
+                }
+#pragma unroll
+            for (int j = 0; j < BATCH; ++j) {
+                if (t0 + j >= ntaps) break;
+                const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    lo[q] = max_u16x2(lo[q], (w[q] ^ 0x80808080u) & 0x00ff00ffu);
+                    hi[q] = max_u16x2(hi[q], ((w[q] >> 8) ^ 0x00808080u) & 0x00ff00ffu);
                 }
             }
         }

@@ -146,6 +146,7 @@ struct GemmParams {
     int KW, dil_h, dil_w;
     int c_blocks;              // k blocks per filter tap
     int IC;                    // channels per tap (B column offset per tap)
+    int taps;                  // filter taps (KH * KW) of a convolution
     // output
     void* out;
     long long out_batch_stride;  // elements
@@ -163,7 +164,12 @@ struct GemmParams {
     int epi_groups;
 };
 
-template <int KIND, int BN, int BK_BYTES, bool B_MN_MAJOR, bool IM2COL, int STAGES>
+// TAP2 (int8 im2col convolutions with exactly 64 input channels): two filter taps per stage,
+// each tap's A box in its own 64-byte-swizzled sub-tile, the two taps' weights as one
+// 128-byte-swizzled B box (they are adjacent in K), four MMAs per stage. Halves the number of
+// stages of a 3x3 convolution over 64 channels, whose time is set by the per-stage latency of
+// the producer and MMA issue chains rather than by either unit's throughput.
+template <int KIND, int BN, int BK_BYTES, bool B_MN_MAJOR, bool IM2COL, int STAGES, bool TAP2 = false>
 struct GemmCfg {
     static constexpr int kKind = KIND;            // 0: int8, 1: f16/bf16
     static constexpr int BM = 128;
@@ -175,11 +181,16 @@ struct GemmCfg {
     static constexpr int kStages = STAGES;
     static constexpr bool kBMN = B_MN_MAJOR;
     static constexpr bool kIm2col = IM2COL;
-    static constexpr int A_BYTES = BM * BK_BYTES;
-    static constexpr int B_BYTES = BN * BK_BYTES;
+    static constexpr bool kTap2 = TAP2;
+    static constexpr int A_SUB = BM * BK_BYTES;                     // one tap's A box
+    static constexpr int A_BYTES = TAP2 ? 2 * A_SUB : A_SUB;
+    static constexpr int kBKBytesB = TAP2 ? 2 * BK_BYTES : BK_BYTES;  // K bytes of B per stage
+    static constexpr int B_BYTES = BN * kBKBytesB;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int SW_CODE = BK_BYTES == 128 ? 2 : 4;        // UMMA layout type
     static constexpr int ATOM_SBO = 8 * BK_BYTES;                   // 8 rows of one swizzle atom
+    static constexpr int SW_CODE_B = kBKBytesB == 128 ? 2 : 4;
+    static constexpr int ATOM_SBO_B = 8 * kBKBytesB;
     // MN-major B: 128-byte rows of N, one box per 128 bytes of N.
     static constexpr int B_MN_CHUNK = 128 / kElem;                  // N elements per box
     static constexpr int B_MN_BOX_BYTES = BK * 128;                 // BK k-rows x 128 bytes
@@ -190,6 +201,7 @@ struct GemmCfg {
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 2048 /*barriers, row sums*/ + SCRATCH_BYTES;
     static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "UMMA N for M=128; each epilogue warp walks pairs of 16-column chunks");
     static_assert(!B_MN_MAJOR || BK_BYTES == 128, "MN-major B uses 128-byte K blocks");
+    static_assert(!TAP2 || (KIND == 0 && IM2COL && BK_BYTES == 64), "two taps per stage: int8 im2col, 64 channels");
 };
 
 // ---------------------------------------------------------------------------
@@ -624,6 +636,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     uint8_t* sa = stage_base + s * Cfg::STAGE_BYTES;
                     uint8_t* sb = sa + Cfg::A_BYTES;
                     if (p.trace && blockIdx.x == 0 && it < 128) p.trace[it] = clock64();
+                    if constexpr (Cfg::kTap2) {
+                        // taps tap and tap + 1 (the last stage of an odd tap count has one; the B box's
+                        // second half then lies past K and is filled with zeros)
+                        const bool two = tap + 1 < p.taps;
+                        mbar_arrive_expect_tx(&full[s], two ? Cfg::STAGE_BYTES : Cfg::STAGE_BYTES - Cfg::A_SUB);
+                        tma_load_im2col_4d(sa, &tmA, &full[s], 0, wb, hb, img, static_cast<uint16_t>(kx * p.dil_w),
+                                           static_cast<uint16_t>(ky * p.dil_h));
+                        tma_load_3d(sb, &tmB, &full[s], tap * p.IC, n0, 0);
+                        ++tap;
+                        if (++kx == p.KW) {
+                            kx = 0;
+                            ++ky;
+                        }
+                        if (two) {
+                            tma_load_im2col_4d(sa + Cfg::A_SUB, &tmA, &full[s], 0, wb, hb, img,
+                                               static_cast<uint16_t>(kx * p.dil_w), static_cast<uint16_t>(ky * p.dil_h));
+                            ++tap;
+                            if (++kx == p.KW) {
+                                kx = 0;
+                                ++ky;
+                            }
+                        }
+                        continue;
+                    }
                     mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
                     if constexpr (Cfg::kIm2col) {
                         tma_load_im2col_4d(sa, &tmA, &full[s], cb * Cfg::BK, wb, hb, img,
@@ -677,14 +713,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     const uint32_t sa = smem_u32(stage_base + s * Cfg::STAGE_BYTES);
                     const uint32_t sb = sa + Cfg::A_BYTES;
 #pragma unroll
-                    for (int k = 0; k < Cfg::kBKBytes / 32; ++k) {
-                        const uint64_t ad = smem_desc(sa + k * 32, 16, Cfg::ATOM_SBO, Cfg::SW_CODE);
+                    for (int k = 0; k < Cfg::kBKBytesB / 32; ++k) {
+                        // two taps per stage: k-steps 0-1 read A sub-tile 0, 2-3 sub-tile 1 (its stale
+                        // contents meet zero weights in a one-tap stage)
+                        const uint32_t a_k = Cfg::kTap2 ? sa + (k >> 1) * Cfg::A_SUB + (k & 1) * 32 : sa + k * 32;
+                        const uint64_t ad = smem_desc(a_k, 16, Cfg::ATOM_SBO, Cfg::SW_CODE);
                         uint64_t bd;
                         if constexpr (Cfg::kBMN) {
                             // k-rows of 128 bytes; 8-row groups 1024 B apart; 128-byte N chunks one box apart.
                             bd = smem_desc(sb + k * Cfg::kMmaK * 128, Cfg::B_MN_BOX_BYTES, 1024, 2);
                         } else {
-                            bd = smem_desc(sb + k * 32, 16, Cfg::ATOM_SBO, Cfg::SW_CODE);
+                            bd = smem_desc(sb + k * 32, 16, Cfg::ATOM_SBO_B, Cfg::SW_CODE_B);
                         }
                         tc_mma<Cfg::kKind>(d_tmem, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
                     }
@@ -713,7 +752,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     const int s = it % S;
                     const uint32_t ph = (it / S) & 1;
                     if (!mbar_wait_bounded(&full[s], ph, abort_flag, limit)) { ok = false; break; }
-                    const uint8_t* sa = stage_base + s * Cfg::STAGE_BYTES;
+                    const uint8_t* sa0 = stage_base + s * Cfg::STAGE_BYTES;
+                    // two taps per stage: the second sub-tile holds data only when the stage has two taps
+                    const int subs = Cfg::kTap2 && 2 * kb + 1 < p.taps ? 2 : 1;
+                    for (int sub = 0; sub < subs; ++sub) {
+                    const uint8_t* sa = sa0 + sub * Cfg::A_SUB;
                     const int4* r0 = reinterpret_cast<const int4*>(sa + (row0 + lane) * Cfg::kBKBytes);
                     const int4* r1 = reinterpret_cast<const int4*>(sa + (row0 + 32 + lane) * Cfg::kBKBytes);
                     // Chunk order rotated per lane: the 8 lanes of a shared-memory phase hit 8 different
@@ -732,6 +775,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         sum1 = __dp4a(v1.y, 0x01010101, sum1);
                         sum1 = __dp4a(v1.z, 0x01010101, sum1);
                         sum1 = __dp4a(v1.w, 0x01010101, sum1);
+                    }
                     }
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&empty[s]);
