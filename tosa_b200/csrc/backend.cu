@@ -722,12 +722,13 @@ struct tb_conv2d_plan {
     // path 9 (depthwise int8 on dp2a): [taps][ic] masked weight words, then bias2 [ic]
     uint32_t* d_dw = nullptr;
     int strip_rows = 0;             // output rows per block of the 3x3 strip kernel (0: chosen per launch)
+    int dw_k = 0;                   // path 9: the table's weights and bias pre-scaled by 2^dw_k (small-range RESCALE in sr)
 };
 
 // Path 9 tables (depthwise_i8_dp2a): the masked 16-bit weight words and the bias with the
 // input zero point's terms taken out, from the weight and bias contents at plan creation.
 // Leaves the plan on path 4 when the input zero point does not fit a signed byte.
-static tb_status prepare_dw_dp2a(tb_conv2d_plan* p) {
+static tb_status prepare_dw_dp2a(tb_conv2d_plan* p, const tb_rescale_attr* rescale) {
     const tb_conv2d_desc& d = p->d;
     const int c = d.ic;
     const long long taps = static_cast<long long>(d.kh) * d.kw;
@@ -736,19 +737,49 @@ static tb_status prepare_dw_dp2a(tb_conv2d_plan* p) {
     std::vector<int32_t> bias(static_cast<size_t>(d.bias_len));
     TB_CUDA(cudaMemcpy(w.data(), p->weight, w.size(), cudaMemcpyDeviceToHost));
     TB_CUDA(cudaMemcpy(bias.data(), p->bias, sizeof(int32_t) * bias.size(), cudaMemcpyDeviceToHost));
-    std::vector<uint32_t> blob(static_cast<size_t>(taps * c + c), 0);
-    std::vector<long long> wsum(c, 0);
+    std::vector<long long> wsum(c, 0), wabs(c, 0);
+    int wmax = 1;
     for (long long t = 0; t < taps; ++t)
         for (int ch = 0; ch < c; ++ch) {
             const int wv = w[static_cast<size_t>(t * c + ch)] - d.weight_zp;
             if (wv < -32768 || wv > 32767) return TB_OK;
             wsum[ch] += wv;
+            wabs[ch] += std::abs(wv);
+            wmax = std::max(wmax, std::abs(wv));
+        }
+    // The 3x3 strip kernel's small-range RESCALE: weights and bias pre-scaled by 2^k, so the
+    // accumulator is v * 2^k and the epilogue is one mad.hi and a shift (as in the GEMM). k is
+    // bounded by the 16-bit weight lanes (|w - zw| * 2^k <= 32767) and by |v| * 2^k < 2^31 over
+    // |v| <= (128 + |zx|) * sum |w - zw| + |bias| (the host bound; the substituted zero-point
+    // taps are inside it).
+    const bool strip = d.kh == 3 && d.kw == 3 && d.stride[0] == d.stride[1] && d.stride[0] <= 2 &&
+                       d.dilation[0] == 1 && d.dilation[1] == 1;
+    int k = 0;
+    if (strip && rescale != nullptr && p->rs.fast && p->rs.out_dtype == TB_DT_INT8) {
+        int kcap = 0;
+        while (kcap < 15 && (static_cast<long long>(wmax) << (kcap + 1)) <= 32767) ++kcap;
+        long long bound = 0;
+        for (int ch = 0; ch < c; ++ch)
+            bound = std::max(bound, (128ll + std::abs(d.input_zp)) * wabs[ch] +
+                                        std::llabs(static_cast<long long>(bias[d.bias_len == 1 ? 0 : ch])));
+        // a bound of at least 2^(30 - kcap) keeps prepare_small_range's k at or below kcap
+        bound = std::max(bound, 1ll << (30 - kcap));
+        tb_status s = make_small_range(*rescale, p->rs, bound, &p->sr);
+        if (s != TB_OK) return s;
+        if (p->sr.ok && p->sr.k >= 1) k = p->sr.k;
+        else free_small_range(&p->sr);
+    }
+    p->dw_k = k;
+    std::vector<uint32_t> blob(static_cast<size_t>(taps * c + c), 0);
+    for (long long t = 0; t < taps; ++t)
+        for (int ch = 0; ch < c; ++ch) {
+            const int wv = (w[static_cast<size_t>(t * c + ch)] - d.weight_zp) * (1 << k);
             blob[static_cast<size_t>(t * c + ch)] = static_cast<uint32_t>(static_cast<uint16_t>(wv)) << (16 * (ch & 1));
         }
     for (int ch = 0; ch < c; ++ch) {
         const long long b = bias[d.bias_len == 1 ? 0 : ch];
-        blob[static_cast<size_t>(taps * c + ch)] =
-            static_cast<uint32_t>(static_cast<unsigned long long>(b - static_cast<long long>(d.input_zp) * wsum[ch]));
+        blob[static_cast<size_t>(taps * c + ch)] = static_cast<uint32_t>(
+            static_cast<unsigned long long>(b - static_cast<long long>(d.input_zp) * wsum[ch]) << k);
     }
     TB_CUDA(cudaMalloc(&p->d_dw, sizeof(uint32_t) * blob.size()));
     TB_CUDA(cudaMemcpy(p->d_dw, blob.data(), sizeof(uint32_t) * blob.size(), cudaMemcpyHostToDevice));
@@ -879,7 +910,7 @@ static tb_status conv_plan_create(tb_context* ctx, const tb_conv2d_desc* d, cons
         p->path = int8 ? ((d->m == 1 && d->ic % 4 == 0) ? 4 : 5) : 6;
         if (p->path == 4 && d->dilation[1] == 1 && (d->kw == 3 || d->kw == 5) && d->kh == d->kw &&
             (d->stride[1] == 1 || d->stride[1] == 2) && d->n <= 65535 && oh <= 65535) {
-            tb_status s = prepare_dw_dp2a(p);
+            tb_status s = prepare_dw_dp2a(p, rescale);
             if (s != TB_OK) return bail(s);
         }
         *out = p;
@@ -1118,7 +1149,7 @@ extern "C" TB_API tb_status tb_conv2d_plan_run(tb_conv2d_plan* p, const void* in
         const int ng = std::min(std::max(1, 256 / cx), groups);
         const dim3 block(cx, ng);
         const dim3 grid(dg.chunks * ((groups + ng - 1) / ng), p->oh, d.n);
-        DwEpi e;
+        DwEpi e{};
         e.gen = int_epi(p->rs);
         e.fq_m = p->rs.fq_m;
         e.fq_sh = p->rs.fq_sh;
@@ -1127,9 +1158,16 @@ extern "C" TB_API tb_status tb_conv2d_plan_run(tb_conv2d_plan* p, const void* in
         e.zp_add = p->rs.zp_folded ? 0 : p->rs.out_zp;
         e.lo = p->rs.lo;
         e.hi = p->rs.hi;
-        const int ek = (p->rs.enabled && p->rs.fast && p->rs.out_dtype == TB_DT_INT8)
-                           ? (p->rs.rounding == ROUND_DOUBLE ? 2 : 1)
-                           : 0;
+        int ek = (p->rs.enabled && p->rs.fast && p->rs.out_dtype == TB_DT_INT8)
+                     ? (p->rs.rounding == ROUND_DOUBLE ? 2 : 1)
+                     : 0;
+        if (p->dw_k > 0) {  // pre-scaled table: the small-range RESCALE (3x3 strip kernel only)
+            ek += 2;
+            e.sr_sh = p->sr.d_sh;
+            e.sr_c = p->sr.d_c;
+            e.k2 = p->sr.k2;
+            e.zp_add = p->sr.zp_folded ? 0 : p->rs.out_zp;
+        }
         const uint32_t zxw = static_cast<uint32_t>(static_cast<uint8_t>(d.input_zp)) * 0x01010101u;
         auto x = static_cast<const uint32_t*>(input);
         auto wm = reinterpret_cast<const uint4*>(p->d_dw);
@@ -1146,17 +1184,22 @@ extern "C" TB_API tb_status tb_conv2d_plan_run(tb_conv2d_plan* p, const void* in
             const dim3 sgrid(grid.x, (p->oh + dg.rows - 1) / dg.rows, d.n);
             auto x4 = x;
             if (d.stride[0] == 1) {
-                if (ek == 2) depthwise_i8_dp2a_strip<1, 2><<<sgrid, block, 0, st>>>(dg, x4, wm, b2, zxw, e, out, ctx->dev_err);
+                if (ek == 4) depthwise_i8_dp2a_strip<1, 4><<<sgrid, block, 0, st>>>(dg, x4, wm, b2, zxw, e, out, ctx->dev_err);
+                else if (ek == 3) depthwise_i8_dp2a_strip<1, 3><<<sgrid, block, 0, st>>>(dg, x4, wm, b2, zxw, e, out, ctx->dev_err);
+                else if (ek == 2) depthwise_i8_dp2a_strip<1, 2><<<sgrid, block, 0, st>>>(dg, x4, wm, b2, zxw, e, out, ctx->dev_err);
                 else if (ek == 1) depthwise_i8_dp2a_strip<1, 1><<<sgrid, block, 0, st>>>(dg, x4, wm, b2, zxw, e, out, ctx->dev_err);
                 else depthwise_i8_dp2a_strip<1, 0><<<sgrid, block, 0, st>>>(dg, x4, wm, b2, zxw, e, out, ctx->dev_err);
             } else {
-                if (ek == 2) depthwise_i8_dp2a_strip<2, 2><<<sgrid, block, 0, st>>>(dg, x4, wm, b2, zxw, e, out, ctx->dev_err);
+                if (ek == 4) depthwise_i8_dp2a_strip<2, 4><<<sgrid, block, 0, st>>>(dg, x4, wm, b2, zxw, e, out, ctx->dev_err);
+                else if (ek == 3) depthwise_i8_dp2a_strip<2, 3><<<sgrid, block, 0, st>>>(dg, x4, wm, b2, zxw, e, out, ctx->dev_err);
+                else if (ek == 2) depthwise_i8_dp2a_strip<2, 2><<<sgrid, block, 0, st>>>(dg, x4, wm, b2, zxw, e, out, ctx->dev_err);
                 else if (ek == 1) depthwise_i8_dp2a_strip<2, 1><<<sgrid, block, 0, st>>>(dg, x4, wm, b2, zxw, e, out, ctx->dev_err);
                 else depthwise_i8_dp2a_strip<2, 0><<<sgrid, block, 0, st>>>(dg, x4, wm, b2, zxw, e, out, ctx->dev_err);
             }
             TB_LAUNCHED(ctx);
             return TB_OK;
         }
+        if (ek >= 3) return fail(TB_ERR_INVALID_ARGUMENT, "DEPTHWISE_CONV2D: pre-scaled weights outside the 3x3 strip kernel");
         const int key = d.kw * 10 + d.stride[1];
         if (key == 31) launch_dw_dp2a<3, 1>(ek, grid, block, st, dg, x, wm, b2, zxw, e, out, ctx->dev_err);
         else if (key == 32) launch_dw_dp2a<3, 2>(ek, grid, block, st, dg, x, wm, b2, zxw, e, out, ctx->dev_err);

@@ -459,8 +459,13 @@ struct DwEpi {
     const int32_t* fq_sh;
     const int32_t* fq_hz;
     int per_channel;
-    int32_t zp_add;  // the output zero point when it is not folded into fq_hz
+    int32_t zp_add;  // the output zero point when it is not folded into fq_hz (or sr_c)
     int32_t lo, hi;
+    // small-range form (strip kernel, epilogue kinds 3 and 4; the table pre-scaled by 2^k):
+    // r = (mad.hi(v, m, c [- k2 if v < 0])) >> sh, per channel sh and c (padded to 256)
+    const int32_t* sr_sh;
+    const int32_t* sr_c;
+    int32_t k2;
 };
 
 constexpr int kDwPix = 4;
@@ -578,6 +583,8 @@ __global__ void depthwise_i8_dp2a(DwGeom g, const uint32_t* __restrict__ x, cons
 // 9 weight words in registers and walks down a strip of g.rows output rows, loading per
 // output row only the S input rows that enter the window. The three row buffers rotate
 // roles with period 3, written out as one call per role so that no buffer is ever copied.
+// EK: 0 general epilogue, 1/2 fast RESCALE (single/double rounding, rescale_f2), 3/4 the
+// small-range form of a table pre-scaled by 2^k at plan time (single/double rounding).
 template <int S>
 struct DwStrip {
     static constexpr int P = kDwPix;
@@ -647,6 +654,31 @@ __device__ __forceinline__ void dw_strip_row(const uint32_t (&top)[DwStrip<S>::N
             const long long o = (pix0 + p) * cn + c0;
 #pragma unroll
             for (int q = 0; q < 4; ++q) finish_int(e.gen, acc[p][q], c0 + q, out, o + q, lerr);
+        }
+    } else if (EK >= 3) {
+        const int pc = e.per_channel ? c4 : 0;
+        const int4 m = __ldg(reinterpret_cast<const int4*>(e.fq_m) + pc);
+        const int4 sh = __ldg(reinterpret_cast<const int4*>(e.sr_sh) + pc);
+        const int4 c = __ldg(reinterpret_cast<const int4*>(e.sr_c) + pc);
+        auto small = [&](int32_t x, int32_t mm, int32_t s, int32_t cc) -> int32_t {
+            int32_t add = cc;
+            if (EK == 4) add += (x >> 31) * e.k2;  // -2^(31-d) for a negative value (double rounding)
+            int32_t h;
+            asm("mad.hi.s32 %0, %1, %2, %3;" : "=r"(h) : "r"(x), "r"(mm), "r"(add));
+            return h >> s;
+        };
+        uint32_t* o = static_cast<uint32_t*>(out) + pix0 * g.c4 + c4;
+#pragma unroll
+        for (int p = 0; p < P; ++p) {
+            if (ox0 + p >= g.ow) break;
+            int32_t v[4];
+            v[0] = small(acc[p][0], m.x, sh.x, c.x);
+            v[1] = small(acc[p][1], m.y, sh.y, c.y);
+            v[2] = small(acc[p][2], m.z, sh.z, c.z);
+            v[3] = small(acc[p][3], m.w, sh.w, c.w);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) v[q] = min(max(v[q] + e.zp_add, e.lo), e.hi);
+            o[p * g.c4] = pack4_sat_i8(v[0], v[1], v[2], v[3]);
         }
     } else {
         const int pc = e.per_channel ? c4 : 0;
