@@ -22,6 +22,7 @@
  *   CONV2D                     src/ops/conv.rs:502-508 (eval_conv2d), :398-500
  *   DEPTHWISE_CONV2D           src/ops/conv.rs:518-524
  *   MATMUL                     src/ops/matmul.rs:176-178 (eval_matmul), :98-174
+ *   MATMUL_T                   src/ops/matmul.rs:180-182 (eval_matmul_t), :98-174
  *   RESCALE                    src/ops/type_conv.rs:111-191 (eval_rescale)
  *   CLAMP                      src/ops/elementwise.rs:319-343 (eval_clamp)
  *   ADD                        src/ops/elementwise.rs:395-397 (eval_add)
@@ -151,6 +152,21 @@ TB_API tb_status tb_matmul_plan_set_constant_b(tb_matmul_plan *plan, const void 
 TB_API void tb_matmul_plan_destroy(tb_matmul_plan *plan);
 TB_API tb_status tb_matmul(tb_context *ctx, const tb_matmul_desc *desc, const tb_rescale_attr *rescale,
                            const void *a, const void *b, void *out, void *stream);
+
+/* ---- MATMUL_T (src/ops/matmul.rs:180-182 eval_matmul_t, :98-174) ----------
+ * a [n,h,c], b [b_batch,w,c] with b_batch == n or 1 (one B for every batch of
+ * a) -> out [n,h,w]; desc fields mean what they mean for MATMUL. Types are
+ * matmul_t_types (matmul.rs:42-51): INT8 x INT8 -> INT32 (zero points, and an
+ * optional fused rescale, as MATMUL), INT16 x INT16 -> INT48, FP16 x FP16 ->
+ * FP16, and any pair of FP8/FP16/BF16/FP32 into FP32, or into BF16 without
+ * FP32 operands and not FP16 x FP16. INT8 with c % 16 == 0 and BF16 x BF16 /
+ * FP16 x FP16 -> FP32 with c % 8 == 0 run on the tensor cores (B K-major);
+ * the rest on the direct kernels in the reference's order. The plan runs,
+ * declares a constant B and is destroyed with the tb_matmul_plan_* calls. */
+TB_API tb_status tb_matmul_t_plan_create(tb_context *ctx, const tb_matmul_desc *desc, int32_t b_batch,
+                                         const tb_rescale_attr *rescale, tb_matmul_plan **out);
+TB_API tb_status tb_matmul_t(tb_context *ctx, const tb_matmul_desc *desc, int32_t b_batch,
+                             const tb_rescale_attr *rescale, const void *a, const void *b, void *out, void *stream);
 
 /* INT8 x INT8 -> INT32 MATMUL (+ optional fused RESCALE) that allocates no
  * device memory. This entry point has no counterpart in the reference; it is

@@ -12,7 +12,7 @@ It restates the reference interpreter (tosa-interp) on the CPU:
   conformance and network fixtures use.
 
 Parity is pinned: tests/test_oracle_golden.py requires this oracle to match
-every checked-in conformance vector of CONV2D, DEPTHWISE_CONV2D, MATMUL,
+every checked-in conformance vector of CONV2D, DEPTHWISE_CONV2D, MATMUL, MATMUL_T,
 RESCALE, AVG_POOL2D, MAX_POOL2D and CLAMP bit for bit, to reject every
 ERROR_IF case, and to reproduce the network fixtures.
 
@@ -436,6 +436,19 @@ def matmul_types(a, b, out):
     return False
 
 
+def matmul_t_types(a, b, out):
+    """matmul.rs:42-51"""
+    fl = set(FP8_TYPES) | {D["FP16"], D["BF16"], D["FP32"]}
+    if (a, b, out) in ((D["INT8"], D["INT8"], D["INT32"]), (D["INT16"], D["INT16"], D["INT48"]),
+                       (D["FP16"], D["FP16"], D["FP16"])):
+        return True
+    if out == D["FP32"]:
+        return a in fl and b in fl
+    if out == D["BF16"]:
+        return a in fl and b in fl and D["FP32"] not in (a, b) and (a, b) != (D["FP16"], D["FP16"])
+    return False
+
+
 def default_output(a):
     """matmul.rs:54-61"""
     if a == D["INT8"]:
@@ -448,8 +461,17 @@ def default_output(a):
 
 
 def eval_matmul(st: State, op):
+    """matmul.rs:176-178"""
+    return _eval_matmul(st, op, "MATMUL", False, matmul_types)
+
+
+def eval_matmul_t(st: State, op):
+    """matmul.rs:180-182: b [D,W,C], D == N or 1 (broadcast)"""
+    return _eval_matmul(st, op, "MATMUL_T", True, matmul_t_types)
+
+
+def _eval_matmul(st: State, op, name, transposed, types_ok):
     """matmul.rs:98-174"""
-    name = "MATMUL"
     expect_operands(op, name, 4, 1)
     a = st.get(op.inputs[0])
     b = st.get(op.inputs[1])
@@ -458,14 +480,17 @@ def eval_matmul(st: State, op):
     expect_rank(name, "a", a, 3)
     expect_rank(name, "b", b, 3)
     n, h, c = a.shape
-    bn, bc, w = b.shape
-    if bc != c or bn != n:
+    if transposed:
+        bn, w, bc = b.shape
+    else:
+        bn, bc, w = b.shape
+    if bc != c or (bn != n and not (transposed and bn == 1)):
         raise OracleError("ShapeMismatch", f"{name}: b shape {b.shape} incompatible with a {a.shape}")
     out_shape = [n, h, w]
     out_t = st.declared(name, op.outputs[0], out_shape)
     if out_t is None:
         out_t = default_output(a.dtype)
-    if not matmul_types(a.dtype, b.dtype, out_t):
+    if not types_ok(a.dtype, b.dtype, out_t):
         raise OracleError("DTypeMismatch", f"{name}: unsupported types")
     if azp.dtype != a.dtype or bzp.dtype != b.dtype:
         raise OracleError("DTypeMismatch", f"{name}: zero points must match input dtypes")
@@ -475,15 +500,24 @@ def eval_matmul(st: State, op):
         if (za != 0 and a.dtype != D["INT8"]) or (zb != 0 and b.dtype != D["INT8"]):
             raise graph_error(name, "zero points must be zero for non-int8 inputs")
         out = np.zeros(n * h * w, dtype=np.int64)
-        L.orc_matmul_int(ctypes.c_int64(n), ctypes.c_int64(h), ctypes.c_int64(c), ctypes.c_int64(w),
-                         _p(_i64(a.values)), _p(_i64(b.values)), ctypes.c_int64(za), ctypes.c_int64(zb),
-                         ctypes.c_int(out_t == D["INT48"]), _p(out))
+        if transposed:
+            L.orc_matmul_t_int(ctypes.c_int64(n), ctypes.c_int64(h), ctypes.c_int64(c), ctypes.c_int64(w),
+                               ctypes.c_int64(bn), _p(_i64(a.values)), _p(_i64(b.values)), ctypes.c_int64(za),
+                               ctypes.c_int64(zb), ctypes.c_int(out_t == D["INT48"]), _p(out))
+        else:
+            L.orc_matmul_int(ctypes.c_int64(n), ctypes.c_int64(h), ctypes.c_int64(c), ctypes.c_int64(w),
+                             _p(_i64(a.values)), _p(_i64(b.values)), ctypes.c_int64(za), ctypes.c_int64(zb),
+                             ctypes.c_int(out_t == D["INT48"]), _p(out))
         return T(out_t, out_shape, out)
     if float(azp.values[0]) != 0.0 or float(bzp.values[0]) != 0.0:
         raise graph_error(name, "zero points must be zero for floating-point inputs")
     out = np.zeros(n * h * w, dtype=np.float32)
-    L.orc_matmul_float(ctypes.c_int64(n), ctypes.c_int64(h), ctypes.c_int64(c), ctypes.c_int64(w),
-                       _p(_f32(a.values)), _p(_f32(b.values)), ctypes.c_int(out_t), _p(out))
+    if transposed:
+        L.orc_matmul_t_float(ctypes.c_int64(n), ctypes.c_int64(h), ctypes.c_int64(c), ctypes.c_int64(w),
+                             ctypes.c_int64(bn), _p(_f32(a.values)), _p(_f32(b.values)), ctypes.c_int(out_t), _p(out))
+    else:
+        L.orc_matmul_float(ctypes.c_int64(n), ctypes.c_int64(h), ctypes.c_int64(c), ctypes.c_int64(w),
+                           _p(_f32(a.values)), _p(_f32(b.values)), ctypes.c_int(out_t), _p(out))
     return T(out_t, out_shape, out)
 
 
@@ -775,7 +809,7 @@ EVAL = {
     "CONST": eval_const, "CONST_SHAPE": eval_const, "IDENTITY": eval_identity,
     "CONV2D": lambda s, o: eval_conv(s, o, False),
     "DEPTHWISE_CONV2D": lambda s, o: eval_conv(s, o, True),
-    "MATMUL": eval_matmul, "RESCALE": eval_rescale, "AVG_POOL2D": eval_avg_pool,
+    "MATMUL": eval_matmul, "MATMUL_T": eval_matmul_t, "RESCALE": eval_rescale, "AVG_POOL2D": eval_avg_pool,
     "MAX_POOL2D": eval_max_pool, "CLAMP": eval_clamp, "ADD": eval_add,
     "RESHAPE": eval_reshape, "TRANSPOSE": eval_transpose,
 }

@@ -372,6 +372,45 @@ void orc_matmul_int(int64_t n, int64_t h, int64_t c, int64_t w, const int64_t *a
             }
 }
 
+/* MATMUL_T (matmul.rs:75-78 b_index with b_transposed): b [d,w,c], its batch
+ * index 0 for every bn when d == 1 (b_broadcast); otherwise as MATMUL. */
+static int64_t mt_b_index(int64_t bn, int64_t k, int64_t col, int64_t c, int64_t w, int bcast) {
+    int64_t nb = bcast ? 0 : bn;
+    return (nb * w + col) * c + k;
+}
+
+void orc_matmul_t_int(int64_t n, int64_t h, int64_t c, int64_t w, int64_t d, const int64_t *a, const int64_t *b,
+                      int64_t a_zp, int64_t b_zp, int out_i48, int64_t *out) {
+    int bcast = d != n;
+    for (int64_t bn = 0; bn < n; ++bn)
+        for (int64_t row = 0; row < h; ++row)
+            for (int64_t col = 0; col < w; ++col) {
+                uint64_t acc = 0;
+                for (int64_t k = 0; k < c; ++k) {
+                    int64_t x = a[(bn * h + row) * c + k] - a_zp;
+                    int64_t y = b[mt_b_index(bn, k, col, c, w, bcast)] - b_zp;
+                    if (out_i48) acc += (uint64_t)x * (uint64_t)y;
+                    else acc = (uint32_t)((uint32_t)acc + (uint32_t)(int32_t)x * (uint32_t)(int32_t)y);
+                }
+                out[(bn * h + row) * w + col] = out_i48 ? clamp48((int64_t)acc) : (int64_t)(int32_t)(uint32_t)acc;
+            }
+}
+
+void orc_matmul_t_float(int64_t n, int64_t h, int64_t c, int64_t w, int64_t d, const float *a, const float *b,
+                        int out_type, float *out) {
+    int kind = out_type == ORC_F16 ? ACC_F16_UNROUNDED : out_type == ORC_BF16 ? ACC_BF16_UNROUNDED : ACC_F32;
+    int bcast = d != n;
+    for (int64_t bn = 0; bn < n; ++bn)
+        for (int64_t row = 0; row < h; ++row)
+            for (int64_t col = 0; col < w; ++col) {
+                float acc = 0.0f;
+                for (int64_t k = 0; k < c; ++k)
+                    acc = fmac(kind, acc, orc_round_to(out_type, a[(bn * h + row) * c + k]),
+                               orc_round_to(out_type, b[mt_b_index(bn, k, col, c, w, bcast)]));
+                out[(bn * h + row) * w + col] = orc_round_to(out_type, acc);
+            }
+}
+
 void orc_matmul_float(int64_t n, int64_t h, int64_t c, int64_t w, const float *a, const float *b,
                       int out_type, float *out) {
     /* matmul.rs:160-170: operands rounded to the output type; accumulator per

@@ -100,6 +100,11 @@ void orc_matmul_int(int64_t n, int64_t h, int64_t c, int64_t w, const int64_t *a
                     int64_t a_zp, int64_t b_zp, int out_i48, int64_t *out);
 void orc_matmul_float(int64_t n, int64_t h, int64_t c, int64_t w, const float *a, const float *b,
                       int out_type, float *out);
+/* MATMUL_T, matmul.rs:75-95 with b_transposed: b [d,w,c], d == n, or 1 broadcast. */
+void orc_matmul_t_int(int64_t n, int64_t h, int64_t c, int64_t w, int64_t d, const int64_t *a, const int64_t *b,
+                      int64_t a_zp, int64_t b_zp, int out_i48, int64_t *out);
+void orc_matmul_t_float(int64_t n, int64_t h, int64_t c, int64_t w, int64_t d, const float *a, const float *b,
+                        int out_type, float *out);
 /* MATMUL int path split over `threads` POSIX threads by (batch,row): used only
  * as the timed CPU reference arm, same arithmetic and loop order per row. */
 void orc_matmul_int_mt(int64_t n, int64_t h, int64_t c, int64_t w, const int64_t *a,

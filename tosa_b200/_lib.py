@@ -115,6 +115,8 @@ SIGNATURES = [
     ("tb_matmul_plan_destroy", None, [_V]),
     ("tb_matmul", _I, [_V, _P(MatmulDesc), _P(RescaleAttr), _V, _V, _V, _V]),
     ("tb_matmul_i8_noalloc", _I, [_P(MatmulDesc), _P(RescaleAttr), _V, _V, _V, _V]),
+    ("tb_matmul_t_plan_create", _I, [_V, _P(MatmulDesc), ctypes.c_int32, _P(RescaleAttr), _P(_V)]),
+    ("tb_matmul_t", _I, [_V, _P(MatmulDesc), ctypes.c_int32, _P(RescaleAttr), _V, _V, _V, _V]),
     ("tb_conv2d_plan_create", _I, [_V, _P(Conv2dDesc), _V, _V, _P(RescaleAttr), _P(_V)]),
     ("tb_depthwise_conv2d_plan_create", _I, [_V, _P(Conv2dDesc), _V, _V, _P(RescaleAttr), _P(_V)]),
     ("tb_conv2d_plan_run", _I, [_V, _V, _V, _V]),

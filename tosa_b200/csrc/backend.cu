@@ -448,36 +448,55 @@ TB_API uint64_t tb_launch_count(tb_context* ctx) { return ctx ? ctx->launches : 
 
 namespace tb {
 
-tb_status matmul_validate(const tb_matmul_desc* d, bool has_rescale, int* path, int* bn) {
-    if (d->n < 0 || d->h < 0 || d->c < 0 || d->w < 0) return fail(TB_ERR_SHAPE_MISMATCH, "MATMUL: negative dimension");
-    // matmul_types (src/ops/matmul.rs:30-38), restricted to what runs here.
+tb_status matmul_validate(const tb_matmul_desc* d, bool has_rescale, int* path, int* bn, int t_batch) {
+    const bool tr = t_batch != 0;
+    const char* name = tr ? "MATMUL_T" : "MATMUL";
+    if (d->n < 0 || d->h < 0 || d->c < 0 || d->w < 0) return fail(TB_ERR_SHAPE_MISMATCH, "%s: negative dimension", name);
+    if (tr && t_batch != d->n && t_batch != 1)
+        return fail(TB_ERR_SHAPE_MISMATCH, "MATMUL_T: b batch %d is neither n=%d nor 1", t_batch, d->n);
     const int at = d->a_dtype, bt = d->b_dtype, ot = d->out_dtype;
     const bool int8 = at == TB_DT_INT8 && bt == TB_DT_INT8 && ot == TB_DT_INT32;
     const bool int16 = at == TB_DT_INT16 && bt == TB_DT_INT16 && ot == TB_DT_INT48;
     const bool fp8a = at == TB_DT_FP8E4M3 || at == TB_DT_FP8E5M2, fp8b = bt == TB_DT_FP8E4M3 || bt == TB_DT_FP8E5M2;
-    // (F16, F16, F16|F32), (BF16, BF16, F32), (F32, F32, F32), (FP8, FP8, F16|F32)
-    const bool fl = (at == TB_DT_FP16 && bt == TB_DT_FP16 && (ot == TB_DT_FP16 || ot == TB_DT_FP32)) ||
-                    (at == TB_DT_BF16 && bt == TB_DT_BF16 && ot == TB_DT_FP32) ||
-                    (at == TB_DT_FP32 && bt == TB_DT_FP32 && ot == TB_DT_FP32) ||
-                    (fp8a && fp8b && (ot == TB_DT_FP16 || ot == TB_DT_FP32));
-    if (!int8 && !int16 && !fl) return fail(TB_ERR_DTYPE_MISMATCH, "MATMUL: unsupported types a=%d b=%d output=%d", at, bt, ot);
+    bool fl;
+    if (!tr) {
+        // matmul_types (src/ops/matmul.rs:30-38):
+        // (F16, F16, F16|F32), (BF16, BF16, F32), (F32, F32, F32), (FP8, FP8, F16|F32)
+        fl = (at == TB_DT_FP16 && bt == TB_DT_FP16 && (ot == TB_DT_FP16 || ot == TB_DT_FP32)) ||
+             (at == TB_DT_BF16 && bt == TB_DT_BF16 && ot == TB_DT_FP32) ||
+             (at == TB_DT_FP32 && bt == TB_DT_FP32 && ot == TB_DT_FP32) ||
+             (fp8a && fp8b && (ot == TB_DT_FP16 || ot == TB_DT_FP32));
+    } else {
+        // matmul_t_types (src/ops/matmul.rs:42-51): (F16, F16, F16); any FP8/F16/BF16/F32 pair
+        // into F32; into BF16 without F32 operands and not (F16, F16)
+        auto isf = [](int t) {
+            return t == TB_DT_FP8E4M3 || t == TB_DT_FP8E5M2 || t == TB_DT_FP16 || t == TB_DT_BF16 || t == TB_DT_FP32;
+        };
+        fl = (at == TB_DT_FP16 && bt == TB_DT_FP16 && ot == TB_DT_FP16) || (ot == TB_DT_FP32 && isf(at) && isf(bt)) ||
+             (ot == TB_DT_BF16 && isf(at) && isf(bt) && at != TB_DT_FP32 && bt != TB_DT_FP32 &&
+              !(at == TB_DT_FP16 && bt == TB_DT_FP16));
+    }
+    if (!int8 && !int16 && !fl)
+        return fail(TB_ERR_DTYPE_MISMATCH, "%s: unsupported types a=%d b=%d output=%d", name, at, bt, ot);
     if (int8 || int16) {
         if ((d->a_zp != 0 && at != TB_DT_INT8) || (d->b_zp != 0 && bt != TB_DT_INT8))
-            return fail(TB_ERR_GRAPH, "MATMUL: zero points must be zero for non-int8 inputs");
+            return fail(TB_ERR_GRAPH, "%s: zero points must be zero for non-int8 inputs", name);
     } else if (d->a_zp != 0 || d->b_zp != 0) {
-        return fail(TB_ERR_GRAPH, "MATMUL: zero points must be zero for floating-point inputs");
+        return fail(TB_ERR_GRAPH, "%s: zero points must be zero for floating-point inputs", name);
     }
-    if (has_rescale && !int8) return fail(TB_ERR_DTYPE_MISMATCH, "MATMUL: RESCALE needs an int32 result");
+    if (has_rescale && !int8) return fail(TB_ERR_DTYPE_MISMATCH, "%s: RESCALE needs an int32 result", name);
     const int e = int8 ? 1 : 2;
-    const bool tma_ok = (static_cast<long long>(d->c) * e) % 16 == 0 && (static_cast<long long>(d->w) * e) % 16 == 0 &&
-                        d->c > 0 && d->w > 0 && d->h > 0 && d->n > 0;
+    // TMA row strides: A's and B's rows are c elements long for MATMUL_T; B's are w long for MATMUL
+    const bool tma_ok = (static_cast<long long>(d->c) * e) % 16 == 0 &&
+                        (tr || (static_cast<long long>(d->w) * e) % 16 == 0) && d->c > 0 && d->w > 0 && d->h > 0 &&
+                        d->n > 0;
     // tensor cores: int8 -> int32, and BF16/F16 pairs with an FP32 result; everything else runs
     // the direct kernels in the reference's accumulation order (path 2 int8, 3 float, 4 int16)
     const bool tc_float = at == bt && (at == TB_DT_BF16 || at == TB_DT_FP16) && ot == TB_DT_FP32;
     // int8 with A rows TMA-addressable but B rows not (e.g. 1000 classes): B is copied
     // into column-padded rows each run and the tensor cores take it (path 5)
     // (w % 4 == 0: the in-kernel column sums of B read 4-byte words of its rows)
-    const bool pad_b = int8 && !tma_ok && d->c % 16 == 0 && d->c > 0 && d->h > 0 && d->n > 0 && d->w >= 16 &&
+    const bool pad_b = !tr && int8 && !tma_ok && d->c % 16 == 0 && d->c > 0 && d->h > 0 && d->n > 0 && d->w >= 16 &&
                        d->w % 4 == 0 && static_cast<long long>(d->h) * d->n >= 64;
     if (int16) *path = 4;
     else if (int8) *path = tma_ok ? 0 : (pad_b ? 5 : 2);
@@ -488,18 +507,21 @@ tb_status matmul_validate(const tb_matmul_desc* d, bool has_rescale, int* path, 
 
 }  // namespace tb
 
-extern "C" TB_API tb_status tb_matmul_plan_create(tb_context* ctx, const tb_matmul_desc* d,
-                                                  const tb_rescale_attr* rescale, tb_matmul_plan** out) {
+namespace {
+
+tb_status matmul_plan_create(tb_context* ctx, const tb_matmul_desc* d, int t_batch, const tb_rescale_attr* rescale,
+                             tb_matmul_plan** out) {
     if (!ctx || !d || !out) return fail(TB_ERR_INVALID_ARGUMENT, "null argument");
     *out = nullptr;
     TB_CUDA(cudaSetDevice(ctx->device));
     int path = 0, bn = 256;
-    TB_TRY(matmul_validate(d, rescale != nullptr, &path, &bn));
+    TB_TRY(matmul_validate(d, rescale != nullptr, &path, &bn, t_batch));
     tb_matmul_plan* p = new tb_matmul_plan;
     p->ctx = ctx;
     p->d = *d;
     p->path = path;
     p->bn = bn;
+    p->t_batch = t_batch;
     if (rescale) {
         tb_status s = make_rescale_plan(ctx, rescale, TB_DT_INT32, d->w, &p->rs);
         if (s != TB_OK) { delete p; return s; }
@@ -517,13 +539,30 @@ extern "C" TB_API tb_status tb_matmul_plan_create(tb_context* ctx, const tb_matm
     }
     if ((p->path == 0 || p->path == 5) && d->a_zp != 0) {
         // padded by one tile: the epilogue reads whole 16-column chunks without clamping
-        cudaError_t ce = cudaMalloc(&p->d_colterm, sizeof(int32_t) * (static_cast<size_t>(d->n) * d->w + 256));
+        const size_t cbatch = t_batch ? static_cast<size_t>(t_batch) : static_cast<size_t>(d->n);
+        cudaError_t ce = cudaMalloc(&p->d_colterm, sizeof(int32_t) * (cbatch * d->w + 256));
         if (ce == cudaSuccess) ce = cudaMalloc(&p->d_counter, sizeof(unsigned int));
         if (ce == cudaSuccess) ce = cudaMemset(p->d_counter, 0, sizeof(unsigned int));
         if (ce != cudaSuccess) { free_rescale_plan(&p->rs); delete p; return fail(TB_ERR_CUDA, "colterm alloc failed"); }
     }
     *out = p;
     return TB_OK;
+}
+
+}  // namespace
+
+extern "C" TB_API tb_status tb_matmul_plan_create(tb_context* ctx, const tb_matmul_desc* d,
+                                                  const tb_rescale_attr* rescale, tb_matmul_plan** out) {
+    return matmul_plan_create(ctx, d, 0, rescale, out);
+}
+
+extern "C" TB_API tb_status tb_matmul_t_plan_create(tb_context* ctx, const tb_matmul_desc* d, int32_t b_batch,
+                                                    const tb_rescale_attr* rescale, tb_matmul_plan** out) {
+    if (b_batch <= 0) {
+        if (out) *out = nullptr;
+        return fail(TB_ERR_SHAPE_MISMATCH, "MATMUL_T: b batch %d is neither n nor 1", b_batch);
+    }
+    return matmul_plan_create(ctx, d, b_batch, rescale, out);
 }
 
 extern "C" TB_API tb_status tb_matmul_plan_run(tb_matmul_plan* p, const void* a, const void* b, void* out,
@@ -546,17 +585,18 @@ extern "C" TB_API tb_status tb_matmul_plan_run(tb_matmul_plan* p, const void* a,
         }
         b_tma = p->d_bpad;
     } else if (p->path >= 2 || !aligned16(a) || !aligned16(b)) {
+        const int bt = p->t_batch != 0, bb = p->t_batch == 1;
         if (d.a_dtype == TB_DT_INT8) {
             matmul_direct_int<<<grid_for(ctx, total), 256, 0, st>>>(d.n, d.h, d.c, d.w, static_cast<const int8_t*>(a),
-                                                                    static_cast<const int8_t*>(b), d.a_zp, d.b_zp,
-                                                                    int_epi(p->rs), out, ctx->dev_err);
+                                                                    static_cast<const int8_t*>(b), bt, bb, d.a_zp,
+                                                                    d.b_zp, int_epi(p->rs), out, ctx->dev_err);
         } else if (d.a_dtype == TB_DT_INT16) {
             matmul_direct_i48<<<grid_for(ctx, total), 256, 0, st>>>(d.n, d.h, d.c, d.w, static_cast<const int16_t*>(a),
-                                                                    static_cast<const int16_t*>(b),
+                                                                    static_cast<const int16_t*>(b), bt, bb,
                                                                     static_cast<int64_t*>(out));
         } else {
-            matmul_direct_float<<<grid_for(ctx, total), 256, 0, st>>>(d.n, d.h, d.c, d.w, a, b, d.a_dtype, d.b_dtype,
-                                                                      d.out_dtype, out);
+            matmul_direct_float<<<grid_for(ctx, total), 256, 0, st>>>(d.n, d.h, d.c, d.w, a, b, bt, bb, d.a_dtype,
+                                                                      d.b_dtype, d.out_dtype, out);
         }
         TB_LAUNCHED(ctx);
         return TB_OK;
@@ -570,7 +610,15 @@ extern "C" TB_API tb_status tb_matmul_plan_run(tb_matmul_plan* p, const void* a,
         TB_TRY(encode_tiled(&p->tmA, tmap_dtype(d.a_dtype), 3, a, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B));
         p->a_cached = a;
     }
-    if (b_tma != p->b_cached) {
+    if (b_tma != p->b_cached && p->t_batch) {
+        // MATMUL_T: B [t_batch][w][c], K-major rows of c elements
+        const uint64_t dims[3] = {static_cast<uint64_t>(d.c), static_cast<uint64_t>(d.w),
+                                  static_cast<uint64_t>(p->t_batch)};
+        const uint64_t str[2] = {static_cast<uint64_t>(d.c) * e, static_cast<uint64_t>(d.c) * d.w * e};
+        const uint32_t box[3] = {static_cast<uint32_t>(128 / e), static_cast<uint32_t>(p->bn), 1};
+        TB_TRY(encode_tiled(&p->tmB, tmap_dtype(d.b_dtype), 3, b_tma, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B));
+        p->b_cached = b_tma;
+    } else if (b_tma != p->b_cached) {
         const uint64_t dims[3] = {static_cast<uint64_t>(wt), static_cast<uint64_t>(d.c), static_cast<uint64_t>(d.n)};
         const uint64_t str[2] = {static_cast<uint64_t>(wt) * e, static_cast<uint64_t>(wt) * d.c * e};
         const uint32_t box[3] = {static_cast<uint32_t>(128 / e), static_cast<uint32_t>(128 / e), 1};
@@ -587,9 +635,39 @@ extern "C" TB_API tb_status tb_matmul_plan_run(tb_matmul_plan* p, const void* a,
     gp.out = out;
     gp.out_batch_stride = static_cast<long long>(d.h) * d.w;
     gp.ldo = d.w;
+    gp.b_bcast = p->t_batch == 1;
     GemmEpilogue& ep = gp.epi;
     // the small-range epilogue takes its integer terms pre-multiplied by 2^k
     const uint32_t tmul = p->sr.ok ? static_cast<uint32_t>(p->sr.mul) : 1u;
+    if (p->path == 0 && p->t_batch) {
+        if (d.a_zp != 0) {
+            // colterm = -a_zp * rowsum(B) + c * a_zp * b_zp per B row (x 2^k for the small-range
+            // epilogue); computed by the kernel before the GEMM, which waits for it in its epilogue
+            if (!b_prepared) {
+                const long long rows = static_cast<long long>(p->t_batch) * d.w;
+                const int32_t add = static_cast<int32_t>(static_cast<uint32_t>(d.c) * static_cast<uint32_t>(d.a_zp) *
+                                                         static_cast<uint32_t>(d.b_zp) * tmul);
+                colterm_rows_i8<<<static_cast<unsigned>(std::min<long long>((rows + 7) / 8, 4LL * ctx->num_sms)), 256, 0,
+                                  st>>>(rows, d.c, static_cast<const int8_t*>(b),
+                                        static_cast<int32_t>(static_cast<uint32_t>(-d.a_zp) * tmul), add, p->d_colterm);
+                TB_LAUNCHED(ctx);
+                ep.pdl_wait = 1;
+            }
+            ep.colterm = p->d_colterm;
+            ep.colterm_bstride = p->t_batch == 1 ? 0 : d.w;
+        }
+        ep.row_zp_neg = static_cast<int32_t>(static_cast<uint32_t>(-d.b_zp) * tmul);
+        if (p->rs.enabled) {
+            ep.mode = EPI_RESCALE;
+            ep.rs = rescale_args(p->rs);
+            set_fast_epilogue(&ep, p->rs, p->sr);
+            ep.out_dtype = p->rs.out_dtype;
+        } else {
+            ep.mode = EPI_I32;
+            ep.out_dtype = TB_DT_INT32;
+        }
+        return launch_i8_matmul_t(ctx, p->bn, epilogue_kind(ep), p->tmA, p->tmB, gp, st);
+    }
     if (p->path == 0 || p->path == 5) {
         if (d.a_zp != 0 && b_prepared) {
             ep.colterm = p->d_colterm;
@@ -632,6 +710,7 @@ extern "C" TB_API tb_status tb_matmul_plan_run(tb_matmul_plan* p, const void* a,
     }
     ep.mode = EPI_F32;
     ep.out_dtype = TB_DT_FP32;
+    if (p->t_batch) return launch_f16_matmul_t(ctx, p->bn, p->tmA, p->tmB, gp, st);
     return launch_f16_matmul(ctx, p->bn, p->tmA, p->tmB, gp, st);
 }
 
@@ -644,12 +723,23 @@ extern "C" TB_API tb_status tb_matmul_plan_set_constant_b(tb_matmul_plan* p, con
     TB_CUDA(cudaSetDevice(ctx->device));
     cudaStream_t st = static_cast<cudaStream_t>(stream_);
     if (static_cast<long long>(d.n) * d.c * d.w == 0) return TB_OK;
-    if (p->path == 5) {
+    if (p->path == 5 && !p->t_batch) {
         pad_weight_rows_i8<<<grid_for(ctx, static_cast<long long>(d.n) * d.c * p->wp), 256, 0, st>>>(
             d.n * d.c, d.w, p->wp, static_cast<const int8_t*>(b), p->d_bpad);
         TB_LAUNCHED(ctx);
     }
-    if (d.a_zp != 0) {
+    if (d.a_zp != 0 && p->t_batch) {
+        // runs with an unaligned B take the direct kernel, which keeps nothing per B
+        if (!aligned16(b)) return TB_OK;
+        const uint32_t tmul = p->sr.ok ? static_cast<uint32_t>(p->sr.mul) : 1u;
+        const long long rows = static_cast<long long>(p->t_batch) * d.w;
+        const int32_t add = static_cast<int32_t>(static_cast<uint32_t>(d.c) * static_cast<uint32_t>(d.a_zp) *
+                                                 static_cast<uint32_t>(d.b_zp) * tmul);
+        colterm_rows_i8<<<static_cast<unsigned>(std::min<long long>((rows + 7) / 8, 4LL * ctx->num_sms)), 256, 0, st>>>(
+            rows, d.c, static_cast<const int8_t*>(b), static_cast<int32_t>(static_cast<uint32_t>(-d.a_zp) * tmul), add,
+            p->d_colterm);
+        TB_LAUNCHED(ctx);
+    } else if (d.a_zp != 0) {
         // colterm = -a_zp * colsum(B) + c * a_zp * b_zp (the in-GEMM column-sum job's values)
         const uint32_t tmul = p->sr.ok ? static_cast<uint32_t>(p->sr.mul) : 1u;  // small-range epilogue: x 2^k
         const int32_t add = static_cast<int32_t>(static_cast<uint32_t>(d.c) * static_cast<uint32_t>(d.a_zp) *
@@ -672,6 +762,17 @@ extern "C" TB_API void tb_matmul_plan_destroy(tb_matmul_plan* p) {
     if (p->d_counter) cudaFree(p->d_counter);
     if (p->d_bpad) cudaFree(p->d_bpad);
     delete p;
+}
+
+extern "C" TB_API tb_status tb_matmul_t(tb_context* ctx, const tb_matmul_desc* d, int32_t b_batch,
+                                        const tb_rescale_attr* rescale, const void* a, const void* b, void* out,
+                                        void* stream) {
+    tb_matmul_plan* p = nullptr;
+    TB_TRY(tb_matmul_t_plan_create(ctx, d, b_batch, rescale, &p));
+    tb_status s = tb_matmul_plan_run(p, a, b, out, stream);
+    cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+    tb_matmul_plan_destroy(p);
+    return s;
 }
 
 extern "C" TB_API tb_status tb_matmul(tb_context* ctx, const tb_matmul_desc* d, const tb_rescale_attr* rescale,

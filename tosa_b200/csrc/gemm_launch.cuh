@@ -136,6 +136,11 @@ tb_status launch_i8_conv_tap2(tb_context* ctx, int bn, int ek, const CUtensorMap
                               const GemmParams& p, cudaStream_t st);
 tb_status launch_f16_matmul(tb_context* ctx, int bn, const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p,
                             cudaStream_t st);
+// MATMUL_T (B K-major, [d,w,c]); in gemm_mm_t.cu.
+tb_status launch_i8_matmul_t(tb_context* ctx, int bn, int ek, const CUtensorMap& a, const CUtensorMap& b,
+                             const GemmParams& p, cudaStream_t st);
+tb_status launch_f16_matmul_t(tb_context* ctx, int bn, const CUtensorMap& a, const CUtensorMap& b,
+                              const GemmParams& p, cudaStream_t st);
 tb_status launch_f16_conv(tb_context* ctx, int bn, const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p,
                           cudaStream_t st);
 

@@ -176,7 +176,8 @@ tb_status launch_residual(tb_context* ctx, const void* a, int a_dt, int a_uns, i
 
 // MATMUL static checks (src/ops/matmul.rs:112-153) and path choice:
 // path 0 tensor-core int8, 1 tensor-core f16/bf16, 2 direct int8, 3 direct float.
-tb_status matmul_validate(const tb_matmul_desc* d, bool has_rescale, int* path, int* bn);
+// t_batch: 0 for MATMUL; for MATMUL_T the batch of B [t_batch, w, c] (n or 1)
+tb_status matmul_validate(const tb_matmul_desc* d, bool has_rescale, int* path, int* bn, int t_batch = 0);
 
 }  // namespace tb
 
@@ -185,6 +186,7 @@ struct tb_matmul_plan {
     tb_context* ctx = nullptr;
     tb_matmul_desc d{};
     int path = 0;  // 0 TC int8, 1 TC f16/bf16, 2 direct int, 3 direct float, 4 direct int16, 5 TC int8, padded B
+    int t_batch = 0;  // MATMUL_T: batch of B [t_batch, w, c] (n, or 1 broadcast); 0 for MATMUL
     tb::RescalePlan rs;
     tb::SmallRange sr;
     int bn = 256;

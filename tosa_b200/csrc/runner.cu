@@ -65,6 +65,7 @@ const char* op_name(int op) {
     case fb::OP_CONV2D: return "CONV2D";
     case fb::OP_DEPTHWISE_CONV2D: return "DEPTHWISE_CONV2D";
     case fb::OP_MATMUL: return "MATMUL";
+    case fb::OP_MATMUL_T: return "MATMUL_T";
     case fb::OP_MAX_POOL2D: return "MAX_POOL2D";
     case fb::OP_CLAMP: return "CLAMP";
     case fb::OP_ADD: return "ADD";
@@ -143,6 +144,7 @@ struct Step {
     bool depthwise = false;
     tb_conv2d_desc cdesc{};
     tb_matmul_desc mdesc{};
+    int mt_batch = 0;               // MATMUL_T: batch of b [mt_batch, w, c] (n or 1); 0 for MATMUL
     tb_conv2d_plan* conv = nullptr;
     tb_matmul_plan* mm = nullptr;
     tb_rescale_attr rattr{};        // fused or standalone RESCALE attribute (host arrays below)
@@ -583,8 +585,9 @@ class Compiler {
         s.out = {make_out(o.outputs[0], B.dtype, out_shape)};
     }
 
-    void c_matmul(const fb::Operator& o, Step& s) {
-        const char* op = "MATMUL";
+    // MATMUL, and MATMUL_T (transposed) with b [d,w,c], d == n or 1 (src/ops/matmul.rs:98-174)
+    void c_matmul(const fb::Operator& o, Step& s, bool transposed) {
+        const char* op = transposed ? "MATMUL_T" : "MATMUL";
         expect_operands(o, op, 4, 1);
         const int a = get(o.inputs[0]), b = get(o.inputs[1]);
         const Tensor& za = single(op, "a_zp", get(o.inputs[2]));
@@ -592,10 +595,11 @@ class Compiler {
         const Tensor &A = T(a), &B = T(b);
         expect_rank(op, "a", A, 3);
         expect_rank(op, "b", B, 3);
-        if (B.shape[1] != A.shape[2] || B.shape[0] != A.shape[0])
+        const int64_t bc = transposed ? B.shape[2] : B.shape[1], bw = transposed ? B.shape[1] : B.shape[2];
+        if (bc != A.shape[2] || (B.shape[0] != A.shape[0] && !(transposed && B.shape[0] == 1)))
             raise(TB_ERR_SHAPE_MISMATCH, "%s: b shape %s incompatible with a shape %s", op, shape_str(B.shape).c_str(),
                   shape_str(A.shape).c_str());
-        const std::vector<int64_t> out_shape = {A.shape[0], A.shape[1], B.shape[2]};
+        const std::vector<int64_t> out_shape = {A.shape[0], A.shape[1], bw};
         int out_t = declared(op, o.outputs[0], out_shape);
         if (!out_t) {
             const int at = A.dtype;
@@ -608,7 +612,7 @@ class Compiler {
         d.n = static_cast<int32_t>(A.shape[0]);
         d.h = static_cast<int32_t>(A.shape[1]);
         d.c = static_cast<int32_t>(A.shape[2]);
-        d.w = static_cast<int32_t>(B.shape[2]);
+        d.w = static_cast<int32_t>(bw);
         d.a_dtype = A.dtype;
         d.b_dtype = B.dtype;
         d.out_dtype = out_t;
@@ -620,8 +624,9 @@ class Compiler {
                             (zb.hf.empty() ? ival(zb) != 0 : zb.hf[0] != 0.f);
             if (nz) raise(TB_ERR_GRAPH, "%s: zero points must be zero for floating-point inputs", op);
         }
+        s.mt_batch = transposed ? static_cast<int>(B.shape[0]) : 0;
         int path = 0, bn = 0;
-        tb_status st = matmul_validate(&d, false, &path, &bn);
+        tb_status st = matmul_validate(&d, false, &path, &bn, s.mt_batch);
         if (st != TB_OK) raise(st, "%s", tb_last_error());
         s.kind = K_MATMUL;
         s.in = {a, b, get(o.inputs[2]), get(o.inputs[3])};
@@ -867,7 +872,8 @@ class Compiler {
         case fb::OP_TRANSPOSE: c_transpose(o, s); break;
         case fb::OP_CONV2D: c_conv(o, s, false); break;
         case fb::OP_DEPTHWISE_CONV2D: c_conv(o, s, true); break;
-        case fb::OP_MATMUL: c_matmul(o, s); break;
+        case fb::OP_MATMUL: c_matmul(o, s, false); break;
+        case fb::OP_MATMUL_T: c_matmul(o, s, true); break;
         case fb::OP_RESCALE: c_rescale(o, s); break;
         case fb::OP_CLAMP: c_clamp(o, s); break;
         case fb::OP_ADD: c_add(o, s); break;
@@ -1142,7 +1148,8 @@ tb_status do_compile(tb_graph* G) {
             break;
         }
         case K_MATMUL:
-            st = tb_matmul_plan_create(ctx, &s.mdesc, s.has_rescale ? &s.rattr : nullptr, &s.mm);
+            st = s.mt_batch ? tb_matmul_t_plan_create(ctx, &s.mdesc, s.mt_batch, s.has_rescale ? &s.rattr : nullptr, &s.mm)
+                            : tb_matmul_plan_create(ctx, &s.mdesc, s.has_rescale ? &s.rattr : nullptr, &s.mm);
             if (st == TB_OK) s.mm->replayable = (G->flags & TB_GRAPH_CUDA_GRAPH) != 0;
             if (st == TB_OK && G->tensors[s.in[1]].is_static && G->tensors[s.in[1]].dev != nullptr)
                 st = tb_matmul_plan_set_constant_b(s.mm, G->tensors[s.in[1]].dev, nullptr);  // e.g. FC weights

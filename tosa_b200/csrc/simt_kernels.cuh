@@ -308,6 +308,32 @@ __global__ void colterm_const_i8(int c, int w, const int8_t* __restrict__ b, int
     }
 }
 
+// Column terms of MATMUL_T's B [d][w][c] (K-major rows, c % 16 == 0): out[r] = scale *
+// sum_k B[r][k] + add for the d*w rows r. One warp per row, 16-byte loads. Releases its
+// dependent launch at once: the GEMM reading `out` waits for it only in its epilogue.
+__global__ void __launch_bounds__(256) colterm_rows_i8(long long rows, int c, const int8_t* __restrict__ b,
+                                                       int32_t scale, int32_t add, int32_t* __restrict__ out) {
+    grid_launch_dependents();
+    const int lane = threadIdx.x & 31;
+    const long long nw = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+    for (long long r = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += nw) {
+        const int4* row = reinterpret_cast<const int4*>(b + r * c);
+        int sum = 0;
+        for (int j = lane; j < (c >> 4); j += 32) {
+            const int4 v = row[j];
+            sum = __dp4a(v.x, 0x01010101, sum);
+            sum = __dp4a(v.y, 0x01010101, sum);
+            sum = __dp4a(v.z, 0x01010101, sum);
+            sum = __dp4a(v.w, 0x01010101, sum);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (lane == 0)
+            out[r] = static_cast<int32_t>(static_cast<uint32_t>(scale) * static_cast<uint32_t>(sum) +
+                                          static_cast<uint32_t>(add));
+    }
+}
+
 // INT16 x INT8 -> INT48 (AccI64, src/ops/accum.rs:43-56): int64 accumulation,
 // bias added with wrap-around, then clamped to 48 bits (src/ops/conv.rs:466-470).
 // INT48 values are stored as int64. depthwise: weight [KH,KW,C,M].
@@ -353,8 +379,15 @@ __global__ void conv2d_direct_i48(ConvGeomDev g, const int16_t* __restrict__ x, 
     }
 }
 
+// Offset of B's element (k, col) for batch bn: MATMUL's B is [n,c,w]; MATMUL_T's (bt) is
+// [d,w,c] (src/ops/matmul.rs:75-78), its one batch broadcast over every bn when bb.
+__device__ __forceinline__ long long mm_b_index(int bn, int k, int col, int c, int w, int bt, int bb) {
+    const long long nb = bb ? 0 : bn;
+    return bt ? (nb * w + col) * c + k : (nb * c + k) * w + col;
+}
+
 __global__ void matmul_direct_i48(int n, int h, int c, int w, const int16_t* __restrict__ a,
-                                  const int16_t* __restrict__ bm, int64_t* __restrict__ out) {
+                                  const int16_t* __restrict__ bm, int bt, int bb, int64_t* __restrict__ out) {
     const long long total = static_cast<long long>(n) * h * w;
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -363,8 +396,7 @@ __global__ void matmul_direct_i48(int n, int h, int c, int w, const int16_t* __r
         const int bn = static_cast<int>(rowi / h);
         uint64_t acc = 0;
         for (int k = 0; k < c; ++k)
-            acc += static_cast<uint64_t>(static_cast<int64_t>(a[rowi * c + k]) *
-                                         bm[(static_cast<long long>(bn) * c + k) * w + col]);
+            acc += static_cast<uint64_t>(static_cast<int64_t>(a[rowi * c + k]) * bm[mm_b_index(bn, k, col, c, w, bt, bb)]);
         out[i] = clamp48(static_cast<int64_t>(acc));
     }
 }
@@ -835,8 +867,8 @@ __global__ void depthwise_float(ConvGeomDev g, const void* __restrict__ x, const
 // Direct MATMUL (src/ops/matmul.rs:80-95), one thread per output element.
 // ---------------------------------------------------------------------------
 __global__ void matmul_direct_int(int n, int h, int c, int w, const int8_t* __restrict__ a,
-                                  const int8_t* __restrict__ bm, int32_t za, int32_t zb, IntEpiDev e, void* out,
-                                  uint32_t* err) {
+                                  const int8_t* __restrict__ bm, int bt, int bb, int32_t za, int32_t zb, IntEpiDev e,
+                                  void* out, uint32_t* err) {
     const long long total = static_cast<long long>(n) * h * w;
     uint32_t lerr = 0;
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
@@ -845,17 +877,18 @@ __global__ void matmul_direct_int(int n, int h, int c, int w, const int8_t* __re
         const long long rowi = i / w;  // bn*h + row
         const int bn = static_cast<int>(rowi / h);
         const int8_t* ar = a + rowi * c;
-        const int8_t* bc = bm + static_cast<long long>(bn) * c * w + col;
+        const int8_t* bc = bm + mm_b_index(bn, 0, col, c, w, bt, bb);
+        const long long kstep = bt ? 1 : w;
         uint32_t acc = 0;
         for (int k = 0; k < c; ++k)
-            acc += static_cast<uint32_t>(ar[k] - za) * static_cast<uint32_t>(bc[static_cast<long long>(k) * w] - zb);
+            acc += static_cast<uint32_t>(ar[k] - za) * static_cast<uint32_t>(bc[k * kstep] - zb);
         finish_int(e, static_cast<int32_t>(acc), col, out, i, &lerr);
     }
     if (lerr) atomicOr(err, lerr);
 }
 
 __global__ void matmul_direct_float(int n, int h, int c, int w, const void* __restrict__ a, const void* __restrict__ bm,
-                                    int in_dt, int b_dt, int out_dt, void* out) {
+                                    int bt, int bb, int in_dt, int b_dt, int out_dt, void* out) {
     const long long total = static_cast<long long>(n) * h * w;
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -863,10 +896,11 @@ __global__ void matmul_direct_float(int n, int h, int c, int w, const void* __re
         const long long rowi = i / w;
         const int bn = static_cast<int>(rowi / h);
         float acc = 0.f;
-        // operands are first converted to the output type (exact for every admitted pair)
+        // operands are first converted to the output type (matmul.rs:160-162; this rounds only
+        // the F16 / F32 operands of a BF16 MATMUL_T)
         for (int k = 0; k < c; ++k)
-            acc = mac_acc(acc, load_f(a, rowi * c + k, in_dt),
-                          load_f(bm, (static_cast<long long>(bn) * c + k) * w + col, b_dt), out_dt, true);
+            acc = mac_acc(acc, round_to_dtype(load_f(a, rowi * c + k, in_dt), out_dt),
+                          round_to_dtype(load_f(bm, mm_b_index(bn, k, col, c, w, bt, bb), b_dt), out_dt), out_dt, true);
         store_f(out, i, out_dt, acc);
     }
 }

@@ -162,6 +162,8 @@ struct GemmParams {
     // epilogue warps in two groups taking alternate tiles (set by the launcher when every CTA
     // has many tiles; otherwise both groups share each tile by column halves)
     int epi_groups;
+    // K-major B without im2col (MATMUL_T): 1 when B has one batch shared by every batch of A
+    int b_bcast;
 };
 
 // TAP2 (int8 im2col convolutions with exactly 64 input channels): two filter taps per stage,
@@ -681,7 +683,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                 tma_load_3d(sb + j * Cfg::B_MN_BOX_BYTES, &tmB, &full[s], n0 + j * Cfg::B_MN_CHUNK,
                                             kb * Cfg::BK, b);
                         } else {
-                            tma_load_3d(sb, &tmB, &full[s], kb * Cfg::BK, n0, 0);
+                            tma_load_3d(sb, &tmB, &full[s], kb * Cfg::BK, n0, p.b_bcast ? 0 : b);
                         }
                     }
                 }

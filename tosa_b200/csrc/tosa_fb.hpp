@@ -20,7 +20,7 @@ namespace fb {
 enum Op : int {
     OP_AVG_POOL2D = 2, OP_CONV2D = 3, OP_DEPTHWISE_CONV2D = 5, OP_MATMUL = 7, OP_MAX_POOL2D = 8,
     OP_CLAMP = 11, OP_ADD = 15, OP_RESHAPE = 57, OP_TRANSPOSE = 61, OP_RESCALE = 66, OP_CONST = 67,
-    OP_IDENTITY = 68, OP_CONST_SHAPE = 75,
+    OP_IDENTITY = 68, OP_CONST_SHAPE = 75, OP_MATMUL_T = 100,
 };
 
 // Attribute union members (schema/tosa.fbs: the Attribute union repeats the Op order).
