@@ -21,6 +21,7 @@
  *   operator dispatch          src/ops/mod.rs:22-150 (dispatch)
  *   CONV2D                     src/ops/conv.rs:502-508 (eval_conv2d), :398-500
  *   DEPTHWISE_CONV2D           src/ops/conv.rs:518-524
+ *   TRANSPOSE_CONV2D           src/ops/conv.rs:526-532 (eval_transpose_conv2d), :286-371
  *   MATMUL                     src/ops/matmul.rs:176-178 (eval_matmul), :98-174
  *   MATMUL_T                   src/ops/matmul.rs:180-182 (eval_matmul_t), :98-174
  *   RESCALE                    src/ops/type_conv.rs:111-191 (eval_rescale)
@@ -213,6 +214,22 @@ TB_API void tb_conv2d_plan_destroy(tb_conv2d_plan *plan);
 TB_API tb_status tb_conv2d(tb_context *ctx, const tb_conv2d_desc *desc, const tb_rescale_attr *rescale,
                            const void *input, const void *weight, const void *bias, void *out, void *stream);
 TB_API tb_status tb_depthwise_conv2d(tb_context *ctx, const tb_conv2d_desc *desc, const tb_rescale_attr *rescale,
+                                     const void *input, const void *weight, const void *bias, void *out,
+                                     void *stream);
+
+/* ---- TRANSPOSE_CONV2D (src/ops/conv.rs:526-532, Transpose :286-371) --------
+ * The tb_conv2d_desc fields keep their CONV2D meaning (weight OHWI [oc,kh,kw,ic],
+ * the types of standard_types conv.rs:388-396) except that pad = out_pad
+ * [top, bottom, left, right], each > -kernel size (may be negative), and
+ * dilation is ignored; output [n, (ih-1)*stride_y + pad[0] + pad[1] + kh,
+ * (iw-1)*stride_x + pad[2] + pad[3] + kw, oc]. INT8 with stride 1 runs as the
+ * CONV2D with reversed taps on the tensor cores (exact: integer sums); every
+ * other case runs the direct gather kernel in the reference's order. Runs and
+ * is destroyed with tb_conv2d_plan_run / tb_conv2d_plan_destroy. */
+TB_API tb_status tb_transpose_conv2d_plan_create(tb_context *ctx, const tb_conv2d_desc *desc, const void *weight,
+                                                 const void *bias, const tb_rescale_attr *rescale,
+                                                 tb_conv2d_plan **out);
+TB_API tb_status tb_transpose_conv2d(tb_context *ctx, const tb_conv2d_desc *desc, const tb_rescale_attr *rescale,
                                      const void *input, const void *weight, const void *bias, void *out,
                                      void *stream);
 

@@ -12,7 +12,8 @@ It restates the reference interpreter (tosa-interp) on the CPU:
   conformance and network fixtures use.
 
 Parity is pinned: tests/test_oracle_golden.py requires this oracle to match
-every checked-in conformance vector of CONV2D, DEPTHWISE_CONV2D, MATMUL, MATMUL_T,
+every checked-in conformance vector of CONV2D, DEPTHWISE_CONV2D, TRANSPOSE_CONV2D,
+MATMUL, MATMUL_T,
 RESCALE, AVG_POOL2D, MAX_POOL2D and CLAMP bit for bit, to reject every
 ERROR_IF case, and to reproduce the network fixtures.
 
@@ -349,9 +350,10 @@ def standard_types(i, w, acc, out):
     return False
 
 
-def eval_conv(st: State, op, depthwise: bool):
-    """conv.rs:398-500 (eval_conv) with ConvNd::new :107-139 / Depthwise::new :201-223."""
-    name = "DEPTHWISE_CONV2D" if depthwise else "CONV2D"
+def eval_conv(st: State, op, depthwise: bool, transpose: bool = False):
+    """conv.rs:398-500 (eval_conv) with ConvNd::new :107-139 / Depthwise::new :201-223 /
+    Transpose::new :286-329."""
+    name = "TRANSPOSE_CONV2D" if transpose else "DEPTHWISE_CONV2D" if depthwise else "CONV2D"
     a = op.attr
     if not a:
         raise graph_error(name, "missing attribute")
@@ -364,9 +366,16 @@ def eval_conv(st: State, op, depthwise: bool):
     expect_rank(name, "bias", bias, 1)
     expect_rank(name, "input", x, 4)
     expect_rank(name, "weight", w, 4)
-    pad, stride, dil = a["pad"], a["stride"], a["dilation"]
-    check_conv_attributes(name, 2, pad, stride, dil)
     n, ih, iw, ic = x.shape
+    if transpose:
+        pad, stride, dil = a["out_pad"], a["stride"], [1, 1]
+        if len(pad) != 4 or len(stride) != 2:
+            raise graph_error(name, "out_pad must have 4 elements and stride 2")
+        if any(v < 1 for v in stride):
+            raise graph_error(name, "stride must be at least 1")
+    else:
+        pad, stride, dil = a["pad"], a["stride"], a["dilation"]
+        check_conv_attributes(name, 2, pad, stride, dil)
     if depthwise:
         kh, kw, kc, m = w.shape
         if kc != ic:
@@ -377,8 +386,17 @@ def eval_conv(st: State, op, depthwise: bool):
         m = 1
         if kc != ic:
             raise OracleError("ShapeMismatch", f"{name}: weight input channels {kc} != input channels {ic}")
-    oh = output_extent(name, ih, pad[0], pad[1], kh, dil[0], stride[0])
-    ow = output_extent(name, iw, pad[2], pad[3], kw, dil[1], stride[1])
+    if transpose:
+        for i, p_ in enumerate(pad):
+            if p_ <= -(kh if i < 2 else kw):
+                raise graph_error(name, "out_pad must be greater than -kernel size")
+        oh = (ih - 1) * stride[0] + pad[0] + pad[1] + kh
+        ow = (iw - 1) * stride[1] + pad[2] + pad[3] + kw
+        if oh < 1 or ow < 1:
+            raise graph_error(name, "output size must be positive")
+    else:
+        oh = output_extent(name, ih, pad[0], pad[1], kh, dil[0], stride[0])
+        ow = output_extent(name, iw, pad[2], pad[3], kw, dil[1], stride[1])
     out_shape = [n, oh, ow, oc]
     bc = bias.shape[0]
     if bc != oc and bc != 1:
@@ -387,7 +405,7 @@ def eval_conv(st: State, op, depthwise: bool):
     declared = st.declared(name, op.outputs[0], out_shape)
     if declared is not None and declared != out_t:
         raise OracleError("DTypeMismatch", f"{name}: output dtype does not match bias dtype")
-    types_ok = standard_types if depthwise else conv2d_types
+    types_ok = standard_types if depthwise or transpose else conv2d_types
     if not types_ok(in_t, w_t, acc_t, out_t):
         raise OracleError("DTypeMismatch", f"{name}: unsupported types")
     if izp.dtype != in_t or wzp.dtype != w_t:
@@ -408,7 +426,7 @@ def eval_conv(st: State, op, depthwise: bool):
             raise graph_error(name, "weight zero point must be zero for non-int8 weight")
         xi, wi, bi = _i64(x.values), _i64(w.values), _i64(bias.values)
         out = np.zeros(count, dtype=np.int64)
-        fn = L.orc_depthwise_int if depthwise else L.orc_conv2d_int
+        fn = L.orc_transpose_conv2d_int if transpose else L.orc_depthwise_int if depthwise else L.orc_conv2d_int
         fn(ctypes.byref(g), _p(xi), _p(wi), _p(bi), ctypes.c_int64(bc), ctypes.c_int64(zx),
            ctypes.c_int64(zw), ctypes.c_int(acc_t == D["INT48"]), _p(out))
         return T(out_t, out_shape, out)
@@ -417,7 +435,8 @@ def eval_conv(st: State, op, depthwise: bool):
         raise graph_error(name, "zero points must be zero for floating-point operands")
     xf, wf, bf = _f32(x.values), _f32(w.values), _f32(bias.values)
     out = np.zeros(count, dtype=np.float32)
-    fn = L.orc_depthwise_float if depthwise else L.orc_conv2d_float
+    fn = (L.orc_transpose_conv2d_float if transpose else L.orc_depthwise_float if depthwise
+          else L.orc_conv2d_float)
     fn(ctypes.byref(g), _p(xf), _p(wf), _p(bf), ctypes.c_int64(bc), ctypes.c_float(zx),
        ctypes.c_float(zw), ctypes.c_int(acc_t), ctypes.c_int(out_t), _p(out))
     return T(out_t, out_shape, out)
@@ -809,6 +828,7 @@ EVAL = {
     "CONST": eval_const, "CONST_SHAPE": eval_const, "IDENTITY": eval_identity,
     "CONV2D": lambda s, o: eval_conv(s, o, False),
     "DEPTHWISE_CONV2D": lambda s, o: eval_conv(s, o, True),
+    "TRANSPOSE_CONV2D": lambda s, o: eval_conv(s, o, False, transpose=True),
     "MATMUL": eval_matmul, "MATMUL_T": eval_matmul_t, "RESCALE": eval_rescale, "AVG_POOL2D": eval_avg_pool,
     "MAX_POOL2D": eval_max_pool, "CLAMP": eval_clamp, "ADD": eval_add,
     "RESHAPE": eval_reshape, "TRANSPOSE": eval_transpose,

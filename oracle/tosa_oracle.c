@@ -333,6 +333,79 @@ void orc_depthwise_float(const orc_conv_geom *g, const float *input, const float
 }
 
 /* ---------------------------------------------------------------------------
+ * TRANSPOSE_CONV2D (src/ops/conv.rs:337-371 Transpose::accumulate, gather form):
+ * output (oy, ox) reads input ((oy - out_pad_top - ky) / stride_y, ...) where
+ * the division is exact and in range; taps (ky, kx) row-major, ic innermost.
+ * g->pad[0] / g->pad[2] hold out_pad_top / out_pad_left (may be negative);
+ * the weight is OHWI as for CONV2D.
+ * ------------------------------------------------------------------------- */
+#define TCONV_LOOP(G, ACC_T, ZERO, MAC, EMIT)                                               \
+    do {                                                                                     \
+        const orc_conv_geom *g_ = (G);                                                       \
+        int64_t sy_ = g_->stride[0], sx_ = g_->stride[1];                                    \
+        for (int64_t b = 0; b < g_->n; ++b)                                                  \
+            for (int64_t oy = 0; oy < g_->oh; ++oy)                                          \
+                for (int64_t ox = 0; ox < g_->ow; ++ox)                                      \
+                    for (int64_t oc = 0; oc < g_->oc; ++oc) {                                \
+                        ACC_T acc = ZERO;                                                    \
+                        for (int64_t ky = 0; ky < g_->kh; ++ky) {                            \
+                            int64_t y = oy - g_->pad[0] - ky;                                \
+                            if (y < 0 || y >= g_->ih * sy_ || y % sy_ != 0) continue;        \
+                            for (int64_t kx = 0; kx < g_->kw; ++kx) {                        \
+                                int64_t x = ox - g_->pad[2] - kx;                            \
+                                if (x < 0 || x >= g_->iw * sx_ || x % sx_ != 0) continue;    \
+                                int64_t ib = ((b * g_->ih + y / sy_) * g_->iw + x / sx_) * g_->ic; \
+                                int64_t wb = ((oc * g_->kh + ky) * g_->kw + kx) * g_->ic;    \
+                                for (int64_t c = 0; c < g_->ic; ++c) { MAC(ib + c, wb + c); } \
+                            }                                                                \
+                        }                                                                    \
+                        int64_t oi = ((b * g_->oh + oy) * g_->ow + ox) * g_->oc + oc;       \
+                        EMIT(oi, oc);                                                        \
+                    }                                                                        \
+    } while (0)
+
+void orc_transpose_conv2d_int(const orc_conv_geom *g, const int64_t *input, const int64_t *weight,
+                              const int64_t *bias, int64_t bias_len, int64_t input_zp, int64_t weight_zp,
+                              int acc_i48, int64_t *out) {
+    if (!acc_i48) {
+        int32_t *in = sub_zp_i32(input, g->n * g->ih * g->iw * g->ic, input_zp);
+        int32_t *w = sub_zp_i32(weight, g->oc * g->kh * g->kw * g->ic, weight_zp);
+#define MAC_I32(i, j) acc = (int32_t)((uint32_t)acc + (uint32_t)in[i] * (uint32_t)w[j])
+#define EMIT_I32(o, oc) out[o] = (int32_t)((uint32_t)acc + (uint32_t)(int32_t)bias[bias_len == 1 ? 0 : oc])
+        TCONV_LOOP(g, int32_t, 0, MAC_I32, EMIT_I32);
+#undef MAC_I32
+#undef EMIT_I32
+        free(in);
+        free(w);
+        return;
+    }
+#define MAC_I64(i, j) acc = (int64_t)((uint64_t)acc + (uint64_t)(input[i] - input_zp) * (uint64_t)(weight[j] - weight_zp))
+#define EMIT_I64(o, oc) out[o] = clamp48((int64_t)((uint64_t)acc + (uint64_t)bias[bias_len == 1 ? 0 : oc]))
+    TCONV_LOOP(g, int64_t, 0, MAC_I64, EMIT_I64);
+#undef MAC_I64
+#undef EMIT_I64
+}
+
+void orc_transpose_conv2d_float(const orc_conv_geom *g, const float *input, const float *weight,
+                                const float *bias, int64_t bias_len, float input_zp, float weight_zp,
+                                int acc_type, int out_type, float *out) {
+    int64_t in_count = g->n * g->ih * g->iw * g->ic;
+    int64_t w_count = g->oc * g->kh * g->kw * g->ic;
+    float *in = (float *)malloc((size_t)(in_count ? in_count : 1) * sizeof(float));
+    float *w = (float *)malloc((size_t)(w_count ? w_count : 1) * sizeof(float));
+    for (int64_t i = 0; i < in_count; ++i) in[i] = input[i] - input_zp;
+    for (int64_t i = 0; i < w_count; ++i) w[i] = weight[i] - weight_zp;
+    int kind = acc_kind_for(acc_type);
+#define MAC_F(i, j) acc = fmac(kind, acc, in[i], w[j])
+#define EMIT_F(o, oc) out[o] = orc_round_to(out_type, orc_round_to(out_type, acc) + bias[bias_len == 1 ? 0 : oc])
+    TCONV_LOOP(g, float, 0.0f, MAC_F, EMIT_F);
+#undef MAC_F
+#undef EMIT_F
+    free(in);
+    free(w);
+}
+
+/* ---------------------------------------------------------------------------
  * MATMUL (src/ops/matmul.rs:75-95 Dims::run, :137-171 operand handling)
  * ------------------------------------------------------------------------- */
 

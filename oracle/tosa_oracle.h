@@ -95,6 +95,15 @@ void orc_depthwise_float(const orc_conv_geom *g, const float *input, const float
                          const float *bias, int64_t bias_len, float input_zp, float weight_zp,
                          int acc_type, int out_type, float *out);
 
+/* TRANSPOSE_CONV2D, Transpose::accumulate conv.rs:337-371 (gather form); the
+ * geometry's pad[0] / pad[2] are out_pad_top / out_pad_left, weight OHWI. */
+void orc_transpose_conv2d_int(const orc_conv_geom *g, const int64_t *input, const int64_t *weight,
+                              const int64_t *bias, int64_t bias_len, int64_t input_zp, int64_t weight_zp,
+                              int acc_i48, int64_t *out);
+void orc_transpose_conv2d_float(const orc_conv_geom *g, const float *input, const float *weight,
+                                const float *bias, int64_t bias_len, float input_zp, float weight_zp,
+                                int acc_type, int out_type, float *out);
+
 /* MATMUL, matmul.rs:80-95 + :137-171. a [N,H,C], b [N,C,W]. */
 void orc_matmul_int(int64_t n, int64_t h, int64_t c, int64_t w, const int64_t *a, const int64_t *b,
                     int64_t a_zp, int64_t b_zp, int out_i48, int64_t *out);

@@ -1,7 +1,7 @@
 """The graph runner on the GPU, against the reference's own fixtures.
 
 Every conformance case the reference ships for the operators on this path
-(tests/golden/*.zip: CONV2D, DEPTHWISE_CONV2D, MATMUL, MATMUL_T, RESCALE, AVG_POOL2D,
+(tests/golden/*.zip: CONV2D, DEPTHWISE_CONV2D, TRANSPOSE_CONV2D, MATMUL, MATMUL_T, RESCALE, AVG_POOL2D,
 MAX_POOL2D, CLAMP, and the network graphs) runs end to end through
 ``run_graph`` -- the .tosa flatbuffer parsed in C++, constants uploaded, the
 operator executed by the CUDA kernels -- and its result is compared bit for
@@ -29,7 +29,7 @@ from tosa_b200 import _lib as L  # noqa: E402
 from tosa_b200 import interpreter as I  # noqa: E402
 
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
-FAMILIES = ["conv2d", "depthwise_conv2d", "matmul", "matmul_t", "rescale", "avg_pool2d", "max_pool2d", "clamp", "networks"]
+FAMILIES = ["conv2d", "depthwise_conv2d", "transpose_conv2d", "matmul", "matmul_t", "rescale", "avg_pool2d", "max_pool2d", "clamp", "networks"]
 # cases per family the runner executes (the rest are declined as not accelerated or are ERROR_IF cases)
 _RESULTS = {}
 
@@ -117,7 +117,7 @@ def test_fixture_through_runner(ctx, fam, case):
     _RESULTS[fam]["exact"] += 1
 
 
-TOLERANT = {"conv2d", "depthwise_conv2d", "matmul", "matmul_t"}
+TOLERANT = {"conv2d", "depthwise_conv2d", "transpose_conv2d", "matmul", "matmul_t"}
 
 
 def _ulp(x, dtype):

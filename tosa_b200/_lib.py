@@ -123,6 +123,8 @@ SIGNATURES = [
     ("tb_conv2d_plan_destroy", None, [_V]),
     ("tb_conv2d", _I, [_V, _P(Conv2dDesc), _P(RescaleAttr), _V, _V, _V, _V, _V]),
     ("tb_depthwise_conv2d", _I, [_V, _P(Conv2dDesc), _P(RescaleAttr), _V, _V, _V, _V, _V]),
+    ("tb_transpose_conv2d_plan_create", _I, [_V, _P(Conv2dDesc), _V, _V, _P(RescaleAttr), _P(_V)]),
+    ("tb_transpose_conv2d", _I, [_V, _P(Conv2dDesc), _P(RescaleAttr), _V, _V, _V, _V, _V]),
     ("tb_rescale", _I, [_V, _P(RescaleAttr), _I, _V, _L, _V, _V]),
     ("tb_clamp", _I, [_V, _I, _V, _L, _L, _L, ctypes.c_float, ctypes.c_float, _I, _V, _V]),
     ("tb_add", _I, [_V, _I, _V, _V, _L, _V, _V]),

@@ -816,6 +816,8 @@ struct tb_conv2d_plan {
     float* d_fbias = nullptr;  // float bias widened to f32
     // path 8: im2col rows + a 1x1 tensor-core convolution over them
     tb_conv2d_plan* inner = nullptr;
+    bool transpose = false;         // TRANSPOSE_CONV2D: d.pad holds out_pad; path 10 runs `inner` (stride 1,
+                                    // int8) over the tap-reversed weights in d_wpad, else a direct kernel
     int8_t* d_rows = nullptr;       // [n*oh*ow][kp]
     int8_t* d_wpad = nullptr;       // [oc][kp]
     int kp = 0;
@@ -1200,12 +1202,97 @@ extern "C" TB_API tb_status tb_depthwise_conv2d_plan_create(tb_context* ctx, con
     return conv_plan_create(ctx, d, weight, bias, rescale, true, out);
 }
 
+extern "C" TB_API tb_status tb_transpose_conv2d_plan_create(tb_context* ctx, const tb_conv2d_desc* d,
+                                                            const void* weight, const void* bias,
+                                                            const tb_rescale_attr* rescale, tb_conv2d_plan** out) {
+    if (!ctx || !d || !out || !weight || !bias) return fail(TB_ERR_INVALID_ARGUMENT, "null argument");
+    *out = nullptr;
+    TB_CUDA(cudaSetDevice(ctx->device));
+    const char* op = "TRANSPOSE_CONV2D";
+    // Transpose::new (src/ops/conv.rs:286-329)
+    if (d->stride[0] < 1 || d->stride[1] < 1) return fail(TB_ERR_GRAPH, "%s: stride must be at least 1", op);
+    for (int i = 0; i < 4; ++i)
+        if (d->pad[i] <= -(i < 2 ? d->kh : d->kw))
+            return fail(TB_ERR_GRAPH, "%s: out_pad must be greater than -kernel size", op);
+    const long long oh = (static_cast<long long>(d->ih) - 1) * d->stride[0] + d->pad[0] + d->pad[1] + d->kh;
+    const long long ow = (static_cast<long long>(d->iw) - 1) * d->stride[1] + d->pad[2] + d->pad[3] + d->kw;
+    if (oh < 1 || ow < 1) return fail(TB_ERR_GRAPH, "%s: output size %lldx%lld must be positive", op, oh, ow);
+    if (oh > INT32_MAX || ow > INT32_MAX) return fail(TB_ERR_NOT_ACCELERATED, "%s: output above int32", op);
+    if (d->bias_len != d->oc && d->bias_len != 1)
+        return fail(TB_ERR_SHAPE_MISMATCH, "%s: bias channels %d must be 1 or match output channels %d", op,
+                    d->bias_len, d->oc);
+    // standard_types (conv.rs:388-396), the table conv_types_valid applies to depthwise
+    const int it = d->in_dtype, wt = d->w_dtype, at = d->acc_dtype, ot = d->out_dtype;
+    if (!conv_types_valid(true, it, wt, at, ot))
+        return fail(TB_ERR_DTYPE_MISMATCH, "%s: unsupported types input=%d weight=%d acc=%d output=%d", op, it, wt, at,
+                    ot);
+    const bool int8 = it == TB_DT_INT8 && at == TB_DT_INT32;
+    const bool int16 = it == TB_DT_INT16;
+    if (int8 || int16) {
+        if (d->input_zp != 0 && it != TB_DT_INT8)
+            return fail(TB_ERR_GRAPH, "%s: input zero point must be zero for non-int8 input", op);
+        if (d->weight_zp != 0 && wt != TB_DT_INT8)
+            return fail(TB_ERR_GRAPH, "%s: weight zero point must be zero for non-int8 weight", op);
+    } else if (d->input_zp != 0 || d->weight_zp != 0) {
+        return fail(TB_ERR_GRAPH, "%s: zero points must be zero for floating-point operands", op);
+    }
+    if (rescale && !int8) return fail(TB_ERR_DTYPE_MISMATCH, "%s: RESCALE needs an int32 result", op);
+    tb_conv2d_plan* p = new tb_conv2d_plan;
+    p->ctx = ctx;
+    p->d = *d;
+    p->transpose = true;
+    p->oh = static_cast<int>(oh);
+    p->ow = static_cast<int>(ow);
+    p->weight = weight;
+    p->bias = bias;
+    auto bail = [&](tb_status s) {
+        tb_conv2d_plan_destroy(p);
+        return s;
+    };
+    // (the CONV2D's padding k - 1 + out_pad stays inside the im2col corner range of its TMA path)
+    const bool small_pad = d->pad[0] <= 100 && d->pad[1] <= 100 && d->pad[2] <= 100 && d->pad[3] <= 100 &&
+                           d->kh <= 28 && d->kw <= 28;
+    if (int8 && small_pad && d->stride[0] == 1 && d->stride[1] == 1) {
+        // stride 1: out[oy] = sum_ky x[oy - out_pad_top - ky] w[ky] is the CONV2D with the taps
+        // reversed and padding k - 1 + out_pad on each side (all >= 0: out_pad > -k)
+        const size_t wbytes = static_cast<size_t>(d->oc) * d->kh * d->kw * d->ic;
+        if (wbytes) {
+            if (cudaMalloc(&p->d_wpad, wbytes) != cudaSuccess) return bail(fail(TB_ERR_CUDA, "%s: weight alloc failed", op));
+            flip_taps_i8<<<grid_for(ctx, static_cast<long long>(wbytes)), 256>>>(
+                d->oc, d->kh, d->kw, d->ic, static_cast<const int8_t*>(weight), p->d_wpad);
+            TB_LAUNCHED(ctx);
+            if (cudaStreamSynchronize(nullptr) != cudaSuccess) return bail(fail(TB_ERR_CUDA, "%s: weight flip failed", op));
+        }
+        tb_conv2d_desc cd = *d;
+        cd.pad[0] = d->kh - 1 + d->pad[0];
+        cd.pad[1] = d->kh - 1 + d->pad[1];
+        cd.pad[2] = d->kw - 1 + d->pad[2];
+        cd.pad[3] = d->kw - 1 + d->pad[3];
+        cd.dilation[0] = cd.dilation[1] = 1;
+        tb_status s = conv_plan_create(ctx, &cd, p->d_wpad ? static_cast<const void*>(p->d_wpad) : weight, bias,
+                                       rescale, false, &p->inner);
+        if (s != TB_OK) return bail(s);
+        p->path = 10;
+        *out = p;
+        return TB_OK;
+    }
+    if (rescale) {
+        tb_status s = make_rescale_plan(ctx, rescale, TB_DT_INT32, d->oc, &p->rs);
+        if (s != TB_OK) return bail(s);
+    }
+    p->path = int16 ? 7 : int8 ? 2 : 3;  // direct kernels in the reference's gather order
+    *out = p;
+    return TB_OK;
+}
+
 extern "C" TB_API tb_status tb_conv2d_plan_run(tb_conv2d_plan* p, const void* input, void* out, void* stream_) {
     if (!p || !input || !out) return fail(TB_ERR_INVALID_ARGUMENT, "null argument");
     tb_context* ctx = p->ctx;
     cudaStream_t st = static_cast<cudaStream_t>(stream_);
     const tb_conv2d_desc& d = p->d;
+    if (p->path == 10) return tb_conv2d_plan_run(p->inner, input, out, stream_);
     ConvGeomDev g;
+    g.tr = p->transpose ? 1 : 0;
     g.n = d.n; g.ih = d.ih; g.iw = d.iw; g.ic = d.ic; g.oc = d.oc; g.kh = d.kh; g.kw = d.kw;
     g.oh = p->oh; g.ow = p->ow; g.m = d.m;
     g.pad_t = d.pad[0]; g.pad_l = d.pad[2]; g.sh = d.stride[0]; g.sw = d.stride[1];
@@ -1435,6 +1522,17 @@ extern "C" TB_API void tb_conv2d_plan_destroy(tb_conv2d_plan* p) {
     if (p->d_fbias) cudaFree(p->d_fbias);
     if (p->d_dw) cudaFree(p->d_dw);
     delete p;
+}
+
+extern "C" TB_API tb_status tb_transpose_conv2d(tb_context* ctx, const tb_conv2d_desc* d,
+                                                const tb_rescale_attr* rescale, const void* input, const void* weight,
+                                                const void* bias, void* out, void* stream) {
+    tb_conv2d_plan* p = nullptr;
+    TB_TRY(tb_transpose_conv2d_plan_create(ctx, d, weight, bias, rescale, &p));
+    tb_status s = tb_conv2d_plan_run(p, input, out, stream);
+    cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+    tb_conv2d_plan_destroy(p);
+    return s;
 }
 
 extern "C" TB_API tb_status tb_conv2d(tb_context* ctx, const tb_conv2d_desc* d, const tb_rescale_attr* rescale,

@@ -66,6 +66,7 @@ const char* op_name(int op) {
     case fb::OP_DEPTHWISE_CONV2D: return "DEPTHWISE_CONV2D";
     case fb::OP_MATMUL: return "MATMUL";
     case fb::OP_MATMUL_T: return "MATMUL_T";
+    case fb::OP_TRANSPOSE_CONV2D: return "TRANSPOSE_CONV2D";
     case fb::OP_MAX_POOL2D: return "MAX_POOL2D";
     case fb::OP_CLAMP: return "CLAMP";
     case fb::OP_ADD: return "ADD";
@@ -142,6 +143,7 @@ struct Step {
     std::vector<int> group;         // fused op indices led by this step (RESCALE, CLAMP / chain members)
     // contraction
     bool depthwise = false;
+    bool transpose = false;         // TRANSPOSE_CONV2D (cdesc.pad holds out_pad)
     tb_conv2d_desc cdesc{};
     tb_matmul_desc mdesc{};
     int mt_batch = 0;               // MATMUL_T: batch of b [mt_batch, w, c] (n or 1); 0 for MATMUL
@@ -505,8 +507,10 @@ class Compiler {
         s.out = {y};
     }
 
-    void c_conv(const fb::Operator& o, Step& s, bool depthwise) {
-        const char* op = depthwise ? "DEPTHWISE_CONV2D" : "CONV2D";
+    // CONV2D, DEPTHWISE_CONV2D, and TRANSPOSE_CONV2D (transpose: attribute out_pad in a.pad,
+    // no dilation; Transpose::new src/ops/conv.rs:286-329)
+    void c_conv(const fb::Operator& o, Step& s, bool depthwise, bool transpose = false) {
+        const char* op = transpose ? "TRANSPOSE_CONV2D" : depthwise ? "DEPTHWISE_CONV2D" : "CONV2D";
         if (o.attr.type != o.op) raise(TB_ERR_GRAPH, "%s: missing attribute", op);
         expect_operands(o, op, 5, 1);
         const int x = get(o.inputs[0]), w = get(o.inputs[1]), b = get(o.inputs[2]);
@@ -516,12 +520,19 @@ class Compiler {
         expect_rank(op, "bias", B, 1);
         expect_rank(op, "input", X, 4);
         expect_rank(op, "weight", W, 4);
-        const Attr& a = o.attr;
-        if (a.pad.size() != 4 || a.stride.size() != 2 || a.dilation.size() != 2)
-            raise(TB_ERR_GRAPH, "%s: pad must have 4 elements, stride and dilation 2", op);
-        for (int p : a.pad) if (p < 0) raise(TB_ERR_GRAPH, "%s: pad must be non-negative", op);
-        for (int v : a.stride) if (v < 1) raise(TB_ERR_GRAPH, "%s: stride must be at least 1", op);
-        for (int v : a.dilation) if (v < 1) raise(TB_ERR_GRAPH, "%s: dilation must be at least 1", op);
+        Attr a = o.attr;
+        if (transpose) {
+            if (a.pad.size() != 4 || a.stride.size() != 2)
+                raise(TB_ERR_GRAPH, "%s: out_pad must have 4 elements and stride 2", op);
+            for (int v : a.stride) if (v < 1) raise(TB_ERR_GRAPH, "%s: stride must be at least 1", op);
+            a.dilation = {1, 1};
+        } else {
+            if (a.pad.size() != 4 || a.stride.size() != 2 || a.dilation.size() != 2)
+                raise(TB_ERR_GRAPH, "%s: pad must have 4 elements, stride and dilation 2", op);
+            for (int p : a.pad) if (p < 0) raise(TB_ERR_GRAPH, "%s: pad must be non-negative", op);
+            for (int v : a.stride) if (v < 1) raise(TB_ERR_GRAPH, "%s: stride must be at least 1", op);
+            for (int v : a.dilation) if (v < 1) raise(TB_ERR_GRAPH, "%s: dilation must be at least 1", op);
+        }
         const int64_t ic = X.shape[3];
         const int64_t kic = depthwise ? W.shape[2] : W.shape[3];
         if (kic != ic)
@@ -535,8 +546,18 @@ class Compiler {
             if (out < 1) raise(TB_ERR_GRAPH, "%s: output dimension %lld must be positive", op, static_cast<long long>(out));
             return out;
         };
-        const int64_t oh = extent(X.shape[1], a.pad[0], a.pad[1], kh, a.dilation[0], a.stride[0]);
-        const int64_t ow = extent(X.shape[2], a.pad[2], a.pad[3], kw, a.dilation[1], a.stride[1]);
+        int64_t oh, ow;
+        if (transpose) {
+            for (int i = 0; i < 4; ++i)
+                if (a.pad[i] <= -(i < 2 ? kh : kw))
+                    raise(TB_ERR_GRAPH, "%s: out_pad must be greater than -kernel size", op);
+            oh = (X.shape[1] - 1) * a.stride[0] + a.pad[0] + a.pad[1] + kh;
+            ow = (X.shape[2] - 1) * a.stride[1] + a.pad[2] + a.pad[3] + kw;
+            if (oh < 1 || ow < 1) raise(TB_ERR_GRAPH, "%s: output size must be positive", op);
+        } else {
+            oh = extent(X.shape[1], a.pad[0], a.pad[1], kh, a.dilation[0], a.stride[0]);
+            ow = extent(X.shape[2], a.pad[2], a.pad[3], kw, a.dilation[1], a.stride[1]);
+        }
         const int64_t m = depthwise ? W.shape[3] : 1;
         const int64_t oc = depthwise ? ic * m : W.shape[0];
         const int64_t bc = B.shape[0];
@@ -580,6 +601,7 @@ class Compiler {
             d.weight_zp = static_cast<int32_t>(wzp);
         }
         s.depthwise = depthwise;
+        s.transpose = transpose;
         s.kind = K_CONV;
         s.in = {x, w, b, get(o.inputs[3]), get(o.inputs[4])};
         s.out = {make_out(o.outputs[0], B.dtype, out_shape)};
@@ -872,6 +894,7 @@ class Compiler {
         case fb::OP_TRANSPOSE: c_transpose(o, s); break;
         case fb::OP_CONV2D: c_conv(o, s, false); break;
         case fb::OP_DEPTHWISE_CONV2D: c_conv(o, s, true); break;
+        case fb::OP_TRANSPOSE_CONV2D: c_conv(o, s, false, true); break;
         case fb::OP_MATMUL: c_matmul(o, s, false); break;
         case fb::OP_MATMUL_T: c_matmul(o, s, true); break;
         case fb::OP_RESCALE: c_rescale(o, s); break;
@@ -1140,7 +1163,10 @@ tb_status do_compile(tb_graph* G) {
         case K_CONV: {
             const Tensor& W = G->tensors[s.in[1]];
             const Tensor& B = G->tensors[s.in[2]];
-            if (s.depthwise)
+            if (s.transpose)
+                st = tb_transpose_conv2d_plan_create(ctx, &s.cdesc, W.dev, B.dev, s.has_rescale ? &s.rattr : nullptr,
+                                                     &s.conv);
+            else if (s.depthwise)
                 st = tb_depthwise_conv2d_plan_create(ctx, &s.cdesc, W.dev, B.dev, s.has_rescale ? &s.rattr : nullptr,
                                                      &s.conv);
             else

@@ -21,7 +21,37 @@ namespace tb {
 struct ConvGeomDev {
     int n, ih, iw, ic, oc, kh, kw, oh, ow, m;
     int pad_t, pad_l, sh, sw, dh, dw;
+    int tr;  // TRANSPOSE_CONV2D: pad_t / pad_l are out_pad_top / out_pad_left
 };
+
+// Input row (or column) that output position o reads through tap k, or -1 when the tap
+// reads nothing. CONV2D: o*s + k*d - pad inside [0, in) (src/ops/conv.rs:160-170).
+// TRANSPOSE_CONV2D (tr; conv.rs:345-362, gather form): (o - out_pad - k) / s when the
+// division is exact and the quotient lies inside [0, in).
+__device__ __forceinline__ int tap_src(int o, int k, int s, int d, int pad, int in, int tr) {
+    if (tr) {
+        const int v = o - pad - k;
+        return (v < 0 || v >= in * s || v % s != 0) ? -1 : v / s;
+    }
+    const int v = o * s + k * d - pad;
+    return (v < 0 || v >= in) ? -1 : v;
+}
+
+// TRANSPOSE_CONV2D with stride 1 as a CONV2D: weights [oc][kh][kw][ic] with the taps
+// reversed in both spatial dimensions (one byte per value: INT8, or INT4 held in bytes).
+__global__ void flip_taps_i8(int oc, int kh, int kw, int ic, const int8_t* __restrict__ w, int8_t* __restrict__ out) {
+    const long long total = static_cast<long long>(oc) * kh * kw * ic;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int c = static_cast<int>(i % ic);
+        long long r = i / ic;
+        const int kx = static_cast<int>(r % kw);
+        r /= kw;
+        const int ky = static_cast<int>(r % kh);
+        const long long o = r / kh;
+        out[i] = w[((o * kh + (kh - 1 - ky)) * kw + (kw - 1 - kx)) * ic + c];
+    }
+}
 
 // Integer result of a contraction -> optional RESCALE -> store.
 struct IntEpiDev {
@@ -91,11 +121,11 @@ __global__ void conv2d_direct_int(ConvGeomDev g, const int8_t* __restrict__ x, c
         const int b = static_cast<int>(r / g.oh);
         uint32_t acc = 0;
         for (int ky = 0; ky < g.kh; ++ky) {
-            const int y = oy * g.sh + ky * g.dh - g.pad_t;
-            if (y < 0 || y >= g.ih) continue;
+            const int y = tap_src(oy, ky, g.sh, g.dh, g.pad_t, g.ih, g.tr);
+            if (y < 0) continue;
             for (int kx = 0; kx < g.kw; ++kx) {
-                const int xx = ox * g.sw + kx * g.dw - g.pad_l;
-                if (xx < 0 || xx >= g.iw) continue;
+                const int xx = tap_src(ox, kx, g.sw, g.dw, g.pad_l, g.iw, g.tr);
+                if (xx < 0) continue;
                 const int8_t* xp = x + ((static_cast<long long>(b) * g.ih + y) * g.iw + xx) * g.ic;
                 const int8_t* wp = w + ((static_cast<long long>(oc) * g.kh + ky) * g.kw + kx) * g.ic;
                 for (int c = 0; c < g.ic; ++c)
@@ -123,11 +153,11 @@ __global__ void conv2d_direct_float(ConvGeomDev g, const void* __restrict__ x, c
         const int b = static_cast<int>(r / g.oh);
         float acc = 0.f;
         for (int ky = 0; ky < g.kh; ++ky) {
-            const int y = oy * g.sh + ky * g.dh - g.pad_t;
-            if (y < 0 || y >= g.ih) continue;
+            const int y = tap_src(oy, ky, g.sh, g.dh, g.pad_t, g.ih, g.tr);
+            if (y < 0) continue;
             for (int kx = 0; kx < g.kw; ++kx) {
-                const int xx = ox * g.sw + kx * g.dw - g.pad_l;
-                if (xx < 0 || xx >= g.iw) continue;
+                const int xx = tap_src(ox, kx, g.sw, g.dw, g.pad_l, g.iw, g.tr);
+                if (xx < 0) continue;
                 const long long xb = ((static_cast<long long>(b) * g.ih + y) * g.iw + xx) * g.ic;
                 const long long wb = ((static_cast<long long>(oc) * g.kh + ky) * g.kw + kx) * g.ic;
                 for (int c = 0; c < g.ic; ++c)
@@ -356,11 +386,11 @@ __global__ void conv2d_direct_i48(ConvGeomDev g, const int16_t* __restrict__ x, 
         const int b = static_cast<int>(r / g.oh);
         uint64_t acc = 0;
         for (int ky = 0; ky < g.kh; ++ky) {
-            const int y = oy * g.sh + ky * g.dh - g.pad_t;
-            if (y < 0 || y >= g.ih) continue;
+            const int y = tap_src(oy, ky, g.sh, g.dh, g.pad_t, g.ih, g.tr);
+            if (y < 0) continue;
             for (int kx = 0; kx < g.kw; ++kx) {
-                const int xx = ox * g.sw + kx * g.dw - g.pad_l;
-                if (xx < 0 || xx >= g.iw) continue;
+                const int xx = tap_src(ox, kx, g.sw, g.dw, g.pad_l, g.iw, g.tr);
+                if (xx < 0) continue;
                 const int16_t* xp = x + ((static_cast<long long>(b) * g.ih + y) * g.iw + xx) * g.ic;
                 if (depthwise) {
                     const int c = oc / g.m, mm = oc % g.m;
