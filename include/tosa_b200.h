@@ -20,6 +20,7 @@
  * Reference interfaces replaced (tosa-interp, path:line):
  *   operator dispatch          src/ops/mod.rs:22-150 (dispatch)
  *   CONV2D                     src/ops/conv.rs:502-508 (eval_conv2d), :398-500
+ *   CONV3D                     src/ops/conv.rs:510-516 (eval_conv3d), :107-181
  *   DEPTHWISE_CONV2D           src/ops/conv.rs:518-524
  *   TRANSPOSE_CONV2D           src/ops/conv.rs:526-532 (eval_transpose_conv2d), :286-371
  *   MATMUL                     src/ops/matmul.rs:176-178 (eval_matmul), :98-174
@@ -216,6 +217,26 @@ TB_API tb_status tb_conv2d(tb_context *ctx, const tb_conv2d_desc *desc, const tb
 TB_API tb_status tb_depthwise_conv2d(tb_context *ctx, const tb_conv2d_desc *desc, const tb_rescale_attr *rescale,
                                      const void *input, const void *weight, const void *bias, void *out,
                                      void *stream);
+
+/* ---- CONV3D (src/ops/conv.rs:510-516, ConvNd :107-181 with three dims) ------
+ * input NDHWC [n,id,ih,iw,ic]; weight [oc,kd,kh,kw,ic]; bias [bias_len] (1 or
+ * oc) of out_dtype; pad = [front, back, top, bottom, left, right]; stride and
+ * dilation [d, h, w]. Types: standard_types (conv.rs:388-396), zero points as
+ * CONV2D, optional fused rescale for INT8. Runs the direct kernel in the
+ * reference's order (taps kd, kh, kw row-major, ic innermost). The plan shares
+ * tb_conv2d_plan_run / tb_conv2d_plan_destroy with the 2-D convolutions. */
+typedef struct tb_conv3d_desc {
+    int32_t n, id, ih, iw, ic;
+    int32_t oc, kd, kh, kw;
+    int32_t pad[6], stride[3], dilation[3];
+    int32_t in_dtype, w_dtype, acc_dtype, out_dtype;
+    int32_t input_zp, weight_zp;
+    int32_t bias_len;
+} tb_conv3d_desc;
+TB_API tb_status tb_conv3d_plan_create(tb_context *ctx, const tb_conv3d_desc *desc, const void *weight,
+                                       const void *bias, const tb_rescale_attr *rescale, tb_conv2d_plan **out);
+TB_API tb_status tb_conv3d(tb_context *ctx, const tb_conv3d_desc *desc, const tb_rescale_attr *rescale,
+                           const void *input, const void *weight, const void *bias, void *out, void *stream);
 
 /* ---- TRANSPOSE_CONV2D (src/ops/conv.rs:526-532, Transpose :286-371) --------
  * The tb_conv2d_desc fields keep their CONV2D meaning (weight OHWI [oc,kh,kw,ic],

@@ -12,7 +12,7 @@ It restates the reference interpreter (tosa-interp) on the CPU:
   conformance and network fixtures use.
 
 Parity is pinned: tests/test_oracle_golden.py requires this oracle to match
-every checked-in conformance vector of CONV2D, DEPTHWISE_CONV2D, TRANSPOSE_CONV2D,
+every checked-in conformance vector of CONV2D, CONV3D, DEPTHWISE_CONV2D, TRANSPOSE_CONV2D,
 MATMUL, MATMUL_T,
 RESCALE, AVG_POOL2D, MAX_POOL2D and CLAMP bit for bit, to reject every
 ERROR_IF case, and to reproduce the network fixtures.
@@ -348,6 +348,76 @@ def standard_types(i, w, acc, out):
     if i == w and i in FP8_TYPES:
         return (acc, out) in ((D["FP16"], D["FP16"]), (D["FP32"], D["FP32"]))
     return False
+
+
+class Conv3dGeom(ctypes.Structure):
+    _fields_ = [(k, ctypes.c_int64) for k in ("n", "id", "ih", "iw", "ic", "oc", "kd", "kh", "kw", "od", "oh",
+                                               "ow")] + \
+               [("pad", ctypes.c_int64 * 6), ("stride", ctypes.c_int64 * 3), ("dilation", ctypes.c_int64 * 3)]
+
+
+def eval_conv3d(st: State, op):
+    """conv.rs:510-516 (eval_conv3d): eval_conv :398-500 with ConvNd::new :107-139, dims = 3."""
+    name = "CONV3D"
+    a = op.attr
+    if not a:
+        raise graph_error(name, "missing attribute")
+    expect_operands(op, name, 5, 1)
+    x = st.get(op.inputs[0])
+    w = st.get(op.inputs[1])
+    bias = st.get(op.inputs[2])
+    izp = single_value(name, "input_zp", st.get(op.inputs[3]))
+    wzp = single_value(name, "weight_zp", st.get(op.inputs[4]))
+    expect_rank(name, "bias", bias, 1)
+    expect_rank(name, "input", x, 5)
+    expect_rank(name, "weight", w, 5)
+    pad, stride, dil = a["pad"], a["stride"], a["dilation"]
+    check_conv_attributes(name, 3, pad, stride, dil)
+    n, idd, ih, iw, ic = x.shape
+    oc, kd, kh, kw, kc = w.shape
+    if kc != ic:
+        raise OracleError("ShapeMismatch", f"{name}: weight input channels {kc} != input channels {ic}")
+    sp = [output_extent(name, (idd, ih, iw)[d], pad[2 * d], pad[2 * d + 1], (kd, kh, kw)[d], dil[d], stride[d])
+          for d in range(3)]
+    out_shape = [n] + sp + [oc]
+    bc = bias.shape[0]
+    if bc != oc and bc != 1:
+        raise OracleError("ShapeMismatch", f"{name}: bias channels {bc} must be 1 or {oc}")
+    in_t, w_t, out_t, acc_t = x.dtype, w.dtype, bias.dtype, a["acc_type"]
+    declared = st.declared(name, op.outputs[0], out_shape)
+    if declared is not None and declared != out_t:
+        raise OracleError("DTypeMismatch", f"{name}: output dtype does not match bias dtype")
+    if not standard_types(in_t, w_t, acc_t, out_t):
+        raise OracleError("DTypeMismatch", f"{name}: unsupported types")
+    if izp.dtype != in_t or wzp.dtype != w_t:
+        raise OracleError("DTypeMismatch", f"{name}: zero points must match input/weight dtypes")
+    g = Conv3dGeom(n=n, id=idd, ih=ih, iw=iw, ic=ic, oc=oc, kd=kd, kh=kh, kw=kw, od=sp[0], oh=sp[1], ow=sp[2])
+    for i in range(6):
+        g.pad[i] = pad[i]
+    for i in range(3):
+        g.stride[i] = stride[i]
+        g.dilation[i] = dil[i]
+    L = lib()
+    count = int(np.prod(out_shape))
+    if acc_t in INT_TYPES:
+        zx, zw = int(izp.values[0]), int(wzp.values[0])
+        if zx != 0 and in_t != D["INT8"]:
+            raise graph_error(name, "input zero point must be zero for non-int8 input")
+        if zw != 0 and w_t != D["INT8"]:
+            raise graph_error(name, "weight zero point must be zero for non-int8 weight")
+        out = np.zeros(count, dtype=np.int64)
+        L.orc_conv3d_int(ctypes.byref(g), _p(_i64(x.values)), _p(_i64(w.values)), _p(_i64(bias.values)),
+                         ctypes.c_int64(bc), ctypes.c_int64(zx), ctypes.c_int64(zw),
+                         ctypes.c_int(acc_t == D["INT48"]), _p(out))
+        return T(out_t, out_shape, out)
+    zx, zw = float(izp.values[0]), float(wzp.values[0])
+    if zx != 0.0 or zw != 0.0:
+        raise graph_error(name, "zero points must be zero for floating-point operands")
+    out = np.zeros(count, dtype=np.float32)
+    L.orc_conv3d_float(ctypes.byref(g), _p(_f32(x.values)), _p(_f32(w.values)), _p(_f32(bias.values)),
+                       ctypes.c_int64(bc), ctypes.c_float(zx), ctypes.c_float(zw), ctypes.c_int(acc_t),
+                       ctypes.c_int(out_t), _p(out))
+    return T(out_t, out_shape, out)
 
 
 def eval_conv(st: State, op, depthwise: bool, transpose: bool = False):
@@ -829,6 +899,7 @@ EVAL = {
     "CONV2D": lambda s, o: eval_conv(s, o, False),
     "DEPTHWISE_CONV2D": lambda s, o: eval_conv(s, o, True),
     "TRANSPOSE_CONV2D": lambda s, o: eval_conv(s, o, False, transpose=True),
+    "CONV3D": eval_conv3d,
     "MATMUL": eval_matmul, "MATMUL_T": eval_matmul_t, "RESCALE": eval_rescale, "AVG_POOL2D": eval_avg_pool,
     "MAX_POOL2D": eval_max_pool, "CLAMP": eval_clamp, "ADD": eval_add,
     "RESHAPE": eval_reshape, "TRANSPOSE": eval_transpose,

@@ -333,6 +333,79 @@ void orc_depthwise_float(const orc_conv_geom *g, const float *input, const float
 }
 
 /* ---------------------------------------------------------------------------
+ * CONV3D (src/ops/conv.rs:147-181 ConvNd::accumulate, dims = 3): batch, output
+ * position (d, h, w row-major), oc, then taps (kd, kh, kw row-major), ic
+ * innermost; taps reading outside the input are skipped.
+ * ------------------------------------------------------------------------- */
+#define CONV3D_LOOP(G, ACC_T, ZERO, MAC, EMIT)                                              \
+    do {                                                                                     \
+        const orc_conv3d_geom *g_ = (G);                                                     \
+        for (int64_t b = 0; b < g_->n; ++b)                                                  \
+            for (int64_t oz = 0; oz < g_->od; ++oz)                                          \
+                for (int64_t oy = 0; oy < g_->oh; ++oy)                                      \
+                    for (int64_t ox = 0; ox < g_->ow; ++ox)                                  \
+                        for (int64_t oc = 0; oc < g_->oc; ++oc) {                            \
+                            ACC_T acc = ZERO;                                                \
+                            for (int64_t kz = 0; kz < g_->kd; ++kz) {                        \
+                                int64_t z = oz * g_->stride[0] + kz * g_->dilation[0] - g_->pad[0]; \
+                                if (z < 0 || z >= g_->id) continue;                          \
+                                for (int64_t ky = 0; ky < g_->kh; ++ky) {                    \
+                                    int64_t y = oy * g_->stride[1] + ky * g_->dilation[1] - g_->pad[2]; \
+                                    if (y < 0 || y >= g_->ih) continue;                      \
+                                    for (int64_t kx = 0; kx < g_->kw; ++kx) {                \
+                                        int64_t x = ox * g_->stride[2] + kx * g_->dilation[2] - g_->pad[4]; \
+                                        if (x < 0 || x >= g_->iw) continue;                  \
+                                        int64_t ib = (((b * g_->id + z) * g_->ih + y) * g_->iw + x) * g_->ic; \
+                                        int64_t wb = (((oc * g_->kd + kz) * g_->kh + ky) * g_->kw + kx) * g_->ic; \
+                                        for (int64_t c = 0; c < g_->ic; ++c) { MAC(ib + c, wb + c); } \
+                                    }                                                        \
+                                }                                                            \
+                            }                                                                \
+                            int64_t oi = (((b * g_->od + oz) * g_->oh + oy) * g_->ow + ox) * g_->oc + oc; \
+                            EMIT(oi, oc);                                                    \
+                        }                                                                    \
+    } while (0)
+
+void orc_conv3d_int(const orc_conv3d_geom *g, const int64_t *input, const int64_t *weight, const int64_t *bias,
+                    int64_t bias_len, int64_t input_zp, int64_t weight_zp, int acc_i48, int64_t *out) {
+    if (!acc_i48) {
+        int32_t *in = sub_zp_i32(input, g->n * g->id * g->ih * g->iw * g->ic, input_zp);
+        int32_t *w = sub_zp_i32(weight, g->oc * g->kd * g->kh * g->kw * g->ic, weight_zp);
+#define MAC_I32(i, j) acc = (int32_t)((uint32_t)acc + (uint32_t)in[i] * (uint32_t)w[j])
+#define EMIT_I32(o, oc) out[o] = (int32_t)((uint32_t)acc + (uint32_t)(int32_t)bias[bias_len == 1 ? 0 : oc])
+        CONV3D_LOOP(g, int32_t, 0, MAC_I32, EMIT_I32);
+#undef MAC_I32
+#undef EMIT_I32
+        free(in);
+        free(w);
+        return;
+    }
+#define MAC_I64(i, j) acc = (int64_t)((uint64_t)acc + (uint64_t)(input[i] - input_zp) * (uint64_t)(weight[j] - weight_zp))
+#define EMIT_I64(o, oc) out[o] = clamp48((int64_t)((uint64_t)acc + (uint64_t)bias[bias_len == 1 ? 0 : oc]))
+    CONV3D_LOOP(g, int64_t, 0, MAC_I64, EMIT_I64);
+#undef MAC_I64
+#undef EMIT_I64
+}
+
+void orc_conv3d_float(const orc_conv3d_geom *g, const float *input, const float *weight, const float *bias,
+                      int64_t bias_len, float input_zp, float weight_zp, int acc_type, int out_type, float *out) {
+    int64_t in_count = g->n * g->id * g->ih * g->iw * g->ic;
+    int64_t w_count = g->oc * g->kd * g->kh * g->kw * g->ic;
+    float *in = (float *)malloc((size_t)(in_count ? in_count : 1) * sizeof(float));
+    float *w = (float *)malloc((size_t)(w_count ? w_count : 1) * sizeof(float));
+    for (int64_t i = 0; i < in_count; ++i) in[i] = input[i] - input_zp;
+    for (int64_t i = 0; i < w_count; ++i) w[i] = weight[i] - weight_zp;
+    int kind = acc_kind_for(acc_type);
+#define MAC_F(i, j) acc = fmac(kind, acc, in[i], w[j])
+#define EMIT_F(o, oc) out[o] = orc_round_to(out_type, orc_round_to(out_type, acc) + bias[bias_len == 1 ? 0 : oc])
+    CONV3D_LOOP(g, float, 0.0f, MAC_F, EMIT_F);
+#undef MAC_F
+#undef EMIT_F
+    free(in);
+    free(w);
+}
+
+/* ---------------------------------------------------------------------------
  * TRANSPOSE_CONV2D (src/ops/conv.rs:337-371 Transpose::accumulate, gather form):
  * output (oy, ox) reads input ((oy - out_pad_top - ky) / stride_y, ...) where
  * the division is exact and in range; taps (ky, kx) row-major, ic innermost.

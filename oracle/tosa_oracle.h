@@ -95,6 +95,20 @@ void orc_depthwise_float(const orc_conv_geom *g, const float *input, const float
                          const float *bias, int64_t bias_len, float input_zp, float weight_zp,
                          int acc_type, int out_type, float *out);
 
+/* CONV3D geometry: input NDHWC, weight [oc, kd, kh, kw, ic], pad = [front, back,
+ * top, bottom, left, right], stride / dilation [d, h, w]. */
+typedef struct {
+    int64_t n, id, ih, iw, ic, oc, kd, kh, kw, od, oh, ow;
+    int64_t pad[6];
+    int64_t stride[3];
+    int64_t dilation[3];
+} orc_conv3d_geom;
+/* CONV3D, ConvNd::accumulate conv.rs:147-181 with three spatial dimensions. */
+void orc_conv3d_int(const orc_conv3d_geom *g, const int64_t *input, const int64_t *weight, const int64_t *bias,
+                    int64_t bias_len, int64_t input_zp, int64_t weight_zp, int acc_i48, int64_t *out);
+void orc_conv3d_float(const orc_conv3d_geom *g, const float *input, const float *weight, const float *bias,
+                      int64_t bias_len, float input_zp, float weight_zp, int acc_type, int out_type, float *out);
+
 /* TRANSPOSE_CONV2D, Transpose::accumulate conv.rs:337-371 (gather form); the
  * geometry's pad[0] / pad[2] are out_pad_top / out_pad_left, weight OHWI. */
 void orc_transpose_conv2d_int(const orc_conv_geom *g, const int64_t *input, const int64_t *weight,

@@ -61,6 +61,13 @@ class Conv2dDesc(ctypes.Structure):
                 ("bias_len", ctypes.c_int32)]
 
 
+class Conv3dDesc(ctypes.Structure):
+    _fields_ = [(k, ctypes.c_int32) for k in ("n", "id", "ih", "iw", "ic", "oc", "kd", "kh", "kw")] + \
+               [("pad", ctypes.c_int32 * 6), ("stride", ctypes.c_int32 * 3), ("dilation", ctypes.c_int32 * 3)] + \
+               [(k, ctypes.c_int32) for k in ("in_dtype", "w_dtype", "acc_dtype", "out_dtype", "input_zp",
+                                              "weight_zp", "bias_len")]
+
+
 class Pool2dDesc(ctypes.Structure):
     _fields_ = [("n", ctypes.c_int32), ("ih", ctypes.c_int32), ("iw", ctypes.c_int32), ("c", ctypes.c_int32),
                 ("kernel", ctypes.c_int32 * 2), ("stride", ctypes.c_int32 * 2), ("pad", ctypes.c_int32 * 4),
@@ -123,6 +130,8 @@ SIGNATURES = [
     ("tb_conv2d_plan_destroy", None, [_V]),
     ("tb_conv2d", _I, [_V, _P(Conv2dDesc), _P(RescaleAttr), _V, _V, _V, _V, _V]),
     ("tb_depthwise_conv2d", _I, [_V, _P(Conv2dDesc), _P(RescaleAttr), _V, _V, _V, _V, _V]),
+    ("tb_conv3d_plan_create", _I, [_V, _P(Conv3dDesc), _V, _V, _P(RescaleAttr), _P(_V)]),
+    ("tb_conv3d", _I, [_V, _P(Conv3dDesc), _P(RescaleAttr), _V, _V, _V, _V, _V]),
     ("tb_transpose_conv2d_plan_create", _I, [_V, _P(Conv2dDesc), _V, _V, _P(RescaleAttr), _P(_V)]),
     ("tb_transpose_conv2d", _I, [_V, _P(Conv2dDesc), _P(RescaleAttr), _V, _V, _V, _V, _V]),
     ("tb_rescale", _I, [_V, _P(RescaleAttr), _I, _V, _L, _V, _V]),

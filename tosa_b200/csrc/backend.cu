@@ -816,6 +816,8 @@ struct tb_conv2d_plan {
     float* d_fbias = nullptr;  // float bias widened to f32
     // path 8: im2col rows + a 1x1 tensor-core convolution over them
     tb_conv2d_plan* inner = nullptr;
+    tb_conv3d_desc d3{};            // path 11 (CONV3D, direct kernels): the 3-D descriptor
+    int od = 0;                     // path 11: output depth
     bool transpose = false;         // TRANSPOSE_CONV2D: d.pad holds out_pad; path 10 runs `inner` (stride 1,
                                     // int8) over the tap-reversed weights in d_wpad, else a direct kernel
     int8_t* d_rows = nullptr;       // [n*oh*ow][kp]
@@ -1291,6 +1293,30 @@ extern "C" TB_API tb_status tb_conv2d_plan_run(tb_conv2d_plan* p, const void* in
     cudaStream_t st = static_cast<cudaStream_t>(stream_);
     const tb_conv2d_desc& d = p->d;
     if (p->path == 10) return tb_conv2d_plan_run(p->inner, input, out, stream_);
+    if (p->path == 11) {
+        const tb_conv3d_desc& e = p->d3;
+        Conv3GeomDev g3{e.n, e.id, e.ih, e.iw, e.ic, e.oc, e.kd, e.kh, e.kw, p->od, p->oh, p->ow,
+                        e.pad[0], e.pad[2], e.pad[4], e.stride[0], e.stride[1], e.stride[2],
+                        e.dilation[0], e.dilation[1], e.dilation[2]};
+        const long long total3 = static_cast<long long>(e.n) * p->od * p->oh * p->ow * e.oc;
+        if (total3 == 0) return TB_OK;
+        cudaStream_t st3 = static_cast<cudaStream_t>(stream_);
+        if (e.in_dtype == TB_DT_INT8)
+            conv3d_direct_int<<<grid_for(ctx, total3), 256, 0, st3>>>(
+                g3, static_cast<const int8_t*>(input), static_cast<const int8_t*>(p->weight),
+                static_cast<const int32_t*>(p->bias), e.bias_len, e.input_zp, e.weight_zp, int_epi(p->rs), out,
+                ctx->dev_err);
+        else if (e.in_dtype == TB_DT_INT16)
+            conv3d_direct_i48<<<grid_for(ctx, total3), 256, 0, st3>>>(
+                g3, static_cast<const int16_t*>(input), static_cast<const int8_t*>(p->weight),
+                static_cast<const int64_t*>(p->bias), e.bias_len, e.input_zp, e.weight_zp, static_cast<int64_t*>(out));
+        else
+            conv3d_direct_float<<<grid_for(ctx, total3), 256, 0, st3>>>(g3, input, p->weight, p->bias, e.bias_len,
+                                                                        e.in_dtype, e.w_dtype, e.acc_dtype,
+                                                                        e.out_dtype, out);
+        TB_LAUNCHED(ctx);
+        return TB_OK;
+    }
     ConvGeomDev g;
     g.tr = p->transpose ? 1 : 0;
     g.n = d.n; g.ih = d.ih; g.iw = d.iw; g.ic = d.ic; g.oc = d.oc; g.kh = d.kh; g.kw = d.kw;
@@ -1522,6 +1548,73 @@ extern "C" TB_API void tb_conv2d_plan_destroy(tb_conv2d_plan* p) {
     if (p->d_fbias) cudaFree(p->d_fbias);
     if (p->d_dw) cudaFree(p->d_dw);
     delete p;
+}
+
+extern "C" TB_API tb_status tb_conv3d_plan_create(tb_context* ctx, const tb_conv3d_desc* d, const void* weight,
+                                                  const void* bias, const tb_rescale_attr* rescale,
+                                                  tb_conv2d_plan** out) {
+    if (!ctx || !d || !out || !weight || !bias) return fail(TB_ERR_INVALID_ARGUMENT, "null argument");
+    *out = nullptr;
+    TB_CUDA(cudaSetDevice(ctx->device));
+    const char* op = "CONV3D";
+    // check_conv_attributes (src/ops/conv.rs:77-92), ConvNd::new (:107-139)
+    for (int i = 0; i < 6; ++i)
+        if (d->pad[i] < 0) return fail(TB_ERR_GRAPH, "%s: pad must be non-negative", op);
+    for (int i = 0; i < 3; ++i) {
+        if (d->stride[i] < 1) return fail(TB_ERR_GRAPH, "%s: stride must be at least 1", op);
+        if (d->dilation[i] < 1) return fail(TB_ERR_GRAPH, "%s: dilation must be at least 1", op);
+    }
+    int od = 0, oh = 0, ow = 0;
+    TB_TRY(conv_extent(op, d->id, d->pad[0], d->pad[1], d->kd, d->dilation[0], d->stride[0], &od));
+    TB_TRY(conv_extent(op, d->ih, d->pad[2], d->pad[3], d->kh, d->dilation[1], d->stride[1], &oh));
+    TB_TRY(conv_extent(op, d->iw, d->pad[4], d->pad[5], d->kw, d->dilation[2], d->stride[2], &ow));
+    if (d->bias_len != d->oc && d->bias_len != 1)
+        return fail(TB_ERR_SHAPE_MISMATCH, "%s: bias channels %d must be 1 or match output channels %d", op,
+                    d->bias_len, d->oc);
+    const int it = d->in_dtype, wt = d->w_dtype, at = d->acc_dtype, ot = d->out_dtype;
+    if (!conv_types_valid(true, it, wt, at, ot))  // standard_types (conv.rs:388-396)
+        return fail(TB_ERR_DTYPE_MISMATCH, "%s: unsupported types input=%d weight=%d acc=%d output=%d", op, it, wt, at,
+                    ot);
+    const bool integer = it == TB_DT_INT8 || it == TB_DT_INT16;
+    if (integer) {
+        if (d->input_zp != 0 && it != TB_DT_INT8)
+            return fail(TB_ERR_GRAPH, "%s: input zero point must be zero for non-int8 input", op);
+        if (d->weight_zp != 0 && wt != TB_DT_INT8)
+            return fail(TB_ERR_GRAPH, "%s: weight zero point must be zero for non-int8 weight", op);
+    } else if (d->input_zp != 0 || d->weight_zp != 0) {
+        return fail(TB_ERR_GRAPH, "%s: zero points must be zero for floating-point operands", op);
+    }
+    if (rescale && it != TB_DT_INT8) return fail(TB_ERR_DTYPE_MISMATCH, "%s: RESCALE needs an int32 result", op);
+    tb_conv2d_plan* p = new tb_conv2d_plan;
+    p->ctx = ctx;
+    p->d3 = *d;
+    p->d.oc = d->oc;
+    p->od = od;
+    p->oh = oh;
+    p->ow = ow;
+    p->weight = weight;
+    p->bias = bias;
+    p->path = 11;
+    if (rescale) {
+        tb_status s = make_rescale_plan(ctx, rescale, TB_DT_INT32, d->oc, &p->rs);
+        if (s != TB_OK) {
+            tb_conv2d_plan_destroy(p);
+            return s;
+        }
+    }
+    *out = p;
+    return TB_OK;
+}
+
+extern "C" TB_API tb_status tb_conv3d(tb_context* ctx, const tb_conv3d_desc* d, const tb_rescale_attr* rescale,
+                                     const void* input, const void* weight, const void* bias, void* out,
+                                     void* stream) {
+    tb_conv2d_plan* p = nullptr;
+    TB_TRY(tb_conv3d_plan_create(ctx, d, weight, bias, rescale, &p));
+    tb_status s = tb_conv2d_plan_run(p, input, out, stream);
+    cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+    tb_conv2d_plan_destroy(p);
+    return s;
 }
 
 extern "C" TB_API tb_status tb_transpose_conv2d(tb_context* ctx, const tb_conv2d_desc* d,

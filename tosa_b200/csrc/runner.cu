@@ -67,6 +67,7 @@ const char* op_name(int op) {
     case fb::OP_MATMUL: return "MATMUL";
     case fb::OP_MATMUL_T: return "MATMUL_T";
     case fb::OP_TRANSPOSE_CONV2D: return "TRANSPOSE_CONV2D";
+    case fb::OP_CONV3D: return "CONV3D";
     case fb::OP_MAX_POOL2D: return "MAX_POOL2D";
     case fb::OP_CLAMP: return "CLAMP";
     case fb::OP_ADD: return "ADD";
@@ -144,6 +145,8 @@ struct Step {
     // contraction
     bool depthwise = false;
     bool transpose = false;         // TRANSPOSE_CONV2D (cdesc.pad holds out_pad)
+    bool conv3d = false;            // CONV3D: c3desc instead of cdesc
+    tb_conv3d_desc c3desc{};
     tb_conv2d_desc cdesc{};
     tb_matmul_desc mdesc{};
     int mt_batch = 0;               // MATMUL_T: batch of b [mt_batch, w, c] (n or 1); 0 for MATMUL
@@ -607,6 +610,83 @@ class Compiler {
         s.out = {make_out(o.outputs[0], B.dtype, out_shape)};
     }
 
+    // CONV3D (src/ops/conv.rs:510-516; eval_conv :398-500 with ConvNd::new :107-139, dims 3)
+    void c_conv3d(const fb::Operator& o, Step& s) {
+        const char* op = "CONV3D";
+        if (o.attr.type != o.op) raise(TB_ERR_GRAPH, "%s: missing attribute", op);
+        expect_operands(o, op, 5, 1);
+        const int x = get(o.inputs[0]), w = get(o.inputs[1]), b = get(o.inputs[2]);
+        const Tensor& zx = single(op, "input_zp", get(o.inputs[3]));
+        const Tensor& zw = single(op, "weight_zp", get(o.inputs[4]));
+        const Tensor &X = T(x), &W = T(w), &B = T(b);
+        expect_rank(op, "bias", B, 1);
+        expect_rank(op, "input", X, 5);
+        expect_rank(op, "weight", W, 5);
+        const Attr& a = o.attr;
+        if (a.pad.size() != 6 || a.stride.size() != 3 || a.dilation.size() != 3)
+            raise(TB_ERR_GRAPH, "%s: pad must have 6 elements, stride and dilation 3", op);
+        for (int p : a.pad) if (p < 0) raise(TB_ERR_GRAPH, "%s: pad must be non-negative", op);
+        for (int v : a.stride) if (v < 1) raise(TB_ERR_GRAPH, "%s: stride must be at least 1", op);
+        for (int v : a.dilation) if (v < 1) raise(TB_ERR_GRAPH, "%s: dilation must be at least 1", op);
+        if (W.shape[4] != X.shape[4])
+            raise(TB_ERR_SHAPE_MISMATCH, "%s: weight input channels %lld != input channels %lld", op,
+                  static_cast<long long>(W.shape[4]), static_cast<long long>(X.shape[4]));
+        std::vector<int64_t> out_shape = {X.shape[0]};
+        for (int d = 0; d < 3; ++d) {
+            const int64_t full = X.shape[1 + d] - 1 + a.pad[2 * d] + a.pad[2 * d + 1] - (W.shape[1 + d] - 1) * a.dilation[d];
+            if (full % a.stride[d] != 0)
+                raise(TB_ERR_GRAPH, "%s: parameters must yield exact integer output dimensions", op);
+            const int64_t e = full / a.stride[d] + 1;
+            if (e < 1) raise(TB_ERR_GRAPH, "%s: output dimension %lld must be positive", op, static_cast<long long>(e));
+            out_shape.push_back(e);
+        }
+        const int64_t oc = W.shape[0], bc = B.shape[0];
+        out_shape.push_back(oc);
+        if (bc != oc && bc != 1)
+            raise(TB_ERR_SHAPE_MISMATCH, "%s: bias channels %lld must be 1 or match output channels %lld", op,
+                  static_cast<long long>(bc), static_cast<long long>(oc));
+        const int decl = declared(op, o.outputs[0], out_shape);
+        if (decl && decl != B.dtype)
+            raise(TB_ERR_DTYPE_MISMATCH, "%s: output dtype %d does not match bias dtype %d", op, decl, B.dtype);
+        if (zx.dtype != X.dtype || zw.dtype != W.dtype)
+            raise(TB_ERR_DTYPE_MISMATCH, "%s: zero points must match input/weight dtypes", op);
+        for (int64_t v : X.shape) if (v > INT32_MAX) raise(TB_ERR_NOT_ACCELERATED, "%s: dimension above int32", op);
+        for (int64_t v : W.shape) if (v > INT32_MAX) raise(TB_ERR_NOT_ACCELERATED, "%s: dimension above int32", op);
+        tb_conv3d_desc& d = s.c3desc;
+        d.n = static_cast<int32_t>(X.shape[0]);
+        d.id = static_cast<int32_t>(X.shape[1]);
+        d.ih = static_cast<int32_t>(X.shape[2]);
+        d.iw = static_cast<int32_t>(X.shape[3]);
+        d.ic = static_cast<int32_t>(X.shape[4]);
+        d.oc = static_cast<int32_t>(oc);
+        d.kd = static_cast<int32_t>(W.shape[1]);
+        d.kh = static_cast<int32_t>(W.shape[2]);
+        d.kw = static_cast<int32_t>(W.shape[3]);
+        for (int i = 0; i < 6; ++i) d.pad[i] = a.pad[i];
+        for (int i = 0; i < 3; ++i) { d.stride[i] = a.stride[i]; d.dilation[i] = a.dilation[i]; }
+        d.in_dtype = X.dtype;
+        d.w_dtype = W.dtype;
+        d.acc_dtype = a.acc_type;
+        d.out_dtype = B.dtype;
+        d.bias_len = static_cast<int32_t>(bc);
+        const int64_t izp = ival(zx), wzp = ival(zw);
+        if (is_float_dt(X.dtype)) {
+            if (zx.hf.empty() ? izp != 0 : zx.hf[0] != 0.f) raise(TB_ERR_GRAPH, "%s: zero points must be zero", op);
+            if (zw.hf.empty() ? wzp != 0 : zw.hf[0] != 0.f) raise(TB_ERR_GRAPH, "%s: zero points must be zero", op);
+        } else {
+            if (izp != 0 && X.dtype != TB_DT_INT8)
+                raise(TB_ERR_GRAPH, "%s: input zero point must be zero for non-int8 input", op);
+            if (wzp != 0 && W.dtype != TB_DT_INT8)
+                raise(TB_ERR_GRAPH, "%s: weight zero point must be zero for non-int8 weight", op);
+            d.input_zp = static_cast<int32_t>(izp);
+            d.weight_zp = static_cast<int32_t>(wzp);
+        }
+        s.conv3d = true;
+        s.kind = K_CONV;
+        s.in = {x, w, b, get(o.inputs[3]), get(o.inputs[4])};
+        s.out = {make_out(o.outputs[0], B.dtype, out_shape)};
+    }
+
     // MATMUL, and MATMUL_T (transposed) with b [d,w,c], d == n or 1 (src/ops/matmul.rs:98-174)
     void c_matmul(const fb::Operator& o, Step& s, bool transposed) {
         const char* op = transposed ? "MATMUL_T" : "MATMUL";
@@ -895,6 +975,7 @@ class Compiler {
         case fb::OP_CONV2D: c_conv(o, s, false); break;
         case fb::OP_DEPTHWISE_CONV2D: c_conv(o, s, true); break;
         case fb::OP_TRANSPOSE_CONV2D: c_conv(o, s, false, true); break;
+        case fb::OP_CONV3D: c_conv3d(o, s); break;
         case fb::OP_MATMUL: c_matmul(o, s, false); break;
         case fb::OP_MATMUL_T: c_matmul(o, s, true); break;
         case fb::OP_RESCALE: c_rescale(o, s); break;
@@ -1163,7 +1244,9 @@ tb_status do_compile(tb_graph* G) {
         case K_CONV: {
             const Tensor& W = G->tensors[s.in[1]];
             const Tensor& B = G->tensors[s.in[2]];
-            if (s.transpose)
+            if (s.conv3d)
+                st = tb_conv3d_plan_create(ctx, &s.c3desc, W.dev, B.dev, nullptr, &s.conv);
+            else if (s.transpose)
                 st = tb_transpose_conv2d_plan_create(ctx, &s.cdesc, W.dev, B.dev, s.has_rescale ? &s.rattr : nullptr,
                                                      &s.conv);
             else if (s.depthwise)

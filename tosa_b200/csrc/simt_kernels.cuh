@@ -364,12 +364,102 @@ __global__ void __launch_bounds__(256) colterm_rows_i8(long long rows, int c, co
     }
 }
 
+// ---------------------------------------------------------------------------
+// CONV3D (src/ops/conv.rs:147-181, ConvNd with three spatial dimensions), one thread per
+// output element in the reference's order: taps (kd, kh, kw) row-major, ic innermost.
+// Input NDHWC, weight [oc, kd, kh, kw, ic]. INT16 x INT8 -> INT48 needs clamp48 (below).
+// ---------------------------------------------------------------------------
+struct Conv3GeomDev {
+    int n, id, ih, iw, ic, oc, kd, kh, kw, od, oh, ow;
+    int pd, pt, pl, sd, sh, sw, dd, dh, dw;  // front / top / left pad, strides, dilations
+};
+
+// Visits the taps of output element i that read inside the input: f(input offset, weight
+// offset) per tap, in the reference's order; returns the output channel.
+template <class F>
+__device__ __forceinline__ int conv3_taps(const Conv3GeomDev& g, long long i, F f) {
+    const int oc = static_cast<int>(i % g.oc);
+    long long r = i / g.oc;
+    const int ox = static_cast<int>(r % g.ow);
+    r /= g.ow;
+    const int oy = static_cast<int>(r % g.oh);
+    r /= g.oh;
+    const int oz = static_cast<int>(r % g.od);
+    const long long b = r / g.od;
+    for (int kz = 0; kz < g.kd; ++kz) {
+        const int z = oz * g.sd + kz * g.dd - g.pd;
+        if (z < 0 || z >= g.id) continue;
+        for (int ky = 0; ky < g.kh; ++ky) {
+            const int y = oy * g.sh + ky * g.dh - g.pt;
+            if (y < 0 || y >= g.ih) continue;
+            for (int kx = 0; kx < g.kw; ++kx) {
+                const int x = ox * g.sw + kx * g.dw - g.pl;
+                if (x < 0 || x >= g.iw) continue;
+                f((((b * g.id + z) * g.ih + y) * g.iw + x) * g.ic,
+                  (((static_cast<long long>(oc) * g.kd + kz) * g.kh + ky) * g.kw + kx) * g.ic);
+            }
+        }
+    }
+    return oc;
+}
+
+__global__ void conv3d_direct_int(Conv3GeomDev g, const int8_t* __restrict__ x, const int8_t* __restrict__ w,
+                                  const int32_t* __restrict__ bias, int bias_len, int32_t zx, int32_t zw,
+                                  IntEpiDev e, void* out, uint32_t* err) {
+    const long long total = static_cast<long long>(g.n) * g.od * g.oh * g.ow * g.oc;
+    uint32_t lerr = 0;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        uint32_t acc = 0;
+        const int oc = conv3_taps(g, i, [&](long long xb, long long wb) {
+            for (int c = 0; c < g.ic; ++c)
+                acc += static_cast<uint32_t>(static_cast<int32_t>(x[xb + c]) - zx) *
+                       static_cast<uint32_t>(static_cast<int32_t>(w[wb + c]) - zw);
+        });
+        acc += static_cast<uint32_t>(bias[bias_len == 1 ? 0 : oc]);
+        finish_int(e, static_cast<int32_t>(acc), oc, out, i, &lerr);
+    }
+    if (lerr) atomicOr(err, lerr);
+}
+
+__global__ void conv3d_direct_float(Conv3GeomDev g, const void* __restrict__ x, const void* __restrict__ w,
+                                    const void* __restrict__ bias, int bias_len, int in_dt, int w_dt, int acc_dt,
+                                    int out_dt, void* out) {
+    const long long total = static_cast<long long>(g.n) * g.od * g.oh * g.ow * g.oc;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        float acc = 0.f;
+        const int oc = conv3_taps(g, i, [&](long long xb, long long wb) {
+            for (int c = 0; c < g.ic; ++c) acc = mac_acc(acc, load_f(x, xb + c, in_dt), load_f(w, wb + c, w_dt), acc_dt);
+        });
+        const float bv = load_f(bias, bias_len == 1 ? 0 : oc, out_dt);
+        store_f(out, i, out_dt, round_to_dtype(__fadd_rn(round_to_dtype(acc, out_dt), bv), out_dt));
+    }
+}
+
 // INT16 x INT8 -> INT48 (AccI64, src/ops/accum.rs:43-56): int64 accumulation,
 // bias added with wrap-around, then clamped to 48 bits (src/ops/conv.rs:466-470).
 // INT48 values are stored as int64. depthwise: weight [KH,KW,C,M].
 __device__ __forceinline__ int64_t clamp48(int64_t v) {
     const int64_t lo = -(1ll << 47), hi = (1ll << 47) - 1;
     return v < lo ? lo : (v > hi ? hi : v);
+}
+
+__global__ void conv3d_direct_i48(Conv3GeomDev g, const int16_t* __restrict__ x, const int8_t* __restrict__ w,
+                                  const int64_t* __restrict__ bias, int bias_len, int32_t zx, int32_t zw,
+                                  int64_t* __restrict__ out) {
+    const long long total = static_cast<long long>(g.n) * g.od * g.oh * g.ow * g.oc;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        uint64_t acc = 0;
+        const int oc = conv3_taps(g, i, [&](long long xb, long long wb) {
+            for (int c = 0; c < g.ic; ++c)
+                acc += static_cast<uint64_t>((static_cast<int64_t>(x[xb + c]) - zx) *
+                                             (static_cast<int64_t>(w[wb + c]) - zw));
+        });
+        acc += static_cast<uint64_t>(bias[bias_len == 1 ? 0 : oc]);
+        out[i] = clamp48(static_cast<int64_t>(acc));
+    }
 }
 
 __global__ void conv2d_direct_i48(ConvGeomDev g, const int16_t* __restrict__ x, const int8_t* __restrict__ w,

@@ -21,7 +21,7 @@ enum Op : int {
     OP_AVG_POOL2D = 2, OP_CONV2D = 3, OP_DEPTHWISE_CONV2D = 5, OP_MATMUL = 7, OP_MAX_POOL2D = 8,
     OP_CLAMP = 11, OP_ADD = 15, OP_RESHAPE = 57, OP_TRANSPOSE = 61, OP_RESCALE = 66, OP_CONST = 67,
     OP_IDENTITY = 68, OP_CONST_SHAPE = 75, OP_MATMUL_T = 100,
-    OP_TRANSPOSE_CONV2D = 10,
+    OP_TRANSPOSE_CONV2D = 10, OP_CONV3D = 4,
 };
 
 // Attribute union members (schema/tosa.fbs: the Attribute union repeats the Op order).
@@ -232,6 +232,7 @@ inline void parse_attr(Reader& r, int tag, const Reader::Table& t, Attr* a) {
         a->acc_type = static_cast<int32_t>(r.scalar_u32(t, 3));
         break;
     case OP_CONV2D:
+    case OP_CONV3D:
     case OP_DEPTHWISE_CONV2D:
         a->pad = r.i32_vec(t, 0); a->stride = r.i32_vec(t, 1); a->dilation = r.i32_vec(t, 2);
         a->local_bound = r.scalar_u8(t, 3) != 0; a->acc_type = static_cast<int32_t>(r.scalar_u32(t, 4));
