@@ -4,6 +4,7 @@ profiler (and a quick timing with CUDA events).
     python -m tosa_b200.profile_layer conv N HW IC OC K [--runs 5]
     python -m tosa_b200.profile_layer depthwise N HW C K STRIDE [--runs 5]
     python -m tosa_b200.profile_layer residual N HW C [--runs 5]
+    python -m tosa_b200.profile_layer matmul_t N H C W D [--runs 5]
 
 conv: int8 CONV2D (square HW x HW input, K x K window, stride 1, "same" padding, input
 zero point -3) with a fused per-channel RESCALE (double rounding) + CLAMP to int8,
@@ -12,6 +13,8 @@ depthwise: the same for DEPTHWISE_CONV2D (channel multiplier 1, weight zero poin
 stride 1 or 2) through tb_depthwise_conv2d_plan_create.
 residual: one residual chain (two int8 inputs [N, HW, HW, C] -> RESCALE to int32 each,
 ADD, RESCALE to int8, CLAMP) built with graphs.GraphBuilder and run by the graph runner.
+matmul_t: int8 MATMUL_T a [N,H,C] x b [D,W,C] (D = N, or 1 shared by every batch), zero points
+-3 / 2, through tb_matmul_t_plan_create and tb_matmul_plan_run; also prints int8 TOPS (2*N*H*W*C).
 Inputs are seeded uniform int8. The mean time of the runs after the first two is printed.
 """
 
@@ -37,7 +40,7 @@ def _time(run, runs, torch):
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("kind", choices=["conv", "depthwise", "residual"])
+    ap.add_argument("kind", choices=["conv", "depthwise", "residual", "matmul_t"])
     ap.add_argument("dims", type=int, nargs="+")
     ap.add_argument("--runs", type=int, default=5)
     args = ap.parse_args(argv)
@@ -86,6 +89,19 @@ def main(argv=None) -> int:
         us = _time(lambda: L.check(lib.tb_conv2d_plan_run(h, L.ptr(x), L.ptr(o), L.stream_ptr())), args.runs, torch)
         lib.tb_conv2d_plan_destroy(h)
         print(f"depthwise {n}x{hw}x{hw}x{c} k{k} s{st}: {us:.1f} us")
+    elif args.kind == "matmul_t":
+        n, h, c, w, dd = args.dims
+        desc = L.MatmulDesc(n=n, h=h, c=c, w=w, a_dtype=L.DT_INT8, b_dtype=L.DT_INT8, out_dtype=L.DT_INT32,
+                            a_zp=-3, b_zp=2)
+        h_ = ctypes.c_void_p()
+        L.check(lib.tb_matmul_t_plan_create(ctx.h, desc, dd, None, ctypes.byref(h_)))
+        a = torch.from_numpy(rng.integers(-128, 128, (n, h, c), dtype=np.int8)).cuda()
+        b = torch.from_numpy(rng.integers(-128, 128, (dd, w, c), dtype=np.int8)).cuda()
+        o = torch.empty((n, h, w), dtype=torch.int32, device="cuda")
+        us = _time(lambda: L.check(lib.tb_matmul_plan_run(h_, L.ptr(a), L.ptr(b), L.ptr(o), L.stream_ptr())),
+                   args.runs, torch)
+        lib.tb_matmul_plan_destroy(h_)
+        print(f"matmul_t [{n},{h},{c}]x[{dd},{w},{c}]: {us:.1f} us, {2.0 * n * h * w * c / us / 1e6:.1f} TOPS")
     else:
         from . import graphs
         from . import interpreter as I
