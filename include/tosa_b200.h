@@ -222,7 +222,9 @@ TB_API tb_status tb_depthwise_conv2d(tb_context *ctx, const tb_conv2d_desc *desc
  * input NDHWC [n,id,ih,iw,ic]; weight [oc,kd,kh,kw,ic]; bias [bias_len] (1 or
  * oc) of out_dtype; pad = [front, back, top, bottom, left, right]; stride and
  * dilation [d, h, w]. Types: standard_types (conv.rs:388-396), zero points as
- * CONV2D, optional fused rescale for INT8. Runs the direct kernel in the
+ * CONV2D, optional fused rescale for INT8. INT8 with kd == 1, no depth
+ * padding and depth stride 1 runs as one CONV2D over n*id images (tensor
+ * cores where its layout allows); the rest runs the direct kernel in the
  * reference's order (taps kd, kh, kw row-major, ic innermost). The plan shares
  * tb_conv2d_plan_run / tb_conv2d_plan_destroy with the 2-D convolutions. */
 typedef struct tb_conv3d_desc {

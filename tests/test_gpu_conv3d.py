@@ -93,6 +93,9 @@ INT8_CASES = [
     ((2, 6, 7, 8, 16), (12, 3, 3, 3, 16), (1, 1, 1, 1, 1, 1), (1, 1, 1), (1, 1, 1), -3, 2),
     ((1, 5, 9, 6, 8), (6, 2, 3, 1, 8), (0, 1, 2, 0, 0, 0), (1, 2, 1), (2, 1, 1), 5, 0),
     ((2, 5, 4, 4, 3), (5, 1, 2, 2, 3), (0, 0, 0, 1, 1, 0), (2, 1, 3), (1, 2, 1), -128, 127),
+    # one depth tap, depth stride 1: one CONV2D over n * id images (tensor cores)
+    ((2, 4, 14, 14, 64), (64, 1, 3, 3, 64), (0, 0, 1, 1, 1, 1), (1, 1, 1), (3, 1, 1), -3, 2),
+    ((1, 3, 9, 7, 32), (48, 1, 1, 3, 32), (0, 0, 0, 0, 1, 1), (1, 2, 1), (1, 1, 2), 4, 0),
 ]
 
 
@@ -106,15 +109,16 @@ def test_conv3d_int8(ctx, xs, ws, pad, stride, dil, zx, zw):
     assert np.array_equal(got.astype(np.int64), oracle_int(x, w, bias, zx, zw, pad, stride, dil))
 
 
-def test_conv3d_int8_fused_rescale(ctx):
-    rng = np.random.default_rng(21)
+@pytest.mark.parametrize("kd", [3, 1])
+def test_conv3d_int8_fused_rescale(ctx, kd):
+    rng = np.random.default_rng(21 + kd)
     x = rng.integers(-128, 128, (2, 5, 6, 6, 16), dtype=np.int64)
-    w = rng.integers(-128, 128, (10, 3, 3, 3, 16), dtype=np.int64)
+    w = rng.integers(-128, 128, (10, kd, 3, 3, 16), dtype=np.int64)
     bias = rng.integers(-30000, 30000, 10)
     mult = rng.integers(1 << 30, (1 << 31) - 1, 10)
     shift = rng.integers(34, 40, 10)
     attr = L.rescale_attr(mult, shift, rounding=L.ROUND_DOUBLE, per_channel=True, output_zp=1, out_dtype=L.DT_INT8)
-    pad, stride, dil = (1, 1, 1, 1, 1, 1), (1, 1, 1), (1, 1, 1)
+    pad, stride, dil = ((1, 1) if kd == 3 else (0, 0)) + (1, 1, 1, 1), (1, 1, 1), (1, 1, 1)
     got = run(ctx, x, w, bias, I8, pad, stride, dil, -3, 2, rescale=attr)
     acc = oracle_int(x, w, bias, -3, 2, pad, stride, dil).reshape(-1)
     rc, exp = H.oracle_rescale(acc, L.DT_INT32, L.DT_INT8, mult, shift, 0, 1, 1, L.ROUND_DOUBLE, 1)

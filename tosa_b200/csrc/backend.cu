@@ -1585,6 +1585,48 @@ extern "C" TB_API tb_status tb_conv3d_plan_create(tb_context* ctx, const tb_conv
         return fail(TB_ERR_GRAPH, "%s: zero points must be zero for floating-point operands", op);
     }
     if (rescale && it != TB_DT_INT8) return fail(TB_ERR_DTYPE_MISMATCH, "%s: RESCALE needs an int32 result", op);
+    // one depth tap, no depth padding, depth stride 1: each output depth slice is the CONV2D of
+    // its input slice, so the whole op is one CONV2D over n * id images (int8: exact on the
+    // tensor cores)
+    const long long n2 = static_cast<long long>(d->n) * d->id;
+    if (it == TB_DT_INT8 && d->kd == 1 && d->pad[0] == 0 && d->pad[1] == 0 && d->stride[0] == 1 && n2 <= INT32_MAX) {
+        tb_conv2d_desc cd{};
+        cd.n = static_cast<int32_t>(n2);
+        cd.ih = d->ih;
+        cd.iw = d->iw;
+        cd.ic = d->ic;
+        cd.oc = d->oc;
+        cd.kh = d->kh;
+        cd.kw = d->kw;
+        cd.m = 1;
+        for (int i = 0; i < 4; ++i) cd.pad[i] = d->pad[2 + i];
+        for (int i = 0; i < 2; ++i) {
+            cd.stride[i] = d->stride[1 + i];
+            cd.dilation[i] = d->dilation[1 + i];
+        }
+        cd.in_dtype = it;
+        cd.w_dtype = wt;
+        cd.acc_dtype = at;
+        cd.out_dtype = ot;
+        cd.input_zp = d->input_zp;
+        cd.weight_zp = d->weight_zp;
+        cd.bias_len = d->bias_len;
+        tb_conv2d_plan* p = new tb_conv2d_plan;
+        p->ctx = ctx;
+        p->d3 = *d;
+        p->d.oc = d->oc;
+        p->od = od;
+        p->oh = oh;
+        p->ow = ow;
+        p->path = 10;
+        tb_status s = conv_plan_create(ctx, &cd, weight, bias, rescale, false, &p->inner);
+        if (s != TB_OK) {
+            tb_conv2d_plan_destroy(p);
+            return s;
+        }
+        *out = p;
+        return TB_OK;
+    }
     tb_conv2d_plan* p = new tb_conv2d_plan;
     p->ctx = ctx;
     p->d3 = *d;
