@@ -1,7 +1,8 @@
 /*
  * tosa_b200 -- B200 (sm_100a) execution backend for the dense-contraction path
  * of the tosa-interp TOSA interpreter: CONV2D, DEPTHWISE_CONV2D and MATMUL
- * with their zero points, bias and acc_type, fused with the RESCALE (and
+ * (and MATMUL_T, TRANSPOSE_CONV2D, CONV3D) with their zero points, bias and
+ * acc_type, fused with the RESCALE (and
  * CLAMP) that follows them, plus AVG_POOL2D / MAX_POOL2D and the glue ops the
  * quantized graphs need (standalone RESCALE, CLAMP, ADD).
  *

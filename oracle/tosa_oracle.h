@@ -2,8 +2,9 @@
  * CPU oracle for the tosa_b200 dense-contraction path.
  *
  * TEST INFRASTRUCTURE ONLY. This is a single-threaded C restatement of the
- * reference interpreter's (tosa-interp, Rust) arithmetic for CONV2D,
- * DEPTHWISE_CONV2D, MATMUL, RESCALE, AVG_POOL2D, MAX_POOL2D and CLAMP. It is
+ * reference interpreter's (tosa-interp, Rust) arithmetic for CONV2D, CONV3D,
+ * DEPTHWISE_CONV2D, TRANSPOSE_CONV2D, MATMUL, MATMUL_T, RESCALE, AVG_POOL2D,
+ * MAX_POOL2D and CLAMP. It is
  * linked only by tests/, by __graft_entry__.smoke() and by bench.py's CPU
  * baseline legs, where it is the checker or the timed reference arm. The
  * product library (libtosa_b200) never links or calls it.
