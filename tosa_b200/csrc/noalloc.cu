@@ -14,7 +14,13 @@
 //
 // The array is a fixed 2 MiB per device that loads this library (every GPU
 // holds it until the process exits), which bounds the shapes: n*w <= 131072
-// when a_zp != 0 and at most 16384 rescale channels. Every call shares it and
+// when a_zp != 0 and at most 16384 rescale channels. Shapes whose B rows are
+// not 16-byte multiples (w % 16 != 0) and unaligned operands run the direct
+// kernel, which needs no scratch beyond the error word: the tensor-core path
+// for such B copies it into padded rows, a buffer this entry point does not
+// have. The array's device address is resolved once per device and kept, so
+// the entry point assumes the device's primary context is not reset
+// (cudaDeviceReset) while the process uses it. Every call shares it and
 // it keeps the last call's contents: each call clears the error word and the
 // counter first. Calls that overlap on the GPU (other streams, other host
 // threads) race on the array; serialise them.
@@ -32,6 +38,7 @@ namespace {
 constexpr size_t kScratchBytes = 2u << 20;
 constexpr size_t kColtermOffset = 256;                 // after the error word (0) and the counter (4)
 constexpr long long kMaxColterm = 131072;              // n * w when a_zp != 0
+constexpr int kMaxRescaleChannels = 16384;             // per-channel RESCALE multipliers / shifts
 constexpr size_t kBlobOffset = kColtermOffset + sizeof(int32_t) * (kMaxColterm + 256);
 constexpr size_t kMaxBlobWords = (kScratchBytes - kBlobOffset) / sizeof(int32_t);
 constexpr int kMaxDevices = 64;
@@ -81,6 +88,13 @@ extern "C" TB_API tb_status tb_matmul_i8_noalloc(const tb_matmul_desc* d, const 
         return fail(TB_ERR_NOT_ACCELERATED, "tb_matmul_i8_noalloc runs INT8 x INT8 -> INT32 only");
     int path = 0, bn = 256;
     TB_TRY(matmul_validate(d, rescale != nullptr, &path, &bn));
+    // Path 5 (B rows not 16-byte multiples, e.g. 1000 classes) pads B into a buffer of the
+    // plan's own; here those shapes take the direct kernel instead (path 2), which keeps
+    // nothing per call but the error word.
+    if (path == 5) path = 2;
+    if (rescale && rescale->channels > kMaxRescaleChannels)
+        return fail(TB_ERR_INVALID_ARGUMENT, "tb_matmul_i8_noalloc: %d rescale channels exceed the scratch limit %d",
+                    rescale->channels, kMaxRescaleChannels);
     if (d->a_zp != 0 && static_cast<long long>(d->n) * d->w > kMaxColterm)
         return fail(TB_ERR_INVALID_ARGUMENT, "tb_matmul_i8_noalloc: n*w = %lld exceeds the scratch limit %lld",
                     static_cast<long long>(d->n) * d->w, kMaxColterm);
