@@ -100,10 +100,12 @@ TB_API tb_status tb_memcpy_h2d(tb_context *ctx, void *dst, const void *src, size
 TB_API tb_status tb_memcpy_d2h(tb_context *ctx, void *dst, const void *src, size_t bytes, void *stream);
 /* Number of kernels this context launched so far (for launch accounting). */
 TB_API uint64_t tb_launch_count(tb_context *ctx);
-/* Diagnostics: with TB_TRACE=1 in the environment at context creation, the
- * tensor-core kernels record clock64 stamps of CTA 0 (producer stage issues,
- * MMA stage starts, row-sum stage ends, epilogue tile start/end); copies the
- * 512-entry buffer to host512. */
+/* Diagnostics: in a library built with -DTB_GEMM_TRACE=1 and with TB_TRACE=1
+ * in the environment at context creation, the tensor-core kernels record
+ * clock64 stamps of CTA 0 (producer stage issues, MMA stage starts, row-sum
+ * stage ends, epilogue tile start/end); copies the 512-entry buffer to
+ * host512. Regular builds carry no stamp code and return
+ * TB_ERR_INVALID_ARGUMENT. */
 TB_API tb_status tb_debug_trace(tb_context *ctx, long long *host512);
 
 /* ---- fused RESCALE epilogue ---------------------------------------------- */
@@ -179,9 +181,14 @@ TB_API tb_status tb_matmul_t(tb_context *ctx, const tb_matmul_desc *desc, int32_
  * fixed 2 MiB file-scope device array that every GPU using the library holds
  * until exit, which limits n*w to 131072 when a_zp != 0 and the rescale to
  * 16384 channels (larger shapes are rejected with TB_ERR_INVALID_ARGUMENT).
+ * B rows that are not 16-byte multiples (w % 16 != 0, e.g. 1000 classes) and
+ * operands that are not 16-byte aligned run the direct CUDA-core kernel, which
+ * needs no scratch (the tensor-core path would pad B into a buffer of its own).
  * Runs on the calling thread's current device; its first call on a device
- * resolves the array's device address (cudaGetSymbolAddress), so make that
- * first call before any stream capture. Every call clears the scratch it
+ * resolves the array's device address (cudaGetSymbolAddress) and keeps it, so
+ * make that first call before any stream capture, and do not reset the
+ * device's primary context (cudaDeviceReset) while the process still calls
+ * this entry point. Every call clears the scratch it
  * needs, then waits for `stream` and returns data-dependent errors itself.
  * Calls that overlap on the GPU share the array and race: serialise them. */
 TB_API tb_status tb_matmul_i8_noalloc(const tb_matmul_desc *desc, const tb_rescale_attr *rescale, const void *a,

@@ -376,8 +376,15 @@ TB_API tb_status tb_context_create(int device, tb_context** out) {
         return fail(TB_ERR_CUDA, "error-word allocation failed: %s", cudaGetErrorString(e));
     }
     if (const char* env = getenv("TB_TRACE")) {
-        if (atoi(env) && cudaMalloc(&ctx->trace, 512 * sizeof(long long)) == cudaSuccess)
+        if (kGemmTrace && atoi(env) && cudaMalloc(&ctx->trace, 512 * sizeof(long long)) == cudaSuccess)
             cudaMemset(ctx->trace, 0, 512 * sizeof(long long));
+    }
+    // TB_GEMM_EPI_GROUPS=0 / 1: every tensor-core GEMM splits each tile's epilogue by column
+    // halves (0) or gives whole tiles to the two epilogue groups in turn (1), whatever the tile
+    // count (tests run both forms on small shapes)
+    if (const char* env = getenv("TB_GEMM_EPI_GROUPS")) {
+        const int v = atoi(env);
+        if (v == 0 || v == 1) ctx->epi_groups = v;
     }
     *out = ctx;
     return TB_OK;
@@ -385,7 +392,9 @@ TB_API tb_status tb_context_create(int device, tb_context** out) {
 
 TB_API tb_status tb_debug_trace(tb_context* ctx, long long* host512) {
     if (!ctx || !host512) return fail(TB_ERR_INVALID_ARGUMENT, "null argument");
-    if (!ctx->trace) return fail(TB_ERR_INVALID_ARGUMENT, "context created without TB_TRACE=1");
+    if (!ctx->trace)
+        return fail(TB_ERR_INVALID_ARGUMENT, "no trace buffer: a library built with -DTB_GEMM_TRACE=1 and TB_TRACE=1 "
+                                             "at context creation are both needed");
     TB_CUDA(cudaMemcpy(host512, ctx->trace, 512 * sizeof(long long), cudaMemcpyDeviceToHost));
     return TB_OK;
 }

@@ -54,7 +54,7 @@ tb_status launch_gemm(tb_context* ctx, const CUtensorMap& tmA, const CUtensorMap
     const int grid = std::min(p.total_tiles, ctx->num_sms);
     // two epilogue groups on alternate tiles pay off when each CTA has many tiles (measured on
     // B200: ResNet-50's 56x56 layers and stems gain, 14x14 layers with 2-3 tiles per CTA lose)
-    p.epi_groups = p.total_tiles >= 8 * grid ? 1 : 0;
+    p.epi_groups = ctx->epi_groups >= 0 ? ctx->epi_groups : (p.total_tiles >= 8 * grid ? 1 : 0);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kGemmThreads);

@@ -12,13 +12,21 @@
 
 #include "../../include/tosa_b200.h"
 
+// GEMM timeline stamps (clock64 of CTA 0 into tb_context::trace): compiled into the
+// tensor-core kernels only when the library is built with -DTB_GEMM_TRACE=1.
+#ifndef TB_GEMM_TRACE
+#define TB_GEMM_TRACE 0
+#endif
+constexpr bool kGemmTrace = TB_GEMM_TRACE != 0;
+
 struct tb_context {
     int device = 0;
     int num_sms = 148;
     uint32_t* dev_err = nullptr;     // device error word (DEV_ERR_* bits)
     long long timeout_cycles = 0;    // bound on every in-kernel wait
     uint64_t launches = 0;
-    long long* trace = nullptr;      // optional GEMM timeline buffer (TB_TRACE=1)
+    long long* trace = nullptr;      // optional GEMM timeline buffer (TB_TRACE=1, TB_GEMM_TRACE builds)
+    int epi_groups = -1;             // TB_GEMM_EPI_GROUPS: 0 / 1 force the GEMM epilogue split, -1 by tile count
 };
 
 namespace tb {

@@ -520,10 +520,13 @@ __device__ __forceinline__ void fast_tile_pass(const GemmParams& p, const FastCo
             __syncwarp();
             if (next) tmem_wait_regs(fA);
         } else {
+            // one TMEM load per group: the next group's columns load while this group is stored
             fast_chunk_i8<EK, FW, ROW, DELTA>(p, fA, h.nb + g0, h.rowterm, h.cst_n, h.delta, h.fm, h.fsh, h.fc,
                                                    fk, pk);
 #pragma unroll
             for (int j = 0; j < FPK; ++j) h.wst[lane * 4 + (j ^ swz)] = pk[j];
+            __syncwarp();
+            if (g0 + GW < COLS && g0 + GW < h.n_end) tmem_ld_32x32b(h.taddr + g0 + GW, fA);
         }
         if (h.ftr && g0 / GW < 8) h.ftr[3 * (g0 / GW) + 1] = clock64();
         __syncwarp();
@@ -547,6 +550,9 @@ __device__ __forceinline__ void fast_tile_pass(const GemmParams& p, const FastCo
             }
         }
         if (h.ftr && g0 / GW < 8) h.ftr[3 * (g0 / GW) + 2] = clock64();
+        if constexpr (GW != 2 * FW) {
+            if (g0 + GW < COLS && g0 + GW < h.n_end) tmem_wait_regs(fA);
+        }
         __syncwarp();
     }
 }
@@ -611,7 +617,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     const long long limit = p.timeout_cycles;
-    if (p.trace && blockIdx.x == 0 && threadIdx.x == 0) p.trace[400] = clock64();
+    if (kGemmTrace && p.trace && blockIdx.x == 0 && threadIdx.x == 0) p.trace[400] = clock64();
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer
@@ -637,7 +643,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     if (!mbar_wait_bounded(&empty[s], ph ^ 1, abort_flag, limit)) { ok = false; break; }
                     uint8_t* sa = stage_base + s * Cfg::STAGE_BYTES;
                     uint8_t* sb = sa + Cfg::A_BYTES;
-                    if (p.trace && blockIdx.x == 0 && it < 128) p.trace[it] = clock64();
+                    if (kGemmTrace && p.trace && blockIdx.x == 0 && it < 128) p.trace[it] = clock64();
                     if constexpr (Cfg::kTap2) {
                         // taps tap and tap + 1 (the last stage of an odd tap count has one; the B box's
                         // second half then lies past K and is filled with zeros)
@@ -711,7 +717,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     const uint32_t ph = (it / S) & 1;
                     if (!mbar_wait_bounded(&full[s], ph, abort_flag, limit)) { ok = false; break; }
                     tc_fence_after();
-                    if (p.trace && blockIdx.x == 0 && it < 128) p.trace[128 + it] = clock64();
+                    if (kGemmTrace && p.trace && blockIdx.x == 0 && it < 128) p.trace[128 + it] = clock64();
                     const uint32_t sa = smem_u32(stage_base + s * Cfg::STAGE_BYTES);
                     const uint32_t sb = sa + Cfg::A_BYTES;
 #pragma unroll
@@ -781,7 +787,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     }
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&empty[s]);
-                    if (p.trace && blockIdx.x == 0 && it < 128 && warp == 2 && lane == 0) p.trace[256 + it] = clock64();
+                    if (kGemmTrace && p.trace && blockIdx.x == 0 && it < 128 && warp == 2 && lane == 0) p.trace[256 + it] = clock64();
                 }
                 if (!ok) break;
                 const int buf = tcount & 1;
@@ -955,7 +961,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             if constexpr ((EF & kEfDelta) != 0) warp_delta = __any_sync(0xffffffffu, delta != nullptr);
             if (!mbar_wait_bounded(&tfull[buf], tph, abort_flag, limit)) { ok = false; break; }
             tc_fence_after();
-            if (p.trace && blockIdx.x == 0 && tcount < 8 && threadIdx.x == 128) p.trace[384 + 2 * tcount] = clock64();
+            if (kGemmTrace && p.trace && blockIdx.x == 0 && tcount < 8 && threadIdx.x == 128) p.trace[384 + 2 * tcount] = clock64();
             int32_t rowterm = 0;
             if (need_rowsum) {
                 if (!mbar_wait_bounded(&rsfull[buf], tph, abort_flag, limit)) { ok = false; break; }
@@ -986,7 +992,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 // conditions are warp-uniform, so the TMEM loads stay warp-collective)
                 const int n_end = p.N - nb;  // columns of this warp's part that exist
                 // trace slots 416..479: per staging group, start / chunks done / stores done (CTA 0, tiles 0-1)
-                long long* ftr = (p.trace && blockIdx.x == 0 && tcount < 2 && threadIdx.x == 128)
+                long long* ftr = (kGemmTrace && p.trace && blockIdx.x == 0 && tcount < 2 && threadIdx.x == 128)
                                      ? p.trace + 416 + 32 * tcount : nullptr;
                 // a warp with a border row adds every row's delta (zeros for interior rows)
                 const FastTile h{taddr, cols, n_end, nb, rowterm, cst_n, warp_delta ? delta_fast : nullptr,
@@ -1000,7 +1006,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             tmem_wait_regs(accA);
 #pragma unroll 1
             for (int c0 = 0; c0 < cols; c0 += 2 * kChunk) {
-                const bool tr = p.trace && blockIdx.x == 0 && tcount == 0 && threadIdx.x == 128;
+                const bool tr = kGemmTrace && p.trace && blockIdx.x == 0 && tcount == 0 && threadIdx.x == 128;
                 if (tr) p.trace[408 + (c0 / kChunk) * 2] = clock64();
                 __syncwarp();
                 tmem_ld_32x32b_x16(taddr + c0 + kChunk, accB);
@@ -1020,7 +1026,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[buf]);
-            if (p.trace && blockIdx.x == 0 && tcount < 8 && threadIdx.x == 128) p.trace[385 + 2 * tcount] = clock64();
+            if (kGemmTrace && p.trace && blockIdx.x == 0 && tcount < 8 && threadIdx.x == 128) p.trace[385 + 2 * tcount] = clock64();
         }
         if (!ok && lane == 0) { atomicOr(p.err, DEV_ERR_TIMEOUT); *abort_flag = 1; }
         if (err) atomicOr(p.err, err);
