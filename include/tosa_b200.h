@@ -201,7 +201,10 @@ TB_API tb_status tb_matmul_i8_noalloc(const tb_matmul_desc *desc, const tb_resca
  * value per byte) -> INT32 with zero points; float: BF16 x BF16 and
  * FP16 x FP16 with acc_type FP32 -> out_dtype (BF16/FP16/FP32 per the
  * reference's type tables). The weight and bias pointers are read when the
- * plan is created (per-channel sums) and again at every run. */
+ * plan is created (per-channel sums; TRANSPOSE_CONV2D's tap-reversed copy) and
+ * again at every run. Plan creation reads them on the legacy default stream
+ * and waits for that work, so weights written on another stream (in
+ * particular a non-blocking one) must be complete before the plan is created. */
 typedef struct tb_conv2d_desc {
     int32_t n, ih, iw, ic;
     int32_t oc, kh, kw;       /* CONV2D; for DEPTHWISE oc = ic * m */
