@@ -12,6 +12,12 @@ and distributions, random-init weights):
                zero points in [-8,8], fused RESCALE (single multiplier, shift 35,
                single_round) to int8. Metric: int8 TOPS (2*8*1024^3 ops per step).
   mobilenetv2  config 3: the MobileNetV2-shaped int8 graph, batch 64 per GPU.
+  conv1        config 1: one int8 CONV2D [1,56,56,64] x [64,3,3,64] + per-channel RESCALE to
+               int8 (the CPU-runnable case), one image per step; the roofline line times the
+               same layer over 64 images. Metric: int8 TOPS.
+  bf16         config 5: the five bf16 x bf16 -> fp32 MATMULs of one transformer block (QKV,
+               attention scores, P.V, MLP up and down). Metric: TFLOP/s; roofline against the
+               pool's measured sustained bf16 peak.
 
 Multi-GPU (torchrun, one process per GPU): every rank runs its own shard of the
 workload (weak scaling: 64 images per GPU, the global batch 64 x N; the shards
@@ -341,7 +347,301 @@ class MobileNetV2Workload(GraphWorkload):
         return self.graphs.mobilenetv2_int8(batch)
 
 
-WORKLOADS = {"matmul": MatmulWorkload, "resnet50": ResNet50Workload, "mobilenetv2": MobileNetV2Workload}
+class Conv1Workload:
+    """one int8 CONV2D [1,56,56,64] x [64,3,3,64] (pad 1, input zero point -3)
+    with its per-channel double-rounding RESCALE to int8 fused (output zero point 5). The step
+    is that one image; the roofline line times the same layer over 64 images, where the
+    tensor cores have enough tiles to be measured."""
+
+    name = "conv1"
+    unit = "TOPS"
+    kernel = "tc_gemm_kernel"
+    dtype = "int8"
+    seed = 1
+    roof_batch = 64
+
+    def __init__(self, args):
+        rng = np.random.default_rng(self.seed)
+        self.x = rng.integers(-128, 128, (1, 56, 56, 64), dtype=np.int8)
+        self.w = rng.integers(-127, 128, (64, 3, 3, 64), dtype=np.int8)
+        self.bias = rng.integers(-32768, 32768, 64).astype(np.int32)
+        self.mult = rng.integers(1 << 30, (1 << 31) - 1, 64, endpoint=True)
+        self.shift = rng.integers(30, 39, 64)
+        self.macs = 56 * 56 * 64 * 3 * 3 * 64
+        self.ops = 2 * self.macs
+        self.units_per_step = self.ops / 1e12
+
+    def config(self):
+        return {"workload": "config1: int8 CONV2D [1,56,56,64] x [64,3,3,64], pad 1, input_zp -3, weight_zp 0, "
+                            "+ per-channel RESCALE (double_round, shift 30-38, output_zp 5) -> int8, one image",
+                "global_batch": 1, "roofline_batch": self.roof_batch,
+                "l2": "flushed between timed steps (256 MiB write)"}
+
+    def _plan(self, L, ctx, n):
+        d = L.conv_desc(n, 56, 56, 64, 64, 3, 3, (1, 1, 1, 1), (1, 1), (1, 1), L.DT_INT8, L.DT_INT8, L.DT_INT32,
+                        L.DT_INT32, -3, 0, 64)
+        h = ctypes.c_void_p()
+        L.check(L.load().tb_conv2d_plan_create(ctx.h, d, L.ptr(self.dw), L.ptr(self.db), self.attr, ctypes.byref(h)))
+        return h
+
+    def setup(self, L, ctx, torch, stream):
+        self.L, self.torch = L, torch
+        self.attr = L.rescale_attr(self.mult, self.shift, rounding=L.ROUND_DOUBLE, output_zp=5, out_dtype=L.DT_INT8)
+        self.dw = torch.from_numpy(self.w).cuda()
+        self.db = torch.from_numpy(self.bias).cuda()
+        self.plan = self._plan(L, ctx, 1)
+        self.ctx = ctx
+        self.dx = torch.from_numpy(self.x).cuda()
+        self.dout = torch.empty((1, 56, 56, 64), dtype=torch.int8, device="cuda")
+        self.hx = torch.from_numpy(self.x).pin_memory()
+        self.hout = torch.empty((1, 56, 56, 64), dtype=torch.int8).pin_memory()
+        self.h2d = self.x.nbytes
+        self.d2h = self.hout.numel()
+
+    def step(self, stream):
+        L = self.L
+        L.check(L.load().tb_conv2d_plan_run(self.plan, L.ptr(self.dx), L.ptr(self.dout), L.stream_ptr(stream)))
+        return 1
+
+    def e2e_inputs(self):
+        return [(self.hx, self.dx)]
+
+    def e2e_output(self, stream):
+        self.hout.copy_(self.dout, non_blocking=True)
+
+    def _oracle(self, x):
+        from tests import helpers as H
+        acc = H.oracle_conv_int(x.astype(np.int64), self.w.astype(np.int64), self.bias.astype(np.int64), -3, 0,
+                                (1, 1, 1, 1), (1, 1), (1, 1))
+        rc, q = H.oracle_rescale(acc, 5, 3, self.mult, self.shift, 0, 5, 1, 3, 1)
+        return rc, q.reshape(acc.shape)
+
+    def check(self):
+        """The whole output bit-exact against the oracle."""
+        rc, want = self._oracle(self.x)
+        return rc == 0 and np.array_equal(self.dout.cpu().numpy().astype(np.int64), want)
+
+    def kernel_time(self, stream, flush, steps):
+        """CUDA-event time of the same layer over 64 images (one launch of the GEMM)."""
+        torch, L = self.torch, self.L
+        plan = self._plan(L, self.ctx, self.roof_batch)
+        x = torch.randint(-128, 128, (self.roof_batch, 56, 56, 64), dtype=torch.int8, device="cuda")
+        out = torch.empty((self.roof_batch, 56, 56, 64), dtype=torch.int8, device="cuda")
+        run = lambda: L.check(L.load().tb_conv2d_plan_run(plan, L.ptr(x), L.ptr(out), L.stream_ptr(stream)))  # noqa
+        run()
+        evs = []
+        for _ in range(steps):
+            flush.fill_(1)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            run()
+            e.record(stream)
+            evs.append((s, e))
+        torch.cuda.synchronize()
+        L.load().tb_conv2d_plan_destroy(plan)
+        ms = statistics.mean(s.elapsed_time(e) for s, e in evs)
+        return self.roof_batch * self.ops / (ms * 1e-3) / 1e12, "TOPS (int8)", ms, 1
+
+    def close(self):
+        if getattr(self, "plan", None) is not None:
+            self.L.load().tb_conv2d_plan_destroy(self.plan)
+            self.plan = None
+
+    def cpu_run(self, images, threads):
+        """`images` config-1 convolutions (+ RESCALE) through the oracle's C loops."""
+        from oracle import oracle as O
+        from tests import helpers as H
+        if threads > 1:
+            x = np.ascontiguousarray(np.repeat(self.x, images, axis=0), np.int64)
+            g = H.conv_geom(x.shape, self.w.shape, (1, 1, 1, 1), (1, 1), (1, 1))
+            acc = np.zeros(images * 56 * 56 * 64, dtype=np.int64)
+            p = lambda a: a.ctypes.data_as(ctypes.c_void_p)  # noqa: E731
+            O.lib().orc_conv2d_int_mt(ctypes.byref(g), p(x), p(np.ascontiguousarray(self.w, np.int64)),
+                                      p(np.ascontiguousarray(self.bias, np.int64)), ctypes.c_int64(64),
+                                      ctypes.c_int64(-3), ctypes.c_int64(0), p(acc), ctypes.c_int(threads))
+            H.oracle_rescale(acc, 5, 3, self.mult, self.shift, 0, 5, 1, 3, 1)
+        else:
+            for _ in range(images):
+                self._oracle(self.x)
+        return images * self.units_per_step
+
+    def cpu_default(self, args):
+        return 100  # about 12 s of single-core work
+
+    def ref_default(self, args):
+        return 2 * (os.cpu_count() or 1)
+
+    def cpu_sample_desc(self, images, threads):
+        return (f"{images} config-1 convolution(s) + RESCALE (115.6 M MAC each) on {threads} thread(s), "
+                f"C restatement of the reference loops")
+
+
+class Bf16Workload:
+    """the bf16 contractions of one transformer block (batch 32, sequence 512,
+    hidden 4096, 32 heads), MATMUL with fp32 results: QKV [1,16384,4096] x [1,4096,12288],
+    attention scores [1024,512,128] x [1024,128,512] and P.V [1024,512,512] x [1024,512,128],
+    MLP [1,16384,4096] x [1,4096,11008] and [1,16384,11008] x [1,11008,4096]. Activations
+    N(0,1), weights N(0,0.02), cast to bf16. A step runs the five; the metric is TFLOP/s."""
+
+    name = "bf16"
+    unit = "TFLOP/s"
+    kernel = "tc_gemm_kernel"
+    dtype = "bf16"
+    seed = 5
+    # (name, n, h, c, w, B is a weight)
+    SHAPES = [("qkv", 1, 16384, 4096, 12288, True), ("scores", 1024, 512, 128, 512, False),
+              ("pv", 1024, 512, 512, 128, False), ("mlp_up", 1, 16384, 4096, 11008, True),
+              ("mlp_down", 1, 16384, 11008, 4096, True)]
+
+    def __init__(self, args):
+        self.flops = sum(2 * n * h * c * w for _, n, h, c, w, _ in self.SHAPES)
+        self.units_per_step = self.flops / 1e12
+
+    def config(self):
+        return {"workload": "config5: bf16 transformer-block contractions (batch 32, seq 512, hidden 4096, 32 heads): "
+                            "QKV [16384,4096]x[4096,12288], scores [1024,512,128]x[1024,128,512], "
+                            "P.V [1024,512,512]x[1024,512,128], MLP 4096->11008->4096; MATMUL bf16 x bf16 -> fp32",
+                "global_batch": 32, "seq_len": 512, "flop_per_step": self.flops,
+                "l2": "operands larger than L2; flushed between timed steps (256 MiB write)",
+                "e2e_copies": "every activation operand uploaded, the MLP output downloaded"}
+
+    def setup(self, L, ctx, torch, stream):
+        self.L, self.torch, self.ctx = L, torch, ctx
+        g = torch.Generator(device="cuda")
+        g.manual_seed(self.seed)
+        self.ops = []
+        for name, n, h, c, w, weight in self.SHAPES:
+            a = torch.randn((n, h, c), generator=g, device="cuda").to(torch.bfloat16)
+            b = (torch.randn((n, c, w), generator=g, device="cuda") * (0.02 if weight else 1.0)).to(torch.bfloat16)
+            out = torch.empty((n, h, w), dtype=torch.float32, device="cuda")
+            d = L.MatmulDesc(n=n, h=h, c=c, w=w, a_dtype=L.DT_BF16, b_dtype=L.DT_BF16, out_dtype=L.DT_FP32,
+                             a_zp=0, b_zp=0)
+            plan = ctypes.c_void_p()
+            L.check(L.load().tb_matmul_plan_create(ctx.h, d, None, ctypes.byref(plan)))
+            self.ops.append({"name": name, "shape": (n, h, c, w), "a": a, "b": b, "out": out, "plan": plan,
+                             "weight": weight})
+        uploads = []
+        for op in self.ops:
+            uploads.append(op["a"])
+            if not op["weight"]:
+                uploads.append(op["b"])
+        self.pairs = [(t.cpu().pin_memory(), t) for t in uploads]
+        last = self.ops[-1]["out"]
+        self.hout = torch.empty(last.shape, dtype=torch.float32).pin_memory()
+        self.h2d = sum(t.numel() * 2 for t in uploads)
+        self.d2h = last.numel() * 4
+
+    def _run(self, op, stream):
+        L = self.L
+        L.check(L.load().tb_matmul_plan_run(op["plan"], L.ptr(op["a"]), L.ptr(op["b"]), L.ptr(op["out"]),
+                                            L.stream_ptr(stream)))
+
+    def step(self, stream):
+        for op in self.ops:
+            self._run(op, stream)
+        return len(self.ops)
+
+    def e2e_inputs(self):
+        return self.pairs
+
+    def e2e_output(self, stream):
+        self.hout.copy_(self.ops[-1]["out"], non_blocking=True)
+
+    def check(self):
+        """Sampled rows of every product (the first two rows of the first batch, the last row of
+        the last batch) against the oracle's AccF32 loop, within 2 bf16 ULP of the expected value
+        plus 2^-16 of the row's sum of |a*b| (the accumulation order differs)."""
+        from tests import helpers as H
+        from oracle import oracle as O
+        for op in self.ops:
+            n, h, c, w = op["shape"]
+            for bi, r0, nr in ((0, 0, 2), (n - 1, h - 1, 1)):
+                a = op["a"][bi:bi + 1, r0:r0 + nr].float().cpu().numpy()
+                b = op["b"][bi:bi + 1].float().cpu().numpy()
+                want = H.oracle_matmul_float(a, b, O.D["FP32"])
+                got = op["out"][bi:bi + 1, r0:r0 + nr].cpu().numpy()
+                ok, _ = H.float_matmul_within_tolerance(got, want, a, b)
+                if not ok:
+                    return False
+        return True
+
+    def kernel_time(self, stream, flush, steps):
+        """CUDA-event time of every GEMM launch of the step (the step is five launches of the
+        tensor-core kernel): achieved = the step's FLOPs / their summed time."""
+        torch = self.torch
+        evs = []
+        for _ in range(steps):
+            flush.fill_(1)
+            for op in self.ops:
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record(stream)
+                self._run(op, stream)
+                e.record(stream)
+                evs.append((s, e))
+        torch.cuda.synchronize()
+        tot = sum(s.elapsed_time(e) for s, e in evs)
+        return self.flops * steps / (tot * 1e-3) / 1e12, "TFLOP/s (bf16)", tot / len(evs), len(self.ops)
+
+    def peak(self, torch):
+        peaks = _measured_peaks()
+        if peaks.get("bf16_tflops_sustained"):
+            return float(peaks["bf16_tflops_sustained"]), "MEASURED_PEAKS.json bf16_tflops_sustained (of measured)"
+        return 1400.0, "fallback 1.4 PFLOP/s sustained bf16 (of fallback)"
+
+    def close(self):
+        for op in getattr(self, "ops", []):
+            if op["plan"] is not None:
+                self.L.load().tb_matmul_plan_destroy(op["plan"])
+                op["plan"] = None
+
+    # -- CPU (oracle restatement): rows of the QKV product
+    def cpu_prepare(self):
+        """Seeded operands of the QKV product on the host (outside the timed CPU region)."""
+        if not hasattr(self, "_cpu_ab"):
+            from tests import helpers as H
+            g = np.random.default_rng(self.seed)
+            a = g.standard_normal((1, 512, 4096), dtype=np.float32)
+            b = g.standard_normal((1, 4096, 12288), dtype=np.float32) * np.float32(0.02)
+            self._cpu_ab = (H.bf16_round(a), H.bf16_round(b))
+
+    def cpu_run(self, rows, threads):
+        from oracle import oracle as O
+        self.cpu_prepare()
+        a, b = self._cpu_ab
+        rows = min(rows, a.shape[1])
+        a = np.ascontiguousarray(a[:, :rows])
+        out = np.zeros(rows * 12288, dtype=np.float32)
+        p = lambda x: x.ctypes.data_as(ctypes.c_void_p)  # noqa: E731
+        if threads > 1:
+            O.lib().orc_matmul_float_mt(ctypes.c_int64(1), ctypes.c_int64(rows), ctypes.c_int64(4096),
+                                        ctypes.c_int64(12288), p(a), p(b), ctypes.c_int(O.D["FP32"]), p(out),
+                                        ctypes.c_int(threads))
+        else:
+            O.lib().orc_matmul_float(ctypes.c_int64(1), ctypes.c_int64(rows), ctypes.c_int64(4096),
+                                     ctypes.c_int64(12288), p(a), p(b), ctypes.c_int(O.D["FP32"]), p(out))
+        return 2 * rows * 4096 * 12288 / 1e12
+
+    def cpu_default(self, args):
+        return 32  # about 16 s of single-core work
+
+    def ref_default(self, args):
+        return 2 * (os.cpu_count() or 1)
+
+    def cpu_sample_desc(self, rows, threads):
+        return (f"{rows} row(s) of the QKV product [rows,4096] x [4096,12288] (bf16 operands, AccF32), "
+                f"{threads} thread(s), C restatement of the reference loops")
+
+
+def _measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
+
+
+WORKLOADS = {"matmul": MatmulWorkload, "resnet50": ResNet50Workload, "mobilenetv2": MobileNetV2Workload,
+             "conv1": Conv1Workload, "bf16": Bf16Workload}
 
 
 # ---------------------------------------------------------------------------
@@ -453,6 +753,8 @@ def run_reference(args, wl):
         return 0
     threads = os.cpu_count() or 1
     sample = args.ref_sample or wl.ref_default(args)
+    if hasattr(wl, "cpu_prepare"):
+        wl.cpu_prepare()
     for _ in range(args.warmup):
         wl.cpu_run(sample, threads)
     t0 = time.perf_counter()
@@ -463,7 +765,7 @@ def run_reference(args, wl):
     value = units / dt
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": wl.unit, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": getattr(wl, "dtype", "int8"),
             "data": "synthetic", "config": wl.config(),
             "cpu_baseline": {"value": value, "unit": wl.unit, "cores": threads, "kind": "port",
                              "sample": wl.cpu_sample_desc(sample, threads)},
@@ -598,7 +900,7 @@ def run_gpu(args, wl):
     if rank == 0:
         achieved, kunit, kms, _ = wl.kernel_time(stream, flush, max(3, min(args.steps, 10)))
         del flush
-        peak, peak_src = measure_int8_peak(torch)
+        peak, peak_src = wl.peak(torch) if hasattr(wl, "peak") else measure_int8_peak(torch)
 
     value = ws * wl.units_per_step * args.steps / (ms * 1e-3)
     e2e = ws * wl.units_per_step * args.steps / (ms_e2e * 1e-3)
@@ -606,6 +908,8 @@ def run_gpu(args, wl):
         cpu = None
         if ws == 1 and not args.no_cpu:
             sample = args.cpu_sample or wl.cpu_default(args)
+            if hasattr(wl, "cpu_prepare"):
+                wl.cpu_prepare()
             t0 = time.perf_counter()
             done = wl.cpu_run(sample, 1)
             dt = time.perf_counter() - t0
@@ -614,7 +918,7 @@ def run_gpu(args, wl):
         line = {
             "metric": METRIC, "value": value, "unit": wl.unit, "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "int8", "data": "synthetic", "config": wl.config(),
+            "vs_baseline": None, "dtype": getattr(wl, "dtype", "int8"), "data": "synthetic", "config": wl.config(),
             "parity_spot_check": bool(ok),
             "e2e": {"value": e2e, "unit": wl.unit, "h2d_bytes_per_step": wl.h2d, "d2h_bytes_per_step": wl.d2h,
                     "overlap": "step i+1's host-to-device upload (copy stream) during step i's compute"},
@@ -622,9 +926,10 @@ def run_gpu(args, wl):
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": kunit,
                          "frac": achieved / peak if peak else None, "traffic": load_traffic(wl.name),
                          "kernel": wl.kernel, "kernel_ms_per_launch": kms, "peak_source": peak_src,
-                         "note": "achieved = algorithmic int8 ops (2*MACs) of the dominant kernel's launches / "
-                                 "their CUDA-event time, L2 flushed; clocks sampled during a 1.2 s soak of the "
-                                 "same step around the timed region"},
+                         "note": "achieved = algorithmic ops (2*MACs) of the dominant kernel's launches / "
+                                 "their CUDA-event time in an eager run (kernel launches, not the CUDA-graph "
+                                 "replay that `value` times), L2 flushed; clocks sampled during a 1.2 s soak of "
+                                 "the same step around the timed region"},
             "cpu_baseline": cpu,
             "clocks": clk,
         }
@@ -642,7 +947,7 @@ def run_gpu(args, wl):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="resnet50", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="tosa_b200", choices=["tosa_b200", "reference"])

@@ -557,26 +557,33 @@ void orc_matmul_t_float(int64_t n, int64_t h, int64_t c, int64_t w, int64_t d, c
             }
 }
 
-void orc_matmul_float(int64_t n, int64_t h, int64_t c, int64_t w, const float *a, const float *b,
-                      int out_type, float *out) {
+/* Rows r0..r1 of the flattened [n*h] output rows of a float MATMUL. */
+static void matmul_float_rows(int64_t h, int64_t c, int64_t w, const float *a, const float *b, int out_type,
+                              int64_t r0, int64_t r1, float *out) {
     /* matmul.rs:160-170: operands rounded to the output type; accumulator per
      * output type (F32: AccF32, F16/BF16: rounded sum, unrounded product). */
     int kind = out_type == ORC_F16 ? ACC_F16_UNROUNDED : out_type == ORC_BF16 ? ACC_BF16_UNROUNDED : ACC_F32;
-    for (int64_t bn = 0; bn < n; ++bn)
-        for (int64_t row = 0; row < h; ++row)
-            for (int64_t col = 0; col < w; ++col) {
-                float acc = 0.0f;
-                for (int64_t k = 0; k < c; ++k)
-                    acc = fmac(kind, acc, orc_round_to(out_type, a[(bn * h + row) * c + k]),
-                               orc_round_to(out_type, b[(bn * c + k) * w + col]));
-                out[(bn * h + row) * w + col] = orc_round_to(out_type, acc);
-            }
+    for (int64_t r = r0; r < r1; ++r) {
+        const int64_t bn = r / h;
+        for (int64_t col = 0; col < w; ++col) {
+            float acc = 0.0f;
+            for (int64_t k = 0; k < c; ++k)
+                acc = fmac(kind, acc, orc_round_to(out_type, a[r * c + k]),
+                           orc_round_to(out_type, b[(bn * c + k) * w + col]));
+            out[r * w + col] = orc_round_to(out_type, acc);
+        }
+    }
+}
+
+void orc_matmul_float(int64_t n, int64_t h, int64_t c, int64_t w, const float *a, const float *b,
+                      int out_type, float *out) {
+    matmul_float_rows(h, c, w, a, b, out_type, 0, n * h, out);
 }
 
 /* Multi-threaded drivers for the timed reference arm: rows are split into
  * contiguous chunks; each output element is computed exactly as above. */
 typedef struct {
-    int kind; /* 0 matmul, 1 conv */
+    int kind; /* 0 int matmul, 1 int conv, 2 float matmul */
     int64_t h, c, w;
     const int32_t *a, *b;
     const orc_conv_geom *g;
@@ -584,12 +591,16 @@ typedef struct {
     int64_t bias_len;
     int64_t r0, r1;
     int64_t *out;
+    const float *fa, *fb;
+    int out_type;
+    float *fout;
 } mt_job;
 
 static void *mt_worker(void *p) {
     mt_job *j = (mt_job *)p;
     if (j->kind == 0) matmul_i32_rows(j->h, j->c, j->w, j->a, j->b, j->r0, j->r1, j->out);
-    else conv2d_i32_rows(j->g, j->a, j->b, j->bias, j->bias_len, j->r0, j->r1, j->out);
+    else if (j->kind == 1) conv2d_i32_rows(j->g, j->a, j->b, j->bias, j->bias_len, j->r0, j->r1, j->out);
+    else matmul_float_rows(j->h, j->c, j->w, j->fa, j->fb, j->out_type, j->r0, j->r1, j->fout);
     return NULL;
 }
 
@@ -619,6 +630,15 @@ void orc_matmul_int_mt(int64_t n, int64_t h, int64_t c, int64_t w, const int64_t
     run_mt(&proto, n * h, threads);
     free(av);
     free(bv);
+}
+
+void orc_matmul_float_mt(int64_t n, int64_t h, int64_t c, int64_t w, const float *a, const float *b,
+                         int out_type, float *out, int threads) {
+    mt_job proto;
+    memset(&proto, 0, sizeof proto);
+    proto.kind = 2; proto.h = h; proto.c = c; proto.w = w; proto.fa = a; proto.fb = b;
+    proto.out_type = out_type; proto.fout = out;
+    run_mt(&proto, n * h, threads);
 }
 
 void orc_conv2d_int_mt(const orc_conv_geom *g, const int64_t *input, const int64_t *weight,

@@ -133,6 +133,8 @@ void orc_matmul_t_float(int64_t n, int64_t h, int64_t c, int64_t w, int64_t d, c
  * as the timed CPU reference arm, same arithmetic and loop order per row. */
 void orc_matmul_int_mt(int64_t n, int64_t h, int64_t c, int64_t w, const int64_t *a,
                        const int64_t *b, int64_t a_zp, int64_t b_zp, int64_t *out, int threads);
+void orc_matmul_float_mt(int64_t n, int64_t h, int64_t c, int64_t w, const float *a, const float *b,
+                         int out_type, float *out, int threads);
 void orc_conv2d_int_mt(const orc_conv_geom *g, const int64_t *input, const int64_t *weight,
                        const int64_t *bias, int64_t bias_len, int64_t input_zp, int64_t weight_zp,
                        int64_t *out, int threads);

@@ -108,3 +108,14 @@ def ulp_bf16(x):
     a = np.abs(np.asarray(x, np.float64))
     e = np.floor(np.log2(np.maximum(a, 2.0 ** -126)))
     return 2.0 ** (e - 7)
+
+
+def float_matmul_within_tolerance(got, exp, a, b):
+    """The float MATMUL bound of the parity tests: |got - exp| <= 2 bf16 ULP of exp plus
+    2^-16 * sum_k |a_k * b_k| (an absolute floor near zero, where the tensor cores' and the
+    reference's different accumulation orders make a relative bound meaningless). a [n,h,c],
+    b [n,c,w]. Returns (all within, worst error / tolerance)."""
+    absab = np.einsum("nhc,ncw->nhw", np.abs(a.astype(np.float64)), np.abs(b.astype(np.float64)))
+    tol = 2 * ulp_bf16(exp) + 2.0 ** -16 * absab
+    err = np.abs(got.astype(np.float64) - exp.astype(np.float64))
+    return bool(np.all(err <= tol)), float(np.max(err / np.maximum(tol, 1e-30)))

@@ -177,11 +177,7 @@ def test_matmul_int8_direct_path(ctx, n, h, c, w):
     assert np.array_equal(got.astype(np.int64), H.oracle_matmul_int(a, b, -80, -9))
 
 
-def float_tolerance_ok(got, exp, a, b):
-    absab = np.einsum("nhc,ncw->nhw", np.abs(a.astype(np.float64)), np.abs(b.astype(np.float64)))
-    tol = 2 * H.ulp_bf16(exp) + 2.0 ** -16 * absab
-    err = np.abs(got.astype(np.float64) - exp.astype(np.float64))
-    return bool(np.all(err <= tol)), float(np.max(err / np.maximum(tol, 1e-30)))
+float_tolerance_ok = H.float_matmul_within_tolerance
 
 
 @pytest.mark.parametrize("dt", [L.DT_BF16, L.DT_FP16])

@@ -97,3 +97,60 @@ def test_two_gloo_ranks_shard_and_gather(tmp_path):
     whole, names = _oracle_outputs(graphs.residual_block_int8(batch=batch)[0], images)
     for nm in names:
         assert np.array_equal(got[nm], whole[nm]), nm
+
+
+def _failing_rank_main(rank, world, port, images, result_path):
+    """One rank of a sharded step in which TB_FAULT_SHARD makes shard 1 fail: every rank
+    must end the step with ShardError naming shard 1, and the process group must stay
+    consistent afterwards (a barrier completes)."""
+    import json
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        lo, hi = P.shard_bounds(images.shape[0], world, rank)
+        data, _ = graphs.residual_block_int8(batch=hi - lo)
+        outcome = {"rank": rank}
+        try:
+            P.sharded_step(lambda: _oracle_outputs(data, images[lo:hi]), rank)
+            outcome["error"] = None
+        except P.ShardError as e:
+            outcome["error"] = e.shard
+            outcome["injected"] = isinstance(e.__cause__, P.InjectedFault)
+        dist.barrier()
+        with open(f"{result_path}.{rank}", "w") as f:
+            json.dump(outcome, f)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_failed_shard_ends_the_step_on_every_rank(tmp_path, monkeypatch):
+    import json
+
+    import torch.multiprocessing as mp
+
+    world = 2
+    images = np.random.default_rng(6).integers(-128, 128, (2, 14, 14, 64)).astype(np.int8)
+    path = str(tmp_path / "outcome")
+    monkeypatch.setenv("TB_FAULT_SHARD", "1")  # inherited by the spawned ranks
+    ctx = mp.start_processes(_failing_rank_main, args=(world, _free_port(), images, path), nprocs=world,
+                             start_method="spawn", join=False)
+    import time
+    deadline = time.time() + 120
+    while not ctx.join(timeout=5):
+        assert time.time() < deadline, "ranks did not finish: a rank is waiting on the failed one"
+    outcomes = [json.load(open(f"{path}.{r}")) for r in range(world)]
+    assert [o["error"] for o in outcomes] == [1, 1]   # every rank reports shard 1
+    assert outcomes[1]["injected"] and not outcomes[0]["injected"]
+
+
+def test_sharded_step_without_a_process_group(monkeypatch):
+    monkeypatch.delenv("TB_FAULT_SHARD", raising=False)
+    assert P.sharded_step(lambda: 7, 0) == 7
+    monkeypatch.setenv("TB_FAULT_SHARD", "0")
+    with pytest.raises(P.ShardError) as ei:
+        P.sharded_step(lambda: 7, 0)
+    assert ei.value.shard == 0 and isinstance(ei.value.__cause__, P.InjectedFault)

@@ -19,9 +19,64 @@ Two ways to use it:
 
 from __future__ import annotations
 
+import os
+
 import numpy as np
 
 from . import interpreter as I
+
+
+class ShardError(RuntimeError):
+    """A shard of a data-parallel run failed. `shard` is its index (the rank, or the
+    device slot of a ShardedInterpreter); the run as a whole returns this error (the
+    reference's run_graph returns Err for the batch), after every other shard has
+    finished its own work."""
+
+    def __init__(self, shard: int, msg: str):
+        super().__init__(f"shard {shard}: {msg}")
+        self.shard = shard
+
+
+class InjectedFault(RuntimeError):
+    """The failure TB_FAULT_SHARD asked for."""
+
+
+def injected_shards() -> set:
+    """Shards told to fail by TB_FAULT_SHARD (a comma-separated list of shard indices):
+    host-side fault injection for the failure-handling tests. Nothing on the device is
+    made to fail: the shard raises before its work starts."""
+    spec = os.environ.get("TB_FAULT_SHARD", "").strip()
+    return {int(v) for v in spec.split(",") if v.strip()} if spec else set()
+
+
+def sharded_step(work, rank: int = 0):
+    """Run this rank's share of a one-process-per-GPU step, `work()`, and agree on the
+    outcome: every rank joins one all-reduce of a failure flag whether its work succeeded
+    or not, so a failed shard ends the step on every rank with ShardError and no rank is
+    left waiting in a later collective (every rank takes the same collective steps in the
+    same order). Returns work()'s result."""
+    import torch
+    import torch.distributed as dist
+
+    err = None
+    res = None
+    try:
+        if rank in injected_shards():
+            raise InjectedFault(f"TB_FAULT_SHARD: shard {rank} fails before its run")
+        res = work()
+    except Exception as e:  # the error is this shard's; report it after the agreement
+        err = e
+    failed = rank + 1 if err is not None else 0
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
+        dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+        t = torch.tensor([failed], dtype=torch.int64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        failed = int(t.item())
+    if err is not None:
+        raise ShardError(rank, str(err)) from err
+    if failed:
+        raise ShardError(failed - 1, "failed; this shard's own work finished and was discarded")
+    return res
 
 
 def shard_bounds(batch: int, world: int, rank: int) -> tuple[int, int]:
@@ -119,13 +174,28 @@ class ShardedInterpreter:
                 raise ValueError(f"input {name}: batch {t.shape[0]}, expected {want} x {len(self.devices)} devices")
         shards = split_batch(inputs, len(self.devices))
 
-        def work(it, st, shard):
+        fail = injected_shards()
+
+        def work(k, it, st, shard):
+            if k in fail:
+                raise InjectedFault(f"TB_FAULT_SHARD: shard {k} fails before its run")
             it.bind(shard, stream=st)
             it.execute(stream=st)
             return {name: it.output(name) for name, _, _ in it.outputs()}
 
-        futs = [pool.submit(work, it, st, sh) for pool, it, st, sh in zip(self._pools, self._its, self._streams, shards)]
-        return concat_batch([f.result() for f in futs], self._axes)
+        futs = [pool.submit(work, k, it, st, sh)
+                for k, (pool, it, st, sh) in enumerate(zip(self._pools, self._its, self._streams, shards))]
+        # every shard drains before a failure is reported: no device is left running a shard
+        results, errors = [], []
+        for k, f in enumerate(futs):
+            try:
+                results.append(f.result())
+            except Exception as e:
+                errors.append((k, e))
+        if errors:
+            k, e = errors[0]
+            raise ShardError(k, str(e)) from e
+        return concat_batch(results, self._axes)
 
 
 def run_graph_sharded(data: bytes, inputs: dict, devices, **kw) -> dict:
