@@ -98,6 +98,12 @@ TB_API tb_status tb_malloc(tb_context *ctx, size_t bytes, void **dptr);
 TB_API tb_status tb_free(tb_context *ctx, void *dptr);
 TB_API tb_status tb_memcpy_h2d(tb_context *ctx, void *dst, const void *src, size_t bytes, void *stream);
 TB_API tb_status tb_memcpy_d2h(tb_context *ctx, void *dst, const void *src, size_t bytes, void *stream);
+/* Bound on every in-kernel wait of later launches on this context, in
+ * milliseconds (default 2000, or TB_WAIT_TIMEOUT_MS at context creation). A
+ * wait that gives up makes its kernel unwind (its own copies and MMAs drain
+ * under a separate bound of about a second, tensor memory is released) and
+ * the next tb_synchronize return TB_ERR_TIMEOUT; the context stays usable. */
+TB_API tb_status tb_context_set_wait_timeout_ms(tb_context *ctx, double ms);
 /* Number of kernels this context launched so far (for launch accounting). */
 TB_API uint64_t tb_launch_count(tb_context *ctx);
 /* Diagnostics: in a library built with -DTB_GEMM_TRACE=1 and with TB_TRACE=1
@@ -355,7 +361,11 @@ enum {
 
 /* Parse `data` (Graph::from_flatbuffer, src/ir.rs:592-614) and check that
  * every operator is one the runner executes. Plans, constants and device
- * buffers are prepared on the first tb_graph_run for the bound input shapes. */
+ * buffers are prepared on the first tb_graph_run for the bound input shapes.
+ * Fault injection (tests): with TB_FAULT_ALLOC_FAIL=k in the environment at
+ * load, the k-th device buffer allocation of the graph fails as if the device
+ * were out of memory: the run that needed it returns TB_ERR_CUDA, the buffers
+ * made so far stay with the graph, and a later run allocates the rest. */
 TB_API tb_status tb_graph_load(tb_context *ctx, const void *data, size_t len, uint32_t flags, tb_graph **out);
 TB_API void tb_graph_destroy(tb_graph *graph);
 /* The main block's declared inputs / outputs (name, dtype, declared shape). */

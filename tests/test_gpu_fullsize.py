@@ -1,9 +1,10 @@
 """Parity at the benchmark sizes, and under both forms of the GEMM epilogue.
 
-The tensor-core GEMM gives each tile's epilogue to its two groups of four
-warps in one of two ways: by column halves (few tiles per CTA), or whole tiles
-to the groups in turn (at least 8 tiles per CTA, i.e. only at large batch).
-Small parity shapes never reach the second form on their own, so the first
+The tensor-core GEMM gives each tile's epilogue to its three groups of four
+warps in one of two ways: by column thirds (few tiles per CTA, or tiles of 256
+columns), or whole tiles to the groups in turn (tiles of at most 128 columns,
+several per CTA, i.e. only at large batch). Small parity shapes never reach
+the second form on their own, so the first
 test forces each form (TB_GEMM_EPI_GROUPS at context creation) over the
 output widths and epilogue variants the benchmark graphs use: 32 to 256
 output channels, the fused per-channel RESCALE + CLAMP and the int32 result,
@@ -88,7 +89,7 @@ EPI_CASES = [
 ]
 
 
-@pytest.mark.parametrize("groups", [0, 1], ids=["column_halves", "alternate_tiles"])
+@pytest.mark.parametrize("groups", [0, 1], ids=["column_thirds", "whole_tiles"])
 @pytest.mark.parametrize("case", EPI_CASES, ids=lambda c: "x".join(map(str, c)))
 def test_conv_epilogue_forms(monkeypatch, case, groups):
     n, ih, iw, ic, oc, k, stride, zx, zw = case

@@ -116,6 +116,7 @@ SIGNATURES = [
     ("tb_memcpy_d2h", _I, [_V, _V, _V, ctypes.c_size_t, _V]),
     ("tb_launch_count", ctypes.c_uint64, [_V]),
     ("tb_debug_trace", _I, [_V, _P(ctypes.c_longlong)]),
+    ("tb_context_set_wait_timeout_ms", _I, [_V, ctypes.c_double]),
     ("tb_matmul_plan_create", _I, [_V, _P(MatmulDesc), _P(RescaleAttr), _P(_V)]),
     ("tb_matmul_plan_run", _I, [_V, _V, _V, _V, _V]),
     ("tb_matmul_plan_set_constant_b", _I, [_V, _V, _V]),

@@ -380,13 +380,22 @@ TB_API tb_status tb_context_create(int device, tb_context** out) {
             cudaMemset(ctx->trace, 0, 512 * sizeof(long long));
     }
     // TB_GEMM_EPI_GROUPS=0 / 1: every tensor-core GEMM splits each tile's epilogue by column
-    // halves (0) or gives whole tiles to the two epilogue groups in turn (1), whatever the tile
-    // count (tests run both forms on small shapes)
+    // thirds (0) or, for tiles of at most 128 columns, gives whole tiles to the three epilogue
+    // groups in turn (1), whatever the tile count (tests run both forms on small shapes)
     if (const char* env = getenv("TB_GEMM_EPI_GROUPS")) {
         const int v = atoi(env);
         if (v == 0 || v == 1) ctx->epi_groups = v;
     }
     *out = ctx;
+    return TB_OK;
+}
+
+TB_API tb_status tb_context_set_wait_timeout_ms(tb_context* ctx, double ms) {
+    if (!ctx) return fail(TB_ERR_INVALID_ARGUMENT, "null context");
+    if (!(ms >= 0.0) || ms > 3.6e6) return fail(TB_ERR_INVALID_ARGUMENT, "wait timeout %g ms out of range", ms);
+    int khz = 0;
+    TB_CUDA(cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, ctx->device));
+    ctx->timeout_cycles = static_cast<long long>(ms * 1e-3 * khz * 1e3);
     return TB_OK;
 }
 

@@ -37,6 +37,13 @@ tb_status launch_gemm(tb_context* ctx, const CUtensorMap& tmA, const CUtensorMap
                       cudaStream_t stream) {
     static bool attr_set = false;  // the attribute is per function and process-wide
     if (!attr_set) {
+        // The kernel's warpgroups re-split the registers it was launched with (setmaxnreg); that
+        // needs the full launch allocation, or the epilogue warps would wait for registers forever.
+        cudaFuncAttributes fa;
+        TB_CUDA(cudaFuncGetAttributes(&fa, tc_gemm_kernel<Cfg, EK, EF>));
+        if (fa.numRegs < kLaunchRegs)
+            return fail(TB_ERR_CUDA, "tensor-core GEMM built with %d registers a thread; its register split needs %d",
+                        fa.numRegs, kLaunchRegs);
         TB_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<Cfg, EK, EF>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      Cfg::SMEM_BYTES));
         attr_set = true;
@@ -52,9 +59,12 @@ tb_status launch_gemm(tb_context* ctx, const CUtensorMap& tmA, const CUtensorMap
     p.timeout_cycles = ctx->timeout_cycles;
     p.trace = ctx->trace;
     const int grid = std::min(p.total_tiles, ctx->num_sms);
-    // two epilogue groups on alternate tiles pay off when each CTA has many tiles (measured on
-    // B200: ResNet-50's 56x56 layers and stems gain, 14x14 layers with 2-3 tiles per CTA lose)
-    p.epi_groups = ctx->epi_groups >= 0 ? ctx->epi_groups : (p.total_tiles >= 8 * grid ? 1 : 0);
+    // the three epilogue groups take whole tiles in turn (three TMEM buffers: BN <= 128) when
+    // every CTA has several tiles; otherwise they share each tile by column thirds
+    if (Cfg::kWholeTiles)
+        p.epi_groups = ctx->epi_groups >= 0 ? ctx->epi_groups : (p.total_tiles >= 4 * grid ? 1 : 0);
+    else
+        p.epi_groups = 0;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kGemmThreads);
@@ -80,9 +90,9 @@ tb_status launch_gemm(tb_context* ctx, const CUtensorMap& tmA, const CUtensorMap
     return TB_OK;
 }
 
-constexpr int gemm_stages(int bn, int bk) { return (196608 / ((128 + bn) * bk)) < 8 ? (196608 / ((128 + bn) * bk)) : 8; }
+constexpr int gemm_stages(int bn, int bk) { return (kStageBudget / ((128 + bn) * bk)) < 8 ? (kStageBudget / ((128 + bn) * bk)) : 8; }
 // Stages with two taps per stage (A: two 64-byte boxes, B: one 128-byte box).
-constexpr int gemm_stages_tap2(int bn) { return (196608 / ((128 + bn) * 128)) < 8 ? (196608 / ((128 + bn) * 128)) : 8; }
+constexpr int gemm_stages_tap2(int bn) { return (kStageBudget / ((128 + bn) * 128)) < 8 ? (kStageBudget / ((128 + bn) * 128)) : 8; }
 
 // Epilogue kind for a prepared epilogue.
 inline int epilogue_kind(const GemmEpilogue& e) {

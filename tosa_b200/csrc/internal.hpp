@@ -26,7 +26,7 @@ struct tb_context {
     long long timeout_cycles = 0;    // bound on every in-kernel wait
     uint64_t launches = 0;
     long long* trace = nullptr;      // optional GEMM timeline buffer (TB_TRACE=1, TB_GEMM_TRACE builds)
-    int epi_groups = -1;             // TB_GEMM_EPI_GROUPS: 0 / 1 force the GEMM epilogue split, -1 by tile count
+    int epi_groups = -1;             // TB_GEMM_EPI_GROUPS: 0 / 1 force the GEMM epilogue form, -1 by tile count
 };
 
 namespace tb {

@@ -21,6 +21,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <deque>
 #include <memory>
@@ -207,6 +208,8 @@ struct tb_graph {
     std::vector<int> unexecuted;     // ops the order never reaches
     int stop_at = -1;                // position in `order` of the first compile error
     std::vector<void*> buffers;
+    int fault_alloc = 0;             // TB_FAULT_ALLOC_FAIL: fail this buffer allocation (1-based), 0 = never
+    int allocs = 0;                  // buffer allocations attempted so far
 
     std::vector<cudaEvent_t> op_events;   // TB_GRAPH_TIME_OPS: start/stop pair per operator
     std::vector<float> op_ms;             // device time per operator index of the last run (-1: no kernel)
@@ -1213,6 +1216,8 @@ tb_status do_compile(tb_graph* G) {
         if (al != C.alias_of.end()) continue;
         const size_t bytes = std::max<size_t>(t.dev_bytes(), 16);
         void* p = nullptr;
+        if (++G->allocs == G->fault_alloc)
+            return fail(TB_ERR_CUDA, "graph buffer allocation (%zu bytes) failed: injected by TB_FAULT_ALLOC_FAIL", bytes);
         cudaError_t e = cudaMalloc(&p, bytes);
         if (e != cudaSuccess) return fail(TB_ERR_CUDA, "graph buffer allocation (%zu bytes) failed: %s", bytes,
                                           cudaGetErrorString(e));
@@ -1375,6 +1380,7 @@ extern "C" TB_API tb_status tb_graph_load(tb_context* ctx, const void* data, siz
     std::unique_ptr<tb_graph> g(new tb_graph);
     g->ctx = ctx;
     g->flags = flags;
+    if (const char* ev = std::getenv("TB_FAULT_ALLOC_FAIL")) g->fault_alloc = std::max(0, std::atoi(ev));
     std::string err;
     if (!fb::parse_graph(static_cast<const uint8_t*>(data), len, &g->g, &err))
         return fail(TB_ERR_DESERIALIZE, "%s", err.c_str());

@@ -1,24 +1,29 @@
 // Persistent warp-specialised tcgen05 GEMM / implicit-GEMM convolution for
 // sm_100a with a fused TOSA epilogue.
 //
-// One CTA per SM (384 threads, 12 warps):
+// One CTA per SM (512 threads, 16 warps):
 //   warp 0      TMA producer: A tiles (plain 3-D tiles, or im2col windows of
 //               an NHWC activation for CONV2D) and B tiles into a STAGES-deep
 //               shared-memory ring; no multicast.
 //   warp 1      TMEM owner and MMA issuer: tcgen05.mma (kind::i8 -> s32, or
-//               kind::f16 -> f32) into one of two 128 x BN accumulators.
+//               kind::f16 -> f32) into one of the 128 x BN accumulators.
 //   warps 2-3   zero-point row sums: when the B-side zero point is non-zero,
 //               sum every A row of each stage from shared memory (dp4a, bank-
 //               conflict-free chunk order) so the epilogue can apply
 //               -zp_b * rowsum(A). 64 rows per warp.
-//   warps 4-11  epilogue, two warps per SM sub-partition in two groups of four:
-//               group (w-4)/4 takes the tiles of its parity (its accumulator
-//               buffer), warp w reads TMEM lanes 32*(w%4)..+31 (one output row
-//               per thread) and every column of the tile; the next columns are
-//               loaded from TMEM while the current ones are processed.
+//   warps 4-15  epilogue, three warps per SM sub-partition in three groups of
+//               four (one warp per TMEM lane quadrant: warp w reads lanes
+//               32*(w%4)..+31, one output row per thread); with several tiles
+//               per CTA and BN <= 128 group (w-4)/4 takes every third tile and
+//               all its columns, otherwise the groups share every tile by
+//               column thirds; the next columns are loaded from TMEM while the
+//               current ones are processed.
+// Warpgroup 0 needs few registers: it hands most of them to the epilogue
+// warpgroups (setmaxnreg), whose arithmetic needs them.
 //
-// The accumulator is double-buffered in TMEM, so the epilogue of tile t
-// overlaps the main loop of tile t+1 and the epilogue of tile t-1 (the other group). All waits are bounded: a wait that
+// The accumulator has three (whole tiles per group) or two buffers in TMEM, so
+// the epilogue of a tile overlaps the main loop of the next one and the
+// epilogues of the tiles before it. All waits are bounded: a wait that
 // gives up sets DEV_ERR_TIMEOUT in the device error word and the CTA unwinds.
 //
 // Arithmetic contract (integer): the tensor core forms sum(a*b) over raw
@@ -67,8 +72,26 @@ enum : int {
     EK_FCONV = 7,      // float convolution: round(round(acc) + bias) to the output type
 };
 
-constexpr int kGemmThreads = 384;
-constexpr int kEpiWarps = 8;
+// 16 warps: warpgroup 0 = TMA producer, MMA issuer and two row-sum warps; warpgroups 1-3 =
+// 12 epilogue warps in three groups of four (one warp per TMEM lane quadrant). Launched with
+// 128 registers a thread (65,536 for the CTA); warpgroup 0 gives back down to kRoleRegs and
+// the epilogue warpgroups take up to kEpiRegs: 128 * kRoleRegs + 384 * kEpiRegs = 65,536.
+constexpr int kGemmThreads = 512;
+constexpr int kEpiWarps = 12;
+constexpr int kEpiGroups = 3;
+constexpr int kLaunchRegs = 128;
+constexpr int kRoleRegs = 56;
+constexpr int kEpiRegs = 152;
+static_assert(128 * kRoleRegs + 384 * kEpiRegs <= kGemmThreads * kLaunchRegs, "register split above the launch total");
+// Shared memory per CTA: the stage ring, then 1 KB of alignment slack, the barriers and row
+// sums, and the epilogue scratch (column-sum reduction and staged column constants, 12 KB,
+// then a 2 KB output staging buffer per epilogue warp).
+constexpr int kSmemLimit = 232448;
+constexpr int kBarrierBytes = 3072;
+constexpr int kScratchBytes = 12288 + 2048 * kEpiWarps;
+constexpr int kStageBudget = kSmemLimit - 1024 - kBarrierBytes - kScratchBytes;
+// Bound (clock cycles) on a CTA's final waits for its own TMA loads and MMAs.
+constexpr long long kDrainCycles = 2000000000ll;
 
 struct GemmEpilogue {
     int mode;                  // EPI_*
@@ -196,11 +219,13 @@ struct GemmCfg {
     // MN-major B: 128-byte rows of N, one box per 128 bytes of N.
     static constexpr int B_MN_CHUNK = 128 / kElem;                  // N elements per box
     static constexpr int B_MN_BOX_BYTES = BK * 128;                 // BK k-rows x 128 bytes
-    static constexpr int TMEM_COLS = 2 * BN <= 32 ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
-    // epilogue: column-sum reduction and staged per-tile column constants (12 KB), then a 2 KB
-    // output staging buffer per epilogue warp (16 KB)
-    static constexpr int SCRATCH_BYTES = 12288 + 16384;
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 2048 /*barriers, row sums*/ + SCRATCH_BYTES;
+    // accumulator buffers in TMEM (512 columns): three when the epilogue groups take whole tiles
+    // in turn (BN <= 128 only), otherwise two
+    static constexpr bool kWholeTiles = BN <= 128;
+    static constexpr int kTmemNeed = kWholeTiles ? 3 * BN : 2 * BN;
+    static constexpr int TMEM_COLS = kTmemNeed <= 32 ? 32 : (kTmemNeed <= 64 ? 64 : (kTmemNeed <= 128 ? 128 : (kTmemNeed <= 256 ? 256 : 512)));
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + kBarrierBytes + kScratchBytes;
+    static_assert(SMEM_BYTES <= kSmemLimit, "shared memory above 227 KB");
     static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "UMMA N for M=128; each epilogue warp walks pairs of 16-column chunks");
     static_assert(!B_MN_MAJOR || BK_BYTES == 128, "MN-major B uses 128-byte K blocks");
     static_assert(!TAP2 || (KIND == 0 && IM2COL && BK_BYTES == 64), "two taps per stage: int8 im2col, 64 channels");
@@ -465,8 +490,8 @@ __device__ __forceinline__ void fast_chunk_i8(const GemmParams& p, const uint32_
 // packing into the warp's shared staging buffer, and row-contiguous stores of 64-byte groups.
 struct FastTile {
     uint32_t taddr;         // TMEM address of the warp's first column (lane quadrant in the high half)
-    int cols;               // columns of the tile this warp covers (BN or BN / 2)
-    int n_end;              // of them, the ones that exist (N - first column)
+    int cols;               // columns of the tile this warp covers (BN, or its share of a tile)
+    int n_end;              // of them, the ones that exist (at most cols, and N - first column)
     int nb;                 // absolute output column of the warp's first column
     int32_t rowterm;
     const int32_t* cst_n;   // staged column terms, indexed by absolute column
@@ -537,7 +562,8 @@ __device__ __forceinline__ void fast_tile_pass(const GemmParams& p, const FastCo
             const uint4 pv = h.wst[r * 4 + (k ^ ((r >> 1) & 3))];
             const int mr = h.mrow0 + r;
             const int n = h.nb + g0 + k * kChunk;
-            if (mr < p.M && n < p.N) {
+            // only this pass's columns: a group's share of a tile can end before N (column thirds)
+            if (mr < p.M && g0 + k * kChunk < h.n_end) {
                 int8_t* o = h.obase + static_cast<long long>(mr) * p.ldo + n;
                 if (h.vec_ok && n + kChunk <= p.N) {
                     *reinterpret_cast<uint4*>(o) = pv;
@@ -571,29 +597,37 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::STAGE_BYTES);
     uint64_t* full = bars;               // [S]
     uint64_t* empty = bars + S;          // [S]
-    uint64_t* tfull = bars + 2 * S;      // [2]
-    uint64_t* tempty = bars + 2 * S + 2; // [2]
-    uint64_t* rsfull = bars + 2 * S + 4; // [2]
-    uint64_t* rsempty = bars + 2 * S + 6;// [2]
-    uint64_t* mdrain = bars + 2 * S + 8; // [1]
-    uint64_t* ebar = bars + 2 * S + 9;   // [1] epilogue-group barrier (8 warps)
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 10);
+    // TMEM accumulator buffers: with whole tiles per group (p.epi_groups) tile t takes buffer
+    // t % 3 and is processed by group t % 3, so each group waits for consecutive phases of its
+    // own buffer's barriers; otherwise every tile is shared by the groups (column thirds) and
+    // two buffers alternate. Either way no waiter is ever more than one phase ahead.
+    const int NB = p.epi_groups ? kEpiGroups : 2;
+    uint64_t* tfull = bars + 2 * S;      // [3]
+    uint64_t* tempty = tfull + 3;        // [3]
+    uint64_t* rsfull = tempty + 3;       // [3]
+    uint64_t* rsempty = rsfull + 3;      // [3]
+    uint64_t* mdrain = rsempty + 3;      // [1]
+    uint64_t* ebar = mdrain + 1;         // [1] barrier of the 12 epilogue warps
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ebar + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    int32_t* rowsum_buf = reinterpret_cast<int32_t*>(tmem_slot + 4);  // [2][128]
-    int32_t* scratch = reinterpret_cast<int32_t*>(smem + S * Cfg::STAGE_BYTES + 2048);  // SCRATCH_BYTES
+    int32_t* rowsum_buf = reinterpret_cast<int32_t*>(tmem_slot + 4);  // [3][128]
+    int32_t* scratch = reinterpret_cast<int32_t*>(smem + S * Cfg::STAGE_BYTES + kBarrierBytes);  // kScratchBytes
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const bool need_rowsum = Cfg::kKind == 0 && p.epi.row_zp_neg != 0;
 
-    // epilogue warps that release each accumulator buffer: 4 (the owning group) or all 8
-    const uint32_t epi_arrivals = p.epi_groups ? kEpiWarps / 2 : kEpiWarps;
+    // epilogue warps that release each accumulator buffer: the 4 of the group that took the
+    // tile, or those of the groups that have a share of its columns (32-column chunks split in
+    // thirds: with BN 64 group 0 has none)
+    const int n_chunks = BN / 32;
+    const uint32_t epi_arrivals = p.epi_groups ? 4 : 4 * (n_chunks < kEpiGroups ? n_chunks : kEpiGroups);
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], need_rowsum ? 3 : 1);  // MMA commit + two row-sum warps
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < NB; ++b) {
             mbar_init(&tfull[b], 1);
             mbar_init(&tempty[b], epi_arrivals);
             mbar_init(&rsfull[b], 2);
@@ -617,203 +651,216 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     const long long limit = p.timeout_cycles;
+    // waits for this CTA's own copies and MMAs before it exits get a fixed, generous bound (about
+    // a second), whatever the configured timeout: they end once work already issued completes
+    const long long drain_limit = limit > kDrainCycles ? limit : kDrainCycles;
     if (kGemmTrace && p.trace && blockIdx.x == 0 && threadIdx.x == 0) p.trace[400] = clock64();
 
-    if (warp == 0) {
-        // ------------------------------------------------------------ producer
-        if (lane == 0) {
-            uint32_t it = 0;
-            bool ok = true;
-            for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
-                int b, mt, nt;
-                tile_coords(p, tile, b, mt, nt);
-                const int m0 = mt * BM, n0 = nt * BN;
-                int img = 0, wb = 0, hb = 0;
-                if constexpr (Cfg::kIm2col) {
-                    img = fdiv(m0, p.fd_ohow);
-                    const int rem = m0 - img * p.conv_OHOW;
-                    const int oy = fdiv(rem, p.fd_ow), ox = rem - oy * p.conv_OW;
-                    wb = ox * p.stride_w - p.pad_l;
-                    hb = oy * p.stride_h - p.pad_t;
-                }
-                int cb = 0, kx = 0, ky = 0, tap = 0;  // k block kb = (ky * KW + kx) * c_blocks + cb, stepped
-                for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
-                    const int s = it % S;
-                    const uint32_t ph = (it / S) & 1;
-                    if (!mbar_wait_bounded(&empty[s], ph ^ 1, abort_flag, limit)) { ok = false; break; }
-                    uint8_t* sa = stage_base + s * Cfg::STAGE_BYTES;
-                    uint8_t* sb = sa + Cfg::A_BYTES;
-                    if (kGemmTrace && p.trace && blockIdx.x == 0 && it < 128) p.trace[it] = clock64();
-                    if constexpr (Cfg::kTap2) {
-                        // taps tap and tap + 1 (the last stage of an odd tap count has one; the B box's
-                        // second half then lies past K and is filled with zeros)
-                        const bool two = tap + 1 < p.taps;
-                        mbar_arrive_expect_tx(&full[s], two ? Cfg::STAGE_BYTES : Cfg::STAGE_BYTES - Cfg::A_SUB);
-                        tma_load_im2col_4d(sa, &tmA, &full[s], 0, wb, hb, img, static_cast<uint16_t>(kx * p.dil_w),
-                                           static_cast<uint16_t>(ky * p.dil_h));
-                        tma_load_3d(sb, &tmB, &full[s], tap * p.IC, n0, 0);
-                        ++tap;
-                        if (++kx == p.KW) {
-                            kx = 0;
-                            ++ky;
-                        }
-                        if (two) {
-                            tma_load_im2col_4d(sa + Cfg::A_SUB, &tmA, &full[s], 0, wb, hb, img,
-                                               static_cast<uint16_t>(kx * p.dil_w), static_cast<uint16_t>(ky * p.dil_h));
-                            ++tap;
-                            if (++kx == p.KW) {
-                                kx = 0;
-                                ++ky;
-                            }
-                        }
-                        continue;
-                    }
-                    mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
+    if (warp < 4) {
+        // warpgroup 0: producer, MMA issuer, row sums -- few registers, the rest to the epilogue
+        setmaxnreg_dec<kRoleRegs>();
+        if (warp == 0) {
+            // ------------------------------------------------------------ producer
+            if (lane == 0) {
+                uint32_t it = 0;
+                bool ok = true;
+                for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
+                    int b, mt, nt;
+                    tile_coords(p, tile, b, mt, nt);
+                    const int m0 = mt * BM, n0 = nt * BN;
+                    int img = 0, wb = 0, hb = 0;
                     if constexpr (Cfg::kIm2col) {
-                        tma_load_im2col_4d(sa, &tmA, &full[s], cb * Cfg::BK, wb, hb, img,
-                                           static_cast<uint16_t>(kx * p.dil_w), static_cast<uint16_t>(ky * p.dil_h));
-                        tma_load_3d(sb, &tmB, &full[s], tap * p.IC + cb * Cfg::BK, n0, 0);
-                        if (++cb == p.c_blocks) {
-                            cb = 0;
+                        img = fdiv(m0, p.fd_ohow);
+                        const int rem = m0 - img * p.conv_OHOW;
+                        const int oy = fdiv(rem, p.fd_ow), ox = rem - oy * p.conv_OW;
+                        wb = ox * p.stride_w - p.pad_l;
+                        hb = oy * p.stride_h - p.pad_t;
+                    }
+                    int cb = 0, kx = 0, ky = 0, tap = 0;  // k block kb = (ky * KW + kx) * c_blocks + cb, stepped
+                    for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+                        const int s = it % S;
+                        const uint32_t ph = (it / S) & 1;
+                        if (!mbar_wait_bounded(&empty[s], ph ^ 1, abort_flag, limit)) { ok = false; break; }
+                        uint8_t* sa = stage_base + s * Cfg::STAGE_BYTES;
+                        uint8_t* sb = sa + Cfg::A_BYTES;
+                        if (kGemmTrace && p.trace && blockIdx.x == 0 && it < 128) p.trace[it] = clock64();
+                        if constexpr (Cfg::kTap2) {
+                            // taps tap and tap + 1 (the last stage of an odd tap count has one; the B box's
+                            // second half then lies past K and is filled with zeros)
+                            const bool two = tap + 1 < p.taps;
+                            mbar_arrive_expect_tx(&full[s], two ? Cfg::STAGE_BYTES : Cfg::STAGE_BYTES - Cfg::A_SUB);
+                            tma_load_im2col_4d(sa, &tmA, &full[s], 0, wb, hb, img, static_cast<uint16_t>(kx * p.dil_w),
+                                               static_cast<uint16_t>(ky * p.dil_h));
+                            tma_load_3d(sb, &tmB, &full[s], tap * p.IC, n0, 0);
                             ++tap;
                             if (++kx == p.KW) {
                                 kx = 0;
                                 ++ky;
                             }
+                            if (two) {
+                                tma_load_im2col_4d(sa + Cfg::A_SUB, &tmA, &full[s], 0, wb, hb, img,
+                                                   static_cast<uint16_t>(kx * p.dil_w), static_cast<uint16_t>(ky * p.dil_h));
+                                ++tap;
+                                if (++kx == p.KW) {
+                                    kx = 0;
+                                    ++ky;
+                                }
+                            }
+                            continue;
                         }
-                    } else {
-                        tma_load_3d(sa, &tmA, &full[s], kb * Cfg::BK, m0, b);
-                        if constexpr (Cfg::kBMN) {
-#pragma unroll
-                            for (int j = 0; j < BN / Cfg::B_MN_CHUNK; ++j)
-                                tma_load_3d(sb + j * Cfg::B_MN_BOX_BYTES, &tmB, &full[s], n0 + j * Cfg::B_MN_CHUNK,
-                                            kb * Cfg::BK, b);
+                        mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
+                        if constexpr (Cfg::kIm2col) {
+                            tma_load_im2col_4d(sa, &tmA, &full[s], cb * Cfg::BK, wb, hb, img,
+                                               static_cast<uint16_t>(kx * p.dil_w), static_cast<uint16_t>(ky * p.dil_h));
+                            tma_load_3d(sb, &tmB, &full[s], tap * p.IC + cb * Cfg::BK, n0, 0);
+                            if (++cb == p.c_blocks) {
+                                cb = 0;
+                                ++tap;
+                                if (++kx == p.KW) {
+                                    kx = 0;
+                                    ++ky;
+                                }
+                            }
                         } else {
-                            tma_load_3d(sb, &tmB, &full[s], kb * Cfg::BK, n0, p.b_bcast ? 0 : b);
+                            tma_load_3d(sa, &tmA, &full[s], kb * Cfg::BK, m0, b);
+                            if constexpr (Cfg::kBMN) {
+    #pragma unroll
+                                for (int j = 0; j < BN / Cfg::B_MN_CHUNK; ++j)
+                                    tma_load_3d(sb + j * Cfg::B_MN_BOX_BYTES, &tmB, &full[s], n0 + j * Cfg::B_MN_CHUNK,
+                                                kb * Cfg::BK, b);
+                            } else {
+                                tma_load_3d(sb, &tmB, &full[s], kb * Cfg::BK, n0, p.b_bcast ? 0 : b);
+                            }
                         }
                     }
                 }
+                if (!ok) { atomicOr(p.err, DEV_ERR_TIMEOUT); *abort_flag = 1; }
+                // Drain: every issued load must land before the CTA may exit.
+                const uint32_t first = it > static_cast<uint32_t>(S) ? it - S : 0;
+                for (uint32_t i = first; i < it; ++i)
+                    mbar_wait_bounded(&full[i % S], (i / S) & 1, nullptr, drain_limit);
             }
-            if (!ok) { atomicOr(p.err, DEV_ERR_TIMEOUT); *abort_flag = 1; }
-            // Drain: every issued load must land before the CTA may exit.
-            const uint32_t first = it > static_cast<uint32_t>(S) ? it - S : 0;
-            for (uint32_t i = first; i < it; ++i) mbar_wait_bounded(&full[i % S], (i / S) & 1, nullptr, limit);
-        }
-    } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            const uint32_t idesc = Cfg::kKind == 0 ? idesc_i8(BM, BN, Cfg::kBMN)
-                                                   : idesc_f16(BM, BN, p.in_bf16 != 0, Cfg::kBMN);
-            uint32_t it = 0, tcount = 0;
-            bool ok = true;
-            for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++tcount) {
-                const int buf = tcount & 1;
-                const uint32_t tph = (tcount >> 1) & 1;
-                if (!mbar_wait_bounded(&tempty[buf], tph ^ 1, abort_flag, limit)) { ok = false; break; }
-                tc_fence_after();
-                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * BN);
-                for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
-                    const int s = it % S;
-                    const uint32_t ph = (it / S) & 1;
-                    if (!mbar_wait_bounded(&full[s], ph, abort_flag, limit)) { ok = false; break; }
+        } else if (warp == 1) {
+            // ------------------------------------------------------------ MMA issuer
+            if (lane == 0) {
+                const uint32_t idesc = Cfg::kKind == 0 ? idesc_i8(BM, BN, Cfg::kBMN)
+                                                       : idesc_f16(BM, BN, p.in_bf16 != 0, Cfg::kBMN);
+                uint32_t it = 0, tcount = 0;
+                bool ok = true;
+                for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++tcount) {
+                    const int buf = tcount % NB;
+                    const uint32_t tph = (tcount / NB) & 1;
+                    if (!mbar_wait_bounded(&tempty[buf], tph ^ 1, abort_flag, limit)) { ok = false; break; }
                     tc_fence_after();
-                    if (kGemmTrace && p.trace && blockIdx.x == 0 && it < 128) p.trace[128 + it] = clock64();
-                    const uint32_t sa = smem_u32(stage_base + s * Cfg::STAGE_BYTES);
-                    const uint32_t sb = sa + Cfg::A_BYTES;
-#pragma unroll
-                    for (int k = 0; k < Cfg::kBKBytesB / 32; ++k) {
-                        // two taps per stage: k-steps 0-1 read A sub-tile 0, 2-3 sub-tile 1 (its stale
-                        // contents meet zero weights in a one-tap stage)
-                        const uint32_t a_k = Cfg::kTap2 ? sa + (k >> 1) * Cfg::A_SUB + (k & 1) * 32 : sa + k * 32;
-                        const uint64_t ad = smem_desc(a_k, 16, Cfg::ATOM_SBO, Cfg::SW_CODE);
-                        uint64_t bd;
-                        if constexpr (Cfg::kBMN) {
-                            // k-rows of 128 bytes; 8-row groups 1024 B apart; 128-byte N chunks one box apart.
-                            bd = smem_desc(sb + k * Cfg::kMmaK * 128, Cfg::B_MN_BOX_BYTES, 1024, 2);
-                        } else {
-                            bd = smem_desc(sb + k * 32, 16, Cfg::ATOM_SBO_B, Cfg::SW_CODE_B);
+                    const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * BN);
+                    for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+                        const int s = it % S;
+                        const uint32_t ph = (it / S) & 1;
+                        if (!mbar_wait_bounded(&full[s], ph, abort_flag, limit)) { ok = false; break; }
+                        tc_fence_after();
+                        if (kGemmTrace && p.trace && blockIdx.x == 0 && it < 128) p.trace[128 + it] = clock64();
+                        const uint32_t sa = smem_u32(stage_base + s * Cfg::STAGE_BYTES);
+                        const uint32_t sb = sa + Cfg::A_BYTES;
+    #pragma unroll
+                        for (int k = 0; k < Cfg::kBKBytesB / 32; ++k) {
+                            // two taps per stage: k-steps 0-1 read A sub-tile 0, 2-3 sub-tile 1 (its stale
+                            // contents meet zero weights in a one-tap stage)
+                            const uint32_t a_k = Cfg::kTap2 ? sa + (k >> 1) * Cfg::A_SUB + (k & 1) * 32 : sa + k * 32;
+                            const uint64_t ad = smem_desc(a_k, 16, Cfg::ATOM_SBO, Cfg::SW_CODE);
+                            uint64_t bd;
+                            if constexpr (Cfg::kBMN) {
+                                // k-rows of 128 bytes; 8-row groups 1024 B apart; 128-byte N chunks one box apart.
+                                bd = smem_desc(sb + k * Cfg::kMmaK * 128, Cfg::B_MN_BOX_BYTES, 1024, 2);
+                            } else {
+                                bd = smem_desc(sb + k * 32, 16, Cfg::ATOM_SBO_B, Cfg::SW_CODE_B);
+                            }
+                            tc_mma<Cfg::kKind>(d_tmem, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
                         }
-                        tc_mma<Cfg::kKind>(d_tmem, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                        tc_commit(&empty[s]);  // frees the stage once these MMAs have read it
                     }
-                    tc_commit(&empty[s]);  // frees the stage once these MMAs have read it
+                    if (!ok) break;
+                    tc_commit(&tfull[buf]);    // accumulator ready for the epilogue
                 }
-                if (!ok) break;
-                tc_commit(&tfull[buf]);    // accumulator ready for the epilogue
-            }
-            if (!ok) {
-                atomicOr(p.err, DEV_ERR_TIMEOUT);
-                *abort_flag = 1;
-                // Let every issued MMA finish before TMEM is released.
+                if (!ok) {
+                    atomicOr(p.err, DEV_ERR_TIMEOUT);
+                    *abort_flag = 1;
+                }
+                // Every issued MMA finishes before TMEM is released (also when the epilogue gave up
+                // on tiles whose MMAs are still running).
                 tc_commit(&mdrain[0]);
-                mbar_wait_bounded(&mdrain[0], 0, nullptr, limit);
+                mbar_wait_bounded(&mdrain[0], 0, nullptr, drain_limit);
             }
-        }
-    } else if (warp == 2 || warp == 3) {
-        // ------------------------------------------------------------ A row sums (int8, zp_b != 0)
-        if (need_rowsum) {
-            const int row0 = (warp - 2) * 64;
-            uint32_t it = 0, tcount = 0;
-            bool ok = true;
-            for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++tcount) {
-                int sum0 = 0, sum1 = 0;
-                for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
-                    const int s = it % S;
-                    const uint32_t ph = (it / S) & 1;
-                    if (!mbar_wait_bounded(&full[s], ph, abort_flag, limit)) { ok = false; break; }
-                    const uint8_t* sa0 = stage_base + s * Cfg::STAGE_BYTES;
-                    // two taps per stage: the second sub-tile holds data only when the stage has two taps
-                    const int subs = Cfg::kTap2 && 2 * kb + 1 < p.taps ? 2 : 1;
-                    for (int sub = 0; sub < subs; ++sub) {
-                    const uint8_t* sa = sa0 + sub * Cfg::A_SUB;
-                    const int4* r0 = reinterpret_cast<const int4*>(sa + (row0 + lane) * Cfg::kBKBytes);
-                    const int4* r1 = reinterpret_cast<const int4*>(sa + (row0 + 32 + lane) * Cfg::kBKBytes);
-                    // Chunk order rotated per lane: the 8 lanes of a shared-memory phase hit 8 different
-                    // 16-byte bank groups (rows are 128 or 64 bytes long).
-                    const int rot = Cfg::kBKBytes == 128 ? (lane & 7) : ((lane >> 1) & 3);
-#pragma unroll
-                    for (int c = 0; c < Cfg::kBKBytes / 16; ++c) {
-                        const int cc = c ^ rot;
-                        const int4 v0 = r0[cc];
-                        const int4 v1 = r1[cc];
-                        sum0 = __dp4a(v0.x, 0x01010101, sum0);
-                        sum0 = __dp4a(v0.y, 0x01010101, sum0);
-                        sum0 = __dp4a(v0.z, 0x01010101, sum0);
-                        sum0 = __dp4a(v0.w, 0x01010101, sum0);
-                        sum1 = __dp4a(v1.x, 0x01010101, sum1);
-                        sum1 = __dp4a(v1.y, 0x01010101, sum1);
-                        sum1 = __dp4a(v1.z, 0x01010101, sum1);
-                        sum1 = __dp4a(v1.w, 0x01010101, sum1);
+        } else {
+            // ------------------------------------------------------------ A row sums (int8, zp_b != 0)
+            if (need_rowsum) {
+                const int row0 = (warp - 2) * 64;
+                uint32_t it = 0, tcount = 0;
+                bool ok = true;
+                for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++tcount) {
+                    int sum0 = 0, sum1 = 0;
+                    for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+                        const int s = it % S;
+                        const uint32_t ph = (it / S) & 1;
+                        if (!mbar_wait_bounded(&full[s], ph, abort_flag, limit)) { ok = false; break; }
+                        const uint8_t* sa0 = stage_base + s * Cfg::STAGE_BYTES;
+                        // two taps per stage: the second sub-tile holds data only when the stage has two taps
+                        const int subs = Cfg::kTap2 && 2 * kb + 1 < p.taps ? 2 : 1;
+                        for (int sub = 0; sub < subs; ++sub) {
+                        const uint8_t* sa = sa0 + sub * Cfg::A_SUB;
+                        const int4* r0 = reinterpret_cast<const int4*>(sa + (row0 + lane) * Cfg::kBKBytes);
+                        const int4* r1 = reinterpret_cast<const int4*>(sa + (row0 + 32 + lane) * Cfg::kBKBytes);
+                        // Chunk order rotated per lane: the 8 lanes of a shared-memory phase hit 8 different
+                        // 16-byte bank groups (rows are 128 or 64 bytes long).
+                        const int rot = Cfg::kBKBytes == 128 ? (lane & 7) : ((lane >> 1) & 3);
+    #pragma unroll
+                        for (int c = 0; c < Cfg::kBKBytes / 16; ++c) {
+                            const int cc = c ^ rot;
+                            const int4 v0 = r0[cc];
+                            const int4 v1 = r1[cc];
+                            sum0 = __dp4a(v0.x, 0x01010101, sum0);
+                            sum0 = __dp4a(v0.y, 0x01010101, sum0);
+                            sum0 = __dp4a(v0.z, 0x01010101, sum0);
+                            sum0 = __dp4a(v0.w, 0x01010101, sum0);
+                            sum1 = __dp4a(v1.x, 0x01010101, sum1);
+                            sum1 = __dp4a(v1.y, 0x01010101, sum1);
+                            sum1 = __dp4a(v1.z, 0x01010101, sum1);
+                            sum1 = __dp4a(v1.w, 0x01010101, sum1);
+                        }
+                        }
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&empty[s]);
+                        if (kGemmTrace && p.trace && blockIdx.x == 0 && it < 128 && warp == 2 && lane == 0) p.trace[256 + it] = clock64();
                     }
-                    }
+                    if (!ok) break;
+                    const int buf = tcount % NB;
+                    const uint32_t tph = (tcount / NB) & 1;
+                    if (!mbar_wait_bounded(&rsempty[buf], tph ^ 1, abort_flag, limit)) { ok = false; break; }
+                    rowsum_buf[buf * 128 + row0 + lane] = sum0;
+                    rowsum_buf[buf * 128 + row0 + 32 + lane] = sum1;
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&empty[s]);
-                    if (kGemmTrace && p.trace && blockIdx.x == 0 && it < 128 && warp == 2 && lane == 0) p.trace[256 + it] = clock64();
+                    if (lane == 0) mbar_arrive(&rsfull[buf]);
                 }
-                if (!ok) break;
-                const int buf = tcount & 1;
-                const uint32_t tph = (tcount >> 1) & 1;
-                if (!mbar_wait_bounded(&rsempty[buf], tph ^ 1, abort_flag, limit)) { ok = false; break; }
-                rowsum_buf[buf * 128 + row0 + lane] = sum0;
-                rowsum_buf[buf * 128 + row0 + 32 + lane] = sum1;
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&rsfull[buf]);
+                if (!ok && lane == 0) { atomicOr(p.err, DEV_ERR_TIMEOUT); *abort_flag = 1; }
             }
-            if (!ok && lane == 0) { atomicOr(p.err, DEV_ERR_TIMEOUT); *abort_flag = 1; }
         }
     } else {
-        // ------------------------------------------------------------ epilogue (warps 4..11)
-        // Two groups of 4 warps (one per TMEM lane quadrant). With p.epi_groups (many tiles per
-        // CTA) group g takes the tiles with tcount % 2 == g (accumulator buffer g) and every
-        // column of them, so one group's per-tile waits overlap the other group's work;
-        // otherwise both groups share every tile, group g taking half g of its columns.
+        setmaxnreg_inc<kEpiRegs>();
+        // ------------------------------------------------------------ epilogue (warps 4..15)
+        // Three groups of 4 warps (one per TMEM lane quadrant). With p.epi_groups (several tiles
+        // per CTA, BN <= 128) group g takes the tiles with tcount % 3 == g (accumulator buffer g)
+        // and every column of them, so each group's per-tile waits overlap the other groups'
+        // work; otherwise the groups share every tile, group g taking chunks
+        // [g * n / 3, (g + 1) * n / 3) of its n 32-column chunks.
         const int q = warp & 3;                 // TMEM lane quadrant
         const int grp = (warp - 4) >> 2;
-        const int cols = p.epi_groups ? BN : BN / 2;      // columns per warp and tile
-        const int cbase = p.epi_groups ? 0 : grp * (BN / 2);
+        const int c_lo = 32 * ((grp * n_chunks) / kEpiGroups);
+        const int c_hi = 32 * (((grp + 1) * n_chunks) / kEpiGroups);
+        const int cols = p.epi_groups ? BN : c_hi - c_lo;  // columns per warp and tile
+        const int cbase = p.epi_groups ? 0 : c_lo;
         const int row = q * 32 + lane;          // row within the tile
         const GemmEpilogue& e = p.epi;
         if (e.pdl_wait) grid_dependency_wait();
-        const int et = threadIdx.x - 128;       // 0..255 within the epilogue warps
+        const int et = threadIdx.x - 128;       // 0..383 within the epilogue warps
         // Bounded barrier of the 8 epilogue warps (an mbarrier phase per use).
         uint32_t ephase = 0;
         auto epi_sync = [&]() -> bool {
@@ -829,13 +876,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         bool ok = true;
         if (p.cs.b != nullptr) {
             // ---- column sums of B (MATMUL a_zp): 16 column groups of 4 bytes x 16 row slices
+            // (the first 8 epilogue warps sum; the other 4 only join the barriers)
             const ColsumJob& cs = p.cs;
             const int g = et & 15, slice = et >> 4;
             const int units_w = (cs.w + 63) / 64;
             for (int u = blockIdx.x; u < cs.units; u += gridDim.x) {
                 const int bn = u / units_w, col = (u % units_w) * 64 + g * 4;
                 int s0 = 0, s1 = 0, s2 = 0, s3 = 0;
-                if (col < cs.w) {
+                if (col < cs.w && slice < 16) {
                     const int8_t* src = cs.b + (static_cast<long long>(bn) * cs.c + slice) * cs.w + col;
 #pragma unroll 8
                     for (int k = slice; k < cs.c; k += 16, src += 16ll * cs.w) {
@@ -847,10 +895,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     }
                 }
                 int32_t* red = scratch;  // [16 slices][64 columns]
-                red[slice * 64 + g * 4 + 0] = s0;
-                red[slice * 64 + g * 4 + 1] = s1;
-                red[slice * 64 + g * 4 + 2] = s2;
-                red[slice * 64 + g * 4 + 3] = s3;
+                if (slice < 16) {
+                    red[slice * 64 + g * 4 + 0] = s0;
+                    red[slice * 64 + g * 4 + 1] = s1;
+                    red[slice * 64 + g * 4 + 2] = s2;
+                    red[slice * 64 + g * 4 + 3] = s3;
+                }
                 if (!epi_sync()) { ok = false; break; }
                 if (et < 64) {
                     int t = 0;
@@ -899,7 +949,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // Column constants (column terms and per-channel multiplier, shift - 32, hz) of the
         // current (batch, N tile) in shared memory; restaged only when the tile's batch or N
         // block changes (tiles walk M fastest). Two buffers: a warp that runs ahead writes
-        // the other one; it cannot lap, as each staging ends in a barrier of all 8 warps.
+        // the other one; it cannot lap, as each staging ends in a barrier of all 12 warps.
         // The fast path always stages (zero column terms when there are none), so its
         // pointers are plain shared-memory pointers.
         const bool stage_cols = kFast || kPC || e.colterm != nullptr;
@@ -908,8 +958,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++tcount) {
             int b, mt, nt;
             tile_coords(p, tile, b, mt, nt);
-            const int buf = tcount & 1;
-            const uint32_t tph = (tcount >> 1) & 1;
+            const int buf = tcount % NB;
+            const uint32_t tph = (tcount / NB) & 1;
             const int key = b * p.n_tiles + nt;
             if (stage_cols && key != staged_key) {
                 if (e.colterm != nullptr && p.cs.b != nullptr && staged_key < 0) {
@@ -938,7 +988,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
             // (the column-constant staging above is shared by both groups: every warp passes
             // every tile's key check, so the staging barriers pair up)
-            if (p.epi_groups && buf != grp) continue;
+            if (p.epi_groups ? buf != grp : cols == 0) continue;
             // Pointers indexed by the absolute output column.
             const int32_t* cst_n = ct_stage + sbuf * 1024 - nt * BN;
             // Border class of this thread's row (before the accumulator wait: the lookups overlap it).
@@ -990,7 +1040,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 const int swz = (lane >> 1) & 3;
                 // chunks that start at or beyond N (a partial last N tile) are skipped (the
                 // conditions are warp-uniform, so the TMEM loads stay warp-collective)
-                const int n_end = p.N - nb;  // columns of this warp's part that exist
+                const int n_end = min(cols, p.N - nb);  // columns of this warp's part that exist
                 // trace slots 416..479: per staging group, start / chunks done / stores done (CTA 0, tiles 0-1)
                 long long* ftr = (kGemmTrace && p.trace && blockIdx.x == 0 && tcount < 2 && threadIdx.x == 128)
                                      ? p.trace + 416 + 32 * tcount : nullptr;
