@@ -387,3 +387,30 @@ def test_sharded_interpreter_matches_whole_batch():
                 assert np.array_equal(np.asarray(got[nm].data).astype(np.int64).reshape(-1), w.values), nm
     finally:
         si.close()
+
+
+def test_external_constant_data(ctx):
+    """A graph whose constants lie after the flatbuffer (TosaTensor.offset / .size,
+    schema/tosa.fbs:711-716) runs bit-exact like the same graph with inline data; an
+    offset past the end of the file is rejected when the graph is loaded."""
+    from tosa_b200 import graphs
+    from tosa_b200 import tosa_graph as TG
+    data, _ = graphs.residual_block_int8(batch=2)
+    g = TG.read_graph(data)
+    for t in g.main_block.tensors:
+        if t.data is not None and len(t.data) > 64 and t.dtype != TG.DTYPE["SHAPE"]:
+            t.external = True
+    ext = TG.write_graph(g)
+    x = np.random.default_rng(12).integers(-128, 128, (2, 14, 14, 64)).astype(np.int8)
+    inputs = {"x": I.Tensor.from_numpy("x", x, L.DT_INT8)}
+    want = _oracle_run(data, inputs)
+    it = I.Interpreter(ext, context=ctx)
+    try:
+        got = it.run(inputs)
+    finally:
+        it.close()
+    for nm, w in want.items():
+        assert np.array_equal(np.asarray(got[nm].data).astype(np.int64).reshape(-1), w.values), nm
+    with pytest.raises(L.TbError) as ei:
+        I.Interpreter(ext[:-16], context=ctx)
+    assert ei.value.kind == "Deserialize"

@@ -13,8 +13,10 @@ import os
 import subprocess
 import zipfile
 
+import numpy as np
 import pytest
 
+from oracle import oracle as O
 from tosa_b200 import graphs
 from tosa_b200 import tosa_graph as TG
 
@@ -160,3 +162,42 @@ def test_synthetic_graph_shapes():
     ops = [o.name for o in TG.read_graph(data).main_block.operators]
     assert ops.count("DEPTHWISE_CONV2D") == 17 and ops.count("CONV2D") == 2 + 2 * 17
     assert ops.count("ADD") == 10
+
+
+def _externalize(data, min_bytes=64):
+    """The same graph with every constant of more than `min_bytes` stored after the
+    flatbuffer (TosaTensor.offset / .size)."""
+    g = TG.read_graph(data)
+    n = 0
+    for t in g.main_block.tensors:
+        if t.data is not None and len(t.data) > min_bytes and t.dtype != TG.DTYPE["SHAPE"]:
+            t.external = True
+            n += 1
+    return TG.write_graph(g), n
+
+
+def test_external_tensor_data_round_trip():
+    """Constants stored outside the flatbuffer (schema/tosa.fbs:711-716, the form of
+    models above 2 GB) read back to the same tensors, and the oracle computes the
+    same outputs from either file."""
+    from tosa_b200 import graphs
+    data, _ = graphs.residual_block_int8(batch=2)
+    ext, n = _externalize(data)
+    assert n >= 5
+    a, b = TG.read_graph(data).main_block, TG.read_graph(ext).main_block
+    for ta, tb in zip(a.tensors, b.tensors):
+        assert (ta.name, ta.shape, ta.dtype, ta.data) == (tb.name, tb.shape, tb.dtype, tb.data)
+    assert sum(t.external for t in b.tensors) == n
+    x = np.random.default_rng(4).integers(-128, 128, (2, 14, 14, 64)).astype(np.int64)
+    outs = [O.run_block(TG.read_graph(d).main_block, {"x": O.T(3, [2, 14, 14, 64], x.reshape(-1))})
+            for d in (data, ext)]
+    for nm in outs[0]:
+        assert np.array_equal(outs[0][nm].values, outs[1][nm].values)
+
+
+def test_external_tensor_data_outside_the_file():
+    from tosa_b200 import graphs
+    data, _ = graphs.residual_block_int8(batch=2)
+    ext, _ = _externalize(data)
+    with pytest.raises(TG.TosaFormatError):  # the last constant's bytes cut off the end of the file
+        TG.read_graph(ext[:-16])

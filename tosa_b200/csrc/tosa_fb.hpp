@@ -121,6 +121,18 @@ class Reader {
         const uint16_t o = field(t, id);
         return o ? u8(t.pos + o) : def;
     }
+    uint64_t scalar_u64(const Table& t, int id, uint64_t def = 0) {
+        const uint16_t o = field(t, id);
+        if (!o || !need(t.pos + o, 8)) return def;
+        uint64_t v;
+        std::memcpy(&v, d_ + t.pos + o, 8);
+        return v;
+    }
+    // `size` bytes at file offset `off` (tensor data stored outside the flatbuffer).
+    std::vector<uint8_t> span(uint64_t off, uint64_t size) {
+        if (off > n_ || size > n_ - off) { bad("external tensor data outside the file"); return {}; }
+        return std::vector<uint8_t>(d_ + off, d_ + off + size);
+    }
 
     // Position of the referenced object (table, string, vector) or 0 if absent.
     size_t ref(const Table& t, int id) {
@@ -263,7 +275,11 @@ inline void parse_attr(Reader& r, int tag, const Reader::Table& t, Attr* a) {
 
 // TosaGraph {version:0, regions:1}; TosaRegion {name:0, blocks:1};
 // TosaBasicBlock {name:0, operators:1, tensors:2, inputs:3, outputs:4, shapes:5};
-// TosaTensor {name:0, shape:1, type:2, data:3, variable:4}; TosaShape {name:0, rank:1, data:2};
+// TosaTensor {name:0, shape:1, type:2, data:3, variable:4, is_unranked:5, variable_name:6, offset:7,
+//             size:8}; TosaShape {name:0, rank:1, data:2};
+// A tensor without inline data whose offset is above 1 keeps `size` bytes at that offset from the
+// start of the file (models above 2 GB; schema/tosa.fbs:711-716). The reference reads only the
+// inline data (src/ir.rs parses no offset): such constants fail there and load here.
 // TosaOperator {op:0, attribute_type:1, attribute:2, inputs:3, outputs:4}.
 inline bool parse_graph(const uint8_t* data, size_t len, Graph* g, std::string* err) {
     Reader r(data, len);
@@ -281,6 +297,11 @@ inline bool parse_graph(const uint8_t* data, size_t len, Graph* g, std::string* 
                 td.dtype = static_cast<int32_t>(r.scalar_u32(tt, 2));
                 td.data = r.bytes(tt, 3, &td.has_data);
                 td.variable = r.scalar_u8(tt, 4) != 0;
+                const uint64_t off = r.scalar_u64(tt, 7);
+                if (!td.has_data && off > 1) {
+                    td.data = r.span(off, r.scalar_u64(tt, 8));
+                    td.has_data = true;
+                }
                 b.tensors.push_back(std::move(td));
             }
             for (const auto& st : r.table_vec(bt, 5)) {

@@ -86,6 +86,9 @@ class TensorDef:
     dtype: int
     data: bytes | None = None
     variable: bool = False
+    # write the data outside the flatbuffer, at an offset from the start of the file
+    # (TosaTensor.offset / .size, schema/tosa.fbs:711-716); a read sets it when it found them
+    external: bool = False
 
 
 @dataclass
@@ -280,12 +283,22 @@ def read_graph(data: bytes) -> Graph:
         for bt in rt.table_vec(1):
             tensors = []
             for tt in bt.table_vec(2):
+                tdata = tt.bytes_vec(3)
+                ext = False
+                off = tt.scalar(7, "u64")
+                if tdata is None and off > 1:
+                    # data outside the flatbuffer: `size` bytes at `offset` from the start of the file
+                    size = tt.scalar(8, "u64")
+                    b.need(off, size)
+                    tdata = bytes(data[off:off + size])
+                    ext = True
                 tensors.append(TensorDef(
                     name=tt.string(0) or "",
                     shape=tt.i32_vec(1),
                     dtype=tt.scalar(2, "u32"),
-                    data=tt.bytes_vec(3),
+                    data=tdata,
                     variable=bool(tt.scalar(4, "u8")),
+                    external=ext,
                 ))
             for st in bt.table_vec(5):  # shapes: SHAPE tensors of rank `rank`
                 tensors.append(TensorDef(name=st.string(0) or "", shape=[st.scalar(1, "u32")],
@@ -446,7 +459,30 @@ def _attr_fields(opname, attr, b: _Builder):
 
 
 def write_graph(g: Graph) -> bytes:
-    """Serialize a Graph to `.tosa` bytes."""
+    """Serialize a Graph to `.tosa` bytes. Tensors marked `external` keep their data after
+    the flatbuffer, 16-byte aligned, addressed by TosaTensor.offset / .size (the layout the
+    schema defines for models above 2 GB)."""
+    ext = [t for _, blocks in g.regions for blk in blocks for t in blk.tensors
+           if t.external and t.data is not None and t.dtype != DTYPE["SHAPE"]]
+    if not ext:
+        return _write_graph(g, {})
+    # the flatbuffer's size does not depend on the offset values (fixed-size scalars), so a
+    # first pass with placeholders gives the position of the appended data
+    head = len(_write_graph(g, {id(t): (2, len(t.data)) for t in ext}))
+    offs, pos = {}, (head + 15) // 16 * 16
+    for t in ext:
+        offs[id(t)] = (pos, len(t.data))
+        pos = (pos + len(t.data) + 15) // 16 * 16
+    out = bytearray(_write_graph(g, offs))
+    assert len(out) == head
+    for t in ext:
+        p, n = offs[id(t)]
+        out.extend(b"\0" * (p - len(out)))
+        out.extend(t.data)
+    return bytes(out)
+
+
+def _write_graph(g: Graph, external: dict) -> bytes:
     b = _Builder()
     region_offs = []
     for rname, blocks in g.regions:
@@ -470,11 +506,15 @@ def write_graph(g: Graph) -> bytes:
                     continue
                 name = b.create_string(t.name)
                 shape = b.create_i32_vec(t.shape)
-                data = b.create_bytes(t.data) if t.data is not None else None
+                where = external.get(id(t))
+                data = b.create_bytes(t.data) if t.data is not None and where is None else None
                 ten_offs.append(b.table([
                     ("ref", name), ("ref", shape), ("u32", t.dtype),
                     ("ref", data) if data is not None else None,
                     ("bool", t.variable) if t.variable else None,
+                    None, None,
+                    ("u64", where[0]) if where else None,
+                    ("u64", where[1]) if where else None,
                 ]))
             shape_offs = []
             for t in blk.tensors:
