@@ -311,6 +311,32 @@ static void set_fast_epilogue(GemmEpilogue* ep, const RescalePlan& rs, const Sma
     ep->sr_c = sr.d_c;
 }
 
+// The fast int8 epilogue stores each warp's staged [32 rows][GW] block with one TMA store when
+// the output rows are 16-byte multiples and the output is 16-byte aligned: a 3-D map
+// (N, M, batch) over the output, box [GW = min(BN / 2, 64), 32, 1], swizzled as the staging
+// buffer is laid out. The map is made once per output pointer (`cached`). Otherwise (or if the
+// map cannot be made) the epilogue keeps its per-thread stores.
+static void prepare_tma_out(GemmParams* gp, int bn, CUtensorMap* map, const void** cached) {
+    gp->tma_out = 0;
+    const int ek = epilogue_kind(gp->epi);
+    if (ek < EK_FAST_T_S || ek > EK_FAST_PC_D) return;
+    const long long bstride = gp->batch > 1 ? gp->out_batch_stride : gp->ldo * gp->M;
+    if (gp->ldo % 16 != 0 || bstride % 16 != 0 || !aligned16(gp->out)) return;
+    if (gp->out != *cached) {
+        const uint32_t gw = bn / 2 < 64 ? static_cast<uint32_t>(bn / 2) : 64u;
+        const uint64_t dims[3] = {static_cast<uint64_t>(gp->N), static_cast<uint64_t>(gp->M),
+                                  static_cast<uint64_t>(gp->batch)};
+        const uint64_t str[2] = {static_cast<uint64_t>(gp->ldo), static_cast<uint64_t>(bstride)};
+        const uint32_t box[3] = {gw, 32, 1};
+        if (encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, gp->out, dims, str, box,
+                         gw == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B) != TB_OK)
+            return;
+        *cached = gp->out;
+    }
+    gp->tma_out = 1;
+    gp->tmo_host = map;
+}
+
 RescaleArgs rescale_args(const RescalePlan& r) {
     RescaleArgs a;
     a.multiplier = r.d_mult;
@@ -684,6 +710,7 @@ extern "C" TB_API tb_status tb_matmul_plan_run(tb_matmul_plan* p, const void* a,
             ep.mode = EPI_I32;
             ep.out_dtype = TB_DT_INT32;
         }
+        prepare_tma_out(&gp, p->bn, &p->tmO, &p->o_cached);
         return launch_i8_matmul_t(ctx, p->bn, epilogue_kind(ep), p->tmA, p->tmB, gp, st);
     }
     if (p->path == 0 || p->path == 5) {
@@ -724,6 +751,7 @@ extern "C" TB_API tb_status tb_matmul_plan_run(tb_matmul_plan* p, const void* a,
             ep.mode = EPI_I32;
             ep.out_dtype = TB_DT_INT32;
         }
+        prepare_tma_out(&gp, p->bn, &p->tmO, &p->o_cached);
         return launch_i8_matmul(ctx, p->bn, epilogue_kind(ep), p->tmA, p->tmB, gp, st);
     }
     ep.mode = EPI_F32;
@@ -830,7 +858,8 @@ struct tb_conv2d_plan {
     uint8_t* d_colclass = nullptr;
     int n_cx = 1;
     const void* in_cached = nullptr;
-    CUtensorMap tmA, tmB;
+    const void* o_cached = nullptr;  // output the TMA-store map tmO was made for
+    CUtensorMap tmA, tmB, tmO;
     float* d_fbias = nullptr;  // float bias widened to f32
     // path 8: im2col rows + a 1x1 tensor-core convolution over them
     tb_conv2d_plan* inner = nullptr;
@@ -1088,6 +1117,11 @@ static tb_status conv_plan_create(tb_context* ctx, const tb_conv2d_desc* d, cons
     if (p->path >= 2) { *out = p; return TB_OK; }
 
     p->bn = oc <= 64 ? 64 : oc <= 128 ? 128 : 256;
+    // TB_CONV_MAX_BN (read at plan creation) caps the tile width of the tensor-core convolutions
+    if (const char* ev = std::getenv("TB_CONV_MAX_BN")) {
+        const int cap = std::atoi(ev);
+        if ((cap == 64 || cap == 128) && p->bn > cap) p->bn = cap;
+    }
     p->bk = (int8 && d->ic <= 64) ? 64 : 128;
     p->tap2 = p->path == 0 && int8 && d->ic == 64 && taps >= 2 && p->bn <= 128;
     const int bke = p->bk / e;
@@ -1548,6 +1582,7 @@ extern "C" TB_API tb_status tb_conv2d_plan_run(tb_conv2d_plan* p, const void* in
         ep.mode = EPI_I32;
         ep.out_dtype = TB_DT_INT32;
     }
+    prepare_tma_out(&gp, p->bn, &p->tmO, &p->o_cached);
     if (p->tap2) return launch_i8_conv_tap2(ctx, p->bn, epilogue_kind(ep), p->tmA, p->tmB, gp, st);
     return launch_i8_conv(ctx, p->bn, p->bk, epilogue_kind(ep), p->tmA, p->tmB, gp, st);
 }

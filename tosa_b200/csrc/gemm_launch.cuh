@@ -8,6 +8,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstring>
 
 #include "internal.hpp"
 #include "tc_gemm.cuh"
@@ -85,7 +86,14 @@ tb_status launch_gemm(tb_context* ctx, const CUtensorMap& tmA, const CUtensorMap
     }
     cfg.attrs = attr;
     cfg.numAttrs = na;
-    TB_CUDA(cudaLaunchKernelEx(&cfg, tc_gemm_kernel<Cfg, EK, EF>, tmA, tmB, p));
+    // the output map (fast int8 epilogue with TMA stores), or an unused placeholder
+    CUtensorMap tmO;
+    if (p.tma_out && p.tmo_host != nullptr) tmO = *p.tmo_host;
+    else {
+        std::memset(&tmO, 0, sizeof tmO);
+        p.tma_out = 0;
+    }
+    TB_CUDA(cudaLaunchKernelEx(&cfg, tc_gemm_kernel<Cfg, EK, EF>, tmA, tmB, tmO, p));
     TB_GEMM_LAUNCHED(ctx);
     return TB_OK;
 }

@@ -207,5 +207,6 @@ struct tb_matmul_plan {
     const void* a_cached = nullptr;
     const void* b_cached = nullptr;
     const void* b_const = nullptr;  // B declared constant: d_colterm / d_bpad hold its column terms / padded rows
-    CUtensorMap tmA, tmB;
+    const void* o_cached = nullptr; // output the TMA-store map tmO was made for
+    CUtensorMap tmA, tmB, tmO;
 };

@@ -187,6 +187,10 @@ struct GemmParams {
     int epi_groups;
     // K-major B without im2col (MATMUL_T): 1 when B has one batch shared by every batch of A
     int b_bcast;
+    // fast int8 epilogue: each warp writes its staged 32-row block with a TMA store through the
+    // output tensor map (the kernel's third parameter) instead of per-thread stores
+    int tma_out;
+    const CUtensorMap* tmo_host;  // host side only: the map the launcher passes, when tma_out
 };
 
 // TAP2 (int8 im2col convolutions with exactly 64 input channels): two filter taps per stage,
@@ -489,6 +493,8 @@ __device__ __forceinline__ void fast_chunk_i8(const GemmParams& p, const uint32_
 // int8 form: TMEM loads of 32 columns (the next one in flight while this one is rescaled),
 // packing into the warp's shared staging buffer, and row-contiguous stores of 64-byte groups.
 struct FastTile {
+    const CUtensorMap* tmo; // output tensor map (p.tma_out)
+    int oz;                 // batch coordinate of the tile
     uint32_t taddr;         // TMEM address of the warp's first column (lane quadrant in the high half)
     int cols;               // columns of the tile this warp covers (BN, or its share of a tile)
     int n_end;              // of them, the ones that exist (at most cols, and N - first column)
@@ -499,8 +505,8 @@ struct FastTile {
     const int32_t* fm;
     const int32_t* fsh;
     const int32_t* fc;
-    uint4* wst;             // the warp's staging buffer [32 rows][4 x 16 B]
-    int lane, swz, mrow0;
+    uint4* wst;             // the warp's staging buffer [32 rows][GW bytes]
+    int lane, mrow0;
     int8_t* obase;
     bool vec_ok;
     long long* ftr;         // trace slots (CTA 0, first tiles) or null
@@ -510,10 +516,14 @@ template <int EK, int GW, bool ROW, bool DELTA>
 __device__ __forceinline__ void fast_tile_pass(const GemmParams& p, const FastConst& fk, const FastTile& h) {
     constexpr int FW = kChunkF;                // columns per TMEM load
     constexpr int FPK = FW / 16;               // 16-byte packs per chunk
-    // GW: columns per staging group (32 or 64)
+    // GW: columns per staging group (32 or 64). The warp's staging buffer holds 32 rows of GW
+    // bytes, the 16-byte slots of a row permuted as the TMA's 32- / 64-byte swizzle lays them
+    // out (slot j of row r at j ^ (r >> 2 & 1) or j ^ (r >> 1 & 3)): conflict-free row writes,
+    // and the layout a TMA store of a [32 rows][GW] box reads.
+    constexpr int RS = GW / 16;                // 16-byte slots per staging row
     const int COLS = h.cols;
-    constexpr int CPG = GW / kChunk;           // 16-byte slots per row and group: 2 or 4
-    const int lane = h.lane, swz = h.swz;
+    const int lane = h.lane;
+    const int swz = GW == 64 ? (lane >> 1) & 3 : (lane >> 2) & 1;
     uint32_t fA[FW], fB[FW];
     __syncwarp();
     if (h.n_end > 0) {
@@ -524,6 +534,9 @@ __device__ __forceinline__ void fast_tile_pass(const GemmParams& p, const FastCo
     for (int g0 = 0; g0 < COLS && g0 < h.n_end; g0 += GW) {
         uint4 pk[FPK];
         if (h.ftr && g0 / GW < 8) h.ftr[3 * (g0 / GW)] = clock64();
+        // a TMA store writes all GW columns of the box: only when they are this warp's (or lie
+        // past N, where the store writes nothing); a block wholly below M is not stored at all
+        const bool tma = p.tma_out && (g0 + GW <= COLS || h.nb + COLS >= p.N) && h.mrow0 < p.M;
         if constexpr (GW == 2 * FW) {
             const bool second = g0 + FW < h.n_end;
             const bool next = g0 + GW < COLS && g0 + GW < h.n_end;
@@ -531,8 +544,12 @@ __device__ __forceinline__ void fast_tile_pass(const GemmParams& p, const FastCo
             if (second) tmem_ld_32x32b(h.taddr + g0 + FW, fB);
             fast_chunk_i8<EK, FW, ROW, DELTA>(p, fA, h.nb + g0, h.rowterm, h.cst_n, h.delta, h.fm, h.fsh, h.fc,
                                                    fk, pk);
+            if (p.tma_out) {  // the previous store has read the staging buffer
+                if (lane == 0) bulk_wait_read0();
+                __syncwarp();
+            }
 #pragma unroll
-            for (int j = 0; j < FPK; ++j) h.wst[lane * 4 + (j ^ swz)] = pk[j];
+            for (int j = 0; j < FPK; ++j) h.wst[lane * RS + (j ^ swz)] = pk[j];
             __syncwarp();
             if (second) {
                 tmem_wait_regs(fB);
@@ -540,7 +557,7 @@ __device__ __forceinline__ void fast_tile_pass(const GemmParams& p, const FastCo
                 fast_chunk_i8<EK, FW, ROW, DELTA>(p, fB, h.nb + g0 + FW, h.rowterm, h.cst_n, h.delta, h.fm,
                                                        h.fsh, h.fc, fk, pk);
 #pragma unroll
-                for (int j = 0; j < FPK; ++j) h.wst[lane * 4 + ((FPK + j) ^ swz)] = pk[j];
+                for (int j = 0; j < FPK; ++j) h.wst[lane * RS + ((FPK + j) ^ swz)] = pk[j];
             }
             __syncwarp();
             if (next) tmem_wait_regs(fA);
@@ -548,30 +565,44 @@ __device__ __forceinline__ void fast_tile_pass(const GemmParams& p, const FastCo
             // one TMEM load per group: the next group's columns load while this group is stored
             fast_chunk_i8<EK, FW, ROW, DELTA>(p, fA, h.nb + g0, h.rowterm, h.cst_n, h.delta, h.fm, h.fsh, h.fc,
                                                    fk, pk);
+            if (p.tma_out) {
+                if (lane == 0) bulk_wait_read0();
+                __syncwarp();
+            }
 #pragma unroll
-            for (int j = 0; j < FPK; ++j) h.wst[lane * 4 + (j ^ swz)] = pk[j];
+            for (int j = 0; j < FPK; ++j) h.wst[lane * RS + (j ^ swz)] = pk[j];
             __syncwarp();
             if (g0 + GW < COLS && g0 + GW < h.n_end) tmem_ld_32x32b(h.taddr + g0 + GW, fA);
         }
         if (h.ftr && g0 / GW < 8) h.ftr[3 * (g0 / GW) + 1] = clock64();
-        __syncwarp();
+        if (tma) {
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                tma_store_3d(h.tmo, h.wst, h.nb + g0, h.mrow0, h.oz);
+                bulk_commit();
+            }
+        } else {
+            __syncwarp();
 #pragma unroll
-        for (int it = 0; it < CPG; ++it) {
-            const int idx = it * 32 + lane;
-            const int r = idx / CPG, k = idx % CPG;
-            const uint4 pv = h.wst[r * 4 + (k ^ ((r >> 1) & 3))];
-            const int mr = h.mrow0 + r;
-            const int n = h.nb + g0 + k * kChunk;
-            // only this pass's columns: a group's share of a tile can end before N (column thirds)
-            if (mr < p.M && g0 + k * kChunk < h.n_end) {
-                int8_t* o = h.obase + static_cast<long long>(mr) * p.ldo + n;
-                if (h.vec_ok && n + kChunk <= p.N) {
-                    *reinterpret_cast<uint4*>(o) = pv;
-                } else {
-                    const uint32_t w4[4] = {pv.x, pv.y, pv.z, pv.w};
+            for (int it = 0; it < RS; ++it) {
+                const int idx = it * 32 + lane;
+                const int r = idx / RS, k = idx % RS;
+                const int rs = GW == 64 ? (r >> 1) & 3 : (r >> 2) & 1;
+                const uint4 pv = h.wst[r * RS + (k ^ rs)];
+                const int mr = h.mrow0 + r;
+                const int n = h.nb + g0 + k * kChunk;
+                // only this pass's columns: a group's share of a tile can end before N (column thirds)
+                if (mr < p.M && g0 + k * kChunk < h.n_end) {
+                    int8_t* o = h.obase + static_cast<long long>(mr) * p.ldo + n;
+                    if (h.vec_ok && n + kChunk <= p.N) {
+                        *reinterpret_cast<uint4*>(o) = pv;
+                    } else {
+                        const uint32_t w4[4] = {pv.x, pv.y, pv.z, pv.w};
 #pragma unroll
-                    for (int j = 0; j < kChunk; ++j)
-                        if (n + j < p.N) o[j] = static_cast<int8_t>(w4[j >> 2] >> (8 * (j & 3)));
+                        for (int j = 0; j < kChunk; ++j)
+                            if (n + j < p.N) o[j] = static_cast<int8_t>(w4[j >> 2] >> (8 * (j & 3)));
+                    }
                 }
             }
         }
@@ -587,7 +618,8 @@ __device__ __forceinline__ void fast_tile_pass(const GemmParams& p, const FastCo
 // border classes); 0 for the other epilogue kinds.
 template <class Cfg, int EK, int EF>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmO, GemmParams p) {
     constexpr int BM = Cfg::BM, BN = Cfg::kBN, S = Cfg::kStages;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte alignment by an offset into the shared array: pointer arithmetic on smem_raw keeps the
@@ -1029,15 +1061,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const long long orow = static_cast<long long>(b) * p.out_batch_stride + static_cast<long long>(m) * p.ldo;
             const int nb = nt * BN + cbase;
             if constexpr (EK >= EK_FAST_T_S && EK <= EK_FAST_PC_D) {
-                // int8 results pass through a per-warp shared buffer [32 rows][4 x 16 B] (16-byte slots
-                // swizzled by row) so that the global stores are row-contiguous: a warp writes 8 rows x
-                // 64 B per store instead of 32 scattered 16 B pieces.
+                // int8 results pass through a per-warp shared buffer [32 rows][GW bytes] (16-byte slots
+                // swizzled by row): one TMA store of the block when the output allows it (p.tma_out),
+                // else row-contiguous stores (a warp writes 8 rows x 64 B per store instead of 32
+                // scattered 16 B pieces).
                 uint4* wst = reinterpret_cast<uint4*>(scratch + 3072) + (warp - 4) * 128;
                 int8_t* obase = reinterpret_cast<int8_t*>(p.out) + static_cast<long long>(b) * p.out_batch_stride;
                 const bool vec_ok = (p.ldo & 15) == 0 && (p.out_batch_stride & 15) == 0 &&
                                     (reinterpret_cast<uintptr_t>(p.out) & 15) == 0;
                 const int mrow0 = mt * BM + q * 32;
-                const int swz = (lane >> 1) & 3;
                 // chunks that start at or beyond N (a partial last N tile) are skipped (the
                 // conditions are warp-uniform, so the TMEM loads stay warp-collective)
                 const int n_end = min(cols, p.N - nb);  // columns of this warp's part that exist
@@ -1045,8 +1077,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 long long* ftr = (kGemmTrace && p.trace && blockIdx.x == 0 && tcount < 2 && threadIdx.x == 128)
                                      ? p.trace + 416 + 32 * tcount : nullptr;
                 // a warp with a border row adds every row's delta (zeros for interior rows)
-                const FastTile h{taddr, cols, n_end, nb, rowterm, cst_n, warp_delta ? delta_fast : nullptr,
-                                 fm, fsh, fhz, wst, lane, swz, mrow0, obase, vec_ok, ftr};
+                const FastTile h{&tmO, b, taddr, cols, n_end, nb, rowterm, cst_n, warp_delta ? delta_fast : nullptr,
+                                 fm, fsh, fhz, wst, lane, mrow0, obase, vec_ok, ftr};
                 fast_tile_pass<EK, (BN / 2 < 64 ? BN / 2 : 64), (EF & kEfRow) != 0, (EF & kEfDelta) != 0>(p, fk, h);
             } else {
             // Two register sets: the next chunk's TMEM load overlaps this chunk's epilogue.
@@ -1080,6 +1112,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         if (!ok && lane == 0) { atomicOr(p.err, DEV_ERR_TIMEOUT); *abort_flag = 1; }
         if (err) atomicOr(p.err, err);
+        if (p.tma_out && lane == 0) bulk_wait0();  // the warp's TMA stores are done before the CTA exits
     }
 
     __syncthreads();
