@@ -56,6 +56,12 @@ tb_status launch_gemm(tb_context* ctx, const CUtensorMap& tmA, const CUtensorMap
     p.fd_ntiles = make_fastdiv(p.n_tiles);
     p.fd_ow = make_fastdiv(p.conv_OW);
     p.fd_ohow = make_fastdiv(p.conv_OHOW);
+    // the ring: a multiple of the k blocks per tile when that costs at most one stage
+    {
+        const int S = Cfg::kStages, kb = p.k_blocks < 1 ? 1 : p.k_blocks;
+        const int mult = kb <= S ? (S / kb) * kb : S;
+        p.s_eff = S - mult <= 1 ? mult : S;
+    }
     p.err = ctx->dev_err;
     p.timeout_cycles = ctx->timeout_cycles;
     p.trace = ctx->trace;

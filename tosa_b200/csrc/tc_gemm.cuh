@@ -21,7 +21,7 @@
 // Warpgroup 0 needs few registers: it hands most of them to the epilogue
 // warpgroups (setmaxnreg), whose arithmetic needs them.
 //
-// The accumulator has three (whole tiles per group) or two buffers in TMEM, so
+// The accumulator has four (whole tiles per group) or two buffers in TMEM, so
 // the epilogue of a tile overlaps the main loop of the next one and the
 // epilogues of the tiles before it. All waits are bounded: a wait that
 // gives up sets DEV_ERR_TIMEOUT in the device error word and the CTA unwinds.
@@ -85,10 +85,10 @@ constexpr int kEpiRegs = 152;
 static_assert(128 * kRoleRegs + 384 * kEpiRegs <= kGemmThreads * kLaunchRegs, "register split above the launch total");
 // Shared memory per CTA: the stage ring, then 1 KB of alignment slack, the barriers and row
 // sums, and the epilogue scratch (column-sum reduction and staged column constants, 12 KB,
-// then a 2 KB output staging buffer per epilogue warp).
+// then two 2 KB output staging buffers per epilogue warp).
 constexpr int kSmemLimit = 232448;
 constexpr int kBarrierBytes = 3072;
-constexpr int kScratchBytes = 12288 + 2048 * kEpiWarps;
+constexpr int kScratchBytes = 12288 + 4096 * kEpiWarps;
 constexpr int kStageBudget = kSmemLimit - 1024 - kBarrierBytes - kScratchBytes;
 // Bound (clock cycles) on a CTA's final waits for its own TMA loads and MMAs.
 constexpr long long kDrainCycles = 2000000000ll;
@@ -187,6 +187,10 @@ struct GemmParams {
     int epi_groups;
     // K-major B without im2col (MATMUL_T): 1 when B has one batch shared by every batch of A
     int b_bcast;
+    // stages of the ring in use (at most STAGES): a multiple of k_blocks when that costs at most
+    // one stage, so that stage s always holds the same k block and a B tile that the previous
+    // load into the stage already brought need not be loaded again
+    int s_eff;
     // fast int8 epilogue: each warp writes its staged 32-row block with a TMA store through the
     // output tensor map (the kernel's third parameter) instead of per-thread stores
     int tma_out;
@@ -223,10 +227,10 @@ struct GemmCfg {
     // MN-major B: 128-byte rows of N, one box per 128 bytes of N.
     static constexpr int B_MN_CHUNK = 128 / kElem;                  // N elements per box
     static constexpr int B_MN_BOX_BYTES = BK * 128;                 // BK k-rows x 128 bytes
-    // accumulator buffers in TMEM (512 columns): three when the epilogue groups take whole tiles
+    // accumulator buffers in TMEM (512 columns): four when the epilogue groups take whole tiles
     // in turn (BN <= 128 only), otherwise two
     static constexpr bool kWholeTiles = BN <= 128;
-    static constexpr int kTmemNeed = kWholeTiles ? 3 * BN : 2 * BN;
+    static constexpr int kTmemNeed = kWholeTiles ? 4 * BN : 2 * BN;
     static constexpr int TMEM_COLS = kTmemNeed <= 32 ? 32 : (kTmemNeed <= 64 ? 64 : (kTmemNeed <= 128 ? 128 : (kTmemNeed <= 256 ? 256 : 512)));
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + kBarrierBytes + kScratchBytes;
     static_assert(SMEM_BYTES <= kSmemLimit, "shared memory above 227 KB");
@@ -264,7 +268,7 @@ __device__ __forceinline__ void tmem_wait_regs(uint32_t (&r)[32]) {
 }
 
 constexpr int kChunk = 16;   // output columns per thread per TMEM load (general epilogue)
-constexpr int kChunkF = 32;  // the same for the fast int8 RESCALE epilogue
+constexpr int kChunkF = 16;  // the same for the fast int8 RESCALE epilogue
 
 __device__ __forceinline__ uint32_t pack4_i8(int32_t a, int32_t b, int32_t c, int32_t d) {
     const uint32_t lo = __byte_perm(static_cast<uint32_t>(a), static_cast<uint32_t>(b), 0x0040);
@@ -505,7 +509,7 @@ struct FastTile {
     const int32_t* fm;
     const int32_t* fsh;
     const int32_t* fc;
-    uint4* wst;             // the warp's staging buffer [32 rows][GW bytes]
+    uint4* wst;             // the warp's two staging buffers, 2 KB apart: [32 rows][GW bytes] each
     int lane, mrow0;
     int8_t* obase;
     bool vec_ok;
@@ -513,17 +517,25 @@ struct FastTile {
 };
 
 template <int EK, int GW, bool ROW, bool DELTA>
-__device__ __forceinline__ void fast_tile_pass(const GemmParams& p, const FastConst& fk, const FastTile& h) {
+__device__ __forceinline__ void fast_tile_pass(const GemmParams& p, const FastConst& fk, const FastTile& h,
+                                               uint32_t& npass) {
     constexpr int FW = kChunkF;                // columns per TMEM load
     constexpr int FPK = FW / 16;               // 16-byte packs per chunk
-    // GW: columns per staging group (32 or 64). The warp's staging buffer holds 32 rows of GW
-    // bytes, the 16-byte slots of a row permuted as the TMA's 32- / 64-byte swizzle lays them
-    // out (slot j of row r at j ^ (r >> 2 & 1) or j ^ (r >> 1 & 3)): conflict-free row writes,
-    // and the layout a TMA store of a [32 rows][GW] box reads.
+    constexpr int NCH = GW / FW;               // chunks per staging group (an even number)
+    static_assert(NCH % 2 == 0, "staging groups alternate the two TMEM register sets");
+    // GW: columns per staging group (32 or 64). Each of the warp's two staging buffers (used by
+    // alternate groups, `npass` counts the warp's groups) holds 32 rows of GW bytes, the 16-byte
+    // slots of a row permuted as the TMA's 32- / 64-byte swizzle lays them out (slot j of row r
+    // at j ^ (r >> 2 & 1) or j ^ (r >> 1 & 3)): conflict-free row writes, and the layout a TMA
+    // store of a [32 rows][GW] box reads. With two buffers a group waits only for the store of
+    // the group before last, not for the one just issued.
     constexpr int RS = GW / 16;                // 16-byte slots per staging row
     const int COLS = h.cols;
     const int lane = h.lane;
     const int swz = GW == 64 ? (lane >> 1) & 3 : (lane >> 2) & 1;
+    // Two register sets of FW columns: chunk c of a group uses set c % 2, and the next chunk's
+    // TMEM load is in flight while chunk c is rescaled (tcgen05.wait::ld waits for all of this
+    // thread's loads, so exactly one is outstanding at each wait).
     uint32_t fA[FW], fB[FW];
     __syncwarp();
     if (h.n_end > 0) {
@@ -532,64 +544,52 @@ __device__ __forceinline__ void fast_tile_pass(const GemmParams& p, const FastCo
     }
 #pragma unroll 1
     for (int g0 = 0; g0 < COLS && g0 < h.n_end; g0 += GW) {
-        uint4 pk[FPK];
         if (h.ftr && g0 / GW < 8) h.ftr[3 * (g0 / GW)] = clock64();
         // a TMA store writes all GW columns of the box: only when they are this warp's (or lie
         // past N, where the store writes nothing); a block wholly below M is not stored at all
         const bool tma = p.tma_out && (g0 + GW <= COLS || h.nb + COLS >= p.N) && h.mrow0 < p.M;
-        if constexpr (GW == 2 * FW) {
-            const bool second = g0 + FW < h.n_end;
-            const bool next = g0 + GW < COLS && g0 + GW < h.n_end;
+        uint4* wst = h.wst + (npass & 1) * 128;  // 2 KB apart
+        ++npass;
+        if (p.tma_out) {  // the store that read this buffer (the group before last) is done reading
+            if (lane == 0) bulk_wait_read1();
             __syncwarp();
-            if (second) tmem_ld_32x32b(h.taddr + g0 + FW, fB);
-            fast_chunk_i8<EK, FW, ROW, DELTA>(p, fA, h.nb + g0, h.rowterm, h.cst_n, h.delta, h.fm, h.fsh, h.fc,
+        }
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {
+            const int col = g0 + c * FW;
+            if (col >= h.n_end) break;  // warp-uniform
+            const bool next = col + FW < COLS && col + FW < h.n_end;
+            uint32_t(&cur)[FW] = (c & 1) ? fB : fA;
+            uint32_t(&nxt)[FW] = (c & 1) ? fA : fB;
+            __syncwarp();
+            if (next) tmem_ld_32x32b(h.taddr + col + FW, nxt);
+            uint4 pk[FPK];
+            fast_chunk_i8<EK, FW, ROW, DELTA>(p, cur, h.nb + col, h.rowterm, h.cst_n, h.delta, h.fm, h.fsh, h.fc,
                                                    fk, pk);
-            if (p.tma_out) {  // the previous store has read the staging buffer
-                if (lane == 0) bulk_wait_read0();
-                __syncwarp();
-            }
 #pragma unroll
-            for (int j = 0; j < FPK; ++j) h.wst[lane * RS + (j ^ swz)] = pk[j];
+            for (int j = 0; j < FPK; ++j) wst[lane * RS + ((c * FPK + j) ^ swz)] = pk[j];
             __syncwarp();
-            if (second) {
-                tmem_wait_regs(fB);
-                if (next) tmem_ld_32x32b(h.taddr + g0 + GW, fA);
-                fast_chunk_i8<EK, FW, ROW, DELTA>(p, fB, h.nb + g0 + FW, h.rowterm, h.cst_n, h.delta, h.fm,
-                                                       h.fsh, h.fc, fk, pk);
-#pragma unroll
-                for (int j = 0; j < FPK; ++j) h.wst[lane * RS + ((FPK + j) ^ swz)] = pk[j];
-            }
-            __syncwarp();
-            if (next) tmem_wait_regs(fA);
-        } else {
-            // one TMEM load per group: the next group's columns load while this group is stored
-            fast_chunk_i8<EK, FW, ROW, DELTA>(p, fA, h.nb + g0, h.rowterm, h.cst_n, h.delta, h.fm, h.fsh, h.fc,
-                                                   fk, pk);
-            if (p.tma_out) {
-                if (lane == 0) bulk_wait_read0();
-                __syncwarp();
-            }
-#pragma unroll
-            for (int j = 0; j < FPK; ++j) h.wst[lane * RS + (j ^ swz)] = pk[j];
-            __syncwarp();
-            if (g0 + GW < COLS && g0 + GW < h.n_end) tmem_ld_32x32b(h.taddr + g0 + GW, fA);
+            if (next) tmem_wait_regs(nxt);
         }
         if (h.ftr && g0 / GW < 8) h.ftr[3 * (g0 / GW) + 1] = clock64();
         if (tma) {
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-                tma_store_3d(h.tmo, h.wst, h.nb + g0, h.mrow0, h.oz);
+                tma_store_3d(h.tmo, wst, h.nb + g0, h.mrow0, h.oz);
                 bulk_commit();
             }
         } else {
+            // every pass commits one bulk group (an empty one here), so that the wait before a
+            // buffer's reuse always refers to the pass that last used it
+            if (p.tma_out && lane == 0) bulk_commit();
             __syncwarp();
 #pragma unroll
             for (int it = 0; it < RS; ++it) {
                 const int idx = it * 32 + lane;
                 const int r = idx / RS, k = idx % RS;
                 const int rs = GW == 64 ? (r >> 1) & 3 : (r >> 2) & 1;
-                const uint4 pv = h.wst[r * RS + (k ^ rs)];
+                const uint4 pv = wst[r * RS + (k ^ rs)];
                 const int mr = h.mrow0 + r;
                 const int n = h.nb + g0 + k * kChunk;
                 // only this pass's columns: a group's share of a tile can end before N (column thirds)
@@ -607,9 +607,6 @@ __device__ __forceinline__ void fast_tile_pass(const GemmParams& p, const FastCo
             }
         }
         if (h.ftr && g0 / GW < 8) h.ftr[3 * (g0 / GW) + 2] = clock64();
-        if constexpr (GW != 2 * FW) {
-            if (g0 + GW < COLS && g0 + GW < h.n_end) tmem_wait_regs(fA);
-        }
         __syncwarp();
     }
 }
@@ -630,19 +627,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint64_t* full = bars;               // [S]
     uint64_t* empty = bars + S;          // [S]
     // TMEM accumulator buffers: with whole tiles per group (p.epi_groups) tile t takes buffer
-    // t % 3 and is processed by group t % 3, so each group waits for consecutive phases of its
-    // own buffer's barriers; otherwise every tile is shared by the groups (column thirds) and
-    // two buffers alternate. Either way no waiter is ever more than one phase ahead.
-    const int NB = p.epi_groups ? kEpiGroups : 2;
-    uint64_t* tfull = bars + 2 * S;      // [3]
-    uint64_t* tempty = tfull + 3;        // [3]
-    uint64_t* rsfull = tempty + 3;       // [3]
-    uint64_t* rsempty = rsfull + 3;      // [3]
-    uint64_t* mdrain = rsempty + 3;      // [1]
+    // t % 4 and is processed by group t % 3, so the next tile can fill while all three groups
+    // work; otherwise every tile is shared by the groups (column thirds) and two buffers
+    // alternate. No waiter is ever more than one phase ahead: a group's first tile takes a
+    // fresh buffer, and the previous use of the buffer of its later tile t (tile t - 4) was
+    // filled before the group's previous tile t - 3, which it has already waited for.
+    const int NB = p.epi_groups ? 4 : 2;
+    uint64_t* tfull = bars + 2 * S;      // [4]
+    uint64_t* tempty = tfull + 4;        // [4]
+    uint64_t* rsfull = tempty + 4;       // [4]
+    uint64_t* rsempty = rsfull + 4;      // [4]
+    uint64_t* mdrain = rsempty + 4;      // [1]
     uint64_t* ebar = mdrain + 1;         // [1] barrier of the 12 epilogue warps
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ebar + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    int32_t* rowsum_buf = reinterpret_cast<int32_t*>(tmem_slot + 4);  // [3][128]
+    int32_t* rowsum_buf = reinterpret_cast<int32_t*>(tmem_slot + 4);  // [4][128]
     int32_t* scratch = reinterpret_cast<int32_t*>(smem + S * Cfg::STAGE_BYTES + kBarrierBytes);  // kScratchBytes
 
     const int warp = threadIdx.x >> 5;
@@ -686,6 +685,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // waits for this CTA's own copies and MMAs before it exits get a fixed, generous bound (about
     // a second), whatever the configured timeout: they end once work already issued completes
     const long long drain_limit = limit > kDrainCycles ? limit : kDrainCycles;
+    const int SE = p.s_eff;  // stages of the ring in use
     if (kGemmTrace && p.trace && blockIdx.x == 0 && threadIdx.x == 0) p.trace[400] = clock64();
 
     if (warp < 4) {
@@ -696,10 +696,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             if (lane == 0) {
                 uint32_t it = 0;
                 bool ok = true;
+                // the B tile each stage holds: (B batch, N tile, k block), -1 before its first load.
+                // B tiles are the same for every M tile of a (batch, N tile) pair; for short K
+                // (few k blocks, a ring that is a multiple of them) the stages keep their B tiles
+                // across tiles and only A is loaded.
+                long long bkey[S];
+#pragma unroll
+                for (int i = 0; i < S; ++i) bkey[i] = -1;
                 for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
                     int b, mt, nt;
                     tile_coords(p, tile, b, mt, nt);
                     const int m0 = mt * BM, n0 = nt * BN;
+                    const int bb = Cfg::kIm2col || p.b_bcast ? 0 : b;  // batch of the B tile
+                    const long long key0 = (static_cast<long long>(bb) * p.n_tiles + nt) * p.k_blocks;
                     int img = 0, wb = 0, hb = 0;
                     if constexpr (Cfg::kIm2col) {
                         img = fdiv(m0, p.fd_ohow);
@@ -710,20 +719,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     }
                     int cb = 0, kx = 0, ky = 0, tap = 0;  // k block kb = (ky * KW + kx) * c_blocks + cb, stepped
                     for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
-                        const int s = it % S;
-                        const uint32_t ph = (it / S) & 1;
+                        const int s = it % SE;
+                        const uint32_t ph = (it / SE) & 1;
                         if (!mbar_wait_bounded(&empty[s], ph ^ 1, abort_flag, limit)) { ok = false; break; }
                         uint8_t* sa = stage_base + s * Cfg::STAGE_BYTES;
                         uint8_t* sb = sa + Cfg::A_BYTES;
                         if (kGemmTrace && p.trace && blockIdx.x == 0 && it < 128) p.trace[it] = clock64();
+                        const bool load_b = bkey[s] != key0 + kb;
+                        bkey[s] = key0 + kb;
+                        const uint32_t b_tx = load_b ? Cfg::B_BYTES : 0u;
                         if constexpr (Cfg::kTap2) {
                             // taps tap and tap + 1 (the last stage of an odd tap count has one; the B box's
                             // second half then lies past K and is filled with zeros)
                             const bool two = tap + 1 < p.taps;
-                            mbar_arrive_expect_tx(&full[s], two ? Cfg::STAGE_BYTES : Cfg::STAGE_BYTES - Cfg::A_SUB);
+                            mbar_arrive_expect_tx(&full[s], Cfg::A_SUB * (two ? 2 : 1) + b_tx);
                             tma_load_im2col_4d(sa, &tmA, &full[s], 0, wb, hb, img, static_cast<uint16_t>(kx * p.dil_w),
                                                static_cast<uint16_t>(ky * p.dil_h));
-                            tma_load_3d(sb, &tmB, &full[s], tap * p.IC, n0, 0);
+                            if (load_b) tma_load_3d(sb, &tmB, &full[s], tap * p.IC, n0, 0);
                             ++tap;
                             if (++kx == p.KW) {
                                 kx = 0;
@@ -740,11 +752,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                             }
                             continue;
                         }
-                        mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
+                        mbar_arrive_expect_tx(&full[s], Cfg::A_BYTES + b_tx);
                         if constexpr (Cfg::kIm2col) {
                             tma_load_im2col_4d(sa, &tmA, &full[s], cb * Cfg::BK, wb, hb, img,
                                                static_cast<uint16_t>(kx * p.dil_w), static_cast<uint16_t>(ky * p.dil_h));
-                            tma_load_3d(sb, &tmB, &full[s], tap * p.IC + cb * Cfg::BK, n0, 0);
+                            if (load_b) tma_load_3d(sb, &tmB, &full[s], tap * p.IC + cb * Cfg::BK, n0, 0);
                             if (++cb == p.c_blocks) {
                                 cb = 0;
                                 ++tap;
@@ -755,7 +767,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                             }
                         } else {
                             tma_load_3d(sa, &tmA, &full[s], kb * Cfg::BK, m0, b);
-                            if constexpr (Cfg::kBMN) {
+                            if (!load_b) {
+                            } else if constexpr (Cfg::kBMN) {
     #pragma unroll
                                 for (int j = 0; j < BN / Cfg::B_MN_CHUNK; ++j)
                                     tma_load_3d(sb + j * Cfg::B_MN_BOX_BYTES, &tmB, &full[s], n0 + j * Cfg::B_MN_CHUNK,
@@ -768,9 +781,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 }
                 if (!ok) { atomicOr(p.err, DEV_ERR_TIMEOUT); *abort_flag = 1; }
                 // Drain: every issued load must land before the CTA may exit.
-                const uint32_t first = it > static_cast<uint32_t>(S) ? it - S : 0;
+                const uint32_t first = it > static_cast<uint32_t>(SE) ? it - SE : 0;
                 for (uint32_t i = first; i < it; ++i)
-                    mbar_wait_bounded(&full[i % S], (i / S) & 1, nullptr, drain_limit);
+                    mbar_wait_bounded(&full[i % SE], (i / SE) & 1, nullptr, drain_limit);
             }
         } else if (warp == 1) {
             // ------------------------------------------------------------ MMA issuer
@@ -786,8 +799,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     tc_fence_after();
                     const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * BN);
                     for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
-                        const int s = it % S;
-                        const uint32_t ph = (it / S) & 1;
+                        const int s = it % SE;
+                        const uint32_t ph = (it / SE) & 1;
                         if (!mbar_wait_bounded(&full[s], ph, abort_flag, limit)) { ok = false; break; }
                         tc_fence_after();
                         if (kGemmTrace && p.trace && blockIdx.x == 0 && it < 128) p.trace[128 + it] = clock64();
@@ -831,8 +844,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++tcount) {
                     int sum0 = 0, sum1 = 0;
                     for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
-                        const int s = it % S;
-                        const uint32_t ph = (it / S) & 1;
+                        const int s = it % SE;
+                        const uint32_t ph = (it / SE) & 1;
                         if (!mbar_wait_bounded(&full[s], ph, abort_flag, limit)) { ok = false; break; }
                         const uint8_t* sa0 = stage_base + s * Cfg::STAGE_BYTES;
                         // two taps per stage: the second sub-tile holds data only when the stage has two taps
@@ -879,9 +892,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         setmaxnreg_inc<kEpiRegs>();
         // ------------------------------------------------------------ epilogue (warps 4..15)
         // Three groups of 4 warps (one per TMEM lane quadrant). With p.epi_groups (several tiles
-        // per CTA, BN <= 128) group g takes the tiles with tcount % 3 == g (accumulator buffer g)
-        // and every column of them, so each group's per-tile waits overlap the other groups'
-        // work; otherwise the groups share every tile, group g taking chunks
+        // per CTA, BN <= 128) group g takes the tiles with tcount % 3 == g (accumulator buffer
+        // tcount % 4) and every column of them, so each group's per-tile waits overlap the other
+        // groups' work; otherwise the groups share every tile, group g taking chunks
         // [g * n / 3, (g + 1) * n / 3) of its n 32-column chunks.
         const int q = warp & 3;                 // TMEM lane quadrant
         const int grp = (warp - 4) >> 2;
@@ -951,6 +964,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         uint32_t tcount = 0;
         uint32_t err = 0;
+        uint32_t npass = 0;  // staging groups this warp has written (fast int8 epilogue)
         constexpr bool kFast = EK >= EK_FAST_T_S && EK <= EK_FAST_PC_D;
         // Tile-invariant RESCALE constants (per-tensor values are channel 0's).
         FastConst fk{0, 0, 0, 0, false, false, false};
@@ -1020,7 +1034,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
             // (the column-constant staging above is shared by both groups: every warp passes
             // every tile's key check, so the staging barriers pair up)
-            if (p.epi_groups ? buf != grp : cols == 0) continue;
+            if (p.epi_groups ? static_cast<int>(tcount % kEpiGroups) != grp : cols == 0) continue;
             // Pointers indexed by the absolute output column.
             const int32_t* cst_n = ct_stage + sbuf * 1024 - nt * BN;
             // Border class of this thread's row (before the accumulator wait: the lookups overlap it).
@@ -1065,7 +1079,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 // swizzled by row): one TMA store of the block when the output allows it (p.tma_out),
                 // else row-contiguous stores (a warp writes 8 rows x 64 B per store instead of 32
                 // scattered 16 B pieces).
-                uint4* wst = reinterpret_cast<uint4*>(scratch + 3072) + (warp - 4) * 128;
+                uint4* wst = reinterpret_cast<uint4*>(scratch + 3072) + (warp - 4) * 256;
                 int8_t* obase = reinterpret_cast<int8_t*>(p.out) + static_cast<long long>(b) * p.out_batch_stride;
                 const bool vec_ok = (p.ldo & 15) == 0 && (p.out_batch_stride & 15) == 0 &&
                                     (reinterpret_cast<uintptr_t>(p.out) & 15) == 0;
@@ -1079,7 +1093,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 // a warp with a border row adds every row's delta (zeros for interior rows)
                 const FastTile h{&tmO, b, taddr, cols, n_end, nb, rowterm, cst_n, warp_delta ? delta_fast : nullptr,
                                  fm, fsh, fhz, wst, lane, mrow0, obase, vec_ok, ftr};
-                fast_tile_pass<EK, (BN / 2 < 64 ? BN / 2 : 64), (EF & kEfRow) != 0, (EF & kEfDelta) != 0>(p, fk, h);
+                fast_tile_pass<EK, (BN / 2 < 64 ? BN / 2 : 64), (EF & kEfRow) != 0, (EF & kEfDelta) != 0>(p, fk, h,
+                                                                                                          npass);
             } else {
             // Two register sets: the next chunk's TMEM load overlaps this chunk's epilogue.
             uint32_t accA[kChunk], accB[kChunk];
