@@ -633,6 +633,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // fresh buffer, and the previous use of the buffer of its later tile t (tile t - 4) was
     // filled before the group's previous tile t - 3, which it has already waited for.
     const int NB = p.epi_groups ? 4 : 2;
+    const int NB_LOG = p.epi_groups ? 2 : 1;  // buffer of tile count t: t & (NB - 1), its use: t >> NB_LOG
     uint64_t* tfull = bars + 2 * S;      // [4]
     uint64_t* tempty = tfull + 4;        // [4]
     uint64_t* rsfull = tempty + 4;       // [4]
@@ -703,6 +704,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 long long bkey[S];
 #pragma unroll
                 for (int i = 0; i < S; ++i) bkey[i] = -1;
+                int rs_s = 0;       // ring position of `it`: stage it % SE and its phase parity, stepped
+                uint32_t rs_ph = 0; // (no division by the runtime stage count)
                 for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
                     int b, mt, nt;
                     tile_coords(p, tile, b, mt, nt);
@@ -719,8 +722,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     }
                     int cb = 0, kx = 0, ky = 0, tap = 0;  // k block kb = (ky * KW + kx) * c_blocks + cb, stepped
                     for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
-                        const int s = it % SE;
-                        const uint32_t ph = (it / SE) & 1;
+                        const int s = rs_s;
+                        const uint32_t ph = rs_ph;
+                        if (++rs_s == SE) { rs_s = 0; rs_ph ^= 1; }  // the ring position of it + 1
                         if (!mbar_wait_bounded(&empty[s], ph ^ 1, abort_flag, limit)) { ok = false; break; }
                         uint8_t* sa = stage_base + s * Cfg::STAGE_BYTES;
                         uint8_t* sb = sa + Cfg::A_BYTES;
@@ -791,16 +795,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 const uint32_t idesc = Cfg::kKind == 0 ? idesc_i8(BM, BN, Cfg::kBMN)
                                                        : idesc_f16(BM, BN, p.in_bf16 != 0, Cfg::kBMN);
                 uint32_t it = 0, tcount = 0;
+                int rs_s = 0;        // ring position of `it`, stepped
+                uint32_t rs_ph = 0;
                 bool ok = true;
                 for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++tcount) {
-                    const int buf = tcount % NB;
-                    const uint32_t tph = (tcount / NB) & 1;
+                    const int buf = tcount & (NB - 1);
+                    const uint32_t tph = (tcount >> NB_LOG) & 1;
                     if (!mbar_wait_bounded(&tempty[buf], tph ^ 1, abort_flag, limit)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * BN);
                     for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
-                        const int s = it % SE;
-                        const uint32_t ph = (it / SE) & 1;
+                        const int s = rs_s;
+                        const uint32_t ph = rs_ph;
+                        if (++rs_s == SE) { rs_s = 0; rs_ph ^= 1; }
                         if (!mbar_wait_bounded(&full[s], ph, abort_flag, limit)) { ok = false; break; }
                         tc_fence_after();
                         if (kGemmTrace && p.trace && blockIdx.x == 0 && it < 128) p.trace[128 + it] = clock64();
@@ -840,12 +847,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             if (need_rowsum) {
                 const int row0 = (warp - 2) * 64;
                 uint32_t it = 0, tcount = 0;
+                int rs_s = 0;        // ring position of `it`, stepped
+                uint32_t rs_ph = 0;
                 bool ok = true;
                 for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++tcount) {
                     int sum0 = 0, sum1 = 0;
                     for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
-                        const int s = it % SE;
-                        const uint32_t ph = (it / SE) & 1;
+                        const int s = rs_s;
+                        const uint32_t ph = rs_ph;
+                        if (++rs_s == SE) { rs_s = 0; rs_ph ^= 1; }
                         if (!mbar_wait_bounded(&full[s], ph, abort_flag, limit)) { ok = false; break; }
                         const uint8_t* sa0 = stage_base + s * Cfg::STAGE_BYTES;
                         // two taps per stage: the second sub-tile holds data only when the stage has two taps
@@ -877,8 +887,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         if (kGemmTrace && p.trace && blockIdx.x == 0 && it < 128 && warp == 2 && lane == 0) p.trace[256 + it] = clock64();
                     }
                     if (!ok) break;
-                    const int buf = tcount % NB;
-                    const uint32_t tph = (tcount / NB) & 1;
+                    const int buf = tcount & (NB - 1);
+                    const uint32_t tph = (tcount >> NB_LOG) & 1;
                     if (!mbar_wait_bounded(&rsempty[buf], tph ^ 1, abort_flag, limit)) { ok = false; break; }
                     rowsum_buf[buf * 128 + row0 + lane] = sum0;
                     rowsum_buf[buf * 128 + row0 + 32 + lane] = sum1;
@@ -1004,8 +1014,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++tcount) {
             int b, mt, nt;
             tile_coords(p, tile, b, mt, nt);
-            const int buf = tcount % NB;
-            const uint32_t tph = (tcount / NB) & 1;
+            const int buf = tcount & (NB - 1);
+            const uint32_t tph = (tcount >> NB_LOG) & 1;
             const int key = b * p.n_tiles + nt;
             if (stage_cols && key != staged_key) {
                 if (e.colterm != nullptr && p.cs.b != nullptr && staged_key < 0) {
