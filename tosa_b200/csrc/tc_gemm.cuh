@@ -616,7 +616,7 @@ __device__ __forceinline__ void fast_tile_pass(const GemmParams& p, const FastCo
 template <class Cfg, int EK, int EF>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmO, GemmParams p) {
+                   const __grid_constant__ CUtensorMap tmO, const __grid_constant__ GemmParams p) {
     constexpr int BM = Cfg::BM, BN = Cfg::kBN, S = Cfg::kStages;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte alignment by an offset into the shared array: pointer arithmetic on smem_raw keeps the
