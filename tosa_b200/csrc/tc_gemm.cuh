@@ -75,13 +75,13 @@ enum : int {
 // 16 warps: warpgroup 0 = TMA producer, MMA issuer and two row-sum warps; warpgroups 1-3 =
 // 12 epilogue warps in three groups of four (one warp per TMEM lane quadrant). Launched with
 // 128 registers a thread (65,536 for the CTA); warpgroup 0 gives back down to kRoleRegs and
-// the epilogue warpgroups take up to kEpiRegs: 128 * kRoleRegs + 384 * kEpiRegs = 65,536.
+// the epilogue warpgroups take up to kEpiRegs: 128 * kRoleRegs + 384 * kEpiRegs <= 65,536.
 constexpr int kGemmThreads = 512;
 constexpr int kEpiWarps = 12;
 constexpr int kEpiGroups = 3;
 constexpr int kLaunchRegs = 128;
-constexpr int kRoleRegs = 56;
-constexpr int kEpiRegs = 152;
+constexpr int kRoleRegs = 88;
+constexpr int kEpiRegs = 136;
 static_assert(128 * kRoleRegs + 384 * kEpiRegs <= kGemmThreads * kLaunchRegs, "register split above the launch total");
 // Shared memory per CTA: the stage ring, then 1 KB of alignment slack, the barriers and row
 // sums, and the epilogue scratch (column-sum reduction and staged column constants, 12 KB,
