@@ -1,9 +1,8 @@
 """Failure detection on the GPU, in forms that fault, trap or hang nothing.
 
 * A bounded wait that runs out: the context's wait bound is set to zero, so the
-  first wait of an ordinary int8 MATMUL that is not satisfied at once (the
-  cross-CTA wait for the B column sums of the a zero point, a spin on a
-  counter) gives up. The kernel unwinds by design -- its TMA loads and MMAs
+  first wait of an ordinary int8 MATMUL that is not satisfied at once (for
+  example the MMA warp's wait for the first stage's copies) gives up. The kernel unwinds by design -- its TMA loads and MMAs
   drain under their own bound, tensor memory is released -- and the next
   synchronize reports Timeout (TB_ERR_TIMEOUT). With the bound restored, the
   same context runs the same product and a convolution exactly (a leaked

@@ -3,8 +3,8 @@
 It serves callers that cannot call cudaMalloc themselves or through this
 library -- for example code whose device memory is owned by another
 allocator, or code running where allocation is not allowed -- by keeping the
-kernel's scratch (column sums for the a zero point, a cross-CTA counter, the
-packed RESCALE constants, the error word) in a fixed file-scope device array.
+kernel's scratch (column terms for the a zero point, the packed RESCALE
+constants, the error word) in a fixed file-scope device array.
 
 The checks: its results equal the regular entry point's (tb_matmul, which
 allocates per-plan scratch) and the oracle's bit for bit -- integer results,

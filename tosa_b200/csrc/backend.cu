@@ -585,8 +585,6 @@ tb_status matmul_plan_create(tb_context* ctx, const tb_matmul_desc* d, int t_bat
         // padded by one tile: the epilogue reads whole 16-column chunks without clamping
         const size_t cbatch = t_batch ? static_cast<size_t>(t_batch) : static_cast<size_t>(d->n);
         cudaError_t ce = cudaMalloc(&p->d_colterm, sizeof(int32_t) * (cbatch * d->w + 256));
-        if (ce == cudaSuccess) ce = cudaMalloc(&p->d_counter, sizeof(unsigned int));
-        if (ce == cudaSuccess) ce = cudaMemset(p->d_counter, 0, sizeof(unsigned int));
         if (ce != cudaSuccess) { free_rescale_plan(&p->rs); delete p; return fail(TB_ERR_CUDA, "colterm alloc failed"); }
     }
     *out = p;
@@ -718,26 +716,20 @@ extern "C" TB_API tb_status tb_matmul_plan_run(tb_matmul_plan* p, const void* a,
             ep.colterm = p->d_colterm;
             ep.colterm_bstride = d.w;
         } else if (d.a_zp != 0) {
-            // colterm = -a_zp * colsum(B) + c * a_zp * b_zp, reduced inside the GEMM by the epilogue warps
-            // during the first main loop (cooperative launch; see ColsumJob).
-            const uint32_t cst = static_cast<uint32_t>(d.c) * static_cast<uint32_t>(d.a_zp) *
-                                 static_cast<uint32_t>(d.b_zp);
-            ColsumJob& cs = gp.cs;
-            cs.b = static_cast<const int8_t*>(b);
-            cs.c = d.c;
-            cs.w = d.w;
-            cs.units = d.n * ((d.w + 63) / 64);
-            cs.scale = static_cast<int32_t>(static_cast<uint32_t>(-d.a_zp) * tmul);
-            cs.add = static_cast<int32_t>(cst * tmul);
-            cs.out = p->d_colterm;
-            cs.counter = p->d_counter;
-            if (p->replayable || static_cast<unsigned long long>(p->epoch + 1) * cs.units >= (1ull << 31)) {
-                // replayable: the same counter target on every run, so a captured launch can be replayed
-                TB_CUDA(cudaMemsetAsync(p->d_counter, 0, sizeof(unsigned int), st));
-                p->epoch = 0;
-            }
-            p->epoch += 1;
-            cs.target = p->epoch * static_cast<unsigned int>(cs.units);
+            // colterm = -a_zp * colsum(B) + c * a_zp * b_zp (x 2^k for the small-range epilogue), by a
+            // kernel before the GEMM; the GEMM is a programmatic dependent launch and waits for the
+            // column terms only in its epilogue, so its main loop overlaps the column sums
+            const int32_t scale = static_cast<int32_t>(static_cast<uint32_t>(-d.a_zp) * tmul);
+            const int32_t add = static_cast<int32_t>(static_cast<uint32_t>(d.c) * static_cast<uint32_t>(d.a_zp) *
+                                                     static_cast<uint32_t>(d.b_zp) * tmul);
+            if (p->path == 0)  // 16-byte B rows
+                colterm_cols_i8<<<dim3((d.w + 63) / 64, d.n), kColtermThreads, 0, st>>>(
+                    d.c, d.w, static_cast<const int8_t*>(b), scale, add, p->d_colterm);
+            else
+                colterm_const_i8<<<dim3((d.w + 31) / 32, d.n), dim3(32, 8), 0, st>>>(
+                    d.c, d.w, static_cast<const int8_t*>(b), scale, add, p->d_colterm);
+            TB_LAUNCHED(ctx);
+            ep.pdl_wait = 1;
             ep.colterm = p->d_colterm;
             ep.colterm_bstride = d.w;
         }
@@ -805,7 +797,6 @@ extern "C" TB_API void tb_matmul_plan_destroy(tb_matmul_plan* p) {
     free_rescale_plan(&p->rs);
     free_small_range(&p->sr);
     if (p->d_colterm) cudaFree(p->d_colterm);
-    if (p->d_counter) cudaFree(p->d_counter);
     if (p->d_bpad) cudaFree(p->d_bpad);
     delete p;
 }

@@ -84,12 +84,6 @@ tb_status launch_gemm(tb_context* ctx, const CUtensorMap& tmA, const CUtensorMap
         attr[na].val.programmaticStreamSerializationAllowed = 1;
         ++na;
     }
-    if (p.cs.b != nullptr) {
-        // CTAs wait on one another's column sums: all must be resident at once.
-        attr[na].id = cudaLaunchAttributeCooperative;
-        attr[na].val.cooperative = 1;
-        ++na;
-    }
     cfg.attrs = attr;
     cfg.numAttrs = na;
     // the output map (fast int8 epilogue with TMA stores), or an unused placeholder

@@ -199,9 +199,6 @@ struct tb_matmul_plan {
     tb::SmallRange sr;
     int bn = 256;
     int32_t* d_colterm = nullptr;  // [n][w] (+ one tile of padding) when a_zp != 0
-    unsigned int* d_counter = nullptr;  // column-sum units finished, grows by `units` per run
-    unsigned int epoch = 0;
-    bool replayable = false;  // reset the column-sum counter on every run (CUDA-graph replay)
     int wp = 0;                // path 5: padded B row length
     int8_t* d_bpad = nullptr;  // path 5: [n][c][wp] copy of B
     const void* a_cached = nullptr;

@@ -7,8 +7,8 @@
 // forbids allocation (for example while another component holds the device's
 // memory budget), or embedders that only hand over pre-sized input and output
 // buffers. The regular MATMUL entry points allocate per-plan device scratch
-// (the B column sums used for the a zero point, a cross-CTA counter, the packed
-// RESCALE constants and the error word); this entry point keeps all of that in
+// (the B column terms used for the a zero point, the packed RESCALE constants
+// and the error word); this entry point keeps all of that in
 // one file-scope device array instead, so it performs no allocation. The
 // caller still passes inputs and outputs.
 //
@@ -21,8 +21,7 @@
 // have. The array's device address is resolved once per device and kept, so
 // the entry point assumes the device's primary context is not reset
 // (cudaDeviceReset) while the process uses it. Every call shares it and
-// it keeps the last call's contents: each call clears the error word and the
-// counter first. Calls that overlap on the GPU (other streams, other host
+// it keeps the last call's contents: each call clears the error word first. Calls that overlap on the GPU (other streams, other host
 // threads) race on the array; serialise them.
 #include <cuda_runtime.h>
 
@@ -36,7 +35,7 @@
 namespace {
 
 constexpr size_t kScratchBytes = 2u << 20;
-constexpr size_t kColtermOffset = 256;                 // after the error word (0) and the counter (4)
+constexpr size_t kColtermOffset = 256;                 // after the error word (0)
 constexpr long long kMaxColterm = 131072;              // n * w when a_zp != 0
 constexpr int kMaxRescaleChannels = 16384;             // per-channel RESCALE multipliers / shifts
 constexpr size_t kBlobOffset = kColtermOffset + sizeof(int32_t) * (kMaxColterm + 256);
@@ -135,11 +134,8 @@ extern "C" TB_API tb_status tb_matmul_i8_noalloc(const tb_matmul_desc* d, const 
             place_small_range(&plan.sr, dev_sr, rescale->channels);
         }
     }
-    if (path == 0 && d->a_zp != 0) {
-        plan.d_colterm = reinterpret_cast<int32_t*>(su.scratch + kColtermOffset);
-        plan.d_counter = reinterpret_cast<unsigned int*>(su.scratch + 4);
-    }
-    // The array keeps the previous call's contents: the error word and the counter start at zero.
+    if (path == 0 && d->a_zp != 0) plan.d_colterm = reinterpret_cast<int32_t*>(su.scratch + kColtermOffset);
+    // The array keeps the previous call's contents: the error word starts at zero.
     TB_CUDA(cudaMemsetAsync(su.scratch, 0, 8, st));
     TB_TRY(tb_matmul_plan_run(&plan, a, b, out, stream_));
     // Data-dependent errors (RESCALE ranges) are reported by this call itself.

@@ -59,15 +59,24 @@ __device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t pa
     return ok != 0;
 }
 
+// The global nanosecond timer (trace builds).
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
 // Bounded wait: waits (suspended between checks) until the phase with `parity`
 // completes or the shared abort flag (when given) is raised or `limit` clock cycles
 // pass. Returns false when it gave up (the caller then records ERR_TIMEOUT and unwinds).
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                                   long long limit) {
     if (mbar_try_wait(bar, parity)) return true;
+    // suspended at most 20 us per check, less under a short bound (a zero bound fails at once)
+    const uint32_t hint_ns = limit < 40000 ? static_cast<uint32_t>(limit > 0 ? limit / 2 : 0) : 20000u;
     long long t0 = clock64();
     while (true) {
-        if (mbar_try_wait_suspend(bar, parity, 20000u)) return true;
+        if (mbar_try_wait_suspend(bar, parity, hint_ns)) return true;
         if (abort_flag != nullptr && *abort_flag) return false;
         if (clock64() - t0 > limit) return false;
     }

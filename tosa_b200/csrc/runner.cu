@@ -1264,7 +1264,6 @@ tb_status do_compile(tb_graph* G) {
         case K_MATMUL:
             st = s.mt_batch ? tb_matmul_t_plan_create(ctx, &s.mdesc, s.mt_batch, s.has_rescale ? &s.rattr : nullptr, &s.mm)
                             : tb_matmul_plan_create(ctx, &s.mdesc, s.has_rescale ? &s.rattr : nullptr, &s.mm);
-            if (st == TB_OK) s.mm->replayable = (G->flags & TB_GRAPH_CUDA_GRAPH) != 0;
             if (st == TB_OK && G->tensors[s.in[1]].is_static && G->tensors[s.in[1]].dev != nullptr)
                 st = tb_matmul_plan_set_constant_b(s.mm, G->tensors[s.in[1]].dev, nullptr);  // e.g. FC weights
             break;

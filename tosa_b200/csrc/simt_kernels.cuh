@@ -1029,55 +1029,84 @@ __global__ void matmul_direct_float(int n, int h, int c, int w, const void* __re
 // Zero-point helpers of the tensor-core path
 // ---------------------------------------------------------------------------
 
-// colsum[b][col] += scale * sum_{k in chunk} B[b][k][col] (+ add once per
-// column)  (MATMUL, B is [n,c,w], w % 16 == 0; colsum zeroed first). With
-// scale = -a_zp and add = c*a_zp*b_zp this yields the epilogue's column term. Block = 64 column groups of 16 bytes x
-// 4 row slices; grid (ceil(w/1024), ceil(c/kchunk), n). Each thread sums 16
-// columns over kchunk/4 rows with 16-byte loads, the 4 slices are combined in
-// shared memory and each block adds its 1024 partial sums atomically. The
-// kernel releases its dependent launch immediately: the GEMM that consumes the
-// sums waits for them only in its epilogue (griddepcontrol.wait).
-__global__ void __launch_bounds__(256) matmul_colsum(int c, int w, int kchunk, const int8_t* __restrict__ bm,
-                                                     int32_t scale, int32_t add, int32_t* __restrict__ colsum) {
+// Column terms of MATMUL's B [n][c][w] (w % 16 == 0, 16-byte aligned rows):
+// out[bn][x] = scale * sum_k B[bn][k][x] + add (int32 wrap-around); with scale = -a_zp and
+// add = c * a_zp * b_zp (both x 2^k for the small-range epilogue) the epilogue's column term.
+// Block of 384 threads per 64 columns of one batch: 4 groups of 16 columns x 96 row slices,
+// every thread's loads 8 rows at a time in flight. Bytes are biased to unsigned (x ^ 0x80 is
+// x + 128) and summed in 16-bit lanes, even and odd bytes of each word apart (8 rows x 255
+// fits a lane), widened per batch of 8 rows; the bias comes off at the end. The 96 slices
+// are reduced in shared memory in two steps. The kernel releases its dependent launch at
+// once: the GEMM that reads `out` waits for it only in its epilogue (griddepcontrol.wait).
+constexpr int kColtermThreads = 384;
+__global__ void __launch_bounds__(kColtermThreads) colterm_cols_i8(int c, int w, const int8_t* __restrict__ b,
+                                                                  int32_t scale, int32_t add,
+                                                                  int32_t* __restrict__ out) {
     grid_launch_dependents();
-    __shared__ int32_t part[3][1024];
-    const int cg = threadIdx.x & 63, slice = threadIdx.x >> 6;
-    const int col = blockIdx.x * 1024 + cg * 16;
-    const int k0 = blockIdx.y * kchunk;
-    const int bn = blockIdx.z;
-    const int rows = max(0, min(kchunk, c - k0));
+    constexpr int kSlices = kColtermThreads / 4;
+    constexpr int kPitch = 68;  // 64 sums + 4 ints of padding: conflict-free 16-byte writes
+    __shared__ __align__(16) int32_t red[kSlices * kPitch];
+    __shared__ int32_t red2[6][64];
+    const int t = threadIdx.x, g = t & 3, slice = t >> 2;
+    const int bn = blockIdx.y, col0 = blockIdx.x * 64;
+    const int col = col0 + g * 16;
     int s[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) s[i] = 0;
+    for (int j = 0; j < 16; ++j) s[j] = 0;
+    int rows = 0;
     if (col < w) {
-        const int8_t* p = bm + (static_cast<long long>(bn) * c + k0) * w + col;
-#pragma unroll 16
-        for (int k = slice; k < rows; k += 4) {
-            const int4 v = __ldg(reinterpret_cast<const int4*>(p + static_cast<long long>(k) * w));
-            const int words[4] = {v.x, v.y, v.z, v.w};
+        const long long step = static_cast<long long>(kSlices) * w;
+        const int8_t* src = b + (static_cast<long long>(bn) * c + slice) * w + col;
+#pragma unroll 1
+        for (int k = slice; k < c; k += 8 * kSlices, src += 8 * step) {
+            uint4 v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                v[j] = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);  // biased zeros past c
+                if (k + kSlices * j < c) v[j] = __ldg(reinterpret_cast<const uint4*>(src + j * step));
+            }
+            rows += min(8, (c - k + kSlices - 1) / kSlices);
+            uint32_t ev[4] = {0, 0, 0, 0}, od[4] = {0, 0, 0, 0};
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const uint32_t wv[4] = {v[j].x ^ 0x80808080u, v[j].y ^ 0x80808080u, v[j].z ^ 0x80808080u,
+                                        v[j].w ^ 0x80808080u};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    ev[q] += wv[q] & 0x00ff00ffu;
+                    od[q] += (wv[q] >> 8) & 0x00ff00ffu;
+                }
+            }
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                s[4 * q + 0] += static_cast<int8_t>(words[q] & 0xff);
-                s[4 * q + 1] += static_cast<int8_t>((words[q] >> 8) & 0xff);
-                s[4 * q + 2] += static_cast<int8_t>((words[q] >> 16) & 0xff);
-                s[4 * q + 3] += words[q] >> 24;
+                s[4 * q + 0] += static_cast<int>(ev[q] & 0xffffu);
+                s[4 * q + 1] += static_cast<int>(od[q] & 0xffffu);
+                s[4 * q + 2] += static_cast<int>(ev[q] >> 16);
+                s[4 * q + 3] += static_cast<int>(od[q] >> 16);
             }
         }
     }
-    if (slice > 0) {
+    int4* r4 = reinterpret_cast<int4*>(red + slice * kPitch + g * 16);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) part[slice - 1][cg * 16 + i] = s[i];
+    for (int q = 0; q < 4; ++q)
+        r4[q] = make_int4(s[4 * q] - 128 * rows, s[4 * q + 1] - 128 * rows, s[4 * q + 2] - 128 * rows,
+                          s[4 * q + 3] - 128 * rows);
+    __syncthreads();
+    {
+        // 6 parts of 16 slices per column
+        const int cc = t & 63, part = t >> 6;
+        int sum = 0;
+#pragma unroll
+        for (int sl = 0; sl < kSlices / 6; ++sl) sum += red[(part * (kSlices / 6) + sl) * kPitch + cc];
+        red2[part][cc] = sum;
     }
     __syncthreads();
-    if (slice == 0 && col < w) {
-        int32_t* o = colsum + static_cast<long long>(bn) * w + col;
+    if (t < 64 && col0 + t < w) {
+        int sum = 0;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            const int t = s[i] + part[0][cg * 16 + i] + part[1][cg * 16 + i] + part[2][cg * 16 + i];
-            const uint32_t contrib = static_cast<uint32_t>(scale) * static_cast<uint32_t>(t) +
-                                     (blockIdx.y == 0 ? static_cast<uint32_t>(add) : 0u);
-            if (col + i < w) atomicAdd(reinterpret_cast<unsigned int*>(o + i), contrib);
-        }
+        for (int part = 0; part < 6; ++part) sum += red2[part][t];
+        out[static_cast<long long>(bn) * w + col0 + t] =
+            static_cast<int32_t>(static_cast<uint32_t>(scale) * static_cast<uint32_t>(sum) + static_cast<uint32_t>(add));
     }
 }
 

@@ -84,8 +84,8 @@ constexpr int kRoleRegs = 88;
 constexpr int kEpiRegs = 136;
 static_assert(128 * kRoleRegs + 384 * kEpiRegs <= kGemmThreads * kLaunchRegs, "register split above the launch total");
 // Shared memory per CTA: the stage ring, then 1 KB of alignment slack, the barriers and row
-// sums, and the epilogue scratch (column-sum reduction and staged column constants, 12 KB,
-// then two 2 KB output staging buffers per epilogue warp).
+// sums, and the epilogue scratch (a convolution's border-class tables and the staged column
+// constants, 12 KB, then two 2 KB output staging buffers per epilogue warp).
 constexpr int kSmemLimit = 232448;
 constexpr int kBarrierBytes = 3072;
 constexpr int kScratchBytes = 12288 + 4096 * kEpiWarps;
@@ -128,22 +128,6 @@ struct GemmEpilogue {
     int fbias_len;
 };
 
-// Column sums of MATMUL's B operand computed inside the GEMM (a_zp != 0):
-// the epilogue warps of every CTA reduce a share of 64-column units of
-// B[n][c][w] while the first main loop runs, write the final column term
-// scale * colsum + add, and count finished units on a global counter; every
-// epilogue waits (bounded) until counter >= target before its first tile.
-// target grows by `units` per launch, so the counter never needs a reset.
-// Requires all CTAs co-resident (cooperative launch).
-struct ColsumJob {
-    const int8_t* b;           // nullptr: no job
-    int c, w, units;           // units = n * ceil(w / 64)
-    int32_t scale, add;
-    int32_t* out;              // [n][w] (+ padding)
-    unsigned int* counter;
-    unsigned int target;
-};
-
 // Division by a runtime constant d as a multiply-high (Granlund-Montgomery): with
 // s = ceil(log2 d) and m = floor(2^32 (2^s - d) / d) + 1, n / d = (mulhi(n, m) + n) >> s
 // for 0 <= n < 2^31. The host fills it (make_fastdiv).
@@ -181,7 +165,6 @@ struct GemmParams {
     // [0,128) producer per stage issue, [128,256) MMA per stage start,
     // [256,384) row-sum per stage done, [384,400) epilogue tile start/end.
     long long* trace;
-    ColsumJob cs;
     // epilogue warps in two groups taking alternate tiles (set by the launcher when every CTA
     // has many tiles; otherwise both groups share each tile by column halves)
     int epi_groups;
@@ -688,6 +671,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const long long drain_limit = limit > kDrainCycles ? limit : kDrainCycles;
     const int SE = p.s_eff;  // stages of the ring in use
     if (kGemmTrace && p.trace && blockIdx.x == 0 && threadIdx.x == 0) p.trace[400] = clock64();
+    if (kGemmTrace && p.trace && threadIdx.x == 0) {
+        if (blockIdx.x == 0) p.trace[403] = static_cast<long long>(globaltimer_ns());
+        atomicMax(reinterpret_cast<unsigned long long*>(p.trace + 405), globaltimer_ns());
+    }
 
     if (warp < 4) {
         // warpgroup 0: producer, MMA issuer, row sums -- few registers, the rest to the epilogue
@@ -929,49 +916,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         int32_t* ct_stage = scratch + 1024;
         constexpr bool kPC = EK == EK_FAST_PC_S || EK == EK_FAST_PC_D;
         bool ok = true;
-        if (p.cs.b != nullptr) {
-            // ---- column sums of B (MATMUL a_zp): 16 column groups of 4 bytes x 16 row slices
-            // (the first 8 epilogue warps sum; the other 4 only join the barriers)
-            const ColsumJob& cs = p.cs;
-            const int g = et & 15, slice = et >> 4;
-            const int units_w = (cs.w + 63) / 64;
-            for (int u = blockIdx.x; u < cs.units; u += gridDim.x) {
-                const int bn = u / units_w, col = (u % units_w) * 64 + g * 4;
-                int s0 = 0, s1 = 0, s2 = 0, s3 = 0;
-                if (col < cs.w && slice < 16) {
-                    const int8_t* src = cs.b + (static_cast<long long>(bn) * cs.c + slice) * cs.w + col;
-#pragma unroll 8
-                    for (int k = slice; k < cs.c; k += 16, src += 16ll * cs.w) {
-                        const int x = __ldg(reinterpret_cast<const int*>(src));
-                        s0 += static_cast<int8_t>(x & 0xff);
-                        s1 += static_cast<int8_t>((x >> 8) & 0xff);
-                        s2 += static_cast<int8_t>((x >> 16) & 0xff);
-                        s3 += x >> 24;
-                    }
-                }
-                int32_t* red = scratch;  // [16 slices][64 columns]
-                if (slice < 16) {
-                    red[slice * 64 + g * 4 + 0] = s0;
-                    red[slice * 64 + g * 4 + 1] = s1;
-                    red[slice * 64 + g * 4 + 2] = s2;
-                    red[slice * 64 + g * 4 + 3] = s3;
-                }
-                if (!epi_sync()) { ok = false; break; }
-                if (et < 64) {
-                    int t = 0;
-#pragma unroll
-                    for (int sl = 0; sl < 16; ++sl) t += red[sl * 64 + et];
-                    const int cc = (u % units_w) * 64 + et;
-                    if (cc < cs.w)
-                        cs.out[static_cast<long long>(bn) * cs.w + cc] =
-                            static_cast<int32_t>(static_cast<uint32_t>(cs.scale) * static_cast<uint32_t>(t) +
-                                                 static_cast<uint32_t>(cs.add));
-                    __threadfence();
-                }
-                if (!epi_sync()) { ok = false; break; }
-                if (et == 0) atomicAdd(cs.counter, 1u);
-            }
-        }
         uint32_t tcount = 0;
         uint32_t err = 0;
         uint32_t npass = 0;  // staging groups this warp has written (fast int8 epilogue)
@@ -987,11 +931,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             fk.clamp_hi = e.rs.hi < 127;
             fk.clamp = fk.clamp_lo || fk.clamp_hi;
         }
-        // Border-class tables of a convolution, copied to shared memory once (the column-sum
-        // reduction area is free when there is no column-sum job).
+        // Border-class tables of a convolution, copied to shared memory once.
         const uint8_t* rcls = e.rowclass;
         const uint8_t* ccls = e.colclass;
-        if (e.rowclass != nullptr && p.cs.b == nullptr) {
+        if (e.rowclass != nullptr) {
             const int oh = p.conv_OHOW / p.conv_OW, ow = p.conv_OW;
             uint8_t* cl = reinterpret_cast<uint8_t*>(scratch);
             if (oh + ow <= 4096) {
@@ -1018,15 +961,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const uint32_t tph = (tcount >> NB_LOG) & 1;
             const int key = b * p.n_tiles + nt;
             if (stage_cols && key != staged_key) {
-                if (e.colterm != nullptr && p.cs.b != nullptr && staged_key < 0) {
-                    // all column sums published (bounded wait on the cross-CTA counter)
-                    const long long t0 = clock64();
-                    while (*reinterpret_cast<volatile unsigned int*>(p.cs.counter) < p.cs.target) {
-                        if (*abort_flag || clock64() - t0 > limit) { ok = false; break; }
-                    }
-                    __threadfence();
-                    if (!ok) break;
-                }
                 sbuf ^= 1;
                 int32_t* cst = ct_stage + sbuf * 1024;
                 // (the tables are padded to whole 256-column tiles)
@@ -1145,6 +1079,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tc_fence_after();
         tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
     }
+    // trace slots 403..405 (global timer, ns): CTA 0's start, the last CTA exit, the last CTA start
+    if (kGemmTrace && p.trace && threadIdx.x == 0)
+        atomicMax(reinterpret_cast<unsigned long long*>(p.trace + 404), globaltimer_ns());
 }
 
 }  // namespace tb
