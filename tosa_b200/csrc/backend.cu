@@ -1113,7 +1113,8 @@ static tb_status conv_plan_create(tb_context* ctx, const tb_conv2d_desc* d, cons
         const int cap = std::atoi(ev);
         if ((cap == 64 || cap == 128) && p->bn > cap) p->bn = cap;
     }
-    p->bk = (int8 && d->ic <= 64) ? 64 : 128;
+    // K block of one stage: the channel run of a tap, rounded up to 32, 64 or 128 bytes
+    p->bk = (int8 && d->ic <= 32) ? 32 : (int8 && d->ic <= 64) ? 64 : 128;
     p->tap2 = p->path == 0 && int8 && d->ic == 64 && taps >= 2 && p->bn <= 128;
     const int bke = p->bk / e;
     // Weight tensor map: [OC][KH*KW*IC], K-major.
@@ -1124,7 +1125,9 @@ static tb_status conv_plan_create(tb_context* ctx, const tb_conv2d_desc* d, cons
         // two taps per stage: one 128-byte box covers both taps' weights (adjacent in K)
         const uint32_t box[3] = {static_cast<uint32_t>(p->tap2 ? 2 * bke : bke), static_cast<uint32_t>(p->bn), 1};
         tb_status s = encode_tiled(&p->tmB, tmap_dtype(wt), 3, weight, dims, str, box,
-                                   (p->bk == 128 || p->tap2) ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+                                   (p->bk == 128 || p->tap2) ? CU_TENSOR_MAP_SWIZZLE_128B
+                                   : p->bk == 64            ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                            : CU_TENSOR_MAP_SWIZZLE_32B);
         if (s != TB_OK) return bail(s);
     }
     if (p->path == 1) {
@@ -1521,7 +1524,9 @@ extern "C" TB_API tb_status tb_conv2d_plan_run(tb_conv2d_plan* p, const void* in
         const uint32_t es[4] = {1, static_cast<uint32_t>(d.stride[1]), static_cast<uint32_t>(d.stride[0]), 1};
         TB_TRY(encode_im2col(&p->tmA, tmap_dtype(d.in_dtype), input, dims, str, lower, upper,
                              static_cast<uint32_t>(bke), 128, es,
-                             p->bk == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B));
+                             p->bk == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                             : p->bk == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                           : CU_TENSOR_MAP_SWIZZLE_32B));
         p->in_cached = input;
     }
     GemmParams gp{};

@@ -10,6 +10,7 @@ tb_status launch_i8_conv(tb_context* ctx, int bn, int bk, int ek, const CUtensor
     if (bn == BN_ && bk == BK_)                                                                      \
         return launch_int_ek<GemmCfg<0, BN_, BK_, false, true, gemm_stages(BN_, BK_)>, true>(ctx, ek, a, b, p, st);
     if (bk == 128) return launch_i8_conv_k128(ctx, bn, ek, a, b, p, st);
+    if (bk == 32) return launch_i8_conv_k32(ctx, bn, ek, a, b, p, st);
     TB_CONV_CASE(256, 64)
     TB_CONV_CASE(128, 64)
     TB_CONV_CASE(64, 64)

@@ -150,6 +150,8 @@ tb_status launch_i8_conv(tb_context* ctx, int bn, int bk, int ek, const CUtensor
                          const GemmParams& p, cudaStream_t st);
 tb_status launch_i8_conv_k128(tb_context* ctx, int bn, int ek, const CUtensorMap& a, const CUtensorMap& b,
                               const GemmParams& p, cudaStream_t st);
+tb_status launch_i8_conv_k32(tb_context* ctx, int bn, int ek, const CUtensorMap& a, const CUtensorMap& b,
+                              const GemmParams& p, cudaStream_t st);
 tb_status launch_i8_conv_tap2(tb_context* ctx, int bn, int ek, const CUtensorMap& a, const CUtensorMap& b,
                               const GemmParams& p, cudaStream_t st);
 tb_status launch_f16_matmul(tb_context* ctx, int bn, const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p,

@@ -190,7 +190,7 @@ struct GemmCfg {
     static constexpr int kKind = KIND;            // 0: int8, 1: f16/bf16
     static constexpr int BM = 128;
     static constexpr int kBN = BN;
-    static constexpr int kBKBytes = BK_BYTES;     // 64 (SW64) or 128 (SW128)
+    static constexpr int kBKBytes = BK_BYTES;     // 32 (SW32), 64 (SW64) or 128 (SW128)
     static constexpr int kElem = KIND == 0 ? 1 : 2;
     static constexpr int BK = BK_BYTES / kElem;   // elements of K per stage
     static constexpr int kMmaK = 32 / kElem;      // K per tcgen05.mma (32 bytes)
@@ -203,9 +203,9 @@ struct GemmCfg {
     static constexpr int kBKBytesB = TAP2 ? 2 * BK_BYTES : BK_BYTES;  // K bytes of B per stage
     static constexpr int B_BYTES = BN * kBKBytesB;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int SW_CODE = BK_BYTES == 128 ? 2 : 4;        // UMMA layout type
+    static constexpr int SW_CODE = BK_BYTES == 128 ? 2 : (BK_BYTES == 64 ? 4 : 6);  // UMMA layout type
     static constexpr int ATOM_SBO = 8 * BK_BYTES;                   // 8 rows of one swizzle atom
-    static constexpr int SW_CODE_B = kBKBytesB == 128 ? 2 : 4;
+    static constexpr int SW_CODE_B = kBKBytesB == 128 ? 2 : (kBKBytesB == 64 ? 4 : 6);
     static constexpr int ATOM_SBO_B = 8 * kBKBytesB;
     // MN-major B: 128-byte rows of N, one box per 128 bytes of N.
     static constexpr int B_MN_CHUNK = 128 / kElem;                  // N elements per box
@@ -218,6 +218,7 @@ struct GemmCfg {
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + kBarrierBytes + kScratchBytes;
     static_assert(SMEM_BYTES <= kSmemLimit, "shared memory above 227 KB");
     static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "UMMA N for M=128; each epilogue warp walks pairs of 16-column chunks");
+    static_assert(BK_BYTES == 32 || BK_BYTES == 64 || BK_BYTES == 128, "K blocks of 32, 64 or 128 bytes");
     static_assert(!B_MN_MAJOR || BK_BYTES == 128, "MN-major B uses 128-byte K blocks");
     static_assert(!TAP2 || (KIND == 0 && IM2COL && BK_BYTES == 64), "two taps per stage: int8 im2col, 64 channels");
 };
@@ -458,22 +459,17 @@ __device__ __forceinline__ void fast_chunk_i8(const GemmParams& p, const uint32_
 #pragma unroll
         for (int j = 0; j < W; ++j) v[j] = one(v[j], fk.m, fk.sh, fk.c);
     }
-    // output zero point (when not folded into c) and the lower clamp in one add-max; the
-    // saturating packs complete the clamp to the int8 range
-    const int32_t zp = fk.add_zp, lo = p.epi.rs.lo;
+    // output zero point (when not folded into c) and the lower clamp in one add-max, the upper
+    // clamp (at most 127), then byte permutes pack the in-range values
+    const int32_t zp = fk.add_zp, lo = max(p.epi.rs.lo, -128), hi = min(p.epi.rs.hi, 127);
 #pragma unroll
-    for (int j = 0; j < W; ++j) v[j] = max(v[j] + zp, lo);
-    if (fk.clamp_hi) {  // an upper bound below 127 (uniform; rare)
-        const int32_t hi = p.epi.rs.hi;
-#pragma unroll
-        for (int j = 0; j < W; ++j) v[j] = min(v[j], hi);
-    }
+    for (int j = 0; j < W; ++j) v[j] = min(max(v[j] + zp, lo), hi);
 #pragma unroll
     for (int q = 0; q < W / 16; ++q)
-        out16[q] = make_uint4(pack4_sat_i8(v[16 * q + 0], v[16 * q + 1], v[16 * q + 2], v[16 * q + 3]),
-                              pack4_sat_i8(v[16 * q + 4], v[16 * q + 5], v[16 * q + 6], v[16 * q + 7]),
-                              pack4_sat_i8(v[16 * q + 8], v[16 * q + 9], v[16 * q + 10], v[16 * q + 11]),
-                              pack4_sat_i8(v[16 * q + 12], v[16 * q + 13], v[16 * q + 14], v[16 * q + 15]));
+        out16[q] = make_uint4(pack4_clamped_i8(v[16 * q + 0], v[16 * q + 1], v[16 * q + 2], v[16 * q + 3]),
+                              pack4_clamped_i8(v[16 * q + 4], v[16 * q + 5], v[16 * q + 6], v[16 * q + 7]),
+                              pack4_clamped_i8(v[16 * q + 8], v[16 * q + 9], v[16 * q + 10], v[16 * q + 11]),
+                              pack4_clamped_i8(v[16 * q + 12], v[16 * q + 13], v[16 * q + 14], v[16 * q + 15]));
 }
 
 // One epilogue warp's pass over its part of a tile (32 rows x h.cols columns) in the fast
@@ -852,8 +848,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         const int4* r0 = reinterpret_cast<const int4*>(sa + (row0 + lane) * Cfg::kBKBytes);
                         const int4* r1 = reinterpret_cast<const int4*>(sa + (row0 + 32 + lane) * Cfg::kBKBytes);
                         // Chunk order rotated per lane: the 8 lanes of a shared-memory phase hit 8 different
-                        // 16-byte bank groups (rows are 128 or 64 bytes long).
-                        const int rot = Cfg::kBKBytes == 128 ? (lane & 7) : ((lane >> 1) & 3);
+                        // 16-byte bank groups (rows are 128, 64 or 32 bytes long).
+                        const int rot = Cfg::kBKBytes == 128 ? (lane & 7)
+                                                             : (Cfg::kBKBytes == 64 ? ((lane >> 1) & 3) : ((lane >> 2) & 1));
     #pragma unroll
                         for (int c = 0; c < Cfg::kBKBytes / 16; ++c) {
                             const int cc = c ^ rot;
