@@ -150,14 +150,6 @@ __device__ __forceinline__ uint32_t pack4_sat_i8(int32_t v0, int32_t v1, int32_t
     return d;
 }
 
-// Four values already inside [-128, 127] packed as int8 bytes by byte permutes (integer
-// ALU), not by the saturating converts (which issue on the narrower conversion pipe).
-__device__ __forceinline__ uint32_t pack4_clamped_i8(int32_t v0, int32_t v1, int32_t v2, int32_t v3) {
-    const uint32_t lo = __byte_perm(static_cast<uint32_t>(v0), static_cast<uint32_t>(v1), 0x0040u);
-    const uint32_t hi = __byte_perm(static_cast<uint32_t>(v2), static_cast<uint32_t>(v3), 0x0040u);
-    return __byte_perm(lo, hi, 0x5410u);
-}
-
 // The fast RESCALE of one value (every shift s in [33, 62], m >= 0, checked on the
 // host): apply_scale_32's (v*m + 2^(s-1) [+-2^30]) >> s as the high word of
 // v*m [+-2^30 by the sign of v] plus hz = 2^(s-33) (+ zp * 2^(s-32)), shifted by

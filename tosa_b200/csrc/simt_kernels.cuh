@@ -797,7 +797,6 @@ __device__ __forceinline__ void dw_strip_row(const uint32_t (&top)[DwStrip<S>::N
     dw_row_mac<S>(acc, top, w[0], w[1], w[2]);
     dw_row_mac<S>(acc, mid, w[3], w[4], w[5]);
     dw_row_mac<S>(acc, bot, w[6], w[7], w[8]);
-    const int32_t lo8 = max(e.lo, -128), hi8 = min(e.hi, 127);  // int8 output bounds inside the clamp
     if (EK == 0) {
         const int c0 = c4 * 4;
         const long long cn = static_cast<long long>(g.c4) * 4;
@@ -830,8 +829,8 @@ __device__ __forceinline__ void dw_strip_row(const uint32_t (&top)[DwStrip<S>::N
             v[2] = small(acc[p][2], m.z, sh.z, c.z);
             v[3] = small(acc[p][3], m.w, sh.w, c.w);
 #pragma unroll
-            for (int q = 0; q < 4; ++q) v[q] = min(max(v[q] + e.zp_add, lo8), hi8);
-            o[p * g.c4] = pack4_clamped_i8(v[0], v[1], v[2], v[3]);
+            for (int q = 0; q < 4; ++q) v[q] = min(max(v[q] + e.zp_add, e.lo), e.hi);
+            o[p * g.c4] = pack4_sat_i8(v[0], v[1], v[2], v[3]);
         }
     } else {
         const int pc = e.per_channel ? c4 : 0;
@@ -848,8 +847,8 @@ __device__ __forceinline__ void dw_strip_row(const uint32_t (&top)[DwStrip<S>::N
             v[2] = rescale_f2<EK == 2>(acc[p][2], m.z, sh.z, hz.z);
             v[3] = rescale_f2<EK == 2>(acc[p][3], m.w, sh.w, hz.w);
 #pragma unroll
-            for (int q = 0; q < 4; ++q) v[q] = min(max(v[q] + e.zp_add, lo8), hi8);
-            o[p * g.c4] = pack4_clamped_i8(v[0], v[1], v[2], v[3]);
+            for (int q = 0; q < 4; ++q) v[q] = min(max(v[q] + e.zp_add, e.lo), e.hi);
+            o[p * g.c4] = pack4_sat_i8(v[0], v[1], v[2], v[3]);
         }
     }
 }

@@ -459,17 +459,22 @@ __device__ __forceinline__ void fast_chunk_i8(const GemmParams& p, const uint32_
 #pragma unroll
         for (int j = 0; j < W; ++j) v[j] = one(v[j], fk.m, fk.sh, fk.c);
     }
-    // output zero point (when not folded into c) and the lower clamp in one add-max, the upper
-    // clamp (at most 127), then byte permutes pack the in-range values
-    const int32_t zp = fk.add_zp, lo = max(p.epi.rs.lo, -128), hi = min(p.epi.rs.hi, 127);
+    // output zero point (when not folded into c) and the lower clamp in one add-max; the
+    // saturating packs complete the clamp to the int8 range
+    const int32_t zp = fk.add_zp, lo = p.epi.rs.lo;
 #pragma unroll
-    for (int j = 0; j < W; ++j) v[j] = min(max(v[j] + zp, lo), hi);
+    for (int j = 0; j < W; ++j) v[j] = max(v[j] + zp, lo);
+    if (fk.clamp_hi) {  // an upper bound below 127 (uniform; rare)
+        const int32_t hi = p.epi.rs.hi;
+#pragma unroll
+        for (int j = 0; j < W; ++j) v[j] = min(v[j], hi);
+    }
 #pragma unroll
     for (int q = 0; q < W / 16; ++q)
-        out16[q] = make_uint4(pack4_clamped_i8(v[16 * q + 0], v[16 * q + 1], v[16 * q + 2], v[16 * q + 3]),
-                              pack4_clamped_i8(v[16 * q + 4], v[16 * q + 5], v[16 * q + 6], v[16 * q + 7]),
-                              pack4_clamped_i8(v[16 * q + 8], v[16 * q + 9], v[16 * q + 10], v[16 * q + 11]),
-                              pack4_clamped_i8(v[16 * q + 12], v[16 * q + 13], v[16 * q + 14], v[16 * q + 15]));
+        out16[q] = make_uint4(pack4_sat_i8(v[16 * q + 0], v[16 * q + 1], v[16 * q + 2], v[16 * q + 3]),
+                              pack4_sat_i8(v[16 * q + 4], v[16 * q + 5], v[16 * q + 6], v[16 * q + 7]),
+                              pack4_sat_i8(v[16 * q + 8], v[16 * q + 9], v[16 * q + 10], v[16 * q + 11]),
+                              pack4_sat_i8(v[16 * q + 12], v[16 * q + 13], v[16 * q + 14], v[16 * q + 15]));
 }
 
 // One epilogue warp's pass over its part of a tile (32 rows x h.cols columns) in the fast
