@@ -560,6 +560,11 @@ tb_status matmul_plan_create(tb_context* ctx, const tb_matmul_desc* d, int t_bat
     TB_CUDA(cudaSetDevice(ctx->device));
     int path = 0, bn = 256;
     TB_TRY(matmul_validate(d, rescale != nullptr, &path, &bn, t_batch));
+    // Few tiles (a classifier over one batch of images): 128-wide tiles when even those fit one
+    // wave of the SMs, so twice as many SMs stream the contraction
+    if (bn == 256 && (path == 0 || path == 1 || path == 5) &&
+        static_cast<long long>(d->n) * ((d->h + 127) / 128) * ((d->w + 127) / 128) <= ctx->num_sms)
+        bn = 128;
     tb_matmul_plan* p = new tb_matmul_plan;
     p->ctx = ctx;
     p->d = *d;
@@ -1108,6 +1113,14 @@ static tb_status conv_plan_create(tb_context* ctx, const tb_conv2d_desc* d, cons
     if (p->path >= 2) { *out = p; return TB_OK; }
 
     p->bn = oc <= 64 ? 64 : oc <= 128 ? 128 : 256;
+    {
+        // Few tiles (small maps, few images): narrower tiles while their count stays within one
+        // wave of the SMs, so more SMs share the contraction (a 7x7 map of 64 images has 25 row
+        // tiles: 50 tiles of 256 output channels, 100 of 128)
+        const long long m_tiles = (static_cast<long long>(d->n) * oh * ow + 127) / 128;
+        auto tiles = [&](int bn) { return m_tiles * ((oc + bn - 1) / bn); };
+        while (p->bn > 64 && tiles(p->bn / 2) <= ctx->num_sms) p->bn /= 2;
+    }
     // TB_CONV_MAX_BN (read at plan creation) caps the tile width of the tensor-core convolutions
     if (const char* ev = std::getenv("TB_CONV_MAX_BN")) {
         const int cap = std::atoi(ev);
