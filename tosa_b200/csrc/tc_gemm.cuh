@@ -538,13 +538,13 @@ __device__ __forceinline__ void fast_tile_pass(const GemmParams& p, const FastCo
             if (lane == 0) bulk_wait_read1();
             __syncwarp();
         }
-#pragma unroll
-        for (int c = 0; c < NCH; ++c) {
+        // chunk c of the group: its accumulators in register set c % 2, the next chunk's TMEM load
+        // in flight into the other set. Pairs of chunks per iteration (not the whole group
+        // unrolled) keep the loop's code small.
+        auto chunk = [&](int c, uint32_t(&cur)[FW], uint32_t(&nxt)[FW]) -> bool {
             const int col = g0 + c * FW;
-            if (col >= h.n_end) break;  // warp-uniform
+            if (col >= h.n_end) return false;  // warp-uniform
             const bool next = col + FW < COLS && col + FW < h.n_end;
-            uint32_t(&cur)[FW] = (c & 1) ? fB : fA;
-            uint32_t(&nxt)[FW] = (c & 1) ? fA : fB;
             __syncwarp();
             if (next) tmem_ld_32x32b(h.taddr + col + FW, nxt);
             uint4 pk[FPK];
@@ -554,6 +554,12 @@ __device__ __forceinline__ void fast_tile_pass(const GemmParams& p, const FastCo
             for (int j = 0; j < FPK; ++j) wst[lane * RS + ((c * FPK + j) ^ swz)] = pk[j];
             __syncwarp();
             if (next) tmem_wait_regs(nxt);
+            return true;
+        };
+#pragma unroll 1
+        for (int c = 0; c < NCH; c += 2) {
+            if (!chunk(c, fA, fB)) break;
+            if (!chunk(c + 1, fB, fA)) break;
         }
         if (h.ftr && g0 / GW < 8) h.ftr[3 * (g0 / GW) + 1] = clock64();
         if (tma) {
