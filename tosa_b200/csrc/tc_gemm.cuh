@@ -178,6 +178,7 @@ struct GemmParams {
     // output tensor map (the kernel's third parameter) instead of per-thread stores
     int tma_out;
     const CUtensorMap* tmo_host;  // host side only: the map the launcher passes, when tma_out
+    int group_m;                  // row tiles per band of the tile order (0: row tiles fastest throughout)
 };
 
 // TAP2 (int8 im2col convolutions with exactly 64 input channels): two filter taps per stage,
@@ -226,11 +227,26 @@ struct GemmCfg {
 // ---------------------------------------------------------------------------
 
 __device__ __forceinline__ void tile_coords(const GemmParams& p, int tile, int& b, int& mt, int& nt) {
-    // m fastest so CTAs running concurrently share the B tile in L2.
-    const int rest = fdiv(tile, p.fd_mtiles);
-    mt = tile - rest * p.m_tiles;
-    b = fdiv(rest, p.fd_ntiles);
-    nt = rest - b * p.n_tiles;
+    if (p.group_m == 0) {
+        // m fastest so CTAs running concurrently share the B tile in L2.
+        const int rest = fdiv(tile, p.fd_mtiles);
+        mt = tile - rest * p.m_tiles;
+        b = fdiv(rest, p.fd_ntiles);
+        nt = rest - b * p.n_tiles;
+        return;
+    }
+    // Large A and B: bands of group_m row tiles, each walked row tile fastest across all column
+    // tiles, so the tiles that run at once share a band of A and a few B tiles in L2 instead of
+    // streaming all of A once per column tile.
+    const int per_batch = p.m_tiles * p.n_tiles;
+    b = tile / per_batch;
+    int t = tile - b * per_batch;
+    const int span = p.group_m * p.n_tiles;
+    const int g = t / span;
+    t -= g * span;
+    const int gm = min(p.group_m, p.m_tiles - g * p.group_m);
+    nt = t / gm;
+    mt = g * p.group_m + (t - nt * gm);
 }
 
 // Makes the 16 registers of a finished tcgen05.ld visible only after the
