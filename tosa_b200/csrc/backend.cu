@@ -1508,7 +1508,14 @@ extern "C" TB_API tb_status tb_conv2d_plan_run(tb_conv2d_plan* p, const void* in
 #define TB_IM2COL(IC_, KW_)                                                                               \
     else if (d.ic == IC_ && d.kw == KW_ && d.dilation[1] == 1)                                           \
         im2col_rows_i8_t<IC_, KW_><<<bl, threads, smem, st>>>(g, x, x_bytes, p->segp, p->kp, zx, p->d_rows)
-        if (false) {}
+        if (d.kh == 1 && d.kw == 1 && d.ic % 4 == 0 && (reinterpret_cast<uintptr_t>(input) & 3) == 0) {
+            // 1x1 (channel counts that are not 16-byte multiples): each row is the pixel's channels
+            // padded with the input zero point, one 16-byte chunk per thread
+            const long long chunks = m_rows * (p->kp / 16);
+            const uint32_t zxw = 0x01010101u * static_cast<uint8_t>(zx);
+            im2col_rows_1x1_i8<<<grid_for(ctx, chunks), 256, 0, st>>>(g, static_cast<const uint32_t*>(input), p->kp,
+                                                                    zxw, reinterpret_cast<uint4*>(p->d_rows));
+        }
         TB_IM2COL(3, 7); TB_IM2COL(3, 5); TB_IM2COL(3, 3); TB_IM2COL(4, 7); TB_IM2COL(4, 5); TB_IM2COL(4, 3);
         else im2col_rows_i8<<<bl, threads, smem, st>>>(g, x, p->segp, p->kp, zx, p->d_rows);
 #undef TB_IM2COL

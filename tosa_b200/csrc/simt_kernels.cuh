@@ -218,6 +218,34 @@ __global__ void im2col_rows_i8(ConvGeomDev g, const int8_t* __restrict__ x, int 
     }
 }
 
+// The rows of a 1x1 convolution (IC % 4 == 0, kp a multiple of 16): the pixel's IC channels
+// then the input zero point up to kp bytes; a pixel outside the input (padding) is a row of
+// the zero point. One thread per 16-byte chunk of a row: word loads of the pixel, one 16-byte
+// store, both contiguous across the threads of a warp.
+__global__ void im2col_rows_1x1_i8(ConvGeomDev g, const uint32_t* __restrict__ x, int kp, uint32_t zxw,
+                                   uint4* __restrict__ rows) {
+    const int icw = g.ic >> 2, chunks = kp >> 4;
+    const long long total = static_cast<long long>(g.n) * g.oh * g.ow * chunks;
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long m = i / chunks;
+        const int q = static_cast<int>(i - m * chunks);
+        const int ox = static_cast<int>(m % g.ow);
+        const long long r = m / g.ow;
+        const int oy = static_cast<int>(r % g.oh);
+        const long long b = r / g.oh;
+        const int y = oy * g.sh - g.pad_t, xx = ox * g.sw - g.pad_l;
+        uint32_t w[4] = {zxw, zxw, zxw, zxw};
+        if (static_cast<unsigned>(y) < static_cast<unsigned>(g.ih) && static_cast<unsigned>(xx) < static_cast<unsigned>(g.iw)) {
+            const uint32_t* src = x + ((b * g.ih + y) * g.iw + xx) * icw;
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                if (4 * q + k < icw) w[k] = __ldg(src + 4 * q + k);
+        }
+        rows[i] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
 // The same rows for the common stems (IC channels, KW taps per filter row known at
 // compile time, no horizontal dilation): a filter row's KW * IC input bytes are
 // contiguous, so an interior segment is read as the aligned 32-bit words covering
