@@ -79,13 +79,14 @@ tb_status launch_gemm(tb_context* ctx, const CUtensorMap& tmA, const CUtensorMap
     cfg.blockDim = dim3(kGemmThreads);
     cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
     cfg.stream = stream;
+    // Programmatic dependent launch: the GEMM may be placed on the SMs as the preceding kernel's
+    // blocks leave (its barrier setup, TMEM allocation and descriptor prefetch overlap that
+    // kernel's tail); its producer waits for the preceding kernel before the first copy.
     cudaLaunchAttribute attr[2];
     int na = 0;
-    if (p.epi.pdl_wait) {
-        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[na].val.programmaticStreamSerializationAllowed = 1;
-        ++na;
-    }
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
     cfg.attrs = attr;
     cfg.numAttrs = na;
     // the output map (fast int8 epilogue with TMA stores), or an unused placeholder

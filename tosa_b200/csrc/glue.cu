@@ -16,6 +16,7 @@
 #include <vector>
 
 #include "internal.hpp"
+#include "ptx.cuh"
 #include "quant.cuh"
 
 namespace tb {
@@ -206,6 +207,7 @@ __global__ void __launch_bounds__(256) residual_fast_i8(const uint4* __restrict_
                                                         const int32_t* __restrict__ fhz, int32_t lo, int32_t hi,
                                                         int32_t add_zp, long long n16, int channels,
                                                         uint4* __restrict__ out) {
+    grid_launch_dependents();  // a programmatic dependent launch of the next kernel may start
     extern __shared__ __align__(16) int32_t lut[];  // [256 entries][a x 16 | b x 16]
     for (int i = threadIdx.x; i < 256 * 16; i += blockDim.x) {
         const int e = i >> 4, c = i & 15;
@@ -288,6 +290,7 @@ __device__ __forceinline__ uint32_t residual_table_word(const uint8_t* tab, uint
 __global__ void __launch_bounds__(512) residual_table_i8(const uint4* __restrict__ a, const uint4* __restrict__ b,
                                                          const uint4* __restrict__ table, long long n16,
                                                          uint4* __restrict__ out) {
+    grid_launch_dependents();  // a programmatic dependent launch of the next kernel may start
     extern __shared__ __align__(16) uint8_t tab[];
     for (int i = threadIdx.x; i < kResidTableBytes / 16; i += blockDim.x)
         reinterpret_cast<uint4*>(tab)[i] = __ldg(table + i);

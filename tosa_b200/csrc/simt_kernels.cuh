@@ -180,6 +180,7 @@ __global__ void conv2d_direct_float(ConvGeomDev g, const void* __restrict__ x, c
 // ---------------------------------------------------------------------------
 __global__ void im2col_rows_i8(ConvGeomDev g, const int8_t* __restrict__ x, int segp, int kp, int8_t zx,
                                int8_t* __restrict__ rows) {
+    grid_launch_dependents();  // a programmatic dependent launch of the next kernel may start
     // One thread per output pixel assembles its row in shared memory, then the
     // block writes its rows out with 16-byte stores.
     extern __shared__ __align__(16) int8_t srow[];
@@ -224,6 +225,7 @@ __global__ void im2col_rows_i8(ConvGeomDev g, const int8_t* __restrict__ x, int 
 // store, both contiguous across the threads of a warp.
 __global__ void im2col_rows_1x1_i8(ConvGeomDev g, const uint32_t* __restrict__ x, int kp, uint32_t zxw,
                                    uint4* __restrict__ rows) {
+    grid_launch_dependents();  // a programmatic dependent launch of the next kernel may start
     const int icw = g.ic >> 2, chunks = kp >> 4;
     const long long total = static_cast<long long>(g.n) * g.oh * g.ow * chunks;
     for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
@@ -255,6 +257,7 @@ template <int IC, int KW>
 __global__ void __launch_bounds__(128) im2col_rows_i8_t(ConvGeomDev g, const int8_t* __restrict__ x,
                                                          long long x_bytes, int segp, int kp, int8_t zx,
                                                          int8_t* __restrict__ rows) {
+    grid_launch_dependents();  // a programmatic dependent launch of the next kernel may start
     constexpr int L = KW * IC, LW = (L + 3) / 4;  // segment bytes and words
     extern __shared__ __align__(16) int8_t srow[];
     const long long m_total = static_cast<long long>(g.n) * g.oh * g.ow;
@@ -693,6 +696,7 @@ template <int K, int SW, int EK>
 __global__ void depthwise_i8_dp2a(DwGeom g, const uint32_t* __restrict__ x, const uint4* __restrict__ wm,
                                   const int32_t* __restrict__ bias2, uint32_t zxw, DwEpi e, void* out,
                                   uint32_t* err) {
+    grid_launch_dependents();  // a programmatic dependent launch of the next kernel may start
     constexpr int P = kDwPix;
     constexpr int NC = (P - 1) * SW + K;  // input columns under P output pixels
     const int c4 = (blockIdx.x % g.chunks) * blockDim.x + threadIdx.x;
@@ -885,6 +889,7 @@ template <int S, int EK>
 __global__ void depthwise_i8_dp2a_strip(DwGeom g, const uint32_t* __restrict__ x, const uint4* __restrict__ wm,
                                         const int32_t* __restrict__ bias2, uint32_t zxw, DwEpi e, void* out,
                                         uint32_t* err) {
+    grid_launch_dependents();  // a programmatic dependent launch of the next kernel may start
     constexpr int NC = DwStrip<S>::NC;
     const int c4 = (blockIdx.x % g.chunks) * blockDim.x + threadIdx.x;
     const int ox0 = ((blockIdx.x / g.chunks) * blockDim.y + threadIdx.y) * DwStrip<S>::P;

@@ -158,6 +158,7 @@ __host__ __device__ inline int pool_block(const PoolTile& pt) {
 template <int BATCH>
 __global__ void avg_pool_i8_vec16(PoolGeomDev g, PoolTile pt, const int8_t* __restrict__ x, int32_t zi, int32_t zo,
                                   RecipTable rt, int8_t* out) {
+    grid_launch_dependents();  // a programmatic dependent launch of the next kernel may start
     const int oy = blockIdx.y, b = blockIdx.z;
     const int iy0 = oy * g.sy - g.pad_t;
     const int ky0 = max(0, -iy0), ky1 = min(g.ky, g.ih - iy0);
@@ -227,6 +228,7 @@ __device__ __forceinline__ uint32_t max_u16x2(uint32_t a, uint32_t b) {
 // unsigned 16-bit maxima; the bytes are rejoined and unbiased at the end.
 template <int BATCH>
 __global__ void max_pool_i8_vec16(PoolGeomDev g, PoolTile pt, const int8_t* __restrict__ x, int8_t* out) {
+    grid_launch_dependents();  // a programmatic dependent launch of the next kernel may start
     const int oy = blockIdx.y, b = blockIdx.z;
     const int iy0 = oy * g.sy - g.pad_t;
     const int ky0 = max(0, -iy0), ky1 = min(g.ky, g.ih - iy0);

@@ -694,6 +694,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const long long drain_limit = limit > kDrainCycles ? limit : kDrainCycles;
     const int SE = p.s_eff;  // stages of the ring in use
     if (kGemmTrace && p.trace && blockIdx.x == 0 && threadIdx.x == 0) p.trace[400] = clock64();
+    // The next kernel on the stream, when launched as a programmatic dependent, may be placed on
+    // the SMs this grid leaves; it waits for this grid's completion before touching its data.
+    if (threadIdx.x == 0) grid_launch_dependents();
     if (kGemmTrace && p.trace && threadIdx.x == 0) {
         if (blockIdx.x == 0) p.trace[403] = static_cast<long long>(globaltimer_ns());
         atomicMax(reinterpret_cast<unsigned long long*>(p.trace + 405), globaltimer_ns());
@@ -716,6 +719,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 for (int i = 0; i < S; ++i) bkey[i] = -1;
                 int rs_s = 0;       // ring position of `it`: stage it % SE and its phase parity, stepped
                 uint32_t rs_ph = 0; // (no division by the runtime stage count)
+                // launched as a programmatic dependent: the preceding kernel's outputs (A, and B
+                // of a MATMUL) are complete and visible only after this wait; nothing of this
+                // kernel reads or writes global data before the first copy (the epilogue's stores
+                // follow the MMAs of these copies)
+                grid_dependency_wait();
                 for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
                     int b, mt, nt;
                     tile_coords(p, tile, b, mt, nt);
