@@ -452,6 +452,8 @@ POOL_CASES = [
     (1, 6, 5, 7, (2, 3), (2, 1), (0, 0, 1, 1)),      # scalar
     (1, 8, 8, 4096, (3, 3), (1, 1), (1, 1, 1, 1)),   # 256 channel groups: one pixel per block
     (2, 10, 10, 32, (8, 8), (2, 2), (3, 3, 3, 3)),   # 64 taps (the widest 16-bit-lane window), borders
+    (1, 8, 8, 1024, (3, 3), (1, 1), (1, 1, 1, 1)),   # max pool rows staged in shared memory, 64 channel groups
+    (3, 15, 13, 16, (4, 3), (1, 2), (2, 1, 0, 2)),   # four-row windows, uneven padding
 ]
 
 
