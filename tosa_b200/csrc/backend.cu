@@ -853,6 +853,7 @@ struct tb_conv2d_plan {
     uint8_t* d_rowclass = nullptr;
     uint8_t* d_colclass = nullptr;
     int n_cx = 1;
+    int n_classes = 1;              // border classes (1: every output pixel sees every tap, e.g. a 1x1)
     const void* in_cached = nullptr;
     const void* o_cached = nullptr;  // output the TMA-store map tmO was made for
     CUtensorMap tmA, tmB, tmO;
@@ -1210,6 +1211,7 @@ static tb_status conv_plan_create(tb_context* ctx, const tb_conv2d_desc* d, cons
     const int n_ry = static_cast<int>(ky_r.size() / 2), n_rx = static_cast<int>(kx_r.size() / 2);
     if (n_ry > 255 || n_rx > 255) return bail(fail(TB_ERR_NOT_ACCELERATED, "%s: too many border classes", op));
     p->n_cx = n_rx;
+    p->n_classes = n_ry * n_rx;
     int ry_full = 0, rx_full = 0;
     for (int c = 0; c < n_ry; ++c)
         if (ky_r[2 * c] == 0 && ky_r[2 * c + 1] == d->kh - 1) ry_full = c;
@@ -1584,8 +1586,10 @@ extern "C" TB_API tb_status tb_conv2d_plan_run(tb_conv2d_plan* p, const void* in
     ep.ct_delta = p->d_ctdelta;
     ep.ct_ld = p->ct_ld;
     ep.base_class = p->base_class;
-    ep.rowclass = p->d_rowclass;
-    ep.colclass = p->d_colclass;
+    // one border class (no padding reaches a window): the base column terms are the whole
+    // story, and the kernel without border-class code runs
+    ep.rowclass = p->n_classes > 1 ? p->d_rowclass : nullptr;
+    ep.colclass = p->n_classes > 1 ? p->d_colclass : nullptr;
     ep.n_col_classes = p->n_cx;
     ep.row_zp_neg = static_cast<int32_t>(static_cast<uint32_t>(-d.weight_zp) *
                                          (p->sr.ok ? static_cast<uint32_t>(p->sr.mul) : 1u));
