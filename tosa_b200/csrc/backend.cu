@@ -1586,10 +1586,13 @@ extern "C" TB_API tb_status tb_conv2d_plan_run(tb_conv2d_plan* p, const void* in
     ep.ct_delta = p->d_ctdelta;
     ep.ct_ld = p->ct_ld;
     ep.base_class = p->base_class;
-    // one border class (no padding reaches a window): the base column terms are the whole
-    // story, and the kernel without border-class code runs
-    ep.rowclass = p->n_classes > 1 ? p->d_rowclass : nullptr;
-    ep.colclass = p->n_classes > 1 ? p->d_colclass : nullptr;
+    // one border class (no padding reaches a window), or classes that differ only through the
+    // input zero point when it is 0: the base column terms are the whole story, and the kernel
+    // without border-class code runs
+    // (with input zero point 0 every class has the same terms: bias + 0)
+    const bool classes = p->n_classes > 1 && d.input_zp != 0;
+    ep.rowclass = classes ? p->d_rowclass : nullptr;
+    ep.colclass = classes ? p->d_colclass : nullptr;
     ep.n_col_classes = p->n_cx;
     ep.row_zp_neg = static_cast<int32_t>(static_cast<uint32_t>(-d.weight_zp) *
                                          (p->sr.ok ? static_cast<uint32_t>(p->sr.mul) : 1u));

@@ -43,6 +43,7 @@ def main(argv=None) -> int:
     ap.add_argument("kind", choices=["conv", "depthwise", "residual", "matmul_t"])
     ap.add_argument("dims", type=int, nargs="+")
     ap.add_argument("--runs", type=int, default=5)
+    ap.add_argument("--zx", type=int, default=-3, help="input zero point of conv (default -3)")
     args = ap.parse_args(argv)
 
     import torch
@@ -56,7 +57,7 @@ def main(argv=None) -> int:
         n, hw, ic, oc, k = args.dims
         pad = (k // 2,) * 4
         d = L.conv_desc(n, hw, hw, ic, oc, k, k, pad, (1, 1), (1, 1), L.DT_INT8, L.DT_INT8, L.DT_INT32,
-                        L.DT_INT32, input_zp=-3)
+                        L.DT_INT32, input_zp=args.zx)
         w = torch.from_numpy(rng.integers(-127, 128, (oc, k, k, ic), dtype=np.int8)).cuda()
         bias = torch.from_numpy(rng.integers(-30000, 30000, oc).astype(np.int32)).cuda()
         at = L.rescale_attr(rng.integers(1 << 30, (1 << 31) - 1, oc), rng.integers(36, 40, oc),
