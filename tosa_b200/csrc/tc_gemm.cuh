@@ -422,9 +422,9 @@ constexpr int kEfDelta = 2;
 
 template <int EK, int W, bool ROW, bool DELTA>
 __device__ __forceinline__ void fast_chunk_i8(const GemmParams& p, const uint32_t (&acc)[W], int n0, int32_t rowterm,
-                                              const int32_t* colterm, const int32_t* delta, const int32_t* fm,
-                                              const int32_t* fsh, const int32_t* fc, const FastConst& fk,
-                                              uint4 (&out16)[W / 16]) {
+                                              const int32_t* colterm, const int32_t* delta, const int4 (&dl)[W / 4],
+                                              const int32_t* fm, const int32_t* fsh, const int32_t* fc,
+                                              const FastConst& fk, uint4 (&out16)[W / 16]) {
     constexpr bool PC = EK == EK_FAST_PC_S || EK == EK_FAST_PC_D;
     constexpr bool DBL = EK == EK_FAST_T_D || EK == EK_FAST_PC_D;
     const uint32_t mul = static_cast<uint32_t>(p.epi.sr_mul);
@@ -442,10 +442,10 @@ __device__ __forceinline__ void fast_chunk_i8(const GemmParams& p, const uint32_
         for (int j = 0; j < W; ++j) v[j] = static_cast<int32_t>(static_cast<uint32_t>(v[j]) + static_cast<uint32_t>(rowterm));
     }
     if (DELTA && delta != nullptr) {  // warp-uniform: null for a warp without border rows
-        const int4* d4 = reinterpret_cast<const int4*>(delta + n0);
+        // (the deltas of the chunk's columns, loaded by the caller one chunk ahead)
 #pragma unroll
         for (int j = 0; j < W; j += 4) {
-            const int4 c = __ldg(d4 + j / 4);
+            const int4 c = dl[j / 4];
             v[j + 0] = static_cast<int32_t>(static_cast<uint32_t>(v[j + 0]) + static_cast<uint32_t>(c.x));
             v[j + 1] = static_cast<int32_t>(static_cast<uint32_t>(v[j + 1]) + static_cast<uint32_t>(c.y));
             v[j + 2] = static_cast<int32_t>(static_cast<uint32_t>(v[j + 2]) + static_cast<uint32_t>(c.z));
@@ -537,9 +537,22 @@ __device__ __forceinline__ void fast_tile_pass(const GemmParams& p, const FastCo
     // TMEM load is in flight while chunk c is rescaled (tcgen05.wait::ld waits for all of this
     // thread's loads, so exactly one is outstanding at each wait).
     uint32_t fA[FW], fB[FW];
+    // border-class deltas of a chunk (a warp with a border row), loaded with the chunk's TMEM
+    // load one chunk ahead, so their latency overlaps the previous chunk's arithmetic
+    int4 dA[FW / 4], dB[FW / 4];
+    auto dload = [&](int col, int4(&d)[FW / 4]) {
+        if constexpr (DELTA) {
+            if (h.delta != nullptr) {
+                const int4* d4 = reinterpret_cast<const int4*>(h.delta + h.nb + col);
+#pragma unroll
+                for (int i = 0; i < FW / 4; ++i) d[i] = __ldg(d4 + i);
+            }
+        }
+    };
     __syncwarp();
     if (h.n_end > 0) {
         tmem_ld_32x32b(h.taddr, fA);
+        dload(0, dA);
         tmem_wait_regs(fA);
     }
 #pragma unroll 1
@@ -557,15 +570,19 @@ __device__ __forceinline__ void fast_tile_pass(const GemmParams& p, const FastCo
         // chunk c of the group: its accumulators in register set c % 2, the next chunk's TMEM load
         // in flight into the other set. Pairs of chunks per iteration (not the whole group
         // unrolled) keep the loop's code small.
-        auto chunk = [&](int c, uint32_t(&cur)[FW], uint32_t(&nxt)[FW]) -> bool {
+        auto chunk = [&](int c, uint32_t(&cur)[FW], uint32_t(&nxt)[FW], int4(&dcur)[FW / 4],
+                         int4(&dnxt)[FW / 4]) -> bool {
             const int col = g0 + c * FW;
             if (col >= h.n_end) return false;  // warp-uniform
             const bool next = col + FW < COLS && col + FW < h.n_end;
             __syncwarp();
-            if (next) tmem_ld_32x32b(h.taddr + col + FW, nxt);
+            if (next) {
+                tmem_ld_32x32b(h.taddr + col + FW, nxt);
+                dload(col + FW, dnxt);
+            }
             uint4 pk[FPK];
-            fast_chunk_i8<EK, FW, ROW, DELTA>(p, cur, h.nb + col, h.rowterm, h.cst_n, h.delta, h.fm, h.fsh, h.fc,
-                                                   fk, pk);
+            fast_chunk_i8<EK, FW, ROW, DELTA>(p, cur, h.nb + col, h.rowterm, h.cst_n, h.delta, dcur, h.fm, h.fsh,
+                                                   h.fc, fk, pk);
 #pragma unroll
             for (int j = 0; j < FPK; ++j) wst[lane * RS + ((c * FPK + j) ^ swz)] = pk[j];
             __syncwarp();
@@ -574,8 +591,8 @@ __device__ __forceinline__ void fast_tile_pass(const GemmParams& p, const FastCo
         };
 #pragma unroll 1
         for (int c = 0; c < NCH; c += 2) {
-            if (!chunk(c, fA, fB)) break;
-            if (!chunk(c + 1, fB, fA)) break;
+            if (!chunk(c, fA, fB, dA, dB)) break;
+            if (!chunk(c + 1, fB, fA, dB, dA)) break;
         }
         if (h.ftr && g0 / GW < 8) h.ftr[3 * (g0 / GW) + 1] = clock64();
         if (tma) {
