@@ -1115,6 +1115,15 @@ static tb_status conv_plan_create(tb_context* ctx, const tb_conv2d_desc* d, cons
 
     p->bn = oc <= 64 ? 64 : oc <= 128 ? 128 : 256;
     {
+        // Up to 512 output channels over many pixels (int8): 128-column tiles, which the three
+        // epilogue groups take whole in turn, instead of 256-column tiles split 64 / 96 / 96
+        // columns between them (ResNet-50's 64->256 and 128->512, MobileNetV2's 32->192 and
+        // 64->384 layers at 64 images: 4-18 % faster; at 14x14 the 256-column form is faster)
+        const long long m_tiles = (static_cast<long long>(d->n) * oh * ow + 127) / 128;
+        const long long n128 = (oc + 127) / 128;
+        if (int8 && p->bn == 256 && n128 <= 4 && m_tiles * n128 >= 4ll * ctx->num_sms) p->bn = 128;
+    }
+    {
         // Few tiles (small maps, few images): narrower tiles while their count stays within one
         // wave of the SMs, so more SMs share the contraction (a 7x7 map of 64 images has 25 row
         // tiles: 50 tiles of 256 output channels, 100 of 128)

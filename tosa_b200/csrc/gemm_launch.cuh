@@ -52,8 +52,10 @@ tb_status launch_gemm(tb_context* ctx, const CUtensorMap& tmA, const CUtensorMap
     p.m_tiles = (p.M + Cfg::BM - 1) / Cfg::BM;
     p.n_tiles = (p.N + Cfg::kBN - 1) / Cfg::kBN;
     p.total_tiles = p.batch * p.m_tiles * p.n_tiles;
-    // big GEMMs (many row and column tiles): bands of 16 row tiles in the tile order
-    p.group_m = (p.m_tiles >= 32 && p.n_tiles >= 4) ? 16 : 0;
+    // big MATMULs (many row and column tiles): bands of 16 row tiles in the tile order. Not for
+    // convolutions: their weights (B) are small, and walking column tiles within a band would
+    // make each CTA reload B and restage its column constants on every tile.
+    p.group_m = (!Cfg::kIm2col && p.m_tiles >= 32 && p.n_tiles >= 4) ? 16 : 0;
     p.fd_mtiles = make_fastdiv(p.m_tiles);
     p.fd_ntiles = make_fastdiv(p.n_tiles);
     p.fd_ow = make_fastdiv(p.conv_OW);
