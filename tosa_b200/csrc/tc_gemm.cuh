@@ -1003,13 +1003,40 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const bool stage_cols = kFast || kPC || e.colterm != nullptr;
         int staged_key = -1;
         int sbuf = 0;
-        for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++tcount) {
+        // Whole tiles with at most four (batch, column tile) keys: every key's constants are
+        // staged once, [key][column terms, multiplier, shift, c][128], and each group walks only
+        // its own tiles (no per-tile key checks, no staging barriers inside the loop).
+        const bool static_keys = p.epi_groups != 0 && stage_cols && BN <= 128 && p.batch * p.n_tiles <= 4;
+        int cstride = 256;  // elements between the staged arrays of one key
+        if (static_keys) {
+            cstride = 128;
+            for (int k = 0; k < p.batch * p.n_tiles; ++k) {
+                const int bk = k / p.n_tiles, nk = k - bk * p.n_tiles;
+                int32_t* cst = ct_stage + k * 512;
+                for (int i = et; i < BN; i += kEpiWarps * 32) {
+                    const int n = nk * BN + i;
+                    cst[i] = e.colterm != nullptr ? e.colterm[bk * e.colterm_bstride + n] : 0;
+                    if constexpr (kPC) {
+                        cst[128 + i] = __ldg(e.fq_m + n);
+                        cst[256 + i] = __ldg(e.sr_sh + n);
+                        cst[384 + i] = __ldg(e.sr_c + n);
+                    }
+                }
+            }
+            if (!epi_sync()) ok = false;
+            tcount = static_cast<uint32_t>(grp);
+        }
+        const int tstep = static_keys ? kEpiGroups : 1;
+        for (int tile = blockIdx.x + (static_keys ? grp * static_cast<int>(gridDim.x) : 0); tile < p.total_tiles && ok;
+             tile += tstep * gridDim.x, tcount += tstep) {
             int b, mt, nt;
             tile_coords(p, tile, b, mt, nt);
             const int buf = tcount & (NB - 1);
             const uint32_t tph = (tcount >> NB_LOG) & 1;
             const int key = b * p.n_tiles + nt;
-            if (stage_cols && key != staged_key) {
+            if (static_keys) {
+                sbuf = key;  // (ct_stage + key * 512 below)
+            } else if (stage_cols && key != staged_key) {
                 sbuf ^= 1;
                 int32_t* cst = ct_stage + sbuf * 1024;
                 // (the tables are padded to whole 256-column tiles)
@@ -1027,9 +1054,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
             // (the column-constant staging above is shared by both groups: every warp passes
             // every tile's key check, so the staging barriers pair up)
-            if (p.epi_groups ? static_cast<int>(tcount % kEpiGroups) != grp : cols == 0) continue;
+            if (!static_keys && (p.epi_groups ? static_cast<int>(tcount % kEpiGroups) != grp : cols == 0)) continue;
             // Pointers indexed by the absolute output column.
-            const int32_t* cst_n = ct_stage + sbuf * 1024 - nt * BN;
+            const int32_t* cst_n = ct_stage + sbuf * (static_keys ? 512 : 1024) - nt * BN;
             // Border class of this thread's row (before the accumulator wait: the lookups overlap it).
             const int m = mt * BM + row;
             const bool row_ok = m < p.M;
@@ -1060,9 +1087,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 if (lane == 0) mbar_arrive(&rsempty[buf]);
             }
             const int32_t* colterm = e.colterm != nullptr ? cst_n : nullptr;
-            const int32_t* fm = cst_n + 256;
-            const int32_t* fsh = cst_n + 512;
-            const int32_t* fhz = cst_n + 768;
+            const int32_t* fm = cst_n + cstride;
+            const int32_t* fsh = cst_n + 2 * cstride;
+            const int32_t* fhz = cst_n + 3 * cstride;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                                    static_cast<uint32_t>(buf * BN + cbase);
             const long long orow = static_cast<long long>(b) * p.out_batch_stride + static_cast<long long>(m) * p.ldo;
