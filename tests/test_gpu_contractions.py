@@ -363,6 +363,10 @@ def test_conv2d_float_tensor_core(ctx, dt, out_dt):
     (2, 14, 15, 16, 1, 3, 3, (2, 2, 1, 1), (1, 2), (2, 1), 4, 1),       # vertical dilation
     (1, 9, 9, 24, 1, 3, 3, (0, 0, 0, 0), (1, 1), (1, 1), 6, -100),     # w - zw beyond a byte (9 bits)
     (1, 9, 11, 8, 1, 3, 5, (1, 1, 2, 2), (1, 1), (1, 2), -1, 1),       # horizontal dilation: vec4 kernel
+    # 3x3 strip kernel block shapes: two channel chunks of 130 and of 120 words, 9 words x 10 groups
+    (1, 9, 10, 1040, 1, 3, 3, (1, 1, 1, 1), (1, 1), (1, 1), 3, 0),
+    (2, 12, 30, 960, 1, 3, 3, (1, 0, 1, 0), (2, 2), (1, 1), -7, 1),
+    (1, 11, 37, 36, 1, 3, 3, (1, 1, 1, 1), (1, 1), (1, 1), 0, 2),
 ])
 def test_depthwise_int8(ctx, case):
     n, ih, iw, c, m, kh, kw, pad, stride, dil, zx, zw = case
