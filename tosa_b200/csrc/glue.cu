@@ -287,7 +287,7 @@ __device__ __forceinline__ uint32_t residual_table_word(const uint8_t* tab, uint
     return __byte_perm(__byte_perm(r0, r1, 0x0040), __byte_perm(r2, r3, 0x0040), 0x5410);
 }
 
-__global__ void __launch_bounds__(512) residual_table_i8(const uint4* __restrict__ a, const uint4* __restrict__ b,
+__global__ void __launch_bounds__(1024) residual_table_i8(const uint4* __restrict__ a, const uint4* __restrict__ b,
                                                          const uint4* __restrict__ table, long long n16,
                                                          uint4* __restrict__ out) {
     grid_launch_dependents();  // a programmatic dependent launch of the next kernel may start
@@ -468,17 +468,19 @@ tb_status launch_residual(tb_context* ctx, const void* a, int a_dt, int a_uns, i
     if (count == 0) return TB_OK;
     if (fast.d_table != nullptr && count % 16 == 0 && aligned16(a) && aligned16(b) && aligned16(out)) {
         const long long n16 = count / 16;
-        // at most three blocks per SM (64 KB of table each), about two 16-byte steps per thread
-        // (small tensors: many blocks, so the per-block table load is spread over the SMs)
+        // at most two blocks of 1024 threads per SM (64 KB of table each), about two 16-byte
+        // steps per thread (small tensors: many blocks, so the per-block table load is spread over
+        // the SMs). Measured on B200 in the ResNet-50 step: +1 % over three blocks of 512 threads,
+        // whose third table load per SM cost more than the extra threads gained.
         const int grid = static_cast<int>(std::max<long long>(
-            1, std::min<long long>((n16 + 1023) / 1024, 3ll * ctx->num_sms)));
+            1, std::min<long long>((n16 + 2047) / 2048, 2ll * ctx->num_sms)));
         static bool attr_set = false;
         if (!attr_set) {
             TB_CUDA(cudaFuncSetAttribute(residual_table_i8, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          kResidTableBytes));
             attr_set = true;
         }
-        residual_table_i8<<<grid, 512, kResidTableBytes, st>>>(static_cast<const uint4*>(a),
+        residual_table_i8<<<grid, 1024, kResidTableBytes, st>>>(static_cast<const uint4*>(a),
                                                                static_cast<const uint4*>(b),
                                                                reinterpret_cast<const uint4*>(fast.d_table), n16,
                                                                static_cast<uint4*>(out));

@@ -248,11 +248,12 @@ __global__ void im2col_rows_1x1_i8(ConvGeomDev g, const uint32_t* __restrict__ x
     }
 }
 
-// The same rows for the common stems (IC channels, KW taps per filter row known at
-// compile time, no horizontal dilation): a filter row's KW * IC input bytes are
-// contiguous, so an interior segment is read as the aligned 32-bit words covering
-// it and funnel-shifted into place (word loads and stores instead of byte ones);
-// segments touching the image border take bytes one by one.
+// The same rows for the common stems (IC channels, a square K x K window known at compile
+// time, no horizontal dilation): a filter row's K * IC input bytes are contiguous, so an
+// interior segment is read as the aligned 32-bit words covering it and funnel-shifted into
+// place (word loads and stores instead of byte ones); segments touching the image border
+// take bytes one by one. The filter rows are unrolled, so all of a pixel's loads are in
+// flight together.
 template <int IC, int KW>
 __global__ void __launch_bounds__(128) im2col_rows_i8_t(ConvGeomDev g, const int8_t* __restrict__ x,
                                                          long long x_bytes, int segp, int kp, int8_t zx,
@@ -275,8 +276,9 @@ __global__ void __launch_bounds__(128) im2col_rows_i8_t(ConvGeomDev g, const int
             const long long xb = static_cast<long long>(b) * g.ih * g.iw * IC;
             const int x0 = ox * g.sw - g.pad_l;
             const bool x_in = x0 >= 0 && x0 + KW <= g.iw;
-            for (int k = g.kh * (segp >> 2); k < (kp >> 2); ++k) my[k] = fill;
-            for (int ky = 0; ky < g.kh; ++ky) {
+            for (int k = KW * (segp >> 2); k < (kp >> 2); ++k) my[k] = fill;
+#pragma unroll
+            for (int ky = 0; ky < KW; ++ky) {
                 const int y = oy * g.sh + ky * g.dh - g.pad_t;
                 uint32_t* dst = my + ky * (segp >> 2);
                 const long long a = xb + (static_cast<long long>(y) * g.iw + x0) * IC;  // first byte

@@ -6,8 +6,8 @@ profiler (and a quick timing with CUDA events).
     python -m tosa_b200.profile_layer residual N HW C [--runs 5]
     python -m tosa_b200.profile_layer matmul_t N H C W D [--runs 5]
 
-conv: int8 CONV2D (square HW x HW input, K x K window, stride 1, "same" padding, input
-zero point -3) with a fused per-channel RESCALE (double rounding) + CLAMP to int8,
+conv: int8 CONV2D (square HW x HW input, K x K window, stride 1 or --stride, "same" padding,
+input zero point -3 or --zx) with a fused per-channel RESCALE (double rounding) + CLAMP to int8,
 planned once with tb_conv2d_plan_create and run through tb_conv2d_plan_run.
 depthwise: the same for DEPTHWISE_CONV2D (channel multiplier 1, weight zero point 2,
 stride 1 or 2) through tb_depthwise_conv2d_plan_create.
@@ -44,6 +44,7 @@ def main(argv=None) -> int:
     ap.add_argument("dims", type=int, nargs="+")
     ap.add_argument("--runs", type=int, default=5)
     ap.add_argument("--zx", type=int, default=-3, help="input zero point of conv (default -3)")
+    ap.add_argument("--stride", type=int, default=1, help="stride of conv (default 1)")
     args = ap.parse_args(argv)
 
     import torch
@@ -55,8 +56,12 @@ def main(argv=None) -> int:
     rng = np.random.default_rng(2)
     if args.kind == "conv":
         n, hw, ic, oc, k = args.dims
-        pad = (k // 2,) * 4
-        d = L.conv_desc(n, hw, hw, ic, oc, k, k, pad, (1, 1), (1, 1), L.DT_INT8, L.DT_INT8, L.DT_INT32,
+        st = args.stride
+        # "same" padding (the graphs' rule: the extra row and column at the bottom and right)
+        tot = max((-(-hw // st) - 1) * st + k - hw, 0)
+        pad = (tot // 2, tot - tot // 2) * 2
+        pad = (pad[0], pad[1], pad[0], pad[1])
+        d = L.conv_desc(n, hw, hw, ic, oc, k, k, pad, (st, st), (1, 1), L.DT_INT8, L.DT_INT8, L.DT_INT32,
                         L.DT_INT32, input_zp=args.zx)
         w = torch.from_numpy(rng.integers(-127, 128, (oc, k, k, ic), dtype=np.int8)).cuda()
         bias = torch.from_numpy(rng.integers(-30000, 30000, oc).astype(np.int32)).cuda()
@@ -65,12 +70,12 @@ def main(argv=None) -> int:
                             clamp=(3, 127))
         h = ctypes.c_void_p()
         L.check(lib.tb_conv2d_plan_create(ctx.h, d, L.ptr(w), L.ptr(bias), at, ctypes.byref(h)))
-        oh, ow = L.conv_out_hw(hw, hw, k, k, pad, (1, 1), (1, 1))
+        oh, ow = L.conv_out_hw(hw, hw, k, k, pad, (st, st), (1, 1))
         x = torch.from_numpy(rng.integers(-128, 128, (n, hw, hw, ic), dtype=np.int8)).cuda()
         o = torch.empty((n, oh, ow, oc), dtype=torch.int8, device="cuda")
         us = _time(lambda: L.check(lib.tb_conv2d_plan_run(h, L.ptr(x), L.ptr(o), L.stream_ptr())), args.runs, torch)
         lib.tb_conv2d_plan_destroy(h)
-        print(f"conv {n}x{hw}x{hw}x{ic}->{oc} k{k}: {us:.1f} us")
+        print(f"conv {n}x{hw}x{hw}x{ic}->{oc} k{k}" + (f" s{st}" if st > 1 else "") + f": {us:.1f} us")
     elif args.kind == "depthwise":
         n, hw, c, k, st = args.dims
         p = k // 2
