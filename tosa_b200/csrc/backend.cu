@@ -1517,8 +1517,8 @@ extern "C" TB_API tb_status tb_conv2d_plan_run(tb_conv2d_plan* p, const void* in
         // unrolled taps for the common stem shapes (3 or 4 channels, square windows of 3, 5 or 7)
         const long long x_bytes = static_cast<long long>(d.n) * d.ih * d.iw * d.ic;
 #define TB_IM2COL(IC_, KW_)                                                                               \
-    else if (d.ic == IC_ && d.kw == KW_ && d.kh == KW_ && d.dilation[1] == 1)                            \
-        im2col_rows_i8_t<IC_, KW_><<<bl, threads, smem, st>>>(g, x, x_bytes, p->segp, p->kp, zx, p->d_rows)
+    else if (d.ic == IC_ && d.kw == KW_ && d.kh == KW_ && d.dilation[1] == 1 && p->kp == im2col_t_kp(IC_, KW_)) \
+        im2col_rows_i8_t<IC_, KW_><<<bl, threads, smem, st>>>(g, x, x_bytes, zx, p->d_rows)
         if (d.kh == 1 && d.kw == 1 && d.ic % 4 == 0 && (reinterpret_cast<uintptr_t>(input) & 3) == 0) {
             // 1x1 (channel counts that are not 16-byte multiples): each row is the pixel's channels
             // padded with the input zero point, one 16-byte chunk per thread

@@ -251,23 +251,31 @@ __global__ void im2col_rows_1x1_i8(ConvGeomDev g, const uint32_t* __restrict__ x
 // The same rows for the common stems (IC channels, a square K x K window known at compile
 // time, no horizontal dilation): a filter row's K * IC input bytes are contiguous, so an
 // interior segment is read as the aligned 32-bit words covering it and funnel-shifted into
-// place (word loads and stores instead of byte ones); segments touching the image border
-// take bytes one by one. The filter rows are unrolled, so all of a pixel's loads are in
-// flight together.
+// place (word loads instead of byte ones); segments touching the image border take bytes
+// one by one. The row (kp = KPW * 4 bytes, fixed by IC and K) is assembled in registers with
+// the filter rows unrolled, so all of a pixel's loads are in flight together, and staged in
+// shared memory with 16-byte stores: rows of 11 such chunks (the 7x7 RGB stem) put the 8
+// lanes of each store phase in 8 distinct bank groups, where word stores were 4-way
+// conflicts.
+
+// Row bytes of im2col_rows_i8_t<IC, K>: K segments of whole words, rounded up to 16 bytes
+// (the plan's kp for these shapes).
+__host__ __device__ constexpr int im2col_t_kp(int ic, int k) { return (k * ((k * ic + 3) / 4) + 3) / 4 * 16; }
+
 template <int IC, int KW>
 __global__ void __launch_bounds__(128) im2col_rows_i8_t(ConvGeomDev g, const int8_t* __restrict__ x,
-                                                         long long x_bytes, int segp, int kp, int8_t zx,
-                                                         int8_t* __restrict__ rows) {
+                                                         long long x_bytes, int8_t zx, int8_t* __restrict__ rows) {
     grid_launch_dependents();  // a programmatic dependent launch of the next kernel may start
-    constexpr int L = KW * IC, LW = (L + 3) / 4;  // segment bytes and words
+    constexpr int L = KW * IC, LW = (L + 3) / 4;      // segment bytes and words (the segment pitch)
+    constexpr int KPW = (KW * LW + 3) / 4 * 4;        // words per row: whole 16-byte chunks
+    constexpr int kp = KPW * 4;
+    static_assert(kp == im2col_t_kp(IC, KW), "row layout");
     extern __shared__ __align__(16) int8_t srow[];
     const long long m_total = static_cast<long long>(g.n) * g.oh * g.ow;
-    const int chunks = kp >> 4;
     const uint32_t fill = static_cast<uint8_t>(zx) * 0x01010101u;
     for (long long m0 = static_cast<long long>(blockIdx.x) * blockDim.x; m0 < m_total;
          m0 += static_cast<long long>(gridDim.x) * blockDim.x) {
         const long long m = m0 + threadIdx.x;
-        uint32_t* my = reinterpret_cast<uint32_t*>(srow + threadIdx.x * kp);
         if (m < m_total) {
             const int ox = static_cast<int>(m % g.ow);
             const long long r = m / g.ow;
@@ -276,11 +284,12 @@ __global__ void __launch_bounds__(128) im2col_rows_i8_t(ConvGeomDev g, const int
             const long long xb = static_cast<long long>(b) * g.ih * g.iw * IC;
             const int x0 = ox * g.sw - g.pad_l;
             const bool x_in = x0 >= 0 && x0 + KW <= g.iw;
-            for (int k = KW * (segp >> 2); k < (kp >> 2); ++k) my[k] = fill;
+            uint32_t row[KPW];
+#pragma unroll
+            for (int k = KW * LW; k < KPW; ++k) row[k] = fill;
 #pragma unroll
             for (int ky = 0; ky < KW; ++ky) {
                 const int y = oy * g.sh + ky * g.dh - g.pad_t;
-                uint32_t* dst = my + ky * (segp >> 2);
                 const long long a = xb + (static_cast<long long>(y) * g.iw + x0) * IC;  // first byte
                 const long long a0 = a & ~3ll;
                 if (y >= 0 && y < g.ih && x_in && a0 + 4 * (LW + 1) <= x_bytes) {
@@ -296,27 +305,31 @@ __global__ void __launch_bounds__(128) im2col_rows_i8_t(ConvGeomDev g, const int
                             const uint32_t keep = 0xffffffffu >> (8 * (4 * j + 4 - L));
                             v = (v & keep) | (fill & ~keep);
                         }
-                        dst[j] = v;
+                        row[ky * LW + j] = v;
                     }
                 } else {
-                    uint8_t* db = reinterpret_cast<uint8_t*>(dst);
                     const bool yok = y >= 0 && y < g.ih;
 #pragma unroll
-                    for (int kx = 0; kx < KW; ++kx) {
-                        const bool ok = yok && x0 + kx >= 0 && x0 + kx < g.iw;
+                    for (int j = 0; j < LW; ++j) {
+                        uint32_t v = 0;
 #pragma unroll
-                        for (int c = 0; c < IC; ++c)
-                            db[kx * IC + c] = ok ? static_cast<uint8_t>(__ldg(x + a + kx * IC + c)) : static_cast<uint8_t>(zx);
+                        for (int q = 0; q < 4; ++q) {
+                            const int i = 4 * j + q, kx = i / IC;
+                            const bool ok = i < L && yok && x0 + kx >= 0 && x0 + kx < g.iw;
+                            const uint32_t byte = ok ? static_cast<uint8_t>(__ldg(x + a + i)) : static_cast<uint8_t>(zx);
+                            v |= byte << (8 * q);
+                        }
+                        row[ky * LW + j] = v;
                     }
-#pragma unroll
-                    for (int j = L; j < 4 * LW; ++j) db[j] = static_cast<uint8_t>(zx);
                 }
-                for (int j = LW; j < (segp >> 2); ++j) dst[j] = fill;
             }
+            uint4* my = reinterpret_cast<uint4*>(srow + threadIdx.x * kp);
+#pragma unroll
+            for (int c = 0; c < KPW / 4; ++c) my[c] = make_uint4(row[4 * c], row[4 * c + 1], row[4 * c + 2], row[4 * c + 3]);
         }
         __syncthreads();
         const long long rows_here = m_total - m0 < blockDim.x ? m_total - m0 : blockDim.x;
-        const int vecs = static_cast<int>(rows_here) * chunks;
+        const int vecs = static_cast<int>(rows_here) * (KPW / 4);
         uint4* dst = reinterpret_cast<uint4*>(rows + m0 * kp);
         const uint4* s4 = reinterpret_cast<const uint4*>(srow);
         for (int v = threadIdx.x; v < vecs; v += blockDim.x) dst[v] = s4[v];
