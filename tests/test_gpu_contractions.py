@@ -250,6 +250,10 @@ CONV_CASES = [
     (5, 64, 66, 1, 16, 4, 4, (0, 0, 2, 2), (2, 2), (1, 1), 9, -7),      # even kernel, one channel
     (1, 72, 72, 4, 48, 5, 5, (2, 2, 1, 3), (1, 1), (1, 2), -128, -2),
     (7, 50, 50, 3, 32, 7, 7, (3, 2, 3, 2), (2, 2), (1, 1), 2, 1),       # odd pads
+    # the other unrolled stem shapes (4 channels x 7 and 3, 3 channels x 5), borders on every side
+    (2, 94, 98, 4, 16, 7, 7, (3, 2, 3, 2), (2, 2), (1, 1), -3, 0),
+    (4, 40, 40, 4, 24, 3, 3, (1, 1, 1, 1), (1, 1), (1, 1), 100, 2),
+    (3, 40, 40, 3, 40, 5, 5, (2, 2, 2, 2), (1, 1), (1, 1), -100, -1),
     # 64 input channels: two filter taps per stage (odd tap counts end on a one-tap stage)
     (2, 14, 14, 64, 96, 3, 3, (1, 1, 1, 1), (1, 1), (1, 1), 5, -2),     # weight zero point: row sums of both taps
     (1, 13, 13, 64, 64, 5, 5, (2, 2, 2, 2), (2, 2), (1, 1), 4, -4),
