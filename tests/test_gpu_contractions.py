@@ -462,6 +462,7 @@ POOL_CASES = [
     (2, 10, 10, 32, (8, 8), (2, 2), (3, 3, 3, 3)),   # 64 taps (the widest 16-bit-lane window), borders
     (1, 8, 8, 1024, (3, 3), (1, 1), (1, 1, 1, 1)),   # max pool rows staged in shared memory, 64 channel groups
     (3, 15, 13, 16, (4, 3), (1, 2), (2, 1, 0, 2)),   # four-row windows, uneven padding
+    (3, 9, 9, 512, (5, 5), (2, 2), (2, 2, 2, 2)),    # wide windows over few outputs: 8 lanes per group, borders
 ]
 
 

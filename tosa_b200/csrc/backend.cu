@@ -1905,10 +1905,19 @@ extern "C" TB_API tb_status tb_avg_pool2d(tb_context* ctx, const tb_pool2d_desc*
         }();
         const PoolTile pt = pool_tile(g.c, g.ow);
         const dim3 grid((g.ow + pt.ppb - 1) / pt.ppb, g.oh, g.n);
-        // taps in flight per thread: a window of up to 4 taps in one batch, eight at a time for wide
-        // windows, one at a time in between (measured on B200: batches of 8 over a 3x3 window cost
-        // more occupancy than they hide latency)
-        if (g.kx * g.ky <= 4)
+        const long long items = static_cast<long long>(g.n) * g.oh * g.ow * pt.cg;
+        // wide windows over fewer outputs than two 256-thread blocks per SM would cover (global
+        // pools): eight lanes per output group; otherwise taps in flight per thread: a window of up
+        // to 4 taps in one batch, eight at a time for wide windows, one at a time in between
+        // (measured on B200: batches of 8 over a 3x3 window cost more occupancy than they hide
+        // latency)
+        if (g.kx * g.ky >= 16 && items < 2ll * ctx->num_sms * 256) {
+            constexpr int kLanes = 8;
+            const dim3 sgrid((g.ow * pt.cg + 256 / kLanes - 1) / (256 / kLanes), g.oh, g.n);
+            avg_pool_i8_vec16_split<kLanes><<<sgrid, 256, 0, st>>>(g, pt.cg, static_cast<const int8_t*>(input),
+                                                                  d->input_zp, d->output_zp, table,
+                                                                  static_cast<int8_t*>(out));
+        } else if (g.kx * g.ky <= 4)
             avg_pool_i8_vec16<4><<<grid, pool_block(pt), 0, st>>>(g, pt, static_cast<const int8_t*>(input), d->input_zp,
                                                                   d->output_zp, table, static_cast<int8_t*>(out));
         else if (g.kx >= 6)

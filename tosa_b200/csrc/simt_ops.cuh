@@ -217,6 +217,76 @@ __global__ void avg_pool_i8_vec16(PoolGeomDev g, PoolTile pt, const int8_t* __re
     }
 }
 
+// The same AVG_POOL2D for wide windows over few outputs (global pools: 64 images x 128
+// channel groups of a 7x7 window would be 8192 threads walking 49 taps each): S adjacent
+// lanes of a warp share one output group, each summing every S-th tap of the window, and
+// their 16-bit-lane partial sums are added with shuffles inside the S lanes (the lanes'
+// sums add without carries for the same reason the whole window's does). Block b.x covers
+// blockDim.x / S consecutive (pixel, channel group) items of output row b.y of image b.z.
+template <int S>
+__global__ void avg_pool_i8_vec16_split(PoolGeomDev g, int cg, const int8_t* __restrict__ x, int32_t zi, int32_t zo,
+                                        RecipTable rt, int8_t* out) {
+    grid_launch_dependents();  // a programmatic dependent launch of the next kernel may start
+    static_assert(S >= 2 && S <= 32 && (S & (S - 1)) == 0, "S lanes of one warp");
+    const int oy = blockIdx.y, b = blockIdx.z;
+    const int s = threadIdx.x % S;
+    const int item = blockIdx.x * (blockDim.x / S) + threadIdx.x / S;
+    const int ox = item / cg, c16 = (item - ox * cg) * 16;
+    if (ox >= g.ow) return;  // the whole group of S lanes
+    const unsigned lane = threadIdx.x & 31u;
+    const unsigned mask = ((S == 32) ? 0xffffffffu : ((1u << S) - 1u)) << (lane & ~static_cast<unsigned>(S - 1));
+    const int iy0 = oy * g.sy - g.pad_t, ix0 = ox * g.sx - g.pad_l;
+    const int ky0 = max(0, -iy0), ky1 = min(g.ky, g.ih - iy0);
+    const int kx0 = max(0, -ix0), kx1 = min(g.kx, g.iw - ix0);
+    const int nkx = kx1 - kx0, ntaps = (ky1 - ky0) * nkx;
+    const int count = ntaps;
+    if (count <= 0) return;  // cannot happen for a valid geometry (pads smaller than the kernel)
+    const uint4* xb = reinterpret_cast<const uint4*>(x + static_cast<long long>(b) * g.ih * g.iw * g.c + c16);
+    uint32_t lo[4] = {0, 0, 0, 0}, hi[4] = {0, 0, 0, 0};
+    int ky = ky0 + s / nkx, kx = kx0 + s % nkx;  // tap s of the window, row-major
+#pragma unroll 4
+    for (int t = s; t < ntaps; t += S) {
+        const uint4 v = __ldg(xb + static_cast<long long>((iy0 + ky) * g.iw + ix0 + kx) * cg);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            lo[q] += (w[q] ^ 0x80808080u) & 0x00ff00ffu;
+            hi[q] += ((w[q] >> 8) ^ 0x00808080u) & 0x00ff00ffu;
+        }
+        kx += S;
+        while (kx >= kx1) {
+            kx -= nkx;
+            ++ky;
+        }
+    }
+#pragma unroll
+    for (int o = S / 2; o > 0; o >>= 1)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            lo[q] += __shfl_xor_sync(mask, lo[q], o);
+            hi[q] += __shfl_xor_sync(mask, hi[q], o);
+        }
+    if (s != 0) return;
+    const int32_t m = rt.m[count], sh = rt.s[count] - 16;
+    const int32_t bias16 = count * (128 + zi) * 65536;
+    const int32_t cst = (1 << (sh - 1)) + zo * (1 << sh);
+    int32_t r[16];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const int32_t s0 = static_cast<int32_t>(lo[q] << 16) - bias16;          // byte 0
+        const int32_t s2 = static_cast<int32_t>(lo[q] & 0xffff0000u) - bias16;  // byte 2
+        const int32_t s1 = static_cast<int32_t>(hi[q] << 16) - bias16;          // byte 1
+        const int32_t s3 = static_cast<int32_t>(hi[q] & 0xffff0000u) - bias16;  // byte 3
+        r[4 * q + 0] = (__mulhi(s0, m) + cst) >> sh;
+        r[4 * q + 1] = (__mulhi(s1, m) + cst) >> sh;
+        r[4 * q + 2] = (__mulhi(s2, m) + cst) >> sh;
+        r[4 * q + 3] = (__mulhi(s3, m) + cst) >> sh;
+    }
+    reinterpret_cast<uint4*>(out)[((static_cast<long long>(b) * g.oh + oy) * g.ow + ox) * cg + (c16 >> 4)] =
+        make_uint4(pack4_sat_i8(r[0], r[1], r[2], r[3]), pack4_sat_i8(r[4], r[5], r[6], r[7]),
+                   pack4_sat_i8(r[8], r[9], r[10], r[11]), pack4_sat_i8(r[12], r[13], r[14], r[15]));
+}
+
 __device__ __forceinline__ uint32_t max_u16x2(uint32_t a, uint32_t b) {
     uint32_t d;
     asm("max.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
